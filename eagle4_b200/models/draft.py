@@ -1,0 +1,114 @@
+"""EAGLE-4 (and EAGLE-3) one-layer draft head.
+
+Forward of a set of draft rows, as the reference's SGLang port defines it
+(``eagle_harness/sglang/models/llama_eagle4.py:166-336``):
+
+1. target features: ``fc_norm_j`` on each of the aux hidden states, concatenated, through ``fc`` (``n*H_t -> H``);
+   rows that already carry a draft hidden state skip this;
+2. ``qkv(cat(input_layernorm(embed), hidden_norm(hidden)))`` (``2H`` in), RoPE, attention over the draft KV (the
+   frozen committed window plus the row's tree ancestors);
+3. ``residual = hidden + o_proj(attn)``; ``summed = residual + down(swiglu(gate_up(post_norm(residual))))``;
+4. ``normed = norm(summed)`` feeds the head; the next step's hidden is ``normed`` when ``norm_output`` else ``summed``.
+
+Candidate head (EAGLE-4): low-rank scores ``(h @ down^T) @ scores^T`` select the top ``C`` ids; their exact logits
+``lm_head[id] . h`` in fp32 feed a softmax over the ``C`` candidates (equal to the full-vocabulary softmax of the
+-inf-filled row); the top ``K`` of it are the children. EAGLE-3: full draft-vocabulary softmax and a ``d2t`` map.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from eagle4_b200 import ops
+from eagle4_b200.models.configs import DraftConfig
+
+
+@dataclass
+class DraftCache:
+    block_table: torch.Tensor
+    page: int
+    k: torch.Tensor  # [slots, Hkv, D]
+    v: torch.Tensor
+
+    @classmethod
+    def allocate(cls, cfg: DraftConfig, block_table: torch.Tensor, page: int, device, dtype) -> "DraftCache":
+        slots = block_table.numel() * page
+        k = torch.zeros(slots, cfg.num_kv_heads, cfg.head_dim, dtype=dtype, device=device)
+        return cls(block_table, page, k, torch.zeros_like(k))
+
+
+class _AttnShape:
+    """The attention fields ``ops.qkv_prepare`` reads, for the draft layer."""
+
+    def __init__(self, cfg: DraftConfig):
+        self.num_heads = cfg.num_heads
+        self.num_kv_heads = cfg.num_kv_heads
+        self.head_dim = cfg.head_dim
+        self.attn_output_gate = False
+        self.rms_norm_eps = cfg.rms_norm_eps
+        self.norm_offset = False
+        self.rotary_dim = cfg.head_dim if cfg.use_rope else 0
+        self.rope_theta = cfg.rope_theta
+
+
+class DraftModel:
+    def __init__(self, cfg: DraftConfig, weights: Dict[str, torch.Tensor]):
+        self.cfg = cfg
+        self.w = weights
+        self.attn_shape = _AttnShape(cfg)
+        self.device = weights["fc"].device
+
+    def project(self, aux: torch.Tensor) -> torch.Tensor:
+        """Target aux hidden states ``[T, n*H_t]`` -> draft hidden ``[T, H]``."""
+        cfg, w = self.cfg, self.w
+        if cfg.fc_norm:
+            ht = cfg.target_hidden_size
+            parts = [ops.rmsnorm(aux[:, j * ht:(j + 1) * ht], w[f"fc_norm.{j}"], cfg.rms_norm_eps, False)
+                     for j in range(cfg.num_aux)]
+            aux = torch.cat(parts, dim=-1)
+        return ops.linear(aux, w["fc"])
+
+    def forward(self, ids: torch.Tensor, hidden: torch.Tensor, pos: torch.Tensor, req: torch.Tensor,
+                write_slot: torch.Tensor, ctx_start: torch.Tensor, ctx_len: torch.Tensor, extra: torch.Tensor,
+                n_extra: torch.Tensor, cache: DraftCache) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Returns ``(normed [T, H], next hidden [T, H])``."""
+        cfg, w = self.cfg, self.w
+        eps = cfg.rms_norm_eps
+        e = ops.embedding(ids, w["embed"])
+        x = ops.concat_norms(e, hidden, w["input_layernorm"], w["hidden_norm"], eps)
+        qkv = ops.linear(x, w["qkv"])
+        q, _ = ops.qkv_prepare(qkv, self.attn_shape, pos, write_slot, cache.k, cache.v, None, None)
+        o = ops.attention(q, cache.k, cache.v, cache.block_table, cache.page, req, ctx_start, ctx_len, extra,
+                          n_extra, cfg.head_dim ** -0.5)
+        residual = ops.linear_residual(o.reshape(o.shape[0], -1), w["o_proj"], hidden)
+        x = ops.rmsnorm(residual, w["post_attention_layernorm"], eps, False)
+        summed = ops.linear_residual(ops.linear_swiglu(x, w["gate_up"]), w["down"], residual)
+        normed = ops.rmsnorm(summed, w["norm"], eps, False)
+        return normed, (normed if cfg.norm_output else summed)
+
+    def candidates(self, normed: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Top-``k`` children per row: ``(probs fp32 [T, k], target token ids int64 [T, k])``."""
+        cfg, w = self.cfg, self.w
+        if cfg.low_rank:
+            probs, ids = ops.candidate_head(normed, w["lr_down"], w["lr_scores"], w["lm_head"],
+                                            cfg.num_candidates, k)
+        else:
+            probs, ids = ops.full_head_topk(normed, w["lm_head"], k)
+        if "d2t" in w:
+            ids = w["d2t"][ids]
+        return probs, ids
+
+    def candidate_logits(self, normed: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Candidate ids and their exact fp32 logits (the distribution sampled trees draw from)."""
+        cfg, w = self.cfg, self.w
+        if cfg.low_rank:
+            ids, logit = ops.candidate_logits(normed, w["lr_down"], w["lr_scores"], w["lm_head"], cfg.num_candidates)
+        else:
+            logit = ops.logits(normed, w["lm_head"])
+            ids = torch.arange(logit.shape[1], device=logit.device).expand_as(logit)
+        if "d2t" in w:
+            ids = w["d2t"][ids]
+        return ids, logit

@@ -1,0 +1,229 @@
+"""Target language models for verification and plain decode.
+
+One class serves the three target families of the configs (see ``configs.TargetConfig``). Weights are held as plain
+tensors in fused layouts chosen for the sm_100a kernels:
+
+* GDN ``in_proj``: ``[qkv | z | b | a]`` rows in one matrix (one GEMM per layer);
+* attention ``qkv``: ``[q | gate | k | v]`` (the Qwen3.5 per-head ``[q_h, gate_h]`` interleave is undone at load);
+* MLP ``gate_up``: gate and up rows interleaved in 64-row blocks so the GEMM epilogue applies SwiGLU in-tile;
+* the block's output projection (``o_proj`` / ``out_proj`` / ``down``) adds the residual in its epilogue.
+
+Every forward takes a ``RowBatch`` (the rows' positions, KV slots, visible context and tree links), so prefill,
+tree verify and plain decode are the same code; plain decode is a verify of one row.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional
+
+import torch
+
+from eagle4_b200 import ops
+from eagle4_b200.models.configs import TargetConfig
+
+
+@dataclass
+class RowBatch:
+    """Per-row metadata of one forward (T rows). All tensors live on the model's device."""
+
+    ids: torch.Tensor  # [T] int64 token ids
+    pos: torch.Tensor  # [T] int64 logical positions (RoPE)
+    req: torch.Tensor  # [T] int32 request row in the block table
+    write_slot: torch.Tensor  # [T] int64 physical KV slot this row writes
+    ctx_start: torch.Tensor  # [T] int32 first visible committed position
+    ctx_len: torch.Tensor  # [T] int32 end of the visible committed positions
+    extra: torch.Tensor  # [T, X] int32 extra visible physical slots (ancestors, then itself)
+    n_extra: torch.Tensor  # [T] int32
+    parent: torch.Tensor  # [T] int32 parent row inside this forward (-1: the committed state)
+    state_slot: torch.Tensor  # [T] int32 recurrent-state slot of the row's request
+    scan: bool = False  # recurrent layers update their state in place row by row (prefill chains)
+
+    @property
+    def num_rows(self) -> int:
+        return self.ids.shape[0]
+
+
+@dataclass
+class TargetCache:
+    """KV pages for attention layers and per-slot recurrent state for GDN / Mamba2 layers."""
+
+    block_table: torch.Tensor  # [max_reqs, max_blocks] int32
+    page: int
+    k: List[torch.Tensor]  # per attention layer [slots, Hkv, D]
+    v: List[torch.Tensor]
+    conv: List[torch.Tensor]  # per recurrent layer [state_slots, C, K-1]
+    ssm: List[torch.Tensor]  # per recurrent layer, fp32 ([slots, HV, V, K] GDN or [slots, H, P, N] Mamba2)
+
+    @classmethod
+    def allocate(cls, cfg: TargetConfig, *, max_reqs: int, max_len: int, page: int, device, dtype,
+                 state_slots: Optional[int] = None) -> "TargetCache":
+        blocks_per_req = (max_len + page - 1) // page
+        nblocks = max_reqs * blocks_per_req
+        bt = torch.arange(nblocks, dtype=torch.int32, device=device).view(max_reqs, blocks_per_req)
+        slots = nblocks * page
+        nattn = len(cfg.layer_ids("attn"))
+        k = [torch.zeros(slots, cfg.num_kv_heads, cfg.head_dim, dtype=dtype, device=device) for _ in range(nattn)]
+        v = [torch.zeros_like(t) for t in k]
+        ns = state_slots or max_reqs
+        conv, ssm = [], []
+        kw = cfg.conv_kernel
+        for m, _ in cfg.layers:
+            if m == "gdn":
+                conv.append(torch.zeros(ns, cfg.gdn_conv_dim, kw - 1, dtype=dtype, device=device))
+                ssm.append(torch.zeros(ns, cfg.gdn_v_heads, cfg.gdn_v_dim, cfg.gdn_k_dim, dtype=torch.float32,
+                                       device=device))
+            elif m == "mamba":
+                conv.append(torch.zeros(ns, cfg.mamba_conv_dim, kw - 1, dtype=dtype, device=device))
+                ssm.append(torch.zeros(ns, cfg.mamba_heads, cfg.mamba_head_dim, cfg.mamba_state,
+                                       dtype=torch.float32, device=device))
+        return cls(bt, page, k, v, conv, ssm)
+
+    def reset_slot(self, slot: int) -> None:
+        for t in self.conv:
+            t[slot].zero_()
+        for t in self.ssm:
+            t[slot].zero_()
+
+
+@dataclass
+class Records:
+    """What a tree verify keeps per recurrent layer so the accepted path can be committed afterwards."""
+
+    x_pre: List[torch.Tensor] = field(default_factory=list)  # conv inputs [T, C]
+    conv_out: List[torch.Tensor] = field(default_factory=list)  # post-conv [T, C]
+    gate_a: List[torch.Tensor] = field(default_factory=list)  # GDN g [T, HV] fp32 / Mamba2 raw dt [T, H]
+    gate_b: List[torch.Tensor] = field(default_factory=list)  # GDN beta [T, HV] fp32 / unused for Mamba2
+
+
+class TargetModel:
+    def __init__(self, cfg: TargetConfig, weights: Dict[str, torch.Tensor], *, aux_layer_ids=()):
+        self.cfg = cfg
+        self.w = weights
+        self.aux_layer_ids = tuple(aux_layer_ids)
+        self.device = weights["embed"].device
+        self.dtype = weights["embed"].dtype
+        # cache index of each layer inside its kind's list
+        self.attn_index: Dict[int, int] = {}
+        self.rec_index: Dict[int, int] = {}
+        for i, (m, _) in enumerate(cfg.layers):
+            if m == "attn":
+                self.attn_index[i] = len(self.attn_index)
+            elif m in ("gdn", "mamba"):
+                self.rec_index[i] = len(self.rec_index)
+
+    # ------------------------------------------------------------------ blocks
+    def _attn(self, i: int, x: torch.Tensor, h: torch.Tensor, rb: RowBatch, cache: TargetCache) -> torch.Tensor:
+        cfg, w = self.cfg, self.w
+        li = self.attn_index[i]
+        qkv = ops.linear(x, w[f"l{i}.qkv"])
+        q, gate = ops.qkv_prepare(qkv, cfg, rb.pos, rb.write_slot, cache.k[li], cache.v[li],
+                                  w.get(f"l{i}.q_norm"), w.get(f"l{i}.k_norm"))
+        o = ops.attention(q, cache.k[li], cache.v[li], cache.block_table, cache.page, rb.req, rb.ctx_start,
+                          rb.ctx_len, rb.extra, rb.n_extra, cfg.head_dim ** -0.5)
+        o = o.reshape(o.shape[0], -1)
+        if gate is not None:
+            o = ops.sigmoid_gate(o, gate)
+        return ops.linear_residual(o, w[f"l{i}.o_proj"], h)
+
+    def _gdn(self, i: int, x: torch.Tensor, h: torch.Tensor, rb: RowBatch, cache: TargetCache,
+             rec: Optional[Records]) -> torch.Tensor:
+        cfg, w = self.cfg, self.w
+        ri = self.rec_index[i]
+        cd, vd, hv = cfg.gdn_conv_dim, cfg.gdn_value_dim, cfg.gdn_v_heads
+        proj = ops.linear(x, w[f"l{i}.in_proj"])
+        x_pre = proj[:, :cd]
+        z = proj[:, cd: cd + vd]
+        b = proj[:, cd + vd: cd + vd + hv]
+        a = proj[:, cd + vd + hv: cd + vd + 2 * hv]
+        conv = ops.causal_conv_tree(x_pre, cache.conv[ri], rb.state_slot, rb.parent, w[f"l{i}.conv"])
+        g, beta = ops.gdn_gates(a, b, w[f"l{i}.A_log"], w[f"l{i}.dt_bias"])
+        o = ops.gdn_tree(conv, g, beta, cache.ssm[ri], rb.state_slot, rb.parent, cfg, rb.scan)
+        if rb.scan:
+            ops.conv_commit_scan(cache.conv[ri], x_pre, rb.state_slot, cfg.conv_kernel)
+        elif rec is not None:
+            rec.x_pre.append(x_pre)
+            rec.conv_out.append(conv)
+            rec.gate_a.append(g)
+            rec.gate_b.append(beta)
+        o = ops.gated_rmsnorm(o, z, w[f"l{i}.gnorm"], cfg.rms_norm_eps)
+        return ops.linear_residual(o, w[f"l{i}.out_proj"], h)
+
+    def _mamba(self, i: int, x: torch.Tensor, h: torch.Tensor, rb: RowBatch, cache: TargetCache,
+               rec: Optional[Records]) -> torch.Tensor:
+        cfg, w = self.cfg, self.w
+        ri = self.rec_index[i]
+        inner, cd, nh = cfg.mamba_inner, cfg.mamba_conv_dim, cfg.mamba_heads
+        proj = ops.linear(x, w[f"l{i}.in_proj"])
+        z = proj[:, :inner]
+        x_pre = proj[:, inner: inner + cd]
+        dt = proj[:, inner + cd: inner + cd + nh]
+        conv = ops.causal_conv_tree(x_pre, cache.conv[ri], rb.state_slot, rb.parent, w[f"l{i}.conv"])
+        y = ops.mamba_tree(conv, dt, w[f"l{i}.A_log"], w[f"l{i}.dt_bias"], w[f"l{i}.D"], cache.ssm[ri],
+                           rb.state_slot, rb.parent, cfg, rb.scan)
+        if rb.scan:
+            ops.conv_commit_scan(cache.conv[ri], x_pre, rb.state_slot, cfg.conv_kernel)
+        elif rec is not None:
+            rec.x_pre.append(x_pre)
+            rec.conv_out.append(conv)
+            rec.gate_a.append(dt)
+            rec.gate_b.append(dt)
+        group = cfg.mamba_inner // cfg.mamba_groups
+        y = ops.gated_rmsnorm(y.reshape(y.shape[0], cfg.mamba_groups, group), z, w[f"l{i}.gnorm"], cfg.rms_norm_eps)
+        return ops.linear_residual(y, w[f"l{i}.out_proj"], h)
+
+    def _mlp(self, i: int, x: torch.Tensor, h: torch.Tensor, kind: str) -> torch.Tensor:
+        w = self.w
+        if kind == "swiglu":
+            a = ops.linear_swiglu(x, w[f"l{i}.gate_up"])
+        else:
+            a = ops.linear_relu2(x, w[f"l{i}.up"])
+        return ops.linear_residual(a, w[f"l{i}.down"], h)
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, rb: RowBatch, cache: TargetCache, rec: Optional[Records] = None):
+        """Returns ``(final normed hidden [T, H], aux hidden [T, n_aux * H] or None)``."""
+        cfg, w = self.cfg, self.w
+        eps, off = cfg.rms_norm_eps, cfg.norm_offset
+        h = ops.embedding(rb.ids, w["embed"])
+        aux = []
+        for i, (mixer, mlp) in enumerate(cfg.layers):
+            if mixer is not None:
+                x = ops.rmsnorm(h, w[f"l{i}.norm1"], eps, off)
+                if mixer == "attn":
+                    h = self._attn(i, x, h, rb, cache)
+                elif mixer == "gdn":
+                    h = self._gdn(i, x, h, rb, cache, rec)
+                else:
+                    h = self._mamba(i, x, h, rb, cache, rec)
+            if mlp is not None:
+                x = ops.rmsnorm(h, w[f"l{i}.norm2"], eps, off)
+                h = self._mlp(i, x, h, mlp)
+            if i in self.aux_layer_ids:
+                aux.append(h)
+        out = ops.rmsnorm(h, w["norm"], eps, off)
+        return out, (torch.cat(aux, dim=-1) if aux else None)
+
+    def greedy(self, hidden: torch.Tensor):
+        return ops.lm_head_argmax(hidden, self.w["lm_head"])
+
+    def logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        return ops.logits(hidden, self.w["lm_head"])
+
+    # ------------------------------------------------------------------ commit
+    def commit(self, cache: TargetCache, rec: Records, rows: torch.Tensor, n_rows: torch.Tensor,
+               slots: torch.Tensor, src_kv: torch.Tensor, dst_kv: torch.Tensor) -> None:
+        """Commit the accepted rows: recurrent state replay along the path and KV moves in attention layers."""
+        cfg, w = self.cfg, self.w
+        for i, (m, _) in enumerate(cfg.layers):
+            if m not in ("gdn", "mamba"):
+                continue
+            ri = self.rec_index[i]
+            if m == "gdn":
+                ops.gdn_commit(rec.conv_out[ri], rec.gate_a[ri], rec.gate_b[ri], rec.x_pre[ri], cache.ssm[ri],
+                               cache.conv[ri], slots, rows, n_rows, cfg)
+            else:
+                ops.mamba_commit(rec.conv_out[ri], rec.gate_a[ri], w[f"l{i}.A_log"], w[f"l{i}.dt_bias"],
+                                 w[f"l{i}.D"], rec.x_pre[ri], cache.ssm[ri], cache.conv[ri], slots, rows, n_rows, cfg)
+        if cache.k:
+            ops.kv_commit(cache.k, cache.v, src_kv, dst_kv)

@@ -1,0 +1,147 @@
+"""Op entry points used by the models and runtime.
+
+Tensors on a CUDA device run this package's sm_100a kernels (``eagle4_b200/csrc``, loaded by
+``eagle4_b200.ops.native``); CPU tensors run the PyTorch definitions in ``eagle4_b200.ops.reference``, which are also
+the oracle of the kernel tests. There is no other backend: on a GPU a missing extension is an error, never a silent
+fallback.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from eagle4_b200.ops import reference as ref
+
+
+def _cuda(x: torch.Tensor) -> bool:
+    return x.is_cuda
+
+
+def _nat():
+    from eagle4_b200.ops import native
+
+    return native
+
+
+# dense -----------------------------------------------------------------------------------------------------------
+def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    return _nat().linear(x, w) if _cuda(x) else ref.linear(x, w)
+
+
+def linear_residual(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+    return _nat().linear_residual(x, w, residual) if _cuda(x) else ref.linear_residual(x, w, residual)
+
+
+def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor) -> torch.Tensor:
+    return _nat().linear_swiglu(x, w_gu) if _cuda(x) else ref.linear_swiglu(x, w_gu)
+
+
+def linear_relu2(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    return _nat().linear_relu2(x, w) if _cuda(x) else ref.linear_relu2(x, w)
+
+
+def lm_head_argmax(x: torch.Tensor, w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    return _nat().lm_head_argmax(x, w) if _cuda(x) else ref.lm_head_argmax(x, w)
+
+
+def logits(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    return _nat().logits(x, w) if _cuda(x) else ref.logits(x, w)
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, offset: bool) -> torch.Tensor:
+    return _nat().rmsnorm(x, w, eps, offset) if _cuda(x) else ref.rmsnorm(x, w, eps, offset)
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
+    return _nat().embedding(ids, table) if _cuda(table) else ref.embedding(ids, table)
+
+
+def sigmoid_gate(o: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
+    return _nat().sigmoid_gate(o, gate) if _cuda(o) else ref.sigmoid_gate(o, gate)
+
+
+def concat_norms(e, h, we, wh, eps: float) -> torch.Tensor:
+    return _nat().concat_norms(e, h, we, wh, eps) if _cuda(e) else ref.concat_norms(e, h, we, wh, eps)
+
+
+# attention -------------------------------------------------------------------------------------------------------
+def qkv_prepare(qkv, cfg, pos, write_slot, k_cache, v_cache, q_norm, k_norm):
+    if _cuda(qkv):
+        return _nat().qkv_prepare(qkv, cfg, pos, write_slot, k_cache, v_cache, q_norm, k_norm)
+    return ref.qkv_prepare(qkv, cfg, pos, write_slot, k_cache, v_cache, q_norm, k_norm)
+
+
+def attention(q, k_cache, v_cache, block_table, page, req, ctx_start, ctx_len, extra, n_extra, scale):
+    fn = _nat().attention if _cuda(q) else ref.attention
+    return fn(q, k_cache, v_cache, block_table, page, req, ctx_start, ctx_len, extra, n_extra, scale)
+
+
+# recurrent -------------------------------------------------------------------------------------------------------
+def causal_conv_tree(x, conv_state, state_slot, parent, weight):
+    fn = _nat().causal_conv_tree if _cuda(x) else ref.causal_conv_tree
+    return fn(x, conv_state, state_slot, parent, weight)
+
+
+def gdn_gates(a, b, a_log, dt_bias):
+    return _nat().gdn_gates(a, b, a_log, dt_bias) if _cuda(a) else ref.gdn_gates(a, b, a_log, dt_bias)
+
+
+def gdn_tree(qkv, g, beta, state, state_slot, parent, cfg, scan: bool):
+    fn = _nat().gdn_tree if _cuda(qkv) else ref.gdn_tree
+    return fn(qkv, g, beta, state, state_slot, parent, cfg, scan)
+
+
+def gdn_commit(qkv, g, beta, x_pre, state, conv_state, slots, rows, n_rows, cfg):
+    fn = _nat().gdn_commit if _cuda(qkv) else ref.gdn_commit
+    return fn(qkv, g, beta, x_pre, state, conv_state, slots, rows, n_rows, cfg)
+
+
+def conv_commit_scan(conv_state, x_pre, state_slot, kw):
+    fn = _nat().conv_commit_scan if _cuda(x_pre) else ref.conv_commit_scan
+    return fn(conv_state, x_pre, state_slot, kw)
+
+
+def gated_rmsnorm(o, z, w, eps):
+    return _nat().gated_rmsnorm(o, z, w, eps) if _cuda(o) else ref.gated_rmsnorm(o, z, w, eps)
+
+
+def mamba_tree(xbc, dt_raw, a_log, dt_bias, d_skip, state, state_slot, parent, cfg, scan: bool):
+    fn = _nat().mamba_tree if _cuda(xbc) else ref.mamba_tree
+    return fn(xbc, dt_raw, a_log, dt_bias, d_skip, state, state_slot, parent, cfg, scan)
+
+
+def mamba_commit(xbc, dt_raw, a_log, dt_bias, d_skip, x_pre, state, conv_state, slots, rows, n_rows, cfg):
+    fn = _nat().mamba_commit if _cuda(xbc) else ref.mamba_commit
+    return fn(xbc, dt_raw, a_log, dt_bias, d_skip, x_pre, state, conv_state, slots, rows, n_rows, cfg)
+
+
+def kv_commit(k_caches, v_caches, src_slots, dst_slots):
+    fn = _nat().kv_commit if _cuda(src_slots) else ref.kv_commit
+    return fn(k_caches, v_caches, src_slots, dst_slots)
+
+
+# draft head ------------------------------------------------------------------------------------------------------
+def candidate_head(h, down, scores_w, lm_head, num_candidates: int, k: int):
+    fn = _nat().candidate_head if _cuda(h) else ref.candidate_head
+    return fn(h, down, scores_w, lm_head, num_candidates, k)
+
+
+def candidate_logits(h, down, scores_w, lm_head, num_candidates: int):
+    fn = _nat().candidate_logits if _cuda(h) else ref.candidate_logits
+    return fn(h, down, scores_w, lm_head, num_candidates)
+
+
+def full_head_topk(h, lm_head, k: int):
+    return _nat().full_head_topk(h, lm_head, k) if _cuda(h) else ref.full_head_topk(h, lm_head, k)
+
+
+def topk_rows(scores, k: int):
+    return _nat().topk_rows(scores, k) if _cuda(scores) else ref.topk_rows(scores, k)
+
+
+# acceptance ------------------------------------------------------------------------------------------------------
+def accept_greedy(target_ids, tokens, parent_rows, n_rows):
+    fn = _nat().accept_greedy if _cuda(tokens) else ref.accept_greedy
+    return fn(target_ids, tokens, parent_rows, n_rows)
