@@ -1,0 +1,208 @@
+#!/usr/bin/env python
+"""Headline benchmark: EAGLE-4 output tokens/s and speedup over plain decoding.
+
+Config (the benchmark plan's config 2): a Qwen3.8-27B-shaped hybrid target (64 layers, 3 GDN : 1 gated attention,
+hidden 5120, vocab 248320) in bf16 with random-init weights, a one-layer EAGLE-4 draft head (H 5120, 40x128 heads,
+FFN 16384, rank-128 candidate head), tree steps 12 / top-k 4 / 16 draft tokens, batch 1 per GPU, a 1024-token
+uniform-random prompt and 256 greedy output tokens. One step = one whole generation (prefill + 256 tokens).
+
+  python bench.py --gpus N --steps K --warmup W            # this framework
+  python bench.py --impl reference ...                     # the reference's own serving path
+
+With N > 1 (launched by torch.distributed.run) every rank serves its own batch (data-parallel replicas, weak
+scaling); the device time is the max over ranks. Prints one JSON line on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+BASELINE_TPS = 302.7  # SGLang TP1, one request, EAGLE-4 tokens/s on 1x B300 (reference docs/support-matrix.md:258-259)
+METRIC = "EAGLE-4 output tok/s and speedup vs plain decode, batch 1–512, TP 1/2/4/8"
+
+
+def reference_unavailable() -> str:
+    return ("eagle-harness is an engine plugin: its serving path needs SGLang or TokenSpeed with its hooks, or "
+            "vLLM>=0.32 (installed: vllm 0.22, no sglang, no tokenspeed), so it cannot generate on this box")
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                self.rows.append([x.strip() for x in out.stdout.strip().split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self) -> dict:
+        mhz = sorted(float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit())
+        mx = max((float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()), default=None)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) >= 9 for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": mhz[len(mhz) // 2] if mhz else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(mhz)}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="qwen3.8-27b")
+    ap.add_argument("--prompt", type=int, default=1024)
+    ap.add_argument("--new-tokens", type=int, default=256)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--no-plain", action="store_true", help="skip the plain-decode arm")
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": reference_unavailable()}))
+        return
+
+    import torch
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+
+    from eagle4_b200.api import LLM, TreeSpec
+    from eagle4_b200.ops import native
+
+    dev = torch.device("cuda", local)
+    tree = TreeSpec(12, 4, 16)
+    llm = LLM.synthetic(args.model, device=dev, seed=0, tree=tree, max_batch=args.batch,
+                        max_len=args.prompt + args.new_tokens + 64)
+    gen = torch.Generator().manual_seed(1234 + rank)
+    prompts = torch.randint(0, llm.target.cfg.vocab_size, (args.batch, args.prompt), generator=gen).pin_memory()
+    eng = llm.engine
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def device_timed(speculative: bool):
+        dev_prompts = prompts.to(dev)
+        for _ in range(args.warmup):
+            eng.generate(dev_prompts, args.new_tokens, speculative=speculative)
+        barrier()
+        torch.cuda.synchronize()
+        eng.stats.__init__()
+        native.LAUNCHES[0] = 0
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            s.record()
+            outs = [eng.generate(dev_prompts, args.new_tokens, speculative=speculative) for _ in range(args.steps)]
+            e.record()
+            torch.cuda.synchronize()
+        barrier()
+        ms = max_over_ranks(s.elapsed_time(e))
+        toks = sum(len(o) for out in outs for o in out)
+        return ms, toks, clk.summary(), native.LAUNCHES[0], eng.stats.mean_accept, outs
+
+    spec_ms, spec_tok, clocks, launches, accept, spec_out = device_timed(True)
+    plain_ms = plain_tok = None
+    if not args.no_plain:
+        plain_ms, plain_tok, _, _, _, plain_out = device_timed(False)
+        same = plain_out[0] == spec_out[0]
+    else:
+        same = None
+
+    # end to end through the public API: pinned prompt H2D and generated ids D2H inside the timed region
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e2e_tok = 0
+    for _ in range(args.steps):
+        out = llm.generate(prompts, args.new_tokens, speculative=True)
+        e2e_tok += out.numel()
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    native.check_errors(dev)
+
+    total_tok = spec_tok * world
+    value = total_tok / (spec_ms / 1e3)
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(spec_ms / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": round(value / BASELINE_TPS, 4),
+        "dtype": "bf16",
+        "data": "synthetic: uniform-random prompt ids, random-init N(0,0.02) weights of the named shapes",
+        "config": {
+            "model": "Qwen3.8-27B-shaped hybrid (64 layers, 3 GDN:1 attention) + 1-layer EAGLE-4 draft",
+            "global_batch": args.batch * world, "seq_len": args.prompt, "new_tokens": args.new_tokens,
+            "tree": {"steps": tree.steps, "top_k": tree.top_k, "draft_tokens": tree.draft_tokens},
+            "parallelism": f"dp{world}" if world > 1 else "tp1",
+            "l2": "inputs larger than L2: every forward streams the 54 GB of target weights",
+        },
+        "speculative_tok_s": round(value, 2),
+        "plain_tok_s": round(plain_tok * world / (plain_ms / 1e3), 2) if plain_ms else None,
+        "speedup_vs_plain": round((spec_tok / spec_ms) / (plain_tok / plain_ms), 4) if plain_ms else None,
+        "mean_accepted_per_round": round(accept, 3),
+        "spec_equals_plain": same,
+        "clocks": clocks,
+        "e2e": {"value": round(e2e_tok * world / e2e_s, 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(prompts.numel() * prompts.element_size()),
+                "d2h_bytes_per_step": int(args.batch * args.new_tokens * 8)},
+        "gpu_launches": launches,
+    }
+    if rank == 0:
+        print(json.dumps(line))
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,475 @@
+// Skinny bf16 GEMM for sm_100a: Y[T, N] = X[T, K] . W[N, K]^T with fused epilogues.
+//
+// Decode and tree-verify GEMMs have few tokens (T <= 256 per launch) and large weights, so the kernel is
+// weight-streaming: the MMA's M dimension walks the weight rows (128 per tile) and the tokens are its N dimension
+// ("swap AB"). One persistent CTA per SM, warp-specialised:
+//   warp 0      TMA producer: W tile [128 x 64] (evict-first) and X tile [NT x 64] (evict-last) per stage
+//   warp 1      TMEM owner and UMMA issuer (tcgen05.mma kind::f16, M=128, N=NT, K=16 per instruction)
+//   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator, fused op, global store
+// Two TMEM accumulators let the epilogue of one work unit overlap the MMAs of the next.
+//
+// A work unit is (weight tile, K split). The split count depends only on (N, K) and the token tile only on T, and
+// every output element's reduction order is fixed by the split boundaries, so a row's result is the same whatever
+// other rows share the launch (plain decode and tree verify give identical logits). Split partials are reduced by
+// the last-arriving CTA of a tile in split order (no atomics on data, no spinning).
+//
+// Epilogues: plain bf16 store; residual add; SwiGLU over gate/up rows interleaved in 64-row blocks; squared ReLU;
+// fp32 store; and a per-tile (max, argmax) for the vocabulary-parallel greedy head.
+#include <cudaTypedefs.h>
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+
+namespace e4 {
+namespace gemm {
+
+enum Epi : int { kPlain = 0, kResidual = 1, kSwiGLU = 2, kReLU2 = 3, kF32 = 4, kArgmax = 5 };
+
+constexpr int kThreads = 192;
+constexpr int kTileM = 128;
+constexpr int kTileK = 64;
+constexpr int kWTileBytes = kTileM * kTileK * 2;
+
+struct Params {
+  int T, N, K;
+  int nt;           // token tile (MMA N): multiple of 16, <= 256
+  int n_tiles;      // ceil(N / 128)
+  int kb_total;     // ceil(K / 64) k-blocks per tile
+  long total;       // n_tiles * kb_total: the linear k-block space split evenly over the CTAs (stream-K)
+  int stages;
+  int epi;
+  __nv_bfloat16* y;  // [T, ldy] bf16 output (plain / residual / swiglu / relu2)
+  float* yf;         // [T, ldy] fp32 output (kF32)
+  int ldy;
+  const __nv_bfloat16* res;  // residual [T, ldr]
+  int ldr;
+  float* ws;         // partial tiles [2 * grid][nt][128]
+  int* counters;     // [n_tiles] arrival counters (zero between launches)
+  float* amax_val;   // [n_tiles][T] per-tile max (kArgmax)
+  int* amax_idx;     // [n_tiles][T]
+  int* err;
+};
+
+// Stream-K partition: CTA c owns linear k-blocks [start(c), start(c+1)) of the (tile, k-block) space; a tile is
+// split into "pieces" where CTA ranges cut it. The cut points depend only on (N, K, grid), never on T.
+__device__ __forceinline__ long sk_start(const Params& p, int c) { return (long(c) * p.total) / gridDim.x; }
+__device__ __forceinline__ int sk_owner(const Params& p, long g) {  // CTA whose range contains k-block g
+  return int(((g + 1) * long(gridDim.x) - 1) / p.total);
+}
+
+struct Piece {
+  int tile, kb0, kb1;
+};
+
+// Partial-tile slot of CTA ``c`` for ``tile``: each CTA has at most two partial pieces, the tile its range starts in
+// (slot 2c) and the tile it ends in (slot 2c + 1).
+__device__ __forceinline__ int ws_slot(const Params& p, int c, int tile) {
+  const int first_tile = int(sk_start(p, c) / p.kb_total);
+  return 2 * c + (tile == first_tile ? 0 : 1);
+}
+
+// Next piece of this CTA's range at linear position ``g`` (< end).
+__device__ __forceinline__ Piece next_piece(const Params& p, long g, long end) {
+  Piece pc;
+  pc.tile = int(g / p.kb_total);
+  pc.kb0 = int(g - long(pc.tile) * p.kb_total);
+  const long tile_end = long(pc.tile + 1) * p.kb_total;
+  pc.kb1 = int((end < tile_end ? end : tile_end) - long(pc.tile) * p.kb_total);
+  return pc;
+}
+
+// Final epilogue of 16 token columns [j0, j0+16) held by this thread for weight row ``m`` of ``tile``.
+__device__ __forceinline__ void store_chunk(const Params& p, int tile, int m, int j0, const float* v, float* xchg,
+                                            int ep_tid) {
+  const int n = tile * kTileM + m;
+  if (p.epi == kSwiGLU) {
+    // rows [0,64) are gate, [64,128) the matching up rows; output feature tile*64 + (m & 63)
+    if (m >= 64) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) xchg[i * 64 + (m - 64)] = v[i];
+    }
+    named_bar(1, 128);
+    if (m < 64) {
+      const int f = tile * 64 + m;
+      if (f < p.N / 2) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int j = j0 + i;
+          if (j < p.T) p.y[size_t(j) * p.ldy + f] = __float2bfloat16(silu(v[i]) * xchg[i * 64 + m]);
+        }
+      }
+    }
+    named_bar(1, 128);
+    return;
+  }
+  if (p.epi == kArgmax) {
+    // per token: max over the 128 rows of the tile, ties to the lower row
+    const int warp = ep_tid >> 5, lane = ep_tid & 31;
+    float* sv = xchg;                                      // [4 warps][16]
+    int* si = reinterpret_cast<int*>(xchg + 64);           // [4 warps][16]
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float best = (n < p.N) ? v[i] : -INFINITY;
+      int bi = n;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+      }
+      if (lane == 0) { sv[warp * 16 + i] = best; si[warp * 16 + i] = bi; }
+    }
+    named_bar(1, 128);
+    if (ep_tid < 16) {
+      const int j = j0 + ep_tid;
+      float best = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int w = 0; w < 4; ++w) {
+        const float ov = sv[w * 16 + ep_tid];
+        const int oi = si[w * 16 + ep_tid];
+        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+      }
+      if (j < p.T) {
+        p.amax_val[size_t(tile) * p.T + j] = best;
+        p.amax_idx[size_t(tile) * p.T + j] = bi;
+      }
+    }
+    named_bar(1, 128);
+    return;
+  }
+  if (n >= p.N) return;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int j = j0 + i;
+    if (j >= p.T) break;
+    float a = v[i];
+    if (p.epi == kF32) {
+      p.yf[size_t(j) * p.ldy + n] = a;
+      continue;
+    }
+    if (p.epi == kResidual) a += __bfloat162float(p.res[size_t(j) * p.ldr + n]);
+    if (p.epi == kReLU2) { a = fmaxf(a, 0.f); a = a * a; }
+    p.y[size_t(j) * p.ldy + n] = __float2bfloat16(a);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x, Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // carve: [stages x (W tile | X tile)] 1024-aligned, then barriers, TMEM handle, exchange buffer
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int x_bytes = p.nt * kTileK * 2;
+  const int stage_bytes = kWTileBytes + x_bytes;
+  uint8_t* tiles = base;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(tiles + p.stages * stage_bytes);
+  uint64_t* empty_bar = full_bar + p.stages;
+  uint64_t* acc_full = empty_bar + p.stages;   // [2]
+  uint64_t* acc_empty = acc_full + 2;          // [2]
+  uint32_t* tmem_handle = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  int* flag = reinterpret_cast<int*>(tmem_handle + 1);
+  float* xchg = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(tmem_handle) + 64);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const long g_begin = sk_start(p, blockIdx.x), g_end = sk_start(p, blockIdx.x + 1);
+  const uint32_t tmem_cols_per_acc = p.nt;
+  uint32_t tmem_cols = 32;
+  while (tmem_cols < 2 * tmem_cols_per_acc) tmem_cols <<= 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
+    mbar_fence_init();
+    prefetch_tmap(&tmap_w);
+    prefetch_tmap(&tmap_x);
+  }
+  if (warp == 1) tmem_alloc(tmem_handle, tmem_cols);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_handle;
+  bool ok = true;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      for (long g = g_begin; g < g_end && ok;) {
+        const Piece pc = next_piece(p, g, g_end);
+        g += pc.kb1 - pc.kb0;
+        for (int kb = pc.kb0; kb < pc.kb1; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { record_error(p.err, kErrTimeoutProducer); ok = false; break; }
+          uint8_t* st = tiles + stage * stage_bytes;
+          mbar_expect_tx(&full_bar[stage], stage_bytes);
+          tma_load_2d(st, &tmap_w, &full_bar[stage], kb * kTileK, pc.tile * kTileM, pol_w);
+          tma_load_2d(st + kWTileBytes, &tmap_x, &full_bar[stage], kb * kTileK, 0, pol_x);
+          if (++stage == p.stages) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kTileM, p.nt);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (long g = g_begin; g < g_end && ok; ++local) {
+        const Piece pc = next_piece(p, g, g_end);
+        g += pc.kb1 - pc.kb0;
+        const int kb0 = pc.kb0, kb1 = pc.kb1;
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1)) { record_error(p.err, kErrTimeoutMma); ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * tmem_cols_per_acc;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase)) { record_error(p.err, kErrTimeoutMma); ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(tiles + stage * stage_bytes);
+          const uint64_t adesc = sdesc_sw128(sa);
+          const uint64_t bdesc = sdesc_sw128(sa + kWTileBytes);
+#pragma unroll
+          for (int k = 0; k < kTileK / 16; ++k) {
+            umma_bf16(d_tmem, adesc + uint64_t(k * 2), bdesc + uint64_t(k * 2), idesc,
+                      (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == p.stages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[acc]);
+      }
+    }
+  } else {
+    // epilogue warps 2..5: TMEM lane quarter = warp % 4
+    const int ep_tid = threadIdx.x - 64;
+    const int quarter = warp & 3;
+    const int m = quarter * 32 + lane;
+    int local = 0;
+    for (long g = g_begin; g < g_end; ++local) {
+      const Piece pc = next_piece(p, g, g_end);
+      g += pc.kb1 - pc.kb0;
+      const int tile = pc.tile;
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[acc], acc_phase)) { record_error(p.err, kErrTimeoutEpilogue); break; }
+      tc_fence_after();
+      const uint32_t t_addr = tmem_base + (uint32_t(quarter * 32) << 16) + acc * tmem_cols_per_acc;
+      if (pc.kb0 == 0 && pc.kb1 == p.kb_total) {
+        for (int j0 = 0; j0 < p.nt; j0 += 16) {
+          float v[16];
+          tmem_ld16(t_addr + j0, v);
+          if (j0 + 16 >= p.nt) { tc_fence_before(); mbar_arrive(&acc_empty[acc]); }
+          store_chunk(p, tile, m, j0, v, xchg, ep_tid);
+        }
+      } else {
+        // partial tile: store this piece, then the last piece to arrive reduces all pieces in order
+        const long t0 = long(tile) * p.kb_total;
+        const int first_cta = sk_owner(p, t0);
+        const int pieces = sk_owner(p, t0 + p.kb_total - 1) - first_cta + 1;
+        float* part = p.ws + size_t(ws_slot(p, blockIdx.x, tile)) * p.nt * kTileM;
+        for (int j0 = 0; j0 < p.nt; j0 += 16) {
+          float v[16];
+          tmem_ld16(t_addr + j0, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) part[size_t(j0 + i) * kTileM + m] = v[i];
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+        named_bar(1, 128);
+        if (ep_tid == 0) {
+          int old;
+          asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.counters + tile) : "memory");
+          *flag = (old == pieces - 1);
+        }
+        named_bar(1, 128);
+        if (*flag) {
+          for (int j0 = 0; j0 < p.nt; j0 += 16) {
+            float v[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = 0.f;
+            for (int q = 0; q < pieces; ++q) {
+              const float* src = p.ws + size_t(ws_slot(p, first_cta + q, tile)) * p.nt * kTileM;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) v[i] += __ldcg(src + size_t(j0 + i) * kTileM + m);
+            }
+            store_chunk(p, tile, m, j0, v, xchg, ep_tid);
+          }
+          if (ep_tid == 0) p.counters[tile] = 0;
+        }
+        named_bar(1, 128);
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, tmem_cols);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    TORCH_CHECK(ptr != nullptr && q == cudaDriverEntryPointSuccess, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 2-D bf16 row-major [rows, cols] with row stride ``ld`` elements; box [box_cols=64, box_rows], 128-byte swizzle.
+CUtensorMap make_map(const void* ptr, int rows, int cols, int ld, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
+  cuuint32_t box[2] = {cuuint32_t(kTileK), cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", int(r));
+  return m;
+}
+
+struct MapKey {
+  const void* p;
+  int rows, cols, ld, box;
+  bool operator==(const MapKey& o) const {
+    return p == o.p && rows == o.rows && cols == o.cols && ld == o.ld && box == o.box;
+  }
+};
+struct MapHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<const void*>()(k.p) ^ (size_t(k.rows) << 1) ^ (size_t(k.cols) << 21) ^ (size_t(k.box) << 43);
+  }
+};
+
+const CUtensorMap& weight_map(const void* ptr, int rows, int cols, int ld) {
+  static std::unordered_map<MapKey, CUtensorMap, MapHash> cache;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> g(mu);
+  MapKey k{ptr, rows, cols, ld, kTileM};
+  auto it = cache.find(k);
+  if (it == cache.end()) it = cache.emplace(k, make_map(ptr, rows, cols, ld, kTileM)).first;
+  return it->second;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+struct Scratch {
+  torch::Tensor ws, counters, err;
+};
+Scratch& scratch(torch::Device dev) {
+  static std::unordered_map<int, Scratch> per_dev;
+  Scratch& s = per_dev[dev.index()];
+  if (!s.counters.defined()) {
+    auto o = torch::TensorOptions().device(dev);
+    s.counters = torch::zeros({1 << 16}, o.dtype(torch::kInt32));
+    s.err = torch::zeros({1}, o.dtype(torch::kInt32));
+    s.ws = torch::empty({1 << 22}, o.dtype(torch::kFloat32));
+  }
+  return s;
+}
+
+}  // namespace gemm
+
+torch::Tensor gemm_error_word(torch::Device dev) { return gemm::scratch(dev).err; }
+
+// Launch one GEMM over all T tokens (chunks of 256 tokens per launch).
+void gemm_launch(const torch::Tensor& x, const torch::Tensor& w, int epi, torch::Tensor y, torch::Tensor yf,
+                 const torch::Tensor& res, torch::Tensor amax_val, torch::Tensor amax_idx) {
+  using namespace gemm;
+  TORCH_CHECK(x.is_cuda() && w.is_cuda(), "gemm: CUDA tensors expected");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm: bf16 operands expected");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "gemm: shape mismatch");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1, "gemm: inner dimension must be contiguous");
+  TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "gemm: row strides must be 16-byte multiples");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0,
+              "gemm: operands must be 16-byte aligned");
+  const at::cuda::CUDAGuard guard(x.device());
+  const int T = x.size(0), K = x.size(1), N = w.size(0);
+  if (T == 0) return;
+  Scratch& sc = scratch(x.device());
+  const int sms = num_sms();
+  const int n_tiles = (N + kTileM - 1) / kTileM;
+  const int kb_total = (K + kTileK - 1) / kTileK;
+  const long total = long(n_tiles) * kb_total;
+  const int grid = int(std::min<long>(sms, total));
+  const CUtensorMap& wmap = weight_map(w.data_ptr(), N, K, w.stride(0));
+  auto stream = at::cuda::getCurrentCUDAStream();
+  TORCH_CHECK(n_tiles <= sc.counters.numel(), "gemm: too many weight tiles");
+  for (int t0 = 0; t0 < T; t0 += 256) {
+    const int tc = std::min(256, T - t0);
+    Params p{};
+    p.T = tc;
+    p.N = N;
+    p.K = K;
+    p.nt = std::max(16, (tc + 15) / 16 * 16);
+    p.n_tiles = n_tiles;
+    p.kb_total = kb_total;
+    p.total = total;
+    p.epi = epi;
+    const int stage_bytes = kWTileBytes + p.nt * kTileK * 2;
+    p.stages = std::min(10, (200 * 1024) / stage_bytes);
+    const size_t ws_need = size_t(2) * grid * p.nt * kTileM;
+    if (size_t(sc.ws.numel()) < ws_need) sc.ws = torch::empty({int64_t(ws_need)}, sc.ws.options());
+    p.ws = sc.ws.data_ptr<float>();
+    p.counters = sc.counters.data_ptr<int>();
+    p.err = sc.err.data_ptr<int>();
+    const __nv_bfloat16* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()) + size_t(t0) * x.stride(0);
+    CUtensorMap xmap = make_map(xp, tc, K, x.stride(0), p.nt);
+    auto has = [](const torch::Tensor& t) { return t.defined() && t.numel() > 0; };
+    if (has(y)) {
+      p.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr()) + size_t(t0) * y.stride(0);
+      p.ldy = y.stride(0);
+    }
+    if (has(yf)) {
+      p.yf = yf.data_ptr<float>() + size_t(t0) * yf.stride(0);
+      p.ldy = yf.stride(0);
+    }
+    if (has(res)) {
+      p.res = reinterpret_cast<const __nv_bfloat16*>(res.data_ptr()) + size_t(t0) * res.stride(0);
+      p.ldr = res.stride(0);
+    }
+    if (has(amax_val)) {
+      // per-tile partials for this chunk live at column offset t0 of a [n_tiles, T_total] layout: use a chunk view
+      p.amax_val = amax_val.data_ptr<float>() + size_t(t0) * n_tiles;
+      p.amax_idx = amax_idx.data_ptr<int>() + size_t(t0) * n_tiles;
+    }
+    const size_t smem = 1024 + size_t(p.stages) * stage_bytes + 64 + 16 * 64 * 4 + 1024;
+    static bool attr_set = false;
+    if (!attr_set) {
+      cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      attr_set = true;
+    }
+    gemm_kernel<<<grid, kThreads, smem, stream>>>(wmap, xmap, p);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+}
+
+}  // namespace e4

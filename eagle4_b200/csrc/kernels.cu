@@ -1,0 +1,345 @@
+// Row-wise kernels: RMSNorm variants, embedding gather, output gates, GDN gate math, the attention projection's
+// post-processing (q/k norm, RoPE, K/V cache write) and the greedy head's cross-tile argmax.
+//
+// Every reduction runs in a fixed order per row (thread-strided partial sums, a butterfly within the warp, then
+// the warps in index order), so a row's result never depends on how many rows share the launch.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace e4 {
+
+namespace {
+
+constexpr int kRowThreads = 256;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int i = 0; i < nw; ++i) s += red[i];
+  return s;
+}
+
+__device__ __forceinline__ float bf(const __nv_bfloat16 x) { return __bfloat162float(x); }
+
+// y = x * rsqrt(mean(x^2) + eps) * (w or 1 + w)
+__global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int ldx, const __nv_bfloat16* __restrict__ w,
+                               __nv_bfloat16* __restrict__ y, int ldy, int H, float eps, int offset) {
+  __shared__ float red[32];
+  const size_t r = blockIdx.x;
+  const __nv_bfloat16* xr = x + r * ldx;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float v = bf(xr[i]);
+    ss += v * v;
+  }
+  const float rs = rsqrtf(block_sum(ss, red) / H + eps);
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float s = offset ? 1.f + bf(w[i]) : bf(w[i]);
+    y[r * ldy + i] = __float2bfloat16(bf(xr[i]) * rs * s);
+  }
+}
+
+// y[r] = [rmsnorm(e[r], we) | rmsnorm(h[r], wh)]
+__global__ void concat_norms_kernel(const __nv_bfloat16* __restrict__ e, const __nv_bfloat16* __restrict__ h, int ldh,
+                                    const __nv_bfloat16* __restrict__ we, const __nv_bfloat16* __restrict__ wh,
+                                    __nv_bfloat16* __restrict__ y, int H, float eps) {
+  __shared__ float red[32];
+  const size_t r = blockIdx.x;
+  for (int part = 0; part < 2; ++part) {
+    const __nv_bfloat16* xr = part == 0 ? e + r * H : h + r * ldh;
+    const __nv_bfloat16* w = part == 0 ? we : wh;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+      const float v = bf(xr[i]);
+      ss += v * v;
+    }
+    const float rs = rsqrtf(block_sum(ss, red) / H + eps);
+    for (int i = threadIdx.x; i < H; i += blockDim.x)
+      y[r * 2 * H + part * H + i] = __float2bfloat16(bf(xr[i]) * rs * bf(w[i]));
+  }
+}
+
+__global__ void embedding_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
+                                 __nv_bfloat16* __restrict__ y, int H, int64_t V, int* err) {
+  const int64_t id = ids[blockIdx.x];
+  if (id < 0 || id >= V) {
+    if (threadIdx.x == 0) record_error(err, kErrBadIndex);
+    return;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(table + id * H);
+  uint4* dst = reinterpret_cast<uint4*>(y + size_t(blockIdx.x) * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+__global__ void sigmoid_gate_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ g, int ldg,
+                                    __nv_bfloat16* __restrict__ y, int D) {
+  const size_t r = blockIdx.x;
+  for (int i = threadIdx.x; i < D; i += blockDim.x)
+    y[r * D + i] = __float2bfloat16(bf(o[r * D + i]) * sigmoidf_(bf(g[r * ldg + i])));
+}
+
+// per (row, group): rmsnorm over D then * silu(z)
+__global__ void gated_rmsnorm_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ z, int ldz,
+                                     const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y, int G, int D,
+                                     float eps) {
+  // one warp per (row, group)
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int r = warp / G, g = warp % G;
+  if (r >= int(gridDim.y)) return;
+  const __nv_bfloat16* orow = o + (size_t(r) * G + g) * D;
+  float ss = 0.f;
+  for (int i = lane; i < D; i += 32) {
+    const float v = bf(orow[i]);
+    ss += v * v;
+  }
+  const float rs = rsqrtf(warp_sum(ss) / D + eps);
+  for (int i = lane; i < D; i += 32) {
+    const float n = bf(orow[i]) * rs * bf(w[i]);
+    y[(size_t(r) * G + g) * D + i] = __float2bfloat16(n * silu(bf(z[size_t(r) * ldz + g * D + i])));
+  }
+}
+
+__global__ void gdn_gates_kernel(const __nv_bfloat16* __restrict__ a, const __nv_bfloat16* __restrict__ b, int lda,
+                                 const float* __restrict__ a_log, const float* __restrict__ dt_bias, float* g,
+                                 float* beta, int T, int HV) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * HV) return;
+  const int r = i / HV, h = i % HV;
+  g[i] = -__expf(a_log[h]) * softplusf_(bf(a[size_t(r) * lda + h]) + dt_bias[h]);
+  beta[i] = sigmoidf_(bf(b[size_t(r) * lda + h]));
+}
+
+// Split the fused attention projection, RMS-normalise q and k per head (optional), rotate the first ``rot`` dims
+// (NeoX halves, cos/sin from a table), write K and V at the row's cache slot and q to a contiguous buffer.
+// One block per row; ``qkv`` row layout [q (Hq*D) | gate (Hq*D, optional) | k (Hk*D) | v (Hk*D)].
+__global__ void qkv_prepare_kernel(const __nv_bfloat16* __restrict__ qkv, int ldq, const int64_t* __restrict__ pos,
+                                   const int64_t* __restrict__ slot, __nv_bfloat16* kc, __nv_bfloat16* vc,
+                                   const __nv_bfloat16* __restrict__ qn, const __nv_bfloat16* __restrict__ kn,
+                                   int norm_offset, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                   __nv_bfloat16* __restrict__ qout, int Hq, int Hk, int D, int rot, int gated,
+                                   float eps) {
+  const size_t r = blockIdx.x;
+  const __nv_bfloat16* row = qkv + r * ldq;
+  const int64_t p = pos[r];
+  const int64_t s = slot[r];
+  const int half = rot / 2;
+  const int koff = Hq * D * (gated ? 2 : 1);
+  const int voff = koff + Hk * D;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  // heads 0..Hq-1 are q, Hq..Hq+Hk-1 are k: one warp per head
+  for (int hh = warp; hh < Hq + Hk; hh += nw) {
+    const bool isq = hh < Hq;
+    const __nv_bfloat16* src = row + (isq ? hh * D : koff + (hh - Hq) * D);
+    const __nv_bfloat16* nw_ = isq ? qn : kn;
+    float rs = 1.f;
+    if (nw_) {
+      float ss = 0.f;
+      for (int i = lane; i < D; i += 32) {
+        const float v = bf(src[i]);
+        ss += v * v;
+      }
+      rs = rsqrtf(warp_sum(ss) / D + eps);
+    }
+    __nv_bfloat16* dst = isq ? qout + (r * Hq + hh) * D : kc + (size_t(s) * Hk + (hh - Hq)) * D;
+    for (int i = lane; i < D; i += 32) {
+      float v = bf(src[i]) * rs;
+      if (nw_) v = __bfloat162float(__float2bfloat16(v * (norm_offset ? 1.f + bf(nw_[i]) : bf(nw_[i]))));
+      if (i < rot) {
+        const int j = i < half ? i : i - half;
+        float other = bf(src[i < half ? i + half : i - half]) * rs;
+        if (nw_) {
+          const int oi = i < half ? i + half : i - half;
+          other = __bfloat162float(__float2bfloat16(other * (norm_offset ? 1.f + bf(nw_[oi]) : bf(nw_[oi]))));
+        }
+        const float c = cos_t[p * half + j], sn = sin_t[p * half + j];
+        v = i < half ? v * c - other * sn : v * c + other * sn;
+      }
+      dst[i] = __float2bfloat16(v);
+    }
+  }
+  for (int i = threadIdx.x; i < Hk * D; i += blockDim.x) vc[size_t(s) * Hk * D + i] = row[voff + i];
+}
+
+// Greedy head: reduce per-tile (max, argmax) partials to one id per token (ties to the lower id).
+__global__ void argmax_reduce_kernel(const float* __restrict__ val, const int* __restrict__ idx, int n_tiles, int T,
+                                     int64_t* __restrict__ out_id, float* __restrict__ out_val) {
+  const int t = blockIdx.x;
+  const int chunk = t / 256, j = t % 256;
+  const int tc = min(256, T - chunk * 256);
+  const float* v = val + size_t(chunk) * 256 * n_tiles;
+  const int* ix = idx + size_t(chunk) * 256 * n_tiles;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < n_tiles; i += blockDim.x) {
+    const float ov = v[size_t(i) * tc + j];
+    const int oi = ix[size_t(i) * tc + j];
+    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    best = sv[0];
+    bi = si[0];
+    for (int w = 1; w < int(blockDim.x >> 5); ++w)
+      if (sv[w] > best || (sv[w] == best && si[w] < bi)) { best = sv[w]; bi = si[w]; }
+    out_id[t] = bi;
+    out_val[t] = best;
+  }
+}
+
+// Copy accepted rows' K/V (all attention layers at once): pointers of every layer's cache in ``kp`` / ``vp``.
+__global__ void kv_commit_kernel(const int64_t* __restrict__ kp, const int64_t* __restrict__ vp, int layers,
+                                 const int64_t* __restrict__ src, const int64_t* __restrict__ dst, int n, int row_elems) {
+  const int item = blockIdx.x;  // (layer, move)
+  const int l = item / n, m = item % n;
+  if (l >= layers) return;
+  const int64_t s = src[m], d = dst[m];
+  if (s == d) return;
+  uint4* k = reinterpret_cast<uint4*>(kp[l]);
+  uint4* v = reinterpret_cast<uint4*>(vp[l]);
+  const int vec = row_elems / 8;
+  for (int i = threadIdx.x; i < vec; i += blockDim.x) {
+    k[d * vec + i] = k[s * vec + i];
+    v[d * vec + i] = v[s * vec + i];
+  }
+}
+
+}  // namespace
+
+torch::Tensor gemm_error_word(torch::Device dev);
+
+#define BF16(t) reinterpret_cast<__nv_bfloat16*>((t).data_ptr())
+#define CBF16(t) reinterpret_cast<const __nv_bfloat16*>((t).data_ptr())
+
+torch::Tensor rmsnorm(const torch::Tensor& x, const torch::Tensor& w, double eps, bool offset) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1);
+  const at::cuda::CUDAGuard g(x.device());
+  const int H = x.size(-1);
+  auto x2 = x.reshape({-1, H});
+  auto y = torch::empty({x2.size(0), H}, x.options());
+  if (x2.size(0))
+    rmsnorm_kernel<<<x2.size(0), kRowThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+        CBF16(x2), x2.stride(0), CBF16(w), BF16(y), H, H, float(eps), offset ? 1 : 0);
+  return y.view(x.sizes());
+}
+
+torch::Tensor concat_norms(const torch::Tensor& e, const torch::Tensor& h, const torch::Tensor& we,
+                           const torch::Tensor& wh, double eps) {
+  const at::cuda::CUDAGuard g(e.device());
+  const int T = e.size(0), H = e.size(1);
+  auto y = torch::empty({T, 2 * H}, e.options());
+  if (T)
+    concat_norms_kernel<<<T, kRowThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+        CBF16(e.contiguous()), CBF16(h), h.stride(0), CBF16(we), CBF16(wh), BF16(y), H, float(eps));
+  return y;
+}
+
+torch::Tensor embedding(const torch::Tensor& ids, const torch::Tensor& table) {
+  const at::cuda::CUDAGuard g(table.device());
+  const int T = ids.size(0), H = table.size(1);
+  TORCH_CHECK(H % 8 == 0 && table.is_contiguous());
+  auto y = torch::empty({T, H}, table.options());
+  auto id64 = ids.to(torch::kInt64).contiguous();
+  if (T)
+    embedding_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+        id64.data_ptr<int64_t>(), CBF16(table), BF16(y), H, table.size(0),
+        gemm_error_word(table.device()).data_ptr<int>());
+  return y;
+}
+
+torch::Tensor sigmoid_gate(const torch::Tensor& o, const torch::Tensor& gate) {
+  const at::cuda::CUDAGuard g(o.device());
+  auto oc = o.contiguous();
+  auto y = torch::empty_like(oc);
+  const int T = oc.size(0), D = oc.size(1);
+  if (T)
+    sigmoid_gate_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(CBF16(oc), CBF16(gate), gate.stride(0),
+                                                                         BF16(y), D);
+  return y;
+}
+
+torch::Tensor gated_rmsnorm(const torch::Tensor& o, const torch::Tensor& z, const torch::Tensor& w, double eps) {
+  const at::cuda::CUDAGuard g(o.device());
+  auto oc = o.contiguous();
+  const int T = oc.size(0), G = oc.size(1), D = oc.size(2);
+  TORCH_CHECK(z.stride(-1) == 1);
+  auto y = torch::empty({T, G * D}, o.options());
+  const int warps = T * G;
+  if (T) {
+    dim3 grid((warps * 32 + 255) / 256, T);
+    gated_rmsnorm_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(CBF16(oc), CBF16(z), z.stride(0),
+                                                                             CBF16(w), BF16(y), G, D, float(eps));
+  }
+  return y;
+}
+
+std::vector<torch::Tensor> gdn_gates(const torch::Tensor& a, const torch::Tensor& b, const torch::Tensor& a_log,
+                                     const torch::Tensor& dt_bias) {
+  const at::cuda::CUDAGuard g(a.device());
+  const int T = a.size(0), HV = a.size(1);
+  TORCH_CHECK(a.stride(0) == b.stride(0) && a.stride(1) == 1 && b.stride(1) == 1);
+  auto f = a.options().dtype(torch::kFloat32);
+  auto gg = torch::empty({T, HV}, f), beta = torch::empty({T, HV}, f);
+  if (T)
+    gdn_gates_kernel<<<(T * HV + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        CBF16(a), CBF16(b), a.stride(0), a_log.data_ptr<float>(), dt_bias.data_ptr<float>(), gg.data_ptr<float>(),
+        beta.data_ptr<float>(), T, HV);
+  return {gg, beta};
+}
+
+torch::Tensor qkv_prepare(const torch::Tensor& qkv, const torch::Tensor& pos, const torch::Tensor& slot,
+                          torch::Tensor kc, torch::Tensor vc, const c10::optional<torch::Tensor>& qn,
+                          const c10::optional<torch::Tensor>& kn, bool norm_offset, const torch::Tensor& cos_t,
+                          const torch::Tensor& sin_t, int64_t Hq, int64_t Hk, int64_t D, int64_t rot, bool gated,
+                          double eps) {
+  const at::cuda::CUDAGuard g(qkv.device());
+  const int T = qkv.size(0);
+  auto q = torch::empty({T, Hq, D}, qkv.options());
+  if (T)
+    qkv_prepare_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        CBF16(qkv), qkv.stride(0), pos.data_ptr<int64_t>(), slot.data_ptr<int64_t>(), BF16(kc), BF16(vc),
+        qn ? CBF16(*qn) : nullptr, kn ? CBF16(*kn) : nullptr, norm_offset ? 1 : 0, cos_t.data_ptr<float>(),
+        sin_t.data_ptr<float>(), BF16(q), Hq, Hk, D, rot, gated ? 1 : 0, float(eps));
+  return q;
+}
+
+std::vector<torch::Tensor> argmax_reduce(const torch::Tensor& val, const torch::Tensor& idx, int64_t n_tiles,
+                                         int64_t T) {
+  const at::cuda::CUDAGuard g(val.device());
+  auto ids = torch::empty({T}, val.options().dtype(torch::kInt64));
+  auto best = torch::empty({T}, val.options().dtype(torch::kFloat32));
+  if (T)
+    argmax_reduce_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        val.data_ptr<float>(), idx.data_ptr<int>(), n_tiles, T, ids.data_ptr<int64_t>(), best.data_ptr<float>());
+  return {ids, best};
+}
+
+void kv_commit(const torch::Tensor& kp, const torch::Tensor& vp, const torch::Tensor& src, const torch::Tensor& dst,
+               int64_t row_elems) {
+  const at::cuda::CUDAGuard g(src.device());
+  const int n = src.size(0), layers = kp.size(0);
+  TORCH_CHECK(row_elems % 8 == 0);
+  if (n && layers)
+    kv_commit_kernel<<<n * layers, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+        kp.data_ptr<int64_t>(), vp.data_ptr<int64_t>(), layers, src.data_ptr<int64_t>(), dst.data_ptr<int64_t>(), n,
+        row_elems);
+}
+
+}  // namespace e4

@@ -1,0 +1,583 @@
+// Recurrent token mixers over draft trees: causal depthwise conv, the gated delta rule (GDN) and the Mamba2
+// selective state update.
+//
+// Tree verify never writes a request's committed state: each row replays its own path (ancestors, then itself)
+// from the committed state, so branches never see each other's updates. After acceptance the commit kernels replay
+// the accepted path once more, in place. Plain decode is a one-row verify plus its commit. All three modes call the
+// same per-step device function, so a token decoded alone and the same token verified in a tree produce identical
+// states and outputs. Prefill chains use scan mode (rows of a request in order, state updated in place).
+//
+// Layouts: GDN state [slots, HV, V, K] fp32 (K contiguous; thread v of a CTA keeps column v in registers);
+// Mamba2 state [slots, H, P, N] fp32 (thread p keeps row p); conv windows [slots, C, W-1] (oldest first).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <vector>
+
+#include "common.cuh"
+
+namespace e4 {
+namespace {
+
+constexpr int kMaxPath = 64;
+
+__device__ __forceinline__ float bf(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+// ----------------------------------------------------------------------------------------------- causal conv
+// out[r, c] = silu(sum_j w[c, j] * window_j) over the row's last W inputs along its parent chain (oldest first),
+// taking missing ancestors from the committed window.
+__global__ void conv_tree_kernel(const __nv_bfloat16* __restrict__ x, int ldx, const __nv_bfloat16* __restrict__ cs,
+                                 const int* __restrict__ slot, const int* __restrict__ parent,
+                                 const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int T, int C,
+                                 int W) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int r = blockIdx.y;
+  if (c >= C) return;
+  int chain[8];
+  int n = 0, cur = r;
+  while (cur >= 0 && n < W) {
+    chain[n++] = cur;
+    cur = parent[cur];
+  }
+  const int s = slot[r];
+  float acc = 0.f;
+  for (int j = 0; j < W; ++j) {
+    // window position j (0 oldest); the newest n entries come from the chain (chain[0] is the row itself)
+    const int from_end = W - 1 - j;
+    float v;
+    if (from_end < n) {
+      v = bf(x[size_t(chain[from_end]) * ldx + c]);
+    } else {
+      const int k = (W - 1) - (from_end - n) - 1;  // column in the committed window
+      v = bf(cs[(size_t(s) * C + c) * (W - 1) + k]);
+    }
+    acc = fmaf(bf(w[size_t(c) * W + j]), v, acc);
+  }
+  out[size_t(r) * C + c] = __float2bfloat16(silu(acc));
+}
+
+// conv window update: append the rows rows[b, :n[b]] (in order) to request b's window
+__global__ void conv_commit_kernel(const __nv_bfloat16* __restrict__ x, int ldx, __nv_bfloat16* cs,
+                                   const int* __restrict__ slots, const int* __restrict__ rows, int rows_ld,
+                                   const int* __restrict__ nrows, int C, int W) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int b = blockIdx.y;
+  if (c >= C) return;
+  const int n = nrows[b];
+  if (n <= 0) return;
+  const int s = slots[b];
+  __nv_bfloat16 hist[8 + kMaxPath];
+  int len = 0;
+  for (int k = 0; k < W - 1; ++k) hist[len++] = cs[(size_t(s) * C + c) * (W - 1) + k];
+  const int first = max(0, n - (W - 1));
+  for (int i = first; i < n; ++i) hist[len++] = x[size_t(rows[size_t(b) * rows_ld + i]) * ldx + c];
+  for (int k = 0; k < W - 1; ++k) cs[(size_t(s) * C + c) * (W - 1) + k] = hist[len - (W - 1) + k];
+}
+
+// ----------------------------------------------------------------------------------------------- GDN
+struct GdnArgs {
+  const __nv_bfloat16* qkv;   // post-conv [T, 2*HK*K + HV*V] (row stride ldq)
+  int ldq;
+  const __nv_bfloat16* proj;  // in_proj output rows: raw b at column b_off, raw a at a_off, z at z_off
+  int ldp, z_off, b_off, a_off;
+  const float* a_log;         // [HV]
+  const float* dt_bias;       // [HV]
+  float* state;               // [slots, HV, V, K]
+  int HK, HV, K, V;
+};
+
+// Decay gate and write strength of (row, value head): g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b).
+__device__ __forceinline__ float2 gdn_gate(const GdnArgs& a, int row, int h) {
+  const __nv_bfloat16* pr = a.proj + size_t(row) * a.ldp;
+  const float g = -__expf(a.a_log[h]) * softplusf_(bf(pr[a.a_off + h]) + a.dt_bias[h]);
+  const float beta = sigmoidf_(bf(pr[a.b_off + h]));
+  return make_float2(g, beta);
+}
+
+// Loads the l2-normalised q (scaled by K^-1/2) and k of ``row`` for key head ``kh`` into shared memory.
+template <int K>
+__device__ __forceinline__ void gdn_load_qk(const GdnArgs& a, int row, int kh, float* sq, float* sk, float* red) {
+  const __nv_bfloat16* base = a.qkv + size_t(row) * a.ldq;
+  const int t = threadIdx.x;
+  float qv = 0.f, kv = 0.f;
+  if (t < K) {
+    qv = bf(base[kh * K + t]);
+    kv = bf(base[a.HK * K + kh * K + t]);
+  }
+  // fixed-order block sums of q^2 and k^2 (warps, then warps in index order)
+  float q2 = warp_sum(qv * qv), k2 = warp_sum(kv * kv);
+  const int warp = t >> 5, lane = t & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) { red[warp] = q2; red[8 + warp] = k2; }
+  __syncthreads();
+  float sq2 = 0.f, sk2 = 0.f;
+  for (int i = 0; i < nw; ++i) { sq2 += red[i]; sk2 += red[8 + i]; }
+  const float rq = rsqrtf(sq2 + 1e-6f) * rsqrtf(float(K));
+  const float rk = rsqrtf(sk2 + 1e-6f);
+  if (t < K) {
+    sq[t] = qv * rq;
+    sk[t] = kv * rk;
+  }
+  __syncthreads();
+}
+
+// One gated-delta-rule step on this thread's state column S[0..K) (value column v); returns the output o[v].
+template <int K>
+__device__ __forceinline__ float gdn_step(float* S, const float* sq, const float* sk, float vval, float g, float beta) {
+  const float decay = __expf(g);
+  float kvm = 0.f;
+#pragma unroll
+  for (int i = 0; i < K; ++i) {
+    S[i] *= decay;
+    kvm = fmaf(S[i], sk[i], kvm);
+  }
+  const float delta = (vval - kvm) * beta;
+  float o = 0.f;
+#pragma unroll
+  for (int i = 0; i < K; ++i) {
+    S[i] = fmaf(sk[i], delta, S[i]);
+    o = fmaf(S[i], sq[i], o);
+  }
+  return o;
+}
+
+// The output epilogue: o rounded to bf16, RMS-normalised over the head's V values, times w, times silu(z).
+__device__ __forceinline__ void gdn_store(const GdnArgs& a, int row, int h, int v, float o, const __nv_bfloat16* nw,
+                                          float eps, float* red, __nv_bfloat16* out) {
+  const float ob = __bfloat162float(__float2bfloat16(o));
+  const float x2 = v < a.V ? ob * ob : 0.f;
+  float s = warp_sum(x2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwp = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < nwp; ++i) tot += red[i];
+  const float rs = rsqrtf(tot / a.V + eps);
+  if (v < a.V) {
+    const float z = bf(a.proj[size_t(row) * a.ldp + a.z_off + h * a.V + v]);
+    out[(size_t(row) * a.HV + h) * a.V + v] = __float2bfloat16(ob * rs * bf(nw[v]) * silu(z));
+  }
+}
+
+template <int K>
+__device__ __forceinline__ void load_state(float* S, const float* src) {
+#pragma unroll
+  for (int i = 0; i < K; i += 4) {
+    const float4 t4 = *reinterpret_cast<const float4*>(src + i);
+    S[i] = t4.x; S[i + 1] = t4.y; S[i + 2] = t4.z; S[i + 3] = t4.w;
+  }
+}
+template <int K>
+__device__ __forceinline__ void save_state(const float* S, float* dst) {
+#pragma unroll
+  for (int i = 0; i < K; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
+}
+
+// One CTA per (value head, row) in tree mode (the row replays its path, no state write) or per (value head,
+// request segment) in scan mode (rows in order, state updated in place); thread v owns state column v. The output
+// is the gated-RMS-normalised head output [T, HV*V].
+template <int K>
+__global__ void __launch_bounds__(128) gdn_kernel(GdnArgs a, const int* __restrict__ slot,
+                                                  const int* __restrict__ parent, const int* __restrict__ seg,
+                                                  int scan, const __nv_bfloat16* __restrict__ nw, float eps,
+                                                  __nv_bfloat16* __restrict__ out) {
+  __shared__ float sq[K], sk[K], red[16];
+  __shared__ int path[kMaxPath];
+  __shared__ int plen;
+  const int h = blockIdx.x;
+  const int v = threadIdx.x;
+  const int kh = h / (a.HV / a.HK);
+  const int vc = min(v, a.V - 1);
+  float S[K];
+  if (!scan) {
+    const int r = blockIdx.y;
+    if (threadIdx.x == 0) {
+      int n = 0, cur = r;
+      int tmp[kMaxPath];
+      while (cur >= 0 && n < kMaxPath) { tmp[n++] = cur; cur = parent[cur]; }
+      for (int i = 0; i < n; ++i) path[i] = tmp[n - 1 - i];
+      plen = n;
+    }
+    __syncthreads();
+    load_state<K>(S, a.state + ((size_t(slot[r]) * a.HV + h) * a.V + vc) * K);
+    float o = 0.f;
+    for (int p = 0; p < plen; ++p) {
+      const int j = path[p];
+      gdn_load_qk<K>(a, j, kh, sq, sk, red);
+      const float vval = bf(a.qkv[size_t(j) * a.ldq + 2 * a.HK * K + h * a.V + vc]);
+      const float2 gb = gdn_gate(a, j, h);
+      o = gdn_step<K>(S, sq, sk, vval, gb.x, gb.y);
+    }
+    gdn_store(a, r, h, v, o, nw, eps, red, out);
+    return;
+  }
+  const int r0 = seg[blockIdx.y], r1 = seg[blockIdx.y + 1];
+  float* st = a.state + ((size_t(slot[r0]) * a.HV + h) * a.V + vc) * K;
+  load_state<K>(S, st);
+  for (int j = r0; j < r1; ++j) {
+    gdn_load_qk<K>(a, j, kh, sq, sk, red);
+    const float vval = bf(a.qkv[size_t(j) * a.ldq + 2 * a.HK * K + h * a.V + vc]);
+    const float2 gb = gdn_gate(a, j, h);
+    const float o = gdn_step<K>(S, sq, sk, vval, gb.x, gb.y);
+    gdn_store(a, j, h, v, o, nw, eps, red, out);
+  }
+  if (v < a.V) save_state<K>(S, st);
+}
+
+// Per-layer pointers of an all-layers commit.
+struct GdnLayer {
+  const __nv_bfloat16* qkv;   // post-conv rows
+  const __nv_bfloat16* proj;  // in_proj output rows (x_pre at column 0, b / a at b_off / a_off)
+  float* state;
+  __nv_bfloat16* conv_state;
+  const float* a_log;
+  const float* dt_bias;
+};
+
+constexpr int kMaxLayers = 64;
+struct GdnLayerTable {
+  GdnLayer l[kMaxLayers];
+};
+
+// Commit of every GDN layer in one launch: CTA (value head, request, layer) replays rows[b, :n[b]] in place.
+template <int K>
+__global__ void __launch_bounds__(128) gdn_commit_kernel(GdnArgs a, const __grid_constant__ GdnLayerTable layers,
+                                                         const int* __restrict__ slots, const int* __restrict__ rows,
+                                                         int rows_ld, const int* __restrict__ nrows) {
+  __shared__ float sq[K], sk[K], red[16];
+  const int h = blockIdx.x, b = blockIdx.y, l = blockIdx.z, v = threadIdx.x;
+  const int n = nrows[b];
+  if (n <= 0) return;
+  const GdnLayer L = layers.l[l];
+  a.qkv = L.qkv;
+  a.proj = L.proj;
+  a.state = L.state;
+  a.a_log = L.a_log;
+  a.dt_bias = L.dt_bias;
+  const int kh = h / (a.HV / a.HK);
+  const int vc = min(v, a.V - 1);
+  float* st = a.state + ((size_t(slots[b]) * a.HV + h) * a.V + vc) * K;
+  float S[K];
+  load_state<K>(S, st);
+  for (int p = 0; p < n; ++p) {
+    const int j = rows[size_t(b) * rows_ld + p];
+    gdn_load_qk<K>(a, j, kh, sq, sk, red);
+    const float vval = bf(a.qkv[size_t(j) * a.ldq + 2 * a.HK * K + h * a.V + vc]);
+    const float2 gb = gdn_gate(a, j, h);
+    gdn_step<K>(S, sq, sk, vval, gb.x, gb.y);
+  }
+  if (v < a.V) save_state<K>(S, st);
+}
+
+// Conv window update of every layer: append rows[b, :n[b]] of the layer's conv inputs (proj columns [0, C)).
+__global__ void conv_commit_all_kernel(const __grid_constant__ GdnLayerTable layers, int ldp, const int* __restrict__ slots,
+                                       const int* __restrict__ rows, int rows_ld, const int* __restrict__ nrows,
+                                       int C, int W) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int b = blockIdx.y;
+  if (c >= C) return;
+  const int n = nrows[b];
+  if (n <= 0) return;
+  const GdnLayer L = layers.l[blockIdx.z];
+  const int s = slots[b];
+  __nv_bfloat16* cs = L.conv_state;
+  __nv_bfloat16 hist[8 + kMaxPath];
+  int len = 0;
+  for (int k = 0; k < W - 1; ++k) hist[len++] = cs[(size_t(s) * C + c) * (W - 1) + k];
+  const int first = max(0, n - (W - 1));
+  for (int i = first; i < n; ++i) hist[len++] = L.proj[size_t(rows[size_t(b) * rows_ld + i]) * ldp + c];
+  for (int k = 0; k < W - 1; ++k) cs[(size_t(s) * C + c) * (W - 1) + k] = hist[len - (W - 1) + k];
+}
+
+// ----------------------------------------------------------------------------------------------- Mamba2
+struct MambaArgs {
+  const __nv_bfloat16* xbc;  // post-conv [T, H*P + 2*G*N]
+  int ldx;
+  const __nv_bfloat16* dt;   // raw dt [T, H] (row stride lddt)
+  int lddt;
+  const float* a_log;
+  const float* dt_bias;
+  const float* dskip;
+  float* state;  // [slots, H, P, N]
+  int H, P, N, G;
+};
+
+// Thread p owns state row S[p][0..N). Loads B and C of the row's group into shared memory.
+template <int N>
+__device__ __forceinline__ float mamba_step(const MambaArgs& a, float* S, int row, int h, int p, float* sB, float* sC) {
+  const int grp = h / (a.H / a.G);
+  const __nv_bfloat16* base = a.xbc + size_t(row) * a.ldx;
+  __syncthreads();
+  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    sB[i] = bf(base[a.H * a.P + grp * N + i]);
+    sC[i] = bf(base[a.H * a.P + a.G * N + grp * N + i]);
+  }
+  __syncthreads();
+  const float dt = softplusf_(bf(a.dt[size_t(row) * a.lddt + h]) + a.dt_bias[h]);
+  const float A = -__expf(a.a_log[h]);
+  const float da = __expf(dt * A);
+  const float x = p < a.P ? bf(base[h * a.P + p]) : 0.f;
+  const float dx = dt * x;
+  float y = 0.f;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    S[i] = fmaf(S[i], da, dx * sB[i]);
+    y = fmaf(S[i], sC[i], y);
+  }
+  return fmaf(a.dskip[h], x, y);
+}
+
+template <int N>
+__global__ void __launch_bounds__(64) mamba_kernel(MambaArgs a, const int* __restrict__ slot,
+                                                   const int* __restrict__ parent, const int* __restrict__ seg,
+                                                   int scan, __nv_bfloat16* __restrict__ out) {
+  __shared__ float sB[N], sC[N];
+  __shared__ int path[kMaxPath];
+  __shared__ int plen;
+  const int h = blockIdx.x, p = threadIdx.x;
+  float S[N];
+  int r0, r1;
+  if (!scan) {
+    const int r = blockIdx.y;
+    if (threadIdx.x == 0) {
+      int n = 0, cur = r;
+      int tmp[kMaxPath];
+      while (cur >= 0 && n < kMaxPath) { tmp[n++] = cur; cur = parent[cur]; }
+      for (int i = 0; i < n; ++i) path[i] = tmp[n - 1 - i];
+      plen = n;
+    }
+    __syncthreads();
+    const float* src = a.state + ((size_t(slot[r]) * a.H + h) * a.P + min(p, a.P - 1)) * N;
+#pragma unroll
+    for (int i = 0; i < N; ++i) S[i] = src[i];
+    float y = 0.f;
+    for (int q = 0; q < plen; ++q) y = mamba_step<N>(a, S, path[q], h, p, sB, sC);
+    if (p < a.P) out[(size_t(r) * a.H + h) * a.P + p] = __float2bfloat16(y);
+    return;
+  }
+  r0 = seg[blockIdx.y];
+  r1 = seg[blockIdx.y + 1];
+  float* st = a.state + ((size_t(slot[r0]) * a.H + h) * a.P + min(p, a.P - 1)) * N;
+#pragma unroll
+  for (int i = 0; i < N; ++i) S[i] = st[i];
+  for (int j = r0; j < r1; ++j) {
+    const float y = mamba_step<N>(a, S, j, h, p, sB, sC);
+    if (p < a.P) out[(size_t(j) * a.H + h) * a.P + p] = __float2bfloat16(y);
+  }
+  if (p < a.P) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) st[i] = S[i];
+  }
+}
+
+template <int N>
+__global__ void __launch_bounds__(64) mamba_commit_kernel(MambaArgs a, const int* __restrict__ slots,
+                                                          const int* __restrict__ rows, int rows_ld,
+                                                          const int* __restrict__ nrows) {
+  __shared__ float sB[N], sC[N];
+  const int h = blockIdx.x, b = blockIdx.y, p = threadIdx.x;
+  const int n = nrows[b];
+  if (n <= 0) return;
+  float* st = a.state + ((size_t(slots[b]) * a.H + h) * a.P + min(p, a.P - 1)) * N;
+  float S[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) S[i] = st[i];
+  for (int q = 0; q < n; ++q) mamba_step<N>(a, S, rows[size_t(b) * rows_ld + q], h, p, sB, sC);
+  if (p < a.P) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) st[i] = S[i];
+  }
+}
+
+torch::Tensor segments_of(const torch::Tensor& slot) {
+  // consecutive runs of equal slots (rows of a request are contiguous in scan mode)
+  auto s = slot.to(torch::kCPU).to(torch::kInt32).contiguous();
+  const int* p = s.data_ptr<int>();
+  std::vector<int> seg{0};
+  for (int i = 1; i < s.numel(); ++i)
+    if (p[i] != p[i - 1]) seg.push_back(i);
+  seg.push_back(int(s.numel()));
+  return torch::tensor(seg, torch::kInt32).to(slot.device());
+}
+
+}  // namespace
+
+#define CBF(t) reinterpret_cast<const __nv_bfloat16*>((t).data_ptr())
+#define BFP(t) reinterpret_cast<__nv_bfloat16*>((t).data_ptr())
+
+torch::Tensor conv_tree(const torch::Tensor& x, const torch::Tensor& cs, const torch::Tensor& slot,
+                        const torch::Tensor& parent, const torch::Tensor& w) {
+  const at::cuda::CUDAGuard g(x.device());
+  const int T = x.size(0), C = x.size(1), W = w.size(1);
+  TORCH_CHECK(W <= 8 && x.stride(1) == 1);
+  auto out = torch::empty({T, C}, x.options());
+  if (T) {
+    auto sl = slot.to(torch::kInt32).contiguous(), pa = parent.to(torch::kInt32).contiguous();
+    conv_tree_kernel<<<dim3((C + 255) / 256, T), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        CBF(x), x.stride(0), CBF(cs), sl.data_ptr<int>(), pa.data_ptr<int>(), CBF(w.contiguous()), BFP(out), T, C, W);
+  }
+  return out;
+}
+
+void conv_commit(const torch::Tensor& x, torch::Tensor cs, const torch::Tensor& slots, const torch::Tensor& rows,
+                 const torch::Tensor& nrows, int64_t W) {
+  const at::cuda::CUDAGuard g(x.device());
+  const int B = rows.size(0), C = x.size(1);
+  TORCH_CHECK(x.stride(1) == 1 && rows.size(1) <= kMaxPath);
+  if (!B) return;
+  auto sl = slots.to(torch::kInt32).contiguous(), rw = rows.to(torch::kInt32).contiguous(),
+       nr = nrows.to(torch::kInt32).contiguous();
+  conv_commit_kernel<<<dim3((C + 255) / 256, B), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      CBF(x), x.stride(0), BFP(cs), sl.data_ptr<int>(), rw.data_ptr<int>(), rw.size(1), nr.data_ptr<int>(), C, W);
+}
+
+void conv_commit_scan(torch::Tensor cs, const torch::Tensor& x, const torch::Tensor& slot, int64_t W) {
+  // rows of each request are contiguous: commit the last W-1 rows of every run
+  auto seg = segments_of(slot).cpu();
+  const int* s = seg.data_ptr<int>();
+  const int nseg = seg.numel() - 1;
+  std::vector<int> slots_v, nrows_v;
+  std::vector<int> rows_v;
+  const int keep = int(W) - 1;
+  auto slot_c = slot.to(torch::kCPU).to(torch::kInt32);
+  for (int i = 0; i < nseg; ++i) {
+    const int r0 = s[i], r1 = s[i + 1];
+    const int first = std::max(r0, r1 - keep);
+    slots_v.push_back(slot_c.data_ptr<int>()[r0]);
+    nrows_v.push_back(r1 - first);
+    for (int k = 0; k < keep; ++k) rows_v.push_back(first + k < r1 ? first + k : r1 - 1);
+  }
+  auto dev = x.device();
+  auto opt = torch::TensorOptions().dtype(torch::kInt32);
+  auto rows = torch::tensor(rows_v, opt).view({nseg, keep}).to(dev);
+  conv_commit(x, cs, torch::tensor(slots_v, opt).to(dev), rows, torch::tensor(nrows_v, opt).to(dev), W);
+}
+
+static GdnArgs gdn_args(const torch::Tensor& qkv, const torch::Tensor& proj, int64_t z_off, int64_t b_off,
+                        int64_t a_off, const torch::Tensor& a_log, const torch::Tensor& dt_bias, torch::Tensor state,
+                        int64_t HK, int64_t HV, int64_t K, int64_t V) {
+  TORCH_CHECK(qkv.stride(1) == 1 && proj.stride(1) == 1 && state.is_contiguous());
+  TORCH_CHECK(V <= 128 && (K == 128 || K == 64), "gdn: K must be 64 or 128 and V <= 128");
+  return GdnArgs{CBF(qkv), int(qkv.stride(0)), CBF(proj), int(proj.stride(0)), int(z_off), int(b_off), int(a_off),
+                 a_log.data_ptr<float>(), dt_bias.data_ptr<float>(), state.data_ptr<float>(), int(HK), int(HV),
+                 int(K), int(V)};
+}
+
+// Gated delta rule + gated RMSNorm over a forest of rows; returns [T, HV*V].
+torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int64_t z_off, int64_t b_off,
+                       int64_t a_off, const torch::Tensor& a_log, const torch::Tensor& dt_bias, torch::Tensor state,
+                       const torch::Tensor& slot, const torch::Tensor& parent, const torch::Tensor& norm_w,
+                       double eps, int64_t HK, int64_t HV, int64_t K, int64_t V, bool scan) {
+  const at::cuda::CUDAGuard gd(qkv.device());
+  const int T = qkv.size(0);
+  auto out = torch::empty({T, HV * V}, qkv.options());
+  if (!T) return out;
+  GdnArgs a = gdn_args(qkv, proj, z_off, b_off, a_off, a_log, dt_bias, state, HK, HV, K, V);
+  auto sl = slot.to(torch::kInt32).contiguous(), pa = parent.to(torch::kInt32).contiguous();
+  torch::Tensor seg = scan ? segments_of(sl) : torch::zeros({1}, sl.options());
+  const int ny = scan ? seg.numel() - 1 : T;
+  dim3 grid(HV, ny);
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (K == 128)
+    gdn_kernel<128><<<grid, 128, 0, st>>>(a, sl.data_ptr<int>(), pa.data_ptr<int>(), seg.data_ptr<int>(), scan,
+                                          CBF(norm_w), float(eps), BFP(out));
+  else
+    gdn_kernel<64><<<grid, 128, 0, st>>>(a, sl.data_ptr<int>(), pa.data_ptr<int>(), seg.data_ptr<int>(), scan,
+                                         CBF(norm_w), float(eps), BFP(out));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
+// Commit the accepted rows of every GDN layer (state replay and conv window) in two launches. The per-layer
+// tensors are passed by value in a kernel-parameter table (no device-side pointer array to upload, so the call
+// can be captured in a CUDA graph); all layers share the row strides of qkv / proj.
+void gdn_commit_all(const std::vector<torch::Tensor>& qkv, const std::vector<torch::Tensor>& proj,
+                    const std::vector<torch::Tensor>& state, const std::vector<torch::Tensor>& conv_state,
+                    const std::vector<torch::Tensor>& a_log, const std::vector<torch::Tensor>& dt_bias, int64_t b_off,
+                    int64_t a_off, const torch::Tensor& slots, const torch::Tensor& rows, const torch::Tensor& nrows,
+                    int64_t HK, int64_t HV, int64_t K, int64_t V, int64_t C, int64_t W) {
+  const at::cuda::CUDAGuard gd(slots.device());
+  const int B = rows.size(0), nl = int(qkv.size());
+  TORCH_CHECK(nl <= kMaxLayers && rows.size(1) <= kMaxPath);
+  if (!B || !nl) return;
+  GdnLayerTable tab{};
+  for (int i = 0; i < nl; ++i) {
+    TORCH_CHECK(qkv[i].stride(0) == qkv[0].stride(0) && proj[i].stride(0) == proj[0].stride(0));
+    tab.l[i] = GdnLayer{CBF(qkv[i]), CBF(proj[i]), state[i].data_ptr<float>(), BFP(conv_state[i]),
+                        a_log[i].data_ptr<float>(), dt_bias[i].data_ptr<float>()};
+  }
+  auto sl = slots.to(torch::kInt32).contiguous(), rw = rows.to(torch::kInt32).contiguous(),
+       nr = nrows.to(torch::kInt32).contiguous();
+  GdnArgs a{nullptr, int(qkv[0].stride(0)), nullptr, int(proj[0].stride(0)), 0, int(b_off), int(a_off), nullptr,
+            nullptr, nullptr, int(HK), int(HV), int(K), int(V)};
+  auto st = at::cuda::getCurrentCUDAStream();
+  dim3 grid(HV, B, nl);
+  if (K == 128)
+    gdn_commit_kernel<128><<<grid, 128, 0, st>>>(a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(), rw.size(1),
+                                                 nr.data_ptr<int>());
+  else
+    gdn_commit_kernel<64><<<grid, 128, 0, st>>>(a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(), rw.size(1),
+                                                nr.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  conv_commit_all_kernel<<<dim3((C + 255) / 256, B, nl), 256, 0, st>>>(tab, int(proj[0].stride(0)),
+                                                                        sl.data_ptr<int>(), rw.data_ptr<int>(),
+                                                                        rw.size(1), nr.data_ptr<int>(), int(C),
+                                                                        int(W));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+static MambaArgs mamba_args(const torch::Tensor& xbc, const torch::Tensor& dt, const torch::Tensor& a_log,
+                            const torch::Tensor& dt_bias, const torch::Tensor& dskip, torch::Tensor state, int64_t H,
+                            int64_t P, int64_t N, int64_t G) {
+  TORCH_CHECK(xbc.stride(1) == 1 && dt.stride(1) == 1 && state.is_contiguous());
+  TORCH_CHECK(P <= 64 && (N == 128 || N == 64 || N == 16), "mamba: head dim <= 64 and state 16/64/128");
+  return MambaArgs{CBF(xbc), int(xbc.stride(0)), CBF(dt), int(dt.stride(0)), a_log.data_ptr<float>(),
+                   dt_bias.data_ptr<float>(), dskip.data_ptr<float>(), state.data_ptr<float>(), int(H), int(P),
+                   int(N), int(G)};
+}
+
+#define E4_MAMBA_DISPATCH(N_, KERNEL, ...)                         \
+  switch (N_) {                                                      \
+    case 128: KERNEL<128><<<grid, 64, 0, st>>>(__VA_ARGS__); break;  \
+    case 64: KERNEL<64><<<grid, 64, 0, st>>>(__VA_ARGS__); break;    \
+    default: KERNEL<16><<<grid, 64, 0, st>>>(__VA_ARGS__); break;    \
+  }
+
+torch::Tensor mamba_tree(const torch::Tensor& xbc, const torch::Tensor& dt, const torch::Tensor& a_log,
+                         const torch::Tensor& dt_bias, const torch::Tensor& dskip, torch::Tensor state,
+                         const torch::Tensor& slot, const torch::Tensor& parent, int64_t H, int64_t P, int64_t N,
+                         int64_t G, bool scan) {
+  const at::cuda::CUDAGuard gd(xbc.device());
+  const int T = xbc.size(0);
+  auto out = torch::empty({T, H, P}, xbc.options());
+  if (!T) return out;
+  MambaArgs a = mamba_args(xbc, dt, a_log, dt_bias, dskip, state, H, P, N, G);
+  auto sl = slot.to(torch::kInt32).contiguous(), pa = parent.to(torch::kInt32).contiguous();
+  torch::Tensor seg = scan ? segments_of(sl) : torch::zeros({1}, sl.options());
+  dim3 grid(H, scan ? seg.numel() - 1 : T);
+  auto st = at::cuda::getCurrentCUDAStream();
+  E4_MAMBA_DISPATCH(N, mamba_kernel, a, sl.data_ptr<int>(), pa.data_ptr<int>(), seg.data_ptr<int>(), scan, BFP(out))
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
+void mamba_commit(const torch::Tensor& xbc, const torch::Tensor& dt, const torch::Tensor& a_log,
+                  const torch::Tensor& dt_bias, const torch::Tensor& dskip, torch::Tensor state,
+                  const torch::Tensor& slots, const torch::Tensor& rows, const torch::Tensor& nrows, int64_t H,
+                  int64_t P, int64_t N, int64_t G) {
+  const at::cuda::CUDAGuard gd(xbc.device());
+  const int B = rows.size(0);
+  if (!B) return;
+  MambaArgs a = mamba_args(xbc, dt, a_log, dt_bias, dskip, state, H, P, N, G);
+  auto sl = slots.to(torch::kInt32).contiguous(), rw = rows.to(torch::kInt32).contiguous(),
+       nr = nrows.to(torch::kInt32).contiguous();
+  dim3 grid(H, B);
+  auto st = at::cuda::getCurrentCUDAStream();
+  E4_MAMBA_DISPATCH(N, mamba_commit_kernel, a, sl.data_ptr<int>(), rw.data_ptr<int>(), int(rw.size(1)),
+                    nr.data_ptr<int>())
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace e4

@@ -1,0 +1,518 @@
+// Draft-tree kernels: the candidate head's exact re-score and tail (softmax over the candidates, top-K children),
+// and the fused greedy accept walk.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace e4 {
+namespace {
+
+// logit[r, c] = lm_head[idx[r, c]] . h[r] in fp32; one warp per (row, candidate), 16-byte loads.
+__global__ void gather_dot_kernel(const __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ w,
+                                  const int64_t* __restrict__ idx, float* __restrict__ out, int R, int C, int H,
+                                  int64_t V, int* err) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= R * C) return;
+  const int r = gw / C;
+  const int64_t id = idx[gw];
+  if (id < 0 || id >= V) {
+    if (lane == 0) { record_error(err, kErrBadIndex); out[gw] = -INFINITY; }
+    return;
+  }
+  const uint4* wr = reinterpret_cast<const uint4*>(w + id * H);
+  const uint4* hr = reinterpret_cast<const uint4*>(h + size_t(r) * H);
+  float acc = 0.f;
+  for (int i = lane; i < H / 8; i += 32) {
+    const uint4 a = wr[i], b = hr[i];
+    const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 fa = __bfloat1622float2(a2[j]), fb = __bfloat1622float2(b2[j]);
+      acc = fmaf(fa.x, fb.x, acc);
+      acc = fmaf(fa.y, fb.y, acc);
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) out[gw] = acc;
+}
+
+// Per row: softmax (temperature) over C candidate logits, then the top K probabilities (ties to the lower
+// candidate position) and their ids. One block of 128 threads per row; C <= 1024.
+__global__ void softmax_topk_kernel(const float* __restrict__ logit, const int64_t* __restrict__ ids, int C, int K,
+                                    float inv_temp, float* __restrict__ probs, int64_t* __restrict__ out_ids) {
+  __shared__ float p[1024];
+  __shared__ float red[32];
+  const int r = blockIdx.x;
+  const float* lr = logit + size_t(r) * C;
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) mx = fmaxf(mx, lr[i] * inv_temp);
+  mx = warp_max(mx);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int i = 1; i < nw; ++i) mx = fmaxf(mx, red[i]);
+  __syncthreads();
+  float s = 0.f;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    const float e = __expf(lr[i] * inv_temp - mx);
+    p[i] = e;
+    s += e;
+  }
+  s = warp_sum(s);
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < nw; ++i) tot += red[i];
+  const float inv = 1.f / tot;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) p[i] *= inv;
+  __syncthreads();
+  // K rounds of block argmax (K <= 8)
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  for (int k = 0; k < K; ++k) {
+    float best = -1.f;
+    int besti = 0x7fffffff;
+    for (int i = threadIdx.x; i < C; i += blockDim.x)
+      if (p[i] > best || (p[i] == best && i < besti)) { best = p[i]; besti = i; }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+      if (ov > best || (ov == best && oi < besti)) { best = ov; besti = oi; }
+    }
+    if (lane == 0) { bv[warp] = best; bi[warp] = besti; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float b = bv[0];
+      int ix = bi[0];
+      for (int w = 1; w < nw; ++w)
+        if (bv[w] > b || (bv[w] == b && bi[w] < ix)) { b = bv[w]; ix = bi[w]; }
+      probs[size_t(r) * K + k] = b;
+      out_ids[size_t(r) * K + k] = ids ? ids[size_t(r) * C + ix] : ix;
+      p[ix] = -2.f;
+    }
+    __syncthreads();
+  }
+}
+
+// Greedy accept walk, one thread per request: from row 0 follow the child whose token equals the target's argmax
+// at the current row (lowest row on duplicates); the bonus token is the argmax at the last accepted row.
+__global__ void accept_greedy_kernel(const int64_t* __restrict__ tid, const int64_t* __restrict__ tokens,
+                                     const int* __restrict__ parent, const int* __restrict__ nrows, int B, int N,
+                                     int* __restrict__ acc, int* __restrict__ cnt, int64_t* __restrict__ bonus) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const int n = nrows[b];
+  const int64_t* tk = tokens + size_t(b) * N;
+  const int* pr = parent + size_t(b) * N;
+  int* ac = acc + size_t(b) * N;
+  for (int i = 0; i < N; ++i) ac[i] = -1;
+  int cur = 0, c = 1;
+  ac[0] = 0;
+  while (true) {
+    const int64_t want = tid[size_t(b) * N + cur];
+    int nxt = -1;
+    for (int r = 1; r < n; ++r)
+      if (pr[r] == cur && tk[r] == want) { nxt = r; break; }
+    if (nxt < 0) { bonus[b] = want; break; }
+    ac[c++] = nxt;
+    cur = nxt;
+  }
+  cnt[b] = c;
+}
+
+}  // namespace
+
+torch::Tensor gemm_error_word(torch::Device dev);
+
+torch::Tensor gather_dot(const torch::Tensor& h, const torch::Tensor& w, const torch::Tensor& idx) {
+  const at::cuda::CUDAGuard g(h.device());
+  const int R = idx.size(0), C = idx.size(1), H = h.size(1);
+  TORCH_CHECK(H % 8 == 0 && h.is_contiguous() && w.is_contiguous());
+  auto out = torch::empty({R, C}, h.options().dtype(torch::kFloat32));
+  auto ix = idx.to(torch::kInt64).contiguous();
+  const int warps = R * C;
+  if (warps)
+    gather_dot_kernel<<<(warps * 32 + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+        ix.data_ptr<int64_t>(), out.data_ptr<float>(), R, C, H, w.size(0),
+        gemm_error_word(h.device()).data_ptr<int>());
+  return out;
+}
+
+std::vector<torch::Tensor> softmax_topk(const torch::Tensor& logit, const c10::optional<torch::Tensor>& ids, int64_t K,
+                                        double temperature) {
+  const at::cuda::CUDAGuard g(logit.device());
+  const int R = logit.size(0), C = logit.size(1);
+  TORCH_CHECK(C <= 1024 && K <= 8 && logit.is_contiguous());
+  auto probs = torch::empty({R, K}, logit.options());
+  auto oid = torch::empty({R, K}, logit.options().dtype(torch::kInt64));
+  torch::Tensor idc;
+  if (ids) idc = ids->to(torch::kInt64).contiguous();
+  if (R)
+    softmax_topk_kernel<<<R, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+        logit.data_ptr<float>(), ids ? idc.data_ptr<int64_t>() : nullptr, C, K, float(1.0 / temperature),
+        probs.data_ptr<float>(), oid.data_ptr<int64_t>());
+  return {probs, oid};
+}
+
+std::vector<torch::Tensor> accept_greedy(const torch::Tensor& tid, const torch::Tensor& tokens,
+                                         const torch::Tensor& parent, const torch::Tensor& nrows) {
+  const at::cuda::CUDAGuard g(tokens.device());
+  const int B = tokens.size(0), N = tokens.size(1);
+  auto o = tokens.options();
+  auto acc = torch::empty({B, N}, o.dtype(torch::kInt32));
+  auto cnt = torch::empty({B}, o.dtype(torch::kInt32));
+  auto bonus = torch::empty({B}, o.dtype(torch::kInt64));
+  auto t = tid.to(torch::kInt64).contiguous(), tk = tokens.to(torch::kInt64).contiguous(),
+       pr = parent.to(torch::kInt32).contiguous(), nr = nrows.to(torch::kInt32).contiguous();
+  if (B)
+    accept_greedy_kernel<<<(B + 127) / 128, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+        t.data_ptr<int64_t>(), tk.data_ptr<int64_t>(), pr.data_ptr<int>(), nr.data_ptr<int>(), B, N,
+        acc.data_ptr<int>(), cnt.data_ptr<int>(), bonus.data_ptr<int64_t>());
+  return {acc, cnt, bonus};
+}
+
+}  // namespace e4
+
+// =====================================================================================================================
+// Top-C selection over long rows (the candidate shortlist over the draft vocabulary) and the draft-tree updates.
+// =====================================================================================================================
+namespace e4 {
+namespace {
+
+// Order-preserving map of fp32 to uint32 (larger float -> larger key).
+__device__ __forceinline__ uint32_t fkey(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+constexpr int kSelThreads = 256;
+constexpr int kSelPer = 16;  // elements per thread: a CTA selects within 4096 elements
+
+// Radix select inside one CTA: among ``n`` (<= 4096) elements (key, index) find the ``C`` largest keys (ties to the
+// lower index) and write them in index order to (ov, oi). Elements of thread t are [t*16, t*16+16) (index order).
+__device__ void cta_select(const uint32_t* key, const int* idx, const float* val, int n, int C, float* ov, int* oi) {
+  __shared__ int hist[256];
+  __shared__ uint32_t s_prefix;
+  __shared__ int s_remaining, s_digit_above;
+  __shared__ int scan[kSelThreads];
+  const int t = threadIdx.x;
+  uint32_t prefix = 0, mask = 0;
+  int remaining = min(C, n);
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = t; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int i = 0; i < kSelPer; ++i) {
+      const int e = t * kSelPer + i;
+      if (e < n && (key[i] & mask) == prefix) atomicAdd(&hist[(key[i] >> shift) & 255], 1);
+    }
+    __syncthreads();
+    if (t == 0) {
+      int above = 0, d = 255;
+      for (; d > 0; --d) {
+        if (above + hist[d] >= remaining) break;
+        above += hist[d];
+      }
+      s_prefix = prefix | (uint32_t(d) << shift);
+      s_remaining = remaining - above;
+      s_digit_above = above;
+    }
+    __syncthreads();
+    prefix = s_prefix;
+    mask |= 255u << shift;
+    remaining = s_remaining;
+    __syncthreads();
+  }
+  // threshold key = prefix; take every key above it and the first ``remaining`` keys equal to it (index order)
+  int n_gt = 0, n_eq = 0;
+  for (int i = 0; i < kSelPer; ++i) {
+    const int e = t * kSelPer + i;
+    if (e < n) { n_gt += key[i] > prefix; n_eq += key[i] == prefix; }
+  }
+  // exclusive block scans of n_eq then of the combined counts (index order)
+  scan[t] = n_eq;
+  __syncthreads();
+  for (int off = 1; off < kSelThreads; off <<= 1) {
+    const int v = t >= off ? scan[t - off] : 0;
+    __syncthreads();
+    scan[t] += v;
+    __syncthreads();
+  }
+  const int eq_before = scan[t] - n_eq;
+  __syncthreads();
+  const int take_eq = max(0, min(n_eq, remaining - eq_before));
+  const int mine = n_gt + take_eq;
+  scan[t] = mine;
+  __syncthreads();
+  for (int off = 1; off < kSelThreads; off <<= 1) {
+    const int v = t >= off ? scan[t - off] : 0;
+    __syncthreads();
+    scan[t] += v;
+    __syncthreads();
+  }
+  int pos = scan[t] - mine;
+  int eq_taken = 0;
+  for (int i = 0; i < kSelPer; ++i) {
+    const int e = t * kSelPer + i;
+    if (e >= n) break;
+    bool take = key[i] > prefix;
+    if (!take && key[i] == prefix && eq_taken < take_eq) { take = true; ++eq_taken; }
+    if (take) { ov[pos] = val[i]; oi[pos] = idx[i]; ++pos; }
+  }
+}
+
+// Stage 1: CTA (slice, row) selects the top C of scores[row, slice*4096 : ...].
+__global__ void __launch_bounds__(kSelThreads) topk_slice_kernel(const float* __restrict__ scores, int ld, int V, int C,
+                                                                 int nslices, float* __restrict__ ov,
+                                                                 int* __restrict__ oi) {
+  const int slice = blockIdx.x, r = blockIdx.y;
+  const int base = slice * kSelThreads * kSelPer;
+  const int n = min(kSelThreads * kSelPer, V - base);
+  uint32_t key[kSelPer];
+  int idx[kSelPer];
+  float val[kSelPer];
+  for (int i = 0; i < kSelPer; ++i) {
+    const int e = threadIdx.x * kSelPer + i;
+    const bool in = e < n;
+    val[i] = in ? scores[size_t(r) * ld + base + e] : -INFINITY;
+    key[i] = in ? fkey(val[i]) : 0u;
+    idx[i] = base + e;
+  }
+  cta_select(key, idx, val, n, C, ov + (size_t(r) * nslices + slice) * C, oi + (size_t(r) * nslices + slice) * C);
+}
+
+// Stage 2: CTA per row selects the top C of the slices' candidates, then sorts them (value desc, id asc).
+__global__ void __launch_bounds__(kSelThreads) topk_merge_kernel(const float* __restrict__ iv, const int* __restrict__ ii,
+                                                                 int m, int C, float* __restrict__ ov,
+                                                                 int64_t* __restrict__ oi) {
+  const int r = blockIdx.x;
+  __shared__ float sv[1024];
+  __shared__ int si[1024];
+  uint32_t key[kSelPer];
+  int idx[kSelPer];
+  float val[kSelPer];
+  for (int i = 0; i < kSelPer; ++i) {
+    const int e = threadIdx.x * kSelPer + i;
+    const bool in = e < m;
+    val[i] = in ? iv[size_t(r) * m + e] : -INFINITY;
+    idx[i] = in ? ii[size_t(r) * m + e] : 0x7fffffff;
+    key[i] = in ? fkey(val[i]) : 0u;
+  }
+  cta_select(key, idx, val, m, C, sv, si);
+  __syncthreads();
+  // bitonic sort of C (power of two <= 1024) entries: value desc, id asc
+  int P = 1;
+  while (P < C) P <<= 1;
+  for (int i = threadIdx.x + C; i < P; i += blockDim.x) { sv[i] = -INFINITY; si[i] = 0x7fffffff; }
+  __syncthreads();
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        const int l = i ^ j;
+        if (l > i) {
+          const bool a_first = sv[i] > sv[l] || (sv[i] == sv[l] && si[i] < si[l]);
+          const bool up = (i & k) == 0;
+          if (up != a_first) {
+            const float tv = sv[i]; sv[i] = sv[l]; sv[l] = tv;
+            const int ti = si[i]; si[i] = si[l]; si[l] = ti;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    ov[size_t(r) * C + i] = sv[i];
+    oi[size_t(r) * C + i] = si[i];
+  }
+}
+
+// One draft-tree step for request b (one CTA): children scores, frontier top-K (ties to the lower child), tokens,
+// parents, frontier hidden rows and ancestor slots gathered by the picked lanes, and the best-score set merged with
+// the new layer. (DraftTree.step semantics.)
+__global__ void tree_step_kernel(const float* __restrict__ probs, const int64_t* __restrict__ toks,
+                                 const __nv_bfloat16* __restrict__ hidden, int H, int K, int step, int layer_start,
+                                 int parent_col, int work_cap, int cap, int pcap, int depth_cap, float* scores,
+                                 int64_t* tokens, int64_t* parents, float* front_scores, int64_t* front_tokens,
+                                 __nv_bfloat16* front_hidden, int64_t* front_nodes, int* ancestors, float* best,
+                                 float* best_prev, float* layer_top) {
+  const int b = blockIdx.x;
+  __shared__ float layer[64];
+  __shared__ int pick[8];
+  __shared__ float top[8];
+  __shared__ int anc_tmp[8 * 32];
+  __shared__ float merged[64 + 64];
+  const int t = threadIdx.x;
+  const int KK = K * K;
+  if (t < KK) {
+    const int lane = t / K;
+    layer[t] = front_scores[b * K + lane] * probs[size_t(b * K + lane) * K + (t % K)];
+  }
+  __syncthreads();
+  if (t < KK) {
+    scores[size_t(b) * cap + layer_start + t] = layer[t];
+    tokens[size_t(b) * cap + layer_start + t] = toks[size_t(b * K + t / K) * K + (t % K)];
+  }
+  if (t == 0) {
+    // top-K of the layer, stable (ties to the lower index)
+    unsigned used = 0;
+    for (int k = 0; k < K; ++k) {
+      int bi = -1;
+      float bv = -INFINITY;
+      for (int i = 0; i < KK; ++i)
+        if (!((used >> i) & 1ull) && (bi < 0 || layer[i] > bv)) { bv = layer[i]; bi = i; }
+      used |= 1u << bi;
+      pick[k] = bi;
+      top[k] = bv;
+    }
+  }
+  __syncthreads();
+  // ancestors of the picked lanes (read all before writing)
+  for (int i = t; i < K * depth_cap; i += blockDim.x) anc_tmp[i] = ancestors[(size_t(b) * K + pick[i / depth_cap] / K) * depth_cap + i % depth_cap];
+  __syncthreads();
+  for (int i = t; i < K * depth_cap; i += blockDim.x) ancestors[size_t(b) * K * depth_cap + i] = anc_tmp[i];
+  if (t < K) {
+    parents[size_t(b) * pcap + parent_col + t] = pick[t] + layer_start;
+    front_scores[b * K + t] = top[t];
+    front_tokens[b * K + t] = toks[size_t(b * K + pick[t] / K) * K + (pick[t] % K)];
+    front_nodes[b * K + t] = pick[t] + layer_start;
+    layer_top[b * K + t] = top[t];
+  }
+  // frontier hidden rows (16-byte chunks)
+  const int vec = H / 8;
+  for (int i = t; i < K * vec; i += blockDim.x) {
+    const int k = i / vec, c = i % vec;
+    reinterpret_cast<uint4*>(front_hidden + size_t(b * K + k) * H)[c] =
+        reinterpret_cast<const uint4*>(hidden + size_t(b * K + pick[k] / K) * H)[c];
+  }
+  // best set: merge the sorted best list (work_cap, descending) with the layer's values, keep work_cap
+  if (t < work_cap) merged[t] = best[size_t(b) * work_cap + t];
+  __syncthreads();
+  if (t < work_cap) best_prev[size_t(b) * work_cap + t] = merged[t];
+  if (t == 0) {
+    // insertion of the KK layer values into the descending list (values only)
+    float lay[64];
+    for (int i = 0; i < KK; ++i) lay[i] = layer[i];
+    for (int i = 1; i < KK; ++i) {
+      const float v = lay[i];
+      int j = i - 1;
+      while (j >= 0 && lay[j] < v) { lay[j + 1] = lay[j]; --j; }
+      lay[j + 1] = v;
+    }
+    int a = 0, c = 0;
+    for (int o = 0; o < work_cap; ++o) {
+      const float av = a < work_cap ? merged[a] : -INFINITY;
+      const float cv = c < KK ? lay[c] : -INFINITY;
+      if (av >= cv) { best[size_t(b) * work_cap + o] = av; ++a; } else { best[size_t(b) * work_cap + o] = cv; ++c; }
+    }
+  }
+}
+
+// The best ``count`` nodes of each request's tree as verify rows (DraftTree.verify_rows semantics): rank by
+// depth-decayed score (ties to the lower node), emit in node order; tokens and parent rows (root row 0 = -1).
+__global__ void select_rows_kernel(const float* __restrict__ scores, const float* __restrict__ decay,
+                                   const int64_t* __restrict__ tokens, const int64_t* __restrict__ parents, int n,
+                                   int cap, int pcap, int K, int count, int64_t* __restrict__ out_tok,
+                                   int* __restrict__ out_parent) {
+  const int b = blockIdx.x;
+  __shared__ float d[1024];
+  __shared__ int sel_pos[1024];
+  __shared__ int row_node[64];
+  for (int i = threadIdx.x; i < n; i += blockDim.x) d[i] = scores[size_t(b) * cap + i] * decay[i];
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    int rank = 0;
+    const float di = d[i];
+    for (int j = 0; j < n; ++j) rank += (d[j] > di) || (d[j] == di && j < i);
+    sel_pos[i] = rank < count ? 1 : 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int r = 0;
+    for (int i = 0; i < n; ++i) {
+      if (sel_pos[i]) { row_node[r] = i; sel_pos[i] = r + 1; ++r; } else sel_pos[i] = 0;
+    }
+  }
+  __syncthreads();
+  for (int r = threadIdx.x; r < count; r += blockDim.x) {
+    const int node = row_node[r];
+    out_tok[size_t(b) * count + r] = tokens[size_t(b) * cap + node];
+    // parent node: depth 1 nodes hang off the root; depth >= 2 nodes read their frontier column
+    int pnode = -1;
+    if (node >= K) {
+      const int layer = (node - K) / (K * K) + 2;  // depth of the node
+      const int local = node - (K + (layer - 2) * K * K);
+      const int base = layer - 1 > 1 ? (K + 1) + (layer - 1 - 2) * K : 1;  // frontier column of depth layer-1
+      pnode = int(parents[size_t(b) * pcap + base + local / K]);
+    }
+    out_parent[size_t(b) * (count + 1) + r + 1] = pnode >= 0 ? sel_pos[pnode] : 0;
+  }
+  if (threadIdx.x == 0) out_parent[size_t(b) * (count + 1)] = -1;
+}
+
+}  // namespace
+
+// Top-C (value desc, id asc) of each row of fp32 scores [R, V]: (values [R, C], ids int64 [R, C]).
+std::vector<torch::Tensor> topk_large(const torch::Tensor& scores, int64_t C) {
+  const at::cuda::CUDAGuard g(scores.device());
+  TORCH_CHECK(scores.scalar_type() == torch::kFloat32 && scores.stride(1) == 1 && C <= 1024);
+  const int R = scores.size(0), V = scores.size(1);
+  const int per = kSelThreads * kSelPer;
+  const int ns = (V + per - 1) / per;
+  TORCH_CHECK(ns * C <= per, "topk_large: too many slices for one merge CTA");
+  auto o = scores.options();
+  auto sv = torch::empty({R, ns, C}, o), si = torch::empty({R, ns, C}, o.dtype(torch::kInt32));
+  auto ov = torch::empty({R, C}, o), oi = torch::empty({R, C}, o.dtype(torch::kInt64));
+  if (!R) return {ov, oi};
+  auto st = at::cuda::getCurrentCUDAStream();
+  topk_slice_kernel<<<dim3(ns, R), kSelThreads, 0, st>>>(scores.data_ptr<float>(), scores.stride(0), V, int(C), ns,
+                                                         sv.data_ptr<float>(), si.data_ptr<int>());
+  topk_merge_kernel<<<R, kSelThreads, 0, st>>>(sv.data_ptr<float>(), si.data_ptr<int>(), ns * int(C), int(C),
+                                               ov.data_ptr<float>(), oi.data_ptr<int64_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {ov, oi};
+}
+
+void tree_step(const torch::Tensor& probs, const torch::Tensor& toks, const torch::Tensor& hidden, int64_t bs,
+               int64_t K, int64_t step, int64_t layer_start, int64_t parent_col, torch::Tensor scores,
+               torch::Tensor tokens, torch::Tensor parents, torch::Tensor front_scores, torch::Tensor front_tokens,
+               torch::Tensor front_hidden, torch::Tensor front_nodes, torch::Tensor ancestors, torch::Tensor best,
+               torch::Tensor best_prev, torch::Tensor layer_top) {
+  const at::cuda::CUDAGuard g(probs.device());
+  TORCH_CHECK(K <= 8 && best.size(1) <= 64 && ancestors.size(2) <= 32);
+  auto p = probs.to(torch::kFloat32).contiguous();
+  auto tk = toks.to(torch::kInt64).contiguous();
+  auto h = hidden.contiguous();
+  const int H = h.size(1);
+  TORCH_CHECK(H % 8 == 0);
+  tree_step_kernel<<<bs, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+      p.data_ptr<float>(), tk.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()), H, K, step,
+      layer_start, parent_col, best.size(1), scores.size(1), parents.size(1), ancestors.size(2),
+      scores.data_ptr<float>(), tokens.data_ptr<int64_t>(), parents.data_ptr<int64_t>(),
+      front_scores.data_ptr<float>(), front_tokens.data_ptr<int64_t>(),
+      reinterpret_cast<__nv_bfloat16*>(front_hidden.data_ptr()), front_nodes.data_ptr<int64_t>(),
+      ancestors.data_ptr<int>(), best.data_ptr<float>(), best_prev.data_ptr<float>(), layer_top.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+std::vector<torch::Tensor> select_rows(const torch::Tensor& scores, const torch::Tensor& decay,
+                                       const torch::Tensor& tokens, const torch::Tensor& parents, int64_t bs,
+                                       int64_t n, int64_t K, int64_t count) {
+  const at::cuda::CUDAGuard g(scores.device());
+  TORCH_CHECK(n <= 1024 && count <= 63);
+  auto ot = torch::empty({bs, count}, tokens.options());
+  auto op = torch::empty({bs, count + 1}, tokens.options().dtype(torch::kInt32));
+  select_rows_kernel<<<bs, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+      scores.data_ptr<float>(), decay.data_ptr<float>(), tokens.data_ptr<int64_t>(), parents.data_ptr<int64_t>(), n,
+      scores.size(1), parents.size(1), K, count, ot.data_ptr<int64_t>(), op.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {ot, op};
+}
+
+}  // namespace e4

@@ -73,7 +73,8 @@ class DraftModel:
 
     def forward(self, ids: torch.Tensor, hidden: torch.Tensor, pos: torch.Tensor, req: torch.Tensor,
                 write_slot: torch.Tensor, ctx_start: torch.Tensor, ctx_len: torch.Tensor, extra: torch.Tensor,
-                n_extra: torch.Tensor, cache: DraftCache) -> Tuple[torch.Tensor, torch.Tensor]:
+                n_extra: torch.Tensor, cache: DraftCache, max_keys: Optional[int] = None
+                ) -> Tuple[torch.Tensor, torch.Tensor]:
         """Returns ``(normed [T, H], next hidden [T, H])``."""
         cfg, w = self.cfg, self.w
         eps = cfg.rms_norm_eps
@@ -82,15 +83,17 @@ class DraftModel:
         qkv = ops.linear(x, w["qkv"])
         q, _ = ops.qkv_prepare(qkv, self.attn_shape, pos, write_slot, cache.k, cache.v, None, None)
         o = ops.attention(q, cache.k, cache.v, cache.block_table, cache.page, req, ctx_start, ctx_len, extra,
-                          n_extra, cfg.head_dim ** -0.5)
-        residual = ops.linear_residual(o.reshape(o.shape[0], -1), w["o_proj"], hidden)
+                          n_extra, cfg.head_dim ** -0.5, max_keys)
+        residual = ops.linear_residual(o, w["o_proj"], hidden)
         x = ops.rmsnorm(residual, w["post_attention_layernorm"], eps, False)
         summed = ops.linear_residual(ops.linear_swiglu(x, w["gate_up"]), w["down"], residual)
         normed = ops.rmsnorm(summed, w["norm"], eps, False)
         return normed, (normed if cfg.norm_output else summed)
 
-    def candidates(self, normed: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
-        """Top-``k`` children per row: ``(probs fp32 [T, k], target token ids int64 [T, k])``."""
+    def candidates(self, normed: torch.Tensor, k: int, pos: Optional[torch.Tensor] = None
+                   ) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Top-``k`` children per row: ``(probs fp32 [T, k], target token ids int64 [T, k])``. ``pos`` (the rows'
+        positions) is unused by the learned head; position-aware proposers that replace this method read it."""
         cfg, w = self.cfg, self.w
         if cfg.low_rank:
             probs, ids = ops.candidate_head(normed, w["lr_down"], w["lr_scores"], w["lm_head"],

@@ -38,6 +38,7 @@ class RowBatch:
     parent: torch.Tensor  # [T] int32 parent row inside this forward (-1: the committed state)
     state_slot: torch.Tensor  # [T] int32 recurrent-state slot of the row's request
     scan: bool = False  # recurrent layers update their state in place row by row (prefill chains)
+    max_keys: Optional[int] = None  # bound on any row's visible keys (lets attention skip a host read)
 
     @property
     def num_rows(self) -> int:
@@ -90,10 +91,10 @@ class TargetCache:
 class Records:
     """What a tree verify keeps per recurrent layer so the accepted path can be committed afterwards."""
 
-    x_pre: List[torch.Tensor] = field(default_factory=list)  # conv inputs [T, C]
+    layer: List[int] = field(default_factory=list)  # model layer of each entry
+    x_pre: List[torch.Tensor] = field(default_factory=list)  # GDN: the whole in_proj output; Mamba2: conv inputs
     conv_out: List[torch.Tensor] = field(default_factory=list)  # post-conv [T, C]
-    gate_a: List[torch.Tensor] = field(default_factory=list)  # GDN g [T, HV] fp32 / Mamba2 raw dt [T, H]
-    gate_b: List[torch.Tensor] = field(default_factory=list)  # GDN beta [T, HV] fp32 / unused for Mamba2
+    gate_a: List[torch.Tensor] = field(default_factory=list)  # Mamba2 raw dt [T, H] (None for GDN)
 
 
 class TargetModel:
@@ -120,10 +121,7 @@ class TargetModel:
         q, gate = ops.qkv_prepare(qkv, cfg, rb.pos, rb.write_slot, cache.k[li], cache.v[li],
                                   w.get(f"l{i}.q_norm"), w.get(f"l{i}.k_norm"))
         o = ops.attention(q, cache.k[li], cache.v[li], cache.block_table, cache.page, rb.req, rb.ctx_start,
-                          rb.ctx_len, rb.extra, rb.n_extra, cfg.head_dim ** -0.5)
-        o = o.reshape(o.shape[0], -1)
-        if gate is not None:
-            o = ops.sigmoid_gate(o, gate)
+                          rb.ctx_len, rb.extra, rb.n_extra, cfg.head_dim ** -0.5, rb.max_keys, gate)
         return ops.linear_residual(o, w[f"l{i}.o_proj"], h)
 
     def _gdn(self, i: int, x: torch.Tensor, h: torch.Tensor, rb: RowBatch, cache: TargetCache,
@@ -133,21 +131,17 @@ class TargetModel:
         cd, vd, hv = cfg.gdn_conv_dim, cfg.gdn_value_dim, cfg.gdn_v_heads
         proj = ops.linear(x, w[f"l{i}.in_proj"])
         x_pre = proj[:, :cd]
-        z = proj[:, cd: cd + vd]
-        b = proj[:, cd + vd: cd + vd + hv]
-        a = proj[:, cd + vd + hv: cd + vd + 2 * hv]
         conv = ops.causal_conv_tree(x_pre, cache.conv[ri], rb.state_slot, rb.parent, w[f"l{i}.conv"])
-        g, beta = ops.gdn_gates(a, b, w[f"l{i}.A_log"], w[f"l{i}.dt_bias"])
-        o = ops.gdn_tree(conv, g, beta, cache.ssm[ri], rb.state_slot, rb.parent, cfg, rb.scan)
+        y = ops.gdn_mixer(conv, proj, cfg, w[f"l{i}.A_log"], w[f"l{i}.dt_bias"], w[f"l{i}.gnorm"], cache.ssm[ri],
+                          rb.state_slot, rb.parent, rb.scan)
         if rb.scan:
             ops.conv_commit_scan(cache.conv[ri], x_pre, rb.state_slot, cfg.conv_kernel)
         elif rec is not None:
-            rec.x_pre.append(x_pre)
+            rec.layer.append(i)
+            rec.x_pre.append(proj)
             rec.conv_out.append(conv)
-            rec.gate_a.append(g)
-            rec.gate_b.append(beta)
-        o = ops.gated_rmsnorm(o, z, w[f"l{i}.gnorm"], cfg.rms_norm_eps)
-        return ops.linear_residual(o, w[f"l{i}.out_proj"], h)
+            rec.gate_a.append(None)
+        return ops.linear_residual(y, w[f"l{i}.out_proj"], h)
 
     def _mamba(self, i: int, x: torch.Tensor, h: torch.Tensor, rb: RowBatch, cache: TargetCache,
                rec: Optional[Records]) -> torch.Tensor:
@@ -164,10 +158,10 @@ class TargetModel:
         if rb.scan:
             ops.conv_commit_scan(cache.conv[ri], x_pre, rb.state_slot, cfg.conv_kernel)
         elif rec is not None:
+            rec.layer.append(i)
             rec.x_pre.append(x_pre)
             rec.conv_out.append(conv)
             rec.gate_a.append(dt)
-            rec.gate_b.append(dt)
         group = cfg.mamba_inner // cfg.mamba_groups
         y = ops.gated_rmsnorm(y.reshape(y.shape[0], cfg.mamba_groups, group), z, w[f"l{i}.gnorm"], cfg.rms_norm_eps)
         return ops.linear_residual(y, w[f"l{i}.out_proj"], h)
@@ -215,15 +209,18 @@ class TargetModel:
                slots: torch.Tensor, src_kv: torch.Tensor, dst_kv: torch.Tensor) -> None:
         """Commit the accepted rows: recurrent state replay along the path and KV moves in attention layers."""
         cfg, w = self.cfg, self.w
-        for i, (m, _) in enumerate(cfg.layers):
-            if m not in ("gdn", "mamba"):
+        gdn = [(j, li) for j, li in enumerate(rec.layer) if cfg.layers[li][0] == "gdn"]
+        if gdn:
+            ops.gdn_commit_all([rec.conv_out[j] for j, _ in gdn], [rec.x_pre[j] for j, _ in gdn],
+                               [cache.ssm[self.rec_index[li]] for _, li in gdn],
+                               [cache.conv[self.rec_index[li]] for _, li in gdn],
+                               [w[f"l{li}.A_log"] for _, li in gdn], [w[f"l{li}.dt_bias"] for _, li in gdn],
+                               slots, rows, n_rows, cfg)
+        for j, li in enumerate(rec.layer):
+            if cfg.layers[li][0] != "mamba":
                 continue
-            ri = self.rec_index[i]
-            if m == "gdn":
-                ops.gdn_commit(rec.conv_out[ri], rec.gate_a[ri], rec.gate_b[ri], rec.x_pre[ri], cache.ssm[ri],
-                               cache.conv[ri], slots, rows, n_rows, cfg)
-            else:
-                ops.mamba_commit(rec.conv_out[ri], rec.gate_a[ri], w[f"l{i}.A_log"], w[f"l{i}.dt_bias"],
-                                 w[f"l{i}.D"], rec.x_pre[ri], cache.ssm[ri], cache.conv[ri], slots, rows, n_rows, cfg)
+            ri = self.rec_index[li]
+            ops.mamba_commit(rec.conv_out[j], rec.gate_a[j], w[f"l{li}.A_log"], w[f"l{li}.dt_bias"], w[f"l{li}.D"],
+                             rec.x_pre[j], cache.ssm[ri], cache.conv[ri], slots, rows, n_rows, cfg)
         if cache.k:
             ops.kv_commit(cache.k, cache.v, src_kv, dst_kv)

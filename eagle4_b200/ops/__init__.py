@@ -73,15 +73,36 @@ def qkv_prepare(qkv, cfg, pos, write_slot, k_cache, v_cache, q_norm, k_norm):
     return ref.qkv_prepare(qkv, cfg, pos, write_slot, k_cache, v_cache, q_norm, k_norm)
 
 
-def attention(q, k_cache, v_cache, block_table, page, req, ctx_start, ctx_len, extra, n_extra, scale):
-    fn = _nat().attention if _cuda(q) else ref.attention
-    return fn(q, k_cache, v_cache, block_table, page, req, ctx_start, ctx_len, extra, n_extra, scale)
+def attention(q, k_cache, v_cache, block_table, page, req, ctx_start, ctx_len, extra, n_extra, scale,
+              max_keys=None, gate=None):
+    """Tree attention; returns ``[T, Hq*D]`` (times ``sigmoid(gate)`` when a gate ``[T, Hq*D]`` is given).
+    ``max_keys`` bounds every row's context + extras (required inside CUDA graphs: no host read)."""
+    if _cuda(q):
+        return _nat().attention(q, k_cache, v_cache, block_table, page, req, ctx_start, ctx_len, extra, n_extra,
+                                scale, max_keys, gate)
+    o = ref.attention(q, k_cache, v_cache, block_table, page, req, ctx_start, ctx_len, extra, n_extra, scale)
+    o = o.reshape(o.shape[0], -1)
+    return ref.sigmoid_gate(o, gate) if gate is not None else o
 
 
 # recurrent -------------------------------------------------------------------------------------------------------
 def causal_conv_tree(x, conv_state, state_slot, parent, weight):
     fn = _nat().causal_conv_tree if _cuda(x) else ref.causal_conv_tree
     return fn(x, conv_state, state_slot, parent, weight)
+
+
+def gdn_mixer(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent, scan: bool):
+    """Fused GDN token mixer after the conv: gates, tree recurrence and gated RMSNorm -> ``[T, HV*V]``."""
+    fn = _nat().gdn_mixer if _cuda(conv) else ref.gdn_mixer
+    return fn(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent, scan)
+
+
+def gdn_commit_all(convs, projs, states, conv_states, a_logs, dt_biases, slots, rows, n_rows, cfg):
+    """Commit accepted rows in every GDN layer at once (state replay and conv windows)."""
+    if not convs:
+        return
+    fn = _nat().gdn_commit_all if _cuda(slots) else ref.gdn_commit_all
+    return fn(convs, projs, states, conv_states, a_logs, dt_biases, slots, rows, n_rows, cfg)
 
 
 def gdn_gates(a, b, a_log, dt_bias):

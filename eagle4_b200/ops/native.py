@@ -1,0 +1,264 @@
+"""CUDA entry points: thin wrappers over the in-tree sm_100a extension (``eagle4_b200/csrc``).
+
+Importing this module on a machine with a GPU loads the extension; if it cannot be loaded the import fails loudly
+(there is no fallback path for CUDA tensors).
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from eagle4_b200.ops.build import load
+
+
+class _Counted:
+    """The extension module with a count of kernel-launching calls (``LAUNCHES[0]``), for benchmark reports."""
+
+    _QUIET = {"error_word"}
+
+    def __init__(self, mod):
+        self._mod = mod
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if name in self._QUIET or not callable(fn):
+            return fn
+
+        def call(*a, **k):
+            LAUNCHES[0] += 1
+            return fn(*a, **k)
+
+        return call
+
+
+LAUNCHES = [0]
+_C = _Counted(load())
+
+EPI_PLAIN, EPI_RESIDUAL, EPI_SWIGLU, EPI_RELU2, EPI_F32, EPI_ARGMAX = range(6)
+_NONE = torch.Tensor()
+
+
+def error_word(device=None) -> torch.Tensor:
+    """The device word the kernels record their first error code in (0: none)."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    return _C.error_word(dev.index if dev.index is not None else torch.cuda.current_device())
+
+
+def check_errors(device=None) -> None:
+    w = error_word(device)
+    code = int(w.item())
+    if code:
+        w.zero_()
+        raise RuntimeError(f"eagle4_b200 kernel reported error code {code}")
+
+
+def _c2(x: torch.Tensor) -> torch.Tensor:
+    if x.dim() != 2:
+        x = x.reshape(-1, x.shape[-1])
+    if x.stride(-1) != 1 or (x.stride(0) * 2) % 16 or x.data_ptr() % 16:
+        x = x.contiguous()
+    return x
+
+
+# dense ------------------------------------------------------------------------------------------------------------
+def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    x = _c2(x)
+    y = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+    _C.gemm(x, w, EPI_PLAIN, y, _NONE, _NONE, _NONE, _NONE)
+    return y
+
+
+def linear_residual(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+    x = _c2(x)
+    y = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+    _C.gemm(x, w, EPI_RESIDUAL, y, _NONE, residual.contiguous(), _NONE, _NONE)
+    return y
+
+
+def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor) -> torch.Tensor:
+    x = _c2(x)
+    if w_gu.shape[0] % 128:
+        raise ValueError("fused gate/up weight needs a multiple of 128 rows")
+    y = torch.empty(x.shape[0], w_gu.shape[0] // 2, dtype=x.dtype, device=x.device)
+    _C.gemm(x, w_gu, EPI_SWIGLU, y, _NONE, _NONE, _NONE, _NONE)
+    return y
+
+
+def linear_relu2(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    x = _c2(x)
+    y = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+    _C.gemm(x, w, EPI_RELU2, y, _NONE, _NONE, _NONE, _NONE)
+    return y
+
+
+def logits(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    x = _c2(x)
+    y = torch.empty(x.shape[0], w.shape[0], dtype=torch.float32, device=x.device)
+    _C.gemm(x, w, EPI_F32, _NONE, y, _NONE, _NONE, _NONE)
+    return y
+
+
+def lm_head_argmax(x: torch.Tensor, w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    x = _c2(x)
+    t = x.shape[0]
+    n_tiles = (w.shape[0] + 127) // 128
+    chunks = (t + 255) // 256
+    val = torch.empty(chunks * 256 * n_tiles, dtype=torch.float32, device=x.device)
+    idx = torch.empty(chunks * 256 * n_tiles, dtype=torch.int32, device=x.device)
+    _C.gemm(x, w, EPI_ARGMAX, _NONE, _NONE, _NONE, val, idx)
+    ids, best = _C.argmax_reduce(val, idx, n_tiles, t)
+    return ids, best
+
+
+# row ops ----------------------------------------------------------------------------------------------------------
+def rmsnorm(x, w, eps, offset):
+    return _C.rmsnorm(x, w, float(eps), bool(offset))
+
+
+def embedding(ids, table):
+    return _C.embedding(ids, table)
+
+
+def sigmoid_gate(o, gate):
+    return _C.sigmoid_gate(o, gate)
+
+
+def concat_norms(e, h, we, wh, eps):
+    return _C.concat_norms(e, h, we, wh, float(eps))
+
+
+def gated_rmsnorm(o, z, w, eps):
+    return _C.gated_rmsnorm(o, z, w, float(eps))
+
+
+def gdn_gates(a, b, a_log, dt_bias):
+    g, beta = _C.gdn_gates(a, b, a_log, dt_bias)
+    return g, beta
+
+
+# attention --------------------------------------------------------------------------------------------------------
+_ROPE: Dict[tuple, Tuple[torch.Tensor, torch.Tensor]] = {}
+
+
+def rope_tables(rot: int, theta: float, device, max_pos: int = 1 << 17) -> Tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin of ``pos * theta^(-i/half)``, computed in float64 and stored as fp32 ``[max_pos, half]``."""
+    key = (rot, float(theta), str(device), max_pos)
+    if key not in _ROPE:
+        half = max(rot // 2, 1)
+        inv = 1.0 / (theta ** (torch.arange(0, half, dtype=torch.float64) / half))
+        ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
+        _ROPE[key] = (ang.cos().float().to(device), ang.sin().float().to(device))
+    return _ROPE[key]
+
+
+def qkv_prepare(qkv, cfg, pos, write_slot, k_cache, v_cache, q_norm, k_norm):
+    cos_t, sin_t = rope_tables(cfg.rotary_dim, cfg.rope_theta, qkv.device)
+    q = _C.qkv_prepare(qkv, pos.long().contiguous(), write_slot.long().contiguous(), k_cache, v_cache, q_norm,
+                       k_norm, bool(cfg.norm_offset), cos_t, sin_t, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
+                       cfg.rotary_dim, bool(cfg.attn_output_gate), float(cfg.rms_norm_eps))
+    gate = None
+    if cfg.attn_output_gate:
+        hd = cfg.num_heads * cfg.head_dim
+        gate = qkv[:, hd: 2 * hd]
+    return q, gate
+
+
+def attention(q, k_cache, v_cache, block_table, page, req, ctx_start, ctx_len, extra, n_extra, scale,
+              max_keys: Optional[int] = None, gate: Optional[torch.Tensor] = None):
+    if max_keys is None:
+        max_keys = int(((ctx_len - ctx_start).clamp(min=0) + n_extra).max().item()) if q.shape[0] else 0
+    o = _C.attention(q.contiguous(), k_cache, v_cache, block_table, int(page), req, ctx_start, ctx_len, extra,
+                     n_extra, float(scale), int(max_keys), gate)
+    return o.reshape(o.shape[0], -1)
+
+
+# recurrent --------------------------------------------------------------------------------------------------------
+def causal_conv_tree(x, conv_state, state_slot, parent, weight):
+    return _C.conv_tree(x, conv_state, state_slot, parent, weight)
+
+
+def _gdn_offsets(cfg):
+    cd, vd, hv = cfg.gdn_conv_dim, cfg.gdn_value_dim, cfg.gdn_v_heads
+    return cd, cd + vd, cd + vd + hv
+
+
+def gdn_mixer(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent, scan: bool):
+    z_off, b_off, a_off = _gdn_offsets(cfg)
+    return _C.gdn_tree(conv, proj, z_off, b_off, a_off, a_log, dt_bias, state, state_slot, parent, norm_w,
+                       float(cfg.rms_norm_eps), cfg.gdn_k_heads, cfg.gdn_v_heads, cfg.gdn_k_dim, cfg.gdn_v_dim,
+                       bool(scan))
+
+
+def gdn_commit_all(convs, projs, states, conv_states, a_logs, dt_biases, slots, rows, n_rows, cfg):
+    _, b_off, a_off = _gdn_offsets(cfg)
+    _C.gdn_commit_all(list(convs), list(projs), list(states), list(conv_states), list(a_logs), list(dt_biases),
+                      b_off, a_off, slots, rows, n_rows, cfg.gdn_k_heads, cfg.gdn_v_heads, cfg.gdn_k_dim,
+                      cfg.gdn_v_dim, cfg.gdn_conv_dim, cfg.conv_kernel)
+
+
+def conv_commit_scan(conv_state, x_pre, state_slot, kw):
+    _C.conv_commit_scan(conv_state, x_pre, state_slot, int(kw))
+
+
+def mamba_tree(xbc, dt_raw, a_log, dt_bias, d_skip, state, state_slot, parent, cfg, scan: bool):
+    return _C.mamba_tree(xbc, dt_raw, a_log, dt_bias, d_skip, state, state_slot, parent, cfg.mamba_heads,
+                         cfg.mamba_head_dim, cfg.mamba_state, cfg.mamba_groups, bool(scan))
+
+
+def mamba_commit(xbc, dt_raw, a_log, dt_bias, d_skip, x_pre, state, conv_state, slots, rows, n_rows, cfg):
+    _C.mamba_commit(xbc, dt_raw, a_log, dt_bias, d_skip, state, slots, rows, n_rows, cfg.mamba_heads,
+                    cfg.mamba_head_dim, cfg.mamba_state, cfg.mamba_groups)
+    _C.conv_commit(x_pre, conv_state, slots, rows, n_rows, cfg.conv_kernel)
+
+
+_PTRS: Dict[tuple, Tuple[torch.Tensor, torch.Tensor]] = {}
+
+
+def kv_commit(k_caches, v_caches, src_slots, dst_slots):
+    if src_slots.numel() == 0:
+        return
+    key = tuple(t.data_ptr() for t in k_caches)
+    if key not in _PTRS:
+        dev = src_slots.device
+        _PTRS[key] = (torch.tensor([t.data_ptr() for t in k_caches], dtype=torch.int64, device=dev),
+                      torch.tensor([t.data_ptr() for t in v_caches], dtype=torch.int64, device=dev))
+    kp, vp = _PTRS[key]
+    row = k_caches[0].shape[1] * k_caches[0].shape[2]
+    _C.kv_commit(kp, vp, src_slots.long().contiguous(), dst_slots.long().contiguous(), row)
+
+
+# draft head -------------------------------------------------------------------------------------------------------
+def topk_rows(scores: torch.Tensor, k: int):
+    """Top-k per row (value desc, index asc) by a two-stage radix select."""
+    v, i = _C.topk_large(scores.float().contiguous(), int(k))
+    return v, i
+
+
+def candidate_logits(h, down, scores_w, lm_head, num_candidates: int):
+    lr = linear(h, down)
+    s = logits(lr, scores_w)
+    _, idx = topk_rows(s, num_candidates)
+    return idx, _C.gather_dot(h.contiguous(), lm_head, idx)
+
+
+def candidate_head(h, down, scores_w, lm_head, num_candidates: int, k: int):
+    idx, lg = candidate_logits(h, down, scores_w, lm_head, num_candidates)
+    probs, ids = _C.softmax_topk(lg, idx, int(k), 1.0)
+    return probs, ids
+
+
+def full_head_topk(h, lm_head, k: int):
+    lg = logits(h, lm_head)
+    if lg.shape[1] <= 1024:
+        probs, ids = _C.softmax_topk(lg, None, int(k), 1.0)
+        return probs, ids
+    p = torch.softmax(lg, dim=-1)
+    return torch.topk(p, k, dim=-1)
+
+
+def accept_greedy(target_ids, tokens, parent_rows, n_rows):
+    acc, cnt, bonus = _C.accept_greedy(target_ids, tokens, parent_rows, n_rows)
+    return acc, cnt, bonus

@@ -451,3 +451,28 @@ def full_head_topk(h: torch.Tensor, lm_head: torch.Tensor, k: int):
     lg = logits(h, lm_head)
     ids = torch.arange(lg.shape[1]).expand_as(lg)
     return softmax_topk(lg, ids, k)
+
+
+# ----------------------------------------------------------------------------------------------- fused GDN mixer
+def gdn_offsets(cfg):
+    """Column offsets of z, b and a in the fused GDN in_proj output ``[qkv | z | b | a]``."""
+    cd, vd, hv = cfg.gdn_conv_dim, cfg.gdn_value_dim, cfg.gdn_v_heads
+    return cd, cd + vd, cd + vd + hv
+
+
+def gdn_mixer(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent, scan: bool):
+    """Gates from the raw projection, the gated delta rule over the row forest, then the per-head gated RMSNorm:
+    ``[T, HV*V]``."""
+    z_off, b_off, a_off = gdn_offsets(cfg)
+    hv = cfg.gdn_v_heads
+    g, beta = gdn_gates(proj[:, a_off: a_off + hv], proj[:, b_off: b_off + hv], a_log, dt_bias)
+    o = gdn_tree(conv, g, beta, state, state_slot, parent, cfg, scan)
+    return gated_rmsnorm(o, proj[:, z_off: z_off + cfg.gdn_value_dim], norm_w, cfg.rms_norm_eps)
+
+
+def gdn_commit_all(convs, projs, states, conv_states, a_logs, dt_biases, slots, rows, n_rows, cfg) -> None:
+    z_off, b_off, a_off = gdn_offsets(cfg)
+    hv = cfg.gdn_v_heads
+    for conv, proj, st, cs, al, dtb in zip(convs, projs, states, conv_states, a_logs, dt_biases):
+        g, beta = gdn_gates(proj[:, a_off: a_off + hv], proj[:, b_off: b_off + hv], al, dtb)
+        gdn_commit(conv, g, beta, proj[:, : cfg.gdn_conv_dim], st, cs, slots, rows, n_rows, cfg)

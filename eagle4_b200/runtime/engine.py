@@ -11,39 +11,24 @@ Round structure (the reference's SGLang worker, ``eagle_harness/sglang/worker.py
 4. **accept**: greedy walk over the rows (bonus = target token at the last accepted row);
 5. **commit**: recurrent states replay the accepted path, attention KV of accepted rows moves to chain positions.
 
-Invariants: the draft KV and the target KV both hold positions ``[0, L)`` of a request; rows of a round live past
-``L`` (physical position ``L + row``) until commit. Plain decode is step 3-5 with one row, so every target op runs
-the same arithmetic in both modes and greedy output is identical.
+Every step of a round reads and writes *device state* (committed lengths, roots, pending draft-extend rows, emitted
+tokens) with fixed shapes, so on a GPU one round is one CUDA-graph replay per batch size and the host reads only the
+emitted tokens once per round. Invariants: draft and target KV hold positions ``[0, L)`` of a request; a round's rows
+live past ``L`` (physical position ``L + row``) until commit. Plain decode is steps 3-5 with one row, so every target
+op runs the same arithmetic in both modes and greedy output is identical.
 """
 
 from __future__ import annotations
 
-import time
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Sequence
 
 import torch
 
 from eagle4_b200 import ops
-from eagle4_b200.core.draft_tree import DraftTree, TreeShape, rows_meta
+from eagle4_b200.core.draft_tree import DraftTree, TreeShape
 from eagle4_b200.models.draft import DraftCache, DraftModel
 from eagle4_b200.models.target import Records, RowBatch, TargetCache, TargetModel
-
-
-@dataclass
-class Request:
-    prompt: List[int]
-    max_new: int
-    slot: int = -1
-    out: List[int] = field(default_factory=list)
-    L: int = 0  # committed positions in target and draft KV
-    root: int = -1  # emitted token not yet run through the target
-    ext_tokens: Optional[torch.Tensor] = None  # pending draft-extend tokens [n]
-    ext_aux: Optional[torch.Tensor] = None  # pending draft-extend target features [n, n_aux*H]
-
-    @property
-    def done(self) -> bool:
-        return len(self.out) >= self.max_new
 
 
 @dataclass
@@ -64,14 +49,36 @@ class RoundStats:
         return self.emitted / n if n else 0.0
 
 
+def tree_rows_meta(prow: torch.Tensor):
+    """Device-side verify-row structure from parent rows ``[bs, n]`` (row 0 the root with -1).
+
+    Returns ``(depth [bs, n] int64, anc [bs, n, n] bool)`` where ``anc[b, r, j]`` says row ``j`` is ``r`` or one of
+    its ancestors (path doubling over the parent relation; no host synchronisation).
+    """
+    bs, n = prow.shape
+    dev = prow.device
+    eye = torch.eye(n, dtype=torch.float32, device=dev).expand(bs, n, n)
+    par = torch.zeros(bs, n, n, dtype=torch.float32, device=dev)
+    par.scatter_(2, prow.clamp(min=0).long()[:, :, None], 1.0)
+    par[:, 0, :] = 0.0
+    anc = eye + par
+    reach = 1
+    while reach < n:
+        anc = ((anc + torch.bmm(anc, anc)) > 0).float()
+        reach *= 2
+    depth = anc.sum(-1).long() - 1
+    return depth, anc > 0
+
+
 class Engine:
     def __init__(self, target: TargetModel, draft: Optional[DraftModel], *, max_reqs: int, max_len: int,
-                 page: int = 16, steps: int = 4, top_k: int = 2, verify_tokens: int = 8):
+                 page: int = 16, steps: int = 4, top_k: int = 2, verify_tokens: int = 8, use_graphs: bool = True):
         self.target, self.draft = target, draft
         self.device = target.device
         self.dtype = target.dtype
         self.page = page
         self.steps, self.top_k, self.verify_tokens = steps, top_k, verify_tokens
+        self.max_reqs = max_reqs
         span = max(verify_tokens, steps * top_k) + 1
         self.max_len = max_len + span
         self.tcache = TargetCache.allocate(target.cfg, max_reqs=max_reqs, max_len=self.max_len, page=page,
@@ -83,188 +90,225 @@ class Engine:
             shape = TreeShape(top_k=top_k, max_depth=steps)
             self.tree = DraftTree(shape, max_reqs, draft.cfg.hidden_size, self.dtype, self.device,
                                   max_verify=min(verify_tokens, shape.work_cap))
-        self.free_slots = list(range(max_reqs))
+        dev, n = self.device, verify_tokens
+        i64, i32 = torch.int64, torch.int32
+        # device state, one row per batch position
+        self.L = torch.zeros(max_reqs, dtype=i64, device=dev)
+        self.root = torch.zeros(max_reqs, dtype=i64, device=dev)
+        self.slot = torch.arange(max_reqs, dtype=i32, device=dev)
+        self.ext_tok = torch.zeros(max_reqs, n, dtype=i64, device=dev)
+        self.ext_cnt = torch.zeros(max_reqs, dtype=i32, device=dev)
+        aux_w = (draft.cfg.num_aux * draft.cfg.target_hidden_size) if draft is not None else 1
+        self.ext_aux = torch.zeros(max_reqs, n, aux_w, dtype=self.dtype, device=dev)
+        self.out_tok = torch.zeros(max_reqs, n, dtype=i64, device=dev)
+        self.out_cnt = torch.zeros(max_reqs, dtype=i32, device=dev)
+        pin = dev.type == "cuda"
+        self.host_tok = torch.zeros(max_reqs, n, dtype=i64, pin_memory=pin)
+        self.host_cnt = torch.zeros(max_reqs, dtype=i32, pin_memory=pin)
+        self.use_graphs = use_graphs and dev.type == "cuda"
+        self.graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
         self.stats = RoundStats()
 
     # ------------------------------------------------------------------ helpers
-    def _slot(self, req: int, pos: torch.Tensor) -> torch.Tensor:
-        bt = self.tcache.block_table
+    def _slots(self, slot: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """Physical KV slots of positions ``pos`` in the block-table rows ``slot`` (broadcasting)."""
         pos = pos.long()
-        return bt[req, pos // self.page].long() * self.page + pos % self.page
+        return self.tcache.block_table[slot.long(), pos // self.page].long() * self.page + pos % self.page
 
-    def _t(self, data, dtype) -> torch.Tensor:
-        return torch.as_tensor(data, dtype=dtype, device=self.device)
+    def _i32(self, n: int, v: int) -> torch.Tensor:
+        return torch.full((n,), v, dtype=torch.int32, device=self.device)
 
-    def admit(self, req: Request) -> None:
-        req.slot = self.free_slots.pop(0)
-        self.tcache.reset_slot(req.slot)
+    # ------------------------------------------------------------------ prefill (eager)
+    def prefill(self, b: int, prompt: torch.Tensor) -> None:
+        """Prompt of batch row ``b`` through the target (recurrent layers in scan mode); the first token becomes the
+        root; the draft consumes all but the last ``N`` prompt rows now and the rest at the first round."""
+        n = prompt.shape[0]
+        slot = int(self.slot[b])
+        self.tcache.reset_slot(slot)
+        pos = torch.arange(n, device=self.device)
+        slots = self._slots(torch.tensor(slot, device=self.device), pos)
+        rb = RowBatch(ids=prompt.to(self.device), pos=pos, req=self._i32(n, slot), write_slot=slots,
+                      ctx_start=self._i32(n, 0), ctx_len=(pos + 1).int(),
+                      extra=torch.zeros(n, 1, dtype=torch.int32, device=self.device), n_extra=self._i32(n, 0),
+                      parent=(pos - 1).int(), state_slot=self._i32(n, slot), scan=True)
+        out, aux = self.target.forward(rb, self.tcache)
+        first, _ = self.target.greedy(out[-1:])
+        self.L[b] = n
+        self.root[b] = first[0]
+        self.out_tok[b, 0] = first[0]
+        self.out_cnt[b] = 1
+        if self.draft is None:
+            return
+        nxt = torch.cat([prompt.to(self.device)[1:], first])  # token following each prompt position
+        keep = min(n, self.verify_tokens)
+        lead = n - keep
+        if lead:
+            self._draft_rows(nxt[:lead], self.draft.project(aux[:lead]), pos[:lead], slot)
+        self.ext_tok[b, :keep] = nxt[lead:]
+        self.ext_aux[b, :keep] = aux[lead:]
+        self.ext_cnt[b] = keep
 
-    def release(self, req: Request) -> None:
-        self.free_slots.append(req.slot)
-        self.free_slots.sort()
+    def _draft_rows(self, ids, hidden, pos, slot: int):
+        w = self.draft.cfg.sliding_window
+        t = ids.shape[0]
+        start = (pos - w + 1).clamp(min=0) if w else torch.zeros_like(pos)
+        return self.draft.forward(ids, hidden, pos, self._i32(t, slot),
+                                  self._slots(torch.tensor(slot, device=self.device), pos), start.int(),
+                                  (pos + 1).int(), torch.zeros(t, 1, dtype=torch.int32, device=self.device),
+                                  self._i32(t, 0), self.dcache)
 
-    # ------------------------------------------------------------------ prefill
-    def prefill(self, reqs: List[Request]) -> None:
-        """Run the prompts through the target (recurrent layers in scan mode); emit the first token."""
-        for req in reqs:
-            n = len(req.prompt)
-            pos = torch.arange(n, device=self.device)
-            slots = self._slot(req.slot, pos)
-            one = lambda v: torch.full((n,), v, dtype=torch.int32, device=self.device)  # noqa: E731
-            rb = RowBatch(
-                ids=self._t(req.prompt, torch.int64), pos=pos, req=one(req.slot), write_slot=slots,
-                ctx_start=one(0), ctx_len=(pos + 1).int(), extra=torch.zeros(n, 1, dtype=torch.int32,
-                                                                             device=self.device),
-                n_extra=one(0), parent=(pos - 1).int(), state_slot=one(req.slot), scan=True,
-            )
-            out, aux = self.target.forward(rb, self.tcache)
-            ids, _ = self.target.greedy(out[-1:])
-            req.root = int(ids[0])
-            req.out.append(req.root)
-            req.L = n
-            if self.draft is not None:
-                req.ext_tokens = torch.cat([self._t(req.prompt[1:], torch.int64), ids.view(1)])
-                req.ext_aux = aux
-
-    # ------------------------------------------------------------------ plain decode
-    def plain_step(self, reqs: List[Request]) -> None:
-        """One token per request: a one-row verify plus its commit."""
-        bs = len(reqs)
-        L = self._t([r.L for r in reqs], torch.int64)
-        slots = torch.stack([self._slot(r.slot, L[i:i + 1])[0] for i, r in enumerate(reqs)])
-        rb = RowBatch(
-            ids=self._t([r.root for r in reqs], torch.int64), pos=L, req=self._t([r.slot for r in reqs], torch.int32),
-            write_slot=slots, ctx_start=torch.zeros(bs, dtype=torch.int32, device=self.device), ctx_len=L.int(),
-            extra=slots.int().view(bs, 1), n_extra=torch.ones(bs, dtype=torch.int32, device=self.device),
-            parent=torch.full((bs,), -1, dtype=torch.int32, device=self.device),
-            state_slot=self._t([r.slot for r in reqs], torch.int32),
-        )
+    # ------------------------------------------------------------------ device-state rounds
+    def _plain_round(self, bs: int) -> None:
+        """One token per request: a one-row verify plus its commit, all on device state."""
+        L, sl = self.L[:bs], self.slot[:bs]
+        slots = self._slots(sl, L)
+        rb = RowBatch(ids=self.root[:bs].clone(), pos=L.clone(), req=sl, write_slot=slots,
+                      ctx_start=torch.zeros(bs, dtype=torch.int32, device=self.device), ctx_len=L.int(),
+                      extra=slots.int().view(bs, 1), n_extra=torch.ones(bs, dtype=torch.int32, device=self.device),
+                      parent=torch.full((bs,), -1, dtype=torch.int32, device=self.device), state_slot=sl,
+                      max_keys=self.max_len)
         rec = Records()
         out, _ = self.target.forward(rb, self.tcache, rec)
         ids, _ = self.target.greedy(out)
         rows = torch.arange(bs, dtype=torch.int32, device=self.device).view(bs, 1)
-        self.target.commit(self.tcache, rec, rows, torch.ones(bs, dtype=torch.int32, device=self.device),
-                           rb.state_slot, slots, slots)
-        for r, t in zip(reqs, ids.tolist()):
-            r.L += 1
-            r.root = t
-            r.out.append(t)
+        self.target.commit(self.tcache, rec, rows, torch.ones(bs, dtype=torch.int32, device=self.device), sl,
+                           slots, slots)
+        self.L[:bs] += 1
+        self.root[:bs] = ids
+        self.out_tok[:bs, 0] = ids
+        self.out_cnt[:bs] = 1
 
-    # ------------------------------------------------------------------ speculative round
-    def _draft_extend(self, reqs: List[Request]) -> None:
-        draft, cfg = self.draft, self.draft.cfg
-        ids, aux, pos, req_idx, last = [], [], [], [], []
-        total = 0
-        for r in reqs:
-            n = r.ext_tokens.shape[0]
-            ids.append(r.ext_tokens)
-            aux.append(r.ext_aux)
-            pos.append(torch.arange(r.L - n, r.L, device=self.device))
-            req_idx.append(torch.full((n,), r.slot, dtype=torch.int32, device=self.device))
-            total += n
-            last.append(total - 1)
-        ids, aux, pos, req_idx = torch.cat(ids), torch.cat(aux), torch.cat(pos), torch.cat(req_idx)
-        t = ids.shape[0]
-        w = cfg.sliding_window
+    def _draft_extend(self, bs: int) -> None:
+        """Pending rows (``ext_cnt <= N`` per request, padded to N) through the draft; the last valid row's top-K
+        seeds the tree. Padded rows write draft KV into the tree region past L, which the steps overwrite."""
+        n, dev = self.verify_tokens, self.device
+        draft, w = self.draft, self.draft.cfg.sliding_window
+        cnt = self.ext_cnt[:bs].long()
+        d = torch.arange(n, device=dev)
+        pos = (self.L[:bs, None] - cnt[:, None] + d[None, :]).clamp(min=0)  # [bs, n]
+        sl = self.slot[:bs]
+        slots = self._slots(sl[:, None], pos)
         start = (pos - w + 1).clamp(min=0) if w else torch.zeros_like(pos)
-        hidden = draft.project(aux)
-        slots = self.tcache.block_table[req_idx.long(), pos // self.page].long() * self.page + pos % self.page
-        normed, nh = draft.forward(ids, hidden, pos, req_idx, slots, start.int(), (pos + 1).int(),
-                                   torch.zeros(t, 1, dtype=torch.int32, device=self.device),
-                                   torch.zeros(t, dtype=torch.int32, device=self.device), self.dcache)
-        sel = self._t(last, torch.int64)
-        probs, toks = draft.candidates(normed.index_select(0, sel), self.top_k)
-        self.tree.stage_root(len(reqs), probs, toks, nh.index_select(0, sel))
-        for r in reqs:
-            r.ext_tokens = r.ext_aux = None
+        hidden = draft.project(self.ext_aux[:bs].reshape(bs * n, -1))
+        t = bs * n
+        normed, nh = draft.forward(self.ext_tok[:bs].reshape(-1), hidden, pos.reshape(-1),
+                                   sl.repeat_interleave(n), slots.reshape(-1), start.reshape(-1).int(),
+                                   (pos + 1).reshape(-1).int(), torch.zeros(t, 1, dtype=torch.int32, device=dev),
+                                   torch.zeros(t, dtype=torch.int32, device=dev), self.dcache,
+                                   max_keys=self.max_len)
+        last = torch.arange(bs, device=dev) * n + (cnt - 1).clamp(min=0)
+        probs, toks = draft.candidates(normed.index_select(0, last), self.top_k, pos.reshape(-1).index_select(0, last))
+        self.tree.stage_root(bs, probs, toks, nh.index_select(0, last))
 
-    def _draft_steps(self, reqs: List[Request]) -> None:
-        bs, k, tree, draft = len(reqs), self.top_k, self.tree, self.draft
+    def _draft_steps(self, bs: int) -> None:
+        k, tree, draft, dev = self.top_k, self.tree, self.draft, self.device
         w = draft.cfg.sliding_window
-        L = self._t([r.L for r in reqs], torch.int64)
-        req_idx = self._t([r.slot for r in reqs], torch.int32).repeat_interleave(k)
-        lane = torch.arange(k, device=self.device).repeat(bs)
-        Lr = L.repeat_interleave(k)
+        Lr = self.L[:bs].repeat_interleave(k)
+        req = self.slot[:bs].repeat_interleave(k)
+        lane = torch.arange(k, device=dev).repeat(bs)
+        start = ((Lr - w).clamp(min=0) if w else torch.zeros_like(Lr)).int()
+        keys = min(w, self.max_len) + self.steps if w else self.max_len + self.steps
         tree.begin(bs)
         for s in range(1, self.steps):
-            phys = Lr + (s - 1) * k + lane
-            slots = self.tcache.block_table[req_idx.long(), phys // self.page].long() * self.page + phys % self.page
+            slots = self._slots(req, Lr + (s - 1) * k + lane)
             tree.set_step_slots(bs, s, slots.view(bs, k))
             extra = tree.ancestors[:bs, :, :s].reshape(bs * k, s).contiguous()
-            n_extra = torch.full((bs * k,), s, dtype=torch.int32, device=self.device)
-            start = (Lr - w).clamp(min=0) if w else torch.zeros_like(Lr)
-            normed, nh = draft.forward(tree.front_tokens[: bs * k], tree.front_hidden[: bs * k], Lr - 1 + s, req_idx,
-                                       slots, start.int(), Lr.int(), extra, n_extra, self.dcache)
-            probs, toks = draft.candidates(normed, k)
+            n_extra = torch.full((bs * k,), s, dtype=torch.int32, device=dev)
+            normed, nh = draft.forward(tree.front_tokens[: bs * k], tree.front_hidden[: bs * k], Lr - 1 + s, req,
+                                       slots, start, Lr.int(), extra, n_extra, self.dcache, max_keys=keys)
+            probs, toks = draft.candidates(normed, k, Lr - 1 + s)
             tree.step(bs, s, probs, toks, nh)
 
-    def spec_round(self, reqs: List[Request]) -> None:
-        bs, n = len(reqs), self.verify_tokens
-        self._draft_extend(reqs)
-        self._draft_steps(reqs)
+    def _spec_round(self, bs: int) -> None:
+        n, dev = self.verify_tokens, self.device
+        self._draft_extend(bs)
+        self._draft_steps(bs)
         toks, prow = self.tree.verify_rows(bs, self.steps, n - 1)
-        roots = self._t([r.root for r in reqs], torch.int64).view(bs, 1)
-        tokens = torch.cat([roots, toks], dim=1)  # [bs, n]
-        depth, mask = rows_meta(prow)
-        L = self._t([r.L for r in reqs], torch.int64)
-        sl = self._t([r.slot for r in reqs], torch.int32)
-        rowidx = torch.arange(n, device=self.device)
-        phys = L[:, None] + rowidx[None, :]
-        slots = self.tcache.block_table[sl.long()[:, None], phys // self.page].long() * self.page + phys % self.page
-        # extra slots: the row's ancestors and itself, in row order
-        bits = ((mask[:, :, None] >> rowidx[None, None, :]) & 1).bool()  # [bs, n(row), n(j)]
-        n_extra = bits.sum(-1).int()
-        order = torch.argsort((~bits).int() * n + rowidx, dim=-1)  # set bits first, ascending j
+        tokens = torch.cat([self.root[:bs, None], toks], dim=1)  # [bs, n]
+        depth, anc = tree_rows_meta(prow)
+        L, sl = self.L[:bs], self.slot[:bs]
+        rowidx = torch.arange(n, device=dev)
+        slots = self._slots(sl[:, None], L[:, None] + rowidx[None, :])  # [bs, n] physical slot of row r at L + r
+        key = (~anc).long() * n + rowidx[None, None, :]
+        order = torch.argsort(key, dim=-1)
         extra = torch.gather(slots[:, None, :].expand(bs, n, n), 2, order).int()
-        parent = torch.where(prow >= 0, prow + torch.arange(bs, device=self.device)[:, None] * n, prow)
-        rb = RowBatch(
-            ids=tokens.reshape(-1), pos=(L[:, None] + depth).reshape(-1), req=sl.repeat_interleave(n),
-            write_slot=slots.reshape(-1), ctx_start=torch.zeros(bs * n, dtype=torch.int32, device=self.device),
-            ctx_len=L.int().repeat_interleave(n), extra=extra.reshape(bs * n, n), n_extra=n_extra.reshape(-1),
-            parent=parent.reshape(-1).int(), state_slot=sl.repeat_interleave(n),
-        )
+        base = (torch.arange(bs, device=dev) * n)[:, None]
+        parent = torch.where(prow >= 0, prow + base, prow)
+        rb = RowBatch(ids=tokens.reshape(-1), pos=(L[:, None] + depth).reshape(-1), req=sl.repeat_interleave(n),
+                      write_slot=slots.reshape(-1), ctx_start=torch.zeros(bs * n, dtype=torch.int32, device=dev),
+                      ctx_len=L.int().repeat_interleave(n), extra=extra.reshape(bs * n, n),
+                      n_extra=anc.sum(-1).int().reshape(-1), parent=parent.reshape(-1).int(),
+                      state_slot=sl.repeat_interleave(n), max_keys=self.max_len)
         rec = Records()
         out, aux = self.target.forward(rb, self.tcache, rec)
         tid, _ = self.target.greedy(out)
-        tid = tid.view(bs, n)
-        acc, cnt, bonus = ops.accept_greedy(tid, tokens, prow, torch.full((bs,), n, dtype=torch.int32,
-                                                                          device=self.device))
-        acc_c, cnt_c, bonus_c = acc.cpu(), cnt.cpu(), bonus.cpu()
-        base = torch.arange(bs, device=self.device)[:, None] * n
-        rows = torch.where(acc >= 0, acc + base, torch.zeros_like(acc)).int()
-        src = torch.gather(slots, 1, acc.clamp(min=0).long())
-        dst = slots  # position L + d
-        valid = rowidx[None, :] < cnt.to(self.device)[:, None]
-        self.target.commit(self.tcache, rec, rows, cnt.to(self.device).int(), sl, src[valid], dst[valid])
-        accepted = []
-        for b, r in enumerate(reqs):
-            c = int(cnt_c[b])
-            path = acc_c[b, :c].tolist()
-            new = [int(tokens[b, j]) for j in path[1:]] + [int(bonus_c[b])]
-            room = r.max_new - len(r.out)
-            r.out.extend(new[:room])
-            accepted.append(min(len(new), room))
-            keep = self._t(path, torch.int64) + b * n
-            r.ext_tokens = self._t(new, torch.int64)
-            r.ext_aux = aux.index_select(0, keep)
-            r.L += c
-            r.root = new[-1]
-        self.stats.record(accepted)
+        acc, cnt, bonus = ops.accept_greedy(tid.view(bs, n), tokens, prow,
+                                            torch.full((bs,), n, dtype=torch.int32, device=dev))
+        cnt = cnt.to(torch.int32)
+        accc = acc.long().clamp(min=0)
+        valid = rowidx[None, :] < cnt[:, None]
+        rows = torch.where(valid, accc + base, torch.zeros_like(accc)).int()
+        src = torch.gather(slots, 1, accc)
+        dst = torch.where(valid, slots, src)  # invalid entries copy a slot onto itself (skipped)
+        self.target.commit(self.tcache, rec, rows, cnt, sl, src.reshape(-1), dst.reshape(-1))
+        # emitted tokens: the accepted drafted tokens then the bonus; they are also the next extend's inputs
+        path_tok = torch.gather(tokens, 1, accc)
+        shifted = torch.cat([path_tok[:, 1:], torch.zeros_like(path_tok[:, :1])], dim=1)
+        c1 = (cnt - 1)[:, None]
+        emitted = torch.where(rowidx[None, :] < c1, shifted,
+                              torch.where(rowidx[None, :] == c1, bonus[:, None], torch.zeros_like(shifted)))
+        self.out_tok[:bs] = emitted
+        self.out_cnt[:bs] = cnt
+        self.ext_tok[:bs] = emitted
+        self.ext_cnt[:bs] = cnt
+        self.ext_aux[:bs] = aux.index_select(0, (accc + base).reshape(-1)).view(bs, n, -1)
+        self.L[:bs] += cnt.long()
+        self.root[:bs] = bonus
+
+    def _run(self, kind: str, bs: int) -> None:
+        """One round; on a GPU the first round of a (kind, batch size) runs eagerly (which also sizes every
+        lazily allocated workspace) and is then captured, and later rounds replay the graph."""
+        fn = self._spec_round if kind == "spec" else self._plain_round
+        key = (kind, bs)
+        g = self.graphs.get(key)
+        if g is not None:
+            g.replay()
+            return
+        fn(bs)
+        if self.use_graphs:
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn(bs)  # recorded, not executed
+            self.graphs[key] = g
 
     # ------------------------------------------------------------------ driver
-    def generate(self, prompts: Sequence[Sequence[int]], max_new_tokens: int, *, speculative: bool = True
-                 ) -> List[List[int]]:
-        reqs = [Request(list(p), max_new_tokens) for p in prompts]
-        for r in reqs:
-            self.admit(r)
-        self.prefill(reqs)
-        active = [r for r in reqs if not r.done]
-        while active:
-            if speculative and self.draft is not None:
-                self.spec_round(active)
-            else:
-                self.plain_step(active)
-            active = [r for r in active if not r.done]
-        for r in reqs:
-            self.release(r)
-        return [r.out[:max_new_tokens] for r in reqs]
+    def generate(self, prompts, max_new_tokens: int, *, speculative: bool = True) -> List[List[int]]:
+        """Static batch: all prompts prefill, then rounds until every request has ``max_new_tokens`` tokens."""
+        prompts = [p if torch.is_tensor(p) else torch.tensor(list(p), dtype=torch.int64) for p in prompts]
+        bs = len(prompts)
+        if bs > self.max_reqs:
+            raise ValueError(f"batch {bs} exceeds max_reqs {self.max_reqs}")
+        outs: List[List[int]] = [[] for _ in range(bs)]
+        for b, p in enumerate(prompts):
+            self.prefill(b, p)
+        self.host_tok[:bs].copy_(self.out_tok[:bs])
+        for b in range(bs):
+            outs[b].append(int(self.host_tok[b, 0]))
+        spec = speculative and self.draft is not None
+        while min(len(o) for o in outs) < max_new_tokens:
+            self._run("spec" if spec else "plain", bs)
+            self.host_tok[:bs].copy_(self.out_tok[:bs], non_blocking=True)
+            self.host_cnt[:bs].copy_(self.out_cnt[:bs], non_blocking=True)
+            if self.device.type == "cuda":
+                torch.cuda.current_stream().synchronize()
+            got = []
+            for b in range(bs):
+                c = int(self.host_cnt[b])
+                room = max_new_tokens - len(outs[b])
+                take = min(c, room)
+                outs[b].extend(self.host_tok[b, :take].tolist())
+                got.append(take)
+            if spec:
+                self.stats.record(got)
+        return [o[:max_new_tokens] for o in outs]

@@ -38,23 +38,17 @@ def test_spec_accepts_oracle_draft():
     plain = Engine(tgt, drf, max_reqs=1, max_len=96, steps=4, top_k=2, verify_tokens=8)
     ref = plain.generate(prompts, 24, speculative=False)[0]
     seq = prompts[0] + ref + [0] * 16
-    stash = {}
-    fwd, cand = drf.forward, drf.candidates
+    cand = drf.candidates
 
-    def forward(ids, hidden, pos, *a, **kw):
-        stash["pos"] = pos
-        return fwd(ids, hidden, pos, *a, **kw)
-
-    def candidates(normed, k):
-        pos = stash["pos"][-normed.shape[0]:] if normed.shape[0] < stash["pos"].shape[0] else stash["pos"]
+    def candidates(normed, k, pos):
         want = torch.tensor([seq[int(p) + 2] for p in pos])
         ids = torch.stack([want] + [(want + j) % tgt.cfg.vocab_size for j in range(1, k)], dim=1)
         probs = torch.tensor([[0.9] + [0.1 / (k - 1)] * (k - 1)]).expand(normed.shape[0], k)
         return probs, ids
 
-    drf.forward, drf.candidates = forward, candidates
+    drf.candidates = candidates
     eng = Engine(tgt, drf, max_reqs=1, max_len=96, steps=4, top_k=2, verify_tokens=8)
     out = eng.generate(prompts, 24, speculative=True)[0]
-    drf.forward, drf.candidates = fwd, cand
+    drf.candidates = cand
     assert out == ref
     assert eng.stats.mean_accept > 3.0  # depth-4 trees: root + 3 drafted levels + bonus per round
