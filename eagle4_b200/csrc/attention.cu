@@ -43,7 +43,7 @@ attn_chunk_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __re
   const int total = nctx + ne;
   const int k_begin = chunk * kChunk;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __shared__ float sq[kMaxG * D];
+  __shared__ __align__(16) float sq[kMaxG * D];
   __shared__ float sm_m[kWarps][kMaxG], sm_l[kWarps][kMaxG];
   __shared__ float sm_acc[kWarps][kMaxG][D];
   if (k_begin >= total) {
@@ -75,19 +75,30 @@ attn_chunk_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __re
   for (int g = 0; g < kMaxG; ++g) s[g] = 0.f;
   if (live) {
     const uint4* kp = reinterpret_cast<const uint4*>(kc + (size_t(slot) * Hk + h) * D);
-#pragma unroll 4
+    const float4* q4 = reinterpret_cast<const float4*>(sq);
+#pragma unroll 2
     for (int c = 0; c < D / 8; ++c) {
       const uint4 raw = kp[c];
       const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      float kf[8];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float2 kf = __bfloat1622float2(k2[j]);
+        const float2 f = __bfloat1622float2(k2[j]);
+        kf[2 * j] = f.x;
+        kf[2 * j + 1] = f.y;
+      }
 #pragma unroll
-        for (int g = 0; g < kMaxG; ++g) {
-          if (g < G) {
-            s[g] = fmaf(sq[g * D + c * 8 + 2 * j], kf.x, s[g]);
-            s[g] = fmaf(sq[g * D + c * 8 + 2 * j + 1], kf.y, s[g]);
-          }
+      for (int g = 0; g < kMaxG; ++g) {
+        if (g < G) {
+          const float4 qa = q4[(g * D + c * 8) / 4], qb = q4[(g * D + c * 8) / 4 + 1];
+          s[g] = fmaf(qa.x, kf[0], s[g]);
+          s[g] = fmaf(qa.y, kf[1], s[g]);
+          s[g] = fmaf(qa.z, kf[2], s[g]);
+          s[g] = fmaf(qa.w, kf[3], s[g]);
+          s[g] = fmaf(qb.x, kf[4], s[g]);
+          s[g] = fmaf(qb.y, kf[5], s[g]);
+          s[g] = fmaf(qb.z, kf[6], s[g]);
+          s[g] = fmaf(qb.w, kf[7], s[g]);
         }
       }
     }

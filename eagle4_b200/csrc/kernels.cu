@@ -28,22 +28,62 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 __device__ __forceinline__ float bf(const __nv_bfloat16 x) { return __bfloat162float(x); }
 
-// y = x * rsqrt(mean(x^2) + eps) * (w or 1 + w)
+// y = x * rsqrt(mean(x^2) + eps) * (w or 1 + w). Rows of H <= 8192 elements (H % 8 == 0): each thread loads its
+// 16-byte vectors up front (the loads are independent, so they overlap), then reduces.
+constexpr int kMaxVec = 4;  // 16-byte vectors per thread: 256 threads x 4 x 8 = 8192 elements
+__device__ __forceinline__ void load_row(const __nv_bfloat16* __restrict__ x, int H, uint4* v, int& nv) {
+  nv = 0;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c < H / 8) { v[i] = reinterpret_cast<const uint4*>(x)[c]; nv = i + 1; }
+  }
+}
+__device__ __forceinline__ float sumsq(const uint4* v, int nv) {
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    if (i >= nv) break;
+    const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v[i]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(p[j]);
+      ss = fmaf(f.x, f.x, ss);
+      ss = fmaf(f.y, f.y, ss);
+    }
+  }
+  return ss;
+}
+__device__ __forceinline__ void store_normed(const uint4* v, int nv, const __nv_bfloat16* __restrict__ w, int offset,
+                                             float rs, __nv_bfloat16* __restrict__ y) {
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    if (i >= nv) break;
+    const int c = threadIdx.x + i * blockDim.x;
+    const uint4 wv = reinterpret_cast<const uint4*>(w)[c];
+    const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&v[i]);
+    const __nv_bfloat162* wp = reinterpret_cast<const __nv_bfloat162*>(&wv);
+    uint4 out;
+    __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 xf = __bfloat1622float2(xp[j]), wf = __bfloat1622float2(wp[j]);
+      const float sx = offset ? 1.f + wf.x : wf.x, sy = offset ? 1.f + wf.y : wf.y;
+      op[j] = __floats2bfloat162_rn(xf.x * rs * sx, xf.y * rs * sy);
+    }
+    reinterpret_cast<uint4*>(y)[c] = out;
+  }
+}
+
 __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int ldx, const __nv_bfloat16* __restrict__ w,
                                __nv_bfloat16* __restrict__ y, int ldy, int H, float eps, int offset) {
   __shared__ float red[32];
   const size_t r = blockIdx.x;
-  const __nv_bfloat16* xr = x + r * ldx;
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    const float v = bf(xr[i]);
-    ss += v * v;
-  }
-  const float rs = rsqrtf(block_sum(ss, red) / H + eps);
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    const float s = offset ? 1.f + bf(w[i]) : bf(w[i]);
-    y[r * ldy + i] = __float2bfloat16(bf(xr[i]) * rs * s);
-  }
+  uint4 v[kMaxVec];
+  int nv;
+  load_row(x + r * ldx, H, v, nv);
+  const float rs = rsqrtf(block_sum(sumsq(v, nv), red) / H + eps);
+  store_normed(v, nv, w, offset, rs, y + r * ldy);
 }
 
 // y[r] = [rmsnorm(e[r], we) | rmsnorm(h[r], wh)]
@@ -52,18 +92,14 @@ __global__ void concat_norms_kernel(const __nv_bfloat16* __restrict__ e, const _
                                     __nv_bfloat16* __restrict__ y, int H, float eps) {
   __shared__ float red[32];
   const size_t r = blockIdx.x;
-  for (int part = 0; part < 2; ++part) {
-    const __nv_bfloat16* xr = part == 0 ? e + r * H : h + r * ldh;
-    const __nv_bfloat16* w = part == 0 ? we : wh;
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) {
-      const float v = bf(xr[i]);
-      ss += v * v;
-    }
-    const float rs = rsqrtf(block_sum(ss, red) / H + eps);
-    for (int i = threadIdx.x; i < H; i += blockDim.x)
-      y[r * 2 * H + part * H + i] = __float2bfloat16(bf(xr[i]) * rs * bf(w[i]));
-  }
+  uint4 ve[kMaxVec], vh[kMaxVec];
+  int ne, nh;
+  load_row(e + r * H, H, ve, ne);
+  load_row(h + r * ldh, H, vh, nh);
+  const float re = rsqrtf(block_sum(sumsq(ve, ne), red) / H + eps);
+  const float rh = rsqrtf(block_sum(sumsq(vh, nh), red) / H + eps);
+  store_normed(ve, ne, we, 0, re, y + r * 2 * H);
+  store_normed(vh, nh, wh, 0, rh, y + r * 2 * H + H);
 }
 
 __global__ void embedding_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
@@ -119,13 +155,16 @@ __global__ void gdn_gates_kernel(const __nv_bfloat16* __restrict__ a, const __nv
 
 // Split the fused attention projection, RMS-normalise q and k per head (optional), rotate the first ``rot`` dims
 // (NeoX halves, cos/sin from a table), write K and V at the row's cache slot and q to a contiguous buffer.
-// One block per row; ``qkv`` row layout [q (Hq*D) | gate (Hq*D, optional) | k (Hk*D) | v (Hk*D)].
-__global__ void qkv_prepare_kernel(const __nv_bfloat16* __restrict__ qkv, int ldq, const int64_t* __restrict__ pos,
-                                   const int64_t* __restrict__ slot, __nv_bfloat16* kc, __nv_bfloat16* vc,
-                                   const __nv_bfloat16* __restrict__ qn, const __nv_bfloat16* __restrict__ kn,
-                                   int norm_offset, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                                   __nv_bfloat16* __restrict__ qout, int Hq, int Hk, int D, int rot, int gated,
-                                   float eps) {
+// One block per row, one warp per head; a head's D values are loaded as 16-byte vectors into shared memory first.
+// ``qkv`` row layout [q (Hq*D) | gate (Hq*D, optional) | k (Hk*D) | v (Hk*D)].
+constexpr int kPrepWarps = 8;
+__global__ void __launch_bounds__(kPrepWarps * 32)
+qkv_prepare_kernel(const __nv_bfloat16* __restrict__ qkv, int ldq, const int64_t* __restrict__ pos,
+                   const int64_t* __restrict__ slot, __nv_bfloat16* kc, __nv_bfloat16* vc,
+                   const __nv_bfloat16* __restrict__ qn, const __nv_bfloat16* __restrict__ kn, int norm_offset,
+                   const float* __restrict__ cos_t, const float* __restrict__ sin_t, __nv_bfloat16* __restrict__ qout,
+                   int Hq, int Hk, int D, int rot, int gated, float eps) {
+  __shared__ float buf[kPrepWarps][256];
   const size_t r = blockIdx.x;
   const __nv_bfloat16* row = qkv + r * ldq;
   const int64_t p = pos[r];
@@ -133,39 +172,50 @@ __global__ void qkv_prepare_kernel(const __nv_bfloat16* __restrict__ qkv, int ld
   const int half = rot / 2;
   const int koff = Hq * D * (gated ? 2 : 1);
   const int voff = koff + Hk * D;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  // heads 0..Hq-1 are q, Hq..Hq+Hk-1 are k: one warp per head
-  for (int hh = warp; hh < Hq + Hk; hh += nw) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* hb = buf[warp];
+  for (int hh = warp; hh < Hq + Hk; hh += kPrepWarps) {
     const bool isq = hh < Hq;
     const __nv_bfloat16* src = row + (isq ? hh * D : koff + (hh - Hq) * D);
-    const __nv_bfloat16* nw_ = isq ? qn : kn;
-    float rs = 1.f;
-    if (nw_) {
-      float ss = 0.f;
-      for (int i = lane; i < D; i += 32) {
-        const float v = bf(src[i]);
-        ss += v * v;
+    const __nv_bfloat16* nw = isq ? qn : kn;
+    for (int c = lane; c < D / 8; c += 32) {
+      const uint4 raw = reinterpret_cast<const uint4*>(src)[c];
+      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(p2[j]);
+        hb[c * 8 + 2 * j] = f.x;
+        hb[c * 8 + 2 * j + 1] = f.y;
       }
-      rs = rsqrtf(warp_sum(ss) / D + eps);
+    }
+    __syncwarp();
+    if (nw) {
+      float ss = 0.f;
+      for (int i = lane; i < D; i += 32) ss = fmaf(hb[i], hb[i], ss);
+      const float rs = rsqrtf(warp_sum(ss) / D + eps);
+      __syncwarp();
+      for (int i = lane; i < D; i += 32) {
+        const float wv = __bfloat162float(nw[i]);
+        hb[i] = __bfloat162float(__float2bfloat16(hb[i] * rs * (norm_offset ? 1.f + wv : wv)));
+      }
+      __syncwarp();
     }
     __nv_bfloat16* dst = isq ? qout + (r * Hq + hh) * D : kc + (size_t(s) * Hk + (hh - Hq)) * D;
     for (int i = lane; i < D; i += 32) {
-      float v = bf(src[i]) * rs;
-      if (nw_) v = __bfloat162float(__float2bfloat16(v * (norm_offset ? 1.f + bf(nw_[i]) : bf(nw_[i]))));
+      float v = hb[i];
       if (i < rot) {
         const int j = i < half ? i : i - half;
-        float other = bf(src[i < half ? i + half : i - half]) * rs;
-        if (nw_) {
-          const int oi = i < half ? i + half : i - half;
-          other = __bfloat162float(__float2bfloat16(other * (norm_offset ? 1.f + bf(nw_[oi]) : bf(nw_[oi]))));
-        }
+        const float other = hb[i < half ? i + half : i - half];
         const float c = cos_t[p * half + j], sn = sin_t[p * half + j];
         v = i < half ? v * c - other * sn : v * c + other * sn;
       }
       dst[i] = __float2bfloat16(v);
     }
+    __syncwarp();
   }
-  for (int i = threadIdx.x; i < Hk * D; i += blockDim.x) vc[size_t(s) * Hk * D + i] = row[voff + i];
+  const uint4* vs = reinterpret_cast<const uint4*>(row + voff);
+  uint4* vd = reinterpret_cast<uint4*>(vc + size_t(s) * Hk * D);
+  for (int i = threadIdx.x; i < Hk * D / 8; i += blockDim.x) vd[i] = vs[i];
 }
 
 // Greedy head: reduce per-tile (max, argmax) partials to one id per token (ties to the lower id).
@@ -232,6 +282,7 @@ torch::Tensor rmsnorm(const torch::Tensor& x, const torch::Tensor& w, double eps
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1);
   const at::cuda::CUDAGuard g(x.device());
   const int H = x.size(-1);
+  TORCH_CHECK(H % 8 == 0 && H <= kRowThreads * kMaxVec * 8, "rmsnorm: H must be a multiple of 8 up to 8192");
   auto x2 = x.reshape({-1, H});
   auto y = torch::empty({x2.size(0), H}, x.options());
   if (x2.size(0))
@@ -244,6 +295,7 @@ torch::Tensor concat_norms(const torch::Tensor& e, const torch::Tensor& h, const
                            const torch::Tensor& wh, double eps) {
   const at::cuda::CUDAGuard g(e.device());
   const int T = e.size(0), H = e.size(1);
+  TORCH_CHECK(H % 8 == 0 && H <= kRowThreads * kMaxVec * 8 && h.stride(0) % 8 == 0);
   auto y = torch::empty({T, 2 * H}, e.options());
   if (T)
     concat_norms_kernel<<<T, kRowThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
@@ -311,9 +363,10 @@ torch::Tensor qkv_prepare(const torch::Tensor& qkv, const torch::Tensor& pos, co
                           double eps) {
   const at::cuda::CUDAGuard g(qkv.device());
   const int T = qkv.size(0);
+  TORCH_CHECK(D % 8 == 0 && D <= 256 && qkv.stride(0) % 8 == 0, "qkv_prepare: D must be a multiple of 8 up to 256");
   auto q = torch::empty({T, Hq, D}, qkv.options());
   if (T)
-    qkv_prepare_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+    qkv_prepare_kernel<<<T, kPrepWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
         CBF16(qkv), qkv.stride(0), pos.data_ptr<int64_t>(), slot.data_ptr<int64_t>(), BF16(kc), BF16(vc),
         qn ? CBF16(*qn) : nullptr, kn ? CBF16(*kn) : nullptr, norm_offset ? 1 : 0, cos_t.data_ptr<float>(),
         sin_t.data_ptr<float>(), BF16(q), Hq, Hk, D, rot, gated ? 1 : 0, float(eps));

@@ -95,51 +95,87 @@ __device__ __forceinline__ float2 gdn_gate(const GdnArgs& a, int row, int h) {
   return make_float2(g, beta);
 }
 
-// Loads the l2-normalised q (scaled by K^-1/2) and k of ``row`` for key head ``kh`` into shared memory.
+constexpr int kGdnTile = 32;  // path nodes staged in shared memory at a time
+
+// Shared-memory staging of up to kGdnTile nodes: l2-normalised q (scaled by K^-1/2) and k of the key head, the
+// thread's v value of every node, and the node gates.
 template <int K>
-__device__ __forceinline__ void gdn_load_qk(const GdnArgs& a, int row, int kh, float* sq, float* sk, float* red) {
-  const __nv_bfloat16* base = a.qkv + size_t(row) * a.ldq;
-  const int t = threadIdx.x;
-  float qv = 0.f, kv = 0.f;
-  if (t < K) {
-    qv = bf(base[kh * K + t]);
-    kv = bf(base[a.HK * K + kh * K + t]);
+struct GdnStage {
+  float q[kGdnTile][K];
+  float k[kGdnTile][K];
+  float v[kGdnTile][128];
+  float g[kGdnTile], beta[kGdnTile];
+};
+
+// Stage ``n`` (<= kGdnTile) nodes ``rows[0..n)``: warp w normalises nodes w, w+4, ... (fixed-order warp sums).
+template <int K>
+__device__ __forceinline__ void gdn_stage(const GdnArgs& a, const int* rows, int n, int h, int kh, GdnStage<K>& st) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  constexpr int PL = K / 32;
+  for (int j = warp; j < n; j += nw) {
+    const int row = rows[j];
+    const __nv_bfloat16* base = a.qkv + size_t(row) * a.ldq;
+    float qv[PL], kv[PL];
+    float q2 = 0.f, k2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      qv[i] = bf(base[kh * K + lane * PL + i]);
+      kv[i] = bf(base[a.HK * K + kh * K + lane * PL + i]);
+      q2 = fmaf(qv[i], qv[i], q2);
+      k2 = fmaf(kv[i], kv[i], k2);
+    }
+    const float rq = rsqrtf(warp_sum(q2) + 1e-6f) * rsqrtf(float(K));
+    const float rk = rsqrtf(warp_sum(k2) + 1e-6f);
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      st.q[j][lane * PL + i] = qv[i] * rq;
+      st.k[j][lane * PL + i] = kv[i] * rk;
+    }
+    if (lane == 0) {
+      const float2 gb = gdn_gate(a, row, h);
+      st.g[j] = gb.x;
+      st.beta[j] = gb.y;
+    }
   }
-  // fixed-order block sums of q^2 and k^2 (warps, then warps in index order)
-  float q2 = warp_sum(qv * qv), k2 = warp_sum(kv * kv);
-  const int warp = t >> 5, lane = t & 31, nw = blockDim.x >> 5;
-  __syncthreads();
-  if (lane == 0) { red[warp] = q2; red[8 + warp] = k2; }
-  __syncthreads();
-  float sq2 = 0.f, sk2 = 0.f;
-  for (int i = 0; i < nw; ++i) { sq2 += red[i]; sk2 += red[8 + i]; }
-  const float rq = rsqrtf(sq2 + 1e-6f) * rsqrtf(float(K));
-  const float rk = rsqrtf(sk2 + 1e-6f);
-  if (t < K) {
-    sq[t] = qv * rq;
-    sk[t] = kv * rk;
+  for (int i = threadIdx.x; i < n * a.V; i += blockDim.x) {
+    const int j = i / a.V, c = i % a.V;
+    st.v[j][c] = bf(a.qkv[size_t(rows[j]) * a.ldq + 2 * a.HK * K + h * a.V + c]);
   }
   __syncthreads();
 }
 
-// One gated-delta-rule step on this thread's state column S[0..K) (value column v); returns the output o[v].
+// One gated-delta-rule step on this thread's state column S[0..K) with staged node j; returns the output o[v].
+// The two K-long reductions use four interleaved partial sums combined as (p0 + p1) + (p2 + p3).
 template <int K>
-__device__ __forceinline__ float gdn_step(float* S, const float* sq, const float* sk, float vval, float g, float beta) {
-  const float decay = __expf(g);
-  float kvm = 0.f;
+__device__ __forceinline__ float gdn_step(float* S, const GdnStage<K>& st, int j, int v) {
+  const float decay = __expf(st.g[j]);
+  float k0 = 0.f, k1 = 0.f, k2 = 0.f, k3 = 0.f;
 #pragma unroll
-  for (int i = 0; i < K; ++i) {
+  for (int i = 0; i < K; i += 4) {
     S[i] *= decay;
-    kvm = fmaf(S[i], sk[i], kvm);
+    S[i + 1] *= decay;
+    S[i + 2] *= decay;
+    S[i + 3] *= decay;
+    k0 = fmaf(S[i], st.k[j][i], k0);
+    k1 = fmaf(S[i + 1], st.k[j][i + 1], k1);
+    k2 = fmaf(S[i + 2], st.k[j][i + 2], k2);
+    k3 = fmaf(S[i + 3], st.k[j][i + 3], k3);
   }
-  const float delta = (vval - kvm) * beta;
-  float o = 0.f;
+  const float kvm = (k0 + k1) + (k2 + k3);
+  const float delta = (st.v[j][v] - kvm) * st.beta[j];
+  float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
 #pragma unroll
-  for (int i = 0; i < K; ++i) {
-    S[i] = fmaf(sk[i], delta, S[i]);
-    o = fmaf(S[i], sq[i], o);
+  for (int i = 0; i < K; i += 4) {
+    S[i] = fmaf(st.k[j][i], delta, S[i]);
+    S[i + 1] = fmaf(st.k[j][i + 1], delta, S[i + 1]);
+    S[i + 2] = fmaf(st.k[j][i + 2], delta, S[i + 2]);
+    S[i + 3] = fmaf(st.k[j][i + 3], delta, S[i + 3]);
+    o0 = fmaf(S[i], st.q[j][i], o0);
+    o1 = fmaf(S[i + 1], st.q[j][i + 1], o1);
+    o2 = fmaf(S[i + 2], st.q[j][i + 2], o2);
+    o3 = fmaf(S[i + 3], st.q[j][i + 3], o3);
   }
-  return o;
+  return (o0 + o1) + (o2 + o3);
 }
 
 // The output epilogue: o rounded to bf16, RMS-normalised over the head's V values, times w, times silu(z).
@@ -177,13 +213,15 @@ __device__ __forceinline__ void save_state(const float* S, float* dst) {
 
 // One CTA per (value head, row) in tree mode (the row replays its path, no state write) or per (value head,
 // request segment) in scan mode (rows in order, state updated in place); thread v owns state column v. The output
-// is the gated-RMS-normalised head output [T, HV*V].
+// is the gated-RMS-normalised head output [T, HV*V]. Path nodes are staged kGdnTile at a time.
 template <int K>
 __global__ void __launch_bounds__(128) gdn_kernel(GdnArgs a, const int* __restrict__ slot,
                                                   const int* __restrict__ parent, const int* __restrict__ seg,
                                                   int scan, const __nv_bfloat16* __restrict__ nw, float eps,
                                                   __nv_bfloat16* __restrict__ out) {
-  __shared__ float sq[K], sk[K], red[16];
+  extern __shared__ __align__(16) uint8_t gdn_smem[];
+  GdnStage<K>& st = *reinterpret_cast<GdnStage<K>*>(gdn_smem);
+  __shared__ float red[16];
   __shared__ int path[kMaxPath];
   __shared__ int plen;
   const int h = blockIdx.x;
@@ -203,27 +241,30 @@ __global__ void __launch_bounds__(128) gdn_kernel(GdnArgs a, const int* __restri
     __syncthreads();
     load_state<K>(S, a.state + ((size_t(slot[r]) * a.HV + h) * a.V + vc) * K);
     float o = 0.f;
-    for (int p = 0; p < plen; ++p) {
-      const int j = path[p];
-      gdn_load_qk<K>(a, j, kh, sq, sk, red);
-      const float vval = bf(a.qkv[size_t(j) * a.ldq + 2 * a.HK * K + h * a.V + vc]);
-      const float2 gb = gdn_gate(a, j, h);
-      o = gdn_step<K>(S, sq, sk, vval, gb.x, gb.y);
+    for (int p0 = 0; p0 < plen; p0 += kGdnTile) {
+      const int n = min(kGdnTile, plen - p0);
+      if (p0) __syncthreads();
+      gdn_stage<K>(a, path + p0, n, h, kh, st);
+      for (int j = 0; j < n; ++j) o = gdn_step<K>(S, st, j, vc);
     }
     gdn_store(a, r, h, v, o, nw, eps, red, out);
     return;
   }
   const int r0 = seg[blockIdx.y], r1 = seg[blockIdx.y + 1];
-  float* st = a.state + ((size_t(slot[r0]) * a.HV + h) * a.V + vc) * K;
-  load_state<K>(S, st);
-  for (int j = r0; j < r1; ++j) {
-    gdn_load_qk<K>(a, j, kh, sq, sk, red);
-    const float vval = bf(a.qkv[size_t(j) * a.ldq + 2 * a.HK * K + h * a.V + vc]);
-    const float2 gb = gdn_gate(a, j, h);
-    const float o = gdn_step<K>(S, sq, sk, vval, gb.x, gb.y);
-    gdn_store(a, j, h, v, o, nw, eps, red, out);
+  float* stp = a.state + ((size_t(slot[r0]) * a.HV + h) * a.V + vc) * K;
+  load_state<K>(S, stp);
+  for (int p0 = r0; p0 < r1; p0 += kGdnTile) {
+    const int n = min(kGdnTile, r1 - p0);
+    __syncthreads();
+    if (threadIdx.x < n) path[threadIdx.x] = p0 + threadIdx.x;
+    __syncthreads();
+    gdn_stage<K>(a, path, n, h, kh, st);
+    for (int j = 0; j < n; ++j) {
+      const float o = gdn_step<K>(S, st, j, vc);
+      gdn_store(a, p0 + j, h, v, o, nw, eps, red, out);
+    }
   }
-  if (v < a.V) save_state<K>(S, st);
+  if (v < a.V) save_state<K>(S, stp);
 }
 
 // Per-layer pointers of an all-layers commit.
@@ -246,7 +287,8 @@ template <int K>
 __global__ void __launch_bounds__(128) gdn_commit_kernel(GdnArgs a, const __grid_constant__ GdnLayerTable layers,
                                                          const int* __restrict__ slots, const int* __restrict__ rows,
                                                          int rows_ld, const int* __restrict__ nrows) {
-  __shared__ float sq[K], sk[K], red[16];
+  extern __shared__ __align__(16) uint8_t gdn_smem[];
+  GdnStage<K>& st = *reinterpret_cast<GdnStage<K>*>(gdn_smem);
   const int h = blockIdx.x, b = blockIdx.y, l = blockIdx.z, v = threadIdx.x;
   const int n = nrows[b];
   if (n <= 0) return;
@@ -258,17 +300,16 @@ __global__ void __launch_bounds__(128) gdn_commit_kernel(GdnArgs a, const __grid
   a.dt_bias = L.dt_bias;
   const int kh = h / (a.HV / a.HK);
   const int vc = min(v, a.V - 1);
-  float* st = a.state + ((size_t(slots[b]) * a.HV + h) * a.V + vc) * K;
+  float* stp = a.state + ((size_t(slots[b]) * a.HV + h) * a.V + vc) * K;
   float S[K];
-  load_state<K>(S, st);
-  for (int p = 0; p < n; ++p) {
-    const int j = rows[size_t(b) * rows_ld + p];
-    gdn_load_qk<K>(a, j, kh, sq, sk, red);
-    const float vval = bf(a.qkv[size_t(j) * a.ldq + 2 * a.HK * K + h * a.V + vc]);
-    const float2 gb = gdn_gate(a, j, h);
-    gdn_step<K>(S, sq, sk, vval, gb.x, gb.y);
+  load_state<K>(S, stp);
+  for (int p0 = 0; p0 < n; p0 += kGdnTile) {
+    const int m = min(kGdnTile, n - p0);
+    if (p0) __syncthreads();
+    gdn_stage<K>(a, rows + size_t(b) * rows_ld + p0, m, h, kh, st);
+    for (int j = 0; j < m; ++j) gdn_step<K>(S, st, j, vc);
   }
-  if (v < a.V) save_state<K>(S, st);
+  if (v < a.V) save_state<K>(S, stp);
 }
 
 // Conv window update of every layer: append rows[b, :n[b]] of the layer's conv inputs (proj columns [0, C)).
@@ -455,6 +496,11 @@ void conv_commit_scan(torch::Tensor cs, const torch::Tensor& x, const torch::Ten
   conv_commit(x, cs, torch::tensor(slots_v, opt).to(dev), rows, torch::tensor(nrows_v, opt).to(dev), W);
 }
 
+template <typename F>
+static void gdn_smem_attr(F* fn, size_t bytes) {
+  cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+}
+
 static GdnArgs gdn_args(const torch::Tensor& qkv, const torch::Tensor& proj, int64_t z_off, int64_t b_off,
                         int64_t a_off, const torch::Tensor& a_log, const torch::Tensor& dt_bias, torch::Tensor state,
                         int64_t HK, int64_t HV, int64_t K, int64_t V) {
@@ -480,12 +526,17 @@ torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int6
   const int ny = scan ? seg.numel() - 1 : T;
   dim3 grid(HV, ny);
   auto st = at::cuda::getCurrentCUDAStream();
-  if (K == 128)
-    gdn_kernel<128><<<grid, 128, 0, st>>>(a, sl.data_ptr<int>(), pa.data_ptr<int>(), seg.data_ptr<int>(), scan,
-                                          CBF(norm_w), float(eps), BFP(out));
-  else
-    gdn_kernel<64><<<grid, 128, 0, st>>>(a, sl.data_ptr<int>(), pa.data_ptr<int>(), seg.data_ptr<int>(), scan,
-                                         CBF(norm_w), float(eps), BFP(out));
+  if (K == 128) {
+    gdn_smem_attr(gdn_kernel<128>, sizeof(GdnStage<128>));
+    gdn_kernel<128><<<grid, 128, sizeof(GdnStage<128>), st>>>(a, sl.data_ptr<int>(), pa.data_ptr<int>(),
+                                                              seg.data_ptr<int>(), scan, CBF(norm_w), float(eps),
+                                                              BFP(out));
+  } else {
+    gdn_smem_attr(gdn_kernel<64>, sizeof(GdnStage<64>));
+    gdn_kernel<64><<<grid, 128, sizeof(GdnStage<64>), st>>>(a, sl.data_ptr<int>(), pa.data_ptr<int>(),
+                                                            seg.data_ptr<int>(), scan, CBF(norm_w), float(eps),
+                                                            BFP(out));
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
 }
@@ -514,12 +565,15 @@ void gdn_commit_all(const std::vector<torch::Tensor>& qkv, const std::vector<tor
             nullptr, nullptr, int(HK), int(HV), int(K), int(V)};
   auto st = at::cuda::getCurrentCUDAStream();
   dim3 grid(HV, B, nl);
-  if (K == 128)
-    gdn_commit_kernel<128><<<grid, 128, 0, st>>>(a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(), rw.size(1),
-                                                 nr.data_ptr<int>());
-  else
-    gdn_commit_kernel<64><<<grid, 128, 0, st>>>(a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(), rw.size(1),
-                                                nr.data_ptr<int>());
+  if (K == 128) {
+    gdn_smem_attr(gdn_commit_kernel<128>, sizeof(GdnStage<128>));
+    gdn_commit_kernel<128><<<grid, 128, sizeof(GdnStage<128>), st>>>(a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(),
+                                                                     rw.size(1), nr.data_ptr<int>());
+  } else {
+    gdn_smem_attr(gdn_commit_kernel<64>, sizeof(GdnStage<64>));
+    gdn_commit_kernel<64><<<grid, 128, sizeof(GdnStage<64>), st>>>(a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(),
+                                                                   rw.size(1), nr.data_ptr<int>());
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   conv_commit_all_kernel<<<dim3((C + 255) / 256, B, nl), 256, 0, st>>>(tab, int(proj[0].stride(0)),
                                                                         sl.data_ptr<int>(), rw.data_ptr<int>(),

@@ -213,15 +213,35 @@ __device__ void cta_select(const uint32_t* key, const int* idx, const float* val
       if (e < n && (key[i] & mask) == prefix) atomicAdd(&hist[(key[i] >> shift) & 255], 1);
     }
     __syncthreads();
-    if (t == 0) {
-      int above = 0, d = 255;
-      for (; d > 0; --d) {
-        if (above + hist[d] >= remaining) break;
-        above += hist[d];
+    if (t < 32) {
+      // lane l owns bins [255 - 8l - 7, 255 - 8l] (descending); suffix counts from the top bin down
+      int c[8], tot = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { c[i] = hist[255 - 8 * t - i]; tot += c[i]; }
+      int incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (t >= o) incl += v;
       }
-      s_prefix = prefix | (uint32_t(d) << shift);
-      s_remaining = remaining - above;
-      s_digit_above = above;
+      const int before = incl - tot;  // count in bins above this lane's range
+      // the digit: first bin (from the top) where the running count reaches ``remaining``
+      int found = -1, above_d = 0, run = before;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (found < 0 && run + c[i] >= remaining) { found = 255 - 8 * t - i; above_d = run; }
+        run += c[i];
+      }
+      const unsigned hit = __ballot_sync(0xffffffffu, found >= 0);
+      const int src = hit ? __ffs(hit) - 1 : 31;
+      int d = __shfl_sync(0xffffffffu, found, src);
+      int above = __shfl_sync(0xffffffffu, above_d, src);
+      if (!hit) { d = 0; above = __shfl_sync(0xffffffffu, incl, 31) - hist[0]; }
+      if (t == 0) {
+        s_prefix = prefix | (uint32_t(d) << shift);
+        s_remaining = remaining - above;
+        s_digit_above = above;
+      }
     }
     __syncthreads();
     prefix = s_prefix;
@@ -257,6 +277,10 @@ __device__ void cta_select(const uint32_t* key, const int* idx, const float* val
     __syncthreads();
   }
   int pos = scan[t] - mine;
+  for (int i = n + t; i < C; i += blockDim.x) {  // fewer than C elements: pad with -inf
+    ov[i] = -INFINITY;
+    oi[i] = 0x7fffffff;
+  }
   int eq_taken = 0;
   for (int i = 0; i < kSelPer; ++i) {
     const int e = t * kSelPer + i;
@@ -287,24 +311,32 @@ __global__ void __launch_bounds__(kSelThreads) topk_slice_kernel(const float* __
   cta_select(key, idx, val, n, C, ov + (size_t(r) * nslices + slice) * C, oi + (size_t(r) * nslices + slice) * C);
 }
 
-// Stage 2: CTA per row selects the top C of the slices' candidates, then sorts them (value desc, id asc).
+// Merge pass: CTA (row, group) selects the top C of candidates [group*gsize, +gsize) of the row's m candidates.
+// Intermediate passes write unsorted groups (value, id int32); the final pass (one group) sorts (value desc, id asc)
+// and writes int64 ids.
 __global__ void __launch_bounds__(kSelThreads) topk_merge_kernel(const float* __restrict__ iv, const int* __restrict__ ii,
-                                                                 int m, int C, float* __restrict__ ov,
-                                                                 int64_t* __restrict__ oi) {
-  const int r = blockIdx.x;
+                                                                 int m, int gsize, int C, float* __restrict__ ov,
+                                                                 int* __restrict__ oi32, int64_t* __restrict__ oi) {
+  const int r = blockIdx.x, grp = blockIdx.y, ngroups = gridDim.y;
   __shared__ float sv[1024];
   __shared__ int si[1024];
   uint32_t key[kSelPer];
   int idx[kSelPer];
   float val[kSelPer];
+  const int g0 = grp * gsize;
+  const int n = min(gsize, m - g0);
   for (int i = 0; i < kSelPer; ++i) {
     const int e = threadIdx.x * kSelPer + i;
-    const bool in = e < m;
-    val[i] = in ? iv[size_t(r) * m + e] : -INFINITY;
-    idx[i] = in ? ii[size_t(r) * m + e] : 0x7fffffff;
+    const bool in = e < n;
+    val[i] = in ? iv[size_t(r) * m + g0 + e] : -INFINITY;
+    idx[i] = in ? ii[size_t(r) * m + g0 + e] : 0x7fffffff;
     key[i] = in ? fkey(val[i]) : 0u;
   }
-  cta_select(key, idx, val, m, C, sv, si);
+  if (oi == nullptr) {
+    cta_select(key, idx, val, n, C, ov + (size_t(r) * ngroups + grp) * C, oi32 + (size_t(r) * ngroups + grp) * C);
+    return;
+  }
+  cta_select(key, idx, val, n, C, sv, si);
   __syncthreads();
   // bitonic sort of C (power of two <= 1024) entries: value desc, id asc
   int P = 1;
@@ -464,8 +496,8 @@ std::vector<torch::Tensor> topk_large(const torch::Tensor& scores, int64_t C) {
   TORCH_CHECK(scores.scalar_type() == torch::kFloat32 && scores.stride(1) == 1 && C <= 1024);
   const int R = scores.size(0), V = scores.size(1);
   const int per = kSelThreads * kSelPer;
+  TORCH_CHECK(2 * C <= per, "topk_large: C too large");
   const int ns = (V + per - 1) / per;
-  TORCH_CHECK(ns * C <= per, "topk_large: too many slices for one merge CTA");
   auto o = scores.options();
   auto sv = torch::empty({R, ns, C}, o), si = torch::empty({R, ns, C}, o.dtype(torch::kInt32));
   auto ov = torch::empty({R, C}, o), oi = torch::empty({R, C}, o.dtype(torch::kInt64));
@@ -473,8 +505,20 @@ std::vector<torch::Tensor> topk_large(const torch::Tensor& scores, int64_t C) {
   auto st = at::cuda::getCurrentCUDAStream();
   topk_slice_kernel<<<dim3(ns, R), kSelThreads, 0, st>>>(scores.data_ptr<float>(), scores.stride(0), V, int(C), ns,
                                                          sv.data_ptr<float>(), si.data_ptr<int>());
-  topk_merge_kernel<<<R, kSelThreads, 0, st>>>(sv.data_ptr<float>(), si.data_ptr<int>(), ns * int(C), int(C),
-                                               ov.data_ptr<float>(), oi.data_ptr<int64_t>());
+  // merge groups of whole slices until one group of candidates remains
+  const int gsize = (per / int(C)) * int(C);
+  int m = ns * int(C);
+  while (m > gsize) {
+    const int ng = (m + gsize - 1) / gsize;
+    auto nv = torch::empty({R, ng, C}, o), ni = torch::empty({R, ng, C}, o.dtype(torch::kInt32));
+    topk_merge_kernel<<<dim3(R, ng), kSelThreads, 0, st>>>(sv.data_ptr<float>(), si.data_ptr<int>(), m, gsize,
+                                                           int(C), nv.data_ptr<float>(), ni.data_ptr<int>(), nullptr);
+    sv = nv;
+    si = ni;
+    m = ng * int(C);
+  }
+  topk_merge_kernel<<<dim3(R, 1), kSelThreads, 0, st>>>(sv.data_ptr<float>(), si.data_ptr<int>(), m, m, int(C),
+                                                        ov.data_ptr<float>(), nullptr, oi.data_ptr<int64_t>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {ov, oi};
 }
