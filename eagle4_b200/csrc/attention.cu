@@ -35,6 +35,8 @@ attn_chunk_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __re
                   const int* __restrict__ req, const int* __restrict__ ctx_start, const int* __restrict__ ctx_len,
                   const int* __restrict__ extra, int extra_ld, const int* __restrict__ n_extra, float scale, int Hq,
                   int Hk, int nchunks, float* __restrict__ ws) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int D = DPL * 32;
   const int chunk = blockIdx.x, h = blockIdx.y, r = blockIdx.z;
   const int G = Hq / Hk;
@@ -170,6 +172,8 @@ attn_chunk_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __re
 // multiplied by sigmoid(gate) (the gated-attention output gate), saving a separate pass.
 __global__ void attn_merge_kernel(const float* __restrict__ ws, int nchunks, int D, int Hq,
                                   const __nv_bfloat16* __restrict__ gate, int ldg, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const size_t rh = blockIdx.x;
   const float* base = ws + rh * nchunks * (D + 2);
   float M = -INFINITY;
@@ -215,11 +219,11 @@ torch::Tensor attention(const torch::Tensor& q, const torch::Tensor& kc, const t
   dim3 grid(nchunks, Hk, T);
   auto stream = at::cuda::getCurrentCUDAStream();
 #define E4_ATTN(DPL)                                                                                              \
-  attn_chunk_kernel<DPL><<<grid, kWarps * 32, 0, stream>>>(                                                      \
+  C10_CUDA_CHECK(launch_pdl(attn_chunk_kernel<DPL>, grid, kWarps * 32, 0, stream.stream(),                                                       \
       reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(kc.data_ptr()), \
       reinterpret_cast<const __nv_bfloat16*>(vc.data_ptr()), bt_.data_ptr<int>(), bt_.size(1), page,             \
       req_.data_ptr<int>(), cs.data_ptr<int>(), cl.data_ptr<int>(), ex.data_ptr<int>(), ex.size(1),              \
-      ne.data_ptr<int>(), float(scale), Hq, Hk, nchunks, ws.data_ptr<float>())
+      ne.data_ptr<int>(), float(scale), Hq, Hk, nchunks, ws.data_ptr<float>()))
   switch (D / 32) {
     case 2: E4_ATTN(2); break;
     case 4: E4_ATTN(4); break;
@@ -231,8 +235,8 @@ torch::Tensor attention(const torch::Tensor& q, const torch::Tensor& kc, const t
   const __nv_bfloat16* gp = gate ? reinterpret_cast<const __nv_bfloat16*>(gate->data_ptr()) : nullptr;
   const int ldg = gate ? int(gate->stride(0)) : 0;
   if (gate) TORCH_CHECK(gate->stride(1) == 1 && gate->size(0) == T, "attention: gate must be [T, Hq*D] rows");
-  attn_merge_kernel<<<T * Hq, 128, 0, stream>>>(ws.data_ptr<float>(), nchunks, D, Hq, gp, ldg,
-                                                reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+  C10_CUDA_CHECK(launch_pdl(attn_merge_kernel, T * Hq, 128, 0, stream.stream(), ws.data_ptr<float>(), nchunks, D, Hq, gp, ldg,
+                                                reinterpret_cast<__nv_bfloat16*>(out.data_ptr())));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
 }

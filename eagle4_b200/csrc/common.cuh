@@ -10,6 +10,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #define E4_DEV __device__ __forceinline__
 
 namespace e4 {
@@ -170,4 +172,30 @@ E4_DEV float warp_max(float v) {
   return v;
 }
 
+}  // namespace e4
+
+// ---------------------------------------------------------------------------------------------------- PDL
+// Programmatic dependent launch: kernels are launched with programmatic stream serialisation so the next kernel's
+// CTAs may start (prologue, weight prefetch) while this one drains. Every kernel waits for its prerequisites with
+// pdl_wait() before touching activation memory (reads or writes), and lets its dependents start with pdl_trigger().
+namespace e4 {
+E4_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+E4_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launches ``kernel`` with the programmatic-serialisation attribute on ``stream``.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 }  // namespace e4

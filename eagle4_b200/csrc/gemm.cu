@@ -160,6 +160,9 @@ __device__ __forceinline__ void store_chunk(const Params& p, int tile, int m, in
 
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x, Params p) {
+  // Setup and the first weight loads happen before waiting for the previous kernel (weights never change); every
+  // access to activations (X loads, residual reads, output stores, workspace) comes after pdl_wait().
+  pdl_trigger();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // carve: [stages x (W tile | X tile)] 1024-aligned, then barriers, TMEM handle, exchange buffer
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -206,17 +209,31 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
       const uint64_t pol_x = policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
-      for (long g = g_begin; g < g_end && ok;) {
-        const Piece pc = next_piece(p, g, g_end);
-        g += pc.kb1 - pc.kb0;
-        for (int kb = pc.kb0; kb < pc.kb1; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { record_error(p.err, kErrTimeoutProducer); ok = false; break; }
-          uint8_t* st = tiles + stage * stage_bytes;
-          mbar_expect_tx(&full_bar[stage], stage_bytes);
-          tma_load_2d(st, &tmap_w, &full_bar[stage], kb * kTileK, pc.tile * kTileM, pol_w);
-          tma_load_2d(st + kWTileBytes, &tmap_x, &full_bar[stage], kb * kTileK, 0, pol_x);
-          if (++stage == p.stages) { stage = 0; phase ^= 1; }
-        }
+      // prologue: weight tiles of the first stages, before the dependency wait
+      const int pre = int(g_end - g_begin < long(p.stages) ? g_end - g_begin : long(p.stages));
+      for (int i = 0; i < pre; ++i) {
+        const long gg = g_begin + i;
+        const int tile = int(gg / p.kb_total), kb = int(gg - long(tile) * p.kb_total);
+        mbar_expect_tx(&full_bar[i], stage_bytes);
+        tma_load_2d(tiles + i * stage_bytes, &tmap_w, &full_bar[i], kb * kTileK, tile * kTileM, pol_w);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) {
+        const long gg = g_begin + i;
+        const int tile = int(gg / p.kb_total), kb = int(gg - long(tile) * p.kb_total);
+        (void)tile;
+        tma_load_2d(tiles + i * stage_bytes + kWTileBytes, &tmap_x, &full_bar[i], kb * kTileK, 0, pol_x);
+      }
+      stage = pre == p.stages ? 0 : pre;
+      phase = pre == p.stages ? 1 : 0;
+      for (long gg = g_begin + pre; gg < g_end && ok; ++gg) {
+        const int tile = int(gg / p.kb_total), kb = int(gg - long(tile) * p.kb_total);
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { record_error(p.err, kErrTimeoutProducer); ok = false; break; }
+        uint8_t* st = tiles + stage * stage_bytes;
+        mbar_expect_tx(&full_bar[stage], stage_bytes);
+        tma_load_2d(st, &tmap_w, &full_bar[stage], kb * kTileK, tile * kTileM, pol_w);
+        tma_load_2d(st + kWTileBytes, &tmap_x, &full_bar[stage], kb * kTileK, 0, pol_x);
+        if (++stage == p.stages) { stage = 0; phase ^= 1; }
       }
     }
   } else if (warp == 1) {
@@ -254,6 +271,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
     }
   } else {
     // epilogue warps 2..5: TMEM lane quarter = warp % 4
+    pdl_wait();
     const int ep_tid = threadIdx.x - 64;
     const int quarter = warp & 3;
     const int m = quarter * 32 + lane;
@@ -467,7 +485,7 @@ void gemm_launch(const torch::Tensor& x, const torch::Tensor& w, int epi, torch:
       cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
       attr_set = true;
     }
-    gemm_kernel<<<grid, kThreads, smem, stream>>>(wmap, xmap, p);
+    C10_CUDA_CHECK(launch_pdl(gemm_kernel, grid, kThreads, smem, stream.stream(), wmap, xmap, p));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }

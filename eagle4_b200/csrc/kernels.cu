@@ -77,6 +77,8 @@ __device__ __forceinline__ void store_normed(const uint4* v, int nv, const __nv_
 
 __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int ldx, const __nv_bfloat16* __restrict__ w,
                                __nv_bfloat16* __restrict__ y, int ldy, int H, float eps, int offset) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   const size_t r = blockIdx.x;
   uint4 v[kMaxVec];
@@ -90,6 +92,8 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int ldx, con
 __global__ void concat_norms_kernel(const __nv_bfloat16* __restrict__ e, const __nv_bfloat16* __restrict__ h, int ldh,
                                     const __nv_bfloat16* __restrict__ we, const __nv_bfloat16* __restrict__ wh,
                                     __nv_bfloat16* __restrict__ y, int H, float eps) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   const size_t r = blockIdx.x;
   uint4 ve[kMaxVec], vh[kMaxVec];
@@ -104,6 +108,8 @@ __global__ void concat_norms_kernel(const __nv_bfloat16* __restrict__ e, const _
 
 __global__ void embedding_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                                  __nv_bfloat16* __restrict__ y, int H, int64_t V, int* err) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t id = ids[blockIdx.x];
   if (id < 0 || id >= V) {
     if (threadIdx.x == 0) record_error(err, kErrBadIndex);
@@ -116,6 +122,8 @@ __global__ void embedding_kernel(const int64_t* __restrict__ ids, const __nv_bfl
 
 __global__ void sigmoid_gate_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ g, int ldg,
                                     __nv_bfloat16* __restrict__ y, int D) {
+  pdl_wait();
+  pdl_trigger();
   const size_t r = blockIdx.x;
   for (int i = threadIdx.x; i < D; i += blockDim.x)
     y[r * D + i] = __float2bfloat16(bf(o[r * D + i]) * sigmoidf_(bf(g[r * ldg + i])));
@@ -125,6 +133,8 @@ __global__ void sigmoid_gate_kernel(const __nv_bfloat16* __restrict__ o, const _
 __global__ void gated_rmsnorm_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ z, int ldz,
                                      const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y, int G, int D,
                                      float eps) {
+  pdl_wait();
+  pdl_trigger();
   // one warp per (row, group)
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -146,6 +156,8 @@ __global__ void gated_rmsnorm_kernel(const __nv_bfloat16* __restrict__ o, const 
 __global__ void gdn_gates_kernel(const __nv_bfloat16* __restrict__ a, const __nv_bfloat16* __restrict__ b, int lda,
                                  const float* __restrict__ a_log, const float* __restrict__ dt_bias, float* g,
                                  float* beta, int T, int HV) {
+  pdl_wait();
+  pdl_trigger();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= T * HV) return;
   const int r = i / HV, h = i % HV;
@@ -164,6 +176,8 @@ qkv_prepare_kernel(const __nv_bfloat16* __restrict__ qkv, int ldq, const int64_t
                    const __nv_bfloat16* __restrict__ qn, const __nv_bfloat16* __restrict__ kn, int norm_offset,
                    const float* __restrict__ cos_t, const float* __restrict__ sin_t, __nv_bfloat16* __restrict__ qout,
                    int Hq, int Hk, int D, int rot, int gated, float eps) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float buf[kPrepWarps][256];
   const size_t r = blockIdx.x;
   const __nv_bfloat16* row = qkv + r * ldq;
@@ -221,6 +235,8 @@ qkv_prepare_kernel(const __nv_bfloat16* __restrict__ qkv, int ldq, const int64_t
 // Greedy head: reduce per-tile (max, argmax) partials to one id per token (ties to the lower id).
 __global__ void argmax_reduce_kernel(const float* __restrict__ val, const int* __restrict__ idx, int n_tiles, int T,
                                      int64_t* __restrict__ out_id, float* __restrict__ out_val) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const int chunk = t / 256, j = t % 256;
   const int tc = min(256, T - chunk * 256);
@@ -257,6 +273,8 @@ __global__ void argmax_reduce_kernel(const float* __restrict__ val, const int* _
 // Copy accepted rows' K/V (all attention layers at once): pointers of every layer's cache in ``kp`` / ``vp``.
 __global__ void kv_commit_kernel(const int64_t* __restrict__ kp, const int64_t* __restrict__ vp, int layers,
                                  const int64_t* __restrict__ src, const int64_t* __restrict__ dst, int n, int row_elems) {
+  pdl_wait();
+  pdl_trigger();
   const int item = blockIdx.x;  // (layer, move)
   const int l = item / n, m = item % n;
   if (l >= layers) return;
@@ -286,8 +304,8 @@ torch::Tensor rmsnorm(const torch::Tensor& x, const torch::Tensor& w, double eps
   auto x2 = x.reshape({-1, H});
   auto y = torch::empty({x2.size(0), H}, x.options());
   if (x2.size(0))
-    rmsnorm_kernel<<<x2.size(0), kRowThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
-        CBF16(x2), x2.stride(0), CBF16(w), BF16(y), H, H, float(eps), offset ? 1 : 0);
+    C10_CUDA_CHECK(launch_pdl(rmsnorm_kernel, x2.size(0), kRowThreads, 0, at::cuda::getCurrentCUDAStream().stream(), 
+        CBF16(x2), x2.stride(0), CBF16(w), BF16(y), H, H, float(eps), offset ? 1 : 0));
   return y.view(x.sizes());
 }
 
@@ -298,8 +316,8 @@ torch::Tensor concat_norms(const torch::Tensor& e, const torch::Tensor& h, const
   TORCH_CHECK(H % 8 == 0 && H <= kRowThreads * kMaxVec * 8 && h.stride(0) % 8 == 0);
   auto y = torch::empty({T, 2 * H}, e.options());
   if (T)
-    concat_norms_kernel<<<T, kRowThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
-        CBF16(e.contiguous()), CBF16(h), h.stride(0), CBF16(we), CBF16(wh), BF16(y), H, float(eps));
+    C10_CUDA_CHECK(launch_pdl(concat_norms_kernel, T, kRowThreads, 0, at::cuda::getCurrentCUDAStream().stream(), 
+        CBF16(e.contiguous()), CBF16(h), h.stride(0), CBF16(we), CBF16(wh), BF16(y), H, float(eps)));
   return y;
 }
 
@@ -310,9 +328,9 @@ torch::Tensor embedding(const torch::Tensor& ids, const torch::Tensor& table) {
   auto y = torch::empty({T, H}, table.options());
   auto id64 = ids.to(torch::kInt64).contiguous();
   if (T)
-    embedding_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+    C10_CUDA_CHECK(launch_pdl(embedding_kernel, T, 128, 0, at::cuda::getCurrentCUDAStream().stream(), 
         id64.data_ptr<int64_t>(), CBF16(table), BF16(y), H, table.size(0),
-        gemm_error_word(table.device()).data_ptr<int>());
+        gemm_error_word(table.device()).data_ptr<int>()));
   return y;
 }
 
@@ -322,8 +340,8 @@ torch::Tensor sigmoid_gate(const torch::Tensor& o, const torch::Tensor& gate) {
   auto y = torch::empty_like(oc);
   const int T = oc.size(0), D = oc.size(1);
   if (T)
-    sigmoid_gate_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(CBF16(oc), CBF16(gate), gate.stride(0),
-                                                                         BF16(y), D);
+    C10_CUDA_CHECK(launch_pdl(sigmoid_gate_kernel, T, 256, 0, at::cuda::getCurrentCUDAStream().stream(), CBF16(oc), CBF16(gate), gate.stride(0),
+                                                                         BF16(y), D));
   return y;
 }
 
@@ -336,8 +354,8 @@ torch::Tensor gated_rmsnorm(const torch::Tensor& o, const torch::Tensor& z, cons
   const int warps = T * G;
   if (T) {
     dim3 grid((warps * 32 + 255) / 256, T);
-    gated_rmsnorm_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(CBF16(oc), CBF16(z), z.stride(0),
-                                                                             CBF16(w), BF16(y), G, D, float(eps));
+    C10_CUDA_CHECK(launch_pdl(gated_rmsnorm_kernel, grid, 256, 0, at::cuda::getCurrentCUDAStream().stream(), CBF16(oc), CBF16(z), z.stride(0),
+                                                                             CBF16(w), BF16(y), G, D, float(eps)));
   }
   return y;
 }
@@ -350,9 +368,9 @@ std::vector<torch::Tensor> gdn_gates(const torch::Tensor& a, const torch::Tensor
   auto f = a.options().dtype(torch::kFloat32);
   auto gg = torch::empty({T, HV}, f), beta = torch::empty({T, HV}, f);
   if (T)
-    gdn_gates_kernel<<<(T * HV + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+    C10_CUDA_CHECK(launch_pdl(gdn_gates_kernel, (T * HV + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream().stream(), 
         CBF16(a), CBF16(b), a.stride(0), a_log.data_ptr<float>(), dt_bias.data_ptr<float>(), gg.data_ptr<float>(),
-        beta.data_ptr<float>(), T, HV);
+        beta.data_ptr<float>(), T, HV));
   return {gg, beta};
 }
 
@@ -366,10 +384,10 @@ torch::Tensor qkv_prepare(const torch::Tensor& qkv, const torch::Tensor& pos, co
   TORCH_CHECK(D % 8 == 0 && D <= 256 && qkv.stride(0) % 8 == 0, "qkv_prepare: D must be a multiple of 8 up to 256");
   auto q = torch::empty({T, Hq, D}, qkv.options());
   if (T)
-    qkv_prepare_kernel<<<T, kPrepWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+    C10_CUDA_CHECK(launch_pdl(qkv_prepare_kernel, T, kPrepWarps * 32, 0, at::cuda::getCurrentCUDAStream().stream(), 
         CBF16(qkv), qkv.stride(0), pos.data_ptr<int64_t>(), slot.data_ptr<int64_t>(), BF16(kc), BF16(vc),
         qn ? CBF16(*qn) : nullptr, kn ? CBF16(*kn) : nullptr, norm_offset ? 1 : 0, cos_t.data_ptr<float>(),
-        sin_t.data_ptr<float>(), BF16(q), Hq, Hk, D, rot, gated ? 1 : 0, float(eps));
+        sin_t.data_ptr<float>(), BF16(q), Hq, Hk, D, rot, gated ? 1 : 0, float(eps)));
   return q;
 }
 
@@ -379,8 +397,8 @@ std::vector<torch::Tensor> argmax_reduce(const torch::Tensor& val, const torch::
   auto ids = torch::empty({T}, val.options().dtype(torch::kInt64));
   auto best = torch::empty({T}, val.options().dtype(torch::kFloat32));
   if (T)
-    argmax_reduce_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-        val.data_ptr<float>(), idx.data_ptr<int>(), n_tiles, T, ids.data_ptr<int64_t>(), best.data_ptr<float>());
+    C10_CUDA_CHECK(launch_pdl(argmax_reduce_kernel, T, 256, 0, at::cuda::getCurrentCUDAStream().stream(), 
+        val.data_ptr<float>(), idx.data_ptr<int>(), n_tiles, T, ids.data_ptr<int64_t>(), best.data_ptr<float>()));
   return {ids, best};
 }
 
@@ -390,9 +408,9 @@ void kv_commit(const torch::Tensor& kp, const torch::Tensor& vp, const torch::Te
   const int n = src.size(0), layers = kp.size(0);
   TORCH_CHECK(row_elems % 8 == 0);
   if (n && layers)
-    kv_commit_kernel<<<n * layers, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+    C10_CUDA_CHECK(launch_pdl(kv_commit_kernel, n * layers, 128, 0, at::cuda::getCurrentCUDAStream().stream(), 
         kp.data_ptr<int64_t>(), vp.data_ptr<int64_t>(), layers, src.data_ptr<int64_t>(), dst.data_ptr<int64_t>(), n,
-        row_elems);
+        row_elems));
 }
 
 }  // namespace e4

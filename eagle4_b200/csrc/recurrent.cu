@@ -31,6 +31,8 @@ __global__ void conv_tree_kernel(const __nv_bfloat16* __restrict__ x, int ldx, c
                                  const int* __restrict__ slot, const int* __restrict__ parent,
                                  const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int T, int C,
                                  int W) {
+  pdl_wait();
+  pdl_trigger();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   const int r = blockIdx.y;
   if (c >= C) return;
@@ -61,6 +63,8 @@ __global__ void conv_tree_kernel(const __nv_bfloat16* __restrict__ x, int ldx, c
 __global__ void conv_commit_kernel(const __nv_bfloat16* __restrict__ x, int ldx, __nv_bfloat16* cs,
                                    const int* __restrict__ slots, const int* __restrict__ rows, int rows_ld,
                                    const int* __restrict__ nrows, int C, int W) {
+  pdl_wait();
+  pdl_trigger();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   const int b = blockIdx.y;
   if (c >= C) return;
@@ -219,6 +223,8 @@ __global__ void __launch_bounds__(128) gdn_kernel(GdnArgs a, const int* __restri
                                                   const int* __restrict__ parent, const int* __restrict__ seg,
                                                   int scan, const __nv_bfloat16* __restrict__ nw, float eps,
                                                   __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) uint8_t gdn_smem[];
   GdnStage<K>& st = *reinterpret_cast<GdnStage<K>*>(gdn_smem);
   __shared__ float red[16];
@@ -287,6 +293,8 @@ template <int K>
 __global__ void __launch_bounds__(128) gdn_commit_kernel(GdnArgs a, const __grid_constant__ GdnLayerTable layers,
                                                          const int* __restrict__ slots, const int* __restrict__ rows,
                                                          int rows_ld, const int* __restrict__ nrows) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) uint8_t gdn_smem[];
   GdnStage<K>& st = *reinterpret_cast<GdnStage<K>*>(gdn_smem);
   const int h = blockIdx.x, b = blockIdx.y, l = blockIdx.z, v = threadIdx.x;
@@ -316,6 +324,8 @@ __global__ void __launch_bounds__(128) gdn_commit_kernel(GdnArgs a, const __grid
 __global__ void conv_commit_all_kernel(const __grid_constant__ GdnLayerTable layers, int ldp, const int* __restrict__ slots,
                                        const int* __restrict__ rows, int rows_ld, const int* __restrict__ nrows,
                                        int C, int W) {
+  pdl_wait();
+  pdl_trigger();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   const int b = blockIdx.y;
   if (c >= C) return;
@@ -374,6 +384,8 @@ template <int N>
 __global__ void __launch_bounds__(64) mamba_kernel(MambaArgs a, const int* __restrict__ slot,
                                                    const int* __restrict__ parent, const int* __restrict__ seg,
                                                    int scan, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sB[N], sC[N];
   __shared__ int path[kMaxPath];
   __shared__ int plen;
@@ -417,6 +429,8 @@ template <int N>
 __global__ void __launch_bounds__(64) mamba_commit_kernel(MambaArgs a, const int* __restrict__ slots,
                                                           const int* __restrict__ rows, int rows_ld,
                                                           const int* __restrict__ nrows) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sB[N], sC[N];
   const int h = blockIdx.x, b = blockIdx.y, p = threadIdx.x;
   const int n = nrows[b];
@@ -456,8 +470,8 @@ torch::Tensor conv_tree(const torch::Tensor& x, const torch::Tensor& cs, const t
   auto out = torch::empty({T, C}, x.options());
   if (T) {
     auto sl = slot.to(torch::kInt32).contiguous(), pa = parent.to(torch::kInt32).contiguous();
-    conv_tree_kernel<<<dim3((C + 255) / 256, T), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-        CBF(x), x.stride(0), CBF(cs), sl.data_ptr<int>(), pa.data_ptr<int>(), CBF(w.contiguous()), BFP(out), T, C, W);
+    C10_CUDA_CHECK(launch_pdl(conv_tree_kernel, dim3((C + 255) / 256, T), 256, 0, at::cuda::getCurrentCUDAStream().stream(), 
+        CBF(x), x.stride(0), CBF(cs), sl.data_ptr<int>(), pa.data_ptr<int>(), CBF(w.contiguous()), BFP(out), T, C, W));
   }
   return out;
 }
@@ -470,8 +484,8 @@ void conv_commit(const torch::Tensor& x, torch::Tensor cs, const torch::Tensor& 
   if (!B) return;
   auto sl = slots.to(torch::kInt32).contiguous(), rw = rows.to(torch::kInt32).contiguous(),
        nr = nrows.to(torch::kInt32).contiguous();
-  conv_commit_kernel<<<dim3((C + 255) / 256, B), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      CBF(x), x.stride(0), BFP(cs), sl.data_ptr<int>(), rw.data_ptr<int>(), rw.size(1), nr.data_ptr<int>(), C, W);
+  C10_CUDA_CHECK(launch_pdl(conv_commit_kernel, dim3((C + 255) / 256, B), 256, 0, at::cuda::getCurrentCUDAStream().stream(), 
+      CBF(x), x.stride(0), BFP(cs), sl.data_ptr<int>(), rw.data_ptr<int>(), rw.size(1), nr.data_ptr<int>(), C, W));
 }
 
 void conv_commit_scan(torch::Tensor cs, const torch::Tensor& x, const torch::Tensor& slot, int64_t W) {
@@ -528,14 +542,14 @@ torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int6
   auto st = at::cuda::getCurrentCUDAStream();
   if (K == 128) {
     gdn_smem_attr(gdn_kernel<128>, sizeof(GdnStage<128>));
-    gdn_kernel<128><<<grid, 128, sizeof(GdnStage<128>), st>>>(a, sl.data_ptr<int>(), pa.data_ptr<int>(),
+    C10_CUDA_CHECK(launch_pdl(gdn_kernel<128>, grid, 128, sizeof(GdnStage<128>), st.stream(), a, sl.data_ptr<int>(), pa.data_ptr<int>(),
                                                               seg.data_ptr<int>(), scan, CBF(norm_w), float(eps),
-                                                              BFP(out));
+                                                              BFP(out)));
   } else {
     gdn_smem_attr(gdn_kernel<64>, sizeof(GdnStage<64>));
-    gdn_kernel<64><<<grid, 128, sizeof(GdnStage<64>), st>>>(a, sl.data_ptr<int>(), pa.data_ptr<int>(),
+    C10_CUDA_CHECK(launch_pdl(gdn_kernel<64>, grid, 128, sizeof(GdnStage<64>), st.stream(), a, sl.data_ptr<int>(), pa.data_ptr<int>(),
                                                             seg.data_ptr<int>(), scan, CBF(norm_w), float(eps),
-                                                            BFP(out));
+                                                            BFP(out)));
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
@@ -567,18 +581,18 @@ void gdn_commit_all(const std::vector<torch::Tensor>& qkv, const std::vector<tor
   dim3 grid(HV, B, nl);
   if (K == 128) {
     gdn_smem_attr(gdn_commit_kernel<128>, sizeof(GdnStage<128>));
-    gdn_commit_kernel<128><<<grid, 128, sizeof(GdnStage<128>), st>>>(a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(),
-                                                                     rw.size(1), nr.data_ptr<int>());
+    C10_CUDA_CHECK(launch_pdl(gdn_commit_kernel<128>, grid, 128, sizeof(GdnStage<128>), st.stream(), a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(),
+                                                                     rw.size(1), nr.data_ptr<int>()));
   } else {
     gdn_smem_attr(gdn_commit_kernel<64>, sizeof(GdnStage<64>));
-    gdn_commit_kernel<64><<<grid, 128, sizeof(GdnStage<64>), st>>>(a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(),
-                                                                   rw.size(1), nr.data_ptr<int>());
+    C10_CUDA_CHECK(launch_pdl(gdn_commit_kernel<64>, grid, 128, sizeof(GdnStage<64>), st.stream(), a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(),
+                                                                   rw.size(1), nr.data_ptr<int>()));
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  conv_commit_all_kernel<<<dim3((C + 255) / 256, B, nl), 256, 0, st>>>(tab, int(proj[0].stride(0)),
+  C10_CUDA_CHECK(launch_pdl(conv_commit_all_kernel, dim3((C + 255) / 256, B, nl), 256, 0, st.stream(), tab, int(proj[0].stride(0)),
                                                                         sl.data_ptr<int>(), rw.data_ptr<int>(),
                                                                         rw.size(1), nr.data_ptr<int>(), int(C),
-                                                                        int(W));
+                                                                        int(W)));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -594,9 +608,9 @@ static MambaArgs mamba_args(const torch::Tensor& xbc, const torch::Tensor& dt, c
 
 #define E4_MAMBA_DISPATCH(N_, KERNEL, ...)                         \
   switch (N_) {                                                      \
-    case 128: KERNEL<128><<<grid, 64, 0, st>>>(__VA_ARGS__); break;  \
-    case 64: KERNEL<64><<<grid, 64, 0, st>>>(__VA_ARGS__); break;    \
-    default: KERNEL<16><<<grid, 64, 0, st>>>(__VA_ARGS__); break;    \
+    case 128: C10_CUDA_CHECK(launch_pdl(KERNEL<128>, grid, 64, 0, st.stream(), __VA_ARGS__)); break;  \
+    case 64: C10_CUDA_CHECK(launch_pdl(KERNEL<64>, grid, 64, 0, st.stream(), __VA_ARGS__)); break;    \
+    default: C10_CUDA_CHECK(launch_pdl(KERNEL<16>, grid, 64, 0, st.stream(), __VA_ARGS__)); break;    \
   }
 
 torch::Tensor mamba_tree(const torch::Tensor& xbc, const torch::Tensor& dt, const torch::Tensor& a_log,

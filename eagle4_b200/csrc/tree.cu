@@ -13,6 +13,8 @@ namespace {
 __global__ void gather_dot_kernel(const __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ w,
                                   const int64_t* __restrict__ idx, float* __restrict__ out, int R, int C, int H,
                                   int64_t V, int* err) {
+  pdl_wait();
+  pdl_trigger();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gw >= R * C) return;
@@ -44,6 +46,8 @@ __global__ void gather_dot_kernel(const __nv_bfloat16* __restrict__ h, const __n
 // candidate position) and their ids. One block of 128 threads per row; C <= 1024.
 __global__ void softmax_topk_kernel(const float* __restrict__ logit, const int64_t* __restrict__ ids, int C, int K,
                                     float inv_temp, float* __restrict__ probs, int64_t* __restrict__ out_ids) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float p[1024];
   __shared__ float red[32];
   const int r = blockIdx.x;
@@ -105,6 +109,8 @@ __global__ void softmax_topk_kernel(const float* __restrict__ logit, const int64
 __global__ void accept_greedy_kernel(const int64_t* __restrict__ tid, const int64_t* __restrict__ tokens,
                                      const int* __restrict__ parent, const int* __restrict__ nrows, int B, int N,
                                      int* __restrict__ acc, int* __restrict__ cnt, int64_t* __restrict__ bonus) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   const int n = nrows[b];
@@ -138,10 +144,10 @@ torch::Tensor gather_dot(const torch::Tensor& h, const torch::Tensor& w, const t
   auto ix = idx.to(torch::kInt64).contiguous();
   const int warps = R * C;
   if (warps)
-    gather_dot_kernel<<<(warps * 32 + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+    C10_CUDA_CHECK(launch_pdl(gather_dot_kernel, (warps * 32 + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream().stream(), 
         reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
         ix.data_ptr<int64_t>(), out.data_ptr<float>(), R, C, H, w.size(0),
-        gemm_error_word(h.device()).data_ptr<int>());
+        gemm_error_word(h.device()).data_ptr<int>()));
   return out;
 }
 
@@ -155,9 +161,9 @@ std::vector<torch::Tensor> softmax_topk(const torch::Tensor& logit, const c10::o
   torch::Tensor idc;
   if (ids) idc = ids->to(torch::kInt64).contiguous();
   if (R)
-    softmax_topk_kernel<<<R, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+    C10_CUDA_CHECK(launch_pdl(softmax_topk_kernel, R, 128, 0, at::cuda::getCurrentCUDAStream().stream(), 
         logit.data_ptr<float>(), ids ? idc.data_ptr<int64_t>() : nullptr, C, K, float(1.0 / temperature),
-        probs.data_ptr<float>(), oid.data_ptr<int64_t>());
+        probs.data_ptr<float>(), oid.data_ptr<int64_t>()));
   return {probs, oid};
 }
 
@@ -172,9 +178,9 @@ std::vector<torch::Tensor> accept_greedy(const torch::Tensor& tid, const torch::
   auto t = tid.to(torch::kInt64).contiguous(), tk = tokens.to(torch::kInt64).contiguous(),
        pr = parent.to(torch::kInt32).contiguous(), nr = nrows.to(torch::kInt32).contiguous();
   if (B)
-    accept_greedy_kernel<<<(B + 127) / 128, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+    C10_CUDA_CHECK(launch_pdl(accept_greedy_kernel, (B + 127) / 128, 128, 0, at::cuda::getCurrentCUDAStream().stream(), 
         t.data_ptr<int64_t>(), tk.data_ptr<int64_t>(), pr.data_ptr<int>(), nr.data_ptr<int>(), B, N,
-        acc.data_ptr<int>(), cnt.data_ptr<int>(), bonus.data_ptr<int64_t>());
+        acc.data_ptr<int>(), cnt.data_ptr<int>(), bonus.data_ptr<int64_t>()));
   return {acc, cnt, bonus};
 }
 
@@ -295,6 +301,8 @@ __device__ void cta_select(const uint32_t* key, const int* idx, const float* val
 __global__ void __launch_bounds__(kSelThreads) topk_slice_kernel(const float* __restrict__ scores, int ld, int V, int C,
                                                                  int nslices, float* __restrict__ ov,
                                                                  int* __restrict__ oi) {
+  pdl_wait();
+  pdl_trigger();
   const int slice = blockIdx.x, r = blockIdx.y;
   const int base = slice * kSelThreads * kSelPer;
   const int n = min(kSelThreads * kSelPer, V - base);
@@ -317,6 +325,8 @@ __global__ void __launch_bounds__(kSelThreads) topk_slice_kernel(const float* __
 __global__ void __launch_bounds__(kSelThreads) topk_merge_kernel(const float* __restrict__ iv, const int* __restrict__ ii,
                                                                  int m, int gsize, int C, float* __restrict__ ov,
                                                                  int* __restrict__ oi32, int64_t* __restrict__ oi) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x, grp = blockIdx.y, ngroups = gridDim.y;
   __shared__ float sv[1024];
   __shared__ int si[1024];
@@ -374,6 +384,8 @@ __global__ void tree_step_kernel(const float* __restrict__ probs, const int64_t*
                                  int64_t* tokens, int64_t* parents, float* front_scores, int64_t* front_tokens,
                                  __nv_bfloat16* front_hidden, int64_t* front_nodes, int* ancestors, float* best,
                                  float* best_prev, float* layer_top) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x;
   __shared__ float layer[64];
   __shared__ int pick[8];
@@ -452,6 +464,8 @@ __global__ void select_rows_kernel(const float* __restrict__ scores, const float
                                    const int64_t* __restrict__ tokens, const int64_t* __restrict__ parents, int n,
                                    int cap, int pcap, int K, int count, int64_t* __restrict__ out_tok,
                                    int* __restrict__ out_parent) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x;
   __shared__ float d[1024];
   __shared__ int sel_pos[1024];
@@ -503,22 +517,22 @@ std::vector<torch::Tensor> topk_large(const torch::Tensor& scores, int64_t C) {
   auto ov = torch::empty({R, C}, o), oi = torch::empty({R, C}, o.dtype(torch::kInt64));
   if (!R) return {ov, oi};
   auto st = at::cuda::getCurrentCUDAStream();
-  topk_slice_kernel<<<dim3(ns, R), kSelThreads, 0, st>>>(scores.data_ptr<float>(), scores.stride(0), V, int(C), ns,
-                                                         sv.data_ptr<float>(), si.data_ptr<int>());
+  C10_CUDA_CHECK(launch_pdl(topk_slice_kernel, dim3(ns, R), kSelThreads, 0, st.stream(), scores.data_ptr<float>(), scores.stride(0), V, int(C), ns,
+                                                         sv.data_ptr<float>(), si.data_ptr<int>()));
   // merge groups of whole slices until one group of candidates remains
   const int gsize = (per / int(C)) * int(C);
   int m = ns * int(C);
   while (m > gsize) {
     const int ng = (m + gsize - 1) / gsize;
     auto nv = torch::empty({R, ng, C}, o), ni = torch::empty({R, ng, C}, o.dtype(torch::kInt32));
-    topk_merge_kernel<<<dim3(R, ng), kSelThreads, 0, st>>>(sv.data_ptr<float>(), si.data_ptr<int>(), m, gsize,
-                                                           int(C), nv.data_ptr<float>(), ni.data_ptr<int>(), nullptr);
+    C10_CUDA_CHECK(launch_pdl(topk_merge_kernel, dim3(R, ng), kSelThreads, 0, st.stream(), sv.data_ptr<float>(), si.data_ptr<int>(), m, gsize,
+                                                           int(C), nv.data_ptr<float>(), ni.data_ptr<int>(), nullptr));
     sv = nv;
     si = ni;
     m = ng * int(C);
   }
-  topk_merge_kernel<<<dim3(R, 1), kSelThreads, 0, st>>>(sv.data_ptr<float>(), si.data_ptr<int>(), m, m, int(C),
-                                                        ov.data_ptr<float>(), nullptr, oi.data_ptr<int64_t>());
+  C10_CUDA_CHECK(launch_pdl(topk_merge_kernel, dim3(R, 1), kSelThreads, 0, st.stream(), sv.data_ptr<float>(), si.data_ptr<int>(), m, m, int(C),
+                                                        ov.data_ptr<float>(), nullptr, oi.data_ptr<int64_t>()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {ov, oi};
 }
@@ -535,13 +549,13 @@ void tree_step(const torch::Tensor& probs, const torch::Tensor& toks, const torc
   auto h = hidden.contiguous();
   const int H = h.size(1);
   TORCH_CHECK(H % 8 == 0);
-  tree_step_kernel<<<bs, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+  C10_CUDA_CHECK(launch_pdl(tree_step_kernel, bs, 128, 0, at::cuda::getCurrentCUDAStream().stream(), 
       p.data_ptr<float>(), tk.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()), H, K, step,
       layer_start, parent_col, best.size(1), scores.size(1), parents.size(1), ancestors.size(2),
       scores.data_ptr<float>(), tokens.data_ptr<int64_t>(), parents.data_ptr<int64_t>(),
       front_scores.data_ptr<float>(), front_tokens.data_ptr<int64_t>(),
       reinterpret_cast<__nv_bfloat16*>(front_hidden.data_ptr()), front_nodes.data_ptr<int64_t>(),
-      ancestors.data_ptr<int>(), best.data_ptr<float>(), best_prev.data_ptr<float>(), layer_top.data_ptr<float>());
+      ancestors.data_ptr<int>(), best.data_ptr<float>(), best_prev.data_ptr<float>(), layer_top.data_ptr<float>()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -552,9 +566,9 @@ std::vector<torch::Tensor> select_rows(const torch::Tensor& scores, const torch:
   TORCH_CHECK(n <= 1024 && count <= 63);
   auto ot = torch::empty({bs, count}, tokens.options());
   auto op = torch::empty({bs, count + 1}, tokens.options().dtype(torch::kInt32));
-  select_rows_kernel<<<bs, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+  C10_CUDA_CHECK(launch_pdl(select_rows_kernel, bs, 128, 0, at::cuda::getCurrentCUDAStream().stream(), 
       scores.data_ptr<float>(), decay.data_ptr<float>(), tokens.data_ptr<int64_t>(), parents.data_ptr<int64_t>(), n,
-      scores.size(1), parents.size(1), K, count, ot.data_ptr<int64_t>(), op.data_ptr<int>());
+      scores.size(1), parents.size(1), K, count, ot.data_ptr<int64_t>(), op.data_ptr<int>()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {ot, op};
 }
