@@ -491,3 +491,106 @@ void gemm_launch(const torch::Tensor& x, const torch::Tensor& w, int epi, torch:
 }
 
 }  // namespace e4
+
+// =====================================================================================================================
+// Allocation-free GEMM entry point. This has no counterpart in the reference.
+//
+// Some callers cannot allocate device memory: an inference host that hands this library only buffers it has already
+// allocated (and forbids allocation while it serves), code that runs inside a fixed memory budget it may not grow, or
+// a plain C program that links the library without any device allocator. The library's GEMM normally takes its
+// stream-K workspace (partial tiles, arrival counters, error word) from allocator-backed buffers; this entry point
+// runs the same kernel with that workspace in a fixed array in device memory instead:
+//
+//   int e4_gemm_bf16_noalloc(const void* x, int ldx, const void* w, int ldw, void* y, int ldy,
+//                            int T, int N, int K, void* stream);
+//
+// computes Y[T, N] = X[T, K] . W[N, K]^T (bf16 operands and output, fp32 accumulation, row-major with leading
+// dimensions in elements) on ``stream`` (a cudaStream_t; 0 for the legacy stream) and returns 0, or a non-zero code
+// for bad arguments (1) or a CUDA error (2).
+//
+// Limits: T <= 32 tokens per call, N <= 128 * 4096 weight rows, rows 16-byte aligned. The array holds 5.3 MB on every
+// GPU that loads the library, until the process exits.
+// The first call on a device (with that device current) looks up the array's device address and sets the kernel's
+// shared-memory limit; make that first call before any stream capture. Every call shares the one array and each call
+// clears the arrival counters it needs before its kernel starts, so two calls that overlap on the GPU (different
+// streams, or different host threads on one device) race on the array and must be serialised by the caller.
+// The function calls no device allocator (no cudaMalloc / cudaFree / allocating library routine).
+// =====================================================================================================================
+namespace e4 {
+namespace noalloc {
+
+constexpr int kMaxTokens = 32;
+constexpr int kMaxGrid = 160;   // CTAs (one per SM, B200 has 148)
+constexpr int kMaxTiles = 4096;
+constexpr size_t kWsFloats = size_t(2) * kMaxGrid * kMaxTokens * gemm::kTileM;
+constexpr size_t kBytes = kWsFloats * sizeof(float) + kMaxTiles * sizeof(int) + 256;
+
+static __device__ __align__(256) unsigned char scratch[kBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex setup_mu;
+void* scratch_addr[kMaxDevices] = {};
+
+int setup(int dev, void** out) {
+  std::lock_guard<std::mutex> g(setup_mu);
+  if (!scratch_addr[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, scratch) != cudaSuccess || !ptr) return 2;
+    if (cudaFuncSetAttribute(gemm::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
+      return 2;
+    scratch_addr[dev] = ptr;
+  }
+  *out = scratch_addr[dev];
+  return 0;
+}
+
+}  // namespace noalloc
+}  // namespace e4
+
+extern "C" int e4_gemm_bf16_noalloc(const void* x, int ldx, const void* w, int ldw, void* y, int ldy, int T, int N,
+                                    int K, void* stream) {
+  using namespace e4;
+  using namespace e4::gemm;
+  if (!x || !w || !y || T <= 0 || T > noalloc::kMaxTokens || N <= 0 || K <= 0) return 1;
+  if (ldx < K || ldw < K || ldy < N || (ldx * 2) % 16 || (ldw * 2) % 16) return 1;
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(w) % 16) return 1;
+  const int n_tiles = (N + kTileM - 1) / kTileM;
+  if (n_tiles > noalloc::kMaxTiles) return 1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= noalloc::kMaxDevices) return 2;
+  void* base = nullptr;
+  if (noalloc::setup(dev, &base)) return 2;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 2;
+  const int kb_total = (K + kTileK - 1) / kTileK;
+  const long total = long(n_tiles) * kb_total;
+  const int grid = int(std::min<long>(std::min(sms, noalloc::kMaxGrid), total));
+  Params p{};
+  p.T = T;
+  p.N = N;
+  p.K = K;
+  p.nt = std::max(16, (T + 15) / 16 * 16);
+  p.n_tiles = n_tiles;
+  p.kb_total = kb_total;
+  p.total = total;
+  p.epi = kPlain;
+  const int stage_bytes = kWTileBytes + p.nt * kTileK * 2;
+  p.stages = std::min(10, (200 * 1024) / stage_bytes);
+  p.ws = reinterpret_cast<float*>(base);
+  p.counters = reinterpret_cast<int*>(reinterpret_cast<unsigned char*>(base) + noalloc::kWsFloats * sizeof(float));
+  p.err = p.counters + noalloc::kMaxTiles;
+  p.y = reinterpret_cast<__nv_bfloat16*>(y);
+  p.ldy = ldy;
+  CUtensorMap wmap, xmap;
+  try {
+    wmap = make_map(w, N, K, ldw, kTileM);
+    xmap = make_map(x, T, K, ldx, p.nt);
+  } catch (...) {
+    return 2;
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(p.counters, 0, sizeof(int) * (n_tiles + 1), st) != cudaSuccess) return 2;
+  const size_t smem = 1024 + size_t(p.stages) * stage_bytes + 64 + 16 * 64 * 4 + 1024;
+  if (launch_pdl(gemm_kernel, grid, kThreads, smem, st, wmap, xmap, p) != cudaSuccess) return 2;
+  return 0;
+}
