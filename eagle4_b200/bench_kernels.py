@@ -54,7 +54,7 @@ def main() -> None:
     }
     rows = []
     for name, (n, k) in shapes.items():
-        if args.only and name not in args.only:
+        if args.only is not None and name not in args.only:
             continue
         w = (torch.randn(n, k, device=dev) * 0.02).to(torch.bfloat16)
         for t in args.tokens:
@@ -71,7 +71,61 @@ def main() -> None:
                          "frac_of_measured_hbm": round(gbs / peak, 3)})
             print(json.dumps(rows[-1]), flush=True)
         del w
+    if not args.only or "attn_verify" in args.only:
+        rows.extend(_bench_attention(native, args, peak))
+    if not args.only or "gdn_verify" in args.only:
+        rows.extend(_bench_gdn(native, args, peak))
     native.check_errors()
+
+
+def _bench_attention(native, args, peak):
+    """Tree-verify attention at the Qwen3.8-27B attention shape (24 q / 4 kv heads x 256) for one request with a
+    1280-token context and a 16-row chain-shaped tree."""
+    dev = torch.device("cuda")
+    out = []
+    hq, hk, d, page, L = 24, 4, 256, 16, 1280
+    bt = torch.arange(96, dtype=torch.int32, device=dev).view(1, 96)
+    kc = (torch.randn(96 * page, hk, d, device=dev) * 0.1).to(torch.bfloat16)
+    vc = (torch.randn(96 * page, hk, d, device=dev) * 0.1).to(torch.bfloat16)
+    for t in args.tokens:
+        q = torch.randn(t, hq, d, device=dev).to(torch.bfloat16)
+        req = torch.zeros(t, dtype=torch.int32, device=dev)
+        cs = torch.zeros(t, dtype=torch.int32, device=dev)
+        cl = torch.full((t,), L, dtype=torch.int32, device=dev)
+        extra = (L + torch.arange(t, device=dev)).int()[None, :].expand(t, t).contiguous()
+        ne = torch.arange(1, t + 1, dtype=torch.int32, device=dev)
+        fn = lambda: native.attention(q, kc, vc, bt, page, req, cs, cl, extra, ne, d ** -0.5, max_keys=L + t)  # noqa
+        us = time_fn(fn, args.iters, args.warmup)
+        kv_bytes = (L + t) * hk * d * 2 * 2
+        out.append({"kernel": "attn_verify", "T": t, "context": L, "us": round(us, 2),
+                    "GB/s": round(kv_bytes / (us * 1e-6) / 1e9, 1)})
+        print(json.dumps(out[-1]), flush=True)
+    return out
+
+
+def _bench_gdn(native, args, peak):
+    """GDN tree recurrence at the Qwen3.8-27B shape (16 k / 48 v heads x 128) for one request whose rows form a
+    chain (each row replays its path from the committed state)."""
+    from eagle4_b200.models.configs import qwen38_27b
+
+    cfg = qwen38_27b()
+    dev = torch.device("cuda")
+    out = []
+    state = torch.randn(1, cfg.gdn_v_heads, cfg.gdn_v_dim, cfg.gdn_k_dim, device=dev) * 0.01
+    a_log = torch.rand(cfg.gdn_v_heads, device=dev).log1p()
+    dt_bias = torch.ones(cfg.gdn_v_heads, device=dev)
+    gnorm = torch.ones(cfg.gdn_v_dim, dtype=torch.bfloat16, device=dev)
+    for t in args.tokens:
+        conv = torch.randn(t, cfg.gdn_conv_dim, device=dev).to(torch.bfloat16)
+        proj = torch.randn(t, cfg.gdn_conv_dim + cfg.gdn_value_dim + 2 * cfg.gdn_v_heads, device=dev).to(torch.bfloat16)
+        slot = torch.zeros(t, dtype=torch.int32, device=dev)
+        parent = (torch.arange(t, device=dev) - 1).int()
+        fn = lambda: native.gdn_mixer(conv, proj, cfg, a_log, dt_bias, gnorm, state, slot, parent, False)  # noqa
+        us = time_fn(fn, args.iters, args.warmup)
+        out.append({"kernel": "gdn_verify", "T": t, "us": round(us, 2),
+                    "state_GB/s": round(state.numel() * 4 * t / (us * 1e-6) / 1e9, 1)})
+        print(json.dumps(out[-1]), flush=True)
+    return out
 
 
 if __name__ == "__main__":
