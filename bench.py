@@ -83,6 +83,8 @@ def main() -> None:
     ap.add_argument("--new-tokens", type=int, default=256)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-plain", action="store_true", help="skip the plain-decode arm")
+    ap.add_argument("--mode", default="serve", choices=["serve", "static"],
+                    help="serve: live-cost model sizes each round (default); static: the full 12/4/16 tree")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -110,7 +112,7 @@ def main() -> None:
     dev = torch.device("cuda", local)
     tree = TreeSpec(12, 4, 16)
     llm = LLM.synthetic(args.model, device=dev, seed=0, tree=tree, max_batch=args.batch,
-                        max_len=args.prompt + args.new_tokens + 64)
+                        max_len=args.prompt + args.new_tokens + 64, config=json.dumps({"mode": args.mode}))
     gen = torch.Generator().manual_seed(1234 + rank)
     prompts = torch.randint(0, llm.target.cfg.vocab_size, (args.batch, args.prompt), generator=gen).pin_memory()
     eng = llm.engine
@@ -183,7 +185,8 @@ def main() -> None:
         "config": {
             "model": "Qwen3.8-27B-shaped hybrid (64 layers, 3 GDN:1 attention) + 1-layer EAGLE-4 draft",
             "global_batch": args.batch * world, "seq_len": args.prompt, "new_tokens": args.new_tokens,
-            "tree": {"steps": tree.steps, "top_k": tree.top_k, "draft_tokens": tree.draft_tokens},
+            "tree": {"steps": tree.steps, "top_k": tree.top_k, "draft_tokens": tree.draft_tokens,
+                     "mode": args.mode, "last_round_depth": eng.last_depth, "last_round_width": eng.last_width},
             "parallelism": f"dp{world}" if world > 1 else "tp1",
             "l2": "inputs larger than L2: every forward streams the 54 GB of target weights",
         },

@@ -14,6 +14,7 @@ from typing import Optional
 
 import torch
 
+from eagle4_b200.core.config import HarnessConfig, parse_harness_config
 from eagle4_b200.models import configs, weights
 from eagle4_b200.models.draft import DraftModel
 from eagle4_b200.models.target import TargetModel
@@ -36,14 +37,18 @@ class TreeSpec:
 
 class LLM:
     def __init__(self, target: TargetModel, draft: Optional[DraftModel], *, tree: TreeSpec = TreeSpec(),
-                 max_batch: int = 1, max_len: int = 4096, page: int = 16):
+                 max_batch: int = 1, max_len: int = 4096, page: int = 16, config=None):
+        """``config``: a ``HarnessConfig``, or the ``--speculative-algorithm-config`` JSON text (inline or a path);
+        None is the static tree of ``tree``."""
+        if isinstance(config, str):
+            config = parse_harness_config(config)
         self.target, self.draft, self.tree = target, draft, tree
         self.engine = Engine(target, draft, max_reqs=max_batch, max_len=max_len, page=page, steps=tree.steps,
-                             top_k=tree.top_k, verify_tokens=tree.draft_tokens)
+                             top_k=tree.top_k, verify_tokens=tree.draft_tokens, config=config)
 
     @classmethod
     def synthetic(cls, name: str, *, device="cuda", dtype=torch.bfloat16, seed: int = 0, tree: TreeSpec = TreeSpec(),
-                  max_batch: int = 1, max_len: int = 4096, draft: bool = True) -> "LLM":
+                  max_batch: int = 1, max_len: int = 4096, draft: bool = True, config=None) -> "LLM":
         """Random-init weights (N(0, 0.02)) of a named architecture; the draft shares the target's embedding."""
         tcfg_fn, dcfg_fn = NAMED[name]
         tcfg = tcfg_fn()
@@ -54,7 +59,7 @@ class LLM:
         if draft:
             dw = weights.init_draft(dcfg, device=device, dtype=dtype, seed=seed + 1, embed=tw["embed"])
             dm = DraftModel(dcfg, dw)
-        return cls(target, dm, tree=tree, max_batch=max_batch, max_len=max_len)
+        return cls(target, dm, tree=tree, max_batch=max_batch, max_len=max_len, config=config)
 
     def generate(self, prompt_ids: torch.Tensor, max_new_tokens: int, *, speculative: bool = True) -> torch.Tensor:
         """``prompt_ids [B, P]`` int64 on the host -> generated ids ``[B, max_new_tokens]`` on the host."""

@@ -236,7 +236,8 @@ __global__ void __launch_bounds__(128) gdn_kernel(GdnArgs a, const int* __restri
   const int vc = min(v, a.V - 1);
   float S[K];
   if (!scan) {
-    const int r = blockIdx.y;
+    // later rows have the longer paths in a tree's node order: start them first
+    const int r = gridDim.y - 1 - blockIdx.y;
     if (threadIdx.x == 0) {
       int n = 0, cur = r;
       int tmp[kMaxPath];

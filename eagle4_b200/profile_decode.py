@@ -49,16 +49,18 @@ def main() -> None:
         if args.only and kind != args.only:
             continue
         eng.prefill(0, prompt)
-        eng._run(kind, 1)  # first round: eager + capture
+        run = (lambda: eng._spec_round(1, args.prompt)) if kind == "spec" else (lambda: eng._plain(1))
+        run()  # first round: eager + capture
         nvtx.range_push(f"{kind}_round")
-        res[f"{kind}_round_ms"] = _t(lambda: eng._run(kind, 1), args.rounds)
+        res[f"{kind}_round_ms"] = _t(run, args.rounds)
         nvtx.range_pop()
     if args.eager and args.only != "plain":
         eng.prefill(0, prompt)
-        eng._run("spec", 1)
+        eng._spec_round(1, args.prompt)
         parts = {}
-        parts["draft_extend_ms"] = _t(lambda: eng._draft_extend(1))
-        parts["draft_steps_ms"] = _t(lambda: eng._draft_steps(1))
+        parts["draft_begin_ms"] = _t(lambda: eng._phase_begin(1))
+        parts["draft_steps_ms"] = _t(lambda: [eng._phase_step(1, s) for s in range(1, eng.steps)])
+        parts["verify_ms"] = _t(lambda: eng._phase_verify(1, eng.verify_tokens))
         res.update(parts)
     native.check_errors()
     print(json.dumps({k: round(v, 3) for k, v in res.items()}))

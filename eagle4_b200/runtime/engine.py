@@ -26,7 +26,10 @@ from typing import Dict, List, Optional, Sequence
 import torch
 
 from eagle4_b200 import ops
+from eagle4_b200.core.config import HarnessConfig, Mode
+from eagle4_b200.core.cost_model import WidthStep
 from eagle4_b200.core.draft_tree import DraftTree, TreeShape
+from eagle4_b200.runtime.policy import RoundPolicy, fit_width
 from eagle4_b200.models.draft import DraftCache, DraftModel
 from eagle4_b200.models.target import Records, RowBatch, TargetCache, TargetModel
 
@@ -70,9 +73,48 @@ def tree_rows_meta(prow: torch.Tensor):
     return depth, anc > 0
 
 
+def _launch_count() -> int:
+    if not torch.cuda.is_available():
+        return 0
+    from eagle4_b200.ops import native
+
+    return native.LAUNCHES[0]
+
+
+def _count_launches(n: int) -> None:
+    """Account this package's kernels launched by a graph replay (recorded at capture) in ``native.LAUNCHES``."""
+    if torch.cuda.is_available():
+        from eagle4_b200.ops import native
+
+        native.LAUNCHES[0] += n
+
+
+class _Stamp:
+    """A CUDA event on a GPU, a host clock reading on the CPU (the CPU path has no asynchrony)."""
+
+    def __init__(self, device: torch.device):
+        self.cuda = device.type == "cuda"
+        self.ev = torch.cuda.Event(enable_timing=True) if self.cuda else None
+        self.t = 0.0
+
+    def record(self) -> None:
+        if self.cuda:
+            self.ev.record()
+        else:
+            import time
+
+            self.t = time.perf_counter()
+
+    def elapsed_us(self, later: "_Stamp") -> float:
+        if self.cuda:
+            return self.ev.elapsed_time(later.ev) * 1e3
+        return (later.t - self.t) * 1e6
+
+
 class Engine:
     def __init__(self, target: TargetModel, draft: Optional[DraftModel], *, max_reqs: int, max_len: int,
-                 page: int = 16, steps: int = 4, top_k: int = 2, verify_tokens: int = 8, use_graphs: bool = True):
+                 page: int = 16, steps: int = 4, top_k: int = 2, verify_tokens: int = 8, use_graphs: bool = True,
+                 config: Optional[HarnessConfig] = None):
         self.target, self.draft = target, draft
         self.device = target.device
         self.dtype = target.dtype
@@ -88,8 +130,15 @@ class Engine:
         if draft is not None:
             self.dcache = DraftCache.allocate(draft.cfg, self.tcache.block_table, page, self.device, self.dtype)
             shape = TreeShape(top_k=top_k, max_depth=steps)
+        self.config = config or HarnessConfig(mode=Mode.STATIC)
+        self.policy = RoundPolicy(self.config, top_k=top_k, steps=steps, verify_tokens=verify_tokens,
+                                  target_is_moe=target.cfg.is_moe)
+        if draft is not None:
+            # work deltas are only read by the cost model's decisions
+            slots = None if self.policy.cost is not None else ()
+            budget = max(verify_tokens, self.policy.cost.max_history_verify_num if self.policy.cost else 1)
             self.tree = DraftTree(shape, max_reqs, draft.cfg.hidden_size, self.dtype, self.device,
-                                  max_verify=min(verify_tokens, shape.work_cap))
+                                  max_verify=min(budget, shape.work_cap), delta_slots=slots)
         dev, n = self.device, verify_tokens
         i64, i32 = torch.int64, torch.int32
         # device state, one row per batch position
@@ -107,7 +156,14 @@ class Engine:
         self.host_cnt = torch.zeros(max_reqs, dtype=i32, pin_memory=pin)
         self.use_graphs = use_graphs and dev.type == "cuda"
         self.graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
+        self.pool = torch.cuda.graph_pool_handle() if self.use_graphs else None
+        self.graph_launches: Dict[tuple, int] = {}
         self.stats = RoundStats()
+        if self.tree is not None:
+            self.host_deltas = torch.zeros(tuple(self.tree.deltas.shape), dtype=torch.float32, pin_memory=pin)
+            self.host_scores = torch.zeros(n, dtype=torch.float32, pin_memory=pin)
+            self.lagged_scores: Optional[List[float]] = None
+            self.last_depth = self.last_width = 0
 
     # ------------------------------------------------------------------ helpers
     def _slots(self, slot: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
@@ -200,7 +256,16 @@ class Engine:
         probs, toks = draft.candidates(normed.index_select(0, last), self.top_k, pos.reshape(-1).index_select(0, last))
         self.tree.stage_root(bs, probs, toks, nh.index_select(0, last))
 
-    def _draft_steps(self, bs: int) -> None:
+    def _phase_begin(self, bs: int) -> None:
+        """Draft extend, then depth 1 of a fresh tree (its work deltas copied to the host)."""
+        self._draft_extend(bs)
+        self.tree.scores[:bs].zero_()  # undrafted depths rank last in the verify selection
+        self.tree.begin(bs)
+        if 0 in self.tree.delta_slots:
+            self.host_deltas[0].copy_(self.tree.deltas[0], non_blocking=True)
+
+    def _phase_step(self, bs: int, s: int) -> None:
+        """Draft step ``s``: the depth-``s`` frontier through the draft head; adds depth ``s + 1``."""
         k, tree, draft, dev = self.top_k, self.tree, self.draft, self.device
         w = draft.cfg.sliding_window
         Lr = self.L[:bs].repeat_interleave(k)
@@ -208,23 +273,28 @@ class Engine:
         lane = torch.arange(k, device=dev).repeat(bs)
         start = ((Lr - w).clamp(min=0) if w else torch.zeros_like(Lr)).int()
         keys = min(w, self.max_len) + self.steps if w else self.max_len + self.steps
-        tree.begin(bs)
-        for s in range(1, self.steps):
-            slots = self._slots(req, Lr + (s - 1) * k + lane)
-            tree.set_step_slots(bs, s, slots.view(bs, k))
-            extra = tree.ancestors[:bs, :, :s].reshape(bs * k, s).contiguous()
-            n_extra = torch.full((bs * k,), s, dtype=torch.int32, device=dev)
-            normed, nh = draft.forward(tree.front_tokens[: bs * k], tree.front_hidden[: bs * k], Lr - 1 + s, req,
-                                       slots, start, Lr.int(), extra, n_extra, self.dcache, max_keys=keys)
-            probs, toks = draft.candidates(normed, k, Lr - 1 + s)
-            tree.step(bs, s, probs, toks, nh)
+        slots = self._slots(req, Lr + (s - 1) * k + lane)
+        tree.set_step_slots(bs, s, slots.view(bs, k))
+        extra = tree.ancestors[:bs, :, :s].reshape(bs * k, s).contiguous()
+        n_extra = torch.full((bs * k,), s, dtype=torch.int32, device=dev)
+        normed, nh = draft.forward(tree.front_tokens[: bs * k], tree.front_hidden[: bs * k], Lr - 1 + s, req,
+                                   slots, start, Lr.int(), extra, n_extra, self.dcache, max_keys=keys)
+        probs, toks = draft.candidates(normed, k, Lr - 1 + s)
+        tree.step(bs, s, probs, toks, nh)
+        if s in tree.delta_slots:
+            self.host_deltas[s].copy_(tree.deltas[s], non_blocking=True)
 
-    def _spec_round(self, bs: int) -> None:
-        n, dev = self.verify_tokens, self.device
-        self._draft_extend(bs)
-        self._draft_steps(bs)
-        toks, prow = self.tree.verify_rows(bs, self.steps, n - 1)
-        tokens = torch.cat([self.root[:bs, None], toks], dim=1)  # [bs, n]
+    def _phase_verify(self, bs: int, n: int) -> None:
+        """Verify the root and the best ``n - 1`` drafted nodes, accept, commit; rank this round's tree for the
+        next round's verify-width decision."""
+        dev = self.device
+        tree = self.tree
+        if n > 1:
+            toks, prow = tree.verify_rows(bs, self.steps, n - 1)
+            tokens = torch.cat([self.root[:bs, None], toks], dim=1)  # [bs, n]
+        else:
+            tokens = self.root[:bs, None].clone()
+            prow = torch.full((bs, 1), -1, dtype=torch.int32, device=dev)
         depth, anc = tree_rows_meta(prow)
         L, sl = self.L[:bs], self.slot[:bs]
         rowidx = torch.arange(n, device=dev)
@@ -257,30 +327,96 @@ class Engine:
         c1 = (cnt - 1)[:, None]
         emitted = torch.where(rowidx[None, :] < c1, shifted,
                               torch.where(rowidx[None, :] == c1, bonus[:, None], torch.zeros_like(shifted)))
-        self.out_tok[:bs] = emitted
+        self.out_tok[:bs, :n] = emitted
         self.out_cnt[:bs] = cnt
-        self.ext_tok[:bs] = emitted
+        self.ext_tok[:bs, :n] = emitted
         self.ext_cnt[:bs] = cnt
-        self.ext_aux[:bs] = aux.index_select(0, (accc + base).reshape(-1)).view(bs, n, -1)
+        self.ext_aux[:bs, :n] = aux.index_select(0, (accc + base).reshape(-1)).view(bs, n, -1)
         self.L[:bs] += cnt.long()
         self.root[:bs] = bonus
+        if self.policy.cost is not None:
+            # cumulative decayed scores of this round's best nodes (root first), batch mean: the next round's
+            # lagged verify-width input
+            count = self.verify_tokens - 1
+            _, cum = tree.rank_reference(bs, self.steps, count)
+            self.host_scores[: cum.shape[1]].copy_(cum.mean(dim=0), non_blocking=True)
 
-    def _run(self, kind: str, bs: int) -> None:
-        """One round; on a GPU the first round of a (kind, batch size) runs eagerly (which also sizes every
-        lazily allocated workspace) and is then captured, and later rounds replay the graph."""
-        fn = self._spec_round if kind == "spec" else self._plain_round
-        key = (kind, bs)
+    def _graph(self, key: tuple, fn, *args) -> None:
+        """Run ``fn(*args)``; on a GPU the first call of a key runs eagerly (sizing lazily allocated workspaces)
+        and is then captured into a CUDA graph that later calls replay."""
         g = self.graphs.get(key)
         if g is not None:
             g.replay()
+            _count_launches(self.graph_launches[key])
             return
-        fn(bs)
+        fn(*args)
         if self.use_graphs:
             torch.cuda.synchronize()
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                fn(bs)  # recorded, not executed
+            before = _launch_count()
+            with torch.cuda.graph(g, pool=self.pool):
+                fn(*args)  # recorded, not executed
+            self.graph_launches[key] = _launch_count() - before
+            _count_launches(-self.graph_launches[key])  # recorded launches run at replay
             self.graphs[key] = g
+
+    def _spec_round(self, bs: int, context: int) -> int:
+        """One speculative round driven by the round policy (the reference drafter's decision loop,
+        ``eagle_harness/sglang/drafter.py:482-691``): steps run until a DECIDE depth's work deltas say stop, then
+        the verify width comes from the previous round's scores. Returns the verify width."""
+        policy = self.policy.begin_round(bs)
+        timed = self.policy.live is not None
+        if timed:
+            ev = [_Stamp(self.device) for _ in range(3)]
+            ev[0].record()
+        self._graph(("begin", bs), self._phase_begin, bs)
+        row = policy.draft_cost_row(bs, context)
+        past = policy.history_verify_num(bs)
+        deltas_ready = torch.cuda.Event() if self.device.type == "cuda" else None
+        slot = 0
+        depth = 0
+        while depth < self.steps - 1:
+            kind = policy.width_step(depth)
+            if kind is WidthStep.LAST:
+                break
+            if kind is WidthStep.LAUNCH:
+                if deltas_ready is not None:
+                    deltas_ready.record()
+                slot = depth
+            elif kind is WidthStep.DECIDE:
+                if deltas_ready is not None:
+                    deltas_ready.synchronize()
+                budget = policy.deltas_budget(past)
+                deltas = self.host_deltas[slot, budget - 1].tolist()
+                if policy.tree_width(depth, bs, past, row, deltas).stop:
+                    break
+            depth += 1
+            self._graph(("step", bs, depth), self._phase_step, bs, depth)
+        levels = depth + 1
+        nodes = self.tree.shape.num_nodes(levels)
+        widths = self.policy.widths(bs)
+        verify_count = policy.verify_count(bs, nodes + 1)
+        if self.lagged_scores is not None:
+            req = verify_count
+            if not policy.verifies_whole_draft:
+                req, _ = policy.verify_num_paged(self.lagged_scores[:verify_count], verify_count, bs, context,
+                                                 lagged=True)
+                policy.record_verify_num(bs, req)
+                req = min(req, verify_count)
+            width = fit_width(req, widths, nodes + 1)
+        else:
+            width = fit_width(verify_count, widths, nodes + 1)
+        if timed:
+            ev[1].record()
+        self._graph(("verify", bs, width), self._phase_verify, bs, width)
+        if timed:
+            ev[2].record()
+            self._pending_timing = (bs, width, context, ev, depth)
+        self.last_depth, self.last_width = levels, width
+        return width
+
+    def _plain(self, bs: int) -> None:
+        self._graph(("plain", bs), self._plain_round, bs)
 
     # ------------------------------------------------------------------ driver
     def generate(self, prompts, max_new_tokens: int, *, speculative: bool = True) -> List[List[int]]:
@@ -290,24 +426,37 @@ class Engine:
         if bs > self.max_reqs:
             raise ValueError(f"batch {bs} exceeds max_reqs {self.max_reqs}")
         outs: List[List[int]] = [[] for _ in range(bs)]
+        ctx = [int(p.shape[0]) for p in prompts]
         for b, p in enumerate(prompts):
             self.prefill(b, p)
+        if self.tree is not None:
+            self.lagged_scores = None
         self.host_tok[:bs].copy_(self.out_tok[:bs])
         for b in range(bs):
             outs[b].append(int(self.host_tok[b, 0]))
         spec = speculative and self.draft is not None
         while min(len(o) for o in outs) < max_new_tokens:
-            self._run("spec" if spec else "plain", bs)
+            self._pending_timing = None
+            if spec:
+                self._spec_round(bs, sum(ctx) // bs)
+            else:
+                self._plain(bs)
             self.host_tok[:bs].copy_(self.out_tok[:bs], non_blocking=True)
             self.host_cnt[:bs].copy_(self.out_cnt[:bs], non_blocking=True)
             if self.device.type == "cuda":
                 torch.cuda.current_stream().synchronize()
+            if spec and self.policy.cost is not None:
+                self.lagged_scores = self.host_scores.tolist()
+            if self._pending_timing is not None:
+                b_, w_, c_, ev, nsteps = self._pending_timing
+                self.policy.record(b_, w_, c_, ev[1].elapsed_us(ev[2]), nsteps, ev[0].elapsed_us(ev[1]))
             got = []
             for b in range(bs):
                 c = int(self.host_cnt[b])
                 room = max_new_tokens - len(outs[b])
                 take = min(c, room)
                 outs[b].extend(self.host_tok[b, :take].tolist())
+                ctx[b] += c
                 got.append(take)
             if spec:
                 self.stats.record(got)

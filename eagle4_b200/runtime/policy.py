@@ -1,0 +1,121 @@
+"""Round policy of the serving loop: the fixed tree shape, or the measured cost model fed by live costs.
+
+Mirrors the reference drafter's policy choice (``eagle_harness/sglang/drafter.py:315-389``): a round uses the cost
+model once its batch bucket is priced, else the fixed shape (static mode, or the live seed sweep, which forces each
+captured verify width for a few rounds so every width of the bucket gets timed). Live cells are refreshed into the
+cost model's tables when a bucket becomes ready and every ``LIVE_REFRESH_ROUNDS`` rounds; buckets whose measured
+costs the cost model's checks refuse keep the fixed shape.
+"""
+
+from __future__ import annotations
+
+import logging
+import os
+from collections import Counter
+from typing import Callable, List, Optional, Sequence
+
+from eagle4_b200.core.config import HarnessConfig, Mode, build_cost_model
+from eagle4_b200.core.cost_model import CostModel, FixedShapePolicy, depth_loss_ratio
+from eagle4_b200.core.cost_table import cost_model_problem
+from eagle4_b200.core.limits import verify_buckets
+from eagle4_b200.core.live_costs import DRAFT_WIDTH, CostKey, LiveCosts
+
+log = logging.getLogger(__name__)
+
+LIVE_REFRESH_ROUNDS = 64
+
+
+def round_up_width(width: int, widths: Sequence[int]) -> int:
+    """The smallest captured width ``>= width`` (the widest when none is)."""
+    up = [w for w in widths if w >= width]
+    return min(up) if up else max(widths)
+
+
+def fit_width(width: int, widths: Sequence[int], available: int) -> int:
+    """The captured verify width for a requested ``width`` with ``available`` tree tokens (root included): the
+    smallest captured width >= width if the tree fills it, else the widest one it fills."""
+    up = round_up_width(width, widths)
+    if up <= available:
+        return up
+    return max(w for w in widths if w <= available)
+
+
+class RoundPolicy:
+    def __init__(self, config: HarnessConfig, *, top_k: int, steps: int, verify_tokens: int,
+                 target_is_moe: bool = False, key: Optional[CostKey] = None):
+        self.config = config
+        self.top_k, self.steps, self.verify_tokens = top_k, steps, verify_tokens
+        self.fixed = FixedShapePolicy(config.intensity, top_k, steps, verify_tokens)
+        self.cost: Optional[CostModel] = None
+        self.live: Optional[LiveCosts] = None
+        self.visits: Counter = Counter()
+        self.rounds = 0
+        self.unpriced: set = set()
+        self.key = key
+        if not config.mode.uses_cost_model:
+            return
+        if config.data_path:
+            self.cost = build_cost_model(config, node_top_k=top_k, tree_depth=steps, verify_num=verify_tokens,
+                                         target_is_moe=target_is_moe, key=key)
+            return
+        loss = depth_loss_ratio(config.draft_family.value, target_is_moe=target_is_moe, intensity=config.intensity)
+        self.cost = CostModel(tables={}, params=config.cost_model.params(loss), intensity=config.intensity,
+                              node_top_k=top_k, tree_depth=steps, verify_num=verify_tokens,
+                              target_is_moe=target_is_moe)
+        self.live = LiveCosts(self.widths, key=key, draft_shape=(top_k, steps))
+        if key is not None and self.live.load(self.cache_path):
+            self._refresh()
+
+    # ------------------------------------------------------------------ shapes
+    def widths(self, bucket: int) -> List[int]:
+        """Verify widths with a graph at ``bucket``: the calibrated buckets up to the configured draft tokens, plus
+        the configured width itself; widest first."""
+        ws = {w for w in verify_buckets(bucket, self.config.intensity) if w <= self.verify_tokens}
+        ws.update({1, self.verify_tokens})
+        return sorted(ws, reverse=True)
+
+    @property
+    def cache_path(self) -> str:
+        return os.path.join(self.config.cost_cache_dir, f"{self.key.digest}.json")
+
+    # ------------------------------------------------------------------ rounds
+    def begin_round(self, bs: int):
+        """The policy object of this round (``CostModel`` or ``FixedShapePolicy``)."""
+        self.rounds += 1
+        if self.cost is None:
+            return self.fixed
+        if self.live is None:
+            return self.cost
+        self.visits[bs] += 1
+        ready = self.live.ready(bs)
+        if ready and (bs not in self.cost.tables or self.rounds % LIVE_REFRESH_ROUNDS == 0):
+            self._refresh()
+        if ready and bs in self.cost.tables and bs not in self.unpriced:
+            self.fixed.force_width = None
+            return self.cost
+        self.fixed.force_width = self.live.seed_width(bs)
+        return self.fixed
+
+    def _refresh(self) -> None:
+        tables = self.live.tables(also=tuple(self.visits))
+        for b, t in tables.items():
+            problem = cost_model_problem(t, target_is_moe=self.cost.target_is_moe)
+            if problem is None:
+                self.unpriced.discard(b)
+            elif b not in self.unpriced:
+                self.unpriced.add(b)
+                log.warning("eagle4_b200: batch bucket %d keeps the fixed draft shape: %s", b, problem)
+        self.cost.set_tables(tables, refused=self.unpriced)
+        if self.key is not None:
+            try:
+                self.live.save(self.cache_path)
+            except OSError as e:  # a read-only cache directory only costs a re-measurement next start
+                log.info("live cost cache not saved: %s", e)
+
+    def record(self, bs: int, width: int, context: int, verify_us: float, steps: int, draft_us: float) -> None:
+        """One served round's timings: the verify at ``width`` and the mean draft step."""
+        if self.live is None:
+            return
+        self.live.record(bs, width, context, verify_us)
+        if steps > 0:
+            self.live.record(bs, DRAFT_WIDTH, context, draft_us / steps)

@@ -1,0 +1,63 @@
+"""Serve mode: the measured cost model sizes every round (offline tables or live costs) and the output still equals
+plain greedy decoding."""
+
+import json
+import os
+
+import torch
+
+from eagle4_b200.core.config import harness_config_from_dict
+from eagle4_b200.core.cost_table import CostCurve, write_interval
+from eagle4_b200.runtime.engine import Engine
+from eagle4_b200.runtime.policy import fit_width
+
+from test_engine_cpu import _models
+
+
+def _write_tables(root, bss=(1, 2), widths=(1, 8), ratio=20.0):
+    for bs in bss:
+        for i in range(2):
+            tv = [1000.0 * (1 + 0.01 * (w - 1)) for w in widths]
+            tgt = CostCurve.from_values(tv, [w - 1 for w in widths])
+            dft = CostCurve.from_values([tv[0] / ratio], [0])
+            kw = dict(batch_size=bs, cache_length_start=1024, cache_length_step=1024, max_query_length_query=widths[-1],
+                      max_query_length_cache=widths[-1])
+            write_interval(os.path.join(root, "cost", f"bs_{bs}", "model_llm", f"model_interval_{i}.json"), tgt, **kw)
+            write_interval(os.path.join(root, "cost", f"bs_{bs}", "model_slm", f"model_interval_{i}.json"), dft,
+                           **dict(kw, max_query_length_query=1))
+
+
+def test_fit_width():
+    assert fit_width(5, [16, 8, 1], 20) == 8
+    assert fit_width(9, [16, 8, 1], 12) == 8
+    assert fit_width(1, [16, 8, 1], 3) == 1
+
+
+def test_offline_cost_model_rounds_equal_plain(tmp_path):
+    _write_tables(str(tmp_path))
+    cfg = harness_config_from_dict({"data_path": str(tmp_path)})
+    tgt, drf = _models()
+    g = torch.Generator().manual_seed(0)
+    prompts = torch.randint(0, tgt.cfg.vocab_size, (2, 40), generator=g).tolist()
+    eng = Engine(tgt, drf, max_reqs=2, max_len=128, steps=4, top_k=2, verify_tokens=8, config=cfg)
+    assert eng.policy.cost is not None and eng.policy.live is None
+    out = eng.generate(prompts, 20, speculative=True)
+    plain = Engine(tgt, drf, max_reqs=2, max_len=128, steps=4, top_k=2, verify_tokens=8).generate(
+        prompts, 20, speculative=False)
+    assert out == plain
+    assert eng.last_width in (1, 8)
+
+
+def test_live_costs_seed_then_price(tmp_path):
+    cfg = harness_config_from_dict({"cost_cache": str(tmp_path)})
+    tgt, drf = _models()
+    g = torch.Generator().manual_seed(1)
+    prompts = torch.randint(0, tgt.cfg.vocab_size, (1, 24), generator=g).tolist()
+    eng = Engine(tgt, drf, max_reqs=1, max_len=160, steps=4, top_k=2, verify_tokens=8, config=cfg)
+    live = eng.policy.live
+    out = eng.generate(prompts, 40, speculative=True)
+    plain = Engine(tgt, drf, max_reqs=1, max_len=160, steps=4, top_k=2, verify_tokens=8).generate(
+        prompts, 40, speculative=False)
+    assert out == plain
+    # the seed sweep timed every captured width and the draft step of bucket 1
+    assert live.seed_width(1) is None and live.ready(1)
