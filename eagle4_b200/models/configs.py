@@ -132,6 +132,31 @@ class TargetConfig:
             )
         raise ValueError(f"unsupported target model_type {mt!r}")
 
+    def to_hf(self) -> dict:
+        """A Hugging Face style ``config.json`` of this shape (the inverse of :meth:`from_hf`)."""
+        common = {"hidden_size": self.hidden_size, "vocab_size": self.vocab_size,
+                  "num_hidden_layers": self.num_layers, "intermediate_size": self.intermediate_size,
+                  "num_attention_heads": self.num_heads, "num_key_value_heads": self.num_kv_heads,
+                  "head_dim": self.head_dim, "tie_word_embeddings": self.tie_embeddings}
+        if self.family == "qwen3_5":
+            return dict(common, model_type="qwen3_5_text", architectures=["Qwen3_5ForCausalLM"],
+                        rms_norm_eps=self.rms_norm_eps, attn_output_gate=self.attn_output_gate,
+                        layer_types=["linear_attention" if m == "gdn" else "full_attention" for m, _ in self.layers],
+                        linear_num_key_heads=self.gdn_k_heads, linear_num_value_heads=self.gdn_v_heads,
+                        linear_key_head_dim=self.gdn_k_dim, linear_value_head_dim=self.gdn_v_dim,
+                        linear_conv_kernel_dim=self.conv_kernel,
+                        rope_parameters={"rope_theta": self.rope_theta,
+                                         "partial_rotary_factor": self.rotary_dim / self.head_dim})
+        if self.family == "nemotron_h":
+            sym = {("mamba", None): "M", ("attn", None): "*", (None, "relu2"): "-"}
+            return dict(common, model_type="nemotron_h", architectures=["NemotronHForCausalLM"],
+                        layer_norm_epsilon=self.rms_norm_eps,
+                        hybrid_override_pattern="".join(sym[tuple(x)] for x in self.layers),
+                        mamba_num_heads=self.mamba_heads, mamba_head_dim=self.mamba_head_dim,
+                        ssm_state_size=self.mamba_state, n_groups=self.mamba_groups, conv_kernel=self.conv_kernel)
+        return dict(common, model_type="llama", architectures=["LlamaForCausalLM"], rms_norm_eps=self.rms_norm_eps,
+                    rope_theta=self.rope_theta)
+
 
 @dataclass
 class DraftConfig:

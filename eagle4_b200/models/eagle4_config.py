@@ -18,10 +18,11 @@ from numbers import Integral
 from typing import Any, Dict, Mapping, Optional
 
 from eagle4_b200.models.configs import DraftConfig
+from eagle4_b200.models.eagle4_structure import LATENT_MOE_ARCHITECTURE, draft_moe_architecture, draft_uses_rope
 
 EAGLE4_ARCH = "LlamaForCausalLMEagle4"
 LAYER_TYPES = ("full_attention", "sliding_attention")
-LATENT_MOE = "nemotron_latent_relu2"
+LATENT_MOE = LATENT_MOE_ARCHITECTURE
 DENSE_MOE = ("sparse_swiglu",)
 
 STRUCTURAL_KEYS = frozenset({
@@ -62,20 +63,6 @@ def _as_dict(config) -> Dict[str, Any]:
     if isinstance(config, Mapping):
         return dict(config)
     return dict(config.to_dict())
-
-
-def draft_uses_rope(cfg: Mapping[str, Any]) -> bool:
-    """NoPE drafts turn rotary positions off by ``use_rope: false``, ``position_embedding_type: none`` or a zero
-    ``partial_rotary_factor``."""
-    if cfg.get("use_rope") is False or cfg.get("position_embedding_type") == "none":
-        return False
-    return cfg.get("partial_rotary_factor", None) != 0
-
-
-def draft_moe_architecture(cfg: Mapping[str, Any]) -> Optional[str]:
-    if not cfg.get("enable_moe"):
-        return None
-    return cfg.get("moe_architecture") or DENSE_MOE[0]
 
 
 def resolve_draft_sliding_window(config) -> Optional[int]:
