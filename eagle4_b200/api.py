@@ -66,3 +66,44 @@ class LLM:
         dev_ids = prompt_ids.to(self.target.device, non_blocking=True)
         out = self.engine.generate(dev_ids, max_new_tokens, speculative=speculative)
         return torch.tensor(out, dtype=torch.int64)
+
+
+def _load_safetensors_dir(path: str, device) -> dict:
+    import os
+
+    from safetensors.torch import load_file
+
+    sd = {}
+    for name in sorted(os.listdir(path)):
+        if name.endswith(".safetensors"):
+            sd.update(load_file(os.path.join(path, name), device=str(device)))
+    if not sd:
+        raise FileNotFoundError(f"no .safetensors files under {path}")
+    return sd
+
+
+def from_pretrained(model_path: str, draft_path: Optional[str] = None, *, device="cuda", dtype=torch.bfloat16,
+                    tree: TreeSpec = TreeSpec(), max_batch: int = 1, max_len: int = 4096, config=None) -> LLM:
+    """An :class:`LLM` from a Hugging Face target directory and an EAGLE-4 / EAGLE-3 draft directory (both with
+    ``config.json`` and safetensors). Draft configs are validated; structures this package does not build raise."""
+    import json
+    import os
+
+    from eagle4_b200.models.configs import TargetConfig
+    from eagle4_b200.models.eagle4_config import draft_config_from_hf
+
+    with open(os.path.join(model_path, "config.json"), encoding="utf-8") as f:
+        tcfg = TargetConfig.from_hf(json.load(f))
+    dm = None
+    aux = (2, tcfg.num_layers // 2, tcfg.num_layers - 3)
+    if draft_path is not None:
+        with open(os.path.join(draft_path, "config.json"), encoding="utf-8") as f:
+            dcfg = draft_config_from_hf(json.load(f), target_vocab_size=tcfg.vocab_size)
+        aux = dcfg.aux_layer_ids
+    sd = {k: v.to(dtype) if v.is_floating_point() else v for k, v in _load_safetensors_dir(model_path, "cpu").items()}
+    tw = {k: v.to(device) for k, v in weights.target_from_hf(tcfg, sd).items()}
+    del sd
+    target = TargetModel(tcfg, tw, aux_layer_ids=aux)
+    if draft_path is not None:
+        dm = DraftModel(dcfg, weights.load_draft(draft_path, dcfg, device=device, dtype=dtype, embed=tw["embed"]))
+    return LLM(target, dm, tree=tree, max_batch=max_batch, max_len=max_len, config=config)

@@ -1,0 +1,81 @@
+"""CLI, host checks and the engine calibration driver (tiny model on CPU; the GPU run uses the same code)."""
+
+import json
+import os
+
+import pytest
+import torch
+
+from eagle4_b200 import cli, compat
+from eagle4_b200.plugins import contract
+
+
+def test_cli_dry_run(capsys, tmp_path):
+    assert cli.main(["calibrate", "--model", "tiny", "--output", str(tmp_path / "cal"), "--dry-run"]) == 0
+    out = capsys.readouterr().out
+    assert '"batch_sizes"' in out and "eagle4_b200.serve" in out
+    assert not (tmp_path / "cal").exists()
+    with pytest.raises(SystemExit):
+        cli.main(["calibrate", "--model", "tiny", "--batch-sizes", "0,1"])
+
+
+def test_compat_reports_hosts(capsys):
+    compat.main([])
+    out = capsys.readouterr().out
+    for name in ("sglang", "vllm", "tokenspeed"):
+        assert name in out
+
+
+def test_contract_checks_fake_host(tmp_path, monkeypatch):
+    pkg = tmp_path / "fakehost"
+    pkg.mkdir()
+    (pkg / "__init__.py").write_text(
+        "class Algo:\n"
+        "    def hook(self, a, b): pass\n"
+        "    def call(self, a, b, c=1): pass\n"
+        "class Data:\n"
+        "    field_x = 1\n")
+    monkeypatch.syspath_prepend(str(tmp_path))
+    H = contract.Hook
+    ok = [H("fakehost:Algo.hook", ("a", "b"), contract.OVERRIDE), H("fakehost:Algo.call", ("a", "b")),
+          H("fakehost:Data.field_x", (), contract.FIELD), H("fakehost:Nope.x", (), contract.CALL, optional=True)]
+    assert contract.problems(ok) == []
+    bad = [H("fakehost:Algo.hook", ("a",), contract.OVERRIDE), H("fakehost:Algo.call", ("z",)),
+           H("fakehost:Data.missing", (), contract.FIELD), H("fakehost:Gone.x")]
+    assert len(contract.problems(bad)) == 4
+
+
+def test_calibrate_tiny_on_cpu(tmp_path):
+    from eagle4_b200.api import LLM, TreeSpec
+    from eagle4_b200.core.cost_table import load_cost_tables
+    from eagle4_b200.runtime.calibrate import calibrate
+
+    llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_len=512)
+    problems = calibrate(llm.engine, str(tmp_path), batch_sizes=[1], context_step=64, context_stop=256, repeats=2,
+                         progress=lambda s: None)
+    assert set(problems) == {1}
+    tables = load_cost_tables(os.path.join(tmp_path, "cost"))
+    t = tables[1]
+    assert len(t.intervals) == 3 and t.intervals[0].target.value[0] > 0
+    with open(os.path.join(tmp_path, "config", "measure_config.json")) as f:
+        assert json.loads(f.readline())["batch_size"] == 1
+
+
+def test_serve_app_round_trip():
+    from fastapi.testclient import TestClient
+
+    from eagle4_b200.api import LLM, TreeSpec
+    from eagle4_b200.serve import Batcher, make_app
+
+    llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_batch=2, max_len=256)
+    b = Batcher(llm.engine, 2)
+    try:
+        client = TestClient(make_app(b))
+        r = client.post("/v1/generate", json={"prompt_ids": list(range(1, 20)), "max_new_tokens": 6})
+        assert r.status_code == 200 and len(r.json()["output_ids"]) == 6
+        plain = client.post("/v1/generate", json={"prompt_ids": list(range(1, 20)), "max_new_tokens": 6,
+                                                  "speculative": False})
+        assert plain.json()["output_ids"] == r.json()["output_ids"]
+        assert client.get("/health").json()["rounds"] >= 1
+    finally:
+        b.stop.set()
