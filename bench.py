@@ -9,8 +9,10 @@ uniform-random prompt and 256 greedy output tokens. One step = one whole generat
   python bench.py --gpus N --steps K --warmup W            # this framework
   python bench.py --impl reference ...                     # the reference's own serving path
 
-With N > 1 (launched by torch.distributed.run) every rank serves its own batch (data-parallel replicas, weak
-scaling); the device time is the max over ranks. Prints one JSON line on rank 0.
+With N > 1 (launched by torch.distributed.run) the ranks serve one batch together with tensor parallelism (TP = N,
+strong scaling; ``--parallelism dp`` runs data-parallel replicas instead). The tensor-parallel collectives are the
+fused peer-memory kernels (``--tp-backend torch`` measures the NCCL all-reduce baseline). The device time is the max
+over ranks. Prints one JSON line on rank 0.
 """
 
 from __future__ import annotations
@@ -83,6 +85,8 @@ def main() -> None:
     ap.add_argument("--new-tokens", type=int, default=256)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-plain", action="store_true", help="skip the plain-decode arm")
+    ap.add_argument("--parallelism", default="tp", choices=["tp", "dp"])
+    ap.add_argument("--tp-backend", default="fused", choices=["fused", "torch"])
     ap.add_argument("--mode", default="serve", choices=["serve", "static"],
                     help="serve: live-cost model sizes each round (default); static: the full 12/4/16 tree")
     args = ap.parse_args()
@@ -110,10 +114,17 @@ def main() -> None:
     from eagle4_b200.ops import native
 
     dev = torch.device("cuda", local)
+    tp = None
+    tp_mode = world > 1 and args.parallelism == "tp"
+    if tp_mode:
+        from eagle4_b200.parallel.tp import TensorParallel
+
+        tp = TensorParallel(backend=args.tp_backend, max_rows=max(256, args.prompt), max_cols=8192, device=dev)
+    replicas = 1 if tp_mode else world  # independent request streams
     tree = TreeSpec(12, 4, 16)
     llm = LLM.synthetic(args.model, device=dev, seed=0, tree=tree, max_batch=args.batch,
-                        max_len=args.prompt + args.new_tokens + 64, config=json.dumps({"mode": args.mode}))
-    gen = torch.Generator().manual_seed(1234 + rank)
+                        max_len=args.prompt + args.new_tokens + 64, config=json.dumps({"mode": args.mode}), tp=tp)
+    gen = torch.Generator().manual_seed(1234 + (0 if tp_mode else rank))
     prompts = torch.randint(0, llm.target.cfg.vocab_size, (args.batch, args.prompt), generator=gen).pin_memory()
     eng = llm.engine
 
@@ -167,7 +178,7 @@ def main() -> None:
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     native.check_errors(dev)
 
-    total_tok = spec_tok * world
+    total_tok = spec_tok * replicas
     value = total_tok / (spec_ms / 1e3)
     line = {
         "metric": METRIC,
@@ -178,31 +189,36 @@ def main() -> None:
         "warmup": args.warmup,
         "ms_per_step": round(spec_ms / args.steps, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if tp_mode else "weak",
         "vs_baseline": round(value / BASELINE_TPS, 4),
         "dtype": "bf16",
         "data": "synthetic: uniform-random prompt ids, random-init N(0,0.02) weights of the named shapes",
         "config": {
             "model": "Qwen3.8-27B-shaped hybrid (64 layers, 3 GDN:1 attention) + 1-layer EAGLE-4 draft",
-            "global_batch": args.batch * world, "seq_len": args.prompt, "new_tokens": args.new_tokens,
+            "global_batch": args.batch * replicas, "seq_len": args.prompt, "new_tokens": args.new_tokens,
             "tree": {"steps": tree.steps, "top_k": tree.top_k, "draft_tokens": tree.draft_tokens,
                      "mode": args.mode, "last_round_depth": eng.last_depth, "last_round_width": eng.last_width},
-            "parallelism": f"dp{world}" if world > 1 else "tp1",
+            "parallelism": f"tp{world}" if tp_mode else (f"dp{world}" if world > 1 else "tp1"),
+            "tp_collectives": (args.tp_backend if tp_mode else None),
             "l2": "inputs larger than L2: every forward streams the 54 GB of target weights",
         },
         "speculative_tok_s": round(value, 2),
-        "plain_tok_s": round(plain_tok * world / (plain_ms / 1e3), 2) if plain_ms else None,
+        "plain_tok_s": round(plain_tok * replicas / (plain_ms / 1e3), 2) if plain_ms else None,
         "speedup_vs_plain": round((spec_tok / spec_ms) / (plain_tok / plain_ms), 4) if plain_ms else None,
         "mean_accepted_per_round": round(accept, 3),
         "spec_equals_plain": same,
         "clocks": clocks,
-        "e2e": {"value": round(e2e_tok * world / e2e_s, 2), "unit": "tokens/s",
+        "e2e": {"value": round(e2e_tok * replicas / e2e_s, 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(prompts.numel() * prompts.element_size()),
                 "d2h_bytes_per_step": int(args.batch * args.new_tokens * 8)},
         "gpu_launches": launches,
     }
     if rank == 0:
         print(json.dumps(line))
+    eng.graphs.clear()  # graphs may hold NCCL calls (torch backend): release them before the group goes
+    torch.cuda.synchronize()
+    if tp is not None:
+        tp.close()
     if dist is not None:
         dist.destroy_process_group()
 

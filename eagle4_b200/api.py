@@ -48,17 +48,24 @@ class LLM:
 
     @classmethod
     def synthetic(cls, name: str, *, device="cuda", dtype=torch.bfloat16, seed: int = 0, tree: TreeSpec = TreeSpec(),
-                  max_batch: int = 1, max_len: int = 4096, draft: bool = True, config=None) -> "LLM":
-        """Random-init weights (N(0, 0.02)) of a named architecture; the draft shares the target's embedding."""
+                  max_batch: int = 1, max_len: int = 4096, draft: bool = True, config=None, tp=None) -> "LLM":
+        """Random-init weights (N(0, 0.02)) of a named architecture; the draft shares the target's embedding.
+        With ``tp`` (a :class:`~eagle4_b200.parallel.tp.TensorParallel`) every rank draws the same full weights and
+        keeps its shard."""
+        from eagle4_b200.parallel.sharding import shard_draft, shard_target
+
         tcfg_fn, dcfg_fn = NAMED[name]
         tcfg = tcfg_fn()
         dcfg = dcfg_fn(tcfg)
+        world, rank = (tp.world, tp.rank) if tp is not None else (1, 0)
         tw = weights.init_target(tcfg, device=device, dtype=dtype, seed=seed)
-        target = TargetModel(tcfg, tw, aux_layer_ids=dcfg.aux_layer_ids)
+        dw = weights.init_draft(dcfg, device=device, dtype=dtype, seed=seed + 1, embed=tw["embed"]) if draft else None
+        ltcfg, tw = shard_target(tcfg, tw, world, rank)
+        target = TargetModel(ltcfg, tw, aux_layer_ids=dcfg.aux_layer_ids, tp=tp)
         dm = None
         if draft:
-            dw = weights.init_draft(dcfg, device=device, dtype=dtype, seed=seed + 1, embed=tw["embed"])
-            dm = DraftModel(dcfg, dw)
+            ldcfg, dw = shard_draft(dcfg, dw, world, rank)
+            dm = DraftModel(ldcfg, dw, tp=tp)
         return cls(target, dm, tree=tree, max_batch=max_batch, max_len=max_len, config=config)
 
     def generate(self, prompt_ids: torch.Tensor, max_new_tokens: int, *, speculative: bool = True) -> torch.Tensor:

@@ -14,7 +14,10 @@
 // the last-arriving CTA of a tile in split order (no atomics on data, no spinning).
 //
 // Epilogues: plain bf16 store; residual add; SwiGLU over gate/up rows interleaved in 64-row blocks; squared ReLU;
-// fp32 store; and a per-tile (max, argmax) for the vocabulary-parallel greedy head.
+// fp32 store; a per-tile (max, argmax) for the vocabulary-parallel greedy head; and the tensor-parallel scatter:
+// each finished fp32 tile is stored straight into this rank's slot of every rank's receive buffer (peer memory over
+// NVLink), so the transfer of one tile overlaps the MMAs of the next, and every CTA ends with one release signal
+// per rank that the reduce kernel waits on.
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -28,7 +31,9 @@
 namespace e4 {
 namespace gemm {
 
-enum Epi : int { kPlain = 0, kResidual = 1, kSwiGLU = 2, kReLU2 = 3, kF32 = 4, kArgmax = 5 };
+enum Epi : int { kPlain = 0, kResidual = 1, kSwiGLU = 2, kReLU2 = 3, kF32 = 4, kArgmax = 5, kScatter = 6 };
+
+constexpr int kMaxRanks = 8;
 
 constexpr int kThreads = 192;
 constexpr int kTileM = 128;
@@ -53,6 +58,13 @@ struct Params {
   float* amax_val;   // [n_tiles][T] per-tile max (kArgmax)
   int* amax_idx;     // [n_tiles][T]
   int* err;
+  // kScatter: receive buffers recv[parity][src rank][row][ldy] of every rank, their arrival words
+  // arrive[parity][src rank], and this rank's call counter (its low bit is the parity of this call)
+  float* peer_recv[kMaxRanks];
+  unsigned* peer_arrive[kMaxRanks];
+  const unsigned* calls;
+  long slot_stride;  // floats per (parity, src rank) slot
+  int world, rank, row0;
 };
 
 // Stream-K partition: CTA c owns linear k-blocks [start(c), start(c+1)) of the (tile, k-block) space; a tile is
@@ -85,8 +97,21 @@ __device__ __forceinline__ Piece next_piece(const Params& p, long g, long end) {
 
 // Final epilogue of 16 token columns [j0, j0+16) held by this thread for weight row ``m`` of ``tile``.
 __device__ __forceinline__ void store_chunk(const Params& p, int tile, int m, int j0, const float* v, float* xchg,
-                                            int ep_tid) {
+                                            int ep_tid, unsigned parity) {
   const int n = tile * kTileM + m;
+  if (p.epi == kScatter) {
+    if (n >= p.N) return;
+    const size_t slot = (size_t(parity) * p.world + p.rank) * size_t(p.slot_stride);
+    for (int r = 0; r < p.world; ++r) {
+      float* dst = p.peer_recv[r] + slot + size_t(p.row0 + j0) * p.ldy + n;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if (j0 + i >= p.T) break;
+        dst[size_t(i) * p.ldy] = v[i];
+      }
+    }
+    return;
+  }
   if (p.epi == kSwiGLU) {
     // rows [0,64) are gate, [64,128) the matching up rows; output feature tile*64 + (m & 63)
     if (m >= 64) {
@@ -272,6 +297,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
   } else {
     // epilogue warps 2..5: TMEM lane quarter = warp % 4
     pdl_wait();
+    const unsigned parity = p.epi == kScatter ? (*reinterpret_cast<const volatile unsigned*>(p.calls) & 1u) : 0u;
     const int ep_tid = threadIdx.x - 64;
     const int quarter = warp & 3;
     const int m = quarter * 32 + lane;
@@ -290,7 +316,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
           float v[16];
           tmem_ld16(t_addr + j0, v);
           if (j0 + 16 >= p.nt) { tc_fence_before(); mbar_arrive(&acc_empty[acc]); }
-          store_chunk(p, tile, m, j0, v, xchg, ep_tid);
+          store_chunk(p, tile, m, j0, v, xchg, ep_tid, parity);
         }
       } else {
         // partial tile: store this piece, then the last piece to arrive reduces all pieces in order
@@ -323,7 +349,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
 #pragma unroll
               for (int i = 0; i < 16; ++i) v[i] += __ldcg(src + size_t(j0 + i) * kTileM + m);
             }
-            store_chunk(p, tile, m, j0, v, xchg, ep_tid);
+            store_chunk(p, tile, m, j0, v, xchg, ep_tid, parity);
           }
           if (ep_tid == 0) p.counters[tile] = 0;
         }
@@ -335,6 +361,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, tmem_cols);
+  }
+  if (p.epi == kScatter && threadIdx.x == 0) {
+    // every epilogue store of this CTA precedes the barrier above; publish them to all ranks at system scope
+    const unsigned parity = *reinterpret_cast<const volatile unsigned*>(p.calls) & 1u;
+    __threadfence_system();
+    for (int r = 0; r < p.world; ++r) {
+      unsigned* a = p.peer_arrive[r] + parity * kMaxRanks + p.rank;
+      asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a) : "memory");
+    }
   }
 }
 
@@ -418,10 +453,11 @@ Scratch& scratch(torch::Device dev) {
 
 torch::Tensor gemm_error_word(torch::Device dev) { return gemm::scratch(dev).err; }
 
-// Launch one GEMM over all T tokens (chunks of 256 tokens per launch).
-void gemm_launch(const torch::Tensor& x, const torch::Tensor& w, int epi, torch::Tensor y, torch::Tensor yf,
-                 const torch::Tensor& res, torch::Tensor amax_val, torch::Tensor amax_idx) {
-  using namespace gemm;
+namespace gemm {
+// Checks the operands and launches the GEMM in chunks of at most 256 tokens; ``chunk(p, t0)`` points the chunk's
+// outputs. Returns the number of CTAs launched over all chunks.
+template <class F>
+int launch_chunks(const torch::Tensor& x, const torch::Tensor& w, int epi, F chunk) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda(), "gemm: CUDA tensors expected");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm: bf16 operands expected");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "gemm: shape mismatch");
@@ -431,7 +467,7 @@ void gemm_launch(const torch::Tensor& x, const torch::Tensor& w, int epi, torch:
               "gemm: operands must be 16-byte aligned");
   const at::cuda::CUDAGuard guard(x.device());
   const int T = x.size(0), K = x.size(1), N = w.size(0);
-  if (T == 0) return;
+  if (T == 0) return 0;
   Scratch& sc = scratch(x.device());
   const int sms = num_sms();
   const int n_tiles = (N + kTileM - 1) / kTileM;
@@ -441,6 +477,12 @@ void gemm_launch(const torch::Tensor& x, const torch::Tensor& w, int epi, torch:
   const CUtensorMap& wmap = weight_map(w.data_ptr(), N, K, w.stride(0));
   auto stream = at::cuda::getCurrentCUDAStream();
   TORCH_CHECK(n_tiles <= sc.counters.numel(), "gemm: too many weight tiles");
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    attr_set = true;
+  }
+  int launched = 0;
   for (int t0 = 0; t0 < T; t0 += 256) {
     const int tc = std::min(256, T - t0);
     Params p{};
@@ -459,9 +501,26 @@ void gemm_launch(const torch::Tensor& x, const torch::Tensor& w, int epi, torch:
     p.ws = sc.ws.data_ptr<float>();
     p.counters = sc.counters.data_ptr<int>();
     p.err = sc.err.data_ptr<int>();
+    chunk(p, t0);
     const __nv_bfloat16* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()) + size_t(t0) * x.stride(0);
     CUtensorMap xmap = make_map(xp, tc, K, x.stride(0), p.nt);
-    auto has = [](const torch::Tensor& t) { return t.defined() && t.numel() > 0; };
+    const size_t smem = 1024 + size_t(p.stages) * stage_bytes + 64 + 16 * 64 * 4 + 1024;
+    C10_CUDA_CHECK(launch_pdl(gemm_kernel, grid, kThreads, smem, stream.stream(), wmap, xmap, p));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    launched += grid;
+  }
+  return launched;
+}
+}  // namespace gemm
+
+// Launch one GEMM over all T tokens (chunks of 256 tokens per launch).
+void gemm_launch(const torch::Tensor& x, const torch::Tensor& w, int epi, torch::Tensor y, torch::Tensor yf,
+                 const torch::Tensor& res, torch::Tensor amax_val, torch::Tensor amax_idx) {
+  using namespace gemm;
+  TORCH_CHECK(epi != kScatter, "gemm: the scatter epilogue has its own entry point");
+  const int n_tiles = (w.size(0) + kTileM - 1) / kTileM;
+  auto has = [](const torch::Tensor& t) { return t.defined() && t.numel() > 0; };
+  launch_chunks(x, w, epi, [&](Params& p, int t0) {
     if (has(y)) {
       p.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr()) + size_t(t0) * y.stride(0);
       p.ldy = y.stride(0);
@@ -479,15 +538,30 @@ void gemm_launch(const torch::Tensor& x, const torch::Tensor& w, int epi, torch:
       p.amax_val = amax_val.data_ptr<float>() + size_t(t0) * n_tiles;
       p.amax_idx = amax_idx.data_ptr<int>() + size_t(t0) * n_tiles;
     }
-    const size_t smem = 1024 + size_t(p.stages) * stage_bytes + 64 + 16 * 64 * 4 + 1024;
-    static bool attr_set = false;
-    if (!attr_set) {
-      cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-      attr_set = true;
+  });
+}
+
+// Tensor-parallel row-parallel GEMM: Y_partial = X . W^T (fp32) stored into slot [parity][rank] of every rank's
+// receive buffer (``recv`` / ``arrive``: int64 device addresses per rank, peers' from IPC mappings). Returns the
+// number of arrival signals each rank receives from this rank for this call (one per launched CTA).
+int64_t gemm_scatter(const torch::Tensor& x, const torch::Tensor& w, const std::vector<int64_t>& recv,
+                     const std::vector<int64_t>& arrive, int64_t calls, int64_t rank, int64_t slot_stride) {
+  using namespace gemm;
+  const int world = int(recv.size());
+  TORCH_CHECK(world >= 1 && world <= kMaxRanks && int(arrive.size()) == world, "gemm_scatter: 1..8 ranks");
+  TORCH_CHECK(x.size(0) * w.size(0) <= slot_stride, "gemm_scatter: rows x features exceed the receive slot");
+  return launch_chunks(x, w, kScatter, [&](Params& p, int t0) {
+    for (int r = 0; r < world; ++r) {
+      p.peer_recv[r] = reinterpret_cast<float*>(recv[r]);
+      p.peer_arrive[r] = reinterpret_cast<unsigned*>(arrive[r]);
     }
-    C10_CUDA_CHECK(launch_pdl(gemm_kernel, grid, kThreads, smem, stream.stream(), wmap, xmap, p));
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
-  }
+    p.calls = reinterpret_cast<const unsigned*>(calls);
+    p.slot_stride = slot_stride;
+    p.world = world;
+    p.rank = int(rank);
+    p.row0 = t0;
+    p.ldy = int(w.size(0));
+  });
 }
 
 }  // namespace e4

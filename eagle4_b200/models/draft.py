@@ -55,9 +55,11 @@ class _AttnShape:
 
 
 class DraftModel:
-    def __init__(self, cfg: DraftConfig, weights: Dict[str, torch.Tensor]):
+    def __init__(self, cfg: DraftConfig, weights: Dict[str, torch.Tensor], *, tp=None):
+        """``cfg`` / ``weights``: this rank's shard under tensor parallelism (``tp``; the head is replicated)."""
         self.cfg = cfg
         self.w = weights
+        self.tp = tp
         self.attn_shape = _AttnShape(cfg)
         self.device = weights["fc"].device
 
@@ -84,10 +86,15 @@ class DraftModel:
         q, _ = ops.qkv_prepare(qkv, self.attn_shape, pos, write_slot, cache.k, cache.v, None, None)
         o = ops.attention(q, cache.k, cache.v, cache.block_table, cache.page, req, ctx_start, ctx_len, extra,
                           n_extra, cfg.head_dim ** -0.5, max_keys)
-        residual = ops.linear_residual(o, w["o_proj"], hidden)
-        x = ops.rmsnorm(residual, w["post_attention_layernorm"], eps, False)
-        summed = ops.linear_residual(ops.linear_swiglu(x, w["gate_up"]), w["down"], residual)
-        normed = ops.rmsnorm(summed, w["norm"], eps, False)
+        if self.tp is not None:
+            residual, x = self.tp.row_linear(o, w["o_proj"], hidden, w["post_attention_layernorm"], eps)
+            summed, normed = self.tp.row_linear(ops.linear_swiglu(x, w["gate_up"]), w["down"], residual, w["norm"],
+                                                eps)
+        else:
+            residual = ops.linear_residual(o, w["o_proj"], hidden)
+            x = ops.rmsnorm(residual, w["post_attention_layernorm"], eps, False)
+            summed = ops.linear_residual(ops.linear_swiglu(x, w["gate_up"]), w["down"], residual)
+            normed = ops.rmsnorm(summed, w["norm"], eps, False)
         return normed, (normed if cfg.norm_output else summed)
 
     def candidates(self, normed: torch.Tensor, k: int, pos: Optional[torch.Tensor] = None

@@ -98,9 +98,13 @@ class Records:
 
 
 class TargetModel:
-    def __init__(self, cfg: TargetConfig, weights: Dict[str, torch.Tensor], *, aux_layer_ids=()):
+    def __init__(self, cfg: TargetConfig, weights: Dict[str, torch.Tensor], *, aux_layer_ids=(), tp=None):
+        """``cfg`` / ``weights`` are this rank's shard under tensor parallelism (``tp``: a
+        :class:`~eagle4_b200.parallel.tp.TensorParallel`; None on one GPU)."""
         self.cfg = cfg
         self.w = weights
+        self.tp = tp
+        self.lm_lo = int(weights["lm_head_lo"]) if "lm_head_lo" in weights else 0
         self.aux_layer_ids = tuple(aux_layer_ids)
         self.device = weights["embed"].device
         self.dtype = weights["embed"].dtype
@@ -112,6 +116,17 @@ class TargetModel:
                 self.attn_index[i] = len(self.attn_index)
             elif m in ("gdn", "mamba"):
                 self.rec_index[i] = len(self.rec_index)
+        # the norm applied to the residual stream after each sub-block (the next sub-block's input norm)
+        norms = [f"l{i}.{n}" for i, (m, f) in enumerate(cfg.layers) for n, on in (("norm1", m), ("norm2", f)) if on]
+        self.next_norm = dict(zip(norms, norms[1:] + ["norm"]))
+
+    def _row(self, y: torch.Tensor, w_out: torch.Tensor, h: torch.Tensor, after: str):
+        """Row-parallel output projection + residual, then the next sub-block's input norm: ``(h, x_next)``."""
+        nw = self.w[self.next_norm[after]]
+        if self.tp is not None:
+            return self.tp.row_linear(y, w_out, h, nw, self.cfg.rms_norm_eps, self.cfg.norm_offset)
+        h = ops.linear_residual(y, w_out, h)
+        return h, ops.rmsnorm(h, nw, self.cfg.rms_norm_eps, self.cfg.norm_offset)
 
     # ------------------------------------------------------------------ blocks
     def _attn(self, i: int, x: torch.Tensor, h: torch.Tensor, rb: RowBatch, cache: TargetCache) -> torch.Tensor:
@@ -122,7 +137,7 @@ class TargetModel:
                                   w.get(f"l{i}.q_norm"), w.get(f"l{i}.k_norm"))
         o = ops.attention(q, cache.k[li], cache.v[li], cache.block_table, cache.page, rb.req, rb.ctx_start,
                           rb.ctx_len, rb.extra, rb.n_extra, cfg.head_dim ** -0.5, rb.max_keys, gate)
-        return ops.linear_residual(o, w[f"l{i}.o_proj"], h)
+        return self._row(o, w[f"l{i}.o_proj"], h, f"l{i}.norm1")
 
     def _gdn(self, i: int, x: torch.Tensor, h: torch.Tensor, rb: RowBatch, cache: TargetCache,
              rec: Optional[Records]) -> torch.Tensor:
@@ -141,7 +156,7 @@ class TargetModel:
             rec.x_pre.append(proj)
             rec.conv_out.append(conv)
             rec.gate_a.append(None)
-        return ops.linear_residual(y, w[f"l{i}.out_proj"], h)
+        return self._row(y, w[f"l{i}.out_proj"], h, f"l{i}.norm1")
 
     def _mamba(self, i: int, x: torch.Tensor, h: torch.Tensor, rb: RowBatch, cache: TargetCache,
                rec: Optional[Records]) -> torch.Tensor:
@@ -164,7 +179,7 @@ class TargetModel:
             rec.gate_a.append(dt)
         group = cfg.mamba_inner // cfg.mamba_groups
         y = ops.gated_rmsnorm(y.reshape(y.shape[0], cfg.mamba_groups, group), z, w[f"l{i}.gnorm"], cfg.rms_norm_eps)
-        return ops.linear_residual(y, w[f"l{i}.out_proj"], h)
+        return self._row(y, w[f"l{i}.out_proj"], h, f"l{i}.norm1")
 
     def _mlp(self, i: int, x: torch.Tensor, h: torch.Tensor, kind: str) -> torch.Tensor:
         w = self.w
@@ -172,7 +187,7 @@ class TargetModel:
             a = ops.linear_swiglu(x, w[f"l{i}.gate_up"])
         else:
             a = ops.linear_relu2(x, w[f"l{i}.up"])
-        return ops.linear_residual(a, w[f"l{i}.down"], h)
+        return self._row(a, w[f"l{i}.down"], h, f"l{i}.norm2")
 
     # ------------------------------------------------------------------ forward
     def forward(self, rb: RowBatch, cache: TargetCache, rec: Optional[Records] = None):
@@ -180,29 +195,33 @@ class TargetModel:
         cfg, w = self.cfg, self.w
         eps, off = cfg.rms_norm_eps, cfg.norm_offset
         h = ops.embedding(rb.ids, w["embed"])
+        first = next(iter(self.next_norm))
+        x = ops.rmsnorm(h, w[first], eps, off)  # each sub-block returns the next one's normed input
         aux = []
         for i, (mixer, mlp) in enumerate(cfg.layers):
             if mixer is not None:
-                x = ops.rmsnorm(h, w[f"l{i}.norm1"], eps, off)
                 if mixer == "attn":
-                    h = self._attn(i, x, h, rb, cache)
+                    h, x = self._attn(i, x, h, rb, cache)
                 elif mixer == "gdn":
-                    h = self._gdn(i, x, h, rb, cache, rec)
+                    h, x = self._gdn(i, x, h, rb, cache, rec)
                 else:
-                    h = self._mamba(i, x, h, rb, cache, rec)
+                    h, x = self._mamba(i, x, h, rb, cache, rec)
             if mlp is not None:
-                x = ops.rmsnorm(h, w[f"l{i}.norm2"], eps, off)
-                h = self._mlp(i, x, h, mlp)
+                h, x = self._mlp(i, x, h, mlp)
             if i in self.aux_layer_ids:
                 aux.append(h)
-        out = ops.rmsnorm(h, w["norm"], eps, off)
-        return out, (torch.cat(aux, dim=-1) if aux else None)
+        return x, (torch.cat(aux, dim=-1) if aux else None)
 
     def greedy(self, hidden: torch.Tensor):
+        if self.tp is not None:
+            return self.tp.lm_head_argmax(hidden, self.w["lm_head"], self.lm_lo)
         return ops.lm_head_argmax(hidden, self.w["lm_head"])
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
-        return ops.logits(hidden, self.w["lm_head"])
+        local = ops.logits(hidden, self.w["lm_head"])
+        if self.tp is not None and self.tp.world > 1:
+            return self.tp.gather_logits(local, self.cfg.vocab_size)
+        return local
 
     # ------------------------------------------------------------------ commit
     def commit(self, cache: TargetCache, rec: Records, rows: torch.Tensor, n_rows: torch.Tensor,

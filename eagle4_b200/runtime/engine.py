@@ -449,7 +449,10 @@ class Engine:
                 self.lagged_scores = self.host_scores.tolist()
             if self._pending_timing is not None:
                 b_, w_, c_, ev, nsteps = self._pending_timing
-                self.policy.record(b_, w_, c_, ev[1].elapsed_us(ev[2]), nsteps, ev[0].elapsed_us(ev[1]))
+                verify_us, draft_us = ev[1].elapsed_us(ev[2]), ev[0].elapsed_us(ev[1])
+                if self.target.tp is not None:  # every rank must record the same costs to decide alike
+                    verify_us, draft_us = self.target.tp.max_over_ranks([verify_us, draft_us])
+                self.policy.record(b_, w_, c_, verify_us, nsteps, draft_us)
             got = []
             for b in range(bs):
                 c = int(self.host_cnt[b])
