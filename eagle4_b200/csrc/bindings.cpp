@@ -62,8 +62,8 @@ void tree_step(const torch::Tensor& probs, const torch::Tensor& toks, const torc
 std::vector<torch::Tensor> select_rows(const torch::Tensor& scores, const torch::Tensor& decay,
                                        const torch::Tensor& tokens, const torch::Tensor& parents, int64_t bs,
                                        int64_t n, int64_t K, int64_t count);
-int64_t gemm_scatter(const torch::Tensor& x, const torch::Tensor& w, const std::vector<int64_t>& recv,
-                     const std::vector<int64_t>& arrive, int64_t calls, int64_t rank, int64_t slot_stride);
+int64_t gemm_scatter(const torch::Tensor& x, const torch::Tensor& w, const std::vector<int64_t>& recv, int64_t calls,
+                     int64_t rank, int64_t slot_stride);
 int64_t sym_alloc(int64_t bytes, int64_t device);
 void sym_free(int64_t ptr);
 torch::Tensor sym_handle(int64_t ptr);
@@ -72,10 +72,10 @@ void sym_close(int64_t ptr);
 torch::Tensor sym_view(int64_t ptr, int64_t offset, int64_t numel, int64_t dtype_code, int64_t device);
 void tp_reduce(int64_t recv, int64_t world, int64_t slot_stride, const torch::Tensor& residual,
                const c10::optional<torch::Tensor>& norm_w, double eps, bool offset, torch::Tensor out_h,
-               c10::optional<torch::Tensor> out_x, int64_t channel, int64_t expect, torch::Tensor err);
+               c10::optional<torch::Tensor> out_x, int64_t channel, torch::Tensor err);
 void tp_argmax(const torch::Tensor& ids, const torch::Tensor& val, int64_t lo, const std::vector<int64_t>& xbufs,
-               const std::vector<int64_t>& arrives, int64_t rank, int64_t max_rows, int64_t channel,
-               torch::Tensor out_ids, torch::Tensor out_val, torch::Tensor err);
+               int64_t rank, int64_t max_rows, int64_t channel, torch::Tensor out_ids, torch::Tensor out_val,
+               torch::Tensor err);
 }  // namespace e4
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {

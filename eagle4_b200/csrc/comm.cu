@@ -3,13 +3,16 @@
 // (max, argmax) exchange.
 //
 // Each rank owns one buffer of the same layout; peers map it with cudaIpcOpenMemHandle, so a kernel stores into
-// (or loads from) another GPU's buffer through a plain pointer. A "channel" is a set of words in the buffer:
-//   arrive[2][kMaxRanks]   arrival counters per (parity, source rank); peers add to them with release semantics
-//   done                   CTAs of the local reduce that passed the wait (the last one resets the counters)
-//   calls                  local call counter; its low bit is the parity the next call uses
-// Consecutive calls alternate parity, so a rank may run one call ahead of a slower peer without overwriting data the
-// peer still reads: a rank cannot start call n + 2 before every rank has signalled call n + 1, which each does only
-// after finishing call n. Every wait is bounded (2 s) and records kErrTimeoutPeer instead of spinning forever.
+// another GPU's buffer through a plain pointer. Data travel as (value, tag) pairs written by single aligned 8-byte
+// stores: a pair lands whole, and the reader knows it is this call's when the tag equals the call counter + 1. So no
+// fence, flag or counter sits between the producer's stores and the consumer's loads, and a consumer starts on the
+// elements that have landed while the rest are in flight. A channel's words in the buffer:
+//   done    CTAs of the local reduce that have finished (the last one advances the call counter)
+//   calls   local call counter; its low bit selects the buffer half of the call, calls + 1 is the call's tag
+// Consecutive calls alternate halves, so a rank may run one call ahead of a slower peer without overwriting data the
+// peer still reads: a rank cannot finish call n + 1 (and so start writing call n + 2) before every rank has written
+// its call n + 1 data, which each does only after finishing call n. Every wait is bounded (2 s) and records
+// kErrTimeoutPeer instead of spinning forever.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -21,102 +24,119 @@ namespace comm {
 
 constexpr int kMaxRanks = 8;
 
+struct Peers {
+  uint2* xbuf[kMaxRanks];  // exchange area of every rank
+};
+
 struct Channel {
-  unsigned* arrive;  // local [2][kMaxRanks]
   unsigned* done;
   unsigned* calls;
 };
 
-E4_DEV unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+E4_DEV uint4 ld_volatile_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p) : "memory");
   return v;
 }
-E4_DEV void red_release_sys(unsigned* p, unsigned v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+E4_DEV uint2 ld_volatile_v2(const void* p) {
+  uint2 v;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
+E4_DEV void st_volatile_v2(void* p, unsigned a, unsigned b) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(a), "r"(b) : "memory");
 }
 
-// Threads [0, world) wait until arrive[parity][t] >= expect; false after the time limit.
-E4_DEV bool wait_arrivals(const Channel& ch, unsigned parity, int world, unsigned expect) {
-  bool ok = true;
-  if (threadIdx.x < world) {
-    const unsigned* a = ch.arrive + parity * kMaxRanks + threadIdx.x;
-    if (ld_acquire_sys(a) < expect) {
-      const uint64_t t0 = globaltimer();
-      while (ld_acquire_sys(a) < expect) {
-        if (globaltimer() - t0 > kWaitLimitNs) { ok = false; break; }
-      }
-    }
-  }
-  return __syncthreads_and(ok);
+// Re-reads two consecutive (value, tag) pairs until both carry ``tag``; false (v unchanged) after the time limit.
+E4_DEV bool settle(const uint2* p, unsigned tag, uint4& v) {
+  if (v.y == tag && v.w == tag) return true;
+  const uint64_t t0 = globaltimer();
+  do {
+    if (globaltimer() - t0 > kWaitLimitNs) return false;
+    v = ld_volatile_v4(p);
+  } while (v.y != tag || v.w != tag);
+  return true;
 }
 
 // One CTA per row: h = residual + sum over ranks (rank order) of the fp32 partials; x = rmsnorm(h) (optional).
-__global__ void __launch_bounds__(256) reduce_residual_norm_kernel(
-    const float* __restrict__ recv, int world, long slot_stride, int N, const __nv_bfloat16* __restrict__ residual,
-    int ldr, const __nv_bfloat16* __restrict__ norm_w, float eps, int offset, __nv_bfloat16* __restrict__ out_h,
-    __nv_bfloat16* __restrict__ out_x, Channel ch, unsigned expect, int* err) {
+// Each thread owns the 2-element groups c = threadIdx.x + i * kReduceThreads, i < G (N even, N <= 2 * G * 1024).
+// Its G x W pair loads are issued in batches of 8 before any is checked, so a batch costs one memory latency;
+// pairs still in flight are re-read until their tag matches. Sums run in rank order on every rank.
+constexpr int kReduceThreads = 1024;
+template <int W, int G>
+__global__ void __launch_bounds__(kReduceThreads) reduce_residual_norm_kernel(
+    const uint2* __restrict__ recv, long slot_stride, int N, const __nv_bfloat16* __restrict__ residual, int ldr,
+    const __nv_bfloat16* __restrict__ norm_w, float eps, int offset, __nv_bfloat16* __restrict__ out_h,
+    __nv_bfloat16* __restrict__ out_x, Channel ch, int* err) {
+  constexpr int kLoads = W * G, kBatch = 8;
   pdl_wait();
+  pdl_trigger();  // the next kernel's prologue may start; anything it reads of ours comes after its own wait
   const unsigned calls = *reinterpret_cast<volatile unsigned*>(ch.calls);
-  const unsigned parity = calls & 1u;
-  if (!wait_arrivals(ch, parity, world, expect) && threadIdx.x == 0) record_error(err, kErrTimeoutPeer);
-  pdl_trigger();
+  const unsigned half = calls & 1u, tag = calls + 1u;
   const int row = blockIdx.x;
-  __shared__ float red[32];
-  // each thread owns 4-element groups c = threadIdx.x + i * 256 (N % 4 == 0, N <= 8192)
-  constexpr int kMax = 8;
-  float4 acc[kMax];
+  __shared__ float red[kReduceThreads / 32];
+  const uint2* base = recv + size_t(half) * W * size_t(slot_stride) + size_t(row) * N;
+  float2 sum[G];
+#pragma unroll
+  for (int i = 0; i < G; ++i) sum[i] = make_float2(0.f, 0.f);
+  bool ok = true;
+#pragma unroll
+  for (int b0 = 0; b0 < kLoads; b0 += kBatch) {
+    uint4 v[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int i = (b0 + k) / W, r = (b0 + k) % W, c = threadIdx.x + i * kReduceThreads;
+      if (b0 + k < kLoads && c * 2 < N) v[k] = ld_volatile_v4(base + size_t(r) * slot_stride + 2 * c);
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int i = (b0 + k) / W, r = (b0 + k) % W, c = threadIdx.x + i * kReduceThreads;
+      if (b0 + k < kLoads && c * 2 < N) {
+        ok &= settle(base + size_t(r) * slot_stride + 2 * c, tag, v[k]);
+        sum[i].x += __uint_as_float(v[k].x);
+        sum[i].y += __uint_as_float(v[k].z);
+      }
+    }
+  }
+  float2 acc[G];
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMax; ++i) {
-    const int c = threadIdx.x + i * 256;
-    if (c * 4 >= N) break;
-    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int r = 0; r < world; ++r) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(
-          recv + (size_t(parity) * world + r) * size_t(slot_stride) + size_t(row) * N) + c);
-      s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
-    }
-    const __nv_bfloat162* rp = reinterpret_cast<const __nv_bfloat162*>(residual + size_t(row) * ldr) + 2 * c;
-    const float2 r0 = __bfloat1622float2(rp[0]), r1 = __bfloat1622float2(rp[1]);
+  for (int i = 0; i < G; ++i) {
+    const int c = threadIdx.x + i * kReduceThreads;
+    if (c * 2 >= N) break;
+    const float2 rv = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(residual + size_t(row) * ldr)[c]);
     // the residual stream is bf16: round h once, and normalise the rounded values
-    const __nv_bfloat162 h0 = __floats2bfloat162_rn(s.x + r0.x, s.y + r0.y);
-    const __nv_bfloat162 h1 = __floats2bfloat162_rn(s.z + r1.x, s.w + r1.y);
-    __nv_bfloat162* hp = reinterpret_cast<__nv_bfloat162*>(out_h + size_t(row) * N) + 2 * c;
-    hp[0] = h0;
-    hp[1] = h1;
-    const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
-    acc[i] = make_float4(f0.x, f0.y, f1.x, f1.y);
-    ss = fmaf(f0.x, f0.x, ss); ss = fmaf(f0.y, f0.y, ss); ss = fmaf(f1.x, f1.x, ss); ss = fmaf(f1.y, f1.y, ss);
+    const __nv_bfloat162 h = __floats2bfloat162_rn(sum[i].x + rv.x, sum[i].y + rv.y);
+    reinterpret_cast<__nv_bfloat162*>(out_h + size_t(row) * N)[c] = h;
+    acc[i] = __bfloat1622float2(h);
+    ss = fmaf(acc[i].x, acc[i].x, ss);
+    ss = fmaf(acc[i].y, acc[i].y, ss);
   }
+  if (!ok) record_error(err, kErrTimeoutPeer);
   if (norm_w != nullptr) {
     float tot = warp_sum(ss);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) red[warp] = tot;
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = tot;
     __syncthreads();
     tot = 0.f;
-    for (int i = 0; i < 8; ++i) tot += red[i];
+#pragma unroll
+    for (int w = 0; w < kReduceThreads / 32; ++w) tot += red[w];
     const float rs = rsqrtf(tot / N + eps);
 #pragma unroll
-    for (int i = 0; i < kMax; ++i) {
-      const int c = threadIdx.x + i * 256;
-      if (c * 4 >= N) break;
-      const __nv_bfloat162* wp = reinterpret_cast<const __nv_bfloat162*>(norm_w) + 2 * c;
-      const float2 w0 = __bfloat1622float2(wp[0]), w1 = __bfloat1622float2(wp[1]);
-      const float s0 = offset ? 1.f + w0.x : w0.x, s1 = offset ? 1.f + w0.y : w0.y;
-      const float s2 = offset ? 1.f + w1.x : w1.x, s3 = offset ? 1.f + w1.y : w1.y;
-      __nv_bfloat162* xp = reinterpret_cast<__nv_bfloat162*>(out_x + size_t(row) * N) + 2 * c;
-      xp[0] = __floats2bfloat162_rn(acc[i].x * rs * s0, acc[i].y * rs * s1);
-      xp[1] = __floats2bfloat162_rn(acc[i].z * rs * s2, acc[i].w * rs * s3);
+    for (int i = 0; i < G; ++i) {
+      const int c = threadIdx.x + i * kReduceThreads;
+      if (c * 2 >= N) break;
+      const float2 wv = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(norm_w)[c]);
+      const float s0 = offset ? 1.f + wv.x : wv.x, s1 = offset ? 1.f + wv.y : wv.y;
+      reinterpret_cast<__nv_bfloat162*>(out_x + size_t(row) * N)[c] =
+          __floats2bfloat162_rn(acc[i].x * rs * s0, acc[i].y * rs * s1);
     }
   }
-  // the last CTA past the wait resets this parity's counters and advances the call counter
+  // the last CTA to finish advances the call counter (every CTA read it above)
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    const unsigned old = atomicAdd(ch.done, 1u);
-    if (old == gridDim.x - 1) {
-      for (int r = 0; r < world; ++r) ch.arrive[parity * kMaxRanks + r] = 0u;
+    if (atomicAdd(ch.done, 1u) == gridDim.x - 1) {
       *ch.done = 0u;
       __threadfence();
       atomicAdd(ch.calls, 1u);
@@ -124,53 +144,54 @@ __global__ void __launch_bounds__(256) reduce_residual_norm_kernel(
   }
 }
 
-struct Peers {
-  float2* xbuf[kMaxRanks];   // exchange area of every rank: [2][kMaxRanks][max_rows] (value, index as float bits)
-  unsigned* arrive[kMaxRanks];  // channel arrive words of every rank
-};
-
-// One CTA: publish this rank's (max, argmax + lo) per row to every rank, wait for all ranks, pick the global best
-// (ties to the lower vocabulary id, as in the single-GPU head).
+// One CTA: publish this rank's (max, argmax + lo) per row to every rank as one tagged 16-byte pair of pairs
+// ((max, tag), (id, tag)), then pick the global best from every rank's entries (ties to the lower vocabulary id,
+// as in the single-GPU head). Exchange area of each rank: [2 halves][kMaxRanks][max_rows] entries of 16 bytes.
 __global__ void __launch_bounds__(256) argmax_exchange_kernel(
     const int64_t* __restrict__ ids, const float* __restrict__ val, int T, int lo, int world, int rank, int max_rows,
-    Peers peers, Channel ch, int64_t* __restrict__ out_ids, float* __restrict__ out_val, int* err) {
+    const __grid_constant__ Peers peers, Channel ch, int64_t* __restrict__ out_ids, float* __restrict__ out_val,
+    int* err) {
   pdl_wait();
-  const unsigned parity = *reinterpret_cast<volatile unsigned*>(ch.calls) & 1u;
-  const size_t mine = (size_t(parity) * kMaxRanks + rank) * max_rows;
-  for (int j = threadIdx.x; j < T; j += blockDim.x) {
-    const float2 e = make_float2(val[j], __int_as_float(int(ids[j]) + lo));
-    for (int r = 0; r < world; ++r) peers.xbuf[r][mine + j] = e;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    for (int r = 0; r < world; ++r) red_release_sys(peers.arrive[r] + parity * kMaxRanks + rank, 1u);
-  }
-  if (!wait_arrivals(ch, parity, world, 1u) && threadIdx.x == 0) record_error(err, kErrTimeoutPeer);
   pdl_trigger();
-  const float2* local = peers.xbuf[rank];
+  const unsigned calls = *reinterpret_cast<volatile unsigned*>(ch.calls);
+  const unsigned half = calls & 1u, tag = calls + 1u;
+  const size_t mine = (size_t(half) * kMaxRanks + rank) * max_rows;
   for (int j = threadIdx.x; j < T; j += blockDim.x) {
+    const unsigned v = __float_as_uint(val[j]), i = unsigned(int(ids[j]) + lo);
+    for (int r = 0; r < world; ++r) {
+      uint2* dst = peers.xbuf[r] + 2 * (mine + j);
+      st_volatile_v2(dst, v, tag);
+      st_volatile_v2(dst + 1, i, tag);
+    }
+  }
+  bool ok = true;
+  const uint2* local = peers.xbuf[rank];
+  for (int j = threadIdx.x; j < T; j += blockDim.x) {
+    uint4 e[kMaxRanks];
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < world) e[r] = ld_volatile_v4(local + 2 * ((size_t(half) * kMaxRanks + r) * max_rows + j));
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int r = 0; r < world; ++r) {
-      const float2 e = __ldcg(local + (size_t(parity) * kMaxRanks + r) * max_rows + j);
-      const int i = __float_as_int(e.y);
-      if (e.x > best || (e.x == best && i < bi)) { best = e.x; bi = i; }
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+      if (r >= world) break;
+      ok &= settle(local + 2 * ((size_t(half) * kMaxRanks + r) * max_rows + j), tag, e[r]);
+      const float x = __uint_as_float(e[r].x);
+      const int i = int(e[r].z);
+      if (x > best || (x == best && i < bi)) { best = x; bi = i; }
     }
     out_ids[j] = bi;
     out_val[j] = best;
   }
+  if (!ok) record_error(err, kErrTimeoutPeer);
   __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int r = 0; r < world; ++r) ch.arrive[parity * kMaxRanks + r] = 0u;
-    __threadfence();
-    atomicAdd(ch.calls, 1u);
-  }
+  if (threadIdx.x == 0) atomicAdd(ch.calls, 1u);
 }
 
 Channel channel(int64_t base) {
   unsigned* b = reinterpret_cast<unsigned*>(base);
-  return Channel{b, b + 2 * kMaxRanks, b + 2 * kMaxRanks + 1};
+  return Channel{b, b + 1};
 }
 
 }  // namespace comm
@@ -220,35 +241,51 @@ torch::Tensor sym_view(int64_t ptr, int64_t offset, int64_t numel, int64_t dtype
 // h, x = reduce(recv partials) + residual, rmsnorm(h) (x only when ``norm_w`` is given).
 void tp_reduce(int64_t recv, int64_t world, int64_t slot_stride, const torch::Tensor& residual,
                const c10::optional<torch::Tensor>& norm_w, double eps, bool offset, torch::Tensor out_h,
-               c10::optional<torch::Tensor> out_x, int64_t channel, int64_t expect, torch::Tensor err) {
+               c10::optional<torch::Tensor> out_x, int64_t channel, torch::Tensor err) {
   const at::cuda::CUDAGuard g(residual.device());
   const int T = residual.size(0), N = residual.size(1);
-  TORCH_CHECK(N % 4 == 0 && N <= 8192, "tp_reduce: features must be a multiple of 4, at most 8192");
+  TORCH_CHECK(N % 2 == 0 && N <= 8192, "tp_reduce: features must be even, at most 8192");
+  TORCH_CHECK(world == 1 || world == 2 || world == 4 || world == 8, "tp_reduce: 1, 2, 4 or 8 ranks");
   TORCH_CHECK(residual.stride(1) == 1 && out_h.is_contiguous(), "tp_reduce: row-major tensors expected");
   const bool norm = norm_w.has_value() && norm_w->defined();
   if (T == 0) return;
-  C10_CUDA_CHECK(launch_pdl(comm::reduce_residual_norm_kernel, T, 256, 0, at::cuda::getCurrentCUDAStream().stream(),
-                            reinterpret_cast<const float*>(recv), int(world), long(slot_stride), N,
-                            reinterpret_cast<const __nv_bfloat16*>(residual.data_ptr()), int(residual.stride(0)),
-                            norm ? reinterpret_cast<const __nv_bfloat16*>(norm_w->data_ptr()) : nullptr, float(eps),
-                            int(offset), reinterpret_cast<__nv_bfloat16*>(out_h.data_ptr()),
-                            norm ? reinterpret_cast<__nv_bfloat16*>(out_x->data_ptr()) : nullptr,
-                            comm::channel(channel), unsigned(expect), err.data_ptr<int>()));
+  auto launch = [&](auto kernel) {
+    C10_CUDA_CHECK(launch_pdl(kernel, T, comm::kReduceThreads, 0, at::cuda::getCurrentCUDAStream().stream(),
+                              reinterpret_cast<const uint2*>(recv), long(slot_stride), N,
+                              reinterpret_cast<const __nv_bfloat16*>(residual.data_ptr()), int(residual.stride(0)),
+                              norm ? reinterpret_cast<const __nv_bfloat16*>(norm_w->data_ptr()) : nullptr,
+                              float(eps), int(offset), reinterpret_cast<__nv_bfloat16*>(out_h.data_ptr()),
+                              norm ? reinterpret_cast<__nv_bfloat16*>(out_x->data_ptr()) : nullptr,
+                              comm::channel(channel), err.data_ptr<int>()));
+  };
+  const int groups = (N / 2 + comm::kReduceThreads - 1) / comm::kReduceThreads;  // 1..4
+  auto by_groups = [&](auto w_tag) {
+    constexpr int W = decltype(w_tag)::value;
+    switch (groups) {
+      case 1: launch(comm::reduce_residual_norm_kernel<W, 1>); break;
+      case 2: launch(comm::reduce_residual_norm_kernel<W, 2>); break;
+      case 3: launch(comm::reduce_residual_norm_kernel<W, 3>); break;
+      default: launch(comm::reduce_residual_norm_kernel<W, 4>); break;
+    }
+  };
+  switch (world) {
+    case 1: by_groups(std::integral_constant<int, 1>{}); break;
+    case 2: by_groups(std::integral_constant<int, 2>{}); break;
+    case 4: by_groups(std::integral_constant<int, 4>{}); break;
+    default: by_groups(std::integral_constant<int, 8>{}); break;
+  }
 }
 
 void tp_argmax(const torch::Tensor& ids, const torch::Tensor& val, int64_t lo, const std::vector<int64_t>& xbufs,
-               const std::vector<int64_t>& arrives, int64_t rank, int64_t max_rows, int64_t channel,
-               torch::Tensor out_ids, torch::Tensor out_val, torch::Tensor err) {
+               int64_t rank, int64_t max_rows, int64_t channel, torch::Tensor out_ids, torch::Tensor out_val,
+               torch::Tensor err) {
   const at::cuda::CUDAGuard g(ids.device());
   const int world = int(xbufs.size());
-  TORCH_CHECK(world <= comm::kMaxRanks && int(arrives.size()) == world, "tp_argmax: 1..8 ranks");
+  TORCH_CHECK(world <= comm::kMaxRanks, "tp_argmax: 1..8 ranks");
   const int T = ids.size(0);
   TORCH_CHECK(T <= max_rows, "tp_argmax: more rows than the exchange area holds");
   comm::Peers peers{};
-  for (int r = 0; r < world; ++r) {
-    peers.xbuf[r] = reinterpret_cast<float2*>(xbufs[r]);
-    peers.arrive[r] = reinterpret_cast<unsigned*>(arrives[r]);
-  }
+  for (int r = 0; r < world; ++r) peers.xbuf[r] = reinterpret_cast<uint2*>(xbufs[r]);
   C10_CUDA_CHECK(launch_pdl(comm::argmax_exchange_kernel, 1, 256, 0, at::cuda::getCurrentCUDAStream().stream(),
                             ids.data_ptr<int64_t>(), val.data_ptr<float>(), T, int(lo), world, int(rank),
                             int(max_rows), peers, comm::channel(channel), out_ids.data_ptr<int64_t>(),

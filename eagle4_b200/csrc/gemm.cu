@@ -16,8 +16,8 @@
 // Epilogues: plain bf16 store; residual add; SwiGLU over gate/up rows interleaved in 64-row blocks; squared ReLU;
 // fp32 store; a per-tile (max, argmax) for the vocabulary-parallel greedy head; and the tensor-parallel scatter:
 // each finished fp32 tile is stored straight into this rank's slot of every rank's receive buffer (peer memory over
-// NVLink), so the transfer of one tile overlaps the MMAs of the next, and every CTA ends with one release signal
-// per rank that the reduce kernel waits on.
+// NVLink) as (value, call tag) pairs, so the transfer of one tile overlaps the MMAs of the next and the reduce
+// kernel knows an element has landed when its tag matches.
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -58,12 +58,11 @@ struct Params {
   float* amax_val;   // [n_tiles][T] per-tile max (kArgmax)
   int* amax_idx;     // [n_tiles][T]
   int* err;
-  // kScatter: receive buffers recv[parity][src rank][row][ldy] of every rank, their arrival words
-  // arrive[parity][src rank], and this rank's call counter (its low bit is the parity of this call)
+  // kScatter: receive buffers recv[parity][src rank][row][ldy] of (value, tag) pairs on every rank, and this
+  // rank's call counter (its low bit is the parity of this call, calls + 1 the tag)
   float* peer_recv[kMaxRanks];
-  unsigned* peer_arrive[kMaxRanks];
   const unsigned* calls;
-  long slot_stride;  // floats per (parity, src rank) slot
+  long slot_stride;  // pairs per (parity, src rank) slot
   int world, rank, row0;
 };
 
@@ -100,14 +99,16 @@ __device__ __forceinline__ void store_chunk(const Params& p, int tile, int m, in
                                             int ep_tid, unsigned parity) {
   const int n = tile * kTileM + m;
   if (p.epi == kScatter) {
+    // (value, epoch) pairs: an aligned 8-byte store lands whole, so the reader needs no fence or counter
     if (n >= p.N) return;
-    const size_t slot = (size_t(parity) * p.world + p.rank) * size_t(p.slot_stride);
+    const size_t slot = (size_t(parity & 1u) * p.world + p.rank) * size_t(p.slot_stride);
     for (int r = 0; r < p.world; ++r) {
-      float* dst = p.peer_recv[r] + slot + size_t(p.row0 + j0) * p.ldy + n;
+      uint2* dst = reinterpret_cast<uint2*>(p.peer_recv[r]) + slot + size_t(p.row0 + j0) * p.ldy + n;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         if (j0 + i >= p.T) break;
-        dst[size_t(i) * p.ldy] = v[i];
+        asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(dst + size_t(i) * p.ldy),
+                     "r"(__float_as_uint(v[i])), "r"(parity + 1u) : "memory");
       }
     }
     return;
@@ -297,7 +298,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
   } else {
     // epilogue warps 2..5: TMEM lane quarter = warp % 4
     pdl_wait();
-    const unsigned parity = p.epi == kScatter ? (*reinterpret_cast<const volatile unsigned*>(p.calls) & 1u) : 0u;
+    // kScatter: the call counter (its low bit picks the buffer half, calls + 1 tags the data)
+    const unsigned parity = p.epi == kScatter ? *reinterpret_cast<const volatile unsigned*>(p.calls) : 0u;
     const int ep_tid = threadIdx.x - 64;
     const int quarter = warp & 3;
     const int m = quarter * 32 + lane;
@@ -361,15 +363,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, tmem_cols);
-  }
-  if (p.epi == kScatter && threadIdx.x == 0) {
-    // every epilogue store of this CTA precedes the barrier above; publish them to all ranks at system scope
-    const unsigned parity = *reinterpret_cast<const volatile unsigned*>(p.calls) & 1u;
-    __threadfence_system();
-    for (int r = 0; r < p.world; ++r) {
-      unsigned* a = p.peer_arrive[r] + parity * kMaxRanks + p.rank;
-      asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a) : "memory");
-    }
   }
 }
 
@@ -541,19 +534,18 @@ void gemm_launch(const torch::Tensor& x, const torch::Tensor& w, int epi, torch:
   });
 }
 
-// Tensor-parallel row-parallel GEMM: Y_partial = X . W^T (fp32) stored into slot [parity][rank] of every rank's
-// receive buffer (``recv`` / ``arrive``: int64 device addresses per rank, peers' from IPC mappings). Returns the
-// number of arrival signals each rank receives from this rank for this call (one per launched CTA).
-int64_t gemm_scatter(const torch::Tensor& x, const torch::Tensor& w, const std::vector<int64_t>& recv,
-                     const std::vector<int64_t>& arrive, int64_t calls, int64_t rank, int64_t slot_stride) {
+// Tensor-parallel row-parallel GEMM: Y_partial = X . W^T (fp32, tagged with the call) stored into slot
+// [parity][rank] of every rank's receive buffer (``recv``: int64 device addresses per rank, peers' from IPC
+// mappings). Returns the number of CTAs launched.
+int64_t gemm_scatter(const torch::Tensor& x, const torch::Tensor& w, const std::vector<int64_t>& recv, int64_t calls,
+                     int64_t rank, int64_t slot_stride) {
   using namespace gemm;
   const int world = int(recv.size());
-  TORCH_CHECK(world >= 1 && world <= kMaxRanks && int(arrive.size()) == world, "gemm_scatter: 1..8 ranks");
+  TORCH_CHECK(world >= 1 && world <= kMaxRanks, "gemm_scatter: 1..8 ranks");
   TORCH_CHECK(x.size(0) * w.size(0) <= slot_stride, "gemm_scatter: rows x features exceed the receive slot");
   return launch_chunks(x, w, kScatter, [&](Params& p, int t0) {
     for (int r = 0; r < world; ++r) {
       p.peer_recv[r] = reinterpret_cast<float*>(recv[r]);
-      p.peer_arrive[r] = reinterpret_cast<unsigned*>(arrive[r]);
     }
     p.calls = reinterpret_cast<const unsigned*>(calls);
     p.slot_stride = slot_stride;

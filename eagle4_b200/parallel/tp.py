@@ -2,8 +2,8 @@
 
 ``backend="fused"`` (the B200 path): a row-parallel linear is ONE GEMM launch whose epilogue stores each finished
 fp32 tile straight into this rank's slot of every rank's receive buffer over NVLink (peer pointers from CUDA IPC)
-and signals each rank when its CTA is done; a second kernel waits for every rank's signals, sums the partials in rank
-order, adds the residual and applies the next RMSNorm. The greedy head's vocabulary-parallel (max, argmax) is
+as (value, call tag) pairs; a second kernel sums each element over the ranks in rank order as soon as its pairs
+carry this call's tag, adds the residual and applies the next RMSNorm. The greedy head's vocabulary-parallel (max, argmax) is
 exchanged the same way by one small kernel. Both kernels are captured in the engine's CUDA graphs.
 
 ``backend="torch"``: the same math through ``torch.distributed.all_reduce`` / ``all_gather`` (NCCL on GPUs, gloo on
@@ -44,7 +44,9 @@ class TensorParallel:
         self.max_rows, self.max_cols = max_rows, max_cols
         self.base = 0
         self.peers: List[int] = []
-        if self.backend == "fused":
+        # one rank may still run the fused kernels (signalling only itself): measures their cost without NVLink
+        self.force_fused = self.world == 1 and os.environ.get("E4_TP_FORCE_FUSED") == "1"
+        if self.backend == "fused" and (self.world > 1 or self.force_fused):
             self._open()
 
     # ------------------------------------------------------------------ symmetric buffer
@@ -53,10 +55,10 @@ class TensorParallel:
 
         C = native._C
         dev = self.device.index
-        self.slot = self.max_rows * self.max_cols
-        recv_bytes = 2 * self.world * self.slot * 4
+        self.slot = self.max_rows * self.max_cols  # (value, tag) pairs of 8 bytes
+        recv_bytes = 2 * self.world * self.slot * 8
         self.xbuf_off = _RECV + recv_bytes
-        total = self.xbuf_off + 2 * MAX_RANKS * self.max_rows * 8
+        total = self.xbuf_off + 2 * MAX_RANKS * self.max_rows * 16
         self.base = C.sym_alloc(total, dev)
         handle = C.sym_handle(self.base)
         handles: List[Optional[torch.Tensor]] = [None] * self.world
@@ -84,7 +86,7 @@ class TensorParallel:
                    norm_w: Optional[torch.Tensor] = None, eps: float = 1e-6, offset: bool = False
                    ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
         """``h = residual + all_reduce(x @ w^T)``; ``x_next = rmsnorm(h, norm_w)`` when a norm weight is given."""
-        if self.world == 1:
+        if self.world == 1 and not self.force_fused:
             h = ops.linear_residual(x, w, residual)
             return h, (ops.rmsnorm(h, norm_w, eps, offset) if norm_w is not None else None)
         if self.backend == "torch":
@@ -100,10 +102,9 @@ class TensorParallel:
         C = _native()
         for r0 in range(0, t, self.max_rows):
             r1 = min(t, r0 + self.max_rows)
-            expect = C.gemm_scatter(x[r0:r1], w, [p + _RECV for p in self.peers], [p + _CH0 for p in self.peers],
-                                    self.base + _CH0 + 4 * (2 * MAX_RANKS + 1), self.rank, self.slot)
+            C.gemm_scatter(x[r0:r1], w, [p + _RECV for p in self.peers], self.base + _CH0 + 4, self.rank, self.slot)
             C.tp_reduce(self.base + _RECV, self.world, self.slot, residual[r0:r1], norm_w, eps, offset, h[r0:r1],
-                        xn[r0:r1] if xn is not None else None, self.base + _CH0, expect, self.err)
+                        xn[r0:r1] if xn is not None else None, self.base + _CH0, self.err)
         return h, xn
 
     def lm_head_argmax(self, x: torch.Tensor, w_shard: torch.Tensor, lo: int) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -125,9 +126,8 @@ class TensorParallel:
         C = _native()
         for r0 in range(0, t, self.max_rows):
             r1 = min(t, r0 + self.max_rows)
-            C.tp_argmax(ids[r0:r1], val[r0:r1], int(lo), [p + self.xbuf_off for p in self.peers],
-                        [p + _CH1 for p in self.peers], self.rank, self.max_rows, self.base + _CH1, out_ids[r0:r1],
-                        out_val[r0:r1], self.err)
+            C.tp_argmax(ids[r0:r1], val[r0:r1], int(lo), [p + self.xbuf_off for p in self.peers], self.rank,
+                        self.max_rows, self.base + _CH1, out_ids[r0:r1], out_val[r0:r1], self.err)
         return out_ids, out_val
 
     def gather_logits(self, local: torch.Tensor, vocab: int) -> torch.Tensor:
