@@ -41,6 +41,7 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--only", nargs="*", default=None, help="kernel names to run")
+    ap.add_argument("--nk", type=int, nargs="*", default=None, help="extra plain GEMM shapes as N K pairs")
     args = ap.parse_args()
     from eagle4_b200.ops import native
 
@@ -52,6 +53,8 @@ def main() -> None:
         "mlp_gate_up": (2 * F, H), "mlp_down": (H, F), "lm_head": (V, H), "draft_gate_up": (32768, H),
         "draft_qkv": (15360, 2 * H),
     }
+    for i in range(0, len(args.nk or []), 2):
+        shapes[f"gemm_{args.nk[i]}x{args.nk[i + 1]}"] = (args.nk[i], args.nk[i + 1])
     rows = []
     for name, (n, k) in shapes.items():
         if args.only is not None and name not in args.only:

@@ -64,6 +64,7 @@ std::vector<torch::Tensor> select_rows(const torch::Tensor& scores, const torch:
                                        int64_t n, int64_t K, int64_t count);
 int64_t gemm_scatter(const torch::Tensor& x, const torch::Tensor& w, const std::vector<int64_t>& recv, int64_t calls,
                      int64_t rank, int64_t slot_stride);
+torch::Tensor gemm_traced(const torch::Tensor& x, const torch::Tensor& w, int64_t epi);
 int64_t sym_alloc(int64_t bytes, int64_t device);
 void sym_free(int64_t ptr);
 torch::Tensor sym_handle(int64_t ptr);
@@ -83,6 +84,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("error_word", [](int64_t dev) { return e4::gemm_error_word(torch::Device(torch::kCUDA, dev)); });
   m.def("gemm", &e4::gemm_launch, "tcgen05 skinny GEMM with fused epilogue");
   m.def("gemm_scatter", &e4::gemm_scatter, "row-parallel GEMM storing fp32 partials into every rank's buffer");
+  m.def("gemm_traced", &e4::gemm_traced, "one GEMM with per-CTA timestamps (tuning)");
   m.def("sym_alloc", &e4::sym_alloc);
   m.def("sym_free", &e4::sym_free);
   m.def("sym_handle", &e4::sym_handle);

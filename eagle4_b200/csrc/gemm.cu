@@ -10,8 +10,9 @@
 //
 // A work unit is (weight tile, K split). The split count depends only on (N, K) and the token tile only on T, and
 // every output element's reduction order is fixed by the split boundaries, so a row's result is the same whatever
-// other rows share the launch (plain decode and tree verify give identical logits). Split partials are reduced by
-// the last-arriving CTA of a tile in split order (no atomics on data, no spinning).
+// other rows share the launch (plain decode and tree verify give identical logits). A split tile is finished by the
+// CTA holding its first k-block (its range ends there, so that piece is done last): it adds the other pieces in
+// split order after a bounded wait on a per-tile count the other pieces bump with release adds.
 //
 // Epilogues: plain bf16 store; residual add; SwiGLU over gate/up rows interleaved in 64-row blocks; squared ReLU;
 // fp32 store; a per-tile (max, argmax) for the vocabulary-parallel greedy head; and the tensor-parallel scatter:
@@ -23,6 +24,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -64,7 +66,13 @@ struct Params {
   const unsigned* calls;
   long slot_stride;  // pairs per (parity, src rank) slot
   int world, rank, row0;
+  unsigned long long* trace;  // optional [grid][8] globaltimer stamps (tuning runs only)
 };
+
+// trace slots: 0 start, 1 setup done, 2 first stage landed (MMA), 3 last MMA issued, 4 first accumulator ready
+// (epilogue), 5 epilogue done, 6 end
+#define E4_STAMP(p, k) \
+  do { if ((p).trace) (p).trace[size_t(blockIdx.x) * 8 + (k)] = globaltimer(); } while (0)
 
 // Stream-K partition: CTA c owns linear k-blocks [start(c), start(c+1)) of the (tile, k-block) space; a tile is
 // split into "pieces" where CTA ranges cut it. The cut points depend only on (N, K, grid), never on T.
@@ -189,6 +197,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
   // Setup and the first weight loads happen before waiting for the previous kernel (weights never change); every
   // access to activations (X loads, residual reads, output stores, workspace) comes after pdl_wait().
   pdl_trigger();
+  if (threadIdx.x == 0) E4_STAMP(p, 0);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // carve: [stages x (W tile | X tile)] 1024-aligned, then barriers, TMEM handle, exchange buffer
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -228,6 +237,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
   tc_fence_after();
   const uint32_t tmem_base = *tmem_handle;
   bool ok = true;
+  if (threadIdx.x == 0) E4_STAMP(p, 1);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -279,6 +289,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
         const uint32_t d_tmem = tmem_base + acc * tmem_cols_per_acc;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase)) { record_error(p.err, kErrTimeoutMma); ok = false; break; }
+          if (local == 0 && kb == kb0) E4_STAMP(p, 2);
           tc_fence_after();
           const uint32_t sa = smem_u32(tiles + stage * stage_bytes);
           const uint64_t adesc = sdesc_sw128(sa);
@@ -294,6 +305,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
         if (!ok) break;
         umma_commit(&acc_full[acc]);
       }
+      E4_STAMP(p, 3);
     }
   } else {
     // epilogue warps 2..5: TMEM lane quarter = warp % 4
@@ -311,6 +323,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&acc_full[acc], acc_phase)) { record_error(p.err, kErrTimeoutEpilogue); break; }
+      if (local == 0 && ep_tid == 0) E4_STAMP(p, 4);
       tc_fence_after();
       const uint32_t t_addr = tmem_base + (uint32_t(quarter * 32) << 16) + acc * tmem_cols_per_acc;
       if (pc.kb0 == 0 && pc.kb1 == p.kb_total) {
@@ -321,49 +334,87 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
           store_chunk(p, tile, m, j0, v, xchg, ep_tid, parity);
         }
       } else {
-        // partial tile: store this piece, then the last piece to arrive reduces all pieces in order
+        // Partial tile. The CTA holding the tile's first k-block (kb0 == 0) owns it: that piece ends the CTA's range,
+        // so it finishes last. Every other piece stores its partial and counts itself in with a release add (no
+        // waiting); the owner keeps its own accumulator in registers, waits for the count, adds the other pieces in
+        // piece order and stores the tile.
         const long t0 = long(tile) * p.kb_total;
         const int first_cta = sk_owner(p, t0);
         const int pieces = sk_owner(p, t0 + p.kb_total - 1) - first_cta + 1;
-        float* part = p.ws + size_t(ws_slot(p, blockIdx.x, tile)) * p.nt * kTileM;
-        for (int j0 = 0; j0 < p.nt; j0 += 16) {
-          float v[16];
-          tmem_ld16(t_addr + j0, v);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) part[size_t(j0 + i) * kTileM + m] = v[i];
-        }
-        tc_fence_before();
-        mbar_arrive(&acc_empty[acc]);
-        named_bar(1, 128);
-        if (ep_tid == 0) {
-          int old;
-          asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.counters + tile) : "memory");
-          *flag = (old == pieces - 1);
-        }
-        named_bar(1, 128);
-        if (*flag) {
+        if (pc.kb0 != 0) {
+          // partial slot layout [row m][token j]: each thread writes (and the owner reads) 64 contiguous bytes
+          float* part = p.ws + size_t(ws_slot(p, blockIdx.x, tile)) * p.nt * kTileM;
           for (int j0 = 0; j0 < p.nt; j0 += 16) {
             float v[16];
+            tmem_ld16(t_addr + j0, v);
+            float4* dst = reinterpret_cast<float4*>(part + size_t(m) * p.nt + j0);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = 0.f;
-            for (int q = 0; q < pieces; ++q) {
-              const float* src = p.ws + size_t(ws_slot(p, first_cta + q, tile)) * p.nt * kTileM;
+            for (int u = 0; u < 4; ++u) dst[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+          }
+          tc_fence_before();
+          mbar_arrive(&acc_empty[acc]);
+          named_bar(1, 128);  // every thread's partial stores precede the release below
+          if (ep_tid == 0)
+            asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.counters + tile) : "memory");
+        } else {
+          if (ep_tid == 0) {
+            const int* cnt = p.counters + tile;
+            int seen;
+            asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(seen) : "l"(cnt) : "memory");
+            if (seen < pieces - 1) {
+              const uint64_t w0 = globaltimer();
+              while (seen < pieces - 1) {
+                if (globaltimer() - w0 > kWaitLimitNs) { record_error(p.err, kErrTimeoutEpilogue); break; }
+                asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(seen) : "l"(cnt) : "memory");
+              }
+            }
+            E4_STAMP(p, 7);
+          }
+          named_bar(1, 128);
+          for (int j0 = 0; j0 < p.nt; j0 += 16) {
+            float v[16];
+            tmem_ld16(t_addr + j0, v);
+            if (j0 + 16 >= p.nt) { tc_fence_before(); mbar_arrive(&acc_empty[acc]); }
+            // pieces 1.. in order, four at a time: their loads are all issued before the first is summed
+            for (int q0 = 1; q0 < pieces; q0 += 4) {
+              float4 buf[4][4];
 #pragma unroll
-              for (int i = 0; i < 16; ++i) v[i] += __ldcg(src + size_t(j0 + i) * kTileM + m);
+              for (int qq = 0; qq < 4; ++qq) {
+                if (q0 + qq < pieces) {
+                  const float4* src = reinterpret_cast<const float4*>(
+                      p.ws + size_t(ws_slot(p, first_cta + q0 + qq, tile)) * p.nt * kTileM + size_t(m) * p.nt + j0);
+#pragma unroll
+                  for (int u = 0; u < 4; ++u) buf[qq][u] = __ldcg(src + u);
+                }
+              }
+#pragma unroll
+              for (int qq = 0; qq < 4; ++qq) {
+                if (q0 + qq < pieces) {
+#pragma unroll
+                  for (int u = 0; u < 4; ++u) {
+                    v[4 * u] += buf[qq][u].x;
+                    v[4 * u + 1] += buf[qq][u].y;
+                    v[4 * u + 2] += buf[qq][u].z;
+                    v[4 * u + 3] += buf[qq][u].w;
+                  }
+                }
+              }
             }
             store_chunk(p, tile, m, j0, v, xchg, ep_tid, parity);
           }
           if (ep_tid == 0) p.counters[tile] = 0;
+          named_bar(1, 128);
         }
-        named_bar(1, 128);
       }
     }
   }
+  if (threadIdx.x == 64) E4_STAMP(p, 5);
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, tmem_cols);
   }
+  if (threadIdx.x == 0) E4_STAMP(p, 6);
 }
 
 // ------------------------------------------------------------------------------------------------- host side
@@ -424,6 +475,16 @@ int num_sms() {
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   }
+  return n;
+}
+
+// Pipeline depth cap (stages of one W + X tile). E4_GEMM_STAGES overrides it for tuning runs.
+int max_stages() {
+  static int n = [] {
+    const char* e = std::getenv("E4_GEMM_STAGES");
+    const int v = e ? std::atoi(e) : 10;
+    return v >= 2 && v <= 16 ? v : 10;
+  }();
   return n;
 }
 
@@ -488,7 +549,7 @@ int launch_chunks(const torch::Tensor& x, const torch::Tensor& w, int epi, F chu
     p.total = total;
     p.epi = epi;
     const int stage_bytes = kWTileBytes + p.nt * kTileK * 2;
-    p.stages = std::min(10, (200 * 1024) / stage_bytes);
+    p.stages = std::min(max_stages(), (200 * 1024) / stage_bytes);
     const size_t ws_need = size_t(2) * grid * p.nt * kTileM;
     if (size_t(sc.ws.numel()) < ws_need) sc.ws = torch::empty({int64_t(ws_need)}, sc.ws.options());
     p.ws = sc.ws.data_ptr<float>();
@@ -532,6 +593,24 @@ void gemm_launch(const torch::Tensor& x, const torch::Tensor& w, int epi, torch:
       p.amax_idx = amax_idx.data_ptr<int>() + size_t(t0) * n_tiles;
     }
   });
+}
+
+// One plain GEMM with per-CTA globaltimer stamps: returns [CTAs][8] (slots documented at E4_STAMP). Tuning only.
+torch::Tensor gemm_traced(const torch::Tensor& x, const torch::Tensor& w, int64_t epi) {
+  using namespace gemm;
+  auto y = torch::empty({x.size(0), w.size(0)}, x.options());
+  auto yf = torch::empty({x.size(0), w.size(0)}, x.options().dtype(torch::kFloat32));
+  const int grid = std::min<long>(num_sms(), long((w.size(0) + kTileM - 1) / kTileM) * ((x.size(1) + kTileK - 1) / kTileK));
+  auto tr = torch::zeros({grid, 8}, x.options().dtype(torch::kInt64));
+  launch_chunks(x, w, int(epi), [&](Params& p, int) {
+    p.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+    p.yf = yf.data_ptr<float>();
+    p.ldy = int(w.size(0));
+    p.res = reinterpret_cast<const __nv_bfloat16*>(y.data_ptr());
+    p.ldr = int(w.size(0));
+    p.trace = reinterpret_cast<unsigned long long*>(tr.data_ptr<int64_t>());
+  });
+  return tr;
 }
 
 // Tensor-parallel row-parallel GEMM: Y_partial = X . W^T (fp32, tagged with the call) stored into slot
