@@ -9,6 +9,7 @@ returns the generated ids on the host.
 
 from __future__ import annotations
 
+import dataclasses
 from dataclasses import dataclass
 from typing import Optional
 
@@ -25,6 +26,12 @@ NAMED = {
     "qwen3.8-27b": (configs.qwen38_27b, configs.qwen38_draft),
     "nemotron-h-8b": (configs.nemotron_h_8b, lambda t: configs.generic_draft(t, heads=32, kv=8, head_dim=128)),
     "llama-3.1-8b": (configs.llama31_8b, configs.eagle3_llama_draft),
+    # production widths, two layers, tied embeddings: kernel profiling at real shapes within a few GB
+    "qwen3.8-27b-2l": (lambda: configs.profile_slice(configs.qwen38_27b()),
+                       lambda t: dataclasses.replace(configs.qwen38_draft(t), aux_layer_ids=(0, 1, 1))),
+    "nemotron-h-8b-2l": (lambda: configs.profile_slice(configs.nemotron_h_8b(), ("mamba", "attn")),
+                         lambda t: dataclasses.replace(configs.generic_draft(t, heads=32, kv=8, head_dim=128),
+                                                       aux_layer_ids=(0, 1, 1))),
 }
 
 
@@ -59,7 +66,8 @@ class LLM:
         dcfg = dcfg_fn(tcfg)
         world, rank = (tp.world, tp.rank) if tp is not None else (1, 0)
         tw = weights.init_target(tcfg, device=device, dtype=dtype, seed=seed)
-        dw = weights.init_draft(dcfg, device=device, dtype=dtype, seed=seed + 1, embed=tw["embed"]) if draft else None
+        dw = weights.init_draft(dcfg, device=device, dtype=dtype, seed=seed + 1, embed=tw["embed"],
+                                lm_head=tw["lm_head"]) if draft else None
         ltcfg, tw = shard_target(tcfg, tw, world, rank)
         target = TargetModel(ltcfg, tw, aux_layer_ids=dcfg.aux_layer_ids, tp=tp)
         dm = None

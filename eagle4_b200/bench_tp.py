@@ -79,6 +79,15 @@ def main() -> None:
             res["roofline_us"] = round(max(weight_us, link_us), 3)
             res["fused_frac_of_roofline"] = round(res["roofline_us"] / res["fused_us"], 3)
             rows.append(res)
+    # the greedy head: a vocabulary shard's GEMM + argmax, then the cross-rank (max, argmax) exchange
+    lm = (torch.randn(248320 // max(world, 8), H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    for t in args.tokens:
+        x = torch.randn(t, H, generator=g, device=dev).to(torch.bfloat16)
+        res = {"op": "greedy_head", "shape": f"{lm.shape[0]}x{H}", "tokens": t, "world": world}
+        res["local_us"] = graph_us(lambda: ops.lm_head_argmax(x, lm), args.calls)
+        res["fused_us"] = graph_us(lambda: fused.lm_head_argmax(x, lm, 0), args.calls)
+        res["nccl_us"] = graph_us(lambda: nccl.lm_head_argmax(x, lm, 0), args.calls)
+        rows.append(res)
     torch.cuda.synchronize()
     fused.close()
     if rank == 0:

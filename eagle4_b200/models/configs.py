@@ -229,6 +229,15 @@ def qwen38_27b() -> TargetConfig:
     )
 
 
+def profile_slice(target: TargetConfig, mixers=("gdn", "attn")) -> TargetConfig:
+    """A few layers of a target at its real widths (one per mixer kind, tied embeddings): every per-layer kernel runs
+    at the production shapes while the weights stay a few GB (for profiler captures)."""
+    import dataclasses
+
+    layers = [next(l for l in target.layers if l[0] == m) for m in mixers]
+    return dataclasses.replace(target, layers=layers, tie_embeddings=True)
+
+
 def qwen38_draft(target: TargetConfig) -> DraftConfig:
     """The released EAGLE-4 draft shape for Qwen3.8-27B (H=5120, 40x128 heads, FFN 16384, window 4096)."""
     return DraftConfig(

@@ -197,7 +197,7 @@ class TargetModel:
         h = ops.embedding(rb.ids, w["embed"])
         first = next(iter(self.next_norm))
         x = ops.rmsnorm(h, w[first], eps, off)  # each sub-block returns the next one's normed input
-        aux = []
+        saved: Dict[int, torch.Tensor] = {}
         for i, (mixer, mlp) in enumerate(cfg.layers):
             if mixer is not None:
                 if mixer == "attn":
@@ -209,7 +209,8 @@ class TargetModel:
             if mlp is not None:
                 h, x = self._mlp(i, x, h, mlp)
             if i in self.aux_layer_ids:
-                aux.append(h)
+                saved[i] = h
+        aux = [saved[i] for i in self.aux_layer_ids if i in saved]
         return x, (torch.cat(aux, dim=-1) if aux else None)
 
     def greedy(self, hidden: torch.Tensor):
