@@ -131,15 +131,15 @@ __global__ void sigmoid_gate_kernel(const __nv_bfloat16* __restrict__ o, const _
 
 // per (row, group): rmsnorm over D then * silu(z)
 __global__ void gated_rmsnorm_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ z, int ldz,
-                                     const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y, int G, int D,
-                                     float eps) {
+                                     const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y, int T, int G,
+                                     int D, float eps) {
   pdl_wait();
   pdl_trigger();
   // one warp per (row, group)
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int r = warp / G, g = warp % G;
-  if (r >= int(gridDim.y)) return;
+  if (r >= T) return;
   const __nv_bfloat16* orow = o + (size_t(r) * G + g) * D;
   float ss = 0.f;
   for (int i = lane; i < D; i += 32) {
@@ -353,9 +353,9 @@ torch::Tensor gated_rmsnorm(const torch::Tensor& o, const torch::Tensor& z, cons
   auto y = torch::empty({T, G * D}, o.options());
   const int warps = T * G;
   if (T) {
-    dim3 grid((warps * 32 + 255) / 256, T);
-    C10_CUDA_CHECK(launch_pdl(gated_rmsnorm_kernel, grid, 256, 0, at::cuda::getCurrentCUDAStream().stream(), CBF16(oc), CBF16(z), z.stride(0),
-                                                                             CBF16(w), BF16(y), G, D, float(eps)));
+    C10_CUDA_CHECK(launch_pdl(gated_rmsnorm_kernel, (warps * 32 + 255) / 256, 256, 0,
+                              at::cuda::getCurrentCUDAStream().stream(), CBF16(oc), CBF16(z), z.stride(0), CBF16(w),
+                              BF16(y), T, G, D, float(eps)));
   }
   return y;
 }

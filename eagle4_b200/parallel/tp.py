@@ -110,7 +110,7 @@ class TensorParallel:
     def lm_head_argmax(self, x: torch.Tensor, w_shard: torch.Tensor, lo: int) -> Tuple[torch.Tensor, torch.Tensor]:
         """Greedy ids over the whole vocabulary from this rank's row range ``[lo, lo + rows)`` of the LM head."""
         ids, val = ops.lm_head_argmax(x, w_shard)
-        if self.world == 1:
+        if self.world == 1 and not self.force_fused:
             return ids + lo, val
         if self.backend == "torch":
             both = torch.stack([val.double(), (ids + lo).double()], dim=1)
