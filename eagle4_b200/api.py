@@ -44,18 +44,21 @@ class TreeSpec:
 
 class LLM:
     def __init__(self, target: TargetModel, draft: Optional[DraftModel], *, tree: TreeSpec = TreeSpec(),
-                 max_batch: int = 1, max_len: int = 4096, page: int = 16, config=None):
+                 max_batch: int = 1, max_len: int = 4096, page: int = 16, config=None, temperature: float = 0.0,
+                 seed: int = 0):
         """``config``: a ``HarnessConfig``, or the ``--speculative-algorithm-config`` JSON text (inline or a path);
-        None is the static tree of ``tree``."""
+        None is the static tree of ``tree``. ``temperature > 0`` samples (sampled trees with tree rejection)."""
         if isinstance(config, str):
             config = parse_harness_config(config)
         self.target, self.draft, self.tree = target, draft, tree
         self.engine = Engine(target, draft, max_reqs=max_batch, max_len=max_len, page=page, steps=tree.steps,
-                             top_k=tree.top_k, verify_tokens=tree.draft_tokens, config=config)
+                             top_k=tree.top_k, verify_tokens=tree.draft_tokens, config=config,
+                             temperature=temperature, seed=seed)
 
     @classmethod
     def synthetic(cls, name: str, *, device="cuda", dtype=torch.bfloat16, seed: int = 0, tree: TreeSpec = TreeSpec(),
-                  max_batch: int = 1, max_len: int = 4096, draft: bool = True, config=None, tp=None) -> "LLM":
+                  max_batch: int = 1, max_len: int = 4096, draft: bool = True, config=None, tp=None,
+                  temperature: float = 0.0, sample_seed: int = 0) -> "LLM":
         """Random-init weights (N(0, 0.02)) of a named architecture; the draft shares the target's embedding.
         With ``tp`` (a :class:`~eagle4_b200.parallel.tp.TensorParallel`) every rank draws the same full weights and
         keeps its shard."""
@@ -74,7 +77,8 @@ class LLM:
         if draft:
             ldcfg, dw = shard_draft(dcfg, dw, world, rank)
             dm = DraftModel(ldcfg, dw, tp=tp)
-        return cls(target, dm, tree=tree, max_batch=max_batch, max_len=max_len, config=config)
+        return cls(target, dm, tree=tree, max_batch=max_batch, max_len=max_len, config=config,
+                   temperature=temperature, seed=sample_seed)
 
     def generate(self, prompt_ids: torch.Tensor, max_new_tokens: int, *, speculative: bool = True) -> torch.Tensor:
         """``prompt_ids [B, P]`` int64 on the host -> generated ids ``[B, max_new_tokens]`` on the host."""

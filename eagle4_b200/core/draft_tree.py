@@ -94,6 +94,8 @@ class DraftTree:
             raise ValueError(f"delta_slots {sorted(slots)} outside 0..{shape.max_depth - 1}")
         self.delta_slots = slots
         self.shape, self.max_bs, self.max_verify = shape, max_bs, max_verify
+        self.keep_draw_order = False  # sampled trees keep the root's children in draw order
+        self.last_nodes: Optional[torch.Tensor] = None  # node of every row of the last verify selection (-1: root)
         f32, i64 = torch.float32, torch.int64
         dev = torch.device(device)
         self.device = dev
@@ -140,8 +142,11 @@ class DraftTree:
 
     def begin_reference(self, bs: int) -> None:
         k = self.shape.top_k
-        probs, order = torch.sort(self.root_probs[:bs], dim=-1, descending=True, stable=True)
-        toks = torch.gather(self.root_tokens[:bs], 1, order)
+        if self.keep_draw_order:  # sampled trees: node order must stay the draw order
+            probs, toks = self.root_probs[:bs].clone(), self.root_tokens[:bs].clone()
+        else:
+            probs, order = torch.sort(self.root_probs[:bs], dim=-1, descending=True, stable=True)
+            toks = torch.gather(self.root_tokens[:bs], 1, order)
         self.scores[:bs, :k] = probs
         self.tokens[:bs, :k] = toks
         self.front_scores[:bs] = probs
@@ -152,8 +157,9 @@ class DraftTree:
         self.best_prev[:bs, 0] = ROOT_SCORE
         self.best[:bs].zero_()
         self.best[:bs, 0] = ROOT_SCORE
-        self.best[:bs, 1: 1 + k] = probs
-        self.layer_top[:bs] = probs
+        ranked = torch.sort(probs, dim=-1, descending=True).values if self.keep_draw_order else probs
+        self.best[:bs, 1: 1 + k] = ranked
+        self.layer_top[:bs] = ranked
 
     def set_step_slots(self, bs: int, step: int, slots: torch.Tensor) -> None:
         self.ancestors[:bs, :, step - 1] = slots.to(torch.int32)
@@ -249,6 +255,7 @@ class DraftTree:
         hit = index[:, None, :] == pnode[:, :, None]
         prow = torch.where(hit.any(-1), hit.int().argmax(-1) + 1, torch.zeros_like(pnode))
         root = prow.new_full((bs, 1), -1)
+        self.last_nodes = torch.cat([index.new_full((bs, 1), -1), index], dim=1)
         return toks, torch.cat([root, prow], dim=1).int()
 
 

@@ -96,3 +96,98 @@ def reject_children(target_probs: torch.Tensor, proposals: ChildProposals, unifo
     draw = torch.searchsorted(cdf.contiguous(), (final_uniforms.double() * cdf[:, -1])[:, None].contiguous(),
                               right=True).flatten().clamp_max(vocab - 1)
     return RejectionResult(torch.where(chosen < 0, draw, out), chosen)
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# The GPU sampler's definitions in float64: the same random streams (SplitMix64 keyed by seed, round, stream, index),
+# Gumbel-top-k children and the tree walk over verify rows (``eagle4_b200/csrc/sampled.cu``).
+
+_M64 = (1 << 64) - 1
+
+
+def _mix64(z):
+    import numpy as np
+
+    z = (z + np.uint64(0x9E3779B97F4A7C15)) & np.uint64(_M64)
+    z = ((z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)) & np.uint64(_M64)
+    z = ((z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)) & np.uint64(_M64)
+    return z ^ (z >> np.uint64(31))
+
+
+def stream_uniforms(seed: int, round_: int, stream: int, index) -> torch.Tensor:
+    """Uniforms in (0, 1) of the GPU sampler's streams: 24 high bits of the mixed key, centred (float64)."""
+    import numpy as np
+
+    with np.errstate(over="ignore"):
+        idx = np.asarray(index, dtype=np.uint64)
+        h = _mix64(np.uint64(seed & _M64) ^ np.uint64(((round_ & 0xFFFFFFFF) << 32) | (stream & 0xFFFFFFFF)))
+        h = _mix64(h ^ idx)
+        u = ((h >> np.uint64(40)).astype(np.float64) + 0.5) / 16777216.0
+    return torch.from_numpy(np.asarray(u, dtype=np.float64))
+
+
+def sample_children_reference(logits: torch.Tensor, cand_ids: torch.Tensor, k: int, temperature: float, seed: int,
+                              round_: int, stream: int):
+    """``(q [R, C], child probs [R, k], child ids [R, k], child slots [R, k])``: Gumbel-top-k of ``log q`` with the
+    GPU sampler's uniforms (row ``r``, candidate ``c`` uses index ``r * C + c``)."""
+    r, c = logits.shape
+    q = torch.softmax(logits.double() / temperature, dim=-1)
+    u = stream_uniforms(seed, round_, stream, range(r * c)).view(r, c).to(q.device)
+    keys = torch.where(q > 0, torch.log(q) - torch.log(-torch.log(u)), torch.full_like(q, float("-inf")))
+    slots = torch.sort(-keys, dim=-1, stable=True).indices[:, :k]
+    return q, q.gather(1, slots), cand_ids.gather(1, slots), slots
+
+
+def sampled_walk_reference(logits: torch.Tensor, temperature: float, row_parent: torch.Tensor,
+                           row_node: torch.Tensor, q_store: torch.Tensor, q_ids: torch.Tensor,
+                           node_slot: torch.Tensor, top_k: int, seed: int, round_: int, stream: int):
+    """The tree rejection walk of the GPU sampler in float64: ``(accepted rows [bs, n], counts [bs], final token
+    [bs])``. Children of a row are tried in node order (= draw order) while they are the first draws; the final token
+    is drawn from the normalised residual in vocabulary order."""
+    bs, n = row_parent.shape
+    v = logits.shape[1]
+    acc = torch.zeros(bs, n, dtype=torch.int64)
+    cnt = torch.zeros(bs, dtype=torch.int32)
+    bonus = torch.zeros(bs, dtype=torch.int64)
+    for b in range(bs):
+        row, path = 0, [0]
+        while True:
+            p = torch.softmax(logits[b * n + row].double() / temperature, dim=-1)
+            nd = int(row_node[b, row])
+            slot = 0 if nd < 0 else 1 + nd
+            ids = q_ids[b, slot].long()
+            q = q_store[b, slot].double().clone()
+            resid = p.clone()
+            moved = False
+            expect = 0
+            for j in range(row + 1, n):
+                if int(row_parent[b, j]) != row:
+                    continue
+                cn = int(row_node[b, j])
+                draw = cn if cn < top_k else (cn - top_k) % top_k
+                if draw != expect:
+                    break
+                expect += 1
+                s = int(node_slot[b, cn])
+                qsum = float(q.sum())
+                m = float(resid.sum())
+                qy = float(q[s]) / qsum if qsum > 0 else 0.0
+                u = float(stream_uniforms(seed, round_, stream, [b * n + j])[0])
+                if q[s] > 0 and u * m * qy < float(resid[ids[s]]):
+                    path.append(j)
+                    row = j
+                    moved = True
+                    break
+                scale = m / qsum if qsum > 0 else 0.0
+                resid[ids] = (resid[ids] - scale * q).clamp_min(0)
+                q[s] = 0
+            if moved:
+                continue
+            cdf = resid.cumsum(0)
+            target = float(stream_uniforms(seed, round_, stream + 1, [b])[0]) * float(cdf[-1])
+            tok = int(torch.searchsorted(cdf, torch.tensor([target], dtype=cdf.dtype), right=True)[0].clamp_max(v - 1))
+            acc[b, : len(path)] = torch.tensor(path)
+            cnt[b] = len(path)
+            bonus[b] = tok
+            break
+    return acc, cnt, bonus

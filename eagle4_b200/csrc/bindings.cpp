@@ -64,6 +64,17 @@ std::vector<torch::Tensor> select_rows(const torch::Tensor& scores, const torch:
                                        int64_t n, int64_t K, int64_t count);
 int64_t gemm_scatter(const torch::Tensor& x, const torch::Tensor& w, const std::vector<int64_t>& recv, int64_t calls,
                      int64_t rank, int64_t slot_stride);
+std::vector<torch::Tensor> sample_children(const torch::Tensor& logits, const torch::Tensor& cand_ids, int64_t K,
+                                           double temperature, int64_t seed, const torch::Tensor& round_ctr,
+                                           int64_t stream, const c10::optional<torch::Tensor>& front_nodes,
+                                           int64_t lanes, torch::Tensor q_store, torch::Tensor q_ids,
+                                           torch::Tensor node_slot, int64_t child_base);
+std::vector<torch::Tensor> sampled_accept(const torch::Tensor& logits, double temperature,
+                                          const torch::Tensor& row_parent, const torch::Tensor& row_tok,
+                                          const torch::Tensor& row_node, const torch::Tensor& q_store,
+                                          const torch::Tensor& q_ids, const torch::Tensor& node_slot, int64_t K,
+                                          int64_t seed, const torch::Tensor& round_ctr, int64_t stream);
+void advance_round(torch::Tensor round_ctr);
 torch::Tensor gemm_traced(const torch::Tensor& x, const torch::Tensor& w, int64_t epi);
 int64_t sym_alloc(int64_t bytes, int64_t device);
 void sym_free(int64_t ptr);
@@ -84,6 +95,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("error_word", [](int64_t dev) { return e4::gemm_error_word(torch::Device(torch::kCUDA, dev)); });
   m.def("gemm", &e4::gemm_launch, "tcgen05 skinny GEMM with fused epilogue");
   m.def("gemm_scatter", &e4::gemm_scatter, "row-parallel GEMM storing fp32 partials into every rank's buffer");
+  m.def("sample_children", &e4::sample_children, "Gumbel-top-k children from candidate logits");
+  m.def("sampled_accept", &e4::sampled_accept, "recursive tree rejection over the verify rows");
+  m.def("advance_round", &e4::advance_round);
   m.def("gemm_traced", &e4::gemm_traced, "one GEMM with per-CTA timestamps (tuning)");
   m.def("sym_alloc", &e4::sym_alloc);
   m.def("sym_free", &e4::sym_free);

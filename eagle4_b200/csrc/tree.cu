@@ -463,7 +463,7 @@ __global__ void tree_step_kernel(const float* __restrict__ probs, const int64_t*
 __global__ void select_rows_kernel(const float* __restrict__ scores, const float* __restrict__ decay,
                                    const int64_t* __restrict__ tokens, const int64_t* __restrict__ parents, int n,
                                    int cap, int pcap, int K, int count, int64_t* __restrict__ out_tok,
-                                   int* __restrict__ out_parent) {
+                                   int* __restrict__ out_parent, int64_t* __restrict__ out_node) {
   pdl_wait();
   pdl_trigger();
   const int b = blockIdx.x;
@@ -489,6 +489,7 @@ __global__ void select_rows_kernel(const float* __restrict__ scores, const float
   for (int r = threadIdx.x; r < count; r += blockDim.x) {
     const int node = row_node[r];
     out_tok[size_t(b) * count + r] = tokens[size_t(b) * cap + node];
+    out_node[size_t(b) * (count + 1) + r + 1] = node;
     // parent node: depth 1 nodes hang off the root; depth >= 2 nodes read their frontier column
     int pnode = -1;
     if (node >= K) {
@@ -499,7 +500,10 @@ __global__ void select_rows_kernel(const float* __restrict__ scores, const float
     }
     out_parent[size_t(b) * (count + 1) + r + 1] = pnode >= 0 ? sel_pos[pnode] : 0;
   }
-  if (threadIdx.x == 0) out_parent[size_t(b) * (count + 1)] = -1;
+  if (threadIdx.x == 0) {
+    out_parent[size_t(b) * (count + 1)] = -1;
+    out_node[size_t(b) * (count + 1)] = -1;
+  }
 }
 
 }  // namespace
@@ -566,11 +570,12 @@ std::vector<torch::Tensor> select_rows(const torch::Tensor& scores, const torch:
   TORCH_CHECK(n <= 1024 && count <= 63);
   auto ot = torch::empty({bs, count}, tokens.options());
   auto op = torch::empty({bs, count + 1}, tokens.options().dtype(torch::kInt32));
-  C10_CUDA_CHECK(launch_pdl(select_rows_kernel, bs, 128, 0, at::cuda::getCurrentCUDAStream().stream(), 
+  auto on = torch::empty({bs, count + 1}, tokens.options());
+  C10_CUDA_CHECK(launch_pdl(select_rows_kernel, bs, 128, 0, at::cuda::getCurrentCUDAStream().stream(),
       scores.data_ptr<float>(), decay.data_ptr<float>(), tokens.data_ptr<int64_t>(), parents.data_ptr<int64_t>(), n,
-      scores.size(1), parents.size(1), K, count, ot.data_ptr<int64_t>(), op.data_ptr<int>()));
+      scores.size(1), parents.size(1), K, count, ot.data_ptr<int64_t>(), op.data_ptr<int>(), on.data_ptr<int64_t>()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return {ot, op};
+  return {ot, op, on};
 }
 
 }  // namespace e4

@@ -166,3 +166,44 @@ def topk_rows(scores, k: int):
 def accept_greedy(target_ids, tokens, parent_rows, n_rows):
     fn = _nat().accept_greedy if _cuda(tokens) else ref.accept_greedy
     return fn(target_ids, tokens, parent_rows, n_rows)
+
+
+# sampled trees ------------------------------------------------------------------------------------------------------
+def sample_children(logits, cand_ids, k, temperature, seed, round_ctr, stream, front_nodes, lanes, q_store, q_ids,
+                    node_slot, child_base):
+    """K children per row drawn without replacement (Gumbel-top-k) from ``softmax(logits / T)`` over the row's
+    candidates; writes the rows' q and candidate ids to the q store and the children's slots to ``node_slot``.
+    Returns ``(child probs [R, K] fp32, child ids [R, K] int64)``."""
+    if _cuda(logits):
+        return _nat().sample_children(logits, cand_ids, k, temperature, seed, round_ctr, stream, front_nodes, lanes,
+                                      q_store, q_ids, node_slot, child_base)
+    from eagle4_b200.core.sampled_tree import sample_children_reference
+
+    r, c = logits.shape
+    q, cp, ct, slots = sample_children_reference(logits, cand_ids, k, temperature, seed, int(round_ctr[0]), stream)
+    b = torch.arange(r) // lanes
+    lane = torch.arange(r) % lanes
+    qrow = torch.zeros(r, dtype=torch.long) if front_nodes is None else 1 + front_nodes.reshape(-1).long()
+    q_store[b, qrow] = q.to(q_store.dtype)
+    q_ids[b, qrow] = cand_ids.to(q_ids.dtype)
+    node_slot[b[:, None], child_base + lane[:, None] * k + torch.arange(k)[None, :]] = slots.to(node_slot.dtype)
+    return cp.float(), ct.long()
+
+
+def sampled_accept(logits, temperature, row_parent, row_tok, row_node, q_store, q_ids, node_slot, k, seed, round_ctr,
+                   stream):
+    """Recursive tree rejection over the verify rows: ``(accepted rows [bs, n], counts [bs], final token [bs])``."""
+    if _cuda(logits):
+        return _nat().sampled_accept(logits, temperature, row_parent, row_tok, row_node, q_store, q_ids, node_slot, k,
+                                     seed, round_ctr, stream)
+    from eagle4_b200.core.sampled_tree import sampled_walk_reference
+
+    return sampled_walk_reference(logits, temperature, row_parent, row_node, q_store, q_ids, node_slot, k, seed,
+                                  int(round_ctr[0]), stream)
+
+
+def advance_round(round_ctr):
+    if _cuda(round_ctr):
+        _nat().advance_round(round_ctr)
+    else:
+        round_ctr += 1

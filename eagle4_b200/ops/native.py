@@ -262,3 +262,22 @@ def full_head_topk(h, lm_head, k: int):
 def accept_greedy(target_ids, tokens, parent_rows, n_rows):
     acc, cnt, bonus = _C.accept_greedy(target_ids, tokens, parent_rows, n_rows)
     return acc, cnt, bonus
+
+
+# sampled trees -----------------------------------------------------------------------------------------------------
+def sample_children(logits, cand_ids, k, temperature, seed, round_ctr, stream, front_nodes, lanes, q_store, q_ids,
+                    node_slot, child_base):
+    return _C.sample_children(logits.float().contiguous(), cand_ids.long().contiguous(), int(k), float(temperature),
+                              int(seed), round_ctr, int(stream), front_nodes, int(lanes), q_store, q_ids, node_slot,
+                              int(child_base))
+
+
+def sampled_accept(logits, temperature, row_parent, row_tok, row_node, q_store, q_ids, node_slot, k, seed, round_ctr,
+                   stream):
+    return _C.sampled_accept(logits, float(temperature), row_parent.int().contiguous(), row_tok.long().contiguous(),
+                             row_node.long().contiguous(), q_store, q_ids, node_slot, int(k), int(seed), round_ctr,
+                             int(stream))
+
+
+def advance_round(round_ctr):
+    _C.advance_round(round_ctr)

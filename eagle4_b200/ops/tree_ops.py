@@ -33,5 +33,7 @@ def tree_step(tree, bs: int, step: int, probs, tokens, hidden, *, deltas: bool) 
 def select_rows(tree, bs: int, depth: int, count: int):
     n = tree.shape.num_nodes(depth)
     count = min(count, n)
-    toks, prow = _C().select_rows(tree.scores, tree.decay, tree.tokens, tree.parents, bs, n, tree.shape.top_k, count)
+    toks, prow, nodes = _C().select_rows(tree.scores, tree.decay, tree.tokens, tree.parents, bs, n, tree.shape.top_k,
+                                         count)
+    tree.last_nodes = nodes
     return toks, prow

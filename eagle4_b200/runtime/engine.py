@@ -111,11 +111,18 @@ class _Stamp:
         return (later.t - self.t) * 1e6
 
 
+SAMPLED_STREAM = 0x10000  # random stream of the tree walk's coins (draft steps use streams 0..steps-1)
+
+
 class Engine:
     def __init__(self, target: TargetModel, draft: Optional[DraftModel], *, max_reqs: int, max_len: int,
                  page: int = 16, steps: int = 4, top_k: int = 2, verify_tokens: int = 8, use_graphs: bool = True,
-                 config: Optional[HarnessConfig] = None):
+                 config: Optional[HarnessConfig] = None, temperature: float = 0.0, seed: int = 0):
+        """``temperature > 0`` samples: draft children are drawn without replacement from the draft's candidate
+        distribution and verified by recursive tree rejection, so the output follows the target's distribution at
+        that temperature (``temperature == 0``: greedy, equal to plain greedy decoding)."""
         self.target, self.draft = target, draft
+        self.temperature, self.seed = float(temperature), int(seed)
         self.device = target.device
         self.dtype = target.dtype
         self.page = page
@@ -141,6 +148,18 @@ class Engine:
                                   max_verify=min(budget, shape.work_cap), delta_slots=slots)
         dev, n = self.device, verify_tokens
         i64, i32 = torch.int64, torch.int32
+        self.round_ctr = torch.zeros(1, dtype=i32, device=dev)
+        # plain sampling reads one (empty) candidate set per request
+        self.plain_q = torch.zeros(max_reqs, 1, 1, dtype=torch.float32, device=dev)
+        self.plain_ids = torch.zeros(max_reqs, 1, 1, dtype=i32, device=dev)
+        self.plain_slot = torch.zeros(max_reqs, 1, dtype=i32, device=dev)
+        if self.sampled and draft is not None:
+            cap = self.tree.shape.capacity
+            self.cands = draft.cfg.num_candidates if draft.cfg.low_rank else min(256, draft.cfg.draft_vocab_size)
+            self.q_store = torch.zeros(max_reqs, 1 + cap, self.cands, dtype=torch.float32, device=dev)
+            self.q_ids = torch.zeros(max_reqs, 1 + cap, self.cands, dtype=i32, device=dev)
+            self.node_slot = torch.zeros(max_reqs, cap, dtype=i32, device=dev)
+            self.tree.keep_draw_order = True
         # device state, one row per batch position
         self.L = torch.zeros(max_reqs, dtype=i64, device=dev)
         self.root = torch.zeros(max_reqs, dtype=i64, device=dev)
@@ -166,6 +185,20 @@ class Engine:
             self.last_depth = self.last_width = 0
 
     # ------------------------------------------------------------------ helpers
+    @property
+    def sampled(self) -> bool:
+        return self.temperature > 0
+
+    def _sample(self, normed: torch.Tensor, front_nodes: Optional[torch.Tensor], lanes: int, stream: int,
+                child_base: int):
+        """Sampled children of the rows of ``normed`` (see ``ops.sample_children``)."""
+        ids, logit = self.draft.candidate_logits(normed)
+        if logit.shape[1] > self.cands:  # full-vocabulary head: its top candidates are the proposal's support
+            logit, pick = ops.topk_rows(logit, self.cands)
+            ids = ids.gather(1, pick)
+        return ops.sample_children(logit, ids, self.top_k, self.temperature, self.seed, self.round_ctr, stream,
+                                   front_nodes, lanes, self.q_store, self.q_ids, self.node_slot, child_base)
+
     def _slots(self, slot: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         """Physical KV slots of positions ``pos`` in the block-table rows ``slot`` (broadcasting)."""
         pos = pos.long()
@@ -188,7 +221,17 @@ class Engine:
                       extra=torch.zeros(n, 1, dtype=torch.int32, device=self.device), n_extra=self._i32(n, 0),
                       parent=(pos - 1).int(), state_slot=self._i32(n, slot), scan=True)
         out, aux = self.target.forward(rb, self.tcache)
-        first, _ = self.target.greedy(out[-1:])
+        if self.sampled:
+            dev = self.device
+            _, _, first = ops.sampled_accept(self.target.logits(out[-1:]), self.temperature,
+                                             torch.full((1, 1), -1, dtype=torch.int32, device=dev),
+                                             torch.zeros(1, 1, dtype=torch.int64, device=dev),
+                                             torch.full((1, 1), -1, dtype=torch.int64, device=dev), self.plain_q[:1],
+                                             self.plain_ids[:1], self.plain_slot[:1], 1, self.seed, self.round_ctr,
+                                             SAMPLED_STREAM + 2)
+            ops.advance_round(self.round_ctr)
+        else:
+            first, _ = self.target.greedy(out[-1:])
         self.L[b] = n
         self.root[b] = first[0]
         self.out_tok[b, 0] = first[0]
@@ -225,7 +268,16 @@ class Engine:
                       max_keys=self.max_len)
         rec = Records()
         out, _ = self.target.forward(rb, self.tcache, rec)
-        ids, _ = self.target.greedy(out)
+        if self.sampled:  # plain sampling: the walk with no children draws from p
+            dev = self.device
+            _, _, ids = ops.sampled_accept(self.target.logits(out), self.temperature,
+                                           torch.full((bs, 1), -1, dtype=torch.int32, device=dev), self.root[:bs, None],
+                                           torch.full((bs, 1), -1, dtype=torch.int64, device=dev), self.plain_q,
+                                           self.plain_ids, self.plain_slot, 1, self.seed, self.round_ctr,
+                                           SAMPLED_STREAM)
+            ops.advance_round(self.round_ctr)
+        else:
+            ids, _ = self.target.greedy(out)
         rows = torch.arange(bs, dtype=torch.int32, device=self.device).view(bs, 1)
         self.target.commit(self.tcache, rec, rows, torch.ones(bs, dtype=torch.int32, device=self.device), sl,
                            slots, slots)
@@ -253,7 +305,11 @@ class Engine:
                                    torch.zeros(t, dtype=torch.int32, device=dev), self.dcache,
                                    max_keys=self.max_len)
         last = torch.arange(bs, device=dev) * n + (cnt - 1).clamp(min=0)
-        probs, toks = draft.candidates(normed.index_select(0, last), self.top_k, pos.reshape(-1).index_select(0, last))
+        if self.sampled:
+            probs, toks = self._sample(normed.index_select(0, last), None, 1, 0, 0)
+        else:
+            probs, toks = draft.candidates(normed.index_select(0, last), self.top_k,
+                                           pos.reshape(-1).index_select(0, last))
         self.tree.stage_root(bs, probs, toks, nh.index_select(0, last))
 
     def _phase_begin(self, bs: int) -> None:
@@ -279,7 +335,10 @@ class Engine:
         n_extra = torch.full((bs * k,), s, dtype=torch.int32, device=dev)
         normed, nh = draft.forward(tree.front_tokens[: bs * k], tree.front_hidden[: bs * k], Lr - 1 + s, req,
                                    slots, start, Lr.int(), extra, n_extra, self.dcache, max_keys=keys)
-        probs, toks = draft.candidates(normed, k, Lr - 1 + s)
+        if self.sampled:
+            probs, toks = self._sample(normed, tree.front_nodes[:bs].reshape(-1), k, s, tree.shape.layer_start(s + 1))
+        else:
+            probs, toks = draft.candidates(normed, k, Lr - 1 + s)
         tree.step(bs, s, probs, toks, nh)
         if s in tree.delta_slots:
             self.host_deltas[s].copy_(tree.deltas[s], non_blocking=True)
@@ -311,9 +370,16 @@ class Engine:
                       state_slot=sl.repeat_interleave(n), max_keys=self.max_len)
         rec = Records()
         out, aux = self.target.forward(rb, self.tcache, rec)
-        tid, _ = self.target.greedy(out)
-        acc, cnt, bonus = ops.accept_greedy(tid.view(bs, n), tokens, prow,
-                                            torch.full((bs,), n, dtype=torch.int32, device=dev))
+        if self.sampled:
+            nodes = tree.last_nodes if n > 1 else torch.full((bs, 1), -1, dtype=torch.int64, device=dev)
+            acc, cnt, bonus = ops.sampled_accept(self.target.logits(out), self.temperature, prow, tokens, nodes,
+                                                 self.q_store, self.q_ids, self.node_slot, self.top_k, self.seed,
+                                                 self.round_ctr, SAMPLED_STREAM)
+            ops.advance_round(self.round_ctr)
+        else:
+            tid, _ = self.target.greedy(out)
+            acc, cnt, bonus = ops.accept_greedy(tid.view(bs, n), tokens, prow,
+                                                torch.full((bs,), n, dtype=torch.int32, device=dev))
         cnt = cnt.to(torch.int32)
         accc = acc.long().clamp(min=0)
         valid = rowidx[None, :] < cnt[:, None]
