@@ -182,7 +182,8 @@ __device__ __forceinline__ float gdn_step(float* S, const GdnStage<K>& st, int j
   return (o0 + o1) + (o2 + o3);
 }
 
-// The output epilogue: o rounded to bf16, RMS-normalised over the head's V values, times w, times silu(z).
+// The output epilogue: o rounded to bf16, RMS-normalised over the head's V values, times w, times silu(z); with no
+// norm weight, o itself.
 __device__ __forceinline__ void gdn_store(const GdnArgs& a, int row, int h, int v, float o, const __nv_bfloat16* nw,
                                           float eps, float* red, __nv_bfloat16* out) {
   const float ob = __bfloat162float(__float2bfloat16(o));
@@ -196,6 +197,10 @@ __device__ __forceinline__ void gdn_store(const GdnArgs& a, int row, int h, int 
   for (int i = 0; i < nwp; ++i) tot += red[i];
   const float rs = rsqrtf(tot / a.V + eps);
   if (v < a.V) {
+    if (nw == nullptr) {  // raw recurrence output (a caller that applies its own norm)
+      out[(size_t(row) * a.HV + h) * a.V + v] = __float2bfloat16(ob);
+      return;
+    }
     const float z = bf(a.proj[size_t(row) * a.ldp + a.z_off + h * a.V + v]);
     out[(size_t(row) * a.HV + h) * a.V + v] = __float2bfloat16(ob * rs * bf(nw[v]) * silu(z));
   }
@@ -544,12 +549,12 @@ torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int6
   if (K == 128) {
     gdn_smem_attr(gdn_kernel<128>, sizeof(GdnStage<128>));
     C10_CUDA_CHECK(launch_pdl(gdn_kernel<128>, grid, 128, sizeof(GdnStage<128>), st.stream(), a, sl.data_ptr<int>(), pa.data_ptr<int>(),
-                                                              seg.data_ptr<int>(), scan, CBF(norm_w), float(eps),
+                                                              seg.data_ptr<int>(), scan, norm_w.numel() ? CBF(norm_w) : nullptr, float(eps),
                                                               BFP(out)));
   } else {
     gdn_smem_attr(gdn_kernel<64>, sizeof(GdnStage<64>));
     C10_CUDA_CHECK(launch_pdl(gdn_kernel<64>, grid, 128, sizeof(GdnStage<64>), st.stream(), a, sl.data_ptr<int>(), pa.data_ptr<int>(),
-                                                            seg.data_ptr<int>(), scan, CBF(norm_w), float(eps),
+                                                            seg.data_ptr<int>(), scan, norm_w.numel() ? CBF(norm_w) : nullptr, float(eps),
                                                             BFP(out)));
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -110,13 +110,21 @@ def gdn_gates(a, b, a_log, dt_bias):
 
 
 def gdn_tree(qkv, g, beta, state, state_slot, parent, cfg, scan: bool):
-    fn = _nat().gdn_tree if _cuda(qkv) else ref.gdn_tree
-    return fn(qkv, g, beta, state, state_slot, parent, cfg, scan)
+    """Unfused gated delta rule (float64 definition; the CUDA path is ``gdn_mixer`` / ``gdn_recurrence``)."""
+    return ref.gdn_tree(qkv, g, beta, state, state_slot, parent, cfg, scan)
+
+
+def gdn_recurrence(qkv, a, b, a_log, dt_bias, state, state_slot, parent, cfg):
+    """Tree gated delta rule from raw gates, no output norm: ``[T, HV * V]`` (host adapters apply their own norm)."""
+    if _cuda(qkv):
+        return _nat().gdn_recurrence(qkv, a, b, a_log, dt_bias, state, state_slot, parent, cfg)
+    g, beta = ref.gdn_gates(a, b, a_log, dt_bias)
+    return ref.gdn_tree(qkv, g, beta, state, state_slot, parent, cfg, False).reshape(qkv.shape[0], -1)
 
 
 def gdn_commit(qkv, g, beta, x_pre, state, conv_state, slots, rows, n_rows, cfg):
-    fn = _nat().gdn_commit if _cuda(qkv) else ref.gdn_commit
-    return fn(qkv, g, beta, x_pre, state, conv_state, slots, rows, n_rows, cfg)
+    """Unfused commit (float64 definition; the CUDA path is ``gdn_commit_all``)."""
+    return ref.gdn_commit(qkv, g, beta, x_pre, state, conv_state, slots, rows, n_rows, cfg)
 
 
 def conv_commit_scan(conv_state, x_pre, state_slot, kw):

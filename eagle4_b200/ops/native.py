@@ -192,6 +192,14 @@ def gdn_mixer(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent
                        bool(scan))
 
 
+def gdn_recurrence(qkv, a, b, a_log, dt_bias, state, state_slot, parent, cfg):
+    """Tree gated delta rule from raw gate inputs ``a`` / ``b`` ``[T, HV]``, without the output norm."""
+    hv = cfg.gdn_v_heads
+    raw = torch.cat([b, a], dim=1).contiguous()
+    return _C.gdn_tree(qkv, raw, 0, 0, hv, a_log, dt_bias, state, state_slot, parent, _NONE,
+                       float(cfg.rms_norm_eps), cfg.gdn_k_heads, hv, cfg.gdn_k_dim, cfg.gdn_v_dim, False)
+
+
 def gdn_commit_all(convs, projs, states, conv_states, a_logs, dt_biases, slots, rows, n_rows, cfg):
     _, b_off, a_off = _gdn_offsets(cfg)
     _C.gdn_commit_all(list(convs), list(projs), list(states), list(conv_states), list(a_logs), list(dt_biases),

@@ -52,10 +52,12 @@ def field_names(cls) -> Tuple[str, ...]:
 
 
 def parameter_names(func) -> Tuple[str, ...]:
-    """Named parameters after ``self`` / ``cls`` (``*args`` / ``**kwargs`` excluded); a class gives its constructor's."""
+    """Named parameters (``*args`` / ``**kwargs`` excluded) after the receiver of a method defined in a class; a
+    class gives its constructor's. A module-level function keeps a first parameter named ``cls``."""
     ps = [p for p in inspect.signature(func).parameters.values()
           if p.kind not in (inspect.Parameter.VAR_POSITIONAL, inspect.Parameter.VAR_KEYWORD)]
-    if ps and ps[0].name in ("self", "cls"):
+    in_class = "." in getattr(func, "__qualname__", "") and not inspect.isclass(func)
+    if ps and ps[0].name in ("self", "cls") and in_class:
         ps = ps[1:]
     return tuple(p.name for p in ps)
 
