@@ -29,7 +29,7 @@ from eagle4_b200 import ops
 from eagle4_b200.core.config import HarnessConfig, Mode
 from eagle4_b200.core.cost_model import WidthStep
 from eagle4_b200.core.draft_tree import DraftTree, TreeShape
-from eagle4_b200.runtime.policy import RoundPolicy, fit_width
+from eagle4_b200.runtime.policy import RoundPolicy, ServedChainPolicy, fit_width
 from eagle4_b200.models.draft import DraftCache, DraftModel
 from eagle4_b200.models.target import Records, RowBatch, TargetCache, TargetModel
 
@@ -140,6 +140,15 @@ class Engine:
         self.config = config or HarnessConfig(mode=Mode.STATIC)
         self.policy = RoundPolicy(self.config, top_k=top_k, steps=steps, verify_tokens=verify_tokens,
                                   target_is_moe=target.cfg.is_moe)
+        # chain rounds (top-k 1): the width per batch bucket is chosen on served rounds (or a calibrated schedule)
+        self.chain_policy = None
+        if draft is not None and top_k == 1 and self.config.mode.uses_cost_model:
+            schedule = None
+            if self.config.data_path:
+                from eagle4_b200.core.chain_width import chain_widths
+
+                schedule = chain_widths(self.config.data_path, verify_tokens, max_reqs)
+            self.chain_policy = ServedChainPolicy(range(2, verify_tokens + 1), schedule=schedule)
         if draft is not None:
             # work deltas are only read by the cost model's decisions
             slots = None if self.policy.cost is not None else ()
@@ -481,6 +490,15 @@ class Engine:
         self.last_depth, self.last_width = levels, width
         return width
 
+    def _chain_round(self, bs: int, width: int) -> int:
+        """One chain round of verify width ``width`` (``width - 1`` drafted tokens, one per depth)."""
+        self._graph(("begin", bs), self._phase_begin, bs)
+        for depth in range(1, width - 1):
+            self._graph(("step", bs, depth), self._phase_step, bs, depth)
+        self._graph(("verify", bs, width), self._phase_verify, bs, width)
+        self.last_depth, self.last_width = width - 1, width
+        return width
+
     def _plain(self, bs: int) -> None:
         self._graph(("plain", bs), self._plain_round, bs)
 
@@ -503,7 +521,15 @@ class Engine:
         spec = speculative and self.draft is not None
         while min(len(o) for o in outs) < max_new_tokens:
             self._pending_timing = None
-            if spec:
+            chain_t0 = None
+            if spec and self.chain_policy is not None:
+                chain_w = self.chain_policy.width(bs)
+                chain_t0 = _Stamp(self.device)
+                chain_t0.record()
+                self._chain_round(bs, chain_w)
+                chain_t1 = _Stamp(self.device)
+                chain_t1.record()
+            elif spec:
                 self._spec_round(bs, sum(ctx) // bs)
             else:
                 self._plain(bs)
@@ -529,4 +555,9 @@ class Engine:
                 got.append(take)
             if spec:
                 self.stats.record(got)
+            if chain_t0 is not None:
+                us = chain_t0.elapsed_us(chain_t1)
+                if self.target.tp is not None:
+                    us = self.target.tp.max_over_ranks([us])[0]
+                self.chain_policy.record(bs, chain_w, us, sum(got) / len(got))
         return [o[:max_new_tokens] for o in outs]

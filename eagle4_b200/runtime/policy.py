@@ -119,3 +119,53 @@ class RoundPolicy:
         self.live.record(bs, width, context, verify_us)
         if steps > 0:
             self.live.record(bs, DRAFT_WIDTH, context, draft_us / steps)
+
+
+class ServedChainPolicy:
+    """Chain width per batch bucket for chain rounds (top-k 1), chosen on served rounds.
+
+    A calibrated schedule (``core.chain_width.chain_widths``: served round times or cost tables, with the acceptance
+    profile) fixes the width per batch size when one is given. Otherwise each batch bucket first serves every
+    candidate width for ``probe_rounds`` rounds, measuring the round period and the tokens a request gains per round,
+    then serves the width with the most tokens per microsecond (``(1 + accepted) / round_us``, the rule of
+    ``core.chain_width``), re-probing the other widths every ``refresh`` rounds so a changed acceptance moves it
+    (reference ``eagle_harness/sglang/chain_rounds.py``: served chain choices, searched per batch key).
+    """
+
+    def __init__(self, widths: Sequence[int], *, probe_rounds: int = 4, refresh: int = 256,
+                 schedule: Optional[List[tuple]] = None):
+        self.widths = sorted(set(int(w) for w in widths if w >= 1))
+        if not self.widths:
+            raise ValueError("a chain policy needs at least one width")
+        self.probe_rounds, self.refresh, self.schedule = probe_rounds, refresh, schedule
+        self.samples: dict = {}  # (bucket, width) -> [round_us sum, tokens sum, rounds]
+        self.rounds: Counter = Counter()
+
+    @staticmethod
+    def bucket(bs: int) -> int:
+        return 1 << max(bs - 1, 0).bit_length()
+
+    def width(self, bs: int) -> int:
+        if self.schedule:
+            from eagle4_b200.core.chain_width import width_at
+
+            return max(1, width_at(self.schedule, bs))
+        b = self.bucket(bs)
+        n = self.rounds[b]
+        period = len(self.widths) * self.probe_rounds
+        if n < period or (self.refresh and n % self.refresh < period):
+            return self.widths[(n % period) // self.probe_rounds]
+        return self.best(b)
+
+    def best(self, bucket: int) -> int:
+        def rate(w):
+            us, tok, r = self.samples.get((bucket, w), (0.0, 0.0, 0))
+            return (tok / r) / (us / r) if r and us > 0 else -1.0
+
+        return max(self.widths, key=lambda w: (rate(w), -w))
+
+    def record(self, bs: int, width: int, round_us: float, tokens_per_request: float) -> None:
+        b = self.bucket(bs)
+        self.rounds[b] += 1
+        us, tok, r = self.samples.get((b, width), (0.0, 0.0, 0))
+        self.samples[(b, width)] = (us + round_us, tok + tokens_per_request, r + 1)

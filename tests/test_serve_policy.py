@@ -61,3 +61,33 @@ def test_live_costs_seed_then_price(tmp_path):
     assert out == plain
     # the seed sweep timed every captured width and the draft step of bucket 1
     assert live.seed_width(1) is None and live.ready(1)
+
+
+def test_served_chain_policy_probes_then_serves_best():
+    from eagle4_b200.runtime.policy import ServedChainPolicy
+
+    p = ServedChainPolicy([2, 4, 8], probe_rounds=2, refresh=0)
+    seen = []
+    for _ in range(6):  # probing: every width twice
+        w = p.width(1)
+        seen.append(w)
+        # width 4 gains 3 tokens in 1.2 units, width 8 gains 4 in 2.0, width 2 gains 1.5 in 1.0
+        p.record(1, w, {2: 1.0, 4: 1.2, 8: 2.0}[w], {2: 1.5, 4: 3.0, 8: 4.0}[w])
+    assert sorted(seen) == [2, 2, 4, 4, 8, 8]
+    assert p.width(1) == 4  # 2.5 tokens per unit beats 1.5 and 2.0
+    assert p.width(3) == 2  # bucket 4 starts probing from the first width
+
+
+def test_chain_rounds_equal_plain_on_cpu():
+    import torch
+
+    from eagle4_b200.api import LLM, TreeSpec
+
+    llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 1, 5), max_len=256,
+                        max_batch=2, config='{"mode": "serve"}')
+    assert llm.engine.chain_policy is not None
+    p = torch.randint(0, 4096, (2, 20), generator=torch.Generator().manual_seed(0))
+    a = llm.generate(p, 14)
+    b = llm.generate(p, 14, speculative=False)
+    assert torch.equal(a, b)
+    assert sum(llm.engine.chain_policy.rounds.values()) > 0
