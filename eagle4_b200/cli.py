@@ -73,13 +73,20 @@ def _calibrate(args) -> int:
         return 0
     args.output.mkdir(parents=True, exist_ok=False)
     (args.output / "settings.json").write_text(json.dumps(settings, indent=2) + "\n")
-    tree = TreeSpec(args.steps, args.top_k, args.draft_tokens)
+    tree = TreeSpec(args.steps, 1 if args.kind == "chain" else args.top_k, args.draft_tokens)
     llm = build_llm(args.model, args.draft, max_batch=max(args.batch_sizes), max_len=args.context_stop + 256,
                     tree=tree)
     key = CostKey(gpu=torch.cuda.get_device_name(), gpu_count=1, model=args.model, draft=str(args.draft or ""),
                   engine="eagle4_b200", dtype="bfloat16")
-    problems = calibrate(llm.engine, str(args.output), batch_sizes=args.batch_sizes, context_step=args.context_step,
-                         context_stop=args.context_stop, repeats=args.repeats, key=key)
+    if args.kind == "chain":
+        from eagle4_b200.runtime.calibrate import calibrate_chain
+
+        calibrate_chain(llm.engine, str(args.output), batch_sizes=args.batch_sizes, key=key)
+        problems = {}
+    else:
+        problems = calibrate(llm.engine, str(args.output), batch_sizes=args.batch_sizes,
+                             context_step=args.context_step, context_stop=args.context_stop, repeats=args.repeats,
+                             key=key)
     bad = {b: p for b, p in problems.items() if p}
     for b, p in bad.items():
         print(f"batch size {b}: the cost model refuses these costs ({p}); rounds there keep the fixed shape")
@@ -103,6 +110,8 @@ def main(argv: Optional[List[str]] = None) -> int:
     cal.add_argument("--steps", type=_positive, default=12)
     cal.add_argument("--top-k", type=_positive, default=4)
     cal.add_argument("--draft-tokens", type=_positive, default=16)
+    cal.add_argument("--kind", choices=("tree", "chain"), default="tree",
+                     help="tree: cost tables from timed forwards; chain: served chain rounds and acceptance")
     cal.add_argument("--dry-run", action="store_true", help="print settings and the serving command only")
     cal.set_defaults(func=_calibrate)
     chk = sub.add_parser("check", help="report the serving hosts and the native library")

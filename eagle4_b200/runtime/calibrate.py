@@ -176,3 +176,61 @@ def calibrate(engine, data_path: str, *, batch_sizes: Sequence[int], context_ste
         write_key(data_path, key)
     tables = load_cost_tables(paths.cost)
     return {bs: cost_model_problem(t, target_is_moe=engine.target.cfg.is_moe) for bs, t in tables.items()}
+
+
+def calibrate_chain(engine, data_path: str, *, batch_sizes: Sequence[int], prompt_len: int = 256,
+                    new_tokens: int = 128, widths: Optional[Sequence[int]] = None, seed: int = 0,
+                    key: Optional[CostKey] = None, progress: Callable[[str], None] = print) -> str:
+    """Served-chain calibration (the reference's SGLang calibration driver): serve generation at every chain width
+    and batch size, store the median round period per (batch size, width) as ``rounds/chain.json`` and the
+    acceptance by draft position, measured at the widest chain, as ``accept/chain.json``; returns ``data_path``.
+
+    ``engine`` must be a chain engine (top-k 1); width 1 is root-only verification."""
+    from eagle4_b200.core.chain_width import save_accept_profile, save_round_times
+
+    if engine.draft is None or engine.top_k != 1:
+        raise ValueError("chain calibration needs a draft and a top-k 1 (chain) engine")
+    widths = sorted(widths or range(1, engine.verify_tokens + 1))
+    gen = torch.Generator().manual_seed(seed)
+    rows, drafts, accepted = [], 0, [0] * (max(widths) - 1)
+    saved_policy = engine.chain_policy
+    try:
+        for bs in batch_sizes:
+            prompts = torch.randint(0, engine.target.cfg.vocab_size, (bs, prompt_len), generator=gen)
+            for w in widths:
+                engine.chain_policy = _FixedChain(w)
+                engine.generate(prompts, new_tokens)
+                us = sorted(engine.chain_policy.round_us)
+                if not us:
+                    continue
+                rows.append({"batch_size": bs, "width": w, "round_us": us[len(us) // 2], "count": len(us)})
+                if w == max(widths):
+                    for got in engine.chain_policy.emitted:
+                        drafts += 1
+                        for d in range(min(got - 1, len(accepted))):
+                            accepted[d] += 1
+                progress(f"bs {bs} width {w}: {rows[-1]['round_us']:.0f} us per round")
+    finally:
+        engine.chain_policy = saved_policy
+    save_round_times(data_path, rows)
+    if drafts:
+        save_accept_profile(data_path, drafts, accepted)
+    if key is not None:
+        write_key(data_path, key)
+    return data_path
+
+
+class _FixedChain:
+    """A chain policy that serves one width and keeps every round's period and per-request tokens."""
+
+    def __init__(self, width: int):
+        self.w = width
+        self.round_us: List[float] = []
+        self.emitted: List[int] = []
+
+    def width(self, bs: int) -> int:
+        return self.w
+
+    def record(self, bs: int, width: int, round_us: float, tokens_per_request: float) -> None:
+        self.round_us.append(round_us)
+        self.emitted.append(int(round(tokens_per_request)))

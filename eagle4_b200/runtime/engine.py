@@ -491,7 +491,8 @@ class Engine:
         return width
 
     def _chain_round(self, bs: int, width: int) -> int:
-        """One chain round of verify width ``width`` (``width - 1`` drafted tokens, one per depth)."""
+        """One chain round of verify width ``width`` (``width - 1`` drafted tokens, one per depth; width 1 verifies
+        the root only, after the draft extend)."""
         self._graph(("begin", bs), self._phase_begin, bs)
         for depth in range(1, width - 1):
             self._graph(("step", bs, depth), self._phase_step, bs, depth)

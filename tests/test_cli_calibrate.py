@@ -79,3 +79,17 @@ def test_serve_app_round_trip():
         assert client.get("/health").json()["rounds"] >= 1
     finally:
         b.stop.set()
+
+
+def test_chain_calibration_on_cpu(tmp_path):
+    from eagle4_b200.api import LLM, TreeSpec
+    from eagle4_b200.core.chain_width import chain_widths, load_accept_profile, load_round_times
+    from eagle4_b200.runtime.calibrate import calibrate_chain
+
+    llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(3, 1, 4), max_len=256,
+                        config='{"mode": "serve"}')
+    calibrate_chain(llm.engine, str(tmp_path), batch_sizes=[1], prompt_len=16, new_tokens=6, progress=lambda s: None)
+    rounds = load_round_times(str(tmp_path))
+    assert set(rounds[1]) == {1, 2, 3, 4}
+    assert load_accept_profile(str(tmp_path)) is not None
+    assert chain_widths(str(tmp_path), 4, 8)[0][0] == 1
