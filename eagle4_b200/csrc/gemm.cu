@@ -488,6 +488,23 @@ int max_stages() {
   return n;
 }
 
+// Fewest k-blocks (64 x 128 weight tiles) one CTA streams. E4_GEMM_MIN_KB overrides it for tuning runs.
+long min_kblocks() {
+  static long n = [] {
+    const char* e = std::getenv("E4_GEMM_MIN_KB");
+    const long v = e ? std::atol(e) : 6;
+    return v >= 1 && v <= 64 ? v : 6;
+  }();
+  return n;
+}
+
+// CTAs of a GEMM over ``total`` k-blocks: one per SM, but each streams at least min_kblocks() k-blocks, so a small
+// weight is split over fewer CTAs (fewer pieces per tile to add up) instead of one k-block per CTA.
+int gemm_grid(long total, int max_ctas) {
+  const long by_work = (total + min_kblocks() - 1) / min_kblocks();
+  return int(std::max<long>(1, std::min<long>(max_ctas, by_work)));
+}
+
 struct Scratch {
   torch::Tensor ws, counters, err;
 };
@@ -527,7 +544,7 @@ int launch_chunks(const torch::Tensor& x, const torch::Tensor& w, int epi, F chu
   const int n_tiles = (N + kTileM - 1) / kTileM;
   const int kb_total = (K + kTileK - 1) / kTileK;
   const long total = long(n_tiles) * kb_total;
-  const int grid = int(std::min<long>(sms, total));
+  const int grid = gemm_grid(total, sms);
   const CUtensorMap& wmap = weight_map(w.data_ptr(), N, K, w.stride(0));
   auto stream = at::cuda::getCurrentCUDAStream();
   TORCH_CHECK(n_tiles <= sc.counters.numel(), "gemm: too many weight tiles");
@@ -600,7 +617,7 @@ torch::Tensor gemm_traced(const torch::Tensor& x, const torch::Tensor& w, int64_
   using namespace gemm;
   auto y = torch::empty({x.size(0), w.size(0)}, x.options());
   auto yf = torch::empty({x.size(0), w.size(0)}, x.options().dtype(torch::kFloat32));
-  const int grid = std::min<long>(num_sms(), long((w.size(0) + kTileM - 1) / kTileM) * ((x.size(1) + kTileK - 1) / kTileK));
+  const int grid = gemm_grid(long((w.size(0) + kTileM - 1) / kTileM) * ((x.size(1) + kTileK - 1) / kTileK), num_sms());
   auto tr = torch::zeros({grid, 8}, x.options().dtype(torch::kInt64));
   launch_chunks(x, w, int(epi), [&](Params& p, int) {
     p.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
@@ -709,7 +726,7 @@ extern "C" int e4_gemm_bf16_noalloc(const void* x, int ldx, const void* w, int l
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 2;
   const int kb_total = (K + kTileK - 1) / kTileK;
   const long total = long(n_tiles) * kb_total;
-  const int grid = int(std::min<long>(std::min(sms, noalloc::kMaxGrid), total));
+  const int grid = gemm::gemm_grid(total, std::min(sms, noalloc::kMaxGrid));
   Params p{};
   p.T = T;
   p.N = N;

@@ -188,7 +188,8 @@ qkv_prepare_kernel(const __nv_bfloat16* __restrict__ qkv, int ldq, const int64_t
   const int voff = koff + Hk * D;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* hb = buf[warp];
-  for (int hh = warp; hh < Hq + Hk; hh += kPrepWarps) {
+  // grid.y splits the heads: warp w of CTA (r, y) handles heads y * kPrepWarps + w, stepping by the whole grid
+  for (int hh = blockIdx.y * kPrepWarps + warp; hh < Hq + Hk; hh += kPrepWarps * gridDim.y) {
     const bool isq = hh < Hq;
     const __nv_bfloat16* src = row + (isq ? hh * D : koff + (hh - Hq) * D);
     const __nv_bfloat16* nw = isq ? qn : kn;
@@ -229,7 +230,7 @@ qkv_prepare_kernel(const __nv_bfloat16* __restrict__ qkv, int ldq, const int64_t
   }
   const uint4* vs = reinterpret_cast<const uint4*>(row + voff);
   uint4* vd = reinterpret_cast<uint4*>(vc + size_t(s) * Hk * D);
-  for (int i = threadIdx.x; i < Hk * D / 8; i += blockDim.x) vd[i] = vs[i];
+  for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < Hk * D / 8; i += blockDim.x * gridDim.y) vd[i] = vs[i];
 }
 
 // Greedy head: reduce per-tile (max, argmax) partials to one id per token (ties to the lower id).
@@ -384,7 +385,8 @@ torch::Tensor qkv_prepare(const torch::Tensor& qkv, const torch::Tensor& pos, co
   TORCH_CHECK(D % 8 == 0 && D <= 256 && qkv.stride(0) % 8 == 0, "qkv_prepare: D must be a multiple of 8 up to 256");
   auto q = torch::empty({T, Hq, D}, qkv.options());
   if (T)
-    C10_CUDA_CHECK(launch_pdl(qkv_prepare_kernel, T, kPrepWarps * 32, 0, at::cuda::getCurrentCUDAStream().stream(), 
+    C10_CUDA_CHECK(launch_pdl(qkv_prepare_kernel, dim3(T, (Hq + Hk + kPrepWarps - 1) / kPrepWarps), kPrepWarps * 32, 0,
+                              at::cuda::getCurrentCUDAStream().stream(),
         CBF16(qkv), qkv.stride(0), pos.data_ptr<int64_t>(), slot.data_ptr<int64_t>(), BF16(kc), BF16(vc),
         qn ? CBF16(*qn) : nullptr, kn ? CBF16(*kn) : nullptr, norm_offset ? 1 : 0, cos_t.data_ptr<float>(),
         sin_t.data_ptr<float>(), BF16(q), Hq, Hk, D, rot, gated ? 1 : 0, float(eps)));

@@ -403,18 +403,12 @@ __global__ void tree_step_kernel(const float* __restrict__ probs, const int64_t*
     scores[size_t(b) * cap + layer_start + t] = layer[t];
     tokens[size_t(b) * cap + layer_start + t] = toks[size_t(b * K + t / K) * K + (t % K)];
   }
-  if (t == 0) {
-    // top-K of the layer, stable (ties to the lower index)
-    unsigned used = 0;
-    for (int k = 0; k < K; ++k) {
-      int bi = -1;
-      float bv = -INFINITY;
-      for (int i = 0; i < KK; ++i)
-        if (!((used >> i) & 1ull) && (bi < 0 || layer[i] > bv)) { bv = layer[i]; bi = i; }
-      used |= 1u << bi;
-      pick[k] = bi;
-      top[k] = bv;
-    }
+  if (t < KK) {
+    // top-K of the layer by rank (ties to the lower index): one thread per value, no serial scan
+    const float v = layer[t];
+    int rank = 0;
+    for (int i = 0; i < KK; ++i) rank += (layer[i] > v) || (layer[i] == v && i < t);
+    if (rank < K) { pick[rank] = t; top[rank] = v; }
   }
   __syncthreads();
   // ancestors of the picked lanes (read all before writing)
@@ -435,26 +429,17 @@ __global__ void tree_step_kernel(const float* __restrict__ probs, const int64_t*
     reinterpret_cast<uint4*>(front_hidden + size_t(b * K + k) * H)[c] =
         reinterpret_cast<const uint4*>(hidden + size_t(b * K + pick[k] / K) * H)[c];
   }
-  // best set: merge the sorted best list (work_cap, descending) with the layer's values, keep work_cap
-  if (t < work_cap) merged[t] = best[size_t(b) * work_cap + t];
+  // best set: the work_cap largest values of (best list ++ layer), descending; every value finds its rank in
+  // parallel (ties by position), values ranked below work_cap are written at their rank
+  const int m = work_cap + KK;
+  for (int i = t; i < m; i += blockDim.x) merged[i] = i < work_cap ? best[size_t(b) * work_cap + i] : layer[i - work_cap];
   __syncthreads();
   if (t < work_cap) best_prev[size_t(b) * work_cap + t] = merged[t];
-  if (t == 0) {
-    // insertion of the KK layer values into the descending list (values only)
-    float lay[64];
-    for (int i = 0; i < KK; ++i) lay[i] = layer[i];
-    for (int i = 1; i < KK; ++i) {
-      const float v = lay[i];
-      int j = i - 1;
-      while (j >= 0 && lay[j] < v) { lay[j + 1] = lay[j]; --j; }
-      lay[j + 1] = v;
-    }
-    int a = 0, c = 0;
-    for (int o = 0; o < work_cap; ++o) {
-      const float av = a < work_cap ? merged[a] : -INFINITY;
-      const float cv = c < KK ? lay[c] : -INFINITY;
-      if (av >= cv) { best[size_t(b) * work_cap + o] = av; ++a; } else { best[size_t(b) * work_cap + o] = cv; ++c; }
-    }
+  for (int i = t; i < m; i += blockDim.x) {
+    const float v = merged[i];
+    int rank = 0;
+    for (int j = 0; j < m; ++j) rank += (merged[j] > v) || (merged[j] == v && j < i);
+    if (rank < work_cap) best[size_t(b) * work_cap + rank] = v;
   }
 }
 
