@@ -75,6 +75,12 @@ std::vector<torch::Tensor> sampled_accept(const torch::Tensor& logits, double te
                                           const torch::Tensor& q_ids, const torch::Tensor& node_slot, int64_t K,
                                           int64_t seed, const torch::Tensor& round_ctr, int64_t stream);
 void advance_round(torch::Tensor round_ctr);
+std::vector<torch::Tensor> verify_rows_meta(const torch::Tensor& prow, const torch::Tensor& toks,
+                                            const torch::Tensor& root, const torch::Tensor& L,
+                                            const torch::Tensor& slot, const torch::Tensor& block_table, int64_t page);
+std::vector<torch::Tensor> draft_step_rows(const torch::Tensor& L, const torch::Tensor& slot,
+                                           const torch::Tensor& block_table, torch::Tensor ancestors, int64_t bs,
+                                           int64_t K, int64_t s, int64_t page, int64_t window);
 torch::Tensor gemm_traced(const torch::Tensor& x, const torch::Tensor& w, int64_t epi);
 int64_t sym_alloc(int64_t bytes, int64_t device);
 void sym_free(int64_t ptr);
@@ -98,6 +104,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample_children", &e4::sample_children, "Gumbel-top-k children from candidate logits");
   m.def("sampled_accept", &e4::sampled_accept, "recursive tree rejection over the verify rows");
   m.def("advance_round", &e4::advance_round);
+  m.def("verify_rows_meta", &e4::verify_rows_meta, "verify row structure of a round");
+  m.def("draft_step_rows", &e4::draft_step_rows, "row metadata of one draft step");
   m.def("gemm_traced", &e4::gemm_traced, "one GEMM with per-CTA timestamps (tuning)");
   m.def("sym_alloc", &e4::sym_alloc);
   m.def("sym_free", &e4::sym_free);

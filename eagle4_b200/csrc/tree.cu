@@ -491,6 +491,81 @@ __global__ void select_rows_kernel(const float* __restrict__ scores, const float
   }
 }
 
+// Row metadata of draft step ``s`` in one launch (the frontier's K rows per request): RoPE position L - 1 + s, the
+// request's block-table row, the KV slot of position L + (s - 1) * K + k, the window start, the visible context
+// length L, and the ancestor slots (depth-1 .. s, this row's own slot last), which are also recorded in the tree.
+__global__ void draft_step_rows_kernel(const int64_t* __restrict__ L, const int* __restrict__ slot,
+                                       const int* __restrict__ block_table, int bt_stride, int* ancestors,
+                                       int depth_cap, int R, int K, int s, int page, int window, int64_t* pos,
+                                       int* req, int64_t* slots, int* start, int* ctx_len, int* extra, int* n_extra) {
+  pdl_wait();
+  pdl_trigger();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= R) return;
+  const int b = i / K, k = i % K;
+  const int64_t l = L[b];
+  const int rq = slot[b];
+  const int64_t p_kv = l + int64_t(s - 1) * K + k;
+  const int64_t sl = int64_t(block_table[size_t(rq) * bt_stride + p_kv / page]) * page + p_kv % page;
+  pos[i] = l - 1 + s;
+  req[i] = rq;
+  slots[i] = sl;
+  start[i] = window > 0 ? int(l - window > 0 ? l - window : 0) : 0;
+  ctx_len[i] = int(l);
+  n_extra[i] = s;
+  int* anc = ancestors + (size_t(b) * K + k) * depth_cap;
+  anc[s - 1] = int(sl);
+  for (int j = 0; j < s - 1; ++j) extra[size_t(i) * s + j] = anc[j];
+  extra[size_t(i) * s + s - 1] = int(sl);
+}
+
+// Everything the verify forward needs about its rows, one CTA per request and one thread per row (n <= 64): the
+// row's tokens (root first), ancestor-or-self set (walking the parent rows; rows follow node order, parents first),
+// RoPE position L + depth, KV slot of position L + r, the ancestor slots in row order (the attention's extra keys),
+// their count, the parent row in the flattened batch, and the request's block-table row / context length.
+__global__ void verify_rows_meta_kernel(const int* __restrict__ prow, const int64_t* __restrict__ toks,
+                                        const int64_t* __restrict__ root, const int64_t* __restrict__ L,
+                                        const int* __restrict__ slot, const int* __restrict__ block_table,
+                                        int bt_stride, int n, int page, int64_t* tokens, int64_t* pos, int64_t* slots,
+                                        int* extra, int* n_extra, int* parent, int* req, int* ctx_len) {
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x, r = threadIdx.x;
+  __shared__ int64_t s_slot[64];
+  const bool live = r < n;
+  const int64_t l = L[b];
+  const int rq = slot[b];
+  int64_t sl = 0;
+  uint64_t mask = 0;
+  if (live) {
+    const int64_t p = l + r;
+    sl = int64_t(block_table[size_t(rq) * bt_stride + p / page]) * page + p % page;
+    s_slot[r] = sl;
+    int depth = -1;
+    for (int j = r, hops = 0; j >= 0 && hops <= n; j = prow[size_t(b) * n + j], ++hops) {
+      mask |= 1ull << j;
+      ++depth;
+    }
+    const size_t i = size_t(b) * n + r;
+    tokens[i] = r == 0 ? root[b] : toks[size_t(b) * (n - 1) + r - 1];
+    pos[i] = l + depth;
+    slots[i] = sl;
+    const int pr = prow[size_t(b) * n + r];
+    parent[i] = pr >= 0 ? b * n + pr : -1;
+    req[i] = rq;
+    ctx_len[i] = int(l);
+  }
+  __syncthreads();
+  if (live) {
+    const size_t i = size_t(b) * n + r;
+    int c = 0;
+    for (int j = 0; j < n; ++j)
+      if ((mask >> j) & 1ull) extra[i * n + c++] = int(s_slot[j]);
+    n_extra[i] = c;
+    for (int j = c; j < n; ++j) extra[i * n + j] = int(sl);
+  }
+}
+
 }  // namespace
 
 // Top-C (value desc, id asc) of each row of fp32 scores [R, V]: (values [R, C], ids int64 [R, C]).
@@ -561,6 +636,49 @@ std::vector<torch::Tensor> select_rows(const torch::Tensor& scores, const torch:
       scores.size(1), parents.size(1), K, count, ot.data_ptr<int64_t>(), op.data_ptr<int>(), on.data_ptr<int64_t>()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {ot, op, on};
+}
+
+std::vector<torch::Tensor> verify_rows_meta(const torch::Tensor& prow, const torch::Tensor& toks,
+                                            const torch::Tensor& root, const torch::Tensor& L,
+                                            const torch::Tensor& slot, const torch::Tensor& block_table, int64_t page) {
+  const at::cuda::CUDAGuard g(L.device());
+  const int bs = prow.size(0), n = prow.size(1);
+  TORCH_CHECK(n >= 1 && n <= 64 && prow.scalar_type() == at::kInt && prow.is_contiguous());
+  TORCH_CHECK(n == 1 || (toks.size(0) == bs && toks.size(1) == n - 1 && toks.is_contiguous()));
+  auto i64 = L.options(), i32 = L.options().dtype(torch::kInt32);
+  auto tokens = torch::empty({bs, n}, i64), pos = torch::empty({bs * n}, i64), slots = torch::empty({bs, n}, i64);
+  auto extra = torch::empty({bs * n, n}, i32), ne = torch::empty({bs * n}, i32), par = torch::empty({bs * n}, i32);
+  auto req = torch::empty({bs * n}, i32), ctx = torch::empty({bs * n}, i32);
+  if (bs)
+    C10_CUDA_CHECK(launch_pdl(verify_rows_meta_kernel, bs, 64, 0, at::cuda::getCurrentCUDAStream().stream(),
+                              prow.data_ptr<int>(), n > 1 ? toks.data_ptr<int64_t>() : nullptr,
+                              root.data_ptr<int64_t>(), L.data_ptr<int64_t>(), slot.data_ptr<int>(),
+                              block_table.data_ptr<int>(), int(block_table.stride(0)), n, int(page),
+                              tokens.data_ptr<int64_t>(), pos.data_ptr<int64_t>(), slots.data_ptr<int64_t>(),
+                              extra.data_ptr<int>(), ne.data_ptr<int>(), par.data_ptr<int>(), req.data_ptr<int>(),
+                              ctx.data_ptr<int>()));
+  return {tokens, pos, slots, extra, ne, par, req, ctx};
+}
+
+std::vector<torch::Tensor> draft_step_rows(const torch::Tensor& L, const torch::Tensor& slot,
+                                           const torch::Tensor& block_table, torch::Tensor ancestors, int64_t bs,
+                                           int64_t K, int64_t s, int64_t page, int64_t window) {
+  const at::cuda::CUDAGuard g(L.device());
+  TORCH_CHECK(L.scalar_type() == at::kLong && slot.scalar_type() == at::kInt && block_table.scalar_type() == at::kInt);
+  TORCH_CHECK(ancestors.scalar_type() == at::kInt && ancestors.is_contiguous() && s >= 1 && s <= ancestors.size(2));
+  const int R = int(bs * K);
+  auto i64 = L.options(), i32 = L.options().dtype(torch::kInt32);
+  auto pos = torch::empty({R}, i64), slots = torch::empty({R}, i64);
+  auto req = torch::empty({R}, i32), start = torch::empty({R}, i32), ctx = torch::empty({R}, i32);
+  auto extra = torch::empty({R, s}, i32), ne = torch::empty({R}, i32);
+  if (R)
+    C10_CUDA_CHECK(launch_pdl(draft_step_rows_kernel, (R + 127) / 128, 128, 0, at::cuda::getCurrentCUDAStream().stream(),
+                              L.data_ptr<int64_t>(), slot.data_ptr<int>(), block_table.data_ptr<int>(),
+                              int(block_table.stride(0)), ancestors.data_ptr<int>(), int(ancestors.size(2)), R, int(K),
+                              int(s), int(page), int(window), pos.data_ptr<int64_t>(), req.data_ptr<int>(),
+                              slots.data_ptr<int64_t>(), start.data_ptr<int>(), ctx.data_ptr<int>(),
+                              extra.data_ptr<int>(), ne.data_ptr<int>()));
+  return {pos, req, slots, start, ctx, extra, ne};
 }
 
 }  // namespace e4

@@ -333,21 +333,28 @@ class Engine:
         """Draft step ``s``: the depth-``s`` frontier through the draft head; adds depth ``s + 1``."""
         k, tree, draft, dev = self.top_k, self.tree, self.draft, self.device
         w = draft.cfg.sliding_window
-        Lr = self.L[:bs].repeat_interleave(k)
-        req = self.slot[:bs].repeat_interleave(k)
-        lane = torch.arange(k, device=dev).repeat(bs)
-        start = ((Lr - w).clamp(min=0) if w else torch.zeros_like(Lr)).int()
         keys = min(w, self.max_len) + self.steps if w else self.max_len + self.steps
-        slots = self._slots(req, Lr + (s - 1) * k + lane)
-        tree.set_step_slots(bs, s, slots.view(bs, k))
-        extra = tree.ancestors[:bs, :, :s].reshape(bs * k, s).contiguous()
-        n_extra = torch.full((bs * k,), s, dtype=torch.int32, device=dev)
-        normed, nh = draft.forward(tree.front_tokens[: bs * k], tree.front_hidden[: bs * k], Lr - 1 + s, req,
-                                   slots, start, Lr.int(), extra, n_extra, self.dcache, max_keys=keys)
+        if dev.type == "cuda":  # all the rows' metadata in one launch
+            from eagle4_b200.ops import native
+
+            pos, req, slots, start, ctx, extra, n_extra = native._C.draft_step_rows(
+                self.L, self.slot, self.tcache.block_table, tree.ancestors, bs, k, s, self.page, w or 0)
+        else:
+            Lr = self.L[:bs].repeat_interleave(k)
+            req = self.slot[:bs].repeat_interleave(k)
+            lane = torch.arange(k, device=dev).repeat(bs)
+            start = ((Lr - w).clamp(min=0) if w else torch.zeros_like(Lr)).int()
+            slots = self._slots(req, Lr + (s - 1) * k + lane)
+            tree.set_step_slots(bs, s, slots.view(bs, k))
+            extra = tree.ancestors[:bs, :, :s].reshape(bs * k, s).contiguous()
+            n_extra = torch.full((bs * k,), s, dtype=torch.int32, device=dev)
+            pos, ctx = Lr - 1 + s, Lr.int()
+        normed, nh = draft.forward(tree.front_tokens[: bs * k], tree.front_hidden[: bs * k], pos, req,
+                                   slots, start, ctx, extra, n_extra, self.dcache, max_keys=keys)
         if self.sampled:
             probs, toks = self._sample(normed, tree.front_nodes[:bs].reshape(-1), k, s, tree.shape.layer_start(s + 1))
         else:
-            probs, toks = draft.candidates(normed, k, Lr - 1 + s)
+            probs, toks = draft.candidates(normed, k, pos)
         tree.step(bs, s, probs, toks, nh)
         if s in tree.delta_slots:
             self.host_deltas[s].copy_(tree.deltas[s], non_blocking=True)
@@ -359,24 +366,35 @@ class Engine:
         tree = self.tree
         if n > 1:
             toks, prow = tree.verify_rows(bs, self.steps, n - 1)
-            tokens = torch.cat([self.root[:bs, None], toks], dim=1)  # [bs, n]
+            tokens = torch.cat([self.root[:bs, None], toks], dim=1) if dev.type != "cuda" else None  # [bs, n]
         else:
-            tokens = self.root[:bs, None].clone()
+            toks = None
+            tokens = self.root[:bs, None].clone() if dev.type != "cuda" else None
             prow = torch.full((bs, 1), -1, dtype=torch.int32, device=dev)
-        depth, anc = tree_rows_meta(prow)
         L, sl = self.L[:bs], self.slot[:bs]
         rowidx = torch.arange(n, device=dev)
-        slots = self._slots(sl[:, None], L[:, None] + rowidx[None, :])  # [bs, n] physical slot of row r at L + r
-        key = (~anc).long() * n + rowidx[None, None, :]
-        order = torch.argsort(key, dim=-1)
-        extra = torch.gather(slots[:, None, :].expand(bs, n, n), 2, order).int()
         base = (torch.arange(bs, device=dev) * n)[:, None]
-        parent = torch.where(prow >= 0, prow + base, prow)
-        rb = RowBatch(ids=tokens.reshape(-1), pos=(L[:, None] + depth).reshape(-1), req=sl.repeat_interleave(n),
-                      write_slot=slots.reshape(-1), ctx_start=torch.zeros(bs * n, dtype=torch.int32, device=dev),
-                      ctx_len=L.int().repeat_interleave(n), extra=extra.reshape(bs * n, n),
-                      n_extra=anc.sum(-1).int().reshape(-1), parent=parent.reshape(-1).int(),
-                      state_slot=sl.repeat_interleave(n), max_keys=self.max_len)
+        if dev.type == "cuda":  # the rows' structure in one launch
+            from eagle4_b200.ops import native
+
+            tokens, pos, slots, extra, n_extra, parent, req, ctx = native._C.verify_rows_meta(
+                prow.contiguous(), toks.contiguous() if n > 1 else self.root[:bs, None], self.root[:bs].contiguous(),
+                self.L[:bs].contiguous(), self.slot[:bs].contiguous(), self.tcache.block_table, self.page)
+            rb = RowBatch(ids=tokens.reshape(-1), pos=pos, req=req, write_slot=slots.reshape(-1),
+                          ctx_start=torch.zeros(bs * n, dtype=torch.int32, device=dev), ctx_len=ctx, extra=extra,
+                          n_extra=n_extra, parent=parent, state_slot=req, max_keys=self.max_len)
+        else:
+            depth, anc = tree_rows_meta(prow)
+            slots = self._slots(sl[:, None], L[:, None] + rowidx[None, :])  # [bs, n] physical slot of row r at L + r
+            key = (~anc).long() * n + rowidx[None, None, :]
+            order = torch.argsort(key, dim=-1)
+            extra = torch.gather(slots[:, None, :].expand(bs, n, n), 2, order).int()
+            parent = torch.where(prow >= 0, prow + base, prow)
+            rb = RowBatch(ids=tokens.reshape(-1), pos=(L[:, None] + depth).reshape(-1), req=sl.repeat_interleave(n),
+                          write_slot=slots.reshape(-1), ctx_start=torch.zeros(bs * n, dtype=torch.int32, device=dev),
+                          ctx_len=L.int().repeat_interleave(n), extra=extra.reshape(bs * n, n),
+                          n_extra=anc.sum(-1).int().reshape(-1), parent=parent.reshape(-1).int(),
+                          state_slot=sl.repeat_interleave(n), max_keys=self.max_len)
         rec = Records()
         out, aux = self.target.forward(rb, self.tcache, rec)
         if self.sampled:
