@@ -206,6 +206,11 @@ def main() -> None:
         "plain_tok_s": round(plain_tok * replicas / (plain_ms / 1e3), 2) if plain_ms else None,
         "speedup_vs_plain": round((spec_tok / spec_ms) / (plain_tok / plain_ms), 4) if plain_ms else None,
         "mean_accepted_per_round": round(accept, 3),
+        "served_choice": ({"native_round_share": round(
+            sum(v[2] for k, v in eng.tree_choice.samples.items() if k[1] == 0)
+            / max(1, sum(v[2] for v in eng.tree_choice.samples.values())), 3),
+            "rule": "per batch bucket: speculate or decode natively, whichever served more tokens per us"}
+            if getattr(eng, "tree_choice", None) is not None else None),
         "spec_equals_plain": same,
         "clocks": clocks,
         "e2e": {"value": round(e2e_tok * replicas / e2e_s, 2), "unit": "tokens/s",

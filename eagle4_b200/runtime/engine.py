@@ -29,7 +29,7 @@ from eagle4_b200 import ops
 from eagle4_b200.core.config import HarnessConfig, Mode
 from eagle4_b200.core.cost_model import WidthStep
 from eagle4_b200.core.draft_tree import DraftTree, TreeShape
-from eagle4_b200.runtime.policy import RoundPolicy, ServedChainPolicy, fit_width
+from eagle4_b200.runtime.policy import RoundPolicy, ServedChainPolicy, ServedTreeChoice, fit_width
 from eagle4_b200.models.draft import DraftCache, DraftModel
 from eagle4_b200.models.target import Records, RowBatch, TargetCache, TargetModel
 
@@ -149,6 +149,10 @@ class Engine:
 
                 schedule = chain_widths(self.config.data_path, verify_tokens, max_reqs)
             self.chain_policy = ServedChainPolicy(range(2, verify_tokens + 1), schedule=schedule)
+        # serve mode: per batch bucket, speculate or decode natively, whichever yields more tokens per microsecond
+        self.tree_choice = None
+        if draft is not None and top_k > 1 and self.config.mode.uses_cost_model:
+            self.tree_choice = ServedTreeChoice()
         if draft is not None:
             # work deltas are only read by the cost model's decisions
             slots = None if self.policy.cost is not None else ()
@@ -276,7 +280,7 @@ class Engine:
                       parent=torch.full((bs,), -1, dtype=torch.int32, device=self.device), state_slot=sl,
                       max_keys=self.max_len)
         rec = Records()
-        out, _ = self.target.forward(rb, self.tcache, rec)
+        out, aux = self.target.forward(rb, self.tcache, rec)
         if self.sampled:  # plain sampling: the walk with no children draws from p
             dev = self.device
             _, _, ids = ops.sampled_accept(self.target.logits(out), self.temperature,
@@ -294,6 +298,18 @@ class Engine:
         self.root[:bs] = ids
         self.out_tok[:bs, 0] = ids
         self.out_cnt[:bs] = 1
+        if self.draft is not None and aux is not None:
+            # keep the draft's pending rows (the most recent N) so a later speculative round extends from here
+            n = self.verify_tokens
+            cnt = self.ext_cnt[:bs].long()
+            full = (cnt >= n)[:, None]
+            self.ext_tok[:bs] = torch.where(full, torch.roll(self.ext_tok[:bs], -1, 1), self.ext_tok[:bs])
+            self.ext_aux[:bs] = torch.where(full[:, :, None], torch.roll(self.ext_aux[:bs], -1, 1), self.ext_aux[:bs])
+            at = cnt.clamp(max=n - 1)
+            b = torch.arange(bs, device=self.device)
+            self.ext_tok[b, at] = ids
+            self.ext_aux[b, at] = aux
+            self.ext_cnt[:bs] = (cnt + 1).clamp(max=n).int()
 
     def _draft_extend(self, bs: int) -> None:
         """Pending rows (``ext_cnt <= N`` per request, padded to N) through the draft; the last valid row's top-K
@@ -541,7 +557,15 @@ class Engine:
         while min(len(o) for o in outs) < max_new_tokens:
             self._pending_timing = None
             chain_t0 = None
-            if spec and self.chain_policy is not None:
+            tree_t0 = None
+            choice = ServedTreeChoice.SPECULATE
+            if spec and self.tree_choice is not None:
+                choice = self.tree_choice.choice(bs)
+                tree_t0 = _Stamp(self.device)
+                tree_t0.record()
+            if spec and choice == ServedTreeChoice.NATIVE:
+                self._plain(bs)
+            elif spec and self.chain_policy is not None:
                 chain_w = self.chain_policy.width(bs)
                 chain_t0 = _Stamp(self.device)
                 chain_t0.record()
@@ -552,6 +576,9 @@ class Engine:
                 self._spec_round(bs, sum(ctx) // bs)
             else:
                 self._plain(bs)
+            if tree_t0 is not None:
+                tree_t1 = _Stamp(self.device)
+                tree_t1.record()
             self.host_tok[:bs].copy_(self.out_tok[:bs], non_blocking=True)
             self.host_cnt[:bs].copy_(self.out_cnt[:bs], non_blocking=True)
             if self.device.type == "cuda":
@@ -574,6 +601,11 @@ class Engine:
                 got.append(take)
             if spec:
                 self.stats.record(got)
+            if tree_t0 is not None:
+                us = tree_t0.elapsed_us(tree_t1)
+                if self.target.tp is not None:
+                    us = self.target.tp.max_over_ranks([us])[0]
+                self.tree_choice.record(bs, choice, us, sum(got) / len(got))
             if chain_t0 is not None:
                 us = chain_t0.elapsed_us(chain_t1)
                 if self.target.tp is not None:

@@ -169,3 +169,51 @@ class ServedChainPolicy:
         self.rounds[b] += 1
         us, tok, r = self.samples.get((b, width), (0.0, 0.0, 0))
         self.samples[(b, width)] = (us + round_us, tok + tokens_per_request, r + 1)
+
+
+class ServedTreeChoice:
+    """Per batch bucket: speculate (1) or decode natively (0), chosen on served rounds.
+
+    The cost model prices a tree from draft and verify costs and an acceptance prior; what a round actually yields
+    depends on the draft. So each bucket serves ``probe_rounds`` speculative rounds and ``probe_rounds`` native
+    rounds, compares tokens per microsecond (tokens a request gains per round over the round period), serves the
+    better choice, and probes again every ``refresh`` rounds. A measured schedule (``rounds/tree.json`` reduced to
+    0 / 1 per batch key, or packaged served choices) fixes the choice instead (reference served tree choices:
+    ``eagle_harness/core/cost_profiles.py:packaged_served_choices`` and the served-round search of
+    ``eagle_harness/sglang/chain_rounds.py``).
+    """
+
+    SPECULATE, NATIVE = 1, 0
+
+    def __init__(self, *, probe_rounds: int = 4, refresh: int = 256, choices: Optional[dict] = None):
+        self.probe_rounds, self.refresh, self.choices = probe_rounds, refresh, choices
+        self.samples: dict = {}
+        self.rounds: Counter = Counter()
+
+    @staticmethod
+    def bucket(bs: int) -> int:
+        return 1 << max(bs - 1, 0).bit_length()
+
+    def choice(self, bs: int) -> int:
+        b = self.bucket(bs)
+        if self.choices:
+            keys = sorted(self.choices)
+            return self.choices[min(keys, key=lambda k: (abs(k - b), -k))]
+        n = self.rounds[b]
+        period = 2 * self.probe_rounds
+        if n < period or (self.refresh and n % self.refresh < period):
+            return self.SPECULATE if (n % period) < self.probe_rounds else self.NATIVE
+        return self.best(b)
+
+    def best(self, bucket: int) -> int:
+        def rate(c):
+            us, tok, r = self.samples.get((bucket, c), (0.0, 0.0, 0))
+            return tok / us if r and us > 0 else -1.0
+
+        return self.SPECULATE if rate(self.SPECULATE) >= rate(self.NATIVE) else self.NATIVE
+
+    def record(self, bs: int, choice: int, round_us: float, tokens_per_request: float) -> None:
+        b = self.bucket(bs)
+        self.rounds[b] += 1
+        us, tok, r = self.samples.get((b, choice), (0.0, 0.0, 0))
+        self.samples[(b, choice)] = (us + round_us, tok + tokens_per_request, r + 1)

@@ -54,6 +54,7 @@ def test_live_costs_seed_then_price(tmp_path):
     g = torch.Generator().manual_seed(1)
     prompts = torch.randint(0, tgt.cfg.vocab_size, (1, 24), generator=g).tolist()
     eng = Engine(tgt, drf, max_reqs=1, max_len=160, steps=4, top_k=2, verify_tokens=8, config=cfg)
+    eng.tree_choice = None  # every round speculates: this test times the seed sweep
     live = eng.policy.live
     out = eng.generate(prompts, 40, speculative=True)
     plain = Engine(tgt, drf, max_reqs=1, max_len=160, steps=4, top_k=2, verify_tokens=8).generate(
@@ -91,3 +92,33 @@ def test_chain_rounds_equal_plain_on_cpu():
     b = llm.generate(p, 14, speculative=False)
     assert torch.equal(a, b)
     assert sum(llm.engine.chain_policy.rounds.values()) > 0
+
+
+def test_served_tree_choice_switches_to_native_when_faster():
+    from eagle4_b200.runtime.policy import ServedTreeChoice
+
+    c = ServedTreeChoice(probe_rounds=2, refresh=0)
+    for _ in range(4):
+        ch = c.choice(1)
+        # speculation: 1 token in 1.6 units; native: 1 token in 1.0 unit
+        c.record(1, ch, 1.6 if ch == 1 else 1.0, 1.0)
+    assert c.choice(1) == ServedTreeChoice.NATIVE
+    c2 = ServedTreeChoice(probe_rounds=1, refresh=0)
+    c2.record(1, c2.choice(1), 1.5, 3.0)  # speculation: 3 tokens in 1.5
+    c2.record(1, c2.choice(1), 1.0, 1.0)
+    assert c2.choice(1) == ServedTreeChoice.SPECULATE
+
+
+def test_serve_mode_mixes_native_and_speculative_rounds_exactly():
+    import torch
+
+    from eagle4_b200.api import LLM, TreeSpec
+
+    llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_len=256,
+                        config='{"mode": "serve"}')
+    llm.engine.tree_choice.probe_rounds = 2  # alternate quickly: 2 speculative, 2 native, ...
+    p = torch.randint(0, 4096, (1, 24), generator=torch.Generator().manual_seed(0))
+    a = llm.generate(p, 20)
+    b = llm.generate(p, 20, speculative=False)
+    assert torch.equal(a, b)
+    assert sum(llm.engine.tree_choice.rounds.values()) >= 4
