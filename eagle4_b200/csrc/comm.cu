@@ -11,8 +11,8 @@
 //   calls   local call counter; its low bit selects the buffer half of the call, calls + 1 is the call's tag
 // Consecutive calls alternate halves, so a rank may run one call ahead of a slower peer without overwriting data the
 // peer still reads: a rank cannot finish call n + 1 (and so start writing call n + 2) before every rank has written
-// its call n + 1 data, which each does only after finishing call n. Every wait is bounded (2 s) and records
-// kErrTimeoutPeer instead of spinning forever.
+// its call n + 1 data, which each does only after finishing call n. A launch's waits share one 1 s deadline per thread; past it the
+// kernel records kErrTimeoutPeer and finishes with what it has (zeros for missing partials) instead of spinning.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -48,12 +48,15 @@ E4_DEV void st_volatile_v2(void* p, unsigned a, unsigned b) {
   asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(a), "r"(b) : "memory");
 }
 
-// Re-reads two consecutive (value, tag) pairs until both carry ``tag``; false (v unchanged) after the time limit.
-E4_DEV bool settle(const uint2* p, unsigned tag, uint4& v) {
+constexpr uint64_t kPeerWaitNs = 1000000000ull;  // 1 s: one deadline for all of a thread's waits in a launch
+
+// Re-reads two consecutive (value, tag) pairs until both carry ``tag``; false (v unchanged) once the thread's
+// deadline has passed. ``deadline`` is 0 until the first wait of the launch sets it.
+E4_DEV bool settle(const uint2* p, unsigned tag, uint4& v, uint64_t& deadline) {
   if (v.y == tag && v.w == tag) return true;
-  const uint64_t t0 = globaltimer();
+  if (deadline == 0) deadline = globaltimer() + kPeerWaitNs;
   do {
-    if (globaltimer() - t0 > kWaitLimitNs) return false;
+    if (globaltimer() > deadline) return false;
     v = ld_volatile_v4(p);
   } while (v.y != tag || v.w != tag);
   return true;
@@ -81,6 +84,7 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_residual_norm_kernel(
 #pragma unroll
   for (int i = 0; i < G; ++i) sum[i] = make_float2(0.f, 0.f);
   bool ok = true;
+  uint64_t deadline = 0;
 #pragma unroll
   for (int b0 = 0; b0 < kLoads; b0 += kBatch) {
     uint4 v[kBatch];
@@ -93,7 +97,10 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_residual_norm_kernel(
     for (int k = 0; k < kBatch; ++k) {
       const int i = (b0 + k) / W, r = (b0 + k) % W, c = threadIdx.x + i * kReduceThreads;
       if (b0 + k < kLoads && c * 2 < N) {
-        ok &= settle(base + size_t(r) * slot_stride + 2 * c, tag, v[k]);
+        if (!settle(base + size_t(r) * slot_stride + 2 * c, tag, v[k], deadline)) {
+          ok = false;
+          v[k] = make_uint4(0u, 0u, 0u, 0u);  // a missing partial counts as zero
+        }
         sum[i].x += __uint_as_float(v[k].x);
         sum[i].y += __uint_as_float(v[k].z);
       }
@@ -165,6 +172,7 @@ __global__ void __launch_bounds__(256) argmax_exchange_kernel(
     }
   }
   bool ok = true;
+  uint64_t deadline = 0;
   const uint2* local = peers.xbuf[rank];
   for (int j = threadIdx.x; j < T; j += blockDim.x) {
     uint4 e[kMaxRanks];
@@ -176,7 +184,10 @@ __global__ void __launch_bounds__(256) argmax_exchange_kernel(
 #pragma unroll
     for (int r = 0; r < kMaxRanks; ++r) {
       if (r >= world) break;
-      ok &= settle(local + 2 * ((size_t(half) * kMaxRanks + r) * max_rows + j), tag, e[r]);
+      if (!settle(local + 2 * ((size_t(half) * kMaxRanks + r) * max_rows + j), tag, e[r], deadline)) {
+        ok = false;
+        continue;  // a rank that never answered offers no candidate
+      }
       const float x = __uint_as_float(e[r].x);
       const int i = int(e[r].z);
       if (x > best || (x == best && i < bi)) { best = x; bi = i; }
