@@ -191,6 +191,7 @@ class Engine:
         self.pool = torch.cuda.graph_pool_handle() if self.use_graphs else None
         self.graph_launches: Dict[tuple, int] = {}
         self.stats = RoundStats()
+        self.recorder = None  # a runtime.recorder.RoundRecorder to keep per-round records
         if self.tree is not None:
             self.host_deltas = torch.zeros(tuple(self.tree.deltas.shape), dtype=torch.float32, pin_memory=pin)
             self.host_scores = torch.zeros(n, dtype=torch.float32, pin_memory=pin)
@@ -455,7 +456,12 @@ class Engine:
         and is then captured into a CUDA graph that later calls replay."""
         g = self.graphs.get(key)
         if g is not None:
-            g.replay()
+            if self.device.type == "cuda":
+                torch.cuda.nvtx.range_push(f"e4.{key[0]}")
+                g.replay()
+                torch.cuda.nvtx.range_pop()
+            else:
+                g.replay()
             _count_launches(self.graph_launches[key])
             return
         fn(*args)
@@ -601,6 +607,13 @@ class Engine:
                 got.append(take)
             if spec:
                 self.stats.record(got)
+            if self.recorder is not None:
+                kind = "plain" if not spec else ("native" if choice == ServedTreeChoice.NATIVE else
+                                                 ("chain" if chain_t0 is not None else "tree"))
+                t_us = tree_t0.elapsed_us(tree_t1) if tree_t0 is not None else (
+                    chain_t0.elapsed_us(chain_t1) if chain_t0 is not None else None)
+                self.recorder.record(bs=bs, kind=kind, depth=self.last_depth if spec else 0,
+                                     width=self.last_width if spec else 1, tokens=got, round_us=t_us)
             if tree_t0 is not None:
                 us = tree_t0.elapsed_us(tree_t1)
                 if self.target.tp is not None:

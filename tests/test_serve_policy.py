@@ -122,3 +122,20 @@ def test_serve_mode_mixes_native_and_speculative_rounds_exactly():
     b = llm.generate(p, 20, speculative=False)
     assert torch.equal(a, b)
     assert sum(llm.engine.tree_choice.rounds.values()) >= 4
+
+
+def test_round_recorder_writes_jsonl(tmp_path):
+    import json
+
+    import torch
+
+    from eagle4_b200.api import LLM, TreeSpec
+    from eagle4_b200.runtime.recorder import RoundRecorder
+
+    llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_len=256)
+    llm.engine.recorder = RoundRecorder(str(tmp_path / "rounds.jsonl"), flush_every=1)
+    p = torch.randint(0, 4096, (1, 16), generator=torch.Generator().manual_seed(0))
+    llm.generate(p, 8)
+    recs = [json.loads(l) for l in open(tmp_path / "rounds.jsonl")]
+    assert recs and recs[0]["kind"] == "tree" and recs[0]["width"] >= 1
+    assert llm.engine.recorder.summary()["rounds"] == len(recs)
