@@ -25,6 +25,11 @@ import sys
 import threading
 import time
 
+MODEL_NAMES = {
+    "qwen3.8-27b": "Qwen3.8-27B-shaped hybrid (64 layers, 3 GDN:1 attention) + 1-layer EAGLE-4 draft",
+    "nemotron-h-8b": "Nemotron-H-style Mamba2/attention hybrid (52 layers) + 1-layer EAGLE-4 draft",
+    "llama-3.1-8b": "Llama-3.1-8B-shaped dense target + 1-layer EAGLE-3 draft (32000-token draft vocabulary)",
+}
 BASELINE_TPS = 302.7  # SGLang TP1, one request, EAGLE-4 tokens/s on 1x B300 (reference docs/support-matrix.md:258-259)
 METRIC = "EAGLE-4 output tok/s and speedup vs plain decode, batch 1–512, TP 1/2/4/8"
 
@@ -85,6 +90,8 @@ def main() -> None:
     ap.add_argument("--new-tokens", type=int, default=256)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-plain", action="store_true", help="skip the plain-decode arm")
+    ap.add_argument("--tree", default="12,4,16", help="steps,top_k,draft_tokens")
+    ap.add_argument("--temperature", type=float, default=0.0, help="> 0: sampled trees (tree rejection)")
     ap.add_argument("--parallelism", default="tp", choices=["tp", "dp"])
     ap.add_argument("--tp-backend", default="fused", choices=["fused", "torch"])
     ap.add_argument("--mode", default="serve", choices=["serve", "static"],
@@ -121,9 +128,10 @@ def main() -> None:
 
         tp = TensorParallel(backend=args.tp_backend, max_rows=max(256, args.prompt), max_cols=8192, device=dev)
     replicas = 1 if tp_mode else world  # independent request streams
-    tree = TreeSpec(12, 4, 16)
+    tree = TreeSpec(*(int(v) for v in args.tree.split(",")))
     llm = LLM.synthetic(args.model, device=dev, seed=0, tree=tree, max_batch=args.batch,
-                        max_len=args.prompt + args.new_tokens + 64, config=json.dumps({"mode": args.mode}), tp=tp)
+                        max_len=args.prompt + args.new_tokens + 64, config=json.dumps({"mode": args.mode}), tp=tp,
+                        temperature=args.temperature, sample_seed=7)
     gen = torch.Generator().manual_seed(1234 + (0 if tp_mode else rank))
     prompts = torch.randint(0, llm.target.cfg.vocab_size, (args.batch, args.prompt), generator=gen).pin_memory()
     eng = llm.engine
@@ -162,7 +170,7 @@ def main() -> None:
     plain_ms = plain_tok = None
     if not args.no_plain:
         plain_ms, plain_tok, _, _, _, plain_out = device_timed(False)
-        same = plain_out[0] == spec_out[0]
+        same = plain_out[0] == spec_out[0] if args.temperature == 0 else None  # sampled: distributions, not ids
     else:
         same = None
 
@@ -194,7 +202,8 @@ def main() -> None:
         "dtype": "bf16",
         "data": "synthetic: uniform-random prompt ids, random-init N(0,0.02) weights of the named shapes",
         "config": {
-            "model": "Qwen3.8-27B-shaped hybrid (64 layers, 3 GDN:1 attention) + 1-layer EAGLE-4 draft",
+            "model": MODEL_NAMES.get(args.model, args.model),
+            "temperature": args.temperature,
             "global_batch": args.batch * replicas, "seq_len": args.prompt, "new_tokens": args.new_tokens,
             "tree": {"steps": tree.steps, "top_k": tree.top_k, "draft_tokens": tree.draft_tokens,
                      "mode": args.mode, "last_round_depth": eng.last_depth, "last_round_width": eng.last_width},
