@@ -18,7 +18,7 @@ def test_reduce_without_partials_times_out_and_reports():
     dev = torch.device("cuda")
     n, rows = 1024, 2
     slot = rows * n
-    base = C.sym_alloc(4096 + 2 * slot * 8, dev.index)  # zeroed: no pair carries this call's tag
+    base = C.sym_alloc(4096 + 2 * slot * 8, torch.cuda.current_device())  # zeroed: no pair carries this tag
     try:
         err = torch.zeros(1, dtype=torch.int32, device=dev)
         res = torch.randn(rows, n, device=dev).to(torch.bfloat16)
