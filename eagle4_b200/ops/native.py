@@ -35,6 +35,10 @@ class _Counted:
 
 
 LAUNCHES = [0]
+if torch.cuda.is_available():  # refuse a GPU the sm_100a kernels cannot run on, with the reason
+    from eagle4_b200.utils.arch import require_sm100
+
+    require_sm100()
 _C = _Counted(load())
 
 EPI_PLAIN, EPI_RESIDUAL, EPI_SWIGLU, EPI_RELU2, EPI_F32, EPI_ARGMAX = range(6)

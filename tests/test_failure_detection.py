@@ -73,3 +73,18 @@ def test_cost_tables_of_another_setup_are_refused(tmp_path):
     write_key(str(tmp_path), CostKey("NVIDIA H100", 1, "m", "d", "eagle4_b200", "bfloat16"))
     with pytest.raises(ValueError):
         check_key(str(tmp_path), CostKey("NVIDIA B200", 1, "m", "d", "eagle4_b200", "bfloat16"))
+
+
+def test_unsupported_gpu_is_refused(monkeypatch):
+    import torch
+
+    from eagle4_b200.utils import arch
+
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: True)
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 0)
+    monkeypatch.setattr(torch.cuda, "get_device_capability", lambda d=None: (9, 0))
+    monkeypatch.setattr(torch.cuda, "get_device_name", lambda d=None: "NVIDIA H100")
+    with pytest.raises(arch.UnsupportedDevice, match="sm_90"):
+        arch.require_sm100()
+    monkeypatch.setattr(torch.cuda, "get_device_capability", lambda d=None: (10, 0))
+    arch.require_sm100()
