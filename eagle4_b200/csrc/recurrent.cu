@@ -279,6 +279,112 @@ __global__ void __launch_bounds__(128) gdn_kernel(GdnArgs a, const int* __restri
   if (v < a.V) save_state<K>(S, stp);
 }
 
+// Scan mode (prefill chains) with the value dimension split over CTAs: the delta rule's value rows are independent
+// (S[v, :] only meets v's own value), so CTA (head, v-slice) runs one warp over kScanV value columns of one head and
+// writes the raw output o (bf16); the gated RMSNorm over the head's V values follows as its own kernel. One warp per
+// CTA: the staging of kGdnTile tokens and the token loop need no block barrier, and 4x more CTAs share the work.
+constexpr int kScanV = 32;
+template <int K>
+struct ScanStage {
+  float q[kGdnTile][K];
+  float k[kGdnTile][K];
+  float v[kGdnTile][kScanV];
+  float g[kGdnTile], beta[kGdnTile];
+};
+
+template <int K>
+__global__ void __launch_bounds__(32) gdn_scan_kernel(GdnArgs a, const int* __restrict__ slot,
+                                                      const int* __restrict__ seg, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ __align__(16) uint8_t scan_smem[];
+  ScanStage<K>& st = *reinterpret_cast<ScanStage<K>*>(scan_smem);
+  const int h = blockIdx.x, vs = blockIdx.z * kScanV;
+  const int lane = threadIdx.x;
+  const int kh = h / (a.HV / a.HK);
+  const int v = vs + lane;
+  const int vc = min(v, a.V - 1);
+  constexpr int PL = K / 32;
+  const int r0 = seg[blockIdx.y], r1 = seg[blockIdx.y + 1];
+  float* stp = a.state + ((size_t(slot[r0]) * a.HV + h) * a.V + vc) * K;
+  float S[K];
+  load_state<K>(S, stp);
+  for (int p0 = r0; p0 < r1; p0 += kGdnTile) {
+    const int n = min(kGdnTile, r1 - p0);
+    __syncwarp();
+    // stage raw q and k of the tile's tokens with independent 16-byte loads (one memory latency for the tile), this
+    // slice's v and the gates (lane j: token j), then l2-normalise q (scaled by K^-1/2) and k token by token
+    constexpr int VEC = K / 8;  // 16-byte vectors per head row
+    for (int e = lane; e < n * 2 * VEC; e += 32) {
+      const int j = e / (2 * VEC), w = e % (2 * VEC), which = w / VEC, c = w % VEC;
+      const __nv_bfloat16* base = a.qkv + size_t(p0 + j) * a.ldq + (which ? a.HK * K : 0) + kh * K;
+      const uint4 raw = reinterpret_cast<const uint4*>(base)[c];
+      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      float* dst = which ? &st.k[j][c * 8] : &st.q[j][c * 8];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 f = __bfloat1622float2(p2[t]);
+        dst[2 * t] = f.x;
+        dst[2 * t + 1] = f.y;
+      }
+    }
+    for (int j = 0; j < n; ++j) st.v[j][lane] = bf(a.qkv[size_t(p0 + j) * a.ldq + 2 * a.HK * K + h * a.V + vc]);
+    if (lane < n) {
+      const float2 gb = gdn_gate(a, p0 + lane, h);
+      st.g[lane] = gb.x;
+      st.beta[lane] = gb.y;
+    }
+    __syncwarp();
+    for (int j = 0; j < n; ++j) {
+      float q2 = 0.f, k2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < PL; ++i) {
+        const float qv = st.q[j][lane * PL + i], kv = st.k[j][lane * PL + i];
+        q2 = fmaf(qv, qv, q2);
+        k2 = fmaf(kv, kv, k2);
+      }
+      const float rq = rsqrtf(warp_sum(q2) + 1e-6f) * rsqrtf(float(K));
+      const float rk = rsqrtf(warp_sum(k2) + 1e-6f);
+#pragma unroll
+      for (int i = 0; i < PL; ++i) {
+        st.q[j][lane * PL + i] *= rq;
+        st.k[j][lane * PL + i] *= rk;
+      }
+    }
+    __syncwarp();
+    for (int j = 0; j < n; ++j) {
+      const float decay = __expf(st.g[j]);
+      float k0 = 0.f, k1 = 0.f, k2 = 0.f, k3 = 0.f;
+#pragma unroll
+      for (int i = 0; i < K; i += 4) {
+        S[i] *= decay;
+        S[i + 1] *= decay;
+        S[i + 2] *= decay;
+        S[i + 3] *= decay;
+        k0 = fmaf(S[i], st.k[j][i], k0);
+        k1 = fmaf(S[i + 1], st.k[j][i + 1], k1);
+        k2 = fmaf(S[i + 2], st.k[j][i + 2], k2);
+        k3 = fmaf(S[i + 3], st.k[j][i + 3], k3);
+      }
+      const float delta = (st.v[j][lane] - ((k0 + k1) + (k2 + k3))) * st.beta[j];
+      float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+#pragma unroll
+      for (int i = 0; i < K; i += 4) {
+        S[i] = fmaf(st.k[j][i], delta, S[i]);
+        S[i + 1] = fmaf(st.k[j][i + 1], delta, S[i + 1]);
+        S[i + 2] = fmaf(st.k[j][i + 2], delta, S[i + 2]);
+        S[i + 3] = fmaf(st.k[j][i + 3], delta, S[i + 3]);
+        o0 = fmaf(S[i], st.q[j][i], o0);
+        o1 = fmaf(S[i + 1], st.q[j][i + 1], o1);
+        o2 = fmaf(S[i + 2], st.q[j][i + 2], o2);
+        o3 = fmaf(S[i + 3], st.q[j][i + 3], o3);
+      }
+      if (v < a.V) out[(size_t(p0 + j) * a.HV + h) * a.V + v] = __float2bfloat16((o0 + o1) + (o2 + o3));
+    }
+  }
+  if (v < a.V) save_state<K>(S, stp);
+}
+
 // Per-layer pointers of an all-layers commit.
 struct GdnLayer {
   const __nv_bfloat16* qkv;   // post-conv rows
@@ -531,6 +637,8 @@ static GdnArgs gdn_args(const torch::Tensor& qkv, const torch::Tensor& proj, int
                  int(K), int(V)};
 }
 
+torch::Tensor gated_rmsnorm(const torch::Tensor& o, const torch::Tensor& z, const torch::Tensor& w, double eps);
+
 // Gated delta rule + gated RMSNorm over a forest of rows; returns [T, HV*V].
 torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int64_t z_off, int64_t b_off,
                        int64_t a_off, const torch::Tensor& a_log, const torch::Tensor& dt_bias, torch::Tensor state,
@@ -542,7 +650,26 @@ torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int6
   if (!T) return out;
   GdnArgs a = gdn_args(qkv, proj, z_off, b_off, a_off, a_log, dt_bias, state, HK, HV, K, V);
   auto sl = slot.to(torch::kInt32).contiguous(), pa = parent.to(torch::kInt32).contiguous();
-  torch::Tensor seg = scan ? segments_of(sl) : torch::zeros({1}, sl.options());
+  if (scan) {
+    // prefill: value-sliced scan into the raw output, then the gated RMSNorm (skipped for raw callers)
+    torch::Tensor seg = segments_of(sl);
+    dim3 grid(HV, seg.numel() - 1, (V + kScanV - 1) / kScanV);
+    auto st = at::cuda::getCurrentCUDAStream();
+    auto raw = norm_w.numel() ? torch::empty({T, HV * V}, qkv.options()) : out;
+    if (K == 128) {
+      gdn_smem_attr(gdn_scan_kernel<128>, sizeof(ScanStage<128>));
+      C10_CUDA_CHECK(launch_pdl(gdn_scan_kernel<128>, grid, 32, sizeof(ScanStage<128>), st.stream(), a,
+                                sl.data_ptr<int>(), seg.data_ptr<int>(), BFP(raw)));
+    } else {
+      gdn_smem_attr(gdn_scan_kernel<64>, sizeof(ScanStage<64>));
+      C10_CUDA_CHECK(launch_pdl(gdn_scan_kernel<64>, grid, 32, sizeof(ScanStage<64>), st.stream(), a,
+                                sl.data_ptr<int>(), seg.data_ptr<int>(), BFP(raw)));
+    }
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    if (!norm_w.numel()) return out;
+    return gated_rmsnorm(raw.view({T, HV, V}), proj.narrow(1, z_off, HV * V), norm_w, eps);
+  }
+  torch::Tensor seg = torch::zeros({1}, sl.options());
   const int ny = scan ? seg.numel() - 1 : T;
   dim3 grid(HV, ny);
   auto st = at::cuda::getCurrentCUDAStream();
