@@ -78,29 +78,37 @@ attn_chunk_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __re
   if (live) {
     const uint4* kp = reinterpret_cast<const uint4*>(kc + (size_t(slot) * Hk + h) * D);
     const float4* q4 = reinterpret_cast<const float4*>(sq);
-#pragma unroll 2
-    for (int c = 0; c < D / 8; ++c) {
-      const uint4 raw = kp[c];
-      const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-      float kf[8];
+    // kKB 16-byte pieces of the key are requested before any is used (independent loads in flight), then consumed
+    // in dimension order: the dot product's summation order does not change.
+    constexpr int kKB = (D / 8) < 8 ? (D / 8) : 8;
+    for (int c0k = 0; c0k < D / 8; c0k += kKB) {
+      uint4 kr[kKB];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(k2[j]);
-        kf[2 * j] = f.x;
-        kf[2 * j + 1] = f.y;
-      }
+      for (int u = 0; u < kKB; ++u) kr[u] = kp[c0k + u];
 #pragma unroll
-      for (int g = 0; g < kMaxG; ++g) {
-        if (g < G) {
-          const float4 qa = q4[(g * D + c * 8) / 4], qb = q4[(g * D + c * 8) / 4 + 1];
-          s[g] = fmaf(qa.x, kf[0], s[g]);
-          s[g] = fmaf(qa.y, kf[1], s[g]);
-          s[g] = fmaf(qa.z, kf[2], s[g]);
-          s[g] = fmaf(qa.w, kf[3], s[g]);
-          s[g] = fmaf(qb.x, kf[4], s[g]);
-          s[g] = fmaf(qb.y, kf[5], s[g]);
-          s[g] = fmaf(qb.z, kf[6], s[g]);
-          s[g] = fmaf(qb.w, kf[7], s[g]);
+      for (int u = 0; u < kKB; ++u) {
+        const int c = c0k + u;
+        const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kr[u]);
+        float kf[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(k2[j]);
+          kf[2 * j] = f.x;
+          kf[2 * j + 1] = f.y;
+        }
+#pragma unroll
+        for (int g = 0; g < kMaxG; ++g) {
+          if (g < G) {
+            const float4 qa = q4[(g * D + c * 8) / 4], qb = q4[(g * D + c * 8) / 4 + 1];
+            s[g] = fmaf(qa.x, kf[0], s[g]);
+            s[g] = fmaf(qa.y, kf[1], s[g]);
+            s[g] = fmaf(qa.z, kf[2], s[g]);
+            s[g] = fmaf(qa.w, kf[3], s[g]);
+            s[g] = fmaf(qb.x, kf[4], s[g]);
+            s[g] = fmaf(qb.y, kf[5], s[g]);
+            s[g] = fmaf(qb.z, kf[6], s[g]);
+            s[g] = fmaf(qb.w, kf[7], s[g]);
+          }
         }
       }
     }
@@ -122,18 +130,43 @@ attn_chunk_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __re
 #pragma unroll
     for (int i = 0; i < DPL; ++i) acc[g][i] = 0.f;
   const int nlive = min(32, total - (k_begin + warp * 32));
-  for (int j = 0; j < nlive; ++j) {
-    const int64_t sj = __shfl_sync(0xffffffffu, slot, j);
-    const __nv_bfloat16* vp = vc + (size_t(sj) * Hk + h) * D + lane * DPL;
-    float vf[DPL];
+  // V rows of kVB keys are loaded together (independent loads in flight), then accumulated in key order.
+  constexpr int kVB = DPL == 8 ? 4 : 8;
+  for (int j0 = 0; j0 < nlive; j0 += kVB) {
+    float vf[kVB][DPL];
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) vf[i] = __bfloat162float(vp[i]);
+    for (int u = 0; u < kVB; ++u) {
+      const int64_t sj = __shfl_sync(0xffffffffu, slot, (j0 + u) & 31);
+      if (j0 + u < nlive) {
+        const __nv_bfloat16* vp = vc + (size_t(sj) * Hk + h) * D + lane * DPL;
+        if constexpr (DPL == 8) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(vp);
+          const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-    for (int g = 0; g < kMaxG; ++g) {
-      if (g >= G) break;
-      const float pj = __shfl_sync(0xffffffffu, p[g], j);
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(v2[i]);
+            vf[u][2 * i] = f.x;
+            vf[u][2 * i + 1] = f.y;
+          }
+        } else {
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) acc[g][i] = fmaf(pj, vf[i], acc[g][i]);
+          for (int i = 0; i < DPL; ++i) vf[u][i] = __bfloat162float(vp[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) vf[u][i] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kVB; ++u) {
+      if (j0 + u >= nlive) break;
+#pragma unroll
+      for (int g = 0; g < kMaxG; ++g) {
+        if (g >= G) break;
+        const float pj = __shfl_sync(0xffffffffu, p[g], j0 + u);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[g][i] = fmaf(pj, vf[u][i], acc[g][i]);
+      }
     }
   }
 #pragma unroll
