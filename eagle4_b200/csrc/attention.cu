@@ -15,6 +15,8 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <unordered_map>
+
 #include "common.cuh"
 
 namespace e4 {
@@ -24,6 +26,77 @@ constexpr int kChunk = 128;   // logical keys per CTA: 4 warps x 32 keys
 constexpr int kWarps = 4;
 constexpr int kMaxG = 8;      // query heads per kv head handled by one CTA
 constexpr int kMaxDPL = 8;    // head dims per lane (D <= 256)
+
+// Chunk partial layout: [rows * Hq][nchunks][D + 4] floats: the D accumulators, then the chunk's max and sum (the
+// stride keeps every partial 16-byte aligned).
+E4_DEV int part_stride(int D) { return D + 4; }
+
+// Merges ``nheads`` query heads (from ``qh0``) of row ``r`` over their first ``nlc`` chunk partials in chunk order,
+// normalises, applies the optional output gate (``out *= sigmoid(gate)``) and writes bf16 outputs. ``w_s`` holds
+// 2 * nheads * nlc floats and ``l_s`` nheads floats of shared memory. Partials are read through L2 (other CTAs wrote
+// them); the per-chunk weights are computed once per head, and the accumulators' loads are issued 8 chunks at a time.
+E4_DEV void merge_heads(const float* ws, int nchunks, int nlc, int D, int Hq, int r, int qh0, int nheads,
+                        const __nv_bfloat16* gate, int ldg, __nv_bfloat16* out, float* w_s, float* l_s) {
+  const int DS = part_stride(D);
+  const size_t rh0 = size_t(r) * Hq + qh0;
+  float* m_s = w_s + nheads * nlc;
+  for (int i = threadIdx.x; i < nheads * nlc; i += blockDim.x) {
+    const int g = i / nlc, c = i % nlc;
+    const float* o = ws + ((rh0 + g) * nchunks + c) * DS + D;
+    m_s[i] = __ldcg(o);
+    w_s[i] = __ldcg(o + 1);  // the chunk's sum for now
+  }
+  __syncthreads();
+  for (int g = threadIdx.x; g < nheads; g += blockDim.x) {
+    float M = -INFINITY;
+    for (int c = 0; c < nlc; ++c) M = fmaxf(M, m_s[g * nlc + c]);
+    float L = 0.f;
+    for (int c = 0; c < nlc; ++c) {
+      const float mc = m_s[g * nlc + c];
+      const float w = mc == -INFINITY ? 0.f : __expf(mc - M);
+      L += w_s[g * nlc + c] * w;
+      w_s[g * nlc + c] = w;
+    }
+    l_s[g] = L;
+  }
+  __syncthreads();
+  const int D4 = D / 4;
+  for (int it = threadIdx.x; it < nheads * D4; it += blockDim.x) {
+    const int g = it / D4, d4 = it % D4;
+    const float* base = ws + (rh0 + g) * nchunks * DS + 4 * d4;
+    float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c0 = 0; c0 < nlc; c0 += 8) {
+      float4 o[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        o[u] = c0 + u < nlc ? __ldcg(reinterpret_cast<const float4*>(base + size_t(c0 + u) * DS))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (c0 + u >= nlc) break;
+        const float w = w_s[g * nlc + c0 + u];
+        if (w == 0.f) continue;  // empty chunk (its accumulators were never written)
+        A.x = fmaf(o[u].x, w, A.x);
+        A.y = fmaf(o[u].y, w, A.y);
+        A.z = fmaf(o[u].z, w, A.z);
+        A.w = fmaf(o[u].w, w, A.w);
+      }
+    }
+    const float L = l_s[g];
+    float v[4] = {A.x, A.y, A.z, A.w};
+    const size_t rh = rh0 + g;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int d = 4 * d4 + k;
+      float x = L > 0.f ? v[k] / L : 0.f;
+      if (gate) {
+        x = __bfloat162float(__float2bfloat16(x));
+        x *= sigmoidf_(__bfloat162float(gate[size_t(r) * ldg + (qh0 + g) * D + d]));
+      }
+      out[rh * D + d] = __float2bfloat16(x);
+    }
+  }
+}
 
 // One CTA per (chunk, kv head, row). Lane l of warp w scores logical key chunk*128 + w*32 + l against the G query
 // heads (a sequential dot product over D), the warp takes the softmax statistics of its 32 keys, then every lane
@@ -50,7 +123,7 @@ attn_chunk_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __re
   __shared__ float sm_acc[kWarps][kMaxG][D];
   if (k_begin >= total) {
     for (int g = threadIdx.x; g < G; g += blockDim.x) {
-      float* o = ws + ((size_t(r) * Hq + h * G + g) * nchunks + chunk) * (D + 2);
+      float* o = ws + ((size_t(r) * Hq + h * G + g) * nchunks + chunk) * part_stride(D);
       o[D] = -INFINITY;
       o[D + 1] = 0.f;
     }
@@ -192,7 +265,7 @@ attn_chunk_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __re
       L += sm_l[w][g] * c;
       A += sm_acc[w][g][d] * c;
     }
-    float* o = ws + ((size_t(r) * Hq + h * G + g) * nchunks + chunk) * (D + 2);
+    float* o = ws + ((size_t(r) * Hq + h * G + g) * nchunks + chunk) * part_stride(D);
     o[d] = A;
     if (d == 0) {
       o[D] = M;
@@ -201,36 +274,264 @@ attn_chunk_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __re
   }
 }
 
-// Merge a row's chunks in chunk order and normalise: one block per (row, qhead). With ``gate`` the output is
-// multiplied by sigmoid(gate) (the gated-attention output gate), saving a separate pass.
-__global__ void attn_merge_kernel(const float* __restrict__ ws, int nchunks, int D, int Hq,
-                                  const __nv_bfloat16* __restrict__ gate, int ldg, __nv_bfloat16* __restrict__ out) {
-  pdl_wait();
-  pdl_trigger();
-  const size_t rh = blockIdx.x;
-  const float* base = ws + rh * nchunks * (D + 2);
-  float M = -INFINITY;
-  for (int c = 0; c < nchunks; ++c) M = fmaxf(M, base[size_t(c) * (D + 2) + D]);
-  const size_t r = rh / Hq, hh = rh % Hq;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float L = 0.f, A = 0.f;
-    for (int c = 0; c < nchunks; ++c) {
-      const float* o = base + size_t(c) * (D + 2);
-      const float mc = o[D];
-      if (mc == -INFINITY) continue;
-      const float w = __expf(mc - M);
-      L += o[D + 1] * w;
-      A += o[d] * w;
-    }
-    float v = L > 0.f ? A / L : 0.f;
-    if (gate) {
-      v = __bfloat162float(__float2bfloat16(v));
-      v *= sigmoidf_(__bfloat162float(gate[r * ldg + hh * D + d]));
-    }
-    out[rh * D + d] = __float2bfloat16(v);
-  }
+// ------------------------------------------------------------------------------------------------------------------
+// Tensor-core chunk kernel (head dims 128 and 256). One CTA per (chunk, kv head, row), 4 warps:
+//   1. the 128 keys' cache slots are resolved (thread t: key t), and each warp copies its 32 keys' K and V rows into
+//      shared memory with 16-byte asynchronous copies, straight into the 128-byte-swizzled UMMA layouts (dead keys
+//      are zero rows); the G query heads go into a 16-row tile (rows G..15 zero);
+//   2. S^T[key, head] = K . Q^T: M = 128 keys, N = 16, K = D (tcgen05.mma, accumulator in TMEM, one thread issues);
+//   3. thread t reads key t's 16 scores from TMEM; the chunk's softmax statistics per head (max over the 4 warps in
+//      warp order, sum of exp in warp order); P = exp(S - max) is written as bf16 into a K-major tile;
+//   4. O^T[d, head] = V^T . P^T: M = 128 head dims per instruction (V read as an MN-major operand), N = 16,
+//      K = 128 keys; thread t reads its head dim's 16 outputs and writes the chunk partial;
+//   5. the last CTA of (row, kv head) merges the chunks (as in the CUDA-core path).
+// The score of a key and its weight in the output depend on that key alone (fixed instruction shapes; the logical
+// chunk layout is the same for every batch), so a decoded token and the same token verified in a tree get
+// identical outputs.
+template <int DPL>
+constexpr int tc_smem_bytes() {
+  return 2 * (DPL * 32) * 256 + (DPL * 32 / 64) * 2048 + 2 * 2048 + 1024;  // K, V, Q, P tiles + alignment slack
 }
 
+E4_DEV uint64_t sdesc_sw128_mn(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr & 0x3FFFFu) >> 4);
+  d |= uint64_t((lbo >> 4) & 0x3FFFu) << 16;
+  d |= uint64_t((sbo >> 4) & 0x3FFFu) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(2) << 61;
+  return d;
+}
+
+E4_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+template <int DPL>
+__global__ void __launch_bounds__(kWarps * 32)
+attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
+               const __nv_bfloat16* __restrict__ vc, const int* __restrict__ bt, int bt_ld, int page,
+               const int* __restrict__ req, const int* __restrict__ ctx_start, const int* __restrict__ ctx_len,
+               const int* __restrict__ extra, int extra_ld, const int* __restrict__ n_extra, float scale, int Hq, int Hk,
+               int nchunks, float* __restrict__ ws, int* __restrict__ counters, const __nv_bfloat16* __restrict__ gate,
+               int ldg, __nv_bfloat16* __restrict__ out, int* __restrict__ err) {
+  constexpr int D = DPL * 32;
+  constexpr int KB = D / 64;         // 64-element blocks of the head dim
+  constexpr int kTile = 128 * 128;   // bytes of one 64-element block of 128 key rows
+  constexpr int NQ = 16;             // query columns per instruction (G padded)
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ uint64_t mma_bar;
+  __shared__ uint32_t tmem_holder;
+  __shared__ float red_m[kWarps][kMaxG], red_l[kWarps][kMaxG];
+  __shared__ int s_last;
+  unsigned char* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  unsigned char* Kt = smem;                    // [KB][128 keys][128 B], K-major SW128
+  unsigned char* Vt = smem + D * 256;          // [D/64 atoms][16 key groups][1024 B], MN-major SW128
+  unsigned char* Qt = smem + 2 * D * 256;      // [KB][16 heads][128 B], K-major SW128
+  unsigned char* Pt = Qt + KB * 2048;          // [2][16 heads][128 B] (keys 0-63, 64-127), K-major SW128
+  pdl_wait();
+  pdl_trigger();
+  const int chunk = blockIdx.x, h = blockIdx.y, r = blockIdx.z;
+  const int G = Hq / Hk;
+  const int c0 = ctx_start[r], c1 = ctx_len[r], ne = n_extra[r];
+  const int nctx = max(c1 - c0, 0);
+  const int total = nctx + ne;
+  const int nlc = min(max((total + kChunk - 1) / kChunk, 1), nchunks);
+  if (chunk >= nlc) {
+    if (counters == nullptr) {
+      for (int g = threadIdx.x; g < G; g += blockDim.x) {
+        float* o = ws + ((size_t(r) * Hq + h * G + g) * nchunks + chunk) * part_stride(D);
+        o[D] = -INFINITY;
+        o[D + 1] = 0.f;
+      }
+    }
+    return;
+  }
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int k_begin = chunk * kChunk;
+  const int nk = max(0, min(kChunk, total - k_begin));
+  if (warp == 0) tmem_alloc(&tmem_holder, 64);
+  if (tid == 32) {
+    mbar_init(&mma_bar, 1);
+    mbar_fence_init();
+  }
+  // key tid's cache slot
+  const int b = req[r];
+  const bool live = tid < nk;
+  int64_t slot = 0;
+  if (live) {
+    const int kk = k_begin + tid;
+    if (kk < nctx) {
+      const int p = c0 + kk;
+      slot = int64_t(bt[size_t(b) * bt_ld + p / page]) * page + p % page;
+    } else {
+      slot = extra[size_t(r) * extra_ld + (kk - nctx)];
+    }
+  }
+  // K and V rows of the warp's keys: LPR lanes per row (16-byte pieces), RPI rows per pass
+  {
+    constexpr int LPR = D / 8, RPI = 32 / LPR;
+    const int piece = lane % LPR;
+    for (int j0 = 0; j0 < 32; j0 += RPI) {
+      const int j = j0 + lane / LPR, key = warp * 32 + j;
+      const int64_t sj = __shfl_sync(0xffffffffu, slot, j);
+      const uint32_t off = uint32_t(piece / 8) * kTile + uint32_t(key) * 128 + uint32_t(((piece & 7) ^ (key & 7)) * 16);
+      if (key < nk) {
+        const size_t src = (size_t(sj) * Hk + h) * D + piece * 8;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(Kt + off)), "l"(kc + src) : "memory");
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(Vt + off)), "l"(vc + src) : "memory");
+      } else {
+        *reinterpret_cast<uint4*>(Kt + off) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(Vt + off) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  // query tile: row g = query head h*G + g (bf16 as stored; the scale is applied to the scores)
+  {
+    const uint4* q4 = reinterpret_cast<const uint4*>(q + (size_t(r) * Hq + h * G) * D);
+    for (int i = tid; i < NQ * (D / 8); i += blockDim.x) {
+      const int g = i / (D / 8), piece = i % (D / 8);
+      const uint4 v = g < G ? q4[g * (D / 8) + piece] : make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(Qt + (piece / 8) * 2048 + g * 128 + ((piece & 7) ^ (g & 7)) * 16) = v;
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  fence_async_smem();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_holder;
+  const uint32_t id_s = idesc_bf16_f32(128, NQ);
+  if (tid == 0) {
+#pragma unroll
+    for (int kb = 0; kb < KB; ++kb)
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma_bf16(tmem, sdesc_sw128(smem_u32(Kt + kb * kTile + ks * 32)), sdesc_sw128(smem_u32(Qt + kb * 2048 + ks * 32)),
+                  id_s, (kb | ks) != 0);
+    umma_commit(&mma_bar);
+  }
+  if (!mbar_wait(&mma_bar, 0)) record_error(err, kErrTimeoutMma);
+  tc_fence_after();
+  float sv[NQ];
+  tmem_ld16(tmem + (uint32_t(warp * 32) << 16), sv);
+  // chunk softmax statistics per head
+#pragma unroll
+  for (int g = 0; g < kMaxG; ++g) {
+    if (g >= G) break;
+    sv[g] = live ? sv[g] * scale : -INFINITY;
+    const float m = warp_max(sv[g]);
+    if (lane == 0) red_m[warp][g] = m;
+  }
+  __syncthreads();
+  float pv[NQ];
+#pragma unroll
+  for (int g = 0; g < NQ; ++g) pv[g] = 0.f;
+#pragma unroll
+  for (int g = 0; g < kMaxG; ++g) {
+    if (g >= G) break;
+    float M = red_m[0][g];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) M = fmaxf(M, red_m[w][g]);
+    pv[g] = (live && M != -INFINITY) ? __expf(sv[g] - M) : 0.f;
+    const float l = warp_sum(pv[g]);
+    if (lane == 0) red_l[warp][g] = l;
+  }
+  // P^T tile: row g holds head g's weights of the 128 keys (two 64-key blocks)
+  {
+    const int blk = tid / 64, chunk16 = (tid % 64) / 8, e = tid % 8;
+#pragma unroll
+    for (int g = 0; g < NQ; ++g)
+      *reinterpret_cast<__nv_bfloat16*>(Pt + blk * 2048 + g * 128 + ((chunk16 ^ (g & 7)) * 16) + e * 2) =
+          __float2bfloat16(pv[g]);
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t id_o = idesc_bf16_f32(128, NQ) | (1u << 15);  // A (V^T) MN-major
+  if (tid == 0) {
+#pragma unroll
+    for (int half = 0; half < D / 128; ++half)
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_bf16(tmem + NQ + half * NQ, sdesc_sw128_mn(smem_u32(Vt + half * 2 * kTile + ks * 2048), kTile, 1024),
+                  sdesc_sw128(smem_u32(Pt + (ks / 4) * 2048 + (ks % 4) * 32)), id_o, ks != 0);
+    umma_commit(&mma_bar);
+  }
+  if (!mbar_wait(&mma_bar, 1)) record_error(err, kErrTimeoutMma);
+  tc_fence_after();
+#pragma unroll
+  for (int half = 0; half < D / 128; ++half) {
+    float ov[NQ];
+    tmem_ld16(tmem + (uint32_t(warp * 32) << 16) + NQ + half * NQ, ov);
+    const int d = half * 128 + tid;
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g) {
+      if (g >= G) break;
+      ws[((size_t(r) * Hq + h * G + g) * nchunks + chunk) * part_stride(D) + d] = ov[g];
+    }
+  }
+  if (tid < G) {
+    float M = red_m[0][tid], L = 0.f;
+    for (int w = 1; w < kWarps; ++w) M = fmaxf(M, red_m[w][tid]);
+    for (int w = 0; w < kWarps; ++w) L += red_l[w][tid];
+    float* o = ws + ((size_t(r) * Hq + h * G + tid) * nchunks + chunk) * part_stride(D);
+    o[D] = M;
+    o[D + 1] = L;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 64);
+  }
+  if (counters == nullptr) return;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int prev = atomicAdd(counters + size_t(r) * Hk + h, 1);
+    s_last = prev == nlc - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  float* w_s = reinterpret_cast<float*>(Kt);
+  merge_heads(ws, nchunks, nlc, D, Hq, r, h * G, G, gate, ldg, out, w_s, w_s + 2 * G * nlc);
+  if (tid == 0) counters[size_t(r) * Hk + h] = 0;
+}
+
+// Merge kernel for launches without the fused merge: one block per (row, query head) over all ``nchunks`` chunks
+// (chunks past a row's keys hold an empty partial). Dynamic shared memory: (2 * nchunks + 1) floats.
+__global__ void attn_merge_kernel(const float* __restrict__ ws, int nchunks, int D, int Hq,
+                                  const __nv_bfloat16* __restrict__ gate, int ldg, __nv_bfloat16* __restrict__ out) {
+  extern __shared__ float msm[];
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x / Hq, qh = blockIdx.x % Hq;
+  merge_heads(ws, nchunks, nchunks, D, Hq, r, qh, 1, gate, ldg, out, msm, msm + 2 * nchunks);
+}
+
+}  // namespace
+
+torch::Tensor gemm_error_word(torch::Device dev);
+
+namespace {
+// Per-device arrival counters of the fused chunk merge: allocated zeroed on the first (eager) call, kept for the
+// process, and left at zero by every launch. nullptr when ``need`` exceeds them or when they would first be
+// allocated inside a stream capture (the caller then merges with attn_merge_kernel).
+int* arrival_counters(torch::Device dev, int64_t need) {
+  constexpr int64_t kCap = int64_t(1) << 20;
+  static std::unordered_map<int, torch::Tensor> per_dev;
+  if (need > kCap) return nullptr;
+  auto it = per_dev.find(dev.index());
+  if (it == per_dev.end()) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    C10_CUDA_CHECK(cudaStreamIsCapturing(at::cuda::getCurrentCUDAStream().stream(), &st));
+    if (st != cudaStreamCaptureStatusNone) return nullptr;
+    it = per_dev.emplace(dev.index(), torch::zeros({kCap}, torch::TensorOptions().device(dev).dtype(torch::kInt32)))
+             .first;
+  }
+  return it->second.data_ptr<int>();
+}
 }  // namespace
 
 // q [T, Hq, D] bf16; caches [slots, Hk, D]; returns [T, Hq, D]. ``max_keys`` bounds every row's logical length.
@@ -246,31 +547,62 @@ torch::Tensor attention(const torch::Tensor& q, const torch::Tensor& kc, const t
   auto out = torch::empty_like(q);
   if (T == 0) return out;
   const int nchunks = std::max<int64_t>(1, (max_keys + kChunk - 1) / kChunk);
-  auto ws = torch::empty({int64_t(T) * Hq * nchunks * (D + 2)}, q.options().dtype(torch::kFloat32));
+  auto ws = torch::empty({int64_t(T) * Hq * nchunks * (D + 4)}, q.options().dtype(torch::kFloat32));
   auto i32 = [](const torch::Tensor& t) { return t.to(torch::kInt32).contiguous(); };
   auto bt_ = i32(bt), req_ = i32(req), cs = i32(ctx_start), cl = i32(ctx_len), ex = i32(extra), ne = i32(n_extra);
-  dim3 grid(nchunks, Hk, T);
-  auto stream = at::cuda::getCurrentCUDAStream();
-#define E4_ATTN(DPL)                                                                                              \
-  C10_CUDA_CHECK(launch_pdl(attn_chunk_kernel<DPL>, grid, kWarps * 32, 0, stream.stream(),                                                       \
-      reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(kc.data_ptr()), \
-      reinterpret_cast<const __nv_bfloat16*>(vc.data_ptr()), bt_.data_ptr<int>(), bt_.size(1), page,             \
-      req_.data_ptr<int>(), cs.data_ptr<int>(), cl.data_ptr<int>(), ex.data_ptr<int>(), ex.size(1),              \
-      ne.data_ptr<int>(), float(scale), Hq, Hk, nchunks, ws.data_ptr<float>()))
-  switch (D / 32) {
-    case 2: E4_ATTN(2); break;
-    case 4: E4_ATTN(4); break;
-    case 8: E4_ATTN(8); break;
-    default: TORCH_CHECK(false, "attention: head dim must be 64, 128 or 256");
-  }
-#undef E4_ATTN
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
   const __nv_bfloat16* gp = gate ? reinterpret_cast<const __nv_bfloat16*>(gate->data_ptr()) : nullptr;
   const int ldg = gate ? int(gate->stride(0)) : 0;
   if (gate) TORCH_CHECK(gate->stride(1) == 1 && gate->size(0) == T, "attention: gate must be [T, Hq*D] rows");
-  C10_CUDA_CHECK(launch_pdl(attn_merge_kernel, T * Hq, 128, 0, stream.stream(), ws.data_ptr<float>(), nchunks, D, Hq, gp, ldg,
-                                                reinterpret_cast<__nv_bfloat16*>(out.data_ptr())));
+  const int G = Hq / Hk;
+  dim3 grid(nchunks, Hk, T);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto bf = [](const torch::Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); };
+  __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  int* err = gemm_error_word(q.device()).data_ptr<int>();
+  const int dev = q.device().index();
+  TORCH_CHECK(dev >= 0 && dev < 64, "attention: device index");
+  int* counters = nullptr;
+  if (D >= 128) {
+    // tensor-core path; the chunk merge runs in the last CTA of each (row, kv head) when its statistics fit in the
+    // K tile (D * 256 bytes) and the arrival counters cover T * Hk
+    if ((2 * size_t(G) * nchunks + G) * sizeof(float) <= size_t(D) * 256)
+      counters = arrival_counters(q.device(), int64_t(T) * Hk);
+#define E4_ATTN_TC(DPL)                                                                                            \
+  {                                                                                                                \
+    static bool attr_set[64] = {};                                                                                 \
+    if (!attr_set[dev]) {                                                                                          \
+      C10_CUDA_CHECK(cudaFuncSetAttribute(attn_tc_kernel<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,        \
+                                          tc_smem_bytes<DPL>()));                                                  \
+      attr_set[dev] = true;                                                                                        \
+    }                                                                                                              \
+    C10_CUDA_CHECK(launch_pdl(attn_tc_kernel<DPL>, grid, kWarps * 32, tc_smem_bytes<DPL>(), stream.stream(), bf(q),  \
+                              bf(kc), bf(vc), bt_.data_ptr<int>(), int(bt_.size(1)), int(page), req_.data_ptr<int>(), \
+                              cs.data_ptr<int>(), cl.data_ptr<int>(), ex.data_ptr<int>(), int(ex.size(1)),         \
+                              ne.data_ptr<int>(), float(scale), Hq, Hk, nchunks, ws.data_ptr<float>(), counters,   \
+                              gp, ldg, op, err));                                                                  \
+  }
+    if (D == 128) E4_ATTN_TC(4) else if (D == 256) E4_ATTN_TC(8) else TORCH_CHECK(false, "attention: head dim must be 64, 128 or 256");
+#undef E4_ATTN_TC
+  } else {
+    TORCH_CHECK(D == 64, "attention: head dim must be 64, 128 or 256");
+    C10_CUDA_CHECK(launch_pdl(attn_chunk_kernel<2>, grid, kWarps * 32, 0, stream.stream(), bf(q), bf(kc), bf(vc),
+                              bt_.data_ptr<int>(), int(bt_.size(1)), int(page), req_.data_ptr<int>(),
+                              cs.data_ptr<int>(), cl.data_ptr<int>(), ex.data_ptr<int>(), int(ex.size(1)),
+                              ne.data_ptr<int>(), float(scale), Hq, Hk, nchunks, ws.data_ptr<float>()));
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (counters == nullptr) {
+    const size_t msmem = (2 * size_t(nchunks) + 1) * sizeof(float);
+    TORCH_CHECK(msmem <= 200 * 1024, "attention: too many key chunks to merge");
+    static bool merge_attr[64] = {};
+    if (msmem > 48 * 1024 && !merge_attr[dev]) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(attn_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+      merge_attr[dev] = true;
+    }
+    C10_CUDA_CHECK(launch_pdl(attn_merge_kernel, T * Hq, 128, msmem, stream.stream(), ws.data_ptr<float>(), nchunks,
+                              D, Hq, gp, ldg, op));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
   return out;
 }
 

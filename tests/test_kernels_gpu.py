@@ -107,8 +107,9 @@ def ref_rows_meta(prow):
     return rows_meta(prow)
 
 
-def test_attention_tree_and_exactness(nat):
-    bs, n, hq, hk, d, page = 2, 8, 6, 1, 256, 16
+@pytest.mark.parametrize("hq,hk,d", [(6, 1, 256), (16, 2, 128), (4, 2, 64)])
+def test_attention_tree_and_exactness(nat, hq, hk, d):
+    bs, n, page = 2, 8, 16
     L = torch.tensor([300, 517])
     bt = torch.arange(bs * 64, dtype=torch.int32).view(bs, 64)
     slots_total = bt.numel() * page
