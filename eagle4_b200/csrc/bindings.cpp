@@ -4,7 +4,7 @@
 namespace e4 {
 torch::Tensor gemm_error_word(torch::Device dev);
 void gemm_launch(const torch::Tensor& x, const torch::Tensor& w, int epi, torch::Tensor y, torch::Tensor yf,
-                 const torch::Tensor& res, torch::Tensor amax_val, torch::Tensor amax_idx);
+                 const torch::Tensor& res, torch::Tensor amax_val, torch::Tensor amax_idx, double fold_eps);
 torch::Tensor rmsnorm(const torch::Tensor& x, const torch::Tensor& w, double eps, bool offset);
 torch::Tensor concat_norms(const torch::Tensor& e, const torch::Tensor& h, const torch::Tensor& we,
                            const torch::Tensor& wh, double eps);

@@ -14,6 +14,10 @@
 // CTA holding its first k-block (its range ends there, so that piece is done last): it adds the other pieces in
 // split order after a bounded wait on a per-tile count the other pieces bump with release adds.
 //
+// A consumer GEMM of a normalised input can take the raw residual stream instead (the norm weight folded into W):
+// its epilogue warps compute each token's inverse RMS from X while the MMAs run and scale the accumulator by it, so
+// the separate RMSNorm launch between the residual update and the next projection disappears.
+//
 // Epilogues: plain bf16 store; residual add; SwiGLU over gate/up rows interleaved in 64-row blocks; squared ReLU;
 // fp32 store; a per-tile (max, argmax) for the vocabulary-parallel greedy head; and the tensor-parallel scatter:
 // each finished fp32 tile is stored straight into this rank's slot of every rank's receive buffer (peer memory over
@@ -67,6 +71,13 @@ struct Params {
   long slot_stride;  // pairs per (parity, src rank) slot
   int world, rank, row0;
   unsigned long long* trace;  // optional [grid][8] globaltimer stamps (tuning runs only)
+  // RMSNorm folded into the GEMM (fold != 0): X is the raw residual stream, W carries the norm weight in its columns,
+  // and every token column of the accumulator is scaled by rsqrt(mean(x^2) + fold_eps) over that token's row of X
+  // (xr: the launch's first row, ldx its stride), computed by the epilogue warps while the MMAs run.
+  const __nv_bfloat16* xr;
+  int ldx;
+  float fold_eps;
+  int fold;
 };
 
 // trace slots: 0 start, 1 setup done, 2 first stage landed (MMA), 3 last MMA issued, 4 first accumulator ready
@@ -315,6 +326,30 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
     const int ep_tid = threadIdx.x - 64;
     const int quarter = warp & 3;
     const int m = quarter * 32 + lane;
+    float* rsv = xchg + 16 * 64;  // [nt] folded-norm scales
+    if (p.fold) {
+      // token t's sum of squares: lane partials over 16-byte pieces in index order, then a butterfly (fixed order)
+      for (int t = warp - 2; t < p.nt; t += 4) {
+        float ss = 0.f;
+        if (t < p.T) {
+          const uint4* xr = reinterpret_cast<const uint4*>(p.xr + size_t(t) * p.ldx);
+#pragma unroll 4
+          for (int i = lane; i < p.K / 8; i += 32) {
+            const uint4 u = xr[i];
+            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __bfloat1622float2(h2[e]);
+              ss = fmaf(f.x, f.x, ss);
+              ss = fmaf(f.y, f.y, ss);
+            }
+          }
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) rsv[t] = t < p.T ? rsqrtf(ss / float(p.K) + p.fold_eps) : 0.f;
+      }
+      named_bar(1, 128);
+    }
     int local = 0;
     for (long g = g_begin; g < g_end; ++local) {
       const Piece pc = next_piece(p, g, g_end);
@@ -331,6 +366,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
           float v[16];
           tmem_ld16(t_addr + j0, v);
           if (j0 + 16 >= p.nt) { tc_fence_before(); mbar_arrive(&acc_empty[acc]); }
+          if (p.fold) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] *= rsv[j0 + i];
+          }
           store_chunk(p, tile, m, j0, v, xchg, ep_tid, parity);
         }
       } else {
@@ -399,6 +438,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
                   }
                 }
               }
+            }
+            if (p.fold) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) v[i] *= rsv[j0 + i];
             }
             store_chunk(p, tile, m, j0, v, xchg, ep_tid, parity);
           }
@@ -574,8 +617,11 @@ int launch_chunks(const torch::Tensor& x, const torch::Tensor& w, int epi, F chu
     p.err = sc.err.data_ptr<int>();
     chunk(p, t0);
     const __nv_bfloat16* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()) + size_t(t0) * x.stride(0);
+    p.xr = xp;
+    p.ldx = int(x.stride(0));
+    TORCH_CHECK(!p.fold || K % 8 == 0, "gemm: a folded norm needs K % 8 == 0");
     CUtensorMap xmap = make_map(xp, tc, K, x.stride(0), p.nt);
-    const size_t smem = 1024 + size_t(p.stages) * stage_bytes + 64 + 16 * 64 * 4 + 1024;
+    const size_t smem = 1024 + size_t(p.stages) * stage_bytes + 64 + 16 * 64 * 4 + 256 * 4 + 1024;
     C10_CUDA_CHECK(launch_pdl(gemm_kernel, grid, kThreads, smem, stream.stream(), wmap, xmap, p));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     launched += grid;
@@ -585,13 +631,16 @@ int launch_chunks(const torch::Tensor& x, const torch::Tensor& w, int epi, F chu
 }  // namespace gemm
 
 // Launch one GEMM over all T tokens (chunks of 256 tokens per launch).
+// ``fold_eps`` >= 0 folds an RMSNorm into the GEMM (X raw, norm weight pre-multiplied into W's columns).
 void gemm_launch(const torch::Tensor& x, const torch::Tensor& w, int epi, torch::Tensor y, torch::Tensor yf,
-                 const torch::Tensor& res, torch::Tensor amax_val, torch::Tensor amax_idx) {
+                 const torch::Tensor& res, torch::Tensor amax_val, torch::Tensor amax_idx, double fold_eps) {
   using namespace gemm;
   TORCH_CHECK(epi != kScatter, "gemm: the scatter epilogue has its own entry point");
   const int n_tiles = (w.size(0) + kTileM - 1) / kTileM;
   auto has = [](const torch::Tensor& t) { return t.defined() && t.numel() > 0; };
   launch_chunks(x, w, epi, [&](Params& p, int t0) {
+    p.fold = fold_eps >= 0.0;
+    p.fold_eps = float(fold_eps);
     if (has(y)) {
       p.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr()) + size_t(t0) * y.stride(0);
       p.ldy = y.stride(0);

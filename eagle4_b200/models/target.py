@@ -97,12 +97,41 @@ class Records:
     gate_a: List[torch.Tensor] = field(default_factory=list)  # Mamba2 raw dt [T, H] (None for GDN)
 
 
+FOLDED = "__input_norms_folded__"  # marks a weight dict whose projections carry their input norm weights
+
+# the projection that consumes each sub-block's input norm
+_CONSUMER = {"attn": "qkv", "gdn": "in_proj", "mamba": "in_proj", "swiglu": "gate_up", "relu2": "up"}
+
+
+def fold_input_norms(cfg: TargetConfig, weights: Dict[str, torch.Tensor]) -> None:
+    """Multiply every sub-block's input-norm weight into the columns of the projection that consumes it (once per
+    dict: the dict is marked), so the projection can take the raw residual stream and apply the norm's per-token
+    scale in its epilogue. The final norm before the LM head stays a separate op."""
+    if FOLDED in weights:
+        return
+    for i, (mixer, mlp) in enumerate(cfg.layers):
+        for kind, norm in ((mixer, "norm1"), (mlp, "norm2")):
+            if kind is None:
+                continue
+            name = f"l{i}.{_CONSUMER[kind]}"
+            weights[name] = ops.fold_norm_weight(weights[name], weights[f"l{i}.{norm}"], cfg.norm_offset)
+    weights[FOLDED] = torch.ones(())
+
+
 class TargetModel:
-    def __init__(self, cfg: TargetConfig, weights: Dict[str, torch.Tensor], *, aux_layer_ids=(), tp=None):
+    def __init__(self, cfg: TargetConfig, weights: Dict[str, torch.Tensor], *, aux_layer_ids=(), tp=None,
+                 fold_norms: bool = True):
         """``cfg`` / ``weights`` are this rank's shard under tensor parallelism (``tp``: a
-        :class:`~eagle4_b200.parallel.tp.TensorParallel`; None on one GPU)."""
+        :class:`~eagle4_b200.parallel.tp.TensorParallel`; None on one GPU). With ``fold_norms`` (the default) the
+        sub-blocks' input norms are folded into their first projections (``weights`` is updated in place, once)."""
         self.cfg = cfg
         self.w = weights
+        self.fold = fold_norms
+        if fold_norms:
+            fold_input_norms(cfg, weights)
+        elif FOLDED in weights:
+            raise ValueError("these weights carry folded input norms: build the model with fold_norms=True")
+        self.fold_eps = cfg.rms_norm_eps if fold_norms else None
         self.tp = tp
         self.lm_lo = int(weights["lm_head_lo"]) if "lm_head_lo" in weights else 0
         self.aux_layer_ids = tuple(aux_layer_ids)
@@ -121,18 +150,21 @@ class TargetModel:
         self.next_norm = dict(zip(norms, norms[1:] + ["norm"]))
 
     def _row(self, y: torch.Tensor, w_out: torch.Tensor, h: torch.Tensor, after: str):
-        """Row-parallel output projection + residual, then the next sub-block's input norm: ``(h, x_next)``."""
-        nw = self.w[self.next_norm[after]]
+        """Row-parallel output projection + residual, then the next sub-block's input: ``(h, x_next)``. With folded
+        norms ``x_next`` is ``h`` itself (the next projection normalises), except before the LM head."""
+        nxt = self.next_norm[after]
+        nw = None if (self.fold and nxt != "norm") else self.w[nxt]
         if self.tp is not None:
-            return self.tp.row_linear(y, w_out, h, nw, self.cfg.rms_norm_eps, self.cfg.norm_offset)
+            h, xn = self.tp.row_linear(y, w_out, h, nw, self.cfg.rms_norm_eps, self.cfg.norm_offset)
+            return h, (h if nw is None else xn)
         h = ops.linear_residual(y, w_out, h)
-        return h, ops.rmsnorm(h, nw, self.cfg.rms_norm_eps, self.cfg.norm_offset)
+        return h, (h if nw is None else ops.rmsnorm(h, nw, self.cfg.rms_norm_eps, self.cfg.norm_offset))
 
     # ------------------------------------------------------------------ blocks
     def _attn(self, i: int, x: torch.Tensor, h: torch.Tensor, rb: RowBatch, cache: TargetCache) -> torch.Tensor:
         cfg, w = self.cfg, self.w
         li = self.attn_index[i]
-        qkv = ops.linear(x, w[f"l{i}.qkv"])
+        qkv = ops.linear(x, w[f"l{i}.qkv"], self.fold_eps)
         q, gate = ops.qkv_prepare(qkv, cfg, rb.pos, rb.write_slot, cache.k[li], cache.v[li],
                                   w.get(f"l{i}.q_norm"), w.get(f"l{i}.k_norm"))
         o = ops.attention(q, cache.k[li], cache.v[li], cache.block_table, cache.page, rb.req, rb.ctx_start,
@@ -144,7 +176,7 @@ class TargetModel:
         cfg, w = self.cfg, self.w
         ri = self.rec_index[i]
         cd, vd, hv = cfg.gdn_conv_dim, cfg.gdn_value_dim, cfg.gdn_v_heads
-        proj = ops.linear(x, w[f"l{i}.in_proj"])
+        proj = ops.linear(x, w[f"l{i}.in_proj"], self.fold_eps)
         x_pre = proj[:, :cd]
         conv = ops.causal_conv_tree(x_pre, cache.conv[ri], rb.state_slot, rb.parent, w[f"l{i}.conv"])
         y = ops.gdn_mixer(conv, proj, cfg, w[f"l{i}.A_log"], w[f"l{i}.dt_bias"], w[f"l{i}.gnorm"], cache.ssm[ri],
@@ -163,7 +195,7 @@ class TargetModel:
         cfg, w = self.cfg, self.w
         ri = self.rec_index[i]
         inner, cd, nh = cfg.mamba_inner, cfg.mamba_conv_dim, cfg.mamba_heads
-        proj = ops.linear(x, w[f"l{i}.in_proj"])
+        proj = ops.linear(x, w[f"l{i}.in_proj"], self.fold_eps)
         z = proj[:, :inner]
         x_pre = proj[:, inner: inner + cd]
         dt = proj[:, inner + cd: inner + cd + nh]
@@ -184,9 +216,9 @@ class TargetModel:
     def _mlp(self, i: int, x: torch.Tensor, h: torch.Tensor, kind: str) -> torch.Tensor:
         w = self.w
         if kind == "swiglu":
-            a = ops.linear_swiglu(x, w[f"l{i}.gate_up"])
+            a = ops.linear_swiglu(x, w[f"l{i}.gate_up"], self.fold_eps)
         else:
-            a = ops.linear_relu2(x, w[f"l{i}.up"])
+            a = ops.linear_relu2(x, w[f"l{i}.up"], self.fold_eps)
         return self._row(a, w[f"l{i}.down"], h, f"l{i}.norm2")
 
     # ------------------------------------------------------------------ forward
@@ -196,7 +228,8 @@ class TargetModel:
         eps, off = cfg.rms_norm_eps, cfg.norm_offset
         h = ops.embedding(rb.ids, w["embed"])
         first = next(iter(self.next_norm))
-        x = ops.rmsnorm(h, w[first], eps, off)  # each sub-block returns the next one's normed input
+        # each sub-block returns the next one's input (normed, or raw when the next projection folds the norm)
+        x = h if self.fold else ops.rmsnorm(h, w[first], eps, off)
         saved: Dict[int, torch.Tensor] = {}
         for i, (mixer, mlp) in enumerate(cfg.layers):
             if mixer is not None:

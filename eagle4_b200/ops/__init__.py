@@ -26,20 +26,26 @@ def _nat():
 
 
 # dense -----------------------------------------------------------------------------------------------------------
-def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    return _nat().linear(x, w) if _cuda(x) else ref.linear(x, w)
+def linear(x: torch.Tensor, w: torch.Tensor, fold_eps: Optional[float] = None) -> torch.Tensor:
+    """``x @ w^T``; with ``fold_eps`` the RMSNorm of ``x``'s rows is folded in (``w`` made by ``fold_norm_weight``)."""
+    return _nat().linear(x, w, fold_eps) if _cuda(x) else ref.linear(x, w, fold_eps)
 
 
 def linear_residual(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
     return _nat().linear_residual(x, w, residual) if _cuda(x) else ref.linear_residual(x, w, residual)
 
 
-def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor) -> torch.Tensor:
-    return _nat().linear_swiglu(x, w_gu) if _cuda(x) else ref.linear_swiglu(x, w_gu)
+def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor, fold_eps: Optional[float] = None) -> torch.Tensor:
+    return _nat().linear_swiglu(x, w_gu, fold_eps) if _cuda(x) else ref.linear_swiglu(x, w_gu, fold_eps)
 
 
-def linear_relu2(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    return _nat().linear_relu2(x, w) if _cuda(x) else ref.linear_relu2(x, w)
+def linear_relu2(x: torch.Tensor, w: torch.Tensor, fold_eps: Optional[float] = None) -> torch.Tensor:
+    return _nat().linear_relu2(x, w, fold_eps) if _cuda(x) else ref.linear_relu2(x, w, fold_eps)
+
+
+def fold_norm_weight(w: torch.Tensor, norm_w: torch.Tensor, offset: bool) -> torch.Tensor:
+    """``w`` with an RMSNorm weight multiplied into its input columns (computed in float64, rounded once)."""
+    return ref.fold_norm_weight(w, norm_w, offset)
 
 
 def lm_head_argmax(x: torch.Tensor, w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:

@@ -68,40 +68,45 @@ def _c2(x: torch.Tensor) -> torch.Tensor:
 
 
 # dense ------------------------------------------------------------------------------------------------------------
-def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+def _fold(fold_eps: Optional[float]) -> float:
+    return -1.0 if fold_eps is None else float(fold_eps)
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, fold_eps: Optional[float] = None) -> torch.Tensor:
+    """``x @ w^T``; with ``fold_eps`` the RMSNorm of ``x`` is folded in (``w`` carries the norm weight)."""
     x = _c2(x)
     y = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
-    _C.gemm(x, w, EPI_PLAIN, y, _NONE, _NONE, _NONE, _NONE)
+    _C.gemm(x, w, EPI_PLAIN, y, _NONE, _NONE, _NONE, _NONE, _fold(fold_eps))
     return y
 
 
 def linear_residual(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
     x = _c2(x)
     y = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
-    _C.gemm(x, w, EPI_RESIDUAL, y, _NONE, residual.contiguous(), _NONE, _NONE)
+    _C.gemm(x, w, EPI_RESIDUAL, y, _NONE, residual.contiguous(), _NONE, _NONE, -1.0)
     return y
 
 
-def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor) -> torch.Tensor:
+def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor, fold_eps: Optional[float] = None) -> torch.Tensor:
     x = _c2(x)
     if w_gu.shape[0] % 128:
         raise ValueError("fused gate/up weight needs a multiple of 128 rows")
     y = torch.empty(x.shape[0], w_gu.shape[0] // 2, dtype=x.dtype, device=x.device)
-    _C.gemm(x, w_gu, EPI_SWIGLU, y, _NONE, _NONE, _NONE, _NONE)
+    _C.gemm(x, w_gu, EPI_SWIGLU, y, _NONE, _NONE, _NONE, _NONE, _fold(fold_eps))
     return y
 
 
-def linear_relu2(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+def linear_relu2(x: torch.Tensor, w: torch.Tensor, fold_eps: Optional[float] = None) -> torch.Tensor:
     x = _c2(x)
     y = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
-    _C.gemm(x, w, EPI_RELU2, y, _NONE, _NONE, _NONE, _NONE)
+    _C.gemm(x, w, EPI_RELU2, y, _NONE, _NONE, _NONE, _NONE, _fold(fold_eps))
     return y
 
 
 def logits(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     x = _c2(x)
     y = torch.empty(x.shape[0], w.shape[0], dtype=torch.float32, device=x.device)
-    _C.gemm(x, w, EPI_F32, _NONE, y, _NONE, _NONE, _NONE)
+    _C.gemm(x, w, EPI_F32, _NONE, y, _NONE, _NONE, _NONE, -1.0)
     return y
 
 
@@ -112,7 +117,7 @@ def lm_head_argmax(x: torch.Tensor, w: torch.Tensor) -> Tuple[torch.Tensor, torc
     chunks = (t + 255) // 256
     val = torch.empty(chunks * 256 * n_tiles, dtype=torch.float32, device=x.device)
     idx = torch.empty(chunks * 256 * n_tiles, dtype=torch.int32, device=x.device)
-    _C.gemm(x, w, EPI_ARGMAX, _NONE, _NONE, _NONE, val, idx)
+    _C.gemm(x, w, EPI_ARGMAX, _NONE, _NONE, _NONE, val, idx, -1.0)
     ids, best = _C.argmax_reduce(val, idx, n_tiles, t)
     return ids, best
 

@@ -15,9 +15,19 @@ import torch.nn.functional as F
 
 
 # ----------------------------------------------------------------------------------------------- dense ops
-def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+def _matmul(x: torch.Tensor, w: torch.Tensor, fold_eps: Optional[float]) -> torch.Tensor:
+    """``x @ w^T`` in float64; with ``fold_eps`` each row is scaled by ``rsqrt(mean(x_row^2) + fold_eps)`` (an RMSNorm
+    of ``x`` folded into the product, ``w`` carrying the norm weight in its columns)."""
+    xd = x.double()
+    y = xd @ w.double().t()
+    if fold_eps is not None:
+        y = y * torch.rsqrt(xd.square().mean(-1, keepdim=True) + fold_eps)
+    return y
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, fold_eps: Optional[float] = None) -> torch.Tensor:
     """``x [T, K] @ w[N, K]^T``."""
-    return (x.double() @ w.double().t()).to(x.dtype)
+    return _matmul(x, w, fold_eps).to(x.dtype)
 
 
 def linear_residual(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
@@ -25,19 +35,27 @@ def linear_residual(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor) ->
     return (residual.double() + x.double() @ w.double().t()).to(residual.dtype)
 
 
-def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor) -> torch.Tensor:
+def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor, fold_eps: Optional[float] = None) -> torch.Tensor:
     """``silu(x @ g^T) * (x @ u^T)`` with ``w_gu`` holding gate and up rows interleaved in blocks of 64:
     rows ``[128i, 128i+64)`` are gate rows ``[64i, 64i+64)`` and rows ``[128i+64, 128i+128)`` the matching up rows."""
-    y = x.double() @ w_gu.double().t()
+    y = _matmul(x, w_gu, fold_eps)
     t, n2 = y.shape
     y = y.view(t, n2 // 128, 2, 64)
     g, u = y[:, :, 0], y[:, :, 1]
     return (F.silu(g) * u).reshape(t, n2 // 2).to(x.dtype)
 
 
-def linear_relu2(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    y = x.double() @ w.double().t()
+def linear_relu2(x: torch.Tensor, w: torch.Tensor, fold_eps: Optional[float] = None) -> torch.Tensor:
+    y = _matmul(x, w, fold_eps)
     return torch.relu(y).square().to(x.dtype)
+
+
+def fold_norm_weight(w: torch.Tensor, norm_w: torch.Tensor, offset: bool) -> torch.Tensor:
+    """``w`` [N, K] with the RMSNorm weight (``1 + norm_w`` with ``offset``) multiplied into its columns."""
+    # a bf16 x bf16 product is exact in float32; wider weights use float64 (either way one rounding to w's dtype)
+    ct = torch.float32 if w.dtype in (torch.bfloat16, torch.float16) else torch.float64
+    scale = norm_w.to(ct) + 1.0 if offset else norm_w.to(ct)
+    return (w.to(ct) * scale[None, :]).to(w.dtype)
 
 
 def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, block: int = 64) -> torch.Tensor:

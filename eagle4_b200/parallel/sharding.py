@@ -88,6 +88,10 @@ def shard_target(cfg: TargetConfig, w: Dict[str, torch.Tensor], world: int, rank
     lo, hi = vocab_range(cfg.vocab_size, world, rank)
     out["lm_head"] = w["lm_head"][lo:hi].contiguous()
     out["lm_head_lo"] = torch.tensor(lo)
+    from eagle4_b200.models.target import FOLDED
+
+    if FOLDED in w:  # the column-parallel shards of folded projections are folded too
+        out[FOLDED] = w[FOLDED]
     d = cfg.head_dim
     for i, (mixer, mlp) in enumerate(cfg.layers):
         p = f"l{i}."

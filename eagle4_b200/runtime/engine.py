@@ -233,7 +233,7 @@ class Engine:
         rb = RowBatch(ids=prompt.to(self.device), pos=pos, req=self._i32(n, slot), write_slot=slots,
                       ctx_start=self._i32(n, 0), ctx_len=(pos + 1).int(),
                       extra=torch.zeros(n, 1, dtype=torch.int32, device=self.device), n_extra=self._i32(n, 0),
-                      parent=(pos - 1).int(), state_slot=self._i32(n, slot), scan=True)
+                      parent=(pos - 1).int(), state_slot=self._i32(n, slot), scan=True, max_keys=n)
         out, aux = self.target.forward(rb, self.tcache)
         if self.sampled:
             dev = self.device
@@ -265,10 +265,11 @@ class Engine:
         w = self.draft.cfg.sliding_window
         t = ids.shape[0]
         start = (pos - w + 1).clamp(min=0) if w else torch.zeros_like(pos)
+        # rows are the positions 0..t-1 (the prompt's leading rows): at most min(w, t) visible keys
         return self.draft.forward(ids, hidden, pos, self._i32(t, slot),
                                   self._slots(torch.tensor(slot, device=self.device), pos), start.int(),
                                   (pos + 1).int(), torch.zeros(t, 1, dtype=torch.int32, device=self.device),
-                                  self._i32(t, 0), self.dcache)
+                                  self._i32(t, 0), self.dcache, max_keys=min(w, t) if w else t)
 
     # ------------------------------------------------------------------ device-state rounds
     def _plain_round(self, bs: int) -> None:

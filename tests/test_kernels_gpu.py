@@ -60,6 +60,30 @@ def test_gemm_epilogues(nat):
     _close(nat.logits(x, w), ref.logits(x.cpu().float(), w.cpu().float()), 1e-2)
 
 
+@pytest.mark.parametrize("T", [1, 16, 100, 300])
+def test_gemm_folded_norm(nat, T):
+    """RMSNorm folded into the GEMM: raw rows in, the norm weight multiplied into W's columns, the per-token inverse
+    RMS applied in the epilogue; matches norm-then-GEMM, is batch invariant, and works for every epilogue kind."""
+    K, N, F = 5120, 1024, 512
+    x = _bf(T, K, scale=3.0, seed=40)
+    nw = _bf(K, scale=0.1, seed=41)
+    w = _bf(N, K, scale=0.05, seed=42)
+    wf = ref.fold_norm_weight(w, nw, True)
+    eps = 1e-6
+    xn = ref.rmsnorm(x.cpu().float(), nw.cpu().float(), eps, True)
+    want = ref.linear(xn, w.cpu().float())
+    got = nat.linear(x, wf, eps)
+    _close(got, want, 2e-2)
+    _close(got, ref.linear(x.cpu().float(), wf.cpu().float(), eps), 1e-2)
+    single = nat.linear(x[T - 1:].contiguous(), wf, eps)
+    assert torch.equal(single, got[T - 1:])
+    gu = _bf(2 * F, K, scale=0.05, seed=43)
+    guf = ref.fold_norm_weight(gu, nw, True)
+    _close(nat.linear_swiglu(x, guf, eps), ref.linear_swiglu(xn, gu.cpu().float()), 3e-2)
+    _close(nat.linear_relu2(x, wf, eps), ref.linear_relu2(xn, w.cpu().float()), 3e-2)
+    nat.check_errors()
+
+
 def test_lm_head_argmax(nat):
     T, K, V = 21, 1024, 50000
     x, w = _bf(T, K, seed=9), _bf(V, K, scale=0.05, seed=10)
