@@ -669,19 +669,18 @@ torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int6
     if (!norm_w.numel()) return out;
     return gated_rmsnorm(raw.view({T, HV, V}), proj.narrow(1, z_off, HV * V), norm_w, eps);
   }
-  torch::Tensor seg = torch::zeros({1}, sl.options());
-  const int ny = scan ? seg.numel() - 1 : T;
+  const int ny = T;  // tree mode reads no segment table
   dim3 grid(HV, ny);
   auto st = at::cuda::getCurrentCUDAStream();
   if (K == 128) {
     gdn_smem_attr(gdn_kernel<128>, sizeof(GdnStage<128>));
     C10_CUDA_CHECK(launch_pdl(gdn_kernel<128>, grid, 128, sizeof(GdnStage<128>), st.stream(), a, sl.data_ptr<int>(), pa.data_ptr<int>(),
-                                                              seg.data_ptr<int>(), scan, norm_w.numel() ? CBF(norm_w) : nullptr, float(eps),
+                                                              static_cast<const int*>(nullptr), scan, norm_w.numel() ? CBF(norm_w) : nullptr, float(eps),
                                                               BFP(out)));
   } else {
     gdn_smem_attr(gdn_kernel<64>, sizeof(GdnStage<64>));
     C10_CUDA_CHECK(launch_pdl(gdn_kernel<64>, grid, 128, sizeof(GdnStage<64>), st.stream(), a, sl.data_ptr<int>(), pa.data_ptr<int>(),
-                                                            seg.data_ptr<int>(), scan, norm_w.numel() ? CBF(norm_w) : nullptr, float(eps),
+                                                            static_cast<const int*>(nullptr), scan, norm_w.numel() ? CBF(norm_w) : nullptr, float(eps),
                                                             BFP(out)));
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -756,10 +755,11 @@ torch::Tensor mamba_tree(const torch::Tensor& xbc, const torch::Tensor& dt, cons
   if (!T) return out;
   MambaArgs a = mamba_args(xbc, dt, a_log, dt_bias, dskip, state, H, P, N, G);
   auto sl = slot.to(torch::kInt32).contiguous(), pa = parent.to(torch::kInt32).contiguous();
-  torch::Tensor seg = scan ? segments_of(sl) : torch::zeros({1}, sl.options());
+  torch::Tensor seg = scan ? segments_of(sl) : torch::Tensor();  // tree mode reads no segment table
   dim3 grid(H, scan ? seg.numel() - 1 : T);
   auto st = at::cuda::getCurrentCUDAStream();
-  E4_MAMBA_DISPATCH(N, mamba_kernel, a, sl.data_ptr<int>(), pa.data_ptr<int>(), seg.data_ptr<int>(), scan, BFP(out))
+  const int* segp = scan ? seg.data_ptr<int>() : nullptr;
+  E4_MAMBA_DISPATCH(N, mamba_kernel, a, sl.data_ptr<int>(), pa.data_ptr<int>(), segp, scan, BFP(out))
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
 }
