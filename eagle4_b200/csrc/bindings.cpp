@@ -35,11 +35,6 @@ torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int6
                        int64_t a_off, const torch::Tensor& a_log, const torch::Tensor& dt_bias, torch::Tensor state,
                        const torch::Tensor& slot, const torch::Tensor& parent, const torch::Tensor& norm_w,
                        double eps, int64_t HK, int64_t HV, int64_t K, int64_t V, bool scan);
-std::vector<torch::Tensor> gdn_conv_tree(const torch::Tensor& proj, const torch::Tensor& conv_w, const torch::Tensor& cs,
-                                         int64_t z_off, int64_t b_off, int64_t a_off, const torch::Tensor& a_log,
-                                         const torch::Tensor& dt_bias, torch::Tensor state, const torch::Tensor& slot,
-                                         const torch::Tensor& parent, const torch::Tensor& norm_w, double eps,
-                                         int64_t HK, int64_t HV, int64_t K, int64_t V);
 void gdn_commit_all(const std::vector<torch::Tensor>& qkv, const std::vector<torch::Tensor>& proj,
                     const std::vector<torch::Tensor>& state, const std::vector<torch::Tensor>& conv_state,
                     const std::vector<torch::Tensor>& a_log, const std::vector<torch::Tensor>& dt_bias, int64_t b_off,
@@ -134,7 +129,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("conv_commit", &e4::conv_commit);
   m.def("conv_commit_scan", &e4::conv_commit_scan);
   m.def("gdn_tree", &e4::gdn_tree);
-  m.def("gdn_conv_tree", &e4::gdn_conv_tree, "tree-mode GDN with the causal conv fused into its staging");
   m.def("gdn_commit_all", &e4::gdn_commit_all);
   m.def("mamba_tree", &e4::mamba_tree);
   m.def("mamba_commit", &e4::mamba_commit);

@@ -89,35 +89,7 @@ struct GdnArgs {
   const float* dt_bias;       // [HV]
   float* state;               // [slots, HV, V, K]
   int HK, HV, K, V;
-  // causal conv fused into tree mode (conv_out != nullptr): pre-conv inputs cx (row stride ldx), conv weights
-  // cw [C, W], committed windows cs [slots, C, W-1]; each CTA writes its own row's conv outputs to conv_out [T, C]
-  // (the value head's V channels; the key head's q / k channels from the first value head of the group)
-  const __nv_bfloat16* cx;
-  int ldx;
-  const __nv_bfloat16* cw;
-  const __nv_bfloat16* cs;
-  int W, C;
-  __nv_bfloat16* conv_out;
 };
-
-// Causal conv output of channel c at path position p (node path[p], whose ancestors are path[p-1], ... and, below
-// path[0], the committed window of ``slot``): the taps, their order and the bf16 rounding of conv_tree_kernel.
-__device__ __forceinline__ float gdn_conv_at(const GdnArgs& a, const int* path, int p, int slot, int c) {
-  const int n = min(a.W, p + 1);
-  float acc = 0.f;
-  for (int j = 0; j < a.W; ++j) {
-    const int from_end = a.W - 1 - j;
-    float v;
-    if (from_end < n) {
-      v = __bfloat162float(a.cx[size_t(path[p - from_end]) * a.ldx + c]);
-    } else {
-      const int k = (a.W - 1) - (from_end - n) - 1;
-      v = __bfloat162float(a.cs[(size_t(slot) * a.C + c) * (a.W - 1) + k]);
-    }
-    acc = fmaf(__bfloat162float(a.cw[size_t(c) * a.W + j]), v, acc);
-  }
-  return __bfloat162float(__float2bfloat16(silu(acc)));
-}
 
 // Decay gate and write strength of (row, value head): g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b).
 __device__ __forceinline__ float2 gdn_gate(const GdnArgs& a, int row, int h) {
@@ -140,15 +112,10 @@ struct GdnStage {
 };
 
 // Stage ``n`` (<= kGdnTile) nodes ``rows[0..n)``: warp w normalises nodes w, w+4, ... (fixed-order warp sums).
-// With FUSE the q / k / v values are the causal conv of the pre-conv inputs along the path (``rows`` = path + p0,
-// node j at path position p0 + j, request slot ``cslot``), and the CTA's own row ``own`` has its conv outputs stored.
-template <int K, bool FUSE = false>
-__device__ __forceinline__ void gdn_stage(const GdnArgs& a, const int* rows, int n, int h, int kh, GdnStage<K>& st,
-                                          int p0 = 0, int cslot = 0, int own = -1) {
+template <int K>
+__device__ __forceinline__ void gdn_stage(const GdnArgs& a, const int* rows, int n, int h, int kh, GdnStage<K>& st) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   constexpr int PL = K / 32;
-  const int* path = rows - p0;
-  const bool qk_writer = (h % (a.HV / a.HK)) == 0;
   for (int j = warp; j < n; j += nw) {
     const int row = rows[j];
     const __nv_bfloat16* base = a.qkv + size_t(row) * a.ldq;
@@ -156,18 +123,8 @@ __device__ __forceinline__ void gdn_stage(const GdnArgs& a, const int* rows, int
     float q2 = 0.f, k2 = 0.f;
 #pragma unroll
     for (int i = 0; i < PL; ++i) {
-      const int cq = kh * K + lane * PL + i, ck = a.HK * K + kh * K + lane * PL + i;
-      if constexpr (FUSE) {
-        qv[i] = gdn_conv_at(a, path, p0 + j, cslot, cq);
-        kv[i] = gdn_conv_at(a, path, p0 + j, cslot, ck);
-        if (row == own && qk_writer) {
-          a.conv_out[size_t(row) * a.C + cq] = __float2bfloat16(qv[i]);
-          a.conv_out[size_t(row) * a.C + ck] = __float2bfloat16(kv[i]);
-        }
-      } else {
-        qv[i] = bf(base[cq]);
-        kv[i] = bf(base[ck]);
-      }
+      qv[i] = bf(base[kh * K + lane * PL + i]);
+      kv[i] = bf(base[a.HK * K + kh * K + lane * PL + i]);
       q2 = fmaf(qv[i], qv[i], q2);
       k2 = fmaf(kv[i], kv[i], k2);
     }
@@ -186,14 +143,7 @@ __device__ __forceinline__ void gdn_stage(const GdnArgs& a, const int* rows, int
   }
   for (int i = threadIdx.x; i < n * a.V; i += blockDim.x) {
     const int j = i / a.V, c = i % a.V;
-    const int cv = 2 * a.HK * K + h * a.V + c;
-    if constexpr (FUSE) {
-      const float x = gdn_conv_at(a, path, p0 + j, cslot, cv);
-      st.v[j][c] = x;
-      if (rows[j] == own) a.conv_out[size_t(own) * a.C + cv] = __float2bfloat16(x);
-    } else {
-      st.v[j][c] = bf(a.qkv[size_t(rows[j]) * a.ldq + cv]);
-    }
+    st.v[j][c] = bf(a.qkv[size_t(rows[j]) * a.ldq + 2 * a.HK * K + h * a.V + c]);
   }
   __syncthreads();
 }
@@ -273,7 +223,7 @@ __device__ __forceinline__ void save_state(const float* S, float* dst) {
 // One CTA per (value head, row) in tree mode (the row replays its path, no state write) or per (value head,
 // request segment) in scan mode (rows in order, state updated in place); thread v owns state column v. The output
 // is the gated-RMS-normalised head output [T, HV*V]. Path nodes are staged kGdnTile at a time.
-template <int K, bool FUSE = false>
+template <int K>
 __global__ void __launch_bounds__(128) gdn_kernel(GdnArgs a, const int* __restrict__ slot,
                                                   const int* __restrict__ parent, const int* __restrict__ seg,
                                                   int scan, const __nv_bfloat16* __restrict__ nw, float eps,
@@ -306,13 +256,12 @@ __global__ void __launch_bounds__(128) gdn_kernel(GdnArgs a, const int* __restri
     for (int p0 = 0; p0 < plen; p0 += kGdnTile) {
       const int n = min(kGdnTile, plen - p0);
       if (p0) __syncthreads();
-      gdn_stage<K, FUSE>(a, path + p0, n, h, kh, st, p0, slot[r], r);
+      gdn_stage<K>(a, path + p0, n, h, kh, st);
       for (int j = 0; j < n; ++j) o = gdn_step<K>(S, st, j, vc);
     }
     gdn_store(a, r, h, v, o, nw, eps, red, out);
     return;
   }
-  if constexpr (FUSE) return;  // the fused conv serves tree mode only
   const int r0 = seg[blockIdx.y], r1 = seg[blockIdx.y + 1];
   float* stp = a.state + ((size_t(slot[r0]) * a.HV + h) * a.V + vc) * K;
   load_state<K>(S, stp);
@@ -736,49 +685,6 @@ torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int6
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
-}
-
-// Tree-mode GDN with the causal conv fused in: ``proj`` is the in_proj output (pre-conv inputs at columns [0, C), the
-// gates and z at their offsets), ``conv_w`` [C, W] the conv weights and ``cs`` [slots, C, W-1] the committed
-// windows. Returns {gated-RMS-normalised output [T, HV*V], conv output [T, C]} (the conv output feeds the commit).
-std::vector<torch::Tensor> gdn_conv_tree(const torch::Tensor& proj, const torch::Tensor& conv_w, const torch::Tensor& cs,
-                                         int64_t z_off, int64_t b_off, int64_t a_off, const torch::Tensor& a_log,
-                                         const torch::Tensor& dt_bias, torch::Tensor state, const torch::Tensor& slot,
-                                         const torch::Tensor& parent, const torch::Tensor& norm_w, double eps,
-                                         int64_t HK, int64_t HV, int64_t K, int64_t V) {
-  const at::cuda::CUDAGuard gd(proj.device());
-  const int T = proj.size(0);
-  const int C = int(2 * HK * K + HV * V), W = int(conv_w.size(1));
-  TORCH_CHECK(conv_w.is_contiguous() && conv_w.size(0) == C && W >= 1 && W <= 8, "gdn_conv_tree: conv weight [C, W]");
-  TORCH_CHECK(cs.is_contiguous() && cs.size(1) == C && cs.size(2) == W - 1, "gdn_conv_tree: windows [slots, C, W-1]");
-  auto out = torch::empty({T, HV * V}, proj.options());
-  auto conv = torch::empty({T, C}, proj.options());
-  if (!T) return {out, conv};
-  GdnArgs a = gdn_args(conv, proj, z_off, b_off, a_off, a_log, dt_bias, state, HK, HV, K, V);
-  a.cx = CBF(proj);
-  a.ldx = int(proj.stride(0));
-  a.cw = CBF(conv_w);
-  a.cs = CBF(cs);
-  a.W = W;
-  a.C = C;
-  a.conv_out = BFP(conv);
-  auto sl = slot.to(torch::kInt32).contiguous(), pa = parent.to(torch::kInt32).contiguous();
-  dim3 grid(HV, T);
-  auto st = at::cuda::getCurrentCUDAStream();
-  const __nv_bfloat16* nwp = norm_w.numel() ? CBF(norm_w) : nullptr;
-  if (K == 128) {
-    gdn_smem_attr(gdn_kernel<128, true>, sizeof(GdnStage<128>));
-    C10_CUDA_CHECK(launch_pdl(gdn_kernel<128, true>, grid, 128, sizeof(GdnStage<128>), st.stream(), a,
-                              sl.data_ptr<int>(), pa.data_ptr<int>(), static_cast<const int*>(nullptr), 0, nwp,
-                              float(eps), BFP(out)));
-  } else {
-    gdn_smem_attr(gdn_kernel<64, true>, sizeof(GdnStage<64>));
-    C10_CUDA_CHECK(launch_pdl(gdn_kernel<64, true>, grid, 128, sizeof(GdnStage<64>), st.stream(), a,
-                              sl.data_ptr<int>(), pa.data_ptr<int>(), static_cast<const int*>(nullptr), 0, nwp,
-                              float(eps), BFP(out)));
-  }
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return {out, conv};
 }
 
 // Commit the accepted rows of every GDN layer (state replay and conv window) in two launches. The per-layer

@@ -178,14 +178,9 @@ class TargetModel:
         cd, vd, hv = cfg.gdn_conv_dim, cfg.gdn_value_dim, cfg.gdn_v_heads
         proj = ops.linear(x, w[f"l{i}.in_proj"], self.fold_eps)
         x_pre = proj[:, :cd]
-        if rb.scan:
-            conv = ops.causal_conv_tree(x_pre, cache.conv[ri], rb.state_slot, rb.parent, w[f"l{i}.conv"])
-            y = ops.gdn_mixer(conv, proj, cfg, w[f"l{i}.A_log"], w[f"l{i}.dt_bias"], w[f"l{i}.gnorm"],
-                              cache.ssm[ri], rb.state_slot, rb.parent, rb.scan)
-        else:  # tree verify / decode: the conv runs inside the recurrence kernel
-            y, conv = ops.gdn_conv_mixer(proj, w[f"l{i}.conv"], cache.conv[ri], cfg, w[f"l{i}.A_log"],
-                                         w[f"l{i}.dt_bias"], w[f"l{i}.gnorm"], cache.ssm[ri], rb.state_slot,
-                                         rb.parent)
+        conv = ops.causal_conv_tree(x_pre, cache.conv[ri], rb.state_slot, rb.parent, w[f"l{i}.conv"])
+        y = ops.gdn_mixer(conv, proj, cfg, w[f"l{i}.A_log"], w[f"l{i}.dt_bias"], w[f"l{i}.gnorm"], cache.ssm[ri],
+                          rb.state_slot, rb.parent, rb.scan)
         if rb.scan:
             ops.conv_commit_scan(cache.conv[ri], x_pre, rb.state_slot, cfg.conv_kernel)
         elif rec is not None:

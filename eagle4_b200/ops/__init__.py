@@ -103,16 +103,6 @@ def gdn_mixer(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent
     return fn(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent, scan)
 
 
-def gdn_conv_mixer(proj, conv_w, conv_state, cfg, a_log, dt_bias, norm_w, state, state_slot, parent):
-    """Tree-mode GDN mixer from the in_proj output: causal conv along each row's path (committed window below the
-    root), gates, recurrence and gated RMSNorm in one GPU launch. Returns ``(output [T, HV*V], conv output [T, C])``
-    (the conv output is what a commit replays)."""
-    if _cuda(proj):
-        return _nat().gdn_conv_mixer(proj, conv_w, conv_state, cfg, a_log, dt_bias, norm_w, state, state_slot, parent)
-    conv = ref.causal_conv_tree(proj[:, :cfg.gdn_conv_dim], conv_state, state_slot, parent, conv_w)
-    return ref.gdn_mixer(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent, False), conv
-
-
 def gdn_commit_all(convs, projs, states, conv_states, a_logs, dt_biases, slots, rows, n_rows, cfg):
     """Commit accepted rows in every GDN layer at once (state replay and conv windows)."""
     if not convs:

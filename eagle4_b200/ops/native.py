@@ -201,14 +201,6 @@ def gdn_mixer(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent
                        bool(scan))
 
 
-def gdn_conv_mixer(proj, conv_w, conv_state, cfg, a_log, dt_bias, norm_w, state, state_slot, parent):
-    z_off, b_off, a_off = _gdn_offsets(cfg)
-    out, conv = _C.gdn_conv_tree(proj, conv_w.contiguous(), conv_state, z_off, b_off, a_off, a_log, dt_bias, state,
-                                 state_slot, parent, norm_w, float(cfg.rms_norm_eps), cfg.gdn_k_heads, cfg.gdn_v_heads,
-                                 cfg.gdn_k_dim, cfg.gdn_v_dim)
-    return out, conv
-
-
 def gdn_recurrence(qkv, a, b, a_log, dt_bias, state, state_slot, parent, cfg):
     """Tree gated delta rule from raw gate inputs ``a`` / ``b`` ``[T, HV]``, without the output norm."""
     hv = cfg.gdn_v_heads

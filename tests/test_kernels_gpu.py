@@ -209,35 +209,6 @@ def test_gdn_mixer_against_reference(nat):
     assert torch.equal(solo[0], out[3])
 
 
-@pytest.mark.parametrize("hk,hv,kd", [(4, 4, 64), (2, 6, 64), (16, 48, 128)])
-def test_gdn_conv_fused_matches_separate(nat, hk, hv, kd):
-    """The conv fused into the tree recurrence gives bit-identical conv outputs and mixer outputs to the separate conv
-    kernel followed by the mixer, on a forest with paths longer than the conv window (key heads shared by several
-    value heads included)."""
-    import dataclasses
-
-    from eagle4_b200.models.configs import tiny_hybrid
-
-    cfg = dataclasses.replace(tiny_hybrid(), gdn_k_heads=hk, gdn_v_heads=hv, gdn_k_dim=kd, gdn_v_dim=kd)
-    C = cfg.gdn_conv_dim
-    T = 9
-    proj = _bf(T, C + cfg.gdn_value_dim + 2 * cfg.gdn_v_heads, seed=60)
-    wconv = _bf(C, cfg.conv_kernel, scale=0.3, seed=61)
-    a_log = torch.rand(cfg.gdn_v_heads, device="cuda").log1p()
-    dt_bias = torch.ones(cfg.gdn_v_heads, device="cuda")
-    gnorm = _bf(cfg.gdn_v_dim, seed=62)
-    slot = torch.tensor([0, 0, 0, 0, 0, 0, 1, 1, 1], dtype=torch.int32, device="cuda")
-    parent = torch.tensor([-1, 0, 1, 2, 3, 1, -1, 6, 6], dtype=torch.int32, device="cuda")
-    state = torch.randn(2, cfg.gdn_v_heads, cfg.gdn_v_dim, cfg.gdn_k_dim, device="cuda") * 0.1
-    cs = _bf(2, C, cfg.conv_kernel - 1, seed=63)
-    conv_ref = nat.causal_conv_tree(proj[:, :C], cs, slot, parent, wconv)
-    out_ref = nat.gdn_mixer(conv_ref, proj, cfg, a_log, dt_bias, gnorm, state, slot, parent, False)
-    out, conv = nat.gdn_conv_mixer(proj, wconv, cs, cfg, a_log, dt_bias, gnorm, state, slot, parent)
-    assert torch.equal(conv, conv_ref)
-    assert torch.equal(out, out_ref)
-    nat.check_errors()
-
-
 def test_conv_tree(nat):
     T, C, S, W = 6, 96, 2, 4
     x, w = _bf(T, C, seed=40), _bf(C, W, seed=41)
