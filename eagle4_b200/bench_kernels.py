@@ -23,6 +23,15 @@ def _peak_gbs() -> float:
         return 6650.0
 
 
+def _peak_tflops() -> float:
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        return 1590.0
+
+
 def time_fn(fn, iters: int = 20, warmup: int = 3, graph: bool = True) -> float:
     """Mean device time of one ``fn`` call in microseconds. With ``graph`` the ``iters`` calls are captured in one
     CUDA graph and replayed, so host launch cost does not hide the device time of small kernels."""
@@ -88,8 +97,10 @@ def main() -> None:
                 fn = lambda: native.linear(x, next(nxt))  # noqa: E731
             us = time_fn(fn, args.iters, args.warmup, not args.eager)
             gbs = (n * k * 2 + t * k * 2 + t * n * 2) / (us * 1e-6) / 1e9
+            tflops = 2.0 * n * k * t / (us * 1e-6) / 1e12
             rows.append({"kernel": name, "N": n, "K": k, "T": t, "us": round(us, 2), "GB/s": round(gbs, 1),
-                         "frac_of_measured_hbm": round(gbs / peak, 3)})
+                         "frac_of_measured_hbm": round(gbs / peak, 3), "TFLOP/s": round(tflops, 1),
+                         "frac_of_measured_bf16": round(tflops / _peak_tflops(), 3)})
             print(json.dumps(rows[-1]), flush=True)
         del w0, copies
     if not args.only or "attn_verify" in args.only:
