@@ -9,10 +9,7 @@ torch::Tensor rmsnorm(const torch::Tensor& x, const torch::Tensor& w, double eps
 torch::Tensor concat_norms(const torch::Tensor& e, const torch::Tensor& h, const torch::Tensor& we,
                            const torch::Tensor& wh, double eps);
 torch::Tensor embedding(const torch::Tensor& ids, const torch::Tensor& table);
-torch::Tensor sigmoid_gate(const torch::Tensor& o, const torch::Tensor& gate);
 torch::Tensor gated_rmsnorm(const torch::Tensor& o, const torch::Tensor& z, const torch::Tensor& w, double eps);
-std::vector<torch::Tensor> gdn_gates(const torch::Tensor& a, const torch::Tensor& b, const torch::Tensor& a_log,
-                                     const torch::Tensor& dt_bias);
 torch::Tensor qkv_prepare(const torch::Tensor& qkv, const torch::Tensor& pos, const torch::Tensor& slot,
                           torch::Tensor kc, torch::Tensor vc, const c10::optional<torch::Tensor>& qn,
                           const c10::optional<torch::Tensor>& kn, bool norm_offset, const torch::Tensor& cos_t,
@@ -118,9 +115,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm", &e4::rmsnorm);
   m.def("concat_norms", &e4::concat_norms);
   m.def("embedding", &e4::embedding);
-  m.def("sigmoid_gate", &e4::sigmoid_gate);
   m.def("gated_rmsnorm", &e4::gated_rmsnorm);
-  m.def("gdn_gates", &e4::gdn_gates);
   m.def("qkv_prepare", &e4::qkv_prepare);
   m.def("argmax_reduce", &e4::argmax_reduce);
   m.def("kv_commit", &e4::kv_commit);

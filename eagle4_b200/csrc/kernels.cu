@@ -120,15 +120,6 @@ __global__ void embedding_kernel(const int64_t* __restrict__ ids, const __nv_bfl
   for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
 }
 
-__global__ void sigmoid_gate_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ g, int ldg,
-                                    __nv_bfloat16* __restrict__ y, int D) {
-  pdl_wait();
-  pdl_trigger();
-  const size_t r = blockIdx.x;
-  for (int i = threadIdx.x; i < D; i += blockDim.x)
-    y[r * D + i] = __float2bfloat16(bf(o[r * D + i]) * sigmoidf_(bf(g[r * ldg + i])));
-}
-
 // per (row, group): rmsnorm over D then * silu(z)
 __global__ void gated_rmsnorm_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ z, int ldz,
                                      const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y, int T, int G,
@@ -151,18 +142,6 @@ __global__ void gated_rmsnorm_kernel(const __nv_bfloat16* __restrict__ o, const 
     const float n = bf(orow[i]) * rs * bf(w[i]);
     y[(size_t(r) * G + g) * D + i] = __float2bfloat16(n * silu(bf(z[size_t(r) * ldz + g * D + i])));
   }
-}
-
-__global__ void gdn_gates_kernel(const __nv_bfloat16* __restrict__ a, const __nv_bfloat16* __restrict__ b, int lda,
-                                 const float* __restrict__ a_log, const float* __restrict__ dt_bias, float* g,
-                                 float* beta, int T, int HV) {
-  pdl_wait();
-  pdl_trigger();
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= T * HV) return;
-  const int r = i / HV, h = i % HV;
-  g[i] = -__expf(a_log[h]) * softplusf_(bf(a[size_t(r) * lda + h]) + dt_bias[h]);
-  beta[i] = sigmoidf_(bf(b[size_t(r) * lda + h]));
 }
 
 // Split the fused attention projection, RMS-normalise q and k per head (optional), rotate the first ``rot`` dims
@@ -335,17 +314,6 @@ torch::Tensor embedding(const torch::Tensor& ids, const torch::Tensor& table) {
   return y;
 }
 
-torch::Tensor sigmoid_gate(const torch::Tensor& o, const torch::Tensor& gate) {
-  const at::cuda::CUDAGuard g(o.device());
-  auto oc = o.contiguous();
-  auto y = torch::empty_like(oc);
-  const int T = oc.size(0), D = oc.size(1);
-  if (T)
-    C10_CUDA_CHECK(launch_pdl(sigmoid_gate_kernel, T, 256, 0, at::cuda::getCurrentCUDAStream().stream(), CBF16(oc), CBF16(gate), gate.stride(0),
-                                                                         BF16(y), D));
-  return y;
-}
-
 torch::Tensor gated_rmsnorm(const torch::Tensor& o, const torch::Tensor& z, const torch::Tensor& w, double eps) {
   const at::cuda::CUDAGuard g(o.device());
   auto oc = o.contiguous();
@@ -359,20 +327,6 @@ torch::Tensor gated_rmsnorm(const torch::Tensor& o, const torch::Tensor& z, cons
                               BF16(y), T, G, D, float(eps)));
   }
   return y;
-}
-
-std::vector<torch::Tensor> gdn_gates(const torch::Tensor& a, const torch::Tensor& b, const torch::Tensor& a_log,
-                                     const torch::Tensor& dt_bias) {
-  const at::cuda::CUDAGuard g(a.device());
-  const int T = a.size(0), HV = a.size(1);
-  TORCH_CHECK(a.stride(0) == b.stride(0) && a.stride(1) == 1 && b.stride(1) == 1);
-  auto f = a.options().dtype(torch::kFloat32);
-  auto gg = torch::empty({T, HV}, f), beta = torch::empty({T, HV}, f);
-  if (T)
-    C10_CUDA_CHECK(launch_pdl(gdn_gates_kernel, (T * HV + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream().stream(), 
-        CBF16(a), CBF16(b), a.stride(0), a_log.data_ptr<float>(), dt_bias.data_ptr<float>(), gg.data_ptr<float>(),
-        beta.data_ptr<float>(), T, HV));
-  return {gg, beta};
 }
 
 torch::Tensor qkv_prepare(const torch::Tensor& qkv, const torch::Tensor& pos, const torch::Tensor& slot,

@@ -64,10 +64,6 @@ def embedding(ids: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
     return _nat().embedding(ids, table) if _cuda(table) else ref.embedding(ids, table)
 
 
-def sigmoid_gate(o: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
-    return _nat().sigmoid_gate(o, gate) if _cuda(o) else ref.sigmoid_gate(o, gate)
-
-
 def concat_norms(e, h, we, wh, eps: float) -> torch.Tensor:
     return _nat().concat_norms(e, h, we, wh, eps) if _cuda(e) else ref.concat_norms(e, h, we, wh, eps)
 
@@ -109,10 +105,6 @@ def gdn_commit_all(convs, projs, states, conv_states, a_logs, dt_biases, slots, 
         return
     fn = _nat().gdn_commit_all if _cuda(slots) else ref.gdn_commit_all
     return fn(convs, projs, states, conv_states, a_logs, dt_biases, slots, rows, n_rows, cfg)
-
-
-def gdn_gates(a, b, a_log, dt_bias):
-    return _nat().gdn_gates(a, b, a_log, dt_bias) if _cuda(a) else ref.gdn_gates(a, b, a_log, dt_bias)
 
 
 def gdn_tree(qkv, g, beta, state, state_slot, parent, cfg, scan: bool):

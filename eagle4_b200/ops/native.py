@@ -131,21 +131,12 @@ def embedding(ids, table):
     return _C.embedding(ids, table)
 
 
-def sigmoid_gate(o, gate):
-    return _C.sigmoid_gate(o, gate)
-
-
 def concat_norms(e, h, we, wh, eps):
     return _C.concat_norms(e, h, we, wh, float(eps))
 
 
 def gated_rmsnorm(o, z, w, eps):
     return _C.gated_rmsnorm(o, z, w, float(eps))
-
-
-def gdn_gates(a, b, a_log, dt_bias):
-    g, beta = _C.gdn_gates(a, b, a_log, dt_bias)
-    return g, beta
 
 
 # attention --------------------------------------------------------------------------------------------------------
