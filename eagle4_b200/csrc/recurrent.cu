@@ -280,10 +280,14 @@ __global__ void __launch_bounds__(128) gdn_kernel(GdnArgs a, const int* __restri
 }
 
 // Scan mode (prefill chains) with the value dimension split over CTAs: the delta rule's value rows are independent
-// (S[v, :] only meets v's own value), so CTA (head, v-slice) runs one warp over kScanV value columns of one head and
-// writes the raw output o (bf16); the gated RMSNorm over the head's V values follows as its own kernel. One warp per
-// CTA: the staging of kGdnTile tokens and the token loop need no block barrier, and 4x more CTAs share the work.
+// (S[v, :] only meets v's own value), so CTA (head, request segment, v-slice) owns kScanV value columns of one head
+// and writes the raw output o (bf16); the gated RMSNorm over the head's V values follows as its own kernel. Four
+// lanes share a value column, each holding a quarter of the state row S[v, :] (elements 16m + 4r + e, e < 4, for
+// lane quarter r: the four quarters read one contiguous 64-byte run of a staged k / q row, no bank conflicts), so a
+// token step is K/4 multiply-adds per lane and two xor-shuffles per K-long reduction; the CTA's four warps run on the
+// SM's four schedulers instead of one warp doing the whole row.
 constexpr int kScanV = 32;
+constexpr int kScanThreads = 4 * kScanV;
 template <int K>
 struct ScanStage {
   float q[kGdnTile][K];
@@ -292,30 +296,47 @@ struct ScanStage {
   float g[kGdnTile], beta[kGdnTile];
 };
 
+// Sum over the four lanes of a value column; every lane gets the same value ((x0 + x1) + (x2 + x3) in any lane order,
+// float addition being commutative).
+__device__ __forceinline__ float quad_sum(float x) {
+  x += __shfl_xor_sync(0xffffffffu, x, 1);
+  x += __shfl_xor_sync(0xffffffffu, x, 2);
+  return x;
+}
+
 template <int K>
-__global__ void __launch_bounds__(32) gdn_scan_kernel(GdnArgs a, const int* __restrict__ slot,
-                                                      const int* __restrict__ seg, __nv_bfloat16* __restrict__ out) {
+__global__ void __launch_bounds__(kScanThreads) gdn_scan_kernel(GdnArgs a, const int* __restrict__ slot,
+                                                                const int* __restrict__ seg,
+                                                                __nv_bfloat16* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ __align__(16) uint8_t scan_smem[];
   ScanStage<K>& st = *reinterpret_cast<ScanStage<K>*>(scan_smem);
   const int h = blockIdx.x, vs = blockIdx.z * kScanV;
-  const int lane = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int col = tid >> 2, qr = tid & 3;
   const int kh = h / (a.HV / a.HK);
-  const int v = vs + lane;
+  const int v = vs + col;
   const int vc = min(v, a.V - 1);
-  constexpr int PL = K / 32;
+  constexpr int PL = K / 32;   // elements per lane in the per-token l2 norms
+  constexpr int KQ = K / 4;    // state elements per lane
+  constexpr int NG = KQ / 4;   // float4 groups per lane
   const int r0 = seg[blockIdx.y], r1 = seg[blockIdx.y + 1];
   float* stp = a.state + ((size_t(slot[r0]) * a.HV + h) * a.V + vc) * K;
-  float S[K];
-  load_state<K>(S, stp);
+  float S[KQ];
+#pragma unroll
+  for (int m = 0; m < NG; ++m) {
+    const float4 t4 = *reinterpret_cast<const float4*>(stp + 16 * m + 4 * qr);
+    S[4 * m] = t4.x; S[4 * m + 1] = t4.y; S[4 * m + 2] = t4.z; S[4 * m + 3] = t4.w;
+  }
   for (int p0 = r0; p0 < r1; p0 += kGdnTile) {
     const int n = min(kGdnTile, r1 - p0);
-    __syncwarp();
-    // stage raw q and k of the tile's tokens with independent 16-byte loads (one memory latency for the tile), this
-    // slice's v and the gates (lane j: token j), then l2-normalise q (scaled by K^-1/2) and k token by token
+    __syncthreads();
+    // stage raw q and k of the tile's tokens with independent 16-byte loads (one memory latency for the tile), the
+    // slice's v and the gates (thread j: token j), then l2-normalise q (scaled by K^-1/2) and k (warp w: tokens w,
+    // w + 4, ...)
     constexpr int VEC = K / 8;  // 16-byte vectors per head row
-    for (int e = lane; e < n * 2 * VEC; e += 32) {
+    for (int e = tid; e < n * 2 * VEC; e += kScanThreads) {
       const int j = e / (2 * VEC), w = e % (2 * VEC), which = w / VEC, c = w % VEC;
       const __nv_bfloat16* base = a.qkv + size_t(p0 + j) * a.ldq + (which ? a.HK * K : 0) + kh * K;
       const uint4 raw = reinterpret_cast<const uint4*>(base)[c];
@@ -328,14 +349,17 @@ __global__ void __launch_bounds__(32) gdn_scan_kernel(GdnArgs a, const int* __re
         dst[2 * t + 1] = f.y;
       }
     }
-    for (int j = 0; j < n; ++j) st.v[j][lane] = bf(a.qkv[size_t(p0 + j) * a.ldq + 2 * a.HK * K + h * a.V + vc]);
-    if (lane < n) {
-      const float2 gb = gdn_gate(a, p0 + lane, h);
-      st.g[lane] = gb.x;
-      st.beta[lane] = gb.y;
+    for (int e = tid; e < n * kScanV; e += kScanThreads) {
+      const int j = e / kScanV, c = e % kScanV;
+      st.v[j][c] = bf(a.qkv[size_t(p0 + j) * a.ldq + 2 * a.HK * K + h * a.V + min(vs + c, a.V - 1)]);
     }
-    __syncwarp();
-    for (int j = 0; j < n; ++j) {
+    if (tid < n) {
+      const float2 gb = gdn_gate(a, p0 + tid, h);
+      st.g[tid] = gb.x;
+      st.beta[tid] = gb.y;
+    }
+    __syncthreads();
+    for (int j = warp; j < n; j += kScanThreads / 32) {
       float q2 = 0.f, k2 = 0.f;
 #pragma unroll
       for (int i = 0; i < PL; ++i) {
@@ -351,38 +375,49 @@ __global__ void __launch_bounds__(32) gdn_scan_kernel(GdnArgs a, const int* __re
         st.k[j][lane * PL + i] *= rk;
       }
     }
-    __syncwarp();
+    __syncthreads();
     for (int j = 0; j < n; ++j) {
       const float decay = __expf(st.g[j]);
+      const float4* kr = reinterpret_cast<const float4*>(st.k[j]) + qr;
+      const float4* qrow = reinterpret_cast<const float4*>(st.q[j]) + qr;
+      float kk[KQ];
       float k0 = 0.f, k1 = 0.f, k2 = 0.f, k3 = 0.f;
 #pragma unroll
-      for (int i = 0; i < K; i += 4) {
-        S[i] *= decay;
-        S[i + 1] *= decay;
-        S[i + 2] *= decay;
-        S[i + 3] *= decay;
-        k0 = fmaf(S[i], st.k[j][i], k0);
-        k1 = fmaf(S[i + 1], st.k[j][i + 1], k1);
-        k2 = fmaf(S[i + 2], st.k[j][i + 2], k2);
-        k3 = fmaf(S[i + 3], st.k[j][i + 3], k3);
+      for (int m = 0; m < NG; ++m) {
+        const float4 t4 = kr[4 * m];
+        kk[4 * m] = t4.x; kk[4 * m + 1] = t4.y; kk[4 * m + 2] = t4.z; kk[4 * m + 3] = t4.w;
+        S[4 * m] *= decay;
+        S[4 * m + 1] *= decay;
+        S[4 * m + 2] *= decay;
+        S[4 * m + 3] *= decay;
+        k0 = fmaf(S[4 * m], t4.x, k0);
+        k1 = fmaf(S[4 * m + 1], t4.y, k1);
+        k2 = fmaf(S[4 * m + 2], t4.z, k2);
+        k3 = fmaf(S[4 * m + 3], t4.w, k3);
       }
-      const float delta = (st.v[j][lane] - ((k0 + k1) + (k2 + k3))) * st.beta[j];
+      const float delta = (st.v[j][col] - quad_sum((k0 + k1) + (k2 + k3))) * st.beta[j];
       float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
 #pragma unroll
-      for (int i = 0; i < K; i += 4) {
-        S[i] = fmaf(st.k[j][i], delta, S[i]);
-        S[i + 1] = fmaf(st.k[j][i + 1], delta, S[i + 1]);
-        S[i + 2] = fmaf(st.k[j][i + 2], delta, S[i + 2]);
-        S[i + 3] = fmaf(st.k[j][i + 3], delta, S[i + 3]);
-        o0 = fmaf(S[i], st.q[j][i], o0);
-        o1 = fmaf(S[i + 1], st.q[j][i + 1], o1);
-        o2 = fmaf(S[i + 2], st.q[j][i + 2], o2);
-        o3 = fmaf(S[i + 3], st.q[j][i + 3], o3);
+      for (int m = 0; m < NG; ++m) {
+        const float4 q4 = qrow[4 * m];
+        S[4 * m] = fmaf(kk[4 * m], delta, S[4 * m]);
+        S[4 * m + 1] = fmaf(kk[4 * m + 1], delta, S[4 * m + 1]);
+        S[4 * m + 2] = fmaf(kk[4 * m + 2], delta, S[4 * m + 2]);
+        S[4 * m + 3] = fmaf(kk[4 * m + 3], delta, S[4 * m + 3]);
+        o0 = fmaf(S[4 * m], q4.x, o0);
+        o1 = fmaf(S[4 * m + 1], q4.y, o1);
+        o2 = fmaf(S[4 * m + 2], q4.z, o2);
+        o3 = fmaf(S[4 * m + 3], q4.w, o3);
       }
-      if (v < a.V) out[(size_t(p0 + j) * a.HV + h) * a.V + v] = __float2bfloat16((o0 + o1) + (o2 + o3));
+      const float o = quad_sum((o0 + o1) + (o2 + o3));
+      if (qr == 0 && v < a.V) out[(size_t(p0 + j) * a.HV + h) * a.V + v] = __float2bfloat16(o);
     }
   }
-  if (v < a.V) save_state<K>(S, stp);
+  if (v < a.V) {
+#pragma unroll
+    for (int m = 0; m < NG; ++m)
+      *reinterpret_cast<float4*>(stp + 16 * m + 4 * qr) = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
+  }
 }
 
 // Per-layer pointers of an all-layers commit.
@@ -658,11 +693,11 @@ torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int6
     auto raw = norm_w.numel() ? torch::empty({T, HV * V}, qkv.options()) : out;
     if (K == 128) {
       gdn_smem_attr(gdn_scan_kernel<128>, sizeof(ScanStage<128>));
-      C10_CUDA_CHECK(launch_pdl(gdn_scan_kernel<128>, grid, 32, sizeof(ScanStage<128>), st.stream(), a,
+      C10_CUDA_CHECK(launch_pdl(gdn_scan_kernel<128>, grid, kScanThreads, sizeof(ScanStage<128>), st.stream(), a,
                                 sl.data_ptr<int>(), seg.data_ptr<int>(), BFP(raw)));
     } else {
       gdn_smem_attr(gdn_scan_kernel<64>, sizeof(ScanStage<64>));
-      C10_CUDA_CHECK(launch_pdl(gdn_scan_kernel<64>, grid, 32, sizeof(ScanStage<64>), st.stream(), a,
+      C10_CUDA_CHECK(launch_pdl(gdn_scan_kernel<64>, grid, kScanThreads, sizeof(ScanStage<64>), st.stream(), a,
                                 sl.data_ptr<int>(), seg.data_ptr<int>(), BFP(raw)));
     }
     C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -209,6 +209,39 @@ def test_gdn_mixer_against_reference(nat):
     assert torch.equal(solo[0], out[3])
 
 
+@pytest.mark.parametrize("hk,hv,kd", [(4, 4, 64), (2, 6, 128)])
+def test_gdn_scan_against_reference(nat, hk, hv, kd):
+    """Prefill scan (contiguous rows per request, state updated in place) against the float definition: the mixer
+    output and the final state, with one request longer than a 32-token staging tile and key heads shared by several
+    value heads."""
+    import dataclasses
+
+    from eagle4_b200.models.configs import tiny_hybrid
+
+    cfg = dataclasses.replace(tiny_hybrid(), gdn_k_heads=hk, gdn_v_heads=hv, gdn_k_dim=kd, gdn_v_dim=kd)
+    C = cfg.gdn_conv_dim
+    lens = (45, 9)
+    T = sum(lens)
+    proj = _bf(T, C + cfg.gdn_value_dim + 2 * cfg.gdn_v_heads, seed=70)
+    conv = _bf(T, C, seed=71)
+    a_log = torch.rand(cfg.gdn_v_heads, device="cuda").log1p()
+    dt_bias = torch.ones(cfg.gdn_v_heads, device="cuda")
+    gnorm = _bf(cfg.gdn_v_dim, seed=72)
+    state = torch.randn(3, cfg.gdn_v_heads, cfg.gdn_v_dim, cfg.gdn_k_dim, device="cuda") * 0.1
+    slot = torch.tensor([2] * lens[0] + [0] * lens[1], dtype=torch.int32, device="cuda")
+    parent = torch.tensor([-1] + list(range(lens[0] - 1)) + [-1] + list(range(lens[0], T - 1)), dtype=torch.int32,
+                          device="cuda")
+    cpu = lambda t: t.cpu().float()  # noqa: E731
+    st_ref = state.cpu().clone()
+    want = ref.gdn_mixer(cpu(conv), cpu(proj), cfg, a_log.cpu(), dt_bias.cpu(), cpu(gnorm), st_ref, slot.cpu(),
+                         parent.cpu(), True)
+    st = state.clone()
+    out = nat.gdn_mixer(conv, proj, cfg, a_log, dt_bias, gnorm, st, slot, parent, True)
+    _close(out, want, 3e-2)
+    _close(st, st_ref, 2e-3)
+    nat.check_errors()
+
+
 def test_conv_tree(nat):
     T, C, S, W = 6, 96, 2, 4
     x, w = _bf(T, C, seed=40), _bf(C, W, seed=41)
