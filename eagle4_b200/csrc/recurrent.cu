@@ -281,13 +281,14 @@ __global__ void __launch_bounds__(128) gdn_kernel(GdnArgs a, const int* __restri
 
 // Scan mode (prefill chains) with the value dimension split over CTAs: the delta rule's value rows are independent
 // (S[v, :] only meets v's own value), so CTA (head, request segment, v-slice) owns kScanV value columns of one head
-// and writes the raw output o (bf16); the gated RMSNorm over the head's V values follows as its own kernel. Four
-// lanes share a value column, each holding a quarter of the state row S[v, :] (elements 16m + 4r + e, e < 4, for
-// lane quarter r: the four quarters read one contiguous 64-byte run of a staged k / q row, no bank conflicts), so a
-// token step is K/4 multiply-adds per lane and two xor-shuffles per K-long reduction; the CTA's four warps run on the
-// SM's four schedulers instead of one warp doing the whole row.
+// and writes the raw output o (bf16); the gated RMSNorm over the head's V values follows as its own kernel.
+// kScanLanes lanes share a value column, each holding a 1/kScanLanes slice of the state row S[v, :] (elements
+// 4 * kScanLanes * m + 4r + e, e < 4, for lane r of the column: the column's lanes read one contiguous run of a staged
+// k / q row, no bank conflicts), so a token step is K / kScanLanes multiply-adds per lane and log2(kScanLanes)
+// xor-shuffles per K-long reduction; the CTA's warps spread over the SM's four schedulers.
 constexpr int kScanV = 32;
-constexpr int kScanThreads = 4 * kScanV;
+constexpr int kScanLanes = 4;
+constexpr int kScanThreads = kScanLanes * kScanV;
 template <int K>
 struct ScanStage {
   float q[kGdnTile][K];
@@ -296,11 +297,11 @@ struct ScanStage {
   float g[kGdnTile], beta[kGdnTile];
 };
 
-// Sum over the four lanes of a value column; every lane gets the same value ((x0 + x1) + (x2 + x3) in any lane order,
-// float addition being commutative).
-__device__ __forceinline__ float quad_sum(float x) {
-  x += __shfl_xor_sync(0xffffffffu, x, 1);
-  x += __shfl_xor_sync(0xffffffffu, x, 2);
+// Sum over the kScanLanes lanes of a value column by xor butterflies; every lane gets the same value (each level
+// adds two equal-shaped partial sums, and float addition is commutative).
+__device__ __forceinline__ float column_sum(float x) {
+#pragma unroll
+  for (int o = 1; o < kScanLanes; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
   return x;
 }
 
@@ -314,19 +315,20 @@ __global__ void __launch_bounds__(kScanThreads) gdn_scan_kernel(GdnArgs a, const
   ScanStage<K>& st = *reinterpret_cast<ScanStage<K>*>(scan_smem);
   const int h = blockIdx.x, vs = blockIdx.z * kScanV;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int col = tid >> 2, qr = tid & 3;
+  const int col = tid / kScanLanes, qr = tid % kScanLanes;
   const int kh = h / (a.HV / a.HK);
   const int v = vs + col;
   const int vc = min(v, a.V - 1);
   constexpr int PL = K / 32;   // elements per lane in the per-token l2 norms
-  constexpr int KQ = K / 4;    // state elements per lane
-  constexpr int NG = KQ / 4;   // float4 groups per lane
+  constexpr int KQ = K / kScanLanes;  // state elements per lane
+  constexpr int NG = KQ / 4;          // float4 groups per lane
+  constexpr int GS = 4 * kScanLanes;  // floats between a lane's consecutive groups
   const int r0 = seg[blockIdx.y], r1 = seg[blockIdx.y + 1];
   float* stp = a.state + ((size_t(slot[r0]) * a.HV + h) * a.V + vc) * K;
   float S[KQ];
 #pragma unroll
   for (int m = 0; m < NG; ++m) {
-    const float4 t4 = *reinterpret_cast<const float4*>(stp + 16 * m + 4 * qr);
+    const float4 t4 = *reinterpret_cast<const float4*>(stp + GS * m + 4 * qr);
     S[4 * m] = t4.x; S[4 * m + 1] = t4.y; S[4 * m + 2] = t4.z; S[4 * m + 3] = t4.w;
   }
   for (int p0 = r0; p0 < r1; p0 += kGdnTile) {
@@ -384,7 +386,7 @@ __global__ void __launch_bounds__(kScanThreads) gdn_scan_kernel(GdnArgs a, const
       float k0 = 0.f, k1 = 0.f, k2 = 0.f, k3 = 0.f;
 #pragma unroll
       for (int m = 0; m < NG; ++m) {
-        const float4 t4 = kr[4 * m];
+        const float4 t4 = kr[kScanLanes * m];
         kk[4 * m] = t4.x; kk[4 * m + 1] = t4.y; kk[4 * m + 2] = t4.z; kk[4 * m + 3] = t4.w;
         S[4 * m] *= decay;
         S[4 * m + 1] *= decay;
@@ -395,11 +397,11 @@ __global__ void __launch_bounds__(kScanThreads) gdn_scan_kernel(GdnArgs a, const
         k2 = fmaf(S[4 * m + 2], t4.z, k2);
         k3 = fmaf(S[4 * m + 3], t4.w, k3);
       }
-      const float delta = (st.v[j][col] - quad_sum((k0 + k1) + (k2 + k3))) * st.beta[j];
+      const float delta = (st.v[j][col] - column_sum((k0 + k1) + (k2 + k3))) * st.beta[j];
       float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
 #pragma unroll
       for (int m = 0; m < NG; ++m) {
-        const float4 q4 = qrow[4 * m];
+        const float4 q4 = qrow[kScanLanes * m];
         S[4 * m] = fmaf(kk[4 * m], delta, S[4 * m]);
         S[4 * m + 1] = fmaf(kk[4 * m + 1], delta, S[4 * m + 1]);
         S[4 * m + 2] = fmaf(kk[4 * m + 2], delta, S[4 * m + 2]);
@@ -409,14 +411,14 @@ __global__ void __launch_bounds__(kScanThreads) gdn_scan_kernel(GdnArgs a, const
         o2 = fmaf(S[4 * m + 2], q4.z, o2);
         o3 = fmaf(S[4 * m + 3], q4.w, o3);
       }
-      const float o = quad_sum((o0 + o1) + (o2 + o3));
+      const float o = column_sum((o0 + o1) + (o2 + o3));
       if (qr == 0 && v < a.V) out[(size_t(p0 + j) * a.HV + h) * a.V + v] = __float2bfloat16(o);
     }
   }
   if (v < a.V) {
 #pragma unroll
     for (int m = 0; m < NG; ++m)
-      *reinterpret_cast<float4*>(stp + 16 * m + 4 * qr) = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
+      *reinterpret_cast<float4*>(stp + GS * m + 4 * qr) = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
   }
 }
 
