@@ -34,9 +34,74 @@ BASELINE_TPS = 302.7  # SGLang TP1, one request, EAGLE-4 tokens/s on 1x B300 (re
 METRIC = "EAGLE-4 output tok/s and speedup vs plain decode, batch 1–512, TP 1/2/4/8"
 
 
-def reference_unavailable() -> str:
-    return ("eagle-harness is an engine plugin: its serving path needs SGLang or TokenSpeed with its hooks, or "
-            "vLLM>=0.32 (installed: vllm 0.22, no sglang, no tokenspeed), so it cannot generate on this box")
+REF_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+
+
+def _version(module: str):
+    """``(installed version or None, import error or None)`` of an engine module, without importing it twice."""
+    import importlib
+    import importlib.metadata as md
+
+    try:
+        mod = importlib.import_module(module)
+    except Exception as e:  # noqa: BLE001 - any import failure means the engine cannot serve here
+        return None, f"{type(e).__name__}: {e}"[:120]
+    try:
+        return md.version(module), None
+    except md.PackageNotFoundError:
+        return getattr(mod, "__version__", "unknown"), None
+
+
+def reference_probe() -> dict:
+    """What the reference's own serving path needs, checked on this machine: the unmodified reference package from
+    ``baseline/_ref`` (imported through its public API) and the engines it plugs into (its ``pyproject.toml`` names
+    hook-carrying SGLang, TokenSpeed, or vLLM >= 0.32). Returns the findings and, when it cannot generate, why."""
+    found = {"baseline_ref": os.path.isdir(REF_DIR)}
+    if found["baseline_ref"] and REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        import eagle_harness  # noqa: F401
+        from eagle_harness.core.config import parse_harness_config
+
+        parse_harness_config('{"mode": "serve"}')  # the reference's public config entry point works
+        import importlib.metadata as md
+
+        try:
+            found["eagle_harness"] = md.version("eagle-harness")
+        except md.PackageNotFoundError:
+            found["eagle_harness"] = "imported"
+        found["eagle_harness_path"] = os.path.dirname(eagle_harness.__file__)
+    except Exception as e:  # noqa: BLE001
+        found["eagle_harness"] = None
+        found["eagle_harness_error"] = f"{type(e).__name__}: {e}"[:160]
+    engines = {}
+    for mod in ("sglang", "vllm", "tokenspeed"):
+        ver, err = _version(mod)
+        engines[mod] = ver if ver else f"missing ({err})"
+    found["engines"] = engines
+    usable = []
+    if not engines["sglang"].startswith("missing"):
+        usable.append("sglang")
+    if not engines["tokenspeed"].startswith("missing"):
+        usable.append("tokenspeed")
+    ver = engines["vllm"]
+    if not ver.startswith("missing"):
+        try:
+            major, minor = (int(x) for x in ver.split(".")[:2])
+            if (major, minor) >= (0, 32):
+                usable.append("vllm")
+        except ValueError:
+            pass
+    found["usable_engines"] = usable
+    if found["eagle_harness"] is None:
+        found["unavailable"] = "the reference package does not import from baseline/_ref: " + found[
+            "eagle_harness_error"]
+    elif not usable:
+        found["unavailable"] = (
+            "eagle-harness imports (" + str(found["eagle_harness"]) + ") but is an engine plugin: generating needs "
+            "hook-carrying SGLang or TokenSpeed, or vLLM>=0.32; found " +
+            ", ".join(f"{k} {v}" for k, v in engines.items()) + ", so it cannot generate on this box")
+    return found
 
 
 class ClockSampler:
@@ -101,8 +166,14 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
+        found = reference_probe()
         if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable": reference_unavailable()}))
+            if "unavailable" in found:
+                print(json.dumps({"impl": "reference", "unavailable": found.pop("unavailable"), "probe": found}))
+            else:  # an engine with the hooks is installed: its serving path is not wired into this bench
+                print(json.dumps({"impl": "reference", "unavailable": "a hook-carrying engine is installed ("
+                                  + ", ".join(found["usable_engines"]) + ") but this bench has no launcher for it",
+                                  "probe": found}))
         return
 
     import torch
@@ -154,6 +225,8 @@ def main() -> None:
         barrier()
         torch.cuda.synchronize()
         eng.stats.__init__()
+        if getattr(eng, "tree_choice", None) is not None:
+            eng.tree_choice.served.clear()  # the share below counts the timed rounds only
         native.LAUNCHES[0] = 0
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(local) as clk:
@@ -215,10 +288,9 @@ def main() -> None:
         "plain_tok_s": round(plain_tok * replicas / (plain_ms / 1e3), 2) if plain_ms else None,
         "speedup_vs_plain": round((spec_tok / spec_ms) / (plain_tok / plain_ms), 4) if plain_ms else None,
         "mean_accepted_per_round": round(accept, 3),
-        "served_choice": ({"native_round_share": round(
-            sum(v[2] for k, v in eng.tree_choice.samples.items() if k[1] == 0)
-            / max(1, sum(v[2] for v in eng.tree_choice.samples.values())), 3),
-            "rule": "per batch bucket: speculate or decode natively, whichever served more tokens per us"}
+        "served_choice": ({"native_round_share": round(eng.tree_choice.share(eng.tree_choice.NATIVE), 3),
+            "rule": "per batch bucket: speculate or decode natively, whichever served more tokens per us "
+                    "(settled rounds only: no eager run or graph capture inside the period)"}
             if getattr(eng, "tree_choice", None) is not None else None),
         "spec_equals_plain": same,
         "clocks": clocks,

@@ -548,6 +548,19 @@ int gemm_grid(long total, int max_ctas) {
   return int(std::max<long>(1, std::min<long>(max_ctas, by_work)));
 }
 
+// Pipeline stages for a token tile of ``nt`` columns: the stage cap, bounded by 200 KB of tiles.
+int stage_count(int nt) {
+  const int stage_bytes = kWTileBytes + nt * kTileK * 2;
+  return std::min(max_stages(), (200 * 1024) / stage_bytes);
+}
+
+// Dynamic shared memory of one launch: 1 KB alignment slack, the stages, barriers and TMEM handle (64 B), the
+// epilogue exchange buffer (16 x 64 floats), the folded-norm scales (256 floats) and 1 KB of slack.
+size_t smem_bytes(int stages, int nt) {
+  const int stage_bytes = kWTileBytes + nt * kTileK * 2;
+  return 1024 + size_t(stages) * stage_bytes + 64 + 16 * 64 * 4 + 256 * 4 + 1024;
+}
+
 struct Scratch {
   torch::Tensor ws, counters, err;
 };
@@ -608,8 +621,7 @@ int launch_chunks(const torch::Tensor& x, const torch::Tensor& w, int epi, F chu
     p.kb_total = kb_total;
     p.total = total;
     p.epi = epi;
-    const int stage_bytes = kWTileBytes + p.nt * kTileK * 2;
-    p.stages = std::min(max_stages(), (200 * 1024) / stage_bytes);
+    p.stages = stage_count(p.nt);
     const size_t ws_need = size_t(2) * grid * p.nt * kTileM;
     if (size_t(sc.ws.numel()) < ws_need) sc.ws = torch::empty({int64_t(ws_need)}, sc.ws.options());
     p.ws = sc.ws.data_ptr<float>();
@@ -621,8 +633,7 @@ int launch_chunks(const torch::Tensor& x, const torch::Tensor& w, int epi, F chu
     p.ldx = int(x.stride(0));
     TORCH_CHECK(!p.fold || K % 8 == 0, "gemm: a folded norm needs K % 8 == 0");
     CUtensorMap xmap = make_map(xp, tc, K, x.stride(0), p.nt);
-    const size_t smem = 1024 + size_t(p.stages) * stage_bytes + 64 + 16 * 64 * 4 + 256 * 4 + 1024;
-    C10_CUDA_CHECK(launch_pdl(gemm_kernel, grid, kThreads, smem, stream.stream(), wmap, xmap, p));
+    C10_CUDA_CHECK(launch_pdl(gemm_kernel, grid, kThreads, smem_bytes(p.stages, p.nt), stream.stream(), wmap, xmap, p));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     launched += grid;
   }
@@ -704,37 +715,26 @@ int64_t gemm_scatter(const torch::Tensor& x, const torch::Tensor& w, const std::
 }  // namespace e4
 
 // =====================================================================================================================
-// Allocation-free GEMM entry point. This has no counterpart in the reference.
+// Allocation-free GEMM entry point (declared in e4_noalloc.h, which states its callers, limits and sharing rules).
+// This has no counterpart in the reference.
 //
-// Some callers cannot allocate device memory: an inference host that hands this library only buffers it has already
-// allocated (and forbids allocation while it serves), code that runs inside a fixed memory budget it may not grow, or
-// a plain C program that links the library without any device allocator. The library's GEMM normally takes its
-// stream-K workspace (partial tiles, arrival counters, error word) from allocator-backed buffers; this entry point
-// runs the same kernel with that workspace in a fixed array in device memory instead:
-//
-//   int e4_gemm_bf16_noalloc(const void* x, int ldx, const void* w, int ldw, void* y, int ldy,
-//                            int T, int N, int K, void* stream);
-//
-// computes Y[T, N] = X[T, K] . W[N, K]^T (bf16 operands and output, fp32 accumulation, row-major with leading
-// dimensions in elements) on ``stream`` (a cudaStream_t; 0 for the legacy stream) and returns 0, or a non-zero code
-// for bad arguments (1) or a CUDA error (2).
-//
-// Limits: T <= 32 tokens per call, N <= 128 * 4096 weight rows, rows 16-byte aligned. The array holds 5.3 MB on every
-// GPU that loads the library, until the process exits.
-// The first call on a device (with that device current) looks up the array's device address and sets the kernel's
-// shared-memory limit; make that first call before any stream capture. Every call shares the one array and each call
-// clears the arrival counters it needs before its kernel starts, so two calls that overlap on the GPU (different
-// streams, or different host threads on one device) race on the array and must be serialised by the caller.
-// The function calls no device allocator (no cudaMalloc / cudaFree / allocating library routine).
+// The stream-K workspace of the regular entry point (partial tiles, per-tile arrival counters, error word) lives here
+// in one file-scope device array. Host code only ever sees the array's host-side stand-in symbol; the kernel gets the
+// device address that cudaGetSymbolAddress returns for the current device at the first call on that device.
 // =====================================================================================================================
+#include "e4_noalloc.h"
+
 namespace e4 {
 namespace noalloc {
 
-constexpr int kMaxTokens = 32;
+constexpr int kMaxTokens = E4_NOALLOC_MAX_TOKENS;
 constexpr int kMaxGrid = 160;   // CTAs (one per SM, B200 has 148)
-constexpr int kMaxTiles = 4096;
+constexpr int kMaxTiles = E4_NOALLOC_MAX_TILES;
 constexpr size_t kWsFloats = size_t(2) * kMaxGrid * kMaxTokens * gemm::kTileM;
-constexpr size_t kBytes = kWsFloats * sizeof(float) + kMaxTiles * sizeof(int) + 256;
+constexpr size_t kCountersOffset = kWsFloats * sizeof(float);
+constexpr size_t kErrOffset = kCountersOffset + size_t(kMaxTiles) * sizeof(int);
+constexpr size_t kBytes = kErrOffset + 256;
+static_assert(kBytes == E4_NOALLOC_SCRATCH_BYTES, "e4_noalloc.h states the array's size");
 
 static __device__ __align__(256) unsigned char scratch[kBytes];
 
@@ -742,17 +742,24 @@ constexpr int kMaxDevices = 64;
 std::mutex setup_mu;
 void* scratch_addr[kMaxDevices] = {};
 
+// Device address of the array on ``dev`` (the current device), looked up once per device.
 int setup(int dev, void** out) {
   std::lock_guard<std::mutex> g(setup_mu);
   if (!scratch_addr[dev]) {
     void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, scratch) != cudaSuccess || !ptr) return 2;
+    if (cudaGetSymbolAddress(&ptr, scratch) != cudaSuccess || !ptr) return E4_NOALLOC_CUDA_ERROR;
     if (cudaFuncSetAttribute(gemm::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
-      return 2;
+      return E4_NOALLOC_CUDA_ERROR;
     scratch_addr[dev] = ptr;
   }
   *out = scratch_addr[dev];
-  return 0;
+  return E4_NOALLOC_OK;
+}
+
+int current(void** base) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return E4_NOALLOC_CUDA_ERROR;
+  return setup(dev, base);
 }
 
 }  // namespace noalloc
@@ -762,19 +769,19 @@ extern "C" int e4_gemm_bf16_noalloc(const void* x, int ldx, const void* w, int l
                                     int K, void* stream) {
   using namespace e4;
   using namespace e4::gemm;
-  if (!x || !w || !y || T <= 0 || T > noalloc::kMaxTokens || N <= 0 || K <= 0) return 1;
-  if (ldx < K || ldw < K || ldy < N || (ldx * 2) % 16 || (ldw * 2) % 16) return 1;
-  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(w) % 16) return 1;
+  if (!x || !w || !y || T <= 0 || T > noalloc::kMaxTokens || N <= 0 || K <= 0) return E4_NOALLOC_BAD_ARGS;
+  if (ldx < K || ldw < K || ldy < N || (ldx * 2) % 16 || (ldw * 2) % 16) return E4_NOALLOC_BAD_ARGS;
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(w) % 16) return E4_NOALLOC_BAD_ARGS;
   const int n_tiles = (N + kTileM - 1) / kTileM;
-  if (n_tiles > noalloc::kMaxTiles) return 1;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= noalloc::kMaxDevices) return 2;
+  if (n_tiles > noalloc::kMaxTiles) return E4_NOALLOC_BAD_ARGS;
   void* base = nullptr;
-  if (noalloc::setup(dev, &base)) return 2;
-  int sms = 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 2;
+  if (const int rc = noalloc::current(&base)) return rc;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return E4_NOALLOC_CUDA_ERROR;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return E4_NOALLOC_CUDA_ERROR;
   const int kb_total = (K + kTileK - 1) / kTileK;
   const long total = long(n_tiles) * kb_total;
+  // the regular entry point's grid and pipeline (same stream-K cut points, so the same reduction order)
   const int grid = gemm::gemm_grid(total, std::min(sms, noalloc::kMaxGrid));
   Params p{};
   p.T = T;
@@ -785,11 +792,11 @@ extern "C" int e4_gemm_bf16_noalloc(const void* x, int ldx, const void* w, int l
   p.kb_total = kb_total;
   p.total = total;
   p.epi = kPlain;
-  const int stage_bytes = kWTileBytes + p.nt * kTileK * 2;
-  p.stages = std::min(10, (200 * 1024) / stage_bytes);
-  p.ws = reinterpret_cast<float*>(base);
-  p.counters = reinterpret_cast<int*>(reinterpret_cast<unsigned char*>(base) + noalloc::kWsFloats * sizeof(float));
-  p.err = p.counters + noalloc::kMaxTiles;
+  p.stages = stage_count(p.nt);
+  unsigned char* b = reinterpret_cast<unsigned char*>(base);
+  p.ws = reinterpret_cast<float*>(b);
+  p.counters = reinterpret_cast<int*>(b + noalloc::kCountersOffset);
+  p.err = reinterpret_cast<int*>(b + noalloc::kErrOffset);
   p.y = reinterpret_cast<__nv_bfloat16*>(y);
   p.ldy = ldy;
   CUtensorMap wmap, xmap;
@@ -797,11 +804,26 @@ extern "C" int e4_gemm_bf16_noalloc(const void* x, int ldx, const void* w, int l
     wmap = make_map(w, N, K, ldw, kTileM);
     xmap = make_map(x, T, K, ldx, p.nt);
   } catch (...) {
-    return 2;
+    return E4_NOALLOC_CUDA_ERROR;
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(p.counters, 0, sizeof(int) * (n_tiles + 1), st) != cudaSuccess) return 2;
-  const size_t smem = 1024 + size_t(p.stages) * stage_bytes + 64 + 16 * 64 * 4 + 1024;
-  if (launch_pdl(gemm_kernel, grid, kThreads, smem, st, wmap, xmap, p) != cudaSuccess) return 2;
-  return 0;
+  // the counters this call's tiles use, and the error word (the last call's contents are still in the array)
+  if (cudaMemsetAsync(p.counters, 0, sizeof(int) * n_tiles, st) != cudaSuccess) return E4_NOALLOC_CUDA_ERROR;
+  if (cudaMemsetAsync(p.err, 0, sizeof(int), st) != cudaSuccess) return E4_NOALLOC_CUDA_ERROR;
+  if (launch_pdl(gemm_kernel, grid, kThreads, smem_bytes(p.stages, p.nt), st, wmap, xmap, p) != cudaSuccess)
+    return E4_NOALLOC_CUDA_ERROR;
+  return E4_NOALLOC_OK;
+}
+
+extern "C" int e4_gemm_noalloc_status(int* kernel_error, void* stream) {
+  using namespace e4;
+  if (!kernel_error) return E4_NOALLOC_BAD_ARGS;
+  void* base = nullptr;
+  if (const int rc = noalloc::current(&base)) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const void* err = reinterpret_cast<unsigned char*>(base) + noalloc::kErrOffset;
+  if (cudaMemcpyAsync(kernel_error, err, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return E4_NOALLOC_CUDA_ERROR;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return E4_NOALLOC_CUDA_ERROR;
+  return E4_NOALLOC_OK;
 }

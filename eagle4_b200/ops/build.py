@@ -29,9 +29,35 @@ CUDA_FLAGS = [
 ]
 
 
+HASH_FILE = os.path.join(BUILD, f"{NAME}.srchash")
+
+
 def _so_path() -> Optional[str]:
     hits = sorted(glob.glob(os.path.join(BUILD, f"{NAME}*.so")))
     return hits[0] if hits else None
+
+
+def source_hash() -> str:
+    """SHA-256 over every source and header of the extension and the compiler flags: the identity of a build."""
+    import hashlib
+
+    h = hashlib.sha256()
+    files = sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp"))
+                   + glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h")))
+    for f in files:
+        h.update(os.path.basename(f).encode())
+        with open(f, "rb") as fh:
+            h.update(fh.read())
+    h.update(" ".join(CUDA_FLAGS).encode())
+    return h.hexdigest()
+
+
+def _built_hash() -> Optional[str]:
+    try:
+        with open(HASH_FILE) as f:
+            return f.read().strip()
+    except OSError:
+        return None
 
 
 def build(verbose: bool = False):
@@ -41,7 +67,8 @@ def build(verbose: bool = False):
     os.makedirs(BUILD, exist_ok=True)
     os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"
     os.environ.setdefault("MAX_JOBS", str(min(8, os.cpu_count() or 1)))
-    return cpp_extension.load(
+    digest = source_hash()
+    mod = cpp_extension.load(
         name=NAME,
         sources=[os.path.join(CSRC, s) for s in SOURCES],
         build_directory=BUILD,
@@ -50,14 +77,21 @@ def build(verbose: bool = False):
         extra_ldflags=["-lcuda"],
         verbose=verbose,
     )
+    with open(HASH_FILE + ".tmp", "w") as f:
+        f.write(digest)
+    os.replace(HASH_FILE + ".tmp", HASH_FILE)
+    return mod
 
 
 def load():
-    """The extension module: the in-tree library if present, else a fresh build."""
+    """The extension module: the in-tree library if it was built from the current sources, else a fresh build.
+
+    A library whose recorded source hash differs from the sources beside it (a stale build shipped with newer
+    sources) is rebuilt, never run."""
     if NAME in sys.modules:
         return sys.modules[NAME]
     path = _so_path()
-    if path is None:
+    if path is None or _built_hash() != source_hash():
         return build()
     import torch  # noqa: F401  (the extension links against torch's libraries)
 

@@ -90,9 +90,10 @@ class TensorParallel:
             h = ops.linear_residual(x, w, residual)
             return h, (ops.rmsnorm(h, norm_w, eps, offset) if norm_w is not None else None)
         if self.backend == "torch":
-            part = ops.logits(x, w)
+            # the NCCL baseline: a bf16 partial and a bf16 all-reduce (what an engine's all-reduce moves)
+            part = ops.linear(x, w)
             dist.all_reduce(part, group=self.group)
-            h = (residual.float() + part).to(residual.dtype)
+            h = (residual.float() + part.float()).to(residual.dtype)
             return h, (ops.rmsnorm(h, norm_w, eps, offset) if norm_w is not None else None)
         t, n = residual.shape
         if n > self.max_cols:

@@ -231,6 +231,8 @@ class _FixedChain:
     def width(self, bs: int) -> int:
         return self.w
 
-    def record(self, bs: int, width: int, round_us: float, tokens_per_request: float) -> None:
+    def record(self, bs: int, width: int, round_us: float, tokens_per_request: float, settled: bool = True) -> None:
+        if not settled:  # an eager run and a graph capture sit inside this period
+            return
         self.round_us.append(round_us)
         self.emitted.append(int(round(tokens_per_request)))

@@ -190,6 +190,7 @@ class Engine:
         self.graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
         self.pool = torch.cuda.graph_pool_handle() if self.use_graphs else None
         self.graph_launches: Dict[tuple, int] = {}
+        self._captured = False  # a graph was captured during the current round
         self.stats = RoundStats()
         self.recorder = None  # a runtime.recorder.RoundRecorder to keep per-round records
         if self.tree is not None:
@@ -467,6 +468,7 @@ class Engine:
             return
         fn(*args)
         if self.use_graphs:
+            self._captured = True  # this round's period holds an eager run and a capture: not a cost sample
             torch.cuda.synchronize()
             g = torch.cuda.CUDAGraph()
             before = _launch_count()
@@ -563,6 +565,7 @@ class Engine:
         spec = speculative and self.draft is not None
         while min(len(o) for o in outs) < max_new_tokens:
             self._pending_timing = None
+            self._captured = False
             chain_t0 = None
             tree_t0 = None
             choice = ServedTreeChoice.SPECULATE
@@ -597,7 +600,7 @@ class Engine:
                 verify_us, draft_us = ev[1].elapsed_us(ev[2]), ev[0].elapsed_us(ev[1])
                 if self.target.tp is not None:  # every rank must record the same costs to decide alike
                     verify_us, draft_us = self.target.tp.max_over_ranks([verify_us, draft_us])
-                self.policy.record(b_, w_, c_, verify_us, nsteps, draft_us)
+                self.policy.record(b_, w_, c_, verify_us, nsteps, draft_us, settled=not self._captured)
             got = []
             for b in range(bs):
                 c = int(self.host_cnt[b])
@@ -619,10 +622,10 @@ class Engine:
                 us = tree_t0.elapsed_us(tree_t1)
                 if self.target.tp is not None:
                     us = self.target.tp.max_over_ranks([us])[0]
-                self.tree_choice.record(bs, choice, us, sum(got) / len(got))
+                self.tree_choice.record(bs, choice, us, sum(got) / len(got), settled=not self._captured)
             if chain_t0 is not None:
                 us = chain_t0.elapsed_us(chain_t1)
                 if self.target.tp is not None:
                     us = self.target.tp.max_over_ranks([us])[0]
-                self.chain_policy.record(bs, chain_w, us, sum(got) / len(got))
+                self.chain_policy.record(bs, chain_w, us, sum(got) / len(got), settled=not self._captured)
         return [o[:max_new_tokens] for o in outs]
