@@ -59,8 +59,10 @@ void tree_step(const torch::Tensor& probs, const torch::Tensor& toks, const torc
 std::vector<torch::Tensor> select_rows(const torch::Tensor& scores, const torch::Tensor& decay,
                                        const torch::Tensor& tokens, const torch::Tensor& parents, int64_t bs,
                                        int64_t n, int64_t K, int64_t count);
-int64_t gemm_scatter(const torch::Tensor& x, const torch::Tensor& w, const std::vector<int64_t>& recv, int64_t calls,
-                     int64_t rank, int64_t slot_stride);
+int64_t gemm_allreduce(const torch::Tensor& x, const torch::Tensor& w, const torch::Tensor& residual, torch::Tensor y,
+                       const std::vector<int64_t>& part, const std::vector<int64_t>& gath,
+                       const std::vector<int64_t>& flags, int64_t ctrl, int64_t ldp, int64_t rank,
+                       int64_t two_shot_rows);
 std::vector<torch::Tensor> sample_children(const torch::Tensor& logits, const torch::Tensor& cand_ids, int64_t K,
                                            double temperature, int64_t seed, const torch::Tensor& round_ctr,
                                            int64_t stream, const c10::optional<torch::Tensor>& front_nodes,
@@ -85,19 +87,16 @@ torch::Tensor sym_handle(int64_t ptr);
 int64_t sym_open(const torch::Tensor& handle, int64_t device);
 void sym_close(int64_t ptr);
 torch::Tensor sym_view(int64_t ptr, int64_t offset, int64_t numel, int64_t dtype_code, int64_t device);
-void tp_reduce(int64_t recv, int64_t world, int64_t slot_stride, const torch::Tensor& residual,
-               const c10::optional<torch::Tensor>& norm_w, double eps, bool offset, torch::Tensor out_h,
-               c10::optional<torch::Tensor> out_x, int64_t channel, torch::Tensor err);
-void tp_argmax(const torch::Tensor& ids, const torch::Tensor& val, int64_t lo, const std::vector<int64_t>& xbufs,
-               int64_t rank, int64_t max_rows, int64_t channel, torch::Tensor out_ids, torch::Tensor out_val,
-               torch::Tensor err);
+void tp_argmax(const torch::Tensor& val, const torch::Tensor& idx, int64_t n_tiles, int64_t lo,
+               const std::vector<int64_t>& xbufs, int64_t rank, int64_t max_rows, int64_t channel,
+               torch::Tensor out_ids, torch::Tensor out_val, torch::Tensor err);
 }  // namespace e4
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "eagle4_b200 sm_100a kernels";
   m.def("error_word", [](int64_t dev) { return e4::gemm_error_word(torch::Device(torch::kCUDA, dev)); });
   m.def("gemm", &e4::gemm_launch, "tcgen05 skinny GEMM with fused epilogue");
-  m.def("gemm_scatter", &e4::gemm_scatter, "row-parallel GEMM storing fp32 partials into every rank's buffer");
+  m.def("gemm_allreduce", &e4::gemm_allreduce, "row-parallel GEMM fused with its all-reduce and the residual add");
   m.def("sample_children", &e4::sample_children, "Gumbel-top-k children from candidate logits");
   m.def("sampled_accept", &e4::sampled_accept, "recursive tree rejection over the verify rows");
   m.def("advance_round", &e4::advance_round);
@@ -110,7 +109,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sym_open", &e4::sym_open);
   m.def("sym_close", &e4::sym_close);
   m.def("sym_view", &e4::sym_view);
-  m.def("tp_reduce", &e4::tp_reduce);
   m.def("tp_argmax", &e4::tp_argmax);
   m.def("rmsnorm", &e4::rmsnorm);
   m.def("concat_norms", &e4::concat_norms);

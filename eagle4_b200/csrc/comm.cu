@@ -1,18 +1,16 @@
-// Tensor-parallel communication over NVLink peer memory: symmetric buffers shared through CUDA IPC, the reduce that
-// completes a row-parallel GEMM (partial sums + residual + the next RMSNorm), and the greedy head's cross-rank
-// (max, argmax) exchange.
+// Tensor-parallel communication over NVLink peer memory: the symmetric buffers shared through CUDA IPC and the
+// greedy head's cross-rank (max, argmax) exchange. (The row-parallel projections' all-reduce is fused into the GEMM:
+// see the kAllReduce epilogue in gemm.cu.)
 //
 // Each rank owns one buffer of the same layout; peers map it with cudaIpcOpenMemHandle, so a kernel stores into
-// another GPU's buffer through a plain pointer. Data travel as (value, tag) pairs written by single aligned 8-byte
-// stores: a pair lands whole, and the reader knows it is this call's when the tag equals the call counter + 1. So no
-// fence, flag or counter sits between the producer's stores and the consumer's loads, and a consumer starts on the
-// elements that have landed while the rest are in flight. A channel's words in the buffer:
-//   done    CTAs of the local reduce that have finished (the last one advances the call counter)
+// another GPU's buffer through a plain pointer. The exchange's entries travel as (value, tag) pairs written by single
+// aligned 8-byte stores: a pair lands whole, and the reader knows it is this call's when the tag equals the call
+// counter + 1, so no fence or flag sits between the producer's stores and the consumer's loads. A channel's words:
+//   done    CTAs of the exchange that have finished (the last one advances the call counter)
 //   calls   local call counter; its low bit selects the buffer half of the call, calls + 1 is the call's tag
-// Consecutive calls alternate halves, so a rank may run one call ahead of a slower peer without overwriting data the
-// peer still reads: a rank cannot finish call n + 1 (and so start writing call n + 2) before every rank has written
-// its call n + 1 data, which each does only after finishing call n. A launch's waits share one 1 s deadline per thread; past it the
-// kernel records kErrTimeoutPeer and finishes with what it has (zeros for missing partials) instead of spinning.
+// Consecutive calls alternate halves, so a rank may run one call ahead of a slower peer without overwriting entries
+// the peer still reads. A launch's waits share one 1 s deadline per thread; past it the kernel records
+// kErrTimeoutPeer and finishes with what it has instead of spinning.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -62,83 +60,76 @@ E4_DEV bool settle(const uint2* p, unsigned tag, uint4& v, uint64_t& deadline) {
   return true;
 }
 
-// One CTA per row: h = residual + sum over ranks (rank order) of the fp32 partials; x = rmsnorm(h) (optional).
-// Each thread owns the 2-element groups c = threadIdx.x + i * kReduceThreads, i < G (N even, N <= 2 * G * 1024).
-// Its G x W pair loads are issued in batches of 8 before any is checked, so a batch costs one memory latency;
-// pairs still in flight are re-read until their tag matches. Sums run in rank order on every rank.
-constexpr int kReduceThreads = 1024;
-template <int W, int G>
-__global__ void __launch_bounds__(kReduceThreads) reduce_residual_norm_kernel(
-    const uint2* __restrict__ recv, long slot_stride, int N, const __nv_bfloat16* __restrict__ residual, int ldr,
-    const __nv_bfloat16* __restrict__ norm_w, float eps, int offset, __nv_bfloat16* __restrict__ out_h,
-    __nv_bfloat16* __restrict__ out_x, Channel ch, int* err) {
-  constexpr int kLoads = W * G, kBatch = 8;
+// The vocabulary-parallel greedy head's reduce and exchange in one launch. A warp per token row: reduce this rank's
+// per-tile (max, argmax) partials of the LM-head GEMM (ties to the lower id), publish (max, argmax + lo) to every
+// rank as one tagged 16-byte pair of pairs ((max, tag), (id, tag)), then pick the global best from every rank's
+// entries (ties to the lower vocabulary id, as in the single-GPU head). Partials: for token chunk c of 256 rows,
+// entry (tile, j) at val[c * 256 * n_tiles + tile * tc + j] (tc: the chunk's rows). Exchange area of each rank:
+// [2 halves][kMaxRanks][max_rows] entries of 16 bytes.
+constexpr int kExchangeWarps = 8;
+__global__ void __launch_bounds__(kExchangeWarps * 32) argmax_exchange_kernel(
+    const float* __restrict__ pval, const int* __restrict__ pidx, int n_tiles, int T, int lo, int world, int rank,
+    int max_rows, const __grid_constant__ Peers peers, Channel ch, int64_t* __restrict__ out_ids,
+    float* __restrict__ out_val, int* err) {
   pdl_wait();
-  pdl_trigger();  // the next kernel's prologue may start; anything it reads of ours comes after its own wait
+  pdl_trigger();
   const unsigned calls = *reinterpret_cast<volatile unsigned*>(ch.calls);
   const unsigned half = calls & 1u, tag = calls + 1u;
-  const int row = blockIdx.x;
-  __shared__ float red[kReduceThreads / 32];
-  const uint2* base = recv + size_t(half) * W * size_t(slot_stride) + size_t(row) * N;
-  float2 sum[G];
-#pragma unroll
-  for (int i = 0; i < G; ++i) sum[i] = make_float2(0.f, 0.f);
+  const int lane = threadIdx.x & 31;
+  const int j = blockIdx.x * kExchangeWarps + (threadIdx.x >> 5);
   bool ok = true;
-  uint64_t deadline = 0;
-#pragma unroll
-  for (int b0 = 0; b0 < kLoads; b0 += kBatch) {
-    uint4 v[kBatch];
-#pragma unroll
-    for (int k = 0; k < kBatch; ++k) {
-      const int i = (b0 + k) / W, r = (b0 + k) % W, c = threadIdx.x + i * kReduceThreads;
-      if (b0 + k < kLoads && c * 2 < N) v[k] = ld_volatile_v4(base + size_t(r) * slot_stride + 2 * c);
+  if (j < T) {
+    const int chunk = j / 256, jj = j % 256;
+    const int tc = min(256, T - chunk * 256);
+    const float* v = pval + size_t(chunk) * 256 * n_tiles;
+    const int* ix = pidx + size_t(chunk) * 256 * n_tiles;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = lane; i < n_tiles; i += 32) {
+      const float ov = v[size_t(i) * tc + jj];
+      const int oi = ix[size_t(i) * tc + jj];
+      if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
     }
 #pragma unroll
-    for (int k = 0; k < kBatch; ++k) {
-      const int i = (b0 + k) / W, r = (b0 + k) % W, c = threadIdx.x + i * kReduceThreads;
-      if (b0 + k < kLoads && c * 2 < N) {
-        if (!settle(base + size_t(r) * slot_stride + 2 * c, tag, v[k], deadline)) {
-          ok = false;
-          v[k] = make_uint4(0u, 0u, 0u, 0u);  // a missing partial counts as zero
-        }
-        sum[i].x += __uint_as_float(v[k].x);
-        sum[i].y += __uint_as_float(v[k].z);
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    const size_t mine = (size_t(half) * kMaxRanks + rank) * max_rows + j;
+    if (lane < world) {
+      uint2* dst = peers.xbuf[lane] + 2 * mine;
+      st_volatile_v2(dst, __float_as_uint(best), tag);
+      st_volatile_v2(dst + 1, unsigned(bi + lo), tag);
+    }
+    // lane r reads rank r's entry; the merge order does not matter (a strict order: larger value, then lower id)
+    uint4 e = make_uint4(0u, 0u, 0u, 0u);
+    uint64_t deadline = 0;
+    const uint2* local = peers.xbuf[rank];
+    float x = -INFINITY;
+    int xi = 0x7fffffff;
+    if (lane < world) {
+      const uint2* src = local + 2 * ((size_t(half) * kMaxRanks + lane) * max_rows + j);
+      e = ld_volatile_v4(src);
+      if (settle(src, tag, e, deadline)) {
+        x = __uint_as_float(e.x);
+        xi = int(e.z);
+      } else {
+        ok = false;  // a rank that never answered offers no candidate
       }
     }
-  }
-  float2 acc[G];
-  float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < G; ++i) {
-    const int c = threadIdx.x + i * kReduceThreads;
-    if (c * 2 >= N) break;
-    const float2 rv = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(residual + size_t(row) * ldr)[c]);
-    // the residual stream is bf16: round h once, and normalise the rounded values
-    const __nv_bfloat162 h = __floats2bfloat162_rn(sum[i].x + rv.x, sum[i].y + rv.y);
-    reinterpret_cast<__nv_bfloat162*>(out_h + size_t(row) * N)[c] = h;
-    acc[i] = __bfloat1622float2(h);
-    ss = fmaf(acc[i].x, acc[i].x, ss);
-    ss = fmaf(acc[i].y, acc[i].y, ss);
-  }
-  if (!ok) record_error(err, kErrTimeoutPeer);
-  if (norm_w != nullptr) {
-    float tot = warp_sum(ss);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = tot;
-    __syncthreads();
-    tot = 0.f;
-#pragma unroll
-    for (int w = 0; w < kReduceThreads / 32; ++w) tot += red[w];
-    const float rs = rsqrtf(tot / N + eps);
-#pragma unroll
-    for (int i = 0; i < G; ++i) {
-      const int c = threadIdx.x + i * kReduceThreads;
-      if (c * 2 >= N) break;
-      const float2 wv = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(norm_w)[c]);
-      const float s0 = offset ? 1.f + wv.x : wv.x, s1 = offset ? 1.f + wv.y : wv.y;
-      reinterpret_cast<__nv_bfloat162*>(out_x + size_t(row) * N)[c] =
-          __floats2bfloat162_rn(acc[i].x * rs * s0, acc[i].y * rs * s1);
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, x, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, xi, o);
+      if (ov > x || (ov == x && oi < xi)) { x = ov; xi = oi; }
+    }
+    if (lane == 0) {
+      out_ids[j] = xi;
+      out_val[j] = x;
     }
   }
+  if (!__all_sync(0xffffffffu, ok) && lane == 0) record_error(err, kErrTimeoutPeer);
   // the last CTA to finish advances the call counter (every CTA read it above)
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -149,55 +140,6 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_residual_norm_kernel(
       atomicAdd(ch.calls, 1u);
     }
   }
-}
-
-// One CTA: publish this rank's (max, argmax + lo) per row to every rank as one tagged 16-byte pair of pairs
-// ((max, tag), (id, tag)), then pick the global best from every rank's entries (ties to the lower vocabulary id,
-// as in the single-GPU head). Exchange area of each rank: [2 halves][kMaxRanks][max_rows] entries of 16 bytes.
-__global__ void __launch_bounds__(256) argmax_exchange_kernel(
-    const int64_t* __restrict__ ids, const float* __restrict__ val, int T, int lo, int world, int rank, int max_rows,
-    const __grid_constant__ Peers peers, Channel ch, int64_t* __restrict__ out_ids, float* __restrict__ out_val,
-    int* err) {
-  pdl_wait();
-  pdl_trigger();
-  const unsigned calls = *reinterpret_cast<volatile unsigned*>(ch.calls);
-  const unsigned half = calls & 1u, tag = calls + 1u;
-  const size_t mine = (size_t(half) * kMaxRanks + rank) * max_rows;
-  for (int j = threadIdx.x; j < T; j += blockDim.x) {
-    const unsigned v = __float_as_uint(val[j]), i = unsigned(int(ids[j]) + lo);
-    for (int r = 0; r < world; ++r) {
-      uint2* dst = peers.xbuf[r] + 2 * (mine + j);
-      st_volatile_v2(dst, v, tag);
-      st_volatile_v2(dst + 1, i, tag);
-    }
-  }
-  bool ok = true;
-  uint64_t deadline = 0;
-  const uint2* local = peers.xbuf[rank];
-  for (int j = threadIdx.x; j < T; j += blockDim.x) {
-    uint4 e[kMaxRanks];
-#pragma unroll
-    for (int r = 0; r < kMaxRanks; ++r)
-      if (r < world) e[r] = ld_volatile_v4(local + 2 * ((size_t(half) * kMaxRanks + r) * max_rows + j));
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int r = 0; r < kMaxRanks; ++r) {
-      if (r >= world) break;
-      if (!settle(local + 2 * ((size_t(half) * kMaxRanks + r) * max_rows + j), tag, e[r], deadline)) {
-        ok = false;
-        continue;  // a rank that never answered offers no candidate
-      }
-      const float x = __uint_as_float(e[r].x);
-      const int i = int(e[r].z);
-      if (x > best || (x == best && i < bi)) { best = x; bi = i; }
-    }
-    out_ids[j] = bi;
-    out_val[j] = best;
-  }
-  if (!ok) record_error(err, kErrTimeoutPeer);
-  __syncthreads();
-  if (threadIdx.x == 0) atomicAdd(ch.calls, 1u);
 }
 
 Channel channel(int64_t base) {
@@ -249,58 +191,24 @@ torch::Tensor sym_view(int64_t ptr, int64_t offset, int64_t numel, int64_t dtype
                           torch::TensorOptions().dtype(dtype).device(torch::kCUDA, device));
 }
 
-// h, x = reduce(recv partials) + residual, rmsnorm(h) (x only when ``norm_w`` is given).
-void tp_reduce(int64_t recv, int64_t world, int64_t slot_stride, const torch::Tensor& residual,
-               const c10::optional<torch::Tensor>& norm_w, double eps, bool offset, torch::Tensor out_h,
-               c10::optional<torch::Tensor> out_x, int64_t channel, torch::Tensor err) {
-  const at::cuda::CUDAGuard g(residual.device());
-  const int T = residual.size(0), N = residual.size(1);
-  TORCH_CHECK(N % 2 == 0 && N <= 8192, "tp_reduce: features must be even, at most 8192");
-  TORCH_CHECK(world == 1 || world == 2 || world == 4 || world == 8, "tp_reduce: 1, 2, 4 or 8 ranks");
-  TORCH_CHECK(residual.stride(1) == 1 && out_h.is_contiguous(), "tp_reduce: row-major tensors expected");
-  const bool norm = norm_w.has_value() && norm_w->defined();
-  if (T == 0) return;
-  auto launch = [&](auto kernel) {
-    C10_CUDA_CHECK(launch_pdl(kernel, T, comm::kReduceThreads, 0, at::cuda::getCurrentCUDAStream().stream(),
-                              reinterpret_cast<const uint2*>(recv), long(slot_stride), N,
-                              reinterpret_cast<const __nv_bfloat16*>(residual.data_ptr()), int(residual.stride(0)),
-                              norm ? reinterpret_cast<const __nv_bfloat16*>(norm_w->data_ptr()) : nullptr,
-                              float(eps), int(offset), reinterpret_cast<__nv_bfloat16*>(out_h.data_ptr()),
-                              norm ? reinterpret_cast<__nv_bfloat16*>(out_x->data_ptr()) : nullptr,
-                              comm::channel(channel), err.data_ptr<int>()));
-  };
-  const int groups = (N / 2 + comm::kReduceThreads - 1) / comm::kReduceThreads;  // 1..4
-  auto by_groups = [&](auto w_tag) {
-    constexpr int W = decltype(w_tag)::value;
-    switch (groups) {
-      case 1: launch(comm::reduce_residual_norm_kernel<W, 1>); break;
-      case 2: launch(comm::reduce_residual_norm_kernel<W, 2>); break;
-      case 3: launch(comm::reduce_residual_norm_kernel<W, 3>); break;
-      default: launch(comm::reduce_residual_norm_kernel<W, 4>); break;
-    }
-  };
-  switch (world) {
-    case 1: by_groups(std::integral_constant<int, 1>{}); break;
-    case 2: by_groups(std::integral_constant<int, 2>{}); break;
-    case 4: by_groups(std::integral_constant<int, 4>{}); break;
-    default: by_groups(std::integral_constant<int, 8>{}); break;
-  }
-}
-
-void tp_argmax(const torch::Tensor& ids, const torch::Tensor& val, int64_t lo, const std::vector<int64_t>& xbufs,
-               int64_t rank, int64_t max_rows, int64_t channel, torch::Tensor out_ids, torch::Tensor out_val,
-               torch::Tensor err) {
-  const at::cuda::CUDAGuard g(ids.device());
+// Greedy ids over the whole vocabulary from every rank's LM-head partials (``val`` / ``idx``: this rank's per-tile
+// (max, argmax) of the kArgmax GEMM epilogue over its vocabulary rows [lo, lo + rows)).
+void tp_argmax(const torch::Tensor& val, const torch::Tensor& idx, int64_t n_tiles, int64_t lo,
+               const std::vector<int64_t>& xbufs, int64_t rank, int64_t max_rows, int64_t channel,
+               torch::Tensor out_ids, torch::Tensor out_val, torch::Tensor err) {
+  const at::cuda::CUDAGuard g(val.device());
   const int world = int(xbufs.size());
   TORCH_CHECK(world <= comm::kMaxRanks, "tp_argmax: 1..8 ranks");
-  const int T = ids.size(0);
+  const int T = out_ids.size(0);
   TORCH_CHECK(T <= max_rows, "tp_argmax: more rows than the exchange area holds");
+  if (T == 0) return;
   comm::Peers peers{};
   for (int r = 0; r < world; ++r) peers.xbuf[r] = reinterpret_cast<uint2*>(xbufs[r]);
-  C10_CUDA_CHECK(launch_pdl(comm::argmax_exchange_kernel, 1, 256, 0, at::cuda::getCurrentCUDAStream().stream(),
-                            ids.data_ptr<int64_t>(), val.data_ptr<float>(), T, int(lo), world, int(rank),
-                            int(max_rows), peers, comm::channel(channel), out_ids.data_ptr<int64_t>(),
-                            out_val.data_ptr<float>(), err.data_ptr<int>()));
+  const int grid = (T + comm::kExchangeWarps - 1) / comm::kExchangeWarps;
+  C10_CUDA_CHECK(launch_pdl(comm::argmax_exchange_kernel, grid, comm::kExchangeWarps * 32, 0,
+                            at::cuda::getCurrentCUDAStream().stream(), val.data_ptr<float>(), idx.data_ptr<int>(),
+                            int(n_tiles), T, int(lo), world, int(rank), int(max_rows), peers, comm::channel(channel),
+                            out_ids.data_ptr<int64_t>(), out_val.data_ptr<float>(), err.data_ptr<int>()));
 }
 
 }  // namespace e4

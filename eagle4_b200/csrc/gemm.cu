@@ -19,10 +19,14 @@
 // the separate RMSNorm launch between the residual update and the next projection disappears.
 //
 // Epilogues: plain bf16 store; residual add; SwiGLU over gate/up rows interleaved in 64-row blocks; squared ReLU;
-// fp32 store; a per-tile (max, argmax) for the vocabulary-parallel greedy head; and the tensor-parallel scatter:
-// each finished fp32 tile is stored straight into this rank's slot of every rank's receive buffer (peer memory over
-// NVLink) as (value, call tag) pairs, so the transfer of one tile overlaps the MMAs of the next and the reduce
-// kernel knows an element has landed when its tag matches.
+// fp32 store; a per-tile (max, argmax) for the vocabulary-parallel greedy head; and the tensor-parallel all-reduce
+// (kAllReduce, see tp_finish_tile): a row-parallel projection's partial tile goes out over NVLink as bf16 the moment
+// it is finished (so the transfer overlaps the MMAs of the next tiles), the tile is summed over the ranks in rank
+// order with the residual added by the CTA that finished it, and the kernel ends only when this rank holds the whole
+// reduced output. One-shot: every rank receives every partial and reduces every tile (one NVLink hop; small token
+// counts). Two-shot: tile t goes to rank t % world only (reduce-scatter), which reduces it and pushes the result to
+// every other rank (all-gather into a local staging area the ranks' CTAs copy out), moving 2 (w-1)/w of the bytes
+// the one-shot moves w-1 times (large token counts).
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -37,9 +41,15 @@
 namespace e4 {
 namespace gemm {
 
-enum Epi : int { kPlain = 0, kResidual = 1, kSwiGLU = 2, kReLU2 = 3, kF32 = 4, kArgmax = 5, kScatter = 6 };
+enum Epi : int { kPlain = 0, kResidual = 1, kSwiGLU = 2, kReLU2 = 3, kF32 = 4, kArgmax = 5, kAllReduce = 6 };
 
 constexpr int kMaxRanks = 8;
+// peer areas of the all-reduce epilogue: rows per launch (the launch's token chunk) and 128-row weight tiles
+constexpr int kTpRows = 256;
+constexpr int kTpTiles = 64;
+constexpr int kTpPartialFlags = 2 * kTpTiles * kMaxRanks;  // [half][tile][source rank]
+constexpr int kTpFlags = kTpPartialFlags + 2 * kTpTiles;     // + gathered-tile flags [half][tile]
+constexpr uint64_t kTpWaitNs = 1000000000ull;                // 1 s per wait, then the error word and zeros
 
 constexpr int kThreads = 192;
 constexpr int kTileM = 128;
@@ -64,12 +74,18 @@ struct Params {
   float* amax_val;   // [n_tiles][T] per-tile max (kArgmax)
   int* amax_idx;     // [n_tiles][T]
   int* err;
-  // kScatter: receive buffers recv[parity][src rank][row][ldy] of (value, tag) pairs on every rank, and this
-  // rank's call counter (its low bit is the parity of this call, calls + 1 the tag)
-  float* peer_recv[kMaxRanks];
-  const unsigned* calls;
-  long slot_stride;  // pairs per (parity, src rank) slot
-  int world, rank, row0;
+  // kAllReduce: every rank's peer areas (CUDA IPC mappings; this rank's own at index ``rank``):
+  //   tp_part[r]  partial tiles sent to rank r: [2 halves][kMaxRanks source ranks][kTpRows][ldp] bf16
+  //   tp_gath[r]  reduced tiles pushed to rank r (two-shot): [2 halves][kTpRows][ldp] bf16
+  //   tp_flag[r]  rank r's arrival flags: partial [half][tile][source], then gathered [half][tile]; a flag holds
+  //               the tag (call number + 1) of the call whose data it announces
+  // and this rank's call counter (its low bit is the buffer half of the call) and finished-CTA counter.
+  __nv_bfloat16* tp_part[kMaxRanks];
+  __nv_bfloat16* tp_gath[kMaxRanks];
+  unsigned* tp_flag[kMaxRanks];
+  unsigned* tp_calls;
+  unsigned* tp_done;
+  int ldp, two_shot, world, rank;
   unsigned long long* trace;  // optional [grid][8] globaltimer stamps (tuning runs only)
   // RMSNorm folded into the GEMM (fold != 0): X is the raw residual stream, W carries the norm weight in its columns,
   // and every token column of the accumulator is scaled by rsqrt(mean(x^2) + fold_eps) over that token's row of X
@@ -113,23 +129,153 @@ __device__ __forceinline__ Piece next_piece(const Params& p, long g, long end) {
   return pc;
 }
 
-// Final epilogue of 16 token columns [j0, j0+16) held by this thread for weight row ``m`` of ``tile``.
-__device__ __forceinline__ void store_chunk(const Params& p, int tile, int m, int j0, const float* v, float* xchg,
-                                            int ep_tid, unsigned parity) {
-  const int n = tile * kTileM + m;
-  if (p.epi == kScatter) {
-    // (value, epoch) pairs: an aligned 8-byte store lands whole, so the reader needs no fence or counter
-    if (n >= p.N) return;
-    const size_t slot = (size_t(parity & 1u) * p.world + p.rank) * size_t(p.slot_stride);
-    for (int r = 0; r < p.world; ++r) {
-      uint2* dst = reinterpret_cast<uint2*>(p.peer_recv[r]) + slot + size_t(p.row0 + j0) * p.ldy + n;
+// ------------------------------------------------------------------ tensor-parallel all-reduce epilogue
+E4_DEV void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+E4_DEV unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Waits until ``*flag == tag``; false after kTpWaitNs (the caller records the error).
+E4_DEV bool tp_wait_flag(const unsigned* flag, unsigned tag) {
+  if (ld_acquire_sys(flag) == tag) return true;
+  const uint64_t t0 = globaltimer();
+  while (ld_acquire_sys(flag) != tag) {
+    if (globaltimer() - t0 > kTpWaitNs) return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+E4_DEV size_t tp_part_index(const Params& p, unsigned half, int src, int row, int n) {
+  return ((size_t(half) * kMaxRanks + src) * kTpRows + row) * size_t(p.ldp) + n;
+}
+E4_DEV int tp_home(const Params& p, int tile) { return p.two_shot ? tile % p.world : -1; }
+
+// 16 token columns of this thread's feature row as bf16 partials to the ranks that reduce ``tile`` (every rank, or
+// the tile's home rank). The chunk is transposed through shared memory so that each thread stores 16-byte pieces
+// (8 consecutive features of one token) and a warp writes 512 contiguous bytes per token row.
+__device__ __forceinline__ void tp_send_chunk(const Params& p, int tile, int m, int j0, const float* v, float* xchg,
+                                              int ep_tid, unsigned half) {
+  __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(xchg);  // [16 tokens][128 features]
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        if (j0 + i >= p.T) break;
-        asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(dst + size_t(i) * p.ldy),
-                     "r"(__float_as_uint(v[i])), "r"(parity + 1u) : "memory");
+  for (int i = 0; i < 16; ++i) st[i * kTileM + m] = __float2bfloat16(v[i]);
+  named_bar(1, 128);
+  const int home = tp_home(p, tile);
+  for (int q = ep_tid; q < 16 * 16; q += 128) {
+    const int i = q >> 4, piece = q & 15;
+    const int j = j0 + i, n = tile * kTileM + piece * 8;
+    if (j >= p.T || n >= p.N) continue;
+    const uint4 val = *reinterpret_cast<const uint4*>(st + i * kTileM + piece * 8);
+    for (int r = 0; r < p.world; ++r) {
+      if (home >= 0 && r != home) continue;
+      uint4* dst = reinterpret_cast<uint4*>(p.tp_part[r] + tp_part_index(p, half, p.rank, j, n));
+      asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(val.x), "r"(val.y), "r"(val.z),
+                   "r"(val.w) : "memory");
+    }
+  }
+  named_bar(1, 128);
+}
+
+// After the last chunk of ``tile``: announce it (a release store per destination, after every epilogue thread's
+// stores), then, where this rank reduces the tile, wait for every rank's partial and write
+// h = residual + sum over ranks in rank order (fp32 sums of the bf16 partials, h rounded once to bf16); two-shot
+// also pushes h to every other rank and announces it there.
+__device__ __forceinline__ void tp_finish_tile(const Params& p, int tile, int ep_tid, unsigned half, unsigned tag,
+                                               int* missing) {
+  named_bar(1, 128);
+  const int home = tp_home(p, tile);
+  if (ep_tid < p.world && (home < 0 || ep_tid == home))
+    st_release_sys(p.tp_flag[ep_tid] + (size_t(half) * kTpTiles + tile) * kMaxRanks + p.rank, tag);
+  if (home >= 0 && home != p.rank) return;
+  if (ep_tid < kMaxRanks) missing[ep_tid] = 0;
+  named_bar(1, 128);
+  if (ep_tid < p.world) {
+    const unsigned* f = p.tp_flag[p.rank] + (size_t(half) * kTpTiles + tile) * kMaxRanks + ep_tid;
+    if (!tp_wait_flag(f, tag)) {
+      record_error(p.err, kErrTimeoutPeer);
+      missing[ep_tid] = 1;  // a rank that never answered contributes zeros
+    }
+  }
+  named_bar(1, 128);
+  const __nv_bfloat16* mine = p.tp_part[p.rank];
+  for (int q = ep_tid; q < p.T * 16; q += 128) {
+    const int j = q >> 4, n = tile * kTileM + (q & 15) * 8;
+    if (n >= p.N) continue;
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    for (int r = 0; r < p.world; ++r) {
+      if (missing[r]) continue;
+      const uint4 u = __ldcg(reinterpret_cast<const uint4*>(mine + tp_part_index(p, half, r, j, n)));
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h2[e]);
+        acc[2 * e] += f.x;
+        acc[2 * e + 1] += f.y;
       }
     }
+    const uint4 ru = *reinterpret_cast<const uint4*>(p.res + size_t(j) * p.ldr + n);
+    const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&ru);
+    uint4 out;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(r2[e]);
+      o2[e] = __floats2bfloat162_rn(f.x + acc[2 * e], f.y + acc[2 * e + 1]);
+    }
+    *reinterpret_cast<uint4*>(p.y + size_t(j) * p.ldy + n) = out;
+    if (home >= 0) {
+      for (int r = 0; r < p.world; ++r) {
+        if (r == p.rank) continue;
+        uint4* dst = reinterpret_cast<uint4*>(p.tp_gath[r] + (size_t(half) * kTpRows + j) * p.ldp + n);
+        asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(out.x), "r"(out.y), "r"(out.z),
+                     "r"(out.w) : "memory");
+      }
+    }
+  }
+  if (home >= 0) {
+    named_bar(1, 128);
+    if (ep_tid < p.world && ep_tid != p.rank)
+      st_release_sys(p.tp_flag[ep_tid] + kTpPartialFlags + size_t(half) * kTpTiles + tile, tag);
+  }
+}
+
+// Two-shot, after this CTA's own tiles: copy the reduced tiles other ranks pushed here into the output (tiles
+// c, c + grid, ... of CTA c), each after its arrival flag.
+__device__ __forceinline__ void tp_gather_tiles(const Params& p, int ep_tid, unsigned half, unsigned tag,
+                                                int* missing) {
+  for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
+    if (tile % p.world == p.rank) continue;
+    if (ep_tid == 0) {
+      missing[0] = 0;
+      if (!tp_wait_flag(p.tp_flag[p.rank] + kTpPartialFlags + size_t(half) * kTpTiles + tile, tag)) {
+        record_error(p.err, kErrTimeoutPeer);
+        missing[0] = 1;
+      }
+    }
+    named_bar(1, 128);
+    const bool ok = !missing[0];
+    for (int q = ep_tid; q < p.T * 16; q += 128) {
+      const int j = q >> 4, n = tile * kTileM + (q & 15) * 8;
+      if (n >= p.N) continue;
+      const uint4 u = ok ? __ldcg(reinterpret_cast<const uint4*>(p.tp_gath[p.rank] + (size_t(half) * kTpRows + j) *
+                                                                       p.ldp + n))
+                         : make_uint4(0u, 0u, 0u, 0u);
+      *reinterpret_cast<uint4*>(p.y + size_t(j) * p.ldy + n) = u;
+    }
+    named_bar(1, 128);
+  }
+}
+
+// Final epilogue of 16 token columns [j0, j0+16) held by this thread for weight row ``m`` of ``tile``.
+__device__ __forceinline__ void store_chunk(const Params& p, int tile, int m, int j0, const float* v, float* xchg,
+                                            int ep_tid, unsigned half) {
+  const int n = tile * kTileM + m;
+  if (p.epi == kAllReduce) {
+    tp_send_chunk(p, tile, m, j0, v, xchg, ep_tid, half);
     return;
   }
   if (p.epi == kSwiGLU) {
@@ -321,8 +467,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
   } else {
     // epilogue warps 2..5: TMEM lane quarter = warp % 4
     pdl_wait();
-    // kScatter: the call counter (its low bit picks the buffer half, calls + 1 tags the data)
-    const unsigned parity = p.epi == kScatter ? *reinterpret_cast<const volatile unsigned*>(p.calls) : 0u;
+    // kAllReduce: this call's number (its low bit picks the buffer half; number + 1 tags its flags)
+    const unsigned call = p.epi == kAllReduce ? *reinterpret_cast<const volatile unsigned*>(p.tp_calls) : 0u;
+    const unsigned half = call & 1u, tag = call + 1u;
+    int* missing = reinterpret_cast<int*>(xchg + 16 * 64 + 256);  // [kMaxRanks] flags of absent ranks
     const int ep_tid = threadIdx.x - 64;
     const int quarter = warp & 3;
     const int m = quarter * 32 + lane;
@@ -370,8 +518,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[i] *= rsv[j0 + i];
           }
-          store_chunk(p, tile, m, j0, v, xchg, ep_tid, parity);
+          store_chunk(p, tile, m, j0, v, xchg, ep_tid, half);
         }
+        if (p.epi == kAllReduce) tp_finish_tile(p, tile, ep_tid, half, tag, missing);
       } else {
         // Partial tile. The CTA holding the tile's first k-block (kb0 == 0) owns it: that piece ends the CTA's range,
         // so it finishes last. Every other piece stores its partial and counts itself in with a release add (no
@@ -443,19 +592,30 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
 #pragma unroll
               for (int i = 0; i < 16; ++i) v[i] *= rsv[j0 + i];
             }
-            store_chunk(p, tile, m, j0, v, xchg, ep_tid, parity);
+            store_chunk(p, tile, m, j0, v, xchg, ep_tid, half);
           }
           if (ep_tid == 0) p.counters[tile] = 0;
           named_bar(1, 128);
+          if (p.epi == kAllReduce) tp_finish_tile(p, tile, ep_tid, half, tag, missing);
         }
       }
     }
+    if (p.epi == kAllReduce && p.two_shot) tp_gather_tiles(p, ep_tid, half, tag, missing);
   }
   if (threadIdx.x == 64) E4_STAMP(p, 5);
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, tmem_cols);
+  }
+  if (p.epi == kAllReduce && threadIdx.x == 0) {
+    // every CTA read the call number before arriving here: the last one to finish advances it
+    __threadfence();
+    if (atomicAdd(p.tp_done, 1u) == gridDim.x - 1) {
+      *p.tp_done = 0u;
+      __threadfence();
+      atomicAdd(p.tp_calls, 1u);
+    }
   }
   if (threadIdx.x == 0) E4_STAMP(p, 6);
 }
@@ -555,10 +715,11 @@ int stage_count(int nt) {
 }
 
 // Dynamic shared memory of one launch: 1 KB alignment slack, the stages, barriers and TMEM handle (64 B), the
-// epilogue exchange buffer (16 x 64 floats), the folded-norm scales (256 floats) and 1 KB of slack.
+// epilogue exchange buffer (16 x 64 floats), the folded-norm scales (256 floats), the all-reduce's absent-rank
+// flags (kMaxRanks ints) and 1 KB of slack.
 size_t smem_bytes(int stages, int nt) {
   const int stage_bytes = kWTileBytes + nt * kTileK * 2;
-  return 1024 + size_t(stages) * stage_bytes + 64 + 16 * 64 * 4 + 256 * 4 + 1024;
+  return 1024 + size_t(stages) * stage_bytes + 64 + 16 * 64 * 4 + 256 * 4 + kMaxRanks * 4 + 1024;
 }
 
 struct Scratch {
@@ -646,7 +807,7 @@ int launch_chunks(const torch::Tensor& x, const torch::Tensor& w, int epi, F chu
 void gemm_launch(const torch::Tensor& x, const torch::Tensor& w, int epi, torch::Tensor y, torch::Tensor yf,
                  const torch::Tensor& res, torch::Tensor amax_val, torch::Tensor amax_idx, double fold_eps) {
   using namespace gemm;
-  TORCH_CHECK(epi != kScatter, "gemm: the scatter epilogue has its own entry point");
+  TORCH_CHECK(epi != kAllReduce, "gemm: the all-reduce epilogue has its own entry point");
   const int n_tiles = (w.size(0) + kTileM - 1) / kTileM;
   auto has = [](const torch::Tensor& t) { return t.defined() && t.numel() > 0; };
   launch_chunks(x, w, epi, [&](Params& p, int t0) {
@@ -690,25 +851,43 @@ torch::Tensor gemm_traced(const torch::Tensor& x, const torch::Tensor& w, int64_
   return tr;
 }
 
-// Tensor-parallel row-parallel GEMM: Y_partial = X . W^T (fp32, tagged with the call) stored into slot
-// [parity][rank] of every rank's receive buffer (``recv``: int64 device addresses per rank, peers' from IPC
-// mappings). Returns the number of CTAs launched.
-int64_t gemm_scatter(const torch::Tensor& x, const torch::Tensor& w, const std::vector<int64_t>& recv, int64_t calls,
-                     int64_t rank, int64_t slot_stride) {
+// Tensor-parallel row-parallel GEMM fused with its all-reduce and the residual add:
+// y = residual + sum over ranks of X_r . W_r^T, bit-identical on every rank. ``part`` / ``gath`` / ``flags``: int64
+// device addresses of every rank's peer areas (this rank's own at ``rank``); ``ctrl``: this rank's call and
+// finished-CTA counters (two words). ``two_shot_rows``: launches of more tokens than this use the two-shot form.
+// Returns the number of CTAs launched.
+int64_t gemm_allreduce(const torch::Tensor& x, const torch::Tensor& w, const torch::Tensor& residual, torch::Tensor y,
+                       const std::vector<int64_t>& part, const std::vector<int64_t>& gath,
+                       const std::vector<int64_t>& flags, int64_t ctrl, int64_t ldp, int64_t rank,
+                       int64_t two_shot_rows) {
   using namespace gemm;
-  const int world = int(recv.size());
-  TORCH_CHECK(world >= 1 && world <= kMaxRanks, "gemm_scatter: 1..8 ranks");
-  TORCH_CHECK(x.size(0) * w.size(0) <= slot_stride, "gemm_scatter: rows x features exceed the receive slot");
-  return launch_chunks(x, w, kScatter, [&](Params& p, int t0) {
+  const int world = int(part.size());
+  TORCH_CHECK(world >= 1 && world <= kMaxRanks && int(gath.size()) == world && int(flags.size()) == world,
+              "gemm_allreduce: 1..8 ranks");
+  const int N = w.size(0);
+  TORCH_CHECK(N % 8 == 0 && N <= ldp && (N + kTileM - 1) / kTileM <= kTpTiles, "gemm_allreduce: N too large");
+  TORCH_CHECK(ldp % 8 == 0, "gemm_allreduce: peer row stride must be a multiple of 8");
+  TORCH_CHECK(residual.size(0) == x.size(0) && residual.size(1) == N && y.size(0) == x.size(0) && y.size(1) == N,
+              "gemm_allreduce: residual / output shape");
+  TORCH_CHECK(residual.stride(1) == 1 && y.stride(1) == 1 && residual.stride(0) % 8 == 0 && y.stride(0) % 8 == 0 &&
+              reinterpret_cast<uintptr_t>(residual.data_ptr()) % 16 == 0 &&
+              reinterpret_cast<uintptr_t>(y.data_ptr()) % 16 == 0, "gemm_allreduce: 16-byte aligned rows expected");
+  return launch_chunks(x, w, kAllReduce, [&](Params& p, int t0) {
     for (int r = 0; r < world; ++r) {
-      p.peer_recv[r] = reinterpret_cast<float*>(recv[r]);
+      p.tp_part[r] = reinterpret_cast<__nv_bfloat16*>(part[r]);
+      p.tp_gath[r] = reinterpret_cast<__nv_bfloat16*>(gath[r]);
+      p.tp_flag[r] = reinterpret_cast<unsigned*>(flags[r]);
     }
-    p.calls = reinterpret_cast<const unsigned*>(calls);
-    p.slot_stride = slot_stride;
+    p.tp_calls = reinterpret_cast<unsigned*>(ctrl);
+    p.tp_done = reinterpret_cast<unsigned*>(ctrl) + 1;
+    p.ldp = int(ldp);
     p.world = world;
     p.rank = int(rank);
-    p.row0 = t0;
-    p.ldy = int(w.size(0));
+    p.two_shot = (world > 1 && p.T > two_shot_rows) ? 1 : 0;
+    p.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr()) + size_t(t0) * y.stride(0);
+    p.ldy = int(y.stride(0));
+    p.res = reinterpret_cast<const __nv_bfloat16*>(residual.data_ptr()) + size_t(t0) * residual.stride(0);
+    p.ldr = int(residual.stride(0));
   });
 }
 

@@ -122,6 +122,18 @@ def lm_head_argmax(x: torch.Tensor, w: torch.Tensor) -> Tuple[torch.Tensor, torc
     return ids, best
 
 
+def lm_head_partials(x: torch.Tensor, w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, int]:
+    """The LM-head GEMM's per-tile (max, argmax) partials ``(val, idx, n_tiles)`` (layout: see ``tp_argmax``)."""
+    x = _c2(x)
+    t = x.shape[0]
+    n_tiles = (w.shape[0] + 127) // 128
+    chunks = (t + 255) // 256
+    val = torch.empty(chunks * 256 * n_tiles, dtype=torch.float32, device=x.device)
+    idx = torch.empty(chunks * 256 * n_tiles, dtype=torch.int32, device=x.device)
+    _C.gemm(x, w, EPI_ARGMAX, _NONE, _NONE, _NONE, val, idx, -1.0)
+    return val, idx, n_tiles
+
+
 # row ops ----------------------------------------------------------------------------------------------------------
 def rmsnorm(x, w, eps, offset):
     return _C.rmsnorm(x, w, float(eps), bool(offset))

@@ -1,13 +1,19 @@
 """Tensor parallelism: one rank per GPU, ``torch.distributed`` for setup, and two data paths for the collectives.
 
-``backend="fused"`` (the B200 path): a row-parallel linear is ONE GEMM launch whose epilogue stores each finished
-fp32 tile straight into this rank's slot of every rank's receive buffer over NVLink (peer pointers from CUDA IPC)
-as (value, call tag) pairs; a second kernel sums each element over the ranks in rank order as soon as its pairs
-carry this call's tag, adds the residual and applies the next RMSNorm. The greedy head's vocabulary-parallel (max, argmax) is
-exchanged the same way by one small kernel. Both kernels are captured in the engine's CUDA graphs.
+``backend="fused"`` (the B200 path): a row-parallel linear is ONE GEMM launch whose epilogue does the all-reduce
+over NVLink peer memory (CUDA IPC mappings of one symmetric buffer per rank) and adds the residual: each finished
+tile leaves as bf16 while the next tiles' MMAs run, the CTA that finished a tile sums it over the ranks in rank order
+once every rank's copy has landed (per-tile release / acquire flags tagged with the call number), and the kernel
+returns only when this rank holds the whole result. Up to ``two_shot_rows`` tokens per launch every rank receives
+every partial (one-shot: one NVLink hop); above it a tile goes only to its home rank (reduce-scatter), which reduces
+it and pushes the result to the others (all-gather), so each rank sends 2 (w-1)/w of the output instead of w-1 times
+it. The greedy head's vocabulary-parallel argmax is the LM-head GEMM's per-tile (max, argmax) epilogue plus one
+kernel that reduces the tiles and exchanges (max, id) pairs across the ranks. All of it is captured in the engine's
+CUDA graphs.
 
 ``backend="torch"``: the same math through ``torch.distributed.all_reduce`` / ``all_gather`` (NCCL on GPUs, gloo on
-CPU): the baseline the fused path is measured against, and the CPU oracle of the multi-process tests.
+CPU) over bf16 partials: the baseline the fused path is measured against, and the CPU oracle of the multi-process
+tests.
 
 Every rank sums partials in rank order and applies identical elementwise math, so all ranks hold bit-identical
 hidden states, greedy tokens and draft trees, and take the same host decisions without exchanging them.
@@ -24,13 +30,18 @@ import torch.distributed as dist
 from eagle4_b200 import ops
 
 MAX_RANKS = 8
-_CH0, _CH1 = 0, 256  # channel words: GEMM -> reduce, greedy-head exchange
-_RECV = 4096
+TP_ROWS = 256  # tokens per GEMM launch (the GEMM splits larger inputs into launches of at most this many)
+TP_TILES = 64  # 128-row weight tiles per launch: output features up to 8192
+# symmetric buffer layout (bytes): control words, arrival flags, partial areas, gathered areas, argmax exchange
+_CTRL_GEMM, _CTRL_ARGMAX = 0, 256  # GEMM: (calls, done); argmax exchange: (done, calls)
+_FLAGS = 4096
+_FLAG_BYTES = (2 * TP_TILES * MAX_RANKS + 2 * TP_TILES) * 4
+_PART = 16384
 
 
 class TensorParallel:
     def __init__(self, group=None, *, backend: str = "fused", max_rows: int = 1024, max_cols: int = 8192,
-                 device: Optional[torch.device] = None):
+                 device: Optional[torch.device] = None, two_shot_rows: Optional[int] = None):
         if backend not in ("fused", "torch"):
             raise ValueError(f"unknown tensor-parallel backend {backend!r}")
         self.group = group
@@ -41,7 +52,10 @@ class TensorParallel:
         self.device = device or (torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available()
                                  else torch.device("cpu"))
         self.backend = backend if self.device.type == "cuda" else "torch"
-        self.max_rows, self.max_cols = max_rows, max_cols
+        self.max_rows, self.max_cols = (max_rows + 255) // 256 * 256, max_cols
+        if two_shot_rows is None:
+            two_shot_rows = int(os.environ.get("E4_TP_TWO_SHOT_ROWS", "48"))
+        self.two_shot_rows = two_shot_rows
         self.base = 0
         self.peers: List[int] = []
         # one rank may still run the fused kernels (signalling only itself): measures their cost without NVLink
@@ -55,17 +69,35 @@ class TensorParallel:
 
         C = native._C
         dev = self.device.index
-        self.slot = self.max_rows * self.max_cols  # (value, tag) pairs of 8 bytes
-        recv_bytes = 2 * self.world * self.slot * 8
-        self.xbuf_off = _RECV + recv_bytes
+        self.ldp = (self.max_cols + 7) // 8 * 8
+        part_bytes = 2 * MAX_RANKS * TP_ROWS * self.ldp * 2
+        gath_bytes = 2 * TP_ROWS * self.ldp * 2
+        self.gath_off = _PART + part_bytes
+        self.xbuf_off = self.gath_off + gath_bytes
         total = self.xbuf_off + 2 * MAX_RANKS * self.max_rows * 16
-        self.base = C.sym_alloc(total, dev)
+        self.base = C.sym_alloc(total, dev)  # zero-filled: no flag carries a tag yet
         handle = C.sym_handle(self.base)
         handles: List[Optional[torch.Tensor]] = [None] * self.world
         dist.all_gather_object(handles, handle, group=self.group)
         self.peers = [self.base if r == self.rank else C.sym_open(handles[r], dev) for r in range(self.world)]
         self.err = native.error_word(self.device)
         dist.barrier(group=self.group)
+
+    def nvlink_bytes(self, tokens: int, features: int) -> int:
+        """Bytes one rank sends over NVLink for one row-parallel projection of ``tokens`` x ``features``."""
+        if self.world == 1:
+            return 0
+        el = 2 * features
+        total = 0
+        for r0 in range(0, tokens, TP_ROWS):
+            t = min(TP_ROWS, tokens - r0)
+            if t > self.two_shot_rows:  # reduce-scatter then all-gather of this rank's home tiles
+                tiles = (features + 127) // 128
+                home = len([i for i in range(tiles) if i % self.world == self.rank])
+                total += t * 128 * 2 * (tiles - home) + t * 128 * 2 * home * (self.world - 1)
+            else:
+                total += t * el * (self.world - 1)
+        return total
 
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (after a barrier: no peer may still write into it)."""
@@ -97,23 +129,22 @@ class TensorParallel:
             return h, (ops.rmsnorm(h, norm_w, eps, offset) if norm_w is not None else None)
         t, n = residual.shape
         if n > self.max_cols:
-            raise ValueError(f"row_linear: {n} features exceed the receive buffer's {self.max_cols}")
+            raise ValueError(f"row_linear: {n} features exceed the peer areas' {self.max_cols}")
         h = torch.empty_like(residual)
-        xn = torch.empty_like(residual) if norm_w is not None else None
         C = _native()
-        for r0 in range(0, t, self.max_rows):
-            r1 = min(t, r0 + self.max_rows)
-            C.gemm_scatter(x[r0:r1], w, [p + _RECV for p in self.peers], self.base + _CH0 + 4, self.rank, self.slot)
-            C.tp_reduce(self.base + _RECV, self.world, self.slot, residual[r0:r1], norm_w, eps, offset, h[r0:r1],
-                        xn[r0:r1] if xn is not None else None, self.base + _CH0, self.err)
-        return h, xn
+        part = [p + _PART for p in self.peers]
+        gath = [p + self.gath_off for p in self.peers]
+        flags = [p + _FLAGS for p in self.peers]
+        C.gemm_allreduce(_rows16(x), w, residual.contiguous(), h, part, gath, flags, self.base + _CTRL_GEMM,
+                         self.ldp, self.rank, self.two_shot_rows)
+        return h, (ops.rmsnorm(h, norm_w, eps, offset) if norm_w is not None else None)
 
     def lm_head_argmax(self, x: torch.Tensor, w_shard: torch.Tensor, lo: int) -> Tuple[torch.Tensor, torch.Tensor]:
         """Greedy ids over the whole vocabulary from this rank's row range ``[lo, lo + rows)`` of the LM head."""
-        ids, val = ops.lm_head_argmax(x, w_shard)
-        if self.world == 1 and not self.force_fused:
-            return ids + lo, val
-        if self.backend == "torch":
+        if self.backend == "torch" or (self.world == 1 and not self.force_fused):
+            ids, val = ops.lm_head_argmax(x, w_shard)
+            if self.world == 1:
+                return ids + lo, val
             both = torch.stack([val.double(), (ids + lo).double()], dim=1)
             parts = [torch.empty_like(both) for _ in range(self.world)]
             dist.all_gather(parts, both, group=self.group)
@@ -121,14 +152,20 @@ class TensorParallel:
             best_val = stack[..., 0].amax(dim=0)
             cand = torch.where(stack[..., 0] == best_val[None], stack[..., 1], torch.full_like(stack[..., 1], 2 ** 40))
             return cand.amin(dim=0).long(), best_val.float()
-        t = ids.shape[0]
-        out_ids = torch.empty_like(ids)
-        out_val = torch.empty_like(val)
+        from eagle4_b200.ops import native
+
+        val, idx, n_tiles = native.lm_head_partials(x, w_shard)
+        t = x.shape[0]
+        out_ids = torch.empty(t, dtype=torch.int64, device=x.device)
+        out_val = torch.empty(t, dtype=torch.float32, device=x.device)
         C = _native()
         for r0 in range(0, t, self.max_rows):
             r1 = min(t, r0 + self.max_rows)
-            C.tp_argmax(ids[r0:r1], val[r0:r1], int(lo), [p + self.xbuf_off for p in self.peers], self.rank,
-                        self.max_rows, self.base + _CH1, out_ids[r0:r1], out_val[r0:r1], self.err)
+            # partials of rows [r0, r1): whole 256-row chunks of the GEMM's layout (max_rows is a multiple of 256)
+            c0 = r0 // 256
+            C.tp_argmax(val[c0 * 256 * n_tiles:], idx[c0 * 256 * n_tiles:], n_tiles, int(lo),
+                        [p + self.xbuf_off for p in self.peers], self.rank, self.max_rows, self.base + _CTRL_ARGMAX,
+                        out_ids[r0:r1], out_val[r0:r1], self.err)
         return out_ids, out_val
 
     def gather_logits(self, local: torch.Tensor, vocab: int) -> torch.Tensor:
@@ -158,6 +195,13 @@ def _native():
     from eagle4_b200.ops import native
 
     return native._C
+
+
+def _rows16(x: torch.Tensor) -> torch.Tensor:
+    """``x`` as a 2-D tensor with contiguous 16-byte-aligned rows (the GEMM's TMA operand)."""
+    from eagle4_b200.ops import native
+
+    return native._c2(x)
 
 
 def init_distributed(timeout_s: int = 60) -> Tuple[int, int]:

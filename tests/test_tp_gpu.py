@@ -1,7 +1,8 @@
-"""Tensor parallelism on 2 GPUs: the fused peer-memory collectives against the NCCL baseline and one GPU.
+"""Tensor parallelism on 2, 4 and 8 GPUs: the fused GEMM + all-reduce kernel against an fp32 product, the NCCL
+baseline and one GPU.
 
-Runs as two spawned NCCL ranks (skipped with fewer than two GPUs). NVLS is off (``NCCL_NVLS_ENABLE=0``) and the
-fused kernels use plain peer stores and loads, no multicast. Every wait in the fused kernels is bounded and the
+Each case runs as spawned NCCL ranks (skipped with fewer GPUs than ranks). NVLS is off (``NCCL_NVLS_ENABLE=0``) and
+the fused kernels use plain peer stores and loads, no multicast. Every wait in the fused kernels is bounded and the
 process group has a short timeout, so a broken rank ends the test with an error instead of a hang.
 """
 
@@ -21,6 +22,42 @@ def _port() -> int:
         return s.getsockname()[1]
 
 
+def _row_linear_checks(rank, world, dev, res):
+    """One row-parallel projection per (tokens, form): fp32 reference, ranks bit-identical, NCCL within tolerance."""
+    import torch.distributed as dist
+
+    from eagle4_b200.parallel.tp import TensorParallel
+
+    H, K = 5120, 6144 // world
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    w = (torch.randn(H, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    nccl = TensorParallel(backend="torch", device=dev)
+    worst = 0.0
+    for form, rows in (("one_shot", 1 << 30), ("two_shot", 0)):
+        tp = TensorParallel(backend="fused", max_rows=512, max_cols=H, device=dev, two_shot_rows=rows)
+        for t in (1, 16, 100, 300):
+            gx = torch.Generator(device=dev).manual_seed(1000 * t + rank)
+            x = torch.randn(t, K, generator=gx, device=dev).to(torch.bfloat16)
+            r = torch.randn(t, H, generator=torch.Generator(device=dev).manual_seed(t), device=dev).to(torch.bfloat16)
+            h, _ = tp.row_linear(x, w, r)
+            for _ in range(3):  # repeated calls alternate buffer halves: same bits every time
+                h2, _ = tp.row_linear(x, w, r)
+                assert torch.equal(h, h2), "repeated fused calls must give the same bits"
+            part = x.float() @ w.float().t()
+            dist.all_reduce(part)
+            ref = r.float() + part
+            err = (h.float() - ref).abs().max().item() / ref.abs().max().item()
+            worst = max(worst, err)
+            hb, _ = nccl.row_linear(x, w, r)
+            res[f"{form}_t{t}_vs_nccl"] = (h.float() - hb.float()).abs().max().item() / ref.abs().max().item()
+            allh = [torch.empty_like(h) for _ in range(world)]
+            dist.all_gather(allh, h)
+            res[f"{form}_t{t}_ranks_equal"] = all(torch.equal(a, allh[0]) for a in allh)
+        torch.cuda.synchronize()
+        tp.close()
+    res["row_linear_rel_err"] = worst
+
+
 def _worker(rank, world, port, out):
     import torch.distributed as dist
 
@@ -35,6 +72,7 @@ def _worker(rank, world, port, out):
         from eagle4_b200.parallel.tp import TensorParallel
 
         dev = torch.device("cuda", rank)
+        _row_linear_checks(rank, world, dev, res)
         tree = TreeSpec(4, 2, 8)
         fused = TensorParallel(backend="fused", max_rows=256, max_cols=4096, device=dev)
         base = TensorParallel(backend="torch", device=dev)
@@ -79,18 +117,25 @@ def _worker(rank, world, port, out):
         dist.destroy_process_group()
 
 
-def test_fused_tp_matches_nccl_and_one_gpu():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_tp_matches_reference_nccl_and_one_gpu(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     with ctx.Manager() as mgr:
         out = mgr.dict()
-        mp.start_processes(_worker, args=(2, _port(), out), nprocs=2, start_method="spawn", join=True)
+        mp.start_processes(_worker, args=(world, _port(), out), nprocs=world, start_method="spawn", join=True)
         res = dict(out)
-    for r in range(2):
+    for r in range(world):
         assert res[r].get("ok"), res[r]
+        assert res[r]["row_linear_rel_err"] <= 0.02, res[r]
+        for k, v in res[r].items():
+            if k.endswith("_ranks_equal"):
+                assert v, (k, res[r])
+            if k.endswith("_vs_nccl") and k.startswith(("one_shot", "two_shot")):
+                assert v <= 0.02, (k, res[r])
         assert res[r]["fused_vs_nccl"] <= 0.02 * res[r]["scale"], res[r]
         assert res[r]["fused_vs_one"] <= 0.05 * res[r]["scale"], res[r]
         assert res[r]["tok_agree"] >= 0.95 and res[r]["spec_eq_plain"] and res[r]["ranks_agree"], res[r]
