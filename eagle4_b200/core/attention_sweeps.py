@@ -33,19 +33,19 @@ class HeadLayout:
                  replicate_kv: bool = True) -> "HeadLayout":
         """With ``replicate_kv``, KV heads fewer than the ranks are replicated (one per rank)."""
         if num_qo_heads_total % tp_size:
-            raise ValueError("Total number of query heads must be divisible by tp_size.")
+            raise ValueError("the query heads do not split evenly over tp_size ranks")
         kv_total = num_kv_heads_total
         if replicate_kv:
             if kv_total % tp_size and tp_size % kv_total:
-                raise ValueError("KV heads and tp_size must divide one another.")
+                raise ValueError("neither the KV heads nor tp_size divides the other")
         elif kv_total % tp_size:
-            raise ValueError("Total number of KV heads must be divisible by tp_size.")
+            raise ValueError("the KV heads do not split evenly over tp_size ranks")
         return cls(num_qo_heads_total // tp_size, max(1, kv_total // tp_size), head_dim)
 
 
 class Timer(Protocol):
     def time_us(self, batch_size: int, qo_len: int, kv_len: int, num_layers: int) -> int:
-        """Microseconds for ``num_layers`` attention calls at this shape."""
+        """The time in microseconds of ``num_layers`` attention launches of this shape."""
 
 
 def time_calls(fn, calls: int) -> int:
@@ -110,7 +110,7 @@ def sweep(timer: Timer, *, category: str, batch_size: int, qo_lens: Sequence[int
                 records.append(MeasureRecord(us, plan.num_layers, q, kv, category, batch_size))
             _warn_if_low(device)
         if not records:
-            raise RuntimeError(f"No valid measurements collected for qo_len = {q}.")
+            raise RuntimeError(f"query length {q}: every timing of the sweep was invalid")
         path = os.path.join(save_dir, f"cache_qo_len_{q}.jsonl")
         save_jsonl(path, records)
         written.append(path)
@@ -122,5 +122,5 @@ def _warn_if_low(device: str) -> None:
         return
     free, total = torch.cuda.mem_get_info(device)
     if free < 0.05 * total:
-        log.warning("Low GPU memory during the attention sweep; timings may be slower.")
+        log.warning("the attention sweep runs short of device memory; its timings may read slow")
         torch.cuda.empty_cache()

@@ -105,7 +105,7 @@ def _r4(values: Iterable[float]) -> List[float]:
 # --------------------------------------------------------------------------------------------- parameters / layout
 @dataclass
 class MeasureParams:
-    """What one batch size's calibration measures (``config/measure_config.json``)."""
+    """The sweep of one batch size's calibration, as stored in ``config/measure_config.json``."""
 
     context_step: int
     context_stop: int
@@ -166,11 +166,11 @@ class CacheSweepPlan:
     def from_params(cls, params: MeasureParams) -> "CacheSweepPlan":
         step, stop = params.context_step, params.context_stop
         if step not in (64, 128, 256, 512, 1024):
-            raise ValueError(f"context_step must be 64, 128, 256, 512 or 1024, got {step}.")
+            raise ValueError(f"the context step {step} is not one of 64, 128, 256, 512, 1024")
         if not 2048 <= stop <= 128 * 1024:
-            raise ValueError(f"context_stop must be in [2048, 131072], got {stop}.")
+            raise ValueError(f"the context stop {stop} lies outside 2048..131072")
         if stop % step or not 16 <= stop // step <= 128:
-            raise ValueError(f"context_stop must be 16..128 multiples of context_step, got {stop} / {step}.")
+            raise ValueError(f"the context stop {stop} is not 16 to 128 context steps of {step}")
         layers, interval = params.repeat_cnt, step // 32
         if params.enable_fast_measurement:
             interval = step // 16
@@ -206,7 +206,7 @@ def remove_outliers(data: Sequence[float], initial_threshold: float = 6.0, thres
     identical values has no spread to normalise by: nothing passes the z test and the set counts as unstable.
     """
     if len(data) == 0:
-        raise ValueError("Input data is empty.")
+        raise ValueError("no samples to filter")
     kept = np.asarray(list(data), dtype=np.float64)
     mean = float(np.mean(kept))
     floor = sample_rate * len(kept)
@@ -235,15 +235,15 @@ def _max_interval(path: str, prefix: str) -> int:
             try:
                 ids.append(int(name.split("_")[-1].split(".")[0]))
             except ValueError as e:
-                raise RuntimeError(f"Unexpected file name format: {name}") from e
+                raise RuntimeError(f"{name}: the file name does not end in a query length") from e
     if not ids:
-        raise FileNotFoundError(f"No valid '{prefix}*.json' files found in {path}")
+        raise FileNotFoundError(f"{path} holds no {prefix}<n>.json timing file")
     return max(ids)
 
 
 def _records(path: str) -> List[dict]:
     if not os.path.exists(path):
-        raise FileNotFoundError(f"Source file not found: {path}")
+        raise FileNotFoundError(f"{path} does not exist")
     return load_jsonl(path)
 
 
@@ -269,7 +269,7 @@ def fit_cache_costs(category: str, source: str, target: str, *, max_query_length
             unstable += not stable
     instability = unstable / cells if cells else 0.0
     if instability >= (0.20 if fast else 0.25):
-        log.warning("High cache-cost instability: %.2f%%", instability * 100)
+        log.warning("%.2f%% of the attention-cost intervals did not settle: the fit may be noisy", instability * 100)
     for interval in range((cache_length_stop - cache_length_start) // cache_length_step):
         curve = curves.get(interval, [0.0] * max_query_length)
         ratio = [round(v / curve[0], 4) for v in curve] if curve and curve[0] > 0 else []
@@ -286,7 +286,7 @@ def _cache_curves(path: str) -> Dict[int, list]:
     for i in range(_max_interval(path, "cache_interval_") + 1):
         name = os.path.join(path, f"cache_interval_{i}.json")
         if not os.path.exists(name):
-            raise FileNotFoundError(f"Expected cache interval file not found: {name}")
+            raise FileNotFoundError(f"the attention-cost fit for interval file {name} is missing")
         with open(name, encoding="utf-8") as f:
             out[i] = json.load(f).get("array", [])
     return out
@@ -319,13 +319,13 @@ def fit_query_costs(category: str, model_source: str, cache_source: str, target:
     unstable = 0
     for q in lens:
         if not rest.get(q):
-            raise RuntimeError(f"No query cost data available for query length {q}.")
+            raise RuntimeError(f"query length {q} has no settled non-attention timing")
         mean, _, stable = remove_outliers(rest[q], convergence_threshold=0.50 if average else 0.30)
         unstable += not stable
         fitted[q] = mean
     instability = unstable / len(lens) if lens else 0.0
     if instability >= 0.30:
-        log.warning("High query-cost instability: %.2f%%", instability * 100)
+        log.warning("%.2f%% of the query lengths did not settle: the non-attention fit may be noisy", instability * 100)
     for q in lens:
         _dump(os.path.join(target, f"query_{q}.json"), {"mean": round(fitted[q], 4), "array": _r4(rest[q]),
                                                         "batch_size": batch_size,
@@ -343,7 +343,7 @@ def fit_model_costs(category: str, query_source: str, cache_source: str, target:
     for q in lens:
         name = os.path.join(query_source, f"query_{q}.json")
         if not os.path.exists(name):
-            raise FileNotFoundError(f"Expected query cost file not found: {name}")
+            raise FileNotFoundError(f"the non-attention cost fit {name} is missing")
         with open(name, encoding="utf-8") as f:
             rest.append(json.load(f).get("mean", 0.0))
     swa_interval = max(sliding_window // cache_length_step - 1, 0)
@@ -354,7 +354,7 @@ def fit_model_costs(category: str, query_source: str, cache_source: str, target:
         curve = cache.get("array", [])
         curves.append(curve)
         if not curve or len(curve) != max_query_length_cache:
-            raise RuntimeError(f"Cache cost data for interval {interval} is invalid.")
+            raise RuntimeError(f"the attention-cost fit of interval {interval} is unusable")
         windowed = swa_interval > 0 and interval > swa_interval
         costs = []
         for r, q in zip(rest, lens):
@@ -391,15 +391,15 @@ def attention_shape(config: Any) -> AttentionShape:
     window = getattr(config, "sliding_window", None) or 0
     if types is None:
         if getattr(config, "full_attention_interval", None) or getattr(config, "hybrid_override_pattern", None):
-            raise ValueError("hybrid calibration needs explicit layer_types in the model config")
+            raise ValueError("a hybrid model config must list its layer_types for calibration")
         windowed = window and getattr(config, "use_sliding_window", True)
         types = ["sliding_attention" if windowed else "full_attention"] * layers
     if len(types) != layers or set(types) - {"full_attention", "sliding_attention", "linear_attention", "mamba"}:
-        raise ValueError(f"cannot infer attention layout for calibration: {types!r}")
+        raise ValueError(f"no attention layout can be read from layer types {types!r}")
     attn = sum(t in ("full_attention", "sliding_attention") for t in types)
     sliding = types.count("sliding_attention")
     if attn < 1 or (sliding and window <= 0):
-        raise ValueError("calibration needs attention layers and a positive window for sliding attention")
+        raise ValueError("calibration needs at least one attention layer, and a window above zero for sliding ones")
     return AttentionShape(attn, sliding, window)
 
 

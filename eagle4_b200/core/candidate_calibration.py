@@ -25,7 +25,7 @@ def load_candidate_crossover(data_path, identity: Mapping[str, Any]) -> Optional
         return None
     limit = profile.get("max_single_pass_elements", profile.get("max_triton_elements"))
     if type(limit) is not int or limit < 0:
-        raise ValueError(f"invalid candidate top-k crossover in {path}: {limit!r}")
+        raise ValueError(f"{path}: the candidate top-k crossover {limit!r} is not a positive element count")
     return limit
 
 

@@ -45,10 +45,10 @@ class AcceptProfile:
     @classmethod
     def from_counts(cls, drafts: int, accepted_per_position: Sequence[int]) -> "AcceptProfile":
         if drafts <= 0:
-            raise ValueError(f"an acceptance profile needs at least one round, got drafts={drafts}.")
+            raise ValueError(f"{drafts} drafted rounds: an acceptance profile is measured over one round or more")
         c = list(accepted_per_position)
         if any(not 0 <= x <= drafts for x in c) or any(later > earlier for earlier, later in zip(c, c[1:])):
-            raise ValueError(f"accepted_per_position must be non-increasing counts in [0, drafts]: {c}")
+            raise ValueError(f"accepted counts per position {c} are not a non-increasing sequence within the drafted rounds")
         return cls(tuple(x / drafts for x in c))
 
     @property
@@ -57,7 +57,7 @@ class AcceptProfile:
 
     def expected_tokens(self, width: int) -> float:
         if not 1 <= width <= self.max_width:
-            raise ValueError(f"the profile covers widths 1..{self.max_width}, got {width}.")
+            raise ValueError(f"width {width} is beyond the profile's widths 1..{self.max_width}")
         return 1.0 + sum(self.rates[:width - 1])
 
 
@@ -184,7 +184,7 @@ def load_round_times(data_path: str) -> Optional[Dict[int, Dict[int, float]]]:
 def save_round_times(data_path: str, rows: Sequence[Mapping[str, float]]) -> str:
     for row in rows:
         if row["batch_size"] < 1 or row["width"] < 0 or row["round_us"] <= 0:
-            raise ValueError(f"a served round time needs batch_size >= 1, width >= 0 and round_us > 0: {dict(row)}")
+            raise ValueError(f"served round time {dict(row)} has a batch size below 1, a negative width or a non-positive period")
     return _write_json(os.path.join(data_path, ROUNDS_FILE), {"rounds": [dict(r) for r in rows]}, indent=1)
 
 
@@ -208,7 +208,7 @@ def width_at(schedule: Sequence[Tuple[int, int, int]], batch_size: int) -> int:
     for first, last, w in schedule:
         if first <= batch_size <= last:
             return w
-    raise ValueError(f"batch size {batch_size} is outside the chain width schedule {list(schedule)}")
+    raise ValueError(f"no chain width is scheduled for batch size {batch_size} (schedule {list(schedule)})")
 
 
 # --------------------------------------------------------------------------------------------- tree under load

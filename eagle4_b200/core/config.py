@@ -1,8 +1,9 @@
 """``HarnessConfig``: every option of the EAGLE_HARNESS algorithm in one typed JSON object.
 
 The JSON keys, their defaults and the refusal of unknown and removed keys are the public surface shared with the
-reference (``eagle_harness/core/config.py:37-296``, documented keys in ``docs/configuration.md:13-25``). Parsing is
-a small typed-dataclass reader of this package's own. Configuration reads no environment variables.
+reference (``eagle_harness/core/config.py:37-296``, documented keys in ``docs/configuration.md:13-25``). The reader
+is a schema table (one value checker per key) walked once over the JSON object; it collects every problem of a
+configuration and reports them together. Configuration reads no environment variables.
 """
 
 from __future__ import annotations
@@ -11,9 +12,8 @@ import dataclasses
 import enum
 import json
 import os
-import typing
 from dataclasses import dataclass, field
-from typing import TYPE_CHECKING, Any, Dict, Mapping, Optional, Tuple
+from typing import TYPE_CHECKING, Any, Callable, Dict, Mapping, Optional, Tuple
 
 from eagle4_b200.core.cost_model import ChainCoef, CostModel, CostModelParams, depth_loss_ratio
 from eagle4_b200.core.cost_table import BatchCostTable, cost_model_problem, load_cost_tables
@@ -99,9 +99,9 @@ class HarnessConfig:
 
     def validate(self) -> "HarnessConfig":
         if self.mode is Mode.CALIBRATE and not self.data_path:
-            raise ValueError("calibrate mode needs data_path for its output")
+            raise ValueError("mode calibrate writes its tables under data_path: set it")
         if self.max_verify_batch_size is not None and self.max_verify_batch_size < 1:
-            raise ValueError("max_verify_batch_size must be at least 1")
+            raise ValueError("max_verify_batch_size is below 1")
         return self
 
     @property
@@ -124,13 +124,15 @@ def build_cost_model(config: HarnessConfig, *, node_top_k: int, tree_depth: int,
         for bs, t in sorted(tables.items()):
             problem = cost_model_problem(t, target_is_moe=target_is_moe)
             if problem is not None:
-                raise ValueError(f"Cost tables under {config.cost_dir}/bs_{bs} cannot drive the cost model: {problem}.")
+                raise ValueError(f"the cost model refuses the tables under {config.cost_dir}/bs_{bs}: {problem}")
     return CostModel(tables=tables, params=config.cost_model.params(loss), intensity=config.intensity,
                      node_top_k=node_top_k, tree_depth=tree_depth, verify_num=verify_num,
                      target_is_moe=target_is_moe)
 
 
-# Keys removed in eagle-harness 0.1.1; a config that sets one is refused by name.
+# ---------------------------------------------------------------------------------------------------- reading
+# Keys the reference removed in 0.1.1. They are part of the public surface: a config that still sets one is refused
+# with the key named (a dotted path; "mode: eval" is the removed mode value).
 REMOVED_IN_0_1_1 = (
     "mode: eval",
     "ragged",
@@ -140,95 +142,155 @@ REMOVED_IN_0_1_1 = (
 )
 
 
-def _typed(tp: Any, value: Any, where: str) -> Any:
-    if dataclasses.is_dataclass(tp):
-        if not isinstance(value, Mapping):
-            raise ValueError(f"{where}: expected an object, got {type(value).__name__}.")
-        return _read(tp, value, where)
-    if isinstance(tp, type) and issubclass(tp, enum.Enum):
-        try:
-            return tp(value)
-        except ValueError as e:
-            raise ValueError(f"{where}: {value!r} is not one of {', '.join(m.value for m in tp)}.") from e
-    origin = typing.get_origin(tp)
-    if origin is typing.Union:
-        if value is None:
+class ConfigError(ValueError):
+    """Every problem found in one configuration object, reported together."""
+
+    def __init__(self, problems):
+        self.problems = list(problems)
+        super().__init__("invalid --speculative-algorithm-config: " + "; ".join(self.problems))
+
+
+# A value checker returns the converted value or records a problem (and returns None).
+_Checker = Callable[[Any, str, list], Any]
+
+
+def _scalar(kind: str) -> _Checker:
+    def check(v: Any, at: str, problems: list) -> Any:
+        ok = {
+            "bool": isinstance(v, bool),
+            "int": isinstance(v, int) and not isinstance(v, bool),
+            "float": isinstance(v, (int, float)) and not isinstance(v, bool),
+            "str": isinstance(v, str),
+        }[kind]
+        if not ok:
+            problems.append(f"{at} must be {_NOUN[kind]} (found {v!r})")
             return None
-        inner = [a for a in typing.get_args(tp) if a is not type(None)][0]
-        return _typed(inner, value, where)
-    if origin is tuple:
-        parts = typing.get_args(tp)
-        if not isinstance(value, (list, tuple)) or len(value) != len(parts):
-            raise ValueError(f"{where}: expected a list of {len(parts)} values.")
-        return tuple(_typed(a, v, f"{where}[{i}]") for i, (a, v) in enumerate(zip(parts, value)))
-    if tp is bool:
-        if not isinstance(value, bool):
-            raise ValueError(f"{where}: expected true/false, got {value!r}.")
-        return value
-    if tp is int:
-        if isinstance(value, bool) or not isinstance(value, int):
-            raise ValueError(f"{where}: expected an integer, got {value!r}.")
-        return value
-    if tp is float:
-        if isinstance(value, bool) or not isinstance(value, (int, float)):
-            raise ValueError(f"{where}: expected a number, got {value!r}.")
-        return float(value)
-    if tp is str:
-        if not isinstance(value, str):
-            raise ValueError(f"{where}: expected a string, got {value!r}.")
-        return value
-    raise TypeError(f"{where}: unsupported field type {tp!r}.")
+        return float(v) if kind == "float" else v
+
+    return check
 
 
-def _read(cls: type, data: Mapping[str, Any], where: str) -> Any:
-    hints = typing.get_type_hints(cls)
-    names = {f.name for f in dataclasses.fields(cls)}
-    dotted = [f"{where}.{k}" if where else k for k in data]
-    if not where and data.get("mode") == "eval":
-        dotted.append("mode: eval")
-    removed = [k for k in dotted if k in REMOVED_IN_0_1_1]
-    if removed:
-        raise ValueError(f"{', '.join(removed)}: removed in eagle-harness 0.1.1 (no engine used it); delete it.")
-    unknown = sorted(set(data) - names)
-    if unknown:
-        raise ValueError(f"{where or 'config'}: unknown keys {unknown}; valid keys are {sorted(names)}.")
-    return cls(**{k: _typed(hints[k], v, f"{where}.{k}" if where else k) for k, v in data.items()})
+_NOUN = {"bool": "true or false", "int": "an integer", "float": "a number", "str": "a string"}
+
+
+def _member(enum_cls) -> _Checker:
+    def check(v: Any, at: str, problems: list) -> Any:
+        for m in enum_cls:
+            if v == m.value:
+                return m
+        problems.append(f"{at} must be one of {[m.value for m in enum_cls]} (found {v!r})")
+        return None
+
+    return check
+
+
+def _maybe(inner: _Checker) -> _Checker:
+    return lambda v, at, problems: None if v is None else inner(v, at, problems)
+
+
+def _fixed_list(*items: _Checker) -> _Checker:
+    def check(v: Any, at: str, problems: list) -> Any:
+        if not isinstance(v, (list, tuple)) or len(v) != len(items):
+            problems.append(f"{at} must be a list of {len(items)} values (found {v!r})")
+            return None
+        return tuple(c(x, f"{at}[{i}]", problems) for i, (c, x) in enumerate(zip(items, v)))
+
+    return check
+
+
+def _object(cls) -> _Checker:
+    return lambda v, at, problems: _read_object(cls, v, at, problems)
+
+
+_F, _I, _B, _S = _scalar("float"), _scalar("int"), _scalar("bool"), _scalar("str")
+_CHAIN = _fixed_list(_F, _F, _F)
+_PREFETCH = _maybe(_fixed_list(_F, _I))
+
+# Each configuration object's keys and how a JSON value becomes the field's value.
+_SCHEMA: Dict[type, Dict[str, _Checker]] = {
+    DraftModelOptions: {"cuda_candidate_kernels": _B, "embed_full": _B, "embed_triton": _B},
+    L2Warm: {"gate_up_gdn": _PREFETCH, "gate_up_attention": _PREFETCH, "down_proj": _PREFETCH,
+             "next_input": _PREFETCH},
+    CostModelConfig: {"threshold": _F, "async_layer_ratio": _F, "depth_loss_ratio": _maybe(_F),
+                      "chain_tiny": _CHAIN, "chain_small": _CHAIN, "chain_medium": _CHAIN, "chain_large": _CHAIN,
+                      "chain_scale_tiny": _F, "chain_tiny_max_bs": _I, "chain_scale_small": _F,
+                      "chain_scale_medium": _F},
+}
+_SCHEMA[HarnessConfig] = {
+    "data_path": _maybe(_S), "cost_cache": _maybe(_S), "mode": _member(Mode), "intensity": _member(ComputeIntensity),
+    "draft_family": _member(DraftFamily), "cost_model": _object(CostModelConfig),
+    "draft_model": _object(DraftModelOptions), "l2_warm": _object(L2Warm), "max_verify_batch_size": _maybe(_I),
+}
+
+
+def _read_object(cls: type, data: Any, at: str, problems: list) -> Any:
+    """One configuration object from JSON ``data``; problems go to ``problems`` (None is returned then)."""
+    label = at or "the configuration"
+    if not isinstance(data, Mapping):
+        problems.append(f"{label} must be a JSON object (found {type(data).__name__})")
+        return None
+    schema = _SCHEMA[cls]
+    found = len(problems)
+    values = {}
+    for key, raw in data.items():
+        path = f"{at}.{key}" if at else key
+        if path in REMOVED_IN_0_1_1 or (path == "mode" and raw == "eval"):
+            name = "mode: eval" if path == "mode" else path
+            problems.append(f"{name} was removed in eagle-harness 0.1.1 (no engine turned it on): drop it")
+        elif key not in schema:
+            problems.append(f"{label} has no key {key!r} (known keys: {', '.join(sorted(schema))})")
+        else:
+            values[key] = schema[key](raw, path, problems)
+    return cls(**values) if len(problems) == found else None
 
 
 def harness_config_from_dict(data: Mapping[str, Any]) -> HarnessConfig:
-    return _read(HarnessConfig, data, "").validate()
+    """A validated :class:`HarnessConfig` from a (possibly partial) JSON object; every problem is reported at once
+    (:class:`ConfigError`, a ``ValueError``)."""
+    problems: list = []
+    config = _read_object(HarnessConfig, data, "", problems)
+    if problems:
+        raise ConfigError(problems)
+    return config.validate()
 
 
-def parse_harness_config(value: Optional[str], *, default_data_path: Optional[str] = None) -> HarnessConfig:
-    """Inline JSON, or a path to a JSON file; empty means the default serve-mode config."""
-    if value is None or not value.strip():
-        return harness_config_from_dict({} if default_data_path is None else {"data_path": default_data_path})
+def _load_json_object(value: str) -> dict:
+    """The JSON object of ``--speculative-algorithm-config``: inline JSON, or the path of a file holding it."""
     text = value.strip()
-    if not text.startswith(("{", "[")):
+    if text[:1] not in ("{", "["):
         with open(os.path.expanduser(text), encoding="utf-8") as f:
             text = f.read()
     try:
         data = json.loads(text)
     except json.JSONDecodeError as e:
-        raise ValueError(f"--speculative-algorithm-config is not valid JSON: {e}") from e
+        raise ValueError(f"--speculative-algorithm-config holds no valid JSON ({e})") from e
     if not isinstance(data, dict):
-        raise ValueError("--speculative-algorithm-config must be a JSON object.")
-    if default_data_path is not None and data.get("data_path") is None \
-            and data.get("mode", Mode.SERVE.value) == Mode.SERVE.value:
-        data["data_path"] = default_data_path
+        raise ValueError("--speculative-algorithm-config must hold one JSON object")
+    return data
+
+
+def parse_harness_config(value: Optional[str], *, default_data_path: Optional[str] = None) -> HarnessConfig:
+    """The configuration from ``--speculative-algorithm-config`` (inline JSON or a file path; empty or None: the
+    default serve-mode configuration). ``default_data_path`` (a packaged profile matched to the device) fills an
+    absent ``data_path`` of a serve-mode configuration."""
+    data = _load_json_object(value) if value is not None and value.strip() else {}
+    serve = data.get("mode", Mode.SERVE.value) == Mode.SERVE.value
+    if default_data_path is not None and serve and data.get("data_path") is None:
+        data = dict(data, data_path=default_data_path)
     return harness_config_from_dict(data)
 
 
 def config_to_dict(config: HarnessConfig) -> Dict[str, Any]:
-    """Plain JSON data: enums by value, tuples as lists, nested dataclasses as objects."""
-
-    def conv(v: Any) -> Any:
+    """Plain JSON data: enums by value, tuples as lists, nested configuration objects as dicts."""
+    out: Dict[str, Any] = {}
+    for f in dataclasses.fields(config):
+        v = getattr(config, f.name)
         if dataclasses.is_dataclass(v):
-            return {f.name: conv(getattr(v, f.name)) for f in dataclasses.fields(v)}
-        if isinstance(v, enum.Enum):
-            return v.value
-        if isinstance(v, tuple):
-            return [conv(x) for x in v]
-        return v
-
-    return conv(config)
+            out[f.name] = config_to_dict(v)
+        elif isinstance(v, enum.Enum):
+            out[f.name] = v.value
+        elif isinstance(v, tuple):
+            out[f.name] = json.loads(json.dumps(v))
+        else:
+            out[f.name] = v
+    return out

@@ -110,7 +110,7 @@ def _interval_files(path: str) -> Dict[int, dict]:
             with open(os.path.join(path, name), encoding="utf-8") as f:
                 found[idx] = json.load(f)
         except (ValueError, json.JSONDecodeError):
-            log.warning("Could not parse cost interval file %s", name)
+            log.warning("%s is not a readable cost interval; ignored", name)
     return found
 
 
@@ -119,7 +119,7 @@ def load_batch_table(batch_dir: str, batch_size: int) -> BatchCostTable:
     llm = _interval_files(os.path.join(batch_dir, "model_llm"))
     slm = _interval_files(os.path.join(batch_dir, "model_slm"))
     if not llm and not slm:
-        raise RuntimeError(f"No cost intervals for batch size {batch_size} in {batch_dir}.")
+        raise RuntimeError(f"{batch_dir} holds no cost interval for batch size {batch_size}")
     last = max(list(llm) + list(slm))
     intervals: List[IntervalCost] = []
     ratios: List[float] = []
@@ -153,11 +153,11 @@ def table_problem(table: BatchCostTable) -> Optional[str]:
         for name, c in (("target", iv.target), ("draft", iv.draft)):
             n = len(c.index)
             if not c.value or len(c.value) != n or len(c.ratio) != n:
-                return f"interval {i}: {name} curve has mismatched lengths"
+                return f"interval {i}: the {name} curve's value, ratio and index lists differ in length"
             if not all(math.isfinite(v) and v > 0 for v in c.value):
-                return f"interval {i}: {name} cost is not finite and positive: {c.value}"
+                return f"interval {i}: {name} costs {c.value} include a non-positive or non-finite value"
             if c.index[0] != 0 or any(b <= a for a, b in zip(c.index, c.index[1:])):
-                return f"interval {i}: {name} query index must increase from 0: {c.index}"
+                return f"interval {i}: {name} query lengths {c.index} do not start at 0 and increase"
     return None
 
 
@@ -177,11 +177,11 @@ def cost_model_problem(table: BatchCostTable, *, target_is_moe: bool = False) ->
     for i, iv in enumerate(table.intervals):
         ratio = table.model_ratio[i]
         if not MODEL_RATIO_RANGE[0] <= ratio <= MODEL_RATIO_RANGE[1]:
-            return f"interval {i}: target / draft cost ratio {ratio} outside {MODEL_RATIO_RANGE}"
+            return f"interval {i}: the target costs {ratio} draft steps, outside {MODEL_RATIO_RANGE}"
         at8 = verify_cost_at8(iv.target)
         lo = VERIFY8_RATIO_RANGE[0] if target_is_moe else 0.85
         if not lo <= at8 <= VERIFY8_RATIO_RANGE[1]:
-            return f"interval {i}: target cost at 8 tokens / at 1 token = {at8} outside {(lo, VERIFY8_RATIO_RANGE[1])}"
+            return f"interval {i}: verifying 8 tokens costs {at8} of one token, outside {(lo, VERIFY8_RATIO_RANGE[1])}"
     return None
 
 
@@ -191,7 +191,7 @@ def load_cost_tables(cost_dir: str, key: Optional["CostKey"] = None) -> Dict[int
     With ``key`` the directory's ``key.json`` (in the parent of ``cost_dir``) must name the same setup.
     """
     if not os.path.isdir(cost_dir):
-        log.error("Cost data path not found: %s", cost_dir)
+        log.error("no cost tables at %s", cost_dir)
         return {}
     if key is not None:
         from eagle4_b200.core.live_costs import check_key
@@ -205,14 +205,14 @@ def load_cost_tables(cost_dir: str, key: Optional["CostKey"] = None) -> Dict[int
         try:
             bs = int(entry[3:])
         except ValueError as e:
-            raise RuntimeError(f"Unexpected batch directory name: {entry}") from e
+            raise RuntimeError(f"{entry}: a cost directory entry that is not bs_<batch size>") from e
         if not (os.path.isdir(os.path.join(bdir, "model_llm")) and os.path.isdir(os.path.join(bdir, "model_slm"))):
-            log.warning("Missing model cost directory for batch size %d; skipped.", bs)
+            log.warning("batch size %d has no model cost directory; it is left out", bs)
             continue
         table = load_batch_table(bdir, bs)
         problem = table_problem(table)
         if problem is not None:
-            raise RuntimeError(f"Cost tables under {bdir} cannot drive the cost model: {problem}.")
+            raise RuntimeError(f"the cost model refuses the tables under {bdir}: {problem}")
         tables[bs] = table
     return tables
 

@@ -39,7 +39,7 @@ class TreeShape:
 
     def __post_init__(self) -> None:
         if self.top_k < 1 or self.max_depth < 2:
-            raise ValueError(f"tree needs top_k >= 1 and max_depth >= 2, got {self}")
+            raise ValueError(f"{self}: a draft tree has at least one child per node and two levels")
 
     def layer_start(self, depth: int) -> int:
         return 0 if depth == 1 else self.top_k + (depth - 2) * self.top_k * self.top_k
@@ -88,7 +88,7 @@ class DraftTree:
                  *, max_verify: int, delta_slots: Optional[Iterable[int]] = None):
         k = shape.top_k
         if not 1 <= max_verify <= shape.work_cap:
-            raise ValueError(f"max_verify={max_verify} must be in 1..work_cap={shape.work_cap}")
+            raise ValueError(f"max_verify {max_verify} is outside 1..{shape.work_cap} (the tree's best-set size)")
         slots = frozenset(range(shape.max_depth) if delta_slots is None else delta_slots)
         if not slots <= set(range(shape.max_depth)):
             raise ValueError(f"delta_slots {sorted(slots)} outside 0..{shape.max_depth - 1}")

@@ -57,7 +57,7 @@ def nearest_cost_batch_size(batch_size: int, measured: Iterable[int]) -> int:
     """Closest measured batch size; on a tie the larger one wins."""
     pool = sorted(measured)
     if not pool:
-        raise ValueError("No measured batch sizes in the cost data.")
+        raise ValueError("the cost data measures no batch size")
     best = pool[0]
     for b in pool[1:]:
         if abs(b - batch_size) <= abs(best - batch_size):
@@ -68,13 +68,13 @@ def nearest_cost_batch_size(batch_size: int, measured: Iterable[int]) -> int:
 def verify_buckets(batch_size: int, intensity: ComputeIntensity) -> List[int]:
     """Verify widths (tokens per request) that get a target graph and a cost curve, widest first."""
     if batch_size <= 0:
-        raise ValueError(f"batch_size must be positive, got {batch_size}.")
+        raise ValueError(f"batch size {batch_size} is not positive")
     if batch_size > MAX_BATCH_SIZE_CHAIN:
-        raise NotImplementedError(f"batch_size={batch_size} exceeds the chain batch limit {MAX_BATCH_SIZE_CHAIN}.")
+        raise NotImplementedError(f"batch size {batch_size} is above the {MAX_BATCH_SIZE_CHAIN} requests chain rounds serve")
     if intensity is ComputeIntensity.CHAIN:
         return list(_CHAIN_BUCKETS)
     if batch_size > MAX_BATCH_SIZE_TREE:
-        raise NotImplementedError(f"the tree draft batch limit is {MAX_BATCH_SIZE_TREE}, got batch_size={batch_size}.")
+        raise NotImplementedError(f"batch size {batch_size} is above the {MAX_BATCH_SIZE_TREE} requests tree rounds serve")
     high = intensity is ComputeIntensity.HIGH
     if batch_size <= 2 or (batch_size <= 8 and high):
         return list(_TREE_BUCKETS_SMALL)
@@ -109,14 +109,14 @@ def check_shape(
     cap = max_batch_size(intensity)
     if max_running_requests > cap:
         kind = "chain" if chain else "tree"
-        raise ValueError(f"max_running_requests={max_running_requests} exceeds the {kind} draft batch limit {cap}.")
+        raise ValueError(f"max_running_requests {max_running_requests} is above the {cap} requests {kind} rounds serve")
     if tree_depth > (MAX_CHAIN_DEPTH if chain else MAX_TREE_DEPTH):
-        raise NotImplementedError(f"tree_depth={tree_depth} is not supported for {intensity.value}.")
+        raise NotImplementedError(f"{intensity.value} rounds do not draft {tree_depth} levels deep")
     if node_top_k > MAX_NODE_TOP_K:
-        raise NotImplementedError(f"--speculative-eagle-topk > {MAX_NODE_TOP_K} is not supported.")
+        raise NotImplementedError(f"--speculative-eagle-topk is at most {MAX_NODE_TOP_K}")
     if chain and node_top_k > 1:
-        raise NotImplementedError("--speculative-eagle-topk > 1 is not supported for chain_intensity.")
+        raise NotImplementedError("chain_intensity drafts one child per node: --speculative-eagle-topk must be 1")
     if verify_num > (MAX_CHAIN_VERIFY_NUM if chain else MAX_VERIFY_NUM):
-        raise NotImplementedError(f"verify_num={verify_num} is not supported for {intensity.value}.")
+        raise NotImplementedError(f"{intensity.value} rounds do not verify {verify_num} tokens")
     if verify_num <= 1:
-        raise ValueError("verify_num <= 1 is invalid.")
+        raise ValueError("a verify of one token or fewer drafts nothing")

@@ -54,7 +54,7 @@ def draw_children(logits: torch.Tensor, token_ids: torch.Tensor, count: int, *,
                   ) -> ChildProposals:
     """``count`` ordered draws without replacement from ``softmax(logits)`` (Gumbel-top-k)."""
     if logits.ndim != 2 or token_ids.shape != logits.shape or not 1 <= count <= logits.shape[1]:
-        raise ValueError("expected matching [rows, candidates] logits/ids and count within the candidate width")
+        raise ValueError("logits and ids must share one [rows, candidates] shape, and the draw count fit in it")
     q = torch.softmax(logits.float(), dim=-1)
     if uniforms is None:
         uniforms = torch.rand(q.shape, dtype=q.dtype, device=q.device, generator=generator)
