@@ -190,18 +190,19 @@ def save_round_times(data_path: str, rows: Sequence[Mapping[str, float]]) -> str
 
 def chain_widths(data_path: str, max_width: int, max_batch_size: int, *, allow_no_spec: bool = False,
                  key: Optional[CostKey] = None) -> Optional[Schedule]:
-    """Chain widths under ``data_path``: served round times when measured, else the cost tables; both need the
-    acceptance profile. With ``key``, a directory measured on another setup is refused."""
+    """The chain-width schedule a calibration directory gives (None when it lacks the acceptance profile, or both
+    the served round times and the cost tables). Measured round periods take precedence over cost tables, which
+    only estimate them. A directory keyed to another setup than ``key`` is refused."""
     profile = load_accept_profile(data_path)
+    if profile is not None and key is not None:
+        check_key(data_path, key)
     if profile is None:
         return None
-    if key is not None:
-        check_key(data_path, key)
-    rounds = load_round_times(data_path)
-    if rounds is not None:
-        return served_width_schedule(rounds, profile, max_width, max_batch_size, allow_no_spec=allow_no_spec)
-    tables = load_cost_tables(os.path.join(data_path, "cost"))
-    return chain_width_schedule(tables, profile, max_width, max_batch_size) if tables else None
+    periods = load_round_times(data_path)
+    if periods is None:
+        tables = load_cost_tables(os.path.join(data_path, "cost"))
+        return chain_width_schedule(tables, profile, max_width, max_batch_size) if tables else None
+    return served_width_schedule(periods, profile, max_width, max_batch_size, allow_no_spec=allow_no_spec)
 
 
 def width_at(schedule: Sequence[Tuple[int, int, int]], batch_size: int) -> int:
@@ -214,8 +215,8 @@ def width_at(schedule: Sequence[Tuple[int, int, int]], batch_size: int) -> int:
 # --------------------------------------------------------------------------------------------- tree under load
 def _check_tree_row(row: Mapping[str, float]) -> None:
     if row["batch_size"] < 1 or row["width"] < 1 or row["round_us"] <= 0 or row["accept"] < 1 or row["count"] < 1:
-        raise ValueError("a served tree round needs batch_size >= 1, width >= 1, round_us > 0, accept >= 1 and "
-                         f"count >= 1: {dict(row)}")
+        raise ValueError(f"served tree round {dict(row)} needs a batch size, width, accept length and round count "
+                         "of at least 1 and a positive period")
 
 
 TreeCells = Dict[int, Dict[int, Tuple[float, float, int]]]  # batch size -> width -> (round us, accept, rounds)
