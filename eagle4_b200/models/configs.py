@@ -268,6 +268,18 @@ def tiny_draft(target: TargetConfig, draft_vocab: int = 1024) -> DraftConfig:
     )
 
 
+def tiny_nemotron() -> TargetConfig:
+    """A CPU-sized Nemotron-H-style hybrid: Mamba2 and squared-ReLU blocks with one attention layer (hidden 256,
+    Mamba2 8 heads of 32 with state 16 in 2 groups, conv 4, vocab 4096): the Mamba2 tree-verify path in tests."""
+    layers: List[Tuple[Optional[str], Optional[str]]] = [("mamba", None), (None, "relu2"), ("mamba", None),
+                                                         ("attn", None), ("mamba", None), (None, "relu2")]
+    return TargetConfig(
+        family="nemotron_h", hidden_size=256, vocab_size=4096, layers=layers, intermediate_size=512,
+        rms_norm_eps=1e-5, num_heads=4, num_kv_heads=2, head_dim=64, rotary_dim=0, mamba_heads=8,
+        mamba_head_dim=32, mamba_state=16, mamba_groups=2, conv_kernel=4,
+    )
+
+
 def nemotron_h_8b() -> TargetConfig:
     """Nemotron-H-style: 52 layers of single blocks, attention at every 7th layer, Mamba2 128x64 heads, state 128."""
     layers: List[Tuple[Optional[str], Optional[str]]] = []

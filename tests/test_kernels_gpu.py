@@ -308,3 +308,60 @@ def test_topk_large_and_tree_kernels(nat):
     ta, pa = a.verify_rows_reference(bs, 5, 15)
     tb, pb = tree_ops.select_rows(b, bs, 5, 15)
     assert torch.equal(ta, tb) and torch.equal(pa, pb)
+
+
+@pytest.mark.parametrize("shape", ["tiny", "nemotron"])
+def test_mamba_tree_and_commit_against_reference(nat, shape):
+    """Mamba2 tree verify (each row's path replayed from the committed state) and the commit of accepted paths
+    against the float64 definition; one-row decode after a commit equals the row's tree output bit for bit."""
+    import dataclasses
+
+    from eagle4_b200.models.configs import nemotron_h_8b, tiny_nemotron
+
+    cfg = tiny_nemotron() if shape == "tiny" else dataclasses.replace(nemotron_h_8b(), mamba_heads=16)
+    H, P, N, G = cfg.mamba_heads, cfg.mamba_head_dim, cfg.mamba_state, cfg.mamba_groups
+    conv_dim = cfg.mamba_inner + 2 * G * N
+    T, S = 7, 2
+    xbc = _bf(T, conv_dim, scale=0.5, seed=40)
+    dt = _bf(T, H, seed=41)
+    a_log = torch.rand(H, device="cuda").log1p()
+    dt_bias = torch.randn(H, device="cuda") * 0.1
+    dskip = torch.randn(H, device="cuda")
+    state = torch.randn(S, H, P, N, device="cuda") * 0.1
+    slot = torch.tensor([0, 0, 0, 0, 1, 1, 1], dtype=torch.int32, device="cuda")
+    parent = torch.tensor([-1, 0, 0, 1, -1, 4, 5], dtype=torch.int32, device="cuda")
+    out = nat.mamba_tree(xbc, dt, a_log, dt_bias, dskip, state, slot, parent, cfg, False)
+    cpu = lambda t: t.cpu().float()  # noqa: E731
+    want = ref.mamba_tree(cpu(xbc), cpu(dt), a_log.cpu(), dt_bias.cpu(), dskip.cpu(), state.cpu().clone(),
+                          slot.cpu(), parent.cpu(), cfg, False)
+    _close(out, want, 2e-2)
+    # scan mode (prefill): the state advances in place row by row
+    st_scan = state.clone()
+    chain = torch.tensor([-1, 0, 1, 2, -1, 4, 5], dtype=torch.int32, device="cuda")
+    out_scan = nat.mamba_tree(xbc, dt, a_log, dt_bias, dskip, st_scan, slot, chain, cfg, True)
+    st_ref = state.cpu().clone()
+    want_scan = ref.mamba_tree(cpu(xbc), cpu(dt), a_log.cpu(), dt_bias.cpu(), dskip.cpu(), st_ref, slot.cpu(),
+                               chain.cpu(), cfg, True)
+    _close(out_scan, want_scan, 2e-2)
+    _close(st_scan, st_ref, 2e-3)
+    # commit of the paths 0 -> 1 -> 3 and 4 -> 5
+    rows = torch.tensor([[0, 1, 3], [4, 5, 0]], dtype=torch.int32, device="cuda")
+    nrows = torch.tensor([3, 2], dtype=torch.int32, device="cuda")
+    slots = torch.tensor([0, 1], device="cuda")
+    st2 = state.clone()
+    conv = torch.zeros(S, conv_dim, cfg.conv_kernel - 1, dtype=torch.bfloat16, device="cuda")
+    nat.mamba_commit(xbc, dt, a_log, dt_bias, dskip, xbc, st2, conv, slots, rows, nrows, cfg)
+    st_ref = state.cpu().clone()
+    conv_ref = torch.zeros(S, conv_dim, cfg.conv_kernel - 1, dtype=torch.bfloat16)
+    ref.mamba_commit(cpu(xbc), cpu(dt), a_log.cpu(), dt_bias.cpu(), dskip.cpu(), xbc.cpu(), st_ref, conv_ref,
+                     slots.cpu(), rows.cpu(), nrows.cpu(), cfg)
+    _close(st2, st_ref, 2e-3)
+    assert torch.equal(conv.cpu(), conv_ref)
+    # plain decode equals tree verify: commit [0, 1], then verify row 3 alone
+    st3 = state.clone()
+    nat.mamba_commit(xbc, dt, a_log, dt_bias, dskip, xbc, st3, conv.clone(), slots[:1],
+                     torch.tensor([[0, 1]], dtype=torch.int32, device="cuda"),
+                     torch.tensor([2], dtype=torch.int32, device="cuda"), cfg)
+    solo = nat.mamba_tree(xbc[3:4].contiguous(), dt[3:4].contiguous(), a_log, dt_bias, dskip, st3, slot[:1],
+                          torch.tensor([-1], dtype=torch.int32, device="cuda"), cfg, False)
+    assert torch.equal(solo[0], out[3])
