@@ -1,7 +1,8 @@
 """Times the hot kernels at a model's shapes with CUDA events (warm-up first; the weights exceed L2 so every
-launch streams them from HBM) and reports achieved bandwidth against the measured copy peak.
+launch streams them from HBM) and reports achieved bandwidth against the measured copy peak, plus an MD5 of each
+kernel's output on seeded inputs, so two builds can be checked for bit-identical results.
 
-    python -m eagle4_b200.bench_kernels [--model qwen3.8-27b] [--tokens 1 16 64]
+    python -m eagle4_b200.bench_kernels [--tokens 1 16 64 256] [--only mlp_down ...] [--no-hash]
 """
 
 from __future__ import annotations
@@ -58,6 +59,24 @@ def time_fn(fn, iters: int = 20, warmup: int = 3, graph: bool = True) -> float:
     return s.elapsed_time(e) / iters * 1e3  # microseconds
 
 
+def _md5(out) -> str:
+    """MD5 of a kernel's output tensors (their bytes on the host, in order)."""
+    import hashlib
+
+    h = hashlib.md5()
+    for t in (out if isinstance(out, (tuple, list)) else (out,)):
+        h.update(t.detach().contiguous().cpu().view(torch.uint8).numpy().tobytes())
+    return h.hexdigest()
+
+
+def fn_first(fn, copies, nxt):
+    """``fn``'s output on the first weight copy (the cycle is advanced until it comes round)."""
+    for _ in range(len(copies)):
+        if next(nxt) is copies[-1]:
+            break
+    return fn()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, nargs="*", default=[1, 16, 64, 256])
@@ -66,7 +85,9 @@ def main() -> None:
     ap.add_argument("--only", nargs="*", default=None, help="kernel names to run")
     ap.add_argument("--nk", type=int, nargs="*", default=None, help="extra plain GEMM shapes as N K pairs")
     ap.add_argument("--eager", action="store_true", help="time eager calls instead of one captured graph")
+    ap.add_argument("--no-hash", action="store_true", help="skip the output MD5")
     args = ap.parse_args()
+    torch.manual_seed(0)
     from eagle4_b200.ops import native
 
     peak = _peak_gbs()
@@ -89,18 +110,22 @@ def main() -> None:
         nxt = itertools.cycle(copies)
         for t in args.tokens:
             x = torch.randn(t, k, device=dev).to(torch.bfloat16)
+            res = torch.randn(t, n, device=dev).to(torch.bfloat16)
             if name == "mlp_gate_up":
                 fn = lambda: native.linear_swiglu(x, next(nxt))  # noqa: E731
             elif name == "lm_head":
                 fn = lambda: native.lm_head_argmax(x, next(nxt))  # noqa: E731
+            elif name in ("gdn_out_proj", "attn_o_proj", "mlp_down"):  # the block's output projection adds the residual
+                fn = lambda: native.linear_residual(x, next(nxt), res)  # noqa: E731
             else:
                 fn = lambda: native.linear(x, next(nxt))  # noqa: E731
             us = time_fn(fn, args.iters, args.warmup, not args.eager)
+            digest = None if args.no_hash else _md5(fn_first(fn, copies, nxt))
             gbs = (n * k * 2 + t * k * 2 + t * n * 2) / (us * 1e-6) / 1e9
             tflops = 2.0 * n * k * t / (us * 1e-6) / 1e12
             rows.append({"kernel": name, "N": n, "K": k, "T": t, "us": round(us, 2), "GB/s": round(gbs, 1),
                          "frac_of_measured_hbm": round(gbs / peak, 3), "TFLOP/s": round(tflops, 1),
-                         "frac_of_measured_bf16": round(tflops / _peak_tflops(), 3)})
+                         "frac_of_measured_bf16": round(tflops / _peak_tflops(), 3), "md5": digest})
             print(json.dumps(rows[-1]), flush=True)
         del w0, copies
     if not args.only or "attn_verify" in args.only:

@@ -94,6 +94,9 @@ struct Params {
   int ldx;
   float fold_eps;
   int fold;
+  // 1: every output (and residual) row is 16-byte aligned and whole 8-feature pieces fit in N, so the epilogue
+  // stages each 16-token chunk in shared memory and moves it with 16-byte loads and stores (set_vector_epilogue)
+  int vec;
 };
 
 // trace slots: 0 start, 1 setup done, 2 first stage landed (MMA), 3 last MMA issued, 4 first accumulator ready
@@ -270,12 +273,77 @@ __device__ __forceinline__ void tp_gather_tiles(const Params& p, int ep_tid, uns
   }
 }
 
+// Vectorised final epilogue of one 16-token chunk: the accumulator values go to shared memory as [token][row]
+// fp32, then each thread finishes 8 consecutive features of one token (residual, activation) and moves them with
+// 16-byte loads and stores. The per-element arithmetic is the scalar path's (fp32 add, one rounding), so both give
+// the same bits.
+__device__ __forceinline__ void store_chunk_vec(const Params& p, int tile, int m, int j0, const float* v,
+                                                float* xchg, int ep_tid) {
+  float* st = xchg;  // [16 tokens][128 rows]
+#pragma unroll
+  for (int i = 0; i < 16; ++i) st[i * kTileM + m] = v[i];
+  named_bar(1, 128);
+  if (p.epi == kSwiGLU) {
+    // rows [0,64) gate, [64,128) up: 16 tokens x 8 pieces of 8 output features, one piece per thread
+    const int i = ep_tid >> 3, piece = ep_tid & 7;
+    const int j = j0 + i, f = tile * 64 + piece * 8;
+    if (j < p.T && f < p.N / 2) {
+      const float* g = st + i * kTileM + piece * 8;
+      uint4 out;
+      __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        o2[e] = __floats2bfloat162_rn(silu(g[2 * e]) * g[64 + 2 * e], silu(g[2 * e + 1]) * g[64 + 2 * e + 1]);
+      *reinterpret_cast<uint4*>(p.y + size_t(j) * p.ldy + f) = out;
+    }
+  } else {
+    for (int q = ep_tid; q < 16 * 16; q += 128) {
+      const int i = q >> 4, piece = q & 15;
+      const int j = j0 + i, n = tile * kTileM + piece * 8;
+      if (j >= p.T || n >= p.N) continue;
+      const float4 lo = *reinterpret_cast<const float4*>(st + i * kTileM + piece * 8);
+      const float4 hi = *reinterpret_cast<const float4*>(st + i * kTileM + piece * 8 + 4);
+      float a[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+      if (p.epi == kF32) {
+        float4* dst = reinterpret_cast<float4*>(p.yf + size_t(j) * p.ldy + n);
+        dst[0] = lo;
+        dst[1] = hi;
+        continue;
+      }
+      if (p.epi == kResidual) {
+        const uint4 ru = *reinterpret_cast<const uint4*>(p.res + size_t(j) * p.ldr + n);
+        const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&ru);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(r2[e]);
+          a[2 * e] += f.x;
+          a[2 * e + 1] += f.y;
+        }
+      }
+      if (p.epi == kReLU2) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) { a[e] = fmaxf(a[e], 0.f); a[e] = a[e] * a[e]; }
+      }
+      uint4 out;
+      __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o2[e] = __floats2bfloat162_rn(a[2 * e], a[2 * e + 1]);
+      *reinterpret_cast<uint4*>(p.y + size_t(j) * p.ldy + n) = out;
+    }
+  }
+  named_bar(1, 128);
+}
+
 // Final epilogue of 16 token columns [j0, j0+16) held by this thread for weight row ``m`` of ``tile``.
 __device__ __forceinline__ void store_chunk(const Params& p, int tile, int m, int j0, const float* v, float* xchg,
                                             int ep_tid, unsigned half) {
   const int n = tile * kTileM + m;
   if (p.epi == kAllReduce) {
     tp_send_chunk(p, tile, m, j0, v, xchg, ep_tid, half);
+    return;
+  }
+  if (p.vec && p.epi != kArgmax) {
+    store_chunk_vec(p, tile, m, j0, v, xchg, ep_tid);
     return;
   }
   if (p.epi == kSwiGLU) {
@@ -470,11 +538,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
     // kAllReduce: this call's number (its low bit picks the buffer half; number + 1 tags its flags)
     const unsigned call = p.epi == kAllReduce ? *reinterpret_cast<const volatile unsigned*>(p.tp_calls) : 0u;
     const unsigned half = call & 1u, tag = call + 1u;
-    int* missing = reinterpret_cast<int*>(xchg + 16 * 64 + 256);  // [kMaxRanks] flags of absent ranks
+    int* missing = reinterpret_cast<int*>(xchg + 16 * kTileM + 256);  // [kMaxRanks] flags of absent ranks
     const int ep_tid = threadIdx.x - 64;
     const int quarter = warp & 3;
     const int m = quarter * 32 + lane;
-    float* rsv = xchg + 16 * 64;  // [nt] folded-norm scales
+    float* rsv = xchg + 16 * kTileM;  // [nt] folded-norm scales
     if (p.fold) {
       // token t's sum of squares: lane partials over 16-byte pieces in index order, then a butterfly (fixed order)
       for (int t = warp - 2; t < p.nt; t += 4) {
@@ -708,6 +776,18 @@ int gemm_grid(long total, int max_ctas) {
   return int(std::max<long>(1, std::min<long>(max_ctas, by_work)));
 }
 
+// Whether the launch's outputs allow the vectorised epilogue (16-byte aligned rows, whole 8-feature pieces).
+void set_vector_epilogue(Params& p) {
+  auto al16 = [](const void* q) { return q != nullptr && (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  bool ok = false;
+  if (p.epi == kF32) ok = al16(p.yf) && p.ldy % 4 == 0 && p.N % 8 == 0;
+  else if (p.epi == kSwiGLU) ok = al16(p.y) && p.ldy % 8 == 0 && (p.N / 2) % 8 == 0;
+  else if (p.epi == kPlain || p.epi == kReLU2) ok = al16(p.y) && p.ldy % 8 == 0 && p.N % 8 == 0;
+  else if (p.epi == kResidual)
+    ok = al16(p.y) && p.ldy % 8 == 0 && p.N % 8 == 0 && al16(p.res) && p.ldr % 8 == 0;
+  p.vec = ok ? 1 : 0;
+}
+
 // Pipeline stages for a token tile of ``nt`` columns: the stage cap, bounded by 200 KB of tiles.
 int stage_count(int nt) {
   const int stage_bytes = kWTileBytes + nt * kTileK * 2;
@@ -715,11 +795,11 @@ int stage_count(int nt) {
 }
 
 // Dynamic shared memory of one launch: 1 KB alignment slack, the stages, barriers and TMEM handle (64 B), the
-// epilogue exchange buffer (16 x 64 floats), the folded-norm scales (256 floats), the all-reduce's absent-rank
+// epilogue exchange buffer (16 x 128 floats), the folded-norm scales (256 floats), the all-reduce's absent-rank
 // flags (kMaxRanks ints) and 1 KB of slack.
 size_t smem_bytes(int stages, int nt) {
   const int stage_bytes = kWTileBytes + nt * kTileK * 2;
-  return 1024 + size_t(stages) * stage_bytes + 64 + 16 * 64 * 4 + 256 * 4 + kMaxRanks * 4 + 1024;
+  return 1024 + size_t(stages) * stage_bytes + 64 + 16 * kTileM * 4 + 256 * 4 + kMaxRanks * 4 + 1024;
 }
 
 struct Scratch {
@@ -789,6 +869,7 @@ int launch_chunks(const torch::Tensor& x, const torch::Tensor& w, int epi, F chu
     p.counters = sc.counters.data_ptr<int>();
     p.err = sc.err.data_ptr<int>();
     chunk(p, t0);
+    set_vector_epilogue(p);
     const __nv_bfloat16* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()) + size_t(t0) * x.stride(0);
     p.xr = xp;
     p.ldx = int(x.stride(0));
@@ -978,6 +1059,7 @@ extern "C" int e4_gemm_bf16_noalloc(const void* x, int ldx, const void* w, int l
   p.err = reinterpret_cast<int*>(b + noalloc::kErrOffset);
   p.y = reinterpret_cast<__nv_bfloat16*>(y);
   p.ldy = ldy;
+  set_vector_epilogue(p);
   CUtensorMap wmap, xmap;
   try {
     wmap = make_map(w, N, K, ldw, kTileM);
