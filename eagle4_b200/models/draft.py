@@ -34,8 +34,10 @@ class DraftCache:
     v: torch.Tensor
 
     @classmethod
-    def allocate(cls, cfg: DraftConfig, block_table: torch.Tensor, page: int, device, dtype) -> "DraftCache":
-        slots = block_table.numel() * page
+    def allocate(cls, cfg: DraftConfig, block_table: torch.Tensor, page: int, device, dtype,
+                 pages: Optional[int] = None) -> "DraftCache":
+        """Draft KV for the target's block table: ``pages`` physical pages (default: one per table entry)."""
+        slots = (block_table.numel() if pages is None else pages) * page
         k = torch.zeros(slots, cfg.num_kv_heads, cfg.head_dim, dtype=dtype, device=device)
         return cls(block_table, page, k, torch.zeros_like(k))
 

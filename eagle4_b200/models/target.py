@@ -58,10 +58,17 @@ class TargetCache:
 
     @classmethod
     def allocate(cls, cfg: TargetConfig, *, max_reqs: int, max_len: int, page: int, device, dtype,
-                 state_slots: Optional[int] = None) -> "TargetCache":
+                 state_slots: Optional[int] = None, kv_pages: Optional[int] = None) -> "TargetCache":
+        """Caches for ``max_reqs`` block-table rows of up to ``max_len`` positions. Without ``kv_pages`` every row
+        owns ``max_len`` positions (an identity block table); with it the attention caches hold ``kv_pages`` pages
+        that a :class:`~eagle4_b200.runtime.pages.PagePool` maps into the rows (all entries start at page 0)."""
         blocks_per_req = (max_len + page - 1) // page
-        nblocks = max_reqs * blocks_per_req
-        bt = torch.arange(nblocks, dtype=torch.int32, device=device).view(max_reqs, blocks_per_req)
+        if kv_pages is None:
+            nblocks = max_reqs * blocks_per_req
+            bt = torch.arange(nblocks, dtype=torch.int32, device=device).view(max_reqs, blocks_per_req)
+        else:
+            nblocks = kv_pages
+            bt = torch.zeros(max_reqs, blocks_per_req, dtype=torch.int32, device=device)
         slots = nblocks * page
         nattn = len(cfg.layer_ids("attn"))
         k = [torch.zeros(slots, cfg.num_kv_heads, cfg.head_dim, dtype=dtype, device=device) for _ in range(nattn)]

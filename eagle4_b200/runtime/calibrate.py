@@ -59,6 +59,8 @@ class ForwardTimer:
     def __init__(self, engine, repeats: int = 10):
         self.eng = engine
         self.repeats = repeats
+        for row in range(engine.max_reqs):  # timed contexts read real pages, not the trash page
+            engine.pages.reserve(row, engine.max_len)
         self.shapes: Dict[tuple, _Shape] = {}
         self.cuda = engine.device.type == "cuda"
 

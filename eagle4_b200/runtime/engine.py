@@ -29,6 +29,7 @@ from eagle4_b200 import ops
 from eagle4_b200.core.config import HarnessConfig, Mode
 from eagle4_b200.core.cost_model import WidthStep
 from eagle4_b200.core.draft_tree import DraftTree, TreeShape
+from eagle4_b200.runtime.pages import PagePool
 from eagle4_b200.runtime.policy import RoundPolicy, ServedChainPolicy, ServedTreeChoice, fit_width
 from eagle4_b200.models.draft import DraftCache, DraftModel
 from eagle4_b200.models.target import Records, RowBatch, TargetCache, TargetModel
@@ -117,10 +118,13 @@ SAMPLED_STREAM = 0x10000  # random stream of the tree walk's coins (draft steps 
 class Engine:
     def __init__(self, target: TargetModel, draft: Optional[DraftModel], *, max_reqs: int, max_len: int,
                  page: int = 16, steps: int = 4, top_k: int = 2, verify_tokens: int = 8, use_graphs: bool = True,
-                 config: Optional[HarnessConfig] = None, temperature: float = 0.0, seed: int = 0):
+                 config: Optional[HarnessConfig] = None, temperature: float = 0.0, seed: int = 0,
+                 kv_tokens: Optional[int] = None):
         """``temperature > 0`` samples: draft children are drawn without replacement from the draft's candidate
         distribution and verified by recursive tree rejection, so the output follows the target's distribution at
-        that temperature (``temperature == 0``: greedy, equal to plain greedy decoding)."""
+        that temperature (``temperature == 0``: greedy, equal to plain greedy decoding). ``kv_tokens``: positions
+        the attention caches hold over all requests (default ``max_reqs * max_len``); a request's pages are mapped
+        when it is admitted, for the positions it can reach."""
         self.target, self.draft = target, draft
         self.temperature, self.seed = float(temperature), int(seed)
         self.device = target.device
@@ -130,12 +134,16 @@ class Engine:
         self.max_reqs = max_reqs
         span = max(verify_tokens, steps * top_k) + 1
         self.max_len = max_len + span
+        self.span = span
+        kv_pages = (kv_tokens if kv_tokens is not None else max_reqs * self.max_len) // page + 2  # + trash page
         self.tcache = TargetCache.allocate(target.cfg, max_reqs=max_reqs, max_len=self.max_len, page=page,
-                                           device=self.device, dtype=self.dtype)
+                                           device=self.device, dtype=self.dtype, kv_pages=kv_pages)
+        self.pages = PagePool(self.tcache.block_table, kv_pages, page)
         self.dcache = None
         self.tree = None
         if draft is not None:
-            self.dcache = DraftCache.allocate(draft.cfg, self.tcache.block_table, page, self.device, self.dtype)
+            self.dcache = DraftCache.allocate(draft.cfg, self.tcache.block_table, page, self.device, self.dtype,
+                                              pages=kv_pages)
             shape = TreeShape(top_k=top_k, max_depth=steps)
         self.config = config or HarnessConfig(mode=Mode.STATIC)
         self.policy = RoundPolicy(self.config, top_k=top_k, steps=steps, verify_tokens=verify_tokens,
@@ -223,11 +231,14 @@ class Engine:
         return torch.full((n,), v, dtype=torch.int32, device=self.device)
 
     # ------------------------------------------------------------------ prefill (eager)
-    def prefill(self, b: int, prompt: torch.Tensor) -> None:
+    def prefill(self, b: int, prompt: torch.Tensor, reserve_tokens: Optional[int] = None) -> None:
         """Prompt of batch row ``b`` through the target (recurrent layers in scan mode); the first token becomes the
-        root; the draft consumes all but the last ``N`` prompt rows now and the rest at the first round."""
+        root; the draft consumes all but the last ``N`` prompt rows now and the rest at the first round. The row's
+        KV pages are mapped first, for ``reserve_tokens`` positions (default: the engine's ``max_len``)."""
         n = prompt.shape[0]
         slot = int(self.slot[b])
+        self.pages.release(slot)
+        self.pages.reserve(slot, reserve_tokens if reserve_tokens is not None else self.max_len)
         self.tcache.reset_slot(slot)
         pos = torch.arange(n, device=self.device)
         slots = self._slots(torch.tensor(slot, device=self.device), pos)
@@ -556,7 +567,11 @@ class Engine:
         outs: List[List[int]] = [[] for _ in range(bs)]
         ctx = [int(p.shape[0]) for p in prompts]
         for b, p in enumerate(prompts):
-            self.prefill(b, p)
+            need = int(p.shape[0]) + max_new_tokens + self.span
+            if need > self.max_len:
+                raise ValueError(f"request {b}: prompt {int(p.shape[0])} + {max_new_tokens} new tokens + {self.span} "
+                                 f"tree rows exceed max_len {self.max_len - self.span}")
+            self.prefill(b, p, reserve_tokens=need)
         if self.tree is not None:
             self.lagged_scores = None
         self.host_tok[:bs].copy_(self.out_tok[:bs])
