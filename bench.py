@@ -206,6 +206,10 @@ def main() -> None:
     gen = torch.Generator().manual_seed(1234 + (0 if tp_mode else rank))
     prompts = torch.randint(0, llm.target.cfg.vocab_size, (args.batch, args.prompt), generator=gen).pin_memory()
     eng = llm.engine
+    if tp_mode:  # a crashed or hung rank is named between rounds, before the next round's collectives
+        from eagle4_b200.parallel.health import process_group_heartbeat
+
+        eng.heartbeat = process_group_heartbeat()
 
     def barrier():
         if dist is not None:

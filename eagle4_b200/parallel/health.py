@@ -60,3 +60,13 @@ def _td(seconds: float):
     import datetime
 
     return datetime.timedelta(seconds=seconds)
+
+
+def process_group_heartbeat(group=None) -> Optional[Heartbeat]:
+    """A :class:`Heartbeat` in the default process group's store (None without a multi-rank group)."""
+    if not dist.is_initialized() or dist.get_world_size(group) < 2:
+        return None
+    from torch.distributed import distributed_c10d
+
+    store = distributed_c10d._get_default_store()
+    return Heartbeat(store, dist.get_rank(group), dist.get_world_size(group))

@@ -157,6 +157,17 @@ class Engine:
 
                 schedule = chain_widths(self.config.data_path, verify_tokens, max_reqs)
             self.chain_policy = ServedChainPolicy(range(2, verify_tokens + 1), schedule=schedule)
+        # batches above the verify limit decode natively (reference default: 32 requests for trees, 48 for chains,
+        # in serve mode; an explicit max_verify_batch_size applies in every mode)
+        limit = self.config.max_verify_batch_size
+        if limit is None and self.config.mode.uses_cost_model:
+            limit = 48 if top_k == 1 else 32
+        self.verify_batch_limit = limit
+        # failure detection among tensor-parallel ranks: a Heartbeat (parallel.health) beats and checks every
+        # ``heartbeat_every`` rounds, before the round's collectives
+        self.heartbeat = None
+        self.heartbeat_every, self.heartbeat_timeout = 64, 30.0
+        self._rounds_served = 0
         # serve mode: per batch bucket, speculate or decode natively, whichever yields more tokens per microsecond
         self.tree_choice = None
         if draft is not None and top_k > 1 and self.config.mode.uses_cost_model:
@@ -578,17 +589,27 @@ class Engine:
         for b in range(bs):
             outs[b].append(int(self.host_tok[b, 0]))
         spec = speculative and self.draft is not None
+        over_limit = spec and self.verify_batch_limit is not None and bs > self.verify_batch_limit
         while min(len(o) for o in outs) < max_new_tokens:
             self._pending_timing = None
             self._captured = False
+            self._rounds_served += 1
+            if self.heartbeat is not None and self._rounds_served % self.heartbeat_every == 0:
+                # every rank reaches this round; a peer that crashed or hung is named here, before any collective
+                step = self._rounds_served // self.heartbeat_every
+                self.heartbeat.beat(step)
+                self.heartbeat.check(step, self.heartbeat_timeout)
             chain_t0 = None
             tree_t0 = None
             choice = ServedTreeChoice.SPECULATE
-            if spec and self.tree_choice is not None:
+            if spec and self.tree_choice is not None and not over_limit:
                 choice = self.tree_choice.choice(bs)
                 tree_t0 = _Stamp(self.device)
                 tree_t0.record()
-            if spec and choice == ServedTreeChoice.NATIVE:
+            if over_limit:  # above the verify batch limit: native decode (the draft keeps its pending rows)
+                choice = ServedTreeChoice.NATIVE
+                self._plain(bs)
+            elif spec and choice == ServedTreeChoice.NATIVE:
                 self._plain(bs)
             elif spec and self.chain_policy is not None:
                 chain_w = self.chain_policy.width(bs)

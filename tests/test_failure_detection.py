@@ -88,3 +88,57 @@ def test_unsupported_gpu_is_refused(monkeypatch):
         arch.require_sm100()
     monkeypatch.setattr(torch.cuda, "get_device_capability", lambda d=None: (10, 0))
     arch.require_sm100()
+
+
+def test_engine_beats_and_stops_on_a_late_peer():
+    """The serving loop beats and checks its heartbeat every ``heartbeat_every`` rounds, before the round's
+    collectives, and a late peer ends generation with PeerFailure naming it."""
+    import torch
+
+    from eagle4_b200.api import LLM, TreeSpec
+    from eagle4_b200.parallel.health import PeerFailure
+
+    class FakeHeartbeat:
+        def __init__(self, fail_at=None):
+            self.beats, self.checks, self.fail_at = [], [], fail_at
+
+        def beat(self, step):
+            self.beats.append(step)
+
+        def check(self, step, timeout):
+            self.checks.append(step)
+            if self.fail_at is not None and step >= self.fail_at:
+                raise PeerFailure([1], step)
+
+    llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_len=256)
+    eng = llm.engine
+    eng.heartbeat, eng.heartbeat_every = FakeHeartbeat(), 4
+    p = torch.randint(0, 4096, (1, 16), generator=torch.Generator().manual_seed(0))
+    llm.generate(p, 20, speculative=False)
+    assert eng.heartbeat.beats == eng.heartbeat.checks == list(range(1, len(eng.heartbeat.beats) + 1))
+    assert len(eng.heartbeat.beats) >= 4
+    eng.heartbeat = FakeHeartbeat(fail_at=eng._rounds_served // 4 + 2)
+    try:
+        llm.generate(p, 40, speculative=False)
+        raise AssertionError("a late peer must stop the loop")
+    except PeerFailure as e:
+        assert e.ranks == [1]
+
+
+def test_batches_above_the_verify_limit_decode_natively():
+    import torch
+
+    from eagle4_b200.api import LLM, TreeSpec
+    from eagle4_b200.runtime.recorder import RoundRecorder
+
+    llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_len=256, max_batch=2,
+                        config='{"mode": "static", "max_verify_batch_size": 1}')
+    p = torch.randint(0, 4096, (2, 16), generator=torch.Generator().manual_seed(1))
+    rec = []
+    llm.engine.recorder = type("R", (), {"record": lambda self, **kw: rec.append(kw["kind"])})()
+    out = llm.generate(p, 12)
+    assert set(rec) == {"native"}
+    assert torch.equal(out, llm.generate(p, 12, speculative=False))
+    rec.clear()
+    llm.generate(p[:1], 12)  # one request is within the limit: it speculates
+    assert "tree" in rec
