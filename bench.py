@@ -161,6 +161,9 @@ def main() -> None:
     ap.add_argument("--tp-backend", default="fused", choices=["fused", "torch"])
     ap.add_argument("--mode", default="serve", choices=["serve", "static"],
                     help="serve: live-cost model sizes each round (default); static: the full 12/4/16 tree")
+    ap.add_argument("--sweep", default=None,
+                    help="concurrency sweep (benchmark config 3): comma-separated batch sizes, one JSON line each")
+    ap.add_argument("--prompt-range", default="256,4096", help="sweep prompt lengths, uniform in [lo, hi]")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -200,6 +203,9 @@ def main() -> None:
         tp = TensorParallel(backend=args.tp_backend, max_rows=max(256, args.prompt), max_cols=8192, device=dev)
     replicas = 1 if tp_mode else world  # independent request streams
     tree = TreeSpec(*(int(v) for v in args.tree.split(",")))
+    if args.sweep:
+        sweep(args, tree, tp, dev, rank, world, dist)
+        return
     llm = LLM.synthetic(args.model, device=dev, seed=0, tree=tree, max_batch=args.batch,
                         max_len=args.prompt + args.new_tokens + 64, config=json.dumps({"mode": args.mode}), tp=tp,
                         temperature=args.temperature, sample_seed=7)
@@ -308,6 +314,78 @@ def main() -> None:
     eng.graphs.clear()  # graphs may hold NCCL calls (torch backend): release them before the group goes
     torch.cuda.synchronize()
     if tp is not None:
+        tp.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def sweep(args, tree, tp, dev, rank: int, world: int, dist) -> None:
+    """Benchmark config 3: at each batch size, prompts of uniform-random lengths in ``--prompt-range`` and
+    ``--new-tokens`` greedy tokens, speculative (serve mode) and plain decoding. Prints one JSON line per batch size:
+    decode tokens/s (device time of the rounds, max over ranks), the prefill time, and end-to-end tokens/s."""
+    import torch
+
+    from eagle4_b200.api import LLM
+
+    sizes = [int(v) for v in args.sweep.split(",")]
+    lo, hi = (int(v) for v in args.prompt_range.split(","))
+    gen = torch.Generator().manual_seed(4321)
+    plans = {b: [torch.randint(0, 1 << 30, (int(n),), generator=gen)
+                 for n in torch.randint(lo, hi + 1, (b,), generator=gen)] for b in sizes}
+    span = max(tree.draft_tokens, tree.steps * tree.top_k) + 1
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for b in sizes:
+        line = {"metric": METRIC, "impl": "ours", "n_gpus": world, "batch": b, "dtype": "bf16",
+                "data": "synthetic: uniform-random prompt ids, random-init N(0,0.02) weights of the named shapes",
+                "config": {"model": MODEL_NAMES.get(args.model, args.model), "global_batch": b,
+                           "prompt_range": [lo, hi], "new_tokens": args.new_tokens,
+                           "parallelism": f"tp{world}" if tp is not None else "tp1",
+                           "tree": {"steps": tree.steps, "top_k": tree.top_k, "draft_tokens": tree.draft_tokens,
+                                    "mode": args.mode}}}
+        try:
+            kv = sum(int(p.shape[0]) + args.new_tokens + span for p in plans[b])
+            llm = LLM.synthetic(args.model, device=dev, seed=0, tree=tree, max_batch=b,
+                                max_len=hi + args.new_tokens + 64, config=json.dumps({"mode": args.mode}), tp=tp,
+                                kv_tokens=kv)
+            prompts = [(p % llm.target.cfg.vocab_size).pin_memory() for p in plans[b]]
+            eng = llm.engine
+            res = {}
+            for kind, spec in (("speculative", True), ("plain", False)):
+                for _ in range(max(1, min(args.warmup, 1))):  # graph capture and the served choice's exploration
+                    llm.generate(prompts, args.new_tokens, speculative=spec)
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                out = llm.generate(prompts, args.new_tokens, speculative=spec)
+                torch.cuda.synchronize()
+                e2e = max_over_ranks(time.perf_counter() - t0)
+                dec = max_over_ranks(eng.last_timing["decode_ms"])
+                pre = max_over_ranks(eng.last_timing["prefill_ms"])
+                toks = out.numel()
+                res[kind] = {"decode_tok_s": round(toks / (dec / 1e3), 2), "prefill_ms": round(pre, 1),
+                             "e2e_tok_s": round(toks / e2e, 2)}
+            line.update({"value": res["speculative"]["decode_tok_s"], "unit": "tokens/s (decode rounds)",
+                         "speculative": res["speculative"], "plain": res["plain"],
+                         "speedup_vs_plain": round(res["speculative"]["decode_tok_s"]
+                                                   / res["plain"]["decode_tok_s"], 4),
+                         "verify_batch_limit": eng.verify_batch_limit,
+                         "native_round_share": (round(eng.tree_choice.share(eng.tree_choice.NATIVE), 3)
+                                                if eng.tree_choice is not None else None)})
+            eng.graphs.clear()
+            del llm, eng
+        except torch.cuda.OutOfMemoryError as e:
+            line["skipped"] = f"out of device memory at this batch and TP size ({str(e).splitlines()[0][:120]})"
+        torch.cuda.empty_cache()
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    if tp is not None:
+        torch.cuda.synchronize()
         tp.close()
     if dist is not None:
         dist.destroy_process_group()

@@ -46,7 +46,7 @@ class TreeSpec:
 class LLM:
     def __init__(self, target: TargetModel, draft: Optional[DraftModel], *, tree: TreeSpec = TreeSpec(),
                  max_batch: int = 1, max_len: int = 4096, page: int = 16, config=None, temperature: float = 0.0,
-                 seed: int = 0):
+                 seed: int = 0, kv_tokens: Optional[int] = None):
         """``config``: a ``HarnessConfig``, or the ``--speculative-algorithm-config`` JSON text (inline or a path);
         None is the static tree of ``tree``. ``temperature > 0`` samples (sampled trees with tree rejection)."""
         if isinstance(config, str):
@@ -54,12 +54,12 @@ class LLM:
         self.target, self.draft, self.tree = target, draft, tree
         self.engine = Engine(target, draft, max_reqs=max_batch, max_len=max_len, page=page, steps=tree.steps,
                              top_k=tree.top_k, verify_tokens=tree.draft_tokens, config=config,
-                             temperature=temperature, seed=seed)
+                             temperature=temperature, seed=seed, kv_tokens=kv_tokens)
 
     @classmethod
     def synthetic(cls, name: str, *, device="cuda", dtype=torch.bfloat16, seed: int = 0, tree: TreeSpec = TreeSpec(),
                   max_batch: int = 1, max_len: int = 4096, draft: bool = True, config=None, tp=None,
-                  temperature: float = 0.0, sample_seed: int = 0) -> "LLM":
+                  temperature: float = 0.0, sample_seed: int = 0, kv_tokens: Optional[int] = None) -> "LLM":
         """Random-init weights (N(0, 0.02)) of a named architecture; the draft shares the target's embedding.
         With ``tp`` (a :class:`~eagle4_b200.parallel.tp.TensorParallel`) every rank draws the same full weights and
         keeps its shard."""
@@ -79,10 +79,15 @@ class LLM:
             ldcfg, dw = shard_draft(dcfg, dw, world, rank)
             dm = DraftModel(ldcfg, dw, tp=tp)
         return cls(target, dm, tree=tree, max_batch=max_batch, max_len=max_len, config=config,
-                   temperature=temperature, seed=sample_seed)
+                   temperature=temperature, seed=sample_seed, kv_tokens=kv_tokens)
 
-    def generate(self, prompt_ids: torch.Tensor, max_new_tokens: int, *, speculative: bool = True) -> torch.Tensor:
-        """``prompt_ids [B, P]`` int64 on the host -> generated ids ``[B, max_new_tokens]`` on the host."""
+    def generate(self, prompt_ids, max_new_tokens: int, *, speculative: bool = True) -> torch.Tensor:
+        """``prompt_ids [B, P]`` int64 on the host (or a list of 1-D prompts of different lengths) -> generated ids
+        ``[B, max_new_tokens]`` on the host."""
+        if isinstance(prompt_ids, (list, tuple)):
+            dev_ids = [p.to(self.target.device, non_blocking=True) for p in prompt_ids]
+            out = self.engine.generate(dev_ids, max_new_tokens, speculative=speculative)
+            return torch.tensor(out, dtype=torch.int64)
         dev_ids = prompt_ids.to(self.target.device, non_blocking=True)
         out = self.engine.generate(dev_ids, max_new_tokens, speculative=speculative)
         return torch.tensor(out, dtype=torch.int64)

@@ -210,6 +210,7 @@ class Engine:
         self.pool = torch.cuda.graph_pool_handle() if self.use_graphs else None
         self.graph_launches: Dict[tuple, int] = {}
         self._captured = False  # a graph was captured during the current round
+        self.last_timing: Dict[str, float] = {}
         self.stats = RoundStats()
         self.recorder = None  # a runtime.recorder.RoundRecorder to keep per-round records
         if self.tree is not None:
@@ -577,6 +578,8 @@ class Engine:
             raise ValueError(f"batch {bs} exceeds max_reqs {self.max_reqs}")
         outs: List[List[int]] = [[] for _ in range(bs)]
         ctx = [int(p.shape[0]) for p in prompts]
+        marks = [_Stamp(self.device) for _ in range(3)]  # start, prefill done, rounds done
+        marks[0].record()
         for b, p in enumerate(prompts):
             need = int(p.shape[0]) + max_new_tokens + self.span
             if need > self.max_len:
@@ -585,6 +588,7 @@ class Engine:
             self.prefill(b, p, reserve_tokens=need)
         if self.tree is not None:
             self.lagged_scores = None
+        marks[1].record()
         self.host_tok[:bs].copy_(self.out_tok[:bs])
         for b in range(bs):
             outs[b].append(int(self.host_tok[b, 0]))
@@ -664,4 +668,10 @@ class Engine:
                 if self.target.tp is not None:
                     us = self.target.tp.max_over_ranks([us])[0]
                 self.chain_policy.record(bs, chain_w, us, sum(got) / len(got), settled=not self._captured)
+        marks[2].record()
+        if self.device.type == "cuda":
+            torch.cuda.current_stream().synchronize()
+        # device time of this call's prefill (every prompt) and of its decode rounds
+        self.last_timing = {"prefill_ms": marks[0].elapsed_us(marks[1]) / 1e3,
+                            "decode_ms": marks[1].elapsed_us(marks[2]) / 1e3}
         return [o[:max_new_tokens] for o in outs]
