@@ -280,6 +280,16 @@ __device__ __forceinline__ void tp_gather_tiles(const Params& p, int ep_tid, uns
 __device__ __forceinline__ void store_chunk_vec(const Params& p, int tile, int m, int j0, const float* v,
                                                 float* xchg, int ep_tid) {
   float* st = xchg;  // [16 tokens][128 rows]
+  // this thread's two 8-feature residual pieces are requested before the transpose, so their latency overlaps it
+  uint4 rres[2];
+  if (p.epi == kResidual) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int q = ep_tid + h * 128, j = j0 + (q >> 4), n = tile * kTileM + (q & 15) * 8;
+      rres[h] = (j < p.T && n < p.N) ? *reinterpret_cast<const uint4*>(p.res + size_t(j) * p.ldr + n)
+                                     : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
 #pragma unroll
   for (int i = 0; i < 16; ++i) st[i * kTileM + m] = v[i];
   named_bar(1, 128);
@@ -297,7 +307,9 @@ __device__ __forceinline__ void store_chunk_vec(const Params& p, int tile, int m
       *reinterpret_cast<uint4*>(p.y + size_t(j) * p.ldy + f) = out;
     }
   } else {
-    for (int q = ep_tid; q < 16 * 16; q += 128) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int q = ep_tid + h * 128;
       const int i = q >> 4, piece = q & 15;
       const int j = j0 + i, n = tile * kTileM + piece * 8;
       if (j >= p.T || n >= p.N) continue;
@@ -311,8 +323,7 @@ __device__ __forceinline__ void store_chunk_vec(const Params& p, int tile, int m
         continue;
       }
       if (p.epi == kResidual) {
-        const uint4 ru = *reinterpret_cast<const uint4*>(p.res + size_t(j) * p.ldr + n);
-        const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&ru);
+        const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rres[h]);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 f = __bfloat1622float2(r2[e]);
@@ -332,6 +343,37 @@ __device__ __forceinline__ void store_chunk_vec(const Params& p, int tile, int m
     }
   }
   named_bar(1, 128);
+}
+
+// Partial-tile merge: the 16-token chunk at ``j0`` of weight row ``m`` from pieces 1..count of ``tile`` (the pieces
+// of CTAs first + 1 .. first + count), and their sum into ``v`` in piece order.
+template <int P>
+__device__ __forceinline__ void load_pieces(const Params& p, int first, int count, int tile, int m, int j0,
+                                            float4 (&buf)[P][4]) {
+#pragma unroll
+  for (int qq = 0; qq < P; ++qq) {
+    if (qq < count) {
+      const float4* src = reinterpret_cast<const float4*>(
+          p.ws + size_t(ws_slot(p, first + 1 + qq, tile)) * p.nt * kTileM + size_t(m) * p.nt + j0);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) buf[qq][u] = __ldcg(src + u);
+    }
+  }
+}
+template <int P>
+__device__ __forceinline__ void add_pieces(float* v, int count, const float4 (&buf)[P][4]) {
+#pragma unroll
+  for (int qq = 0; qq < P; ++qq) {
+    if (qq < count) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        v[4 * u] += buf[qq][u].x;
+        v[4 * u + 1] += buf[qq][u].y;
+        v[4 * u + 2] += buf[qq][u].z;
+        v[4 * u + 3] += buf[qq][u].w;
+      }
+    }
+  }
 }
 
 // Final epilogue of 16 token columns [j0, j0+16) held by this thread for weight row ``m`` of ``tile``.
@@ -627,40 +669,40 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
             E4_STAMP(p, 7);
           }
           named_bar(1, 128);
-          for (int j0 = 0; j0 < p.nt; j0 += 16) {
-            float v[16];
-            tmem_ld16(t_addr + j0, v);
-            if (j0 + 16 >= p.nt) { tc_fence_before(); mbar_arrive(&acc_empty[acc]); }
-            // pieces 1.. in order, four at a time: their loads are all issued before the first is summed
-            for (int q0 = 1; q0 < pieces; q0 += 4) {
-              float4 buf[4][4];
-#pragma unroll
-              for (int qq = 0; qq < 4; ++qq) {
-                if (q0 + qq < pieces) {
-                  const float4* src = reinterpret_cast<const float4*>(
-                      p.ws + size_t(ws_slot(p, first_cta + q0 + qq, tile)) * p.nt * kTileM + size_t(m) * p.nt + j0);
-#pragma unroll
-                  for (int u = 0; u < 4; ++u) buf[qq][u] = __ldcg(src + u);
-                }
-              }
-#pragma unroll
-              for (int qq = 0; qq < 4; ++qq) {
-                if (q0 + qq < pieces) {
-#pragma unroll
-                  for (int u = 0; u < 4; ++u) {
-                    v[4 * u] += buf[qq][u].x;
-                    v[4 * u + 1] += buf[qq][u].y;
-                    v[4 * u + 2] += buf[qq][u].z;
-                    v[4 * u + 3] += buf[qq][u].w;
-                  }
-                }
-              }
-            }
+          auto finish = [&](int j0, float* v) {
             if (p.fold) {
 #pragma unroll
               for (int i = 0; i < 16; ++i) v[i] *= rsv[j0 + i];
             }
             store_chunk(p, tile, m, j0, v, xchg, ep_tid, half);
+          };
+          if (pieces - 1 <= 4) {
+            // up to four other pieces: a chunk's pieces are summed as soon as they arrive and the next chunk's loads
+            // are issued before this chunk is stored, so each store overlaps the next chunk's memory round trip
+            const int others = pieces - 1;
+            float4 buf[4][4];
+            load_pieces(p, first_cta, others, tile, m, 0, buf);
+            for (int j0 = 0; j0 < p.nt; j0 += 16) {
+              float v[16];
+              tmem_ld16(t_addr + j0, v);
+              if (j0 + 16 >= p.nt) { tc_fence_before(); mbar_arrive(&acc_empty[acc]); }
+              add_pieces(v, others, buf);
+              if (j0 + 16 < p.nt) load_pieces(p, first_cta, others, tile, m, j0 + 16, buf);
+              finish(j0, v);
+            }
+          } else {
+            for (int j0 = 0; j0 < p.nt; j0 += 16) {
+              float v[16];
+              tmem_ld16(t_addr + j0, v);
+              if (j0 + 16 >= p.nt) { tc_fence_before(); mbar_arrive(&acc_empty[acc]); }
+              // pieces 1.. in order, four at a time: their loads are all issued before the first is summed
+              for (int q0 = 1; q0 < pieces; q0 += 4) {
+                float4 buf[4][4];
+                load_pieces(p, first_cta + q0 - 1, min(4, pieces - q0), tile, m, j0, buf);
+                add_pieces(v, min(4, pieces - q0), buf);
+              }
+              finish(j0, v);
+            }
           }
           if (ep_tid == 0) p.counters[tile] = 0;
           named_bar(1, 128);
