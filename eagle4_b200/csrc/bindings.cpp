@@ -55,7 +55,13 @@ void tree_step(const torch::Tensor& probs, const torch::Tensor& toks, const torc
                int64_t K, int64_t step, int64_t layer_start, int64_t parent_col, torch::Tensor scores,
                torch::Tensor tokens, torch::Tensor parents, torch::Tensor front_scores, torch::Tensor front_tokens,
                torch::Tensor front_hidden, torch::Tensor front_nodes, torch::Tensor ancestors, torch::Tensor best,
-               torch::Tensor best_prev, torch::Tensor layer_top);
+               torch::Tensor best_prev, torch::Tensor layer_top, torch::Tensor delta_rows, torch::Tensor deltas_out,
+               torch::Tensor counter);
+void tree_begin(const torch::Tensor& root_probs, const torch::Tensor& root_tokens, const torch::Tensor& root_hidden,
+                int64_t bs, int64_t K, bool keep_order, double root_score, torch::Tensor scores, torch::Tensor tokens,
+                torch::Tensor front_scores, torch::Tensor front_tokens, torch::Tensor front_hidden,
+                torch::Tensor front_nodes, torch::Tensor best, torch::Tensor best_prev, torch::Tensor layer_top,
+                torch::Tensor delta_rows, torch::Tensor deltas_out, torch::Tensor counter);
 std::vector<torch::Tensor> select_rows(const torch::Tensor& scores, const torch::Tensor& decay,
                                        const torch::Tensor& tokens, const torch::Tensor& parents, int64_t bs,
                                        int64_t n, int64_t K, int64_t count);
@@ -130,5 +136,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("accept_greedy", &e4::accept_greedy);
   m.def("topk_large", &e4::topk_large);
   m.def("tree_step", &e4::tree_step);
+  m.def("tree_begin", &e4::tree_begin);
   m.def("select_rows", &e4::select_rows);
 }

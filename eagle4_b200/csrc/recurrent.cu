@@ -504,94 +504,109 @@ struct MambaArgs {
   int H, P, N, G;
 };
 
-// Thread p owns state row S[p][0..N). Loads B and C of the row's group into shared memory.
-template <int N>
-__device__ __forceinline__ float mamba_step(const MambaArgs& a, float* S, int row, int h, int p, float* sB, float* sC) {
-  const int grp = h / (a.H / a.G);
-  const __nv_bfloat16* base = a.xbc + size_t(row) * a.ldx;
-  __syncthreads();
-  for (int i = threadIdx.x; i < N; i += blockDim.x) {
-    sB[i] = bf(base[a.H * a.P + grp * N + i]);
-    sC[i] = bf(base[a.H * a.P + a.G * N + grp * N + i]);
-  }
-  __syncthreads();
-  const float dt = softplusf_(bf(a.dt[size_t(row) * a.lddt + h]) + a.dt_bias[h]);
-  const float A = -__expf(a.a_log[h]);
-  const float da = __expf(dt * A);
-  const float x = p < a.P ? bf(base[h * a.P + p]) : 0.f;
-  const float dx = dt * x;
-  float y = 0.f;
-#pragma unroll
-  for (int i = 0; i < N; ++i) {
-    S[i] = fmaf(S[i], da, dx * sB[i]);
-    y = fmaf(S[i], sC[i], y);
-  }
-  return fmaf(a.dskip[h], x, y);
-}
+// Mamba2 selective-state update along a walk of rows: state_t = exp(A dt_t) state + dt_t x_t B_t^T, and
+// y_t = C_t . state_t + D x_t. One CTA of 256 threads per (head, walk): thread (p, q) owns quarter q of state row p
+// (N/4 consecutive columns, loaded and stored as 16-byte pieces; a warp covers 8 whole rows), and the walk's x, B,
+// C and gate of each row are staged in shared memory 16 rows at a time, so a step is register arithmetic only.
+// y sums each quarter's columns in order, then the quarters as (q0 + q1) + (q2 + q3); every mode runs this same
+// step, so a row verified in a tree, decoded alone, or committed gives identical state and output.
+// Walks: kMambaTree - the root-to-row path of row blockIdx.y (parents inside the launch), output for that row only;
+// kMambaCommit - the accepted rows of request blockIdx.y, state written back; kMambaScan - the rows of segment
+// blockIdx.y in order (prefill), output for every row, state written back.
+enum : int { kMambaTree = 0, kMambaCommit = 1, kMambaScan = 2 };
+constexpr int kMambaStage = 16;
 
 template <int N>
-__global__ void __launch_bounds__(64) mamba_kernel(MambaArgs a, const int* __restrict__ slot,
-                                                   const int* __restrict__ parent, const int* __restrict__ seg,
-                                                   int scan, __nv_bfloat16* __restrict__ out) {
+__global__ void __launch_bounds__(256) mamba_walk_kernel(MambaArgs a, int mode, const int* __restrict__ slot,
+                                                         const int* __restrict__ parent, const int* __restrict__ seg,
+                                                         const int* __restrict__ rows, int rows_ld,
+                                                         const int* __restrict__ nrows,
+                                                         const int64_t* __restrict__ slots,
+                                                         __nv_bfloat16* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
-  __shared__ float sB[N], sC[N];
+  constexpr int NQ = N / 4;
   __shared__ int path[kMaxPath];
+  __shared__ int win[kMaxPath];
   __shared__ int plen;
-  const int h = blockIdx.x, p = threadIdx.x;
-  float S[N];
-  int r0, r1;
-  if (!scan) {
-    const int r = blockIdx.y;
-    if (threadIdx.x == 0) {
-      int n = 0, cur = r;
-      int tmp[kMaxPath];
-      while (cur >= 0 && n < kMaxPath) { tmp[n++] = cur; cur = parent[cur]; }
+  __shared__ float sx[kMambaStage][64], sB[kMambaStage][N], sC[kMambaStage][N], sda[kMambaStage],
+      sdt[kMambaStage];
+  const int h = blockIdx.x, t = threadIdx.x, p = t >> 2, q = t & 3;
+  const int grp = h / (a.H / a.G);
+  const bool live = p < a.P;
+  int state_slot = 0, first = 0, len = 0;
+  if (mode == kMambaTree) {
+    // the parents of the 64 rows up to this one (a request's rows are contiguous, parents precede children)
+    const int r = blockIdx.y, lo = max(0, r - (kMaxPath - 1));
+    if (t < kMaxPath && lo + t <= r) win[t] = parent[lo + t];
+    __syncthreads();
+    if (t == 0) {
+      int n = 0, cur = r, tmp[kMaxPath];
+      while (cur >= lo && n < kMaxPath) { tmp[n++] = cur; cur = win[cur - lo]; }
       for (int i = 0; i < n; ++i) path[i] = tmp[n - 1 - i];
       plen = n;
     }
     __syncthreads();
-    const float* src = a.state + ((size_t(slot[r]) * a.H + h) * a.P + min(p, a.P - 1)) * N;
-#pragma unroll
-    for (int i = 0; i < N; ++i) S[i] = src[i];
-    float y = 0.f;
-    for (int q = 0; q < plen; ++q) y = mamba_step<N>(a, S, path[q], h, p, sB, sC);
-    if (p < a.P) out[(size_t(r) * a.H + h) * a.P + p] = __float2bfloat16(y);
-    return;
+    len = plen;
+    state_slot = slot[r];
+  } else if (mode == kMambaCommit) {
+    const int b = blockIdx.y;
+    len = min(nrows[b], kMaxPath);
+    if (t < len) path[t] = rows[size_t(b) * rows_ld + t];
+    state_slot = int(slots[b]);
+  } else {
+    first = seg[blockIdx.y];
+    len = seg[blockIdx.y + 1] - first;
+    state_slot = slot[first];
   }
-  r0 = seg[blockIdx.y];
-  r1 = seg[blockIdx.y + 1];
-  float* st = a.state + ((size_t(slot[r0]) * a.H + h) * a.P + min(p, a.P - 1)) * N;
+  if (len <= 0) return;
+  float* st = a.state + ((size_t(state_slot) * a.H + h) * a.P + (live ? p : 0)) * N + q * NQ;
+  float S[NQ];
 #pragma unroll
-  for (int i = 0; i < N; ++i) S[i] = st[i];
-  for (int j = r0; j < r1; ++j) {
-    const float y = mamba_step<N>(a, S, j, h, p, sB, sC);
-    if (p < a.P) out[(size_t(j) * a.H + h) * a.P + p] = __float2bfloat16(y);
+  for (int i = 0; i < NQ; i += 4) {
+    const float4 v = *reinterpret_cast<const float4*>(st + i);
+    S[i] = v.x; S[i + 1] = v.y; S[i + 2] = v.z; S[i + 3] = v.w;
   }
-  if (p < a.P) {
+  const float A = -__expf(a.a_log[h]);
+  const float dskip = a.dskip[h];
+  for (int c0 = 0; c0 < len; c0 += kMambaStage) {
+    const int cn = min(kMambaStage, len - c0);
+    __syncthreads();
+    for (int i = t; i < cn * (64 + 2 * N); i += blockDim.x) {
+      const int k = i / (64 + 2 * N), e = i % (64 + 2 * N);
+      const int row = mode == kMambaScan ? first + c0 + k : path[c0 + k];
+      const __nv_bfloat16* base = a.xbc + size_t(row) * a.ldx;
+      if (e < 64) sx[k][e] = e < a.P ? bf(base[h * a.P + e]) : 0.f;
+      else if (e < 64 + N) sB[k][e - 64] = bf(base[a.H * a.P + grp * N + (e - 64)]);
+      else sC[k][e - 64 - N] = bf(base[a.H * a.P + a.G * N + grp * N + (e - 64 - N)]);
+    }
+    if (t < cn) {
+      const int row = mode == kMambaScan ? first + c0 + t : path[c0 + t];
+      const float dt = softplusf_(bf(a.dt[size_t(row) * a.lddt + h]) + a.dt_bias[h]);
+      sdt[t] = dt;
+      sda[t] = __expf(dt * A);
+    }
+    __syncthreads();
+    for (int k = 0; k < cn; ++k) {
+      const float x = sx[k][live ? p : 0];
+      const float da = sda[k], dx = sdt[k] * x;
 #pragma unroll
-    for (int i = 0; i < N; ++i) st[i] = S[i];
+      for (int i = 0; i < NQ; ++i) S[i] = fmaf(S[i], da, dx * sB[k][q * NQ + i]);
+      const bool emit = mode == kMambaScan || (mode == kMambaTree && c0 + k == len - 1);
+      if (emit) {
+        float y = 0.f;
+#pragma unroll
+        for (int i = 0; i < NQ; ++i) y = fmaf(S[i], sC[k][q * NQ + i], y);
+        y += __shfl_xor_sync(0xffffffffu, y, 1);
+        y += __shfl_xor_sync(0xffffffffu, y, 2);
+        const int row = mode == kMambaScan ? first + c0 + k : path[c0 + k];
+        if (live && q == 0) out[(size_t(row) * a.H + h) * a.P + p] = __float2bfloat16(fmaf(dskip, x, y));
+      }
+    }
   }
-}
-
-template <int N>
-__global__ void __launch_bounds__(64) mamba_commit_kernel(MambaArgs a, const int* __restrict__ slots,
-                                                          const int* __restrict__ rows, int rows_ld,
-                                                          const int* __restrict__ nrows) {
-  pdl_wait();
-  pdl_trigger();
-  __shared__ float sB[N], sC[N];
-  const int h = blockIdx.x, b = blockIdx.y, p = threadIdx.x;
-  const int n = nrows[b];
-  if (n <= 0) return;
-  float* st = a.state + ((size_t(slots[b]) * a.H + h) * a.P + min(p, a.P - 1)) * N;
-  float S[N];
+  if (mode != kMambaTree && live) {
 #pragma unroll
-  for (int i = 0; i < N; ++i) S[i] = st[i];
-  for (int q = 0; q < n; ++q) mamba_step<N>(a, S, rows[size_t(b) * rows_ld + q], h, p, sB, sC);
-  if (p < a.P) {
-#pragma unroll
-    for (int i = 0; i < N; ++i) st[i] = S[i];
+    for (int i = 0; i < NQ; i += 4) *reinterpret_cast<float4*>(st + i) = make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
   }
 }
 
@@ -775,11 +790,11 @@ static MambaArgs mamba_args(const torch::Tensor& xbc, const torch::Tensor& dt, c
                    int(N), int(G)};
 }
 
-#define E4_MAMBA_DISPATCH(N_, KERNEL, ...)                         \
-  switch (N_) {                                                      \
-    case 128: C10_CUDA_CHECK(launch_pdl(KERNEL<128>, grid, 64, 0, st.stream(), __VA_ARGS__)); break;  \
-    case 64: C10_CUDA_CHECK(launch_pdl(KERNEL<64>, grid, 64, 0, st.stream(), __VA_ARGS__)); break;    \
-    default: C10_CUDA_CHECK(launch_pdl(KERNEL<16>, grid, 64, 0, st.stream(), __VA_ARGS__)); break;    \
+#define E4_MAMBA_DISPATCH(N_, ...)                                                                      \
+  switch (N_) {                                                                                         \
+    case 128: C10_CUDA_CHECK(launch_pdl(mamba_walk_kernel<128>, grid, 256, 0, st.stream(), __VA_ARGS__)); break; \
+    case 64: C10_CUDA_CHECK(launch_pdl(mamba_walk_kernel<64>, grid, 256, 0, st.stream(), __VA_ARGS__)); break;   \
+    default: C10_CUDA_CHECK(launch_pdl(mamba_walk_kernel<16>, grid, 256, 0, st.stream(), __VA_ARGS__)); break;   \
   }
 
 torch::Tensor mamba_tree(const torch::Tensor& xbc, const torch::Tensor& dt, const torch::Tensor& a_log,
@@ -796,7 +811,8 @@ torch::Tensor mamba_tree(const torch::Tensor& xbc, const torch::Tensor& dt, cons
   dim3 grid(H, scan ? seg.numel() - 1 : T);
   auto st = at::cuda::getCurrentCUDAStream();
   const int* segp = scan ? seg.data_ptr<int>() : nullptr;
-  E4_MAMBA_DISPATCH(N, mamba_kernel, a, sl.data_ptr<int>(), pa.data_ptr<int>(), segp, scan, BFP(out))
+  E4_MAMBA_DISPATCH(N, a, scan ? int(kMambaScan) : int(kMambaTree), sl.data_ptr<int>(), pa.data_ptr<int>(), segp,
+                    nullptr, 0, nullptr, nullptr, BFP(out))
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
 }
@@ -808,13 +824,14 @@ void mamba_commit(const torch::Tensor& xbc, const torch::Tensor& dt, const torch
   const at::cuda::CUDAGuard gd(xbc.device());
   const int B = rows.size(0);
   if (!B) return;
+  TORCH_CHECK(rows.size(1) <= kMaxPath, "mamba_commit: at most 64 accepted rows per request");
   MambaArgs a = mamba_args(xbc, dt, a_log, dt_bias, dskip, state, H, P, N, G);
-  auto sl = slots.to(torch::kInt32).contiguous(), rw = rows.to(torch::kInt32).contiguous(),
+  auto sl = slots.to(torch::kInt64).contiguous(), rw = rows.to(torch::kInt32).contiguous(),
        nr = nrows.to(torch::kInt32).contiguous();
   dim3 grid(H, B);
   auto st = at::cuda::getCurrentCUDAStream();
-  E4_MAMBA_DISPATCH(N, mamba_commit_kernel, a, sl.data_ptr<int>(), rw.data_ptr<int>(), int(rw.size(1)),
-                    nr.data_ptr<int>())
+  E4_MAMBA_DISPATCH(N, a, int(kMambaCommit), nullptr, nullptr, nullptr, rw.data_ptr<int>(), int(rw.size(1)),
+                    nr.data_ptr<int>(), sl.data_ptr<int64_t>(), nullptr)
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -375,6 +375,91 @@ __global__ void __launch_bounds__(kSelThreads) topk_merge_kernel(const float* __
   }
 }
 
+// Work deltas of request b (DraftTree definition): for j = 0..K, the running sums of the first ``max_verify`` values of
+// merge(old best set, the layer's top j) (both descending), written to ``rows[b][v][j]``; the last CTA of the launch
+// to finish stores the batch mean (requests summed in order) into ``out[v][j]`` and resets the arrival counter.
+// ``old_best`` / ``top`` are this CTA's shared-memory copies. Threads 0..K each merge one j.
+__device__ __forceinline__ void store_work_deltas(int b, int bs, int K, int work_cap, int max_verify,
+                                                  const float* old_best, const float* top, float* rows, float* out,
+                                                  unsigned* counter) {
+  const int t = threadIdx.x;
+  __syncthreads();
+  if (t <= K) {
+    float sum = 0.f;
+    int a = 0, c = 0;
+    for (int v = 0; v < max_verify; ++v) {
+      float x;
+      if (c < t && (a >= work_cap || top[c] > old_best[a])) x = top[c++];
+      else x = a < work_cap ? old_best[a++] : 0.f;
+      sum += x;
+      rows[(size_t(b) * max_verify + v) * (K + 1) + t] = sum;
+    }
+  }
+  __shared__ int last;
+  __threadfence();
+  __syncthreads();
+  if (t == 0) last = atomicAdd(counter, 1u) == unsigned(bs - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const int n = max_verify * (K + 1);
+  for (int i = t; i < n; i += blockDim.x) {
+    float s = 0.f;
+    for (int r = 0; r < bs; ++r) s += __ldcg(rows + size_t(r) * n + i);
+    out[i] = s / float(bs);
+  }
+  if (t == 0) *counter = 0u;
+}
+
+// The tree's first level for request b (DraftTree.begin semantics): the root's K children (sorted by probability,
+// ties to the lower child, unless the draw order is kept), the frontier (tokens, scores, nodes, the root's hidden
+// row for every lane), the best set {root, children} and, when asked, the depth-0 work deltas.
+__global__ void tree_begin_kernel(const float* __restrict__ root_probs, const int64_t* __restrict__ root_tokens,
+                                  const __nv_bfloat16* __restrict__ root_hidden, int H, int K, int keep_order,
+                                  float root_score, int work_cap, int cap, float* scores, int64_t* tokens,
+                                  float* front_scores, int64_t* front_tokens, __nv_bfloat16* front_hidden,
+                                  int64_t* front_nodes, float* best, float* best_prev, float* layer_top,
+                                  int max_verify, float* delta_rows, float* deltas_out, unsigned* counter) {
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x, t = threadIdx.x;
+  __shared__ float pr[8], ranked[8], old_best[64];
+  __shared__ int64_t tk[8];
+  if (t < K) {
+    const float v = root_probs[b * K + t];
+    int rank = 0;  // descending, ties to the lower child
+    for (int i = 0; i < K; ++i) {
+      const float o = root_probs[b * K + i];
+      rank += (o > v) || (o == v && i < t);
+    }
+    const int at = keep_order ? t : rank;
+    pr[at] = v;
+    tk[at] = root_tokens[b * K + t];
+    ranked[rank] = v;
+  }
+  for (int i = t; i < work_cap; i += blockDim.x) old_best[i] = i == 0 ? root_score : 0.f;
+  __syncthreads();
+  if (t < K) {
+    scores[size_t(b) * cap + t] = pr[t];
+    tokens[size_t(b) * cap + t] = tk[t];
+    front_scores[b * K + t] = pr[t];
+    front_tokens[b * K + t] = tk[t];
+    front_nodes[b * K + t] = t;
+    layer_top[b * K + t] = ranked[t];
+  }
+  for (int i = t; i < work_cap; i += blockDim.x) {
+    best_prev[size_t(b) * work_cap + i] = old_best[i];
+    best[size_t(b) * work_cap + i] = i == 0 ? root_score : (i <= K ? ranked[i - 1] : 0.f);
+  }
+  const int vec = H / 8;
+  for (int i = t; i < K * vec; i += blockDim.x) {
+    reinterpret_cast<uint4*>(front_hidden + size_t(b * K + i / vec) * H)[i % vec] =
+        reinterpret_cast<const uint4*>(root_hidden + size_t(b) * H)[i % vec];
+  }
+  if (deltas_out != nullptr)
+    store_work_deltas(b, gridDim.x, K, work_cap, max_verify, old_best, ranked, delta_rows, deltas_out, counter);
+}
+
 // One draft-tree step for request b (one CTA): children scores, frontier top-K (ties to the lower child), tokens,
 // parents, frontier hidden rows and ancestor slots gathered by the picked lanes, and the best-score set merged with
 // the new layer. (DraftTree.step semantics.)
@@ -383,7 +468,8 @@ __global__ void tree_step_kernel(const float* __restrict__ probs, const int64_t*
                                  int parent_col, int work_cap, int cap, int pcap, int depth_cap, float* scores,
                                  int64_t* tokens, int64_t* parents, float* front_scores, int64_t* front_tokens,
                                  __nv_bfloat16* front_hidden, int64_t* front_nodes, int* ancestors, float* best,
-                                 float* best_prev, float* layer_top) {
+                                 float* best_prev, float* layer_top, int max_verify, float* delta_rows,
+                                 float* deltas_out, unsigned* counter) {
   pdl_wait();
   pdl_trigger();
   const int b = blockIdx.x;
@@ -441,6 +527,9 @@ __global__ void tree_step_kernel(const float* __restrict__ probs, const int64_t*
     for (int j = 0; j < m; ++j) rank += (merged[j] > v) || (merged[j] == v && j < i);
     if (rank < work_cap) best[size_t(b) * work_cap + rank] = v;
   }
+  // the step's work deltas: the old best set (merged[0, work_cap)) with the new layer's top
+  if (deltas_out != nullptr)
+    store_work_deltas(b, gridDim.x, K, work_cap, max_verify, merged, top, delta_rows, deltas_out, counter);
 }
 
 // The best ``count`` nodes of each request's tree as verify rows (DraftTree.verify_rows semantics): rank by
@@ -464,10 +553,27 @@ __global__ void select_rows_kernel(const float* __restrict__ scores, const float
     sel_pos[i] = rank < count ? 1 : 0;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int r = 0;
-    for (int i = 0; i < n; ++i) {
-      if (sel_pos[i]) { row_node[r] = i; sel_pos[i] = r + 1; ++r; } else sel_pos[i] = 0;
+  // compaction in node order: thread t owns the nodes [t*per, (t+1)*per); an exclusive scan of the per-thread
+  // counts (warp shuffles, then the four warp totals) gives each selected node its row
+  {
+    __shared__ int warp_sum[4];
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int per = (n + blockDim.x - 1) / blockDim.x;
+    const int i0 = t * per, i1 = min(n, i0 + per);
+    int cnt = 0;
+    for (int i = i0; i < i1; ++i) cnt += sel_pos[i];
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) warp_sum[warp] = incl;
+    __syncthreads();
+    int r = incl - cnt;
+    for (int w = 0; w < warp; ++w) r += warp_sum[w];
+    for (int i = i0; i < i1; ++i) {
+      if (sel_pos[i]) { row_node[r] = i; sel_pos[i] = r + 1; ++r; }
     }
   }
   __syncthreads();
@@ -605,7 +711,8 @@ void tree_step(const torch::Tensor& probs, const torch::Tensor& toks, const torc
                int64_t K, int64_t step, int64_t layer_start, int64_t parent_col, torch::Tensor scores,
                torch::Tensor tokens, torch::Tensor parents, torch::Tensor front_scores, torch::Tensor front_tokens,
                torch::Tensor front_hidden, torch::Tensor front_nodes, torch::Tensor ancestors, torch::Tensor best,
-               torch::Tensor best_prev, torch::Tensor layer_top) {
+               torch::Tensor best_prev, torch::Tensor layer_top, torch::Tensor delta_rows, torch::Tensor deltas_out,
+               torch::Tensor counter) {
   const at::cuda::CUDAGuard g(probs.device());
   TORCH_CHECK(K <= 8 && best.size(1) <= 64 && ancestors.size(2) <= 32);
   auto p = probs.to(torch::kFloat32).contiguous();
@@ -619,7 +726,34 @@ void tree_step(const torch::Tensor& probs, const torch::Tensor& toks, const torc
       scores.data_ptr<float>(), tokens.data_ptr<int64_t>(), parents.data_ptr<int64_t>(),
       front_scores.data_ptr<float>(), front_tokens.data_ptr<int64_t>(),
       reinterpret_cast<__nv_bfloat16*>(front_hidden.data_ptr()), front_nodes.data_ptr<int64_t>(),
-      ancestors.data_ptr<int>(), best.data_ptr<float>(), best_prev.data_ptr<float>(), layer_top.data_ptr<float>()));
+      ancestors.data_ptr<int>(), best.data_ptr<float>(), best_prev.data_ptr<float>(), layer_top.data_ptr<float>(),
+      deltas_out.defined() ? int(deltas_out.size(0)) : 0, deltas_out.defined() ? delta_rows.data_ptr<float>() : nullptr,
+      deltas_out.defined() ? deltas_out.data_ptr<float>() : nullptr,
+      deltas_out.defined() ? reinterpret_cast<unsigned*>(counter.data_ptr<int>()) : nullptr));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void tree_begin(const torch::Tensor& root_probs, const torch::Tensor& root_tokens, const torch::Tensor& root_hidden,
+                int64_t bs, int64_t K, bool keep_order, double root_score, torch::Tensor scores, torch::Tensor tokens,
+                torch::Tensor front_scores, torch::Tensor front_tokens, torch::Tensor front_hidden,
+                torch::Tensor front_nodes, torch::Tensor best, torch::Tensor best_prev, torch::Tensor layer_top,
+                torch::Tensor delta_rows, torch::Tensor deltas_out, torch::Tensor counter) {
+  const at::cuda::CUDAGuard g(root_probs.device());
+  TORCH_CHECK(K <= 8 && best.size(1) <= 64 && root_probs.is_contiguous() && root_tokens.is_contiguous() &&
+              root_hidden.is_contiguous() && root_probs.scalar_type() == torch::kFloat32 &&
+              root_tokens.scalar_type() == torch::kInt64);
+  const int H = root_hidden.size(1);
+  TORCH_CHECK(H % 8 == 0);
+  C10_CUDA_CHECK(launch_pdl(tree_begin_kernel, bs, 128, 0, at::cuda::getCurrentCUDAStream().stream(),
+      root_probs.data_ptr<float>(), root_tokens.data_ptr<int64_t>(),
+      reinterpret_cast<const __nv_bfloat16*>(root_hidden.data_ptr()), H, int(K), int(keep_order), float(root_score),
+      int(best.size(1)), int(scores.size(1)), scores.data_ptr<float>(), tokens.data_ptr<int64_t>(),
+      front_scores.data_ptr<float>(), front_tokens.data_ptr<int64_t>(),
+      reinterpret_cast<__nv_bfloat16*>(front_hidden.data_ptr()), front_nodes.data_ptr<int64_t>(),
+      best.data_ptr<float>(), best_prev.data_ptr<float>(), layer_top.data_ptr<float>(),
+      deltas_out.defined() ? int(deltas_out.size(0)) : 0, deltas_out.defined() ? delta_rows.data_ptr<float>() : nullptr,
+      deltas_out.defined() ? deltas_out.data_ptr<float>() : nullptr,
+      deltas_out.defined() ? reinterpret_cast<unsigned*>(counter.data_ptr<int>()) : nullptr));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
