@@ -148,46 +148,12 @@ __device__ __forceinline__ void gdn_stage(const GdnArgs& a, const int* rows, int
   __syncthreads();
 }
 
-// One gated-delta-rule step on this thread's state column S[0..K) with staged node j; returns the output o[v].
-// The two K-long reductions use four interleaved partial sums combined as (p0 + p1) + (p2 + p3).
-template <int K>
-__device__ __forceinline__ float gdn_step(float* S, const GdnStage<K>& st, int j, int v) {
-  const float decay = __expf(st.g[j]);
-  float k0 = 0.f, k1 = 0.f, k2 = 0.f, k3 = 0.f;
-#pragma unroll
-  for (int i = 0; i < K; i += 4) {
-    S[i] *= decay;
-    S[i + 1] *= decay;
-    S[i + 2] *= decay;
-    S[i + 3] *= decay;
-    k0 = fmaf(S[i], st.k[j][i], k0);
-    k1 = fmaf(S[i + 1], st.k[j][i + 1], k1);
-    k2 = fmaf(S[i + 2], st.k[j][i + 2], k2);
-    k3 = fmaf(S[i + 3], st.k[j][i + 3], k3);
-  }
-  const float kvm = (k0 + k1) + (k2 + k3);
-  const float delta = (st.v[j][v] - kvm) * st.beta[j];
-  float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-#pragma unroll
-  for (int i = 0; i < K; i += 4) {
-    S[i] = fmaf(st.k[j][i], delta, S[i]);
-    S[i + 1] = fmaf(st.k[j][i + 1], delta, S[i + 1]);
-    S[i + 2] = fmaf(st.k[j][i + 2], delta, S[i + 2]);
-    S[i + 3] = fmaf(st.k[j][i + 3], delta, S[i + 3]);
-    o0 = fmaf(S[i], st.q[j][i], o0);
-    o1 = fmaf(S[i + 1], st.q[j][i + 1], o1);
-    o2 = fmaf(S[i + 2], st.q[j][i + 2], o2);
-    o3 = fmaf(S[i + 3], st.q[j][i + 3], o3);
-  }
-  return (o0 + o1) + (o2 + o3);
-}
-
 // The output epilogue: o rounded to bf16, RMS-normalised over the head's V values, times w, times silu(z); with no
 // norm weight, o itself.
 __device__ __forceinline__ void gdn_store(const GdnArgs& a, int row, int h, int v, float o, const __nv_bfloat16* nw,
-                                          float eps, float* red, __nv_bfloat16* out) {
+                                          float eps, float* red, __nv_bfloat16* out, bool writer = true) {
   const float ob = __bfloat162float(__float2bfloat16(o));
-  const float x2 = v < a.V ? ob * ob : 0.f;
+  const float x2 = (writer && v < a.V) ? ob * ob : 0.f;
   float s = warp_sum(x2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwp = blockDim.x >> 5;
   __syncthreads();
@@ -196,7 +162,7 @@ __device__ __forceinline__ void gdn_store(const GdnArgs& a, int row, int h, int 
   float tot = 0.f;
   for (int i = 0; i < nwp; ++i) tot += red[i];
   const float rs = rsqrtf(tot / a.V + eps);
-  if (v < a.V) {
+  if (writer && v < a.V) {
     if (nw == nullptr) {  // raw recurrence output (a caller that applies its own norm)
       out[(size_t(row) * a.HV + h) * a.V + v] = __float2bfloat16(ob);
       return;
@@ -218,65 +184,6 @@ template <int K>
 __device__ __forceinline__ void save_state(const float* S, float* dst) {
 #pragma unroll
   for (int i = 0; i < K; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
-}
-
-// One CTA per (value head, row) in tree mode (the row replays its path, no state write) or per (value head,
-// request segment) in scan mode (rows in order, state updated in place); thread v owns state column v. The output
-// is the gated-RMS-normalised head output [T, HV*V]. Path nodes are staged kGdnTile at a time.
-template <int K>
-__global__ void __launch_bounds__(128) gdn_kernel(GdnArgs a, const int* __restrict__ slot,
-                                                  const int* __restrict__ parent, const int* __restrict__ seg,
-                                                  int scan, const __nv_bfloat16* __restrict__ nw, float eps,
-                                                  __nv_bfloat16* __restrict__ out) {
-  pdl_wait();
-  pdl_trigger();
-  extern __shared__ __align__(16) uint8_t gdn_smem[];
-  GdnStage<K>& st = *reinterpret_cast<GdnStage<K>*>(gdn_smem);
-  __shared__ float red[16];
-  __shared__ int path[kMaxPath];
-  __shared__ int plen;
-  const int h = blockIdx.x;
-  const int v = threadIdx.x;
-  const int kh = h / (a.HV / a.HK);
-  const int vc = min(v, a.V - 1);
-  float S[K];
-  if (!scan) {
-    // later rows have the longer paths in a tree's node order: start them first
-    const int r = gridDim.y - 1 - blockIdx.y;
-    if (threadIdx.x == 0) {
-      int n = 0, cur = r;
-      int tmp[kMaxPath];
-      while (cur >= 0 && n < kMaxPath) { tmp[n++] = cur; cur = parent[cur]; }
-      for (int i = 0; i < n; ++i) path[i] = tmp[n - 1 - i];
-      plen = n;
-    }
-    __syncthreads();
-    load_state<K>(S, a.state + ((size_t(slot[r]) * a.HV + h) * a.V + vc) * K);
-    float o = 0.f;
-    for (int p0 = 0; p0 < plen; p0 += kGdnTile) {
-      const int n = min(kGdnTile, plen - p0);
-      if (p0) __syncthreads();
-      gdn_stage<K>(a, path + p0, n, h, kh, st);
-      for (int j = 0; j < n; ++j) o = gdn_step<K>(S, st, j, vc);
-    }
-    gdn_store(a, r, h, v, o, nw, eps, red, out);
-    return;
-  }
-  const int r0 = seg[blockIdx.y], r1 = seg[blockIdx.y + 1];
-  float* stp = a.state + ((size_t(slot[r0]) * a.HV + h) * a.V + vc) * K;
-  load_state<K>(S, stp);
-  for (int p0 = r0; p0 < r1; p0 += kGdnTile) {
-    const int n = min(kGdnTile, r1 - p0);
-    __syncthreads();
-    if (threadIdx.x < n) path[threadIdx.x] = p0 + threadIdx.x;
-    __syncthreads();
-    gdn_stage<K>(a, path, n, h, kh, st);
-    for (int j = 0; j < n; ++j) {
-      const float o = gdn_step<K>(S, st, j, vc);
-      gdn_store(a, p0 + j, h, v, o, nw, eps, red, out);
-    }
-  }
-  if (v < a.V) save_state<K>(S, stp);
 }
 
 // Scan mode (prefill chains) with the value dimension split over CTAs: the delta rule's value rows are independent
@@ -303,6 +210,102 @@ __device__ __forceinline__ float column_sum(float x) {
 #pragma unroll
   for (int o = 1; o < kScanLanes; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
   return x;
+}
+
+// Tree mode: one CTA of 4 V threads per (value head, row); the row replays its root-to-row path from the committed
+// state without writing it. Value column v has kScanLanes lanes, lane r holding K/4 state elements in groups of four
+// at 16m + 4r + e (a column's lanes load one contiguous 64-byte run per group; a staged k / q row is read as
+// conflict-free 16-byte pieces), so a node step is K/4 multiply-adds per lane and two xor-shuffle reductions. The
+// commit kernel runs this same step, so a row decoded alone, verified in a tree, or committed gives the same state.
+template <int K>
+__device__ __forceinline__ float gdn_step4(float* S, const GdnStage<K>& st, int j, int v, int r) {
+  constexpr int NG = K / 16;
+  const float decay = __expf(st.g[j]);
+  float kp = 0.f;
+#pragma unroll
+  for (int m = 0; m < NG; ++m) {
+    const float4 kk = *reinterpret_cast<const float4*>(&st.k[j][16 * m + 4 * r]);
+    S[4 * m] *= decay;
+    S[4 * m + 1] *= decay;
+    S[4 * m + 2] *= decay;
+    S[4 * m + 3] *= decay;
+    kp = fmaf(S[4 * m], kk.x, kp);
+    kp = fmaf(S[4 * m + 1], kk.y, kp);
+    kp = fmaf(S[4 * m + 2], kk.z, kp);
+    kp = fmaf(S[4 * m + 3], kk.w, kp);
+  }
+  const float delta = (st.v[j][v] - column_sum(kp)) * st.beta[j];
+  float op = 0.f;
+#pragma unroll
+  for (int m = 0; m < NG; ++m) {
+    const float4 kk = *reinterpret_cast<const float4*>(&st.k[j][16 * m + 4 * r]);
+    const float4 qq = *reinterpret_cast<const float4*>(&st.q[j][16 * m + 4 * r]);
+    S[4 * m] = fmaf(kk.x, delta, S[4 * m]);
+    S[4 * m + 1] = fmaf(kk.y, delta, S[4 * m + 1]);
+    S[4 * m + 2] = fmaf(kk.z, delta, S[4 * m + 2]);
+    S[4 * m + 3] = fmaf(kk.w, delta, S[4 * m + 3]);
+    op = fmaf(S[4 * m], qq.x, op);
+    op = fmaf(S[4 * m + 1], qq.y, op);
+    op = fmaf(S[4 * m + 2], qq.z, op);
+    op = fmaf(S[4 * m + 3], qq.w, op);
+  }
+  return column_sum(op);
+}
+
+template <int K>
+__device__ __forceinline__ void load_state4(float* S, const float* row, int r) {
+#pragma unroll
+  for (int m = 0; m < K / 16; ++m) {
+    const float4 t4 = *reinterpret_cast<const float4*>(row + 16 * m + 4 * r);
+    S[4 * m] = t4.x; S[4 * m + 1] = t4.y; S[4 * m + 2] = t4.z; S[4 * m + 3] = t4.w;
+  }
+}
+template <int K>
+__device__ __forceinline__ void save_state4(const float* S, float* row, int r) {
+#pragma unroll
+  for (int m = 0; m < K / 16; ++m)
+    *reinterpret_cast<float4*>(row + 16 * m + 4 * r) = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
+}
+
+template <int K>
+__global__ void __launch_bounds__(512) gdn_kernel(GdnArgs a, const int* __restrict__ slot,
+                                                  const int* __restrict__ parent, const __nv_bfloat16* __restrict__ nw,
+                                                  float eps, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ __align__(16) uint8_t gdn_smem[];
+  GdnStage<K>& st = *reinterpret_cast<GdnStage<K>*>(gdn_smem);
+  __shared__ float red[16];
+  __shared__ int path[kMaxPath];
+  __shared__ int win[kMaxPath];
+  __shared__ int plen;
+  const int h = blockIdx.x;
+  const int v = threadIdx.x / kScanLanes, r = threadIdx.x % kScanLanes;
+  const int kh = h / (a.HV / a.HK);
+  const int vc = min(v, a.V - 1);
+  // later rows have the longer paths in a tree's node order: start them first
+  const int row = gridDim.y - 1 - blockIdx.y;
+  // the parents of the 64 rows up to this one (a request's rows are contiguous, parents precede children)
+  const int lo = max(0, row - (kMaxPath - 1));
+  if (threadIdx.x < kMaxPath && lo + int(threadIdx.x) <= row) win[threadIdx.x] = parent[lo + threadIdx.x];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int n = 0, cur = row, tmp[kMaxPath];
+    while (cur >= lo && n < kMaxPath) { tmp[n++] = cur; cur = win[cur - lo]; }
+    for (int i = 0; i < n; ++i) path[i] = tmp[n - 1 - i];
+    plen = n;
+  }
+  float S[K / 4];
+  load_state4<K>(S, a.state + ((size_t(slot[row]) * a.HV + h) * a.V + vc) * K, r);
+  __syncthreads();
+  float o = 0.f;
+  for (int p0 = 0; p0 < plen; p0 += kGdnTile) {
+    const int n = min(kGdnTile, plen - p0);
+    if (p0) __syncthreads();
+    gdn_stage<K>(a, path + p0, n, h, kh, st);
+    for (int j = 0; j < n; ++j) o = gdn_step4<K>(S, st, j, vc, r);
+  }
+  gdn_store(a, row, h, v, o, nw, eps, red, out, r == 0);
 }
 
 template <int K>
@@ -439,14 +442,15 @@ struct GdnLayerTable {
 
 // Commit of every GDN layer in one launch: CTA (value head, request, layer) replays rows[b, :n[b]] in place.
 template <int K>
-__global__ void __launch_bounds__(128) gdn_commit_kernel(GdnArgs a, const __grid_constant__ GdnLayerTable layers,
+__global__ void __launch_bounds__(512) gdn_commit_kernel(GdnArgs a, const __grid_constant__ GdnLayerTable layers,
                                                          const int* __restrict__ slots, const int* __restrict__ rows,
                                                          int rows_ld, const int* __restrict__ nrows) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ __align__(16) uint8_t gdn_smem[];
   GdnStage<K>& st = *reinterpret_cast<GdnStage<K>*>(gdn_smem);
-  const int h = blockIdx.x, b = blockIdx.y, l = blockIdx.z, v = threadIdx.x;
+  const int h = blockIdx.x, b = blockIdx.y, l = blockIdx.z;
+  const int v = threadIdx.x / kScanLanes, r = threadIdx.x % kScanLanes;
   const int n = nrows[b];
   if (n <= 0) return;
   const GdnLayer L = layers.l[l];
@@ -458,15 +462,15 @@ __global__ void __launch_bounds__(128) gdn_commit_kernel(GdnArgs a, const __grid
   const int kh = h / (a.HV / a.HK);
   const int vc = min(v, a.V - 1);
   float* stp = a.state + ((size_t(slots[b]) * a.HV + h) * a.V + vc) * K;
-  float S[K];
-  load_state<K>(S, stp);
+  float S[K / 4];
+  load_state4<K>(S, stp, r);
   for (int p0 = 0; p0 < n; p0 += kGdnTile) {
     const int m = min(kGdnTile, n - p0);
     if (p0) __syncthreads();
     gdn_stage<K>(a, rows + size_t(b) * rows_ld + p0, m, h, kh, st);
-    for (int j = 0; j < m; ++j) gdn_step<K>(S, st, j, vc);
+    for (int j = 0; j < m; ++j) gdn_step4<K>(S, st, j, vc, r);
   }
-  if (v < a.V) save_state<K>(S, stp);
+  if (v < a.V) save_state4<K>(S, stp, r);
 }
 
 // Conv window update of every layer: append rows[b, :n[b]] of the layer's conv inputs (proj columns [0, C)).
@@ -721,19 +725,20 @@ torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int6
     if (!norm_w.numel()) return out;
     return gated_rmsnorm(raw.view({T, HV, V}), proj.narrow(1, z_off, HV * V), norm_w, eps);
   }
-  const int ny = T;  // tree mode reads no segment table
-  dim3 grid(HV, ny);
+  TORCH_CHECK(V <= 128, "gdn tree: at most 128 value columns per head");
+  dim3 grid(HV, T);
+  const int threads = kScanLanes * int(V);
   auto st = at::cuda::getCurrentCUDAStream();
   if (K == 128) {
     gdn_smem_attr(gdn_kernel<128>, sizeof(GdnStage<128>));
-    C10_CUDA_CHECK(launch_pdl(gdn_kernel<128>, grid, 128, sizeof(GdnStage<128>), st.stream(), a, sl.data_ptr<int>(), pa.data_ptr<int>(),
-                                                              static_cast<const int*>(nullptr), scan, norm_w.numel() ? CBF(norm_w) : nullptr, float(eps),
-                                                              BFP(out)));
+    C10_CUDA_CHECK(launch_pdl(gdn_kernel<128>, grid, threads, sizeof(GdnStage<128>), st.stream(), a,
+                              sl.data_ptr<int>(), pa.data_ptr<int>(), norm_w.numel() ? CBF(norm_w) : nullptr,
+                              float(eps), BFP(out)));
   } else {
     gdn_smem_attr(gdn_kernel<64>, sizeof(GdnStage<64>));
-    C10_CUDA_CHECK(launch_pdl(gdn_kernel<64>, grid, 128, sizeof(GdnStage<64>), st.stream(), a, sl.data_ptr<int>(), pa.data_ptr<int>(),
-                                                            static_cast<const int*>(nullptr), scan, norm_w.numel() ? CBF(norm_w) : nullptr, float(eps),
-                                                            BFP(out)));
+    C10_CUDA_CHECK(launch_pdl(gdn_kernel<64>, grid, threads, sizeof(GdnStage<64>), st.stream(), a,
+                              sl.data_ptr<int>(), pa.data_ptr<int>(), norm_w.numel() ? CBF(norm_w) : nullptr,
+                              float(eps), BFP(out)));
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
@@ -765,11 +770,11 @@ void gdn_commit_all(const std::vector<torch::Tensor>& qkv, const std::vector<tor
   dim3 grid(HV, B, nl);
   if (K == 128) {
     gdn_smem_attr(gdn_commit_kernel<128>, sizeof(GdnStage<128>));
-    C10_CUDA_CHECK(launch_pdl(gdn_commit_kernel<128>, grid, 128, sizeof(GdnStage<128>), st.stream(), a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(),
+    C10_CUDA_CHECK(launch_pdl(gdn_commit_kernel<128>, grid, kScanLanes * int(V), sizeof(GdnStage<128>), st.stream(), a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(),
                                                                      rw.size(1), nr.data_ptr<int>()));
   } else {
     gdn_smem_attr(gdn_commit_kernel<64>, sizeof(GdnStage<64>));
-    C10_CUDA_CHECK(launch_pdl(gdn_commit_kernel<64>, grid, 128, sizeof(GdnStage<64>), st.stream(), a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(),
+    C10_CUDA_CHECK(launch_pdl(gdn_commit_kernel<64>, grid, kScanLanes * int(V), sizeof(GdnStage<64>), st.stream(), a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(),
                                                                    rw.size(1), nr.data_ptr<int>()));
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
