@@ -727,9 +727,9 @@ void tree_step(const torch::Tensor& probs, const torch::Tensor& toks, const torc
       front_scores.data_ptr<float>(), front_tokens.data_ptr<int64_t>(),
       reinterpret_cast<__nv_bfloat16*>(front_hidden.data_ptr()), front_nodes.data_ptr<int64_t>(),
       ancestors.data_ptr<int>(), best.data_ptr<float>(), best_prev.data_ptr<float>(), layer_top.data_ptr<float>(),
-      deltas_out.defined() ? int(deltas_out.size(0)) : 0, deltas_out.defined() ? delta_rows.data_ptr<float>() : nullptr,
-      deltas_out.defined() ? deltas_out.data_ptr<float>() : nullptr,
-      deltas_out.defined() ? reinterpret_cast<unsigned*>(counter.data_ptr<int>()) : nullptr));
+      deltas_out.numel() ? int(deltas_out.size(0)) : 0, deltas_out.numel() ? delta_rows.data_ptr<float>() : nullptr,
+      deltas_out.numel() ? deltas_out.data_ptr<float>() : nullptr,
+      deltas_out.numel() ? reinterpret_cast<unsigned*>(counter.data_ptr<int>()) : nullptr));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -751,9 +751,9 @@ void tree_begin(const torch::Tensor& root_probs, const torch::Tensor& root_token
       front_scores.data_ptr<float>(), front_tokens.data_ptr<int64_t>(),
       reinterpret_cast<__nv_bfloat16*>(front_hidden.data_ptr()), front_nodes.data_ptr<int64_t>(),
       best.data_ptr<float>(), best_prev.data_ptr<float>(), layer_top.data_ptr<float>(),
-      deltas_out.defined() ? int(deltas_out.size(0)) : 0, deltas_out.defined() ? delta_rows.data_ptr<float>() : nullptr,
-      deltas_out.defined() ? deltas_out.data_ptr<float>() : nullptr,
-      deltas_out.defined() ? reinterpret_cast<unsigned*>(counter.data_ptr<int>()) : nullptr));
+      deltas_out.numel() ? int(deltas_out.size(0)) : 0, deltas_out.numel() ? delta_rows.data_ptr<float>() : nullptr,
+      deltas_out.numel() ? deltas_out.data_ptr<float>() : nullptr,
+      deltas_out.numel() ? reinterpret_cast<unsigned*>(counter.data_ptr<int>()) : nullptr));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
