@@ -148,30 +148,6 @@ __device__ __forceinline__ void gdn_stage(const GdnArgs& a, const int* rows, int
   __syncthreads();
 }
 
-// The output epilogue: o rounded to bf16, RMS-normalised over the head's V values, times w, times silu(z); with no
-// norm weight, o itself.
-__device__ __forceinline__ void gdn_store(const GdnArgs& a, int row, int h, int v, float o, const __nv_bfloat16* nw,
-                                          float eps, float* red, __nv_bfloat16* out, bool writer = true) {
-  const float ob = __bfloat162float(__float2bfloat16(o));
-  const float x2 = (writer && v < a.V) ? ob * ob : 0.f;
-  float s = warp_sum(x2);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwp = blockDim.x >> 5;
-  __syncthreads();
-  if (lane == 0) red[warp] = s;
-  __syncthreads();
-  float tot = 0.f;
-  for (int i = 0; i < nwp; ++i) tot += red[i];
-  const float rs = rsqrtf(tot / a.V + eps);
-  if (writer && v < a.V) {
-    if (nw == nullptr) {  // raw recurrence output (a caller that applies its own norm)
-      out[(size_t(row) * a.HV + h) * a.V + v] = __float2bfloat16(ob);
-      return;
-    }
-    const float z = bf(a.proj[size_t(row) * a.ldp + a.z_off + h * a.V + v]);
-    out[(size_t(row) * a.HV + h) * a.V + v] = __float2bfloat16(ob * rs * bf(nw[v]) * silu(z));
-  }
-}
-
 template <int K>
 __device__ __forceinline__ void load_state(float* S, const float* src) {
 #pragma unroll
@@ -267,6 +243,87 @@ __device__ __forceinline__ void save_state4(const float* S, float* row, int r) {
     *reinterpret_cast<float4*>(row + 16 * m + 4 * r) = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
 }
 
+// Tree launches walk chains. A request's rows are contiguous and parents precede children, so its tree splits into
+// chains: a chain starts at a root or at a row that is not its parent's first (lowest-index) child and continues
+// through first children, one chain per leaf. The CTA of row ``row`` returns if no chain starts there; otherwise
+// path[0, pre) receives the chain head's ancestors (root first) and path[pre, len) the chain. Replaying path[] from the
+// committed state reaches every chain row by the same step sequence as a root-to-row replay, so each row's state and
+// output are those of the row alone, and a tree costs the chain heads' ancestors plus one step per row.
+// ``win`` / ``fc`` hold 2 kMaxPath ints: the parents of rows [row - 63, row + 64) and each window row's first child.
+__device__ __forceinline__ void chain_walk(const int* __restrict__ parent, int T, int row, int* win, int* fc,
+                                           int* path, int* meta) {
+  const int lo = max(0, row - (kMaxPath - 1)), hi = min(T, row + kMaxPath);
+  const int n = hi - lo;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    win[i] = parent[lo + i];
+    fc[i] = 0x7fffffff;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int p = win[i];
+    if (p >= lo && p < hi) atomicMin(&fc[p - lo], lo + i);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int p = win[row - lo];
+    int len = 0, pre = 0;
+    if (!(p >= lo && fc[p - lo] == row)) {
+      for (int cur = p; cur >= lo && pre < kMaxPath - 1; cur = win[cur - lo]) ++pre;
+      int cur = p;
+      for (int i = pre - 1; i >= 0; --i) {
+        path[i] = cur;
+        cur = win[cur - lo];
+      }
+      len = pre;
+      for (cur = row; cur >= 0 && len < kMaxPath; ++len) {
+        path[len] = cur;
+        const int c = fc[cur - lo];
+        cur = c == 0x7fffffff ? -1 : c;
+      }
+    }
+    meta[0] = len;
+    meta[1] = pre;
+  }
+  __syncthreads();
+}
+
+// Gated RMSNorm of the chain rows' raw outputs (orow[c][v], fp32): warp w finishes rows w, w + 16, ..., lane l the
+// value columns 4l .. 4l+3. o is rounded to bf16, RMS-normalised over the head's V values (a fixed-order warp sum),
+// times w, times silu(z); with no norm weight, the rounded o itself.
+__device__ __forceinline__ void gdn_norm_rows(const GdnArgs& a, const int* rows, int n, int h, const float* orow,
+                                              const __nv_bfloat16* nw, float eps, __nv_bfloat16* out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  for (int c = warp; c < n; c += nwarps) {
+    const int row = rows[c];
+    float ob[4];
+    float x2 = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int v = 4 * lane + e;
+      ob[e] = v < a.V ? __bfloat162float(__float2bfloat16(orow[c * 128 + v])) : 0.f;
+      x2 = fmaf(ob[e], ob[e], x2);
+    }
+    const float rs = rsqrtf(warp_sum(x2) / a.V + eps);
+    __nv_bfloat16* o = out + (size_t(row) * a.HV + h) * a.V;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int v = 4 * lane + e;
+      if (v >= a.V) continue;
+      if (nw == nullptr) {
+        o[v] = __float2bfloat16(ob[e]);
+      } else {
+        const float z = bf(a.proj[size_t(row) * a.ldp + a.z_off + h * a.V + v]);
+        o[v] = __float2bfloat16(ob[e] * rs * bf(nw[v]) * silu(z));
+      }
+    }
+  }
+}
+
+// Tree mode: one CTA of 4 V threads per (value head, chain); the chain's ancestors and rows are replayed from the
+// committed state without writing it (value column v has kScanLanes lanes, lane r holding K/4 state elements in groups
+// of four at 16m + 4r + e: a column's lanes load one contiguous 64-byte run per group, and a staged k / q row is read
+// as conflict-free 16-byte pieces), the chain rows' raw outputs are kept in shared memory and normalised at the end.
+// The commit kernel runs the same step, so a row decoded alone, verified in a tree, or committed gives the same state.
 template <int K>
 __global__ void __launch_bounds__(512) gdn_kernel(GdnArgs a, const int* __restrict__ slot,
                                                   const int* __restrict__ parent, const __nv_bfloat16* __restrict__ nw,
@@ -275,37 +332,30 @@ __global__ void __launch_bounds__(512) gdn_kernel(GdnArgs a, const int* __restri
   pdl_trigger();
   extern __shared__ __align__(16) uint8_t gdn_smem[];
   GdnStage<K>& st = *reinterpret_cast<GdnStage<K>*>(gdn_smem);
-  __shared__ float red[16];
-  __shared__ int path[kMaxPath];
-  __shared__ int win[kMaxPath];
-  __shared__ int plen;
+  float* orow = reinterpret_cast<float*>(gdn_smem + sizeof(GdnStage<K>));  // [kMaxPath][128]
+  __shared__ int win[2 * kMaxPath], fc[2 * kMaxPath], path[kMaxPath], meta[2];
   const int h = blockIdx.x;
   const int v = threadIdx.x / kScanLanes, r = threadIdx.x % kScanLanes;
   const int kh = h / (a.HV / a.HK);
   const int vc = min(v, a.V - 1);
-  // later rows have the longer paths in a tree's node order: start them first
+  // later rows have the longer ancestor runs in a tree's node order: start them first
   const int row = gridDim.y - 1 - blockIdx.y;
-  // the parents of the 64 rows up to this one (a request's rows are contiguous, parents precede children)
-  const int lo = max(0, row - (kMaxPath - 1));
-  if (threadIdx.x < kMaxPath && lo + int(threadIdx.x) <= row) win[threadIdx.x] = parent[lo + threadIdx.x];
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int n = 0, cur = row, tmp[kMaxPath];
-    while (cur >= lo && n < kMaxPath) { tmp[n++] = cur; cur = win[cur - lo]; }
-    for (int i = 0; i < n; ++i) path[i] = tmp[n - 1 - i];
-    plen = n;
-  }
+  chain_walk(parent, gridDim.y, row, win, fc, path, meta);
+  const int len = meta[0], pre = meta[1];
+  if (len == 0) return;
   float S[K / 4];
   load_state4<K>(S, a.state + ((size_t(slot[row]) * a.HV + h) * a.V + vc) * K, r);
-  __syncthreads();
-  float o = 0.f;
-  for (int p0 = 0; p0 < plen; p0 += kGdnTile) {
-    const int n = min(kGdnTile, plen - p0);
+  for (int p0 = 0; p0 < len; p0 += kGdnTile) {
+    const int n = min(kGdnTile, len - p0);
     if (p0) __syncthreads();
     gdn_stage<K>(a, path + p0, n, h, kh, st);
-    for (int j = 0; j < n; ++j) o = gdn_step4<K>(S, st, j, vc, r);
+    for (int j = 0; j < n; ++j) {
+      const float o = gdn_step4<K>(S, st, j, vc, r);
+      if (p0 + j >= pre && r == 0 && v < a.V) orow[(p0 + j - pre) * 128 + v] = o;
+    }
   }
-  gdn_store(a, row, h, v, o, nw, eps, red, out, r == 0);
+  __syncthreads();
+  gdn_norm_rows(a, path + pre, len - pre, h, orow, nw, eps, out);
 }
 
 template <int K>
@@ -440,17 +490,22 @@ struct GdnLayerTable {
   GdnLayer l[kMaxLayers];
 };
 
-// Commit of every GDN layer in one launch: CTA (value head, request, layer) replays rows[b, :n[b]] in place.
+// Commit of every GDN layer in one launch: CTA (value head x 32-column slice, request, layer) replays rows[b, :n[b]]
+// in place with the tree kernel's step (value columns are independent, so a slice needs only its own columns).
+constexpr int kCommitV = 32;
 template <int K>
-__global__ void __launch_bounds__(512) gdn_commit_kernel(GdnArgs a, const __grid_constant__ GdnLayerTable layers,
-                                                         const int* __restrict__ slots, const int* __restrict__ rows,
-                                                         int rows_ld, const int* __restrict__ nrows) {
+__global__ void __launch_bounds__(kScanLanes * kCommitV) gdn_commit_kernel(GdnArgs a,
+                                                                           const __grid_constant__ GdnLayerTable layers,
+                                                                           const int* __restrict__ slots,
+                                                                           const int* __restrict__ rows, int rows_ld,
+                                                                           const int* __restrict__ nrows) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ __align__(16) uint8_t gdn_smem[];
   GdnStage<K>& st = *reinterpret_cast<GdnStage<K>*>(gdn_smem);
-  const int h = blockIdx.x, b = blockIdx.y, l = blockIdx.z;
-  const int v = threadIdx.x / kScanLanes, r = threadIdx.x % kScanLanes;
+  const int slices = (a.V + kCommitV - 1) / kCommitV;
+  const int h = blockIdx.x / slices, b = blockIdx.y, l = blockIdx.z;
+  const int v = (blockIdx.x % slices) * kCommitV + threadIdx.x / kScanLanes, r = threadIdx.x % kScanLanes;
   const int n = nrows[b];
   if (n <= 0) return;
   const GdnLayer L = layers.l[l];
@@ -506,17 +561,20 @@ struct MambaArgs {
   const float* dskip;
   float* state;  // [slots, H, P, N]
   int H, P, N, G;
+  int vec;       // rows staged as 16-byte pieces (row stride, offsets and the base 16-byte aligned)
 };
 
 // Mamba2 selective-state update along a walk of rows: state_t = exp(A dt_t) state + dt_t x_t B_t^T, and
-// y_t = C_t . state_t + D x_t. One CTA of 256 threads per (head, walk): thread (p, q) owns quarter q of state row p
-// (N/4 consecutive columns, loaded and stored as 16-byte pieces; a warp covers 8 whole rows), and the walk's x, B,
-// C and gate of each row are staged in shared memory 16 rows at a time, so a step is register arithmetic only.
-// y sums each quarter's columns in order, then the quarters as (q0 + q1) + (q2 + q3); every mode runs this same
-// step, so a row verified in a tree, decoded alone, or committed gives identical state and output.
-// Walks: kMambaTree - the root-to-row path of row blockIdx.y (parents inside the launch), output for that row only;
-// kMambaCommit - the accepted rows of request blockIdx.y, state written back; kMambaScan - the rows of segment
-// blockIdx.y in order (prefill), output for every row, state written back.
+// y_t = C_t . state_t + D x_t. One CTA of 256 threads per (head, walk): thread (p, q) owns a quarter of state row p in
+// groups of four columns at 16m + 4q + e (the row's four owners read one contiguous 64-byte run of a staged B / C row
+// per group: conflict-free 16-byte shared-memory reads, broadcast over the warp's eight rows), and the walk's x, B, C
+// and gate of each row are staged in shared memory 16 rows at a time (16-byte global loads where the row layout
+// allows), so a step is register arithmetic only. y sums each owner's columns in group order, then the owners as
+// (q0 + q1) + (q2 + q3); every mode runs this same step, so a row verified in a tree, decoded alone, or committed gives
+// identical state and output.
+// Walks: kMambaTree - the chain starting at row blockIdx.y (its ancestors without output, then its rows with output;
+// parents inside the launch); kMambaCommit - the accepted rows of request blockIdx.y, state written back;
+// kMambaScan - the rows of segment blockIdx.y in order (prefill), output for every row, state written back.
 enum : int { kMambaTree = 0, kMambaCommit = 1, kMambaScan = 2 };
 constexpr int kMambaStage = 16;
 
@@ -530,28 +588,19 @@ __global__ void __launch_bounds__(256) mamba_walk_kernel(MambaArgs a, int mode, 
   pdl_wait();
   pdl_trigger();
   constexpr int NQ = N / 4;
-  __shared__ int path[kMaxPath];
-  __shared__ int win[kMaxPath];
-  __shared__ int plen;
-  __shared__ float sx[kMambaStage][64], sB[kMambaStage][N], sC[kMambaStage][N], sda[kMambaStage],
-      sdt[kMambaStage];
+  constexpr int RW = 64 + 2 * N;  // staged values per row: x (padded to 64), B, C
+  __shared__ int path[kMaxPath], win[2 * kMaxPath], fc[2 * kMaxPath], meta[2];
+  __shared__ __align__(16) float sx[kMambaStage][64], sB[kMambaStage][N], sC[kMambaStage][N];
+  __shared__ float sda[kMambaStage], sdt[kMambaStage];
   const int h = blockIdx.x, t = threadIdx.x, p = t >> 2, q = t & 3;
   const int grp = h / (a.H / a.G);
   const bool live = p < a.P;
-  int state_slot = 0, first = 0, len = 0;
+  int state_slot = 0, first = 0, len = 0, pre = 0;
   if (mode == kMambaTree) {
-    // the parents of the 64 rows up to this one (a request's rows are contiguous, parents precede children)
-    const int r = blockIdx.y, lo = max(0, r - (kMaxPath - 1));
-    if (t < kMaxPath && lo + t <= r) win[t] = parent[lo + t];
-    __syncthreads();
-    if (t == 0) {
-      int n = 0, cur = r, tmp[kMaxPath];
-      while (cur >= lo && n < kMaxPath) { tmp[n++] = cur; cur = win[cur - lo]; }
-      for (int i = 0; i < n; ++i) path[i] = tmp[n - 1 - i];
-      plen = n;
-    }
-    __syncthreads();
-    len = plen;
+    const int r = blockIdx.y;
+    chain_walk(parent, gridDim.y, r, win, fc, path, meta);
+    len = meta[0];
+    pre = meta[1];
     state_slot = slot[r];
   } else if (mode == kMambaCommit) {
     const int b = blockIdx.y;
@@ -564,25 +613,55 @@ __global__ void __launch_bounds__(256) mamba_walk_kernel(MambaArgs a, int mode, 
     state_slot = slot[first];
   }
   if (len <= 0) return;
-  float* st = a.state + ((size_t(state_slot) * a.H + h) * a.P + (live ? p : 0)) * N + q * NQ;
+  float* st = a.state + ((size_t(state_slot) * a.H + h) * a.P + (live ? p : 0)) * N + 4 * q;
   float S[NQ];
 #pragma unroll
-  for (int i = 0; i < NQ; i += 4) {
-    const float4 v = *reinterpret_cast<const float4*>(st + i);
-    S[i] = v.x; S[i + 1] = v.y; S[i + 2] = v.z; S[i + 3] = v.w;
+  for (int m = 0; m < NQ / 4; ++m) {
+    const float4 v = *reinterpret_cast<const float4*>(st + 16 * m);
+    S[4 * m] = v.x; S[4 * m + 1] = v.y; S[4 * m + 2] = v.z; S[4 * m + 3] = v.w;
   }
   const float A = -__expf(a.a_log[h]);
   const float dskip = a.dskip[h];
   for (int c0 = 0; c0 < len; c0 += kMambaStage) {
     const int cn = min(kMambaStage, len - c0);
     __syncthreads();
-    for (int i = t; i < cn * (64 + 2 * N); i += blockDim.x) {
-      const int k = i / (64 + 2 * N), e = i % (64 + 2 * N);
-      const int row = mode == kMambaScan ? first + c0 + k : path[c0 + k];
-      const __nv_bfloat16* base = a.xbc + size_t(row) * a.ldx;
-      if (e < 64) sx[k][e] = e < a.P ? bf(base[h * a.P + e]) : 0.f;
-      else if (e < 64 + N) sB[k][e - 64] = bf(base[a.H * a.P + grp * N + (e - 64)]);
-      else sC[k][e - 64 - N] = bf(base[a.H * a.P + a.G * N + grp * N + (e - 64 - N)]);
+    if (a.vec) {
+      // 16-byte pieces: P/8 of x, N/8 of B, N/8 of C per row
+      const int px = a.P / 8, pieces = px + N / 4;
+      for (int i = t; i < cn * pieces; i += blockDim.x) {
+        const int k = i / pieces, e = i % pieces;
+        const int row = mode == kMambaScan ? first + c0 + k : path[c0 + k];
+        const __nv_bfloat16* base = a.xbc + size_t(row) * a.ldx;
+        const __nv_bfloat16* src;
+        float* dst;
+        if (e < px) {
+          src = base + h * a.P + 8 * e;
+          dst = &sx[k][8 * e];
+        } else if (e < px + N / 8) {
+          src = base + a.H * a.P + grp * N + 8 * (e - px);
+          dst = &sB[k][8 * (e - px)];
+        } else {
+          src = base + a.H * a.P + a.G * N + grp * N + 8 * (e - px - N / 8);
+          dst = &sC[k][8 * (e - px - N / 8)];
+        }
+        const uint4 raw = *reinterpret_cast<const uint4*>(src);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(h2[j]);
+          dst[2 * j] = f.x;
+          dst[2 * j + 1] = f.y;
+        }
+      }
+    } else {
+      for (int i = t; i < cn * RW; i += blockDim.x) {
+        const int k = i / RW, e = i % RW;
+        const int row = mode == kMambaScan ? first + c0 + k : path[c0 + k];
+        const __nv_bfloat16* base = a.xbc + size_t(row) * a.ldx;
+        if (e < 64) sx[k][e] = e < a.P ? bf(base[h * a.P + e]) : 0.f;
+        else if (e < 64 + N) sB[k][e - 64] = bf(base[a.H * a.P + grp * N + (e - 64)]);
+        else sC[k][e - 64 - N] = bf(base[a.H * a.P + a.G * N + grp * N + (e - 64 - N)]);
+      }
     }
     if (t < cn) {
       const int row = mode == kMambaScan ? first + c0 + t : path[c0 + t];
@@ -592,15 +671,27 @@ __global__ void __launch_bounds__(256) mamba_walk_kernel(MambaArgs a, int mode, 
     }
     __syncthreads();
     for (int k = 0; k < cn; ++k) {
-      const float x = sx[k][live ? p : 0];
+      const float x = live ? sx[k][p] : 0.f;
       const float da = sda[k], dx = sdt[k] * x;
 #pragma unroll
-      for (int i = 0; i < NQ; ++i) S[i] = fmaf(S[i], da, dx * sB[k][q * NQ + i]);
-      const bool emit = mode == kMambaScan || (mode == kMambaTree && c0 + k == len - 1);
+      for (int m = 0; m < NQ / 4; ++m) {
+        const float4 b4 = *reinterpret_cast<const float4*>(&sB[k][16 * m + 4 * q]);
+        S[4 * m] = fmaf(S[4 * m], da, dx * b4.x);
+        S[4 * m + 1] = fmaf(S[4 * m + 1], da, dx * b4.y);
+        S[4 * m + 2] = fmaf(S[4 * m + 2], da, dx * b4.z);
+        S[4 * m + 3] = fmaf(S[4 * m + 3], da, dx * b4.w);
+      }
+      const bool emit = mode == kMambaScan || (mode == kMambaTree && c0 + k >= pre);
       if (emit) {
         float y = 0.f;
 #pragma unroll
-        for (int i = 0; i < NQ; ++i) y = fmaf(S[i], sC[k][q * NQ + i], y);
+        for (int m = 0; m < NQ / 4; ++m) {
+          const float4 c4 = *reinterpret_cast<const float4*>(&sC[k][16 * m + 4 * q]);
+          y = fmaf(S[4 * m], c4.x, y);
+          y = fmaf(S[4 * m + 1], c4.y, y);
+          y = fmaf(S[4 * m + 2], c4.z, y);
+          y = fmaf(S[4 * m + 3], c4.w, y);
+        }
         y += __shfl_xor_sync(0xffffffffu, y, 1);
         y += __shfl_xor_sync(0xffffffffu, y, 2);
         const int row = mode == kMambaScan ? first + c0 + k : path[c0 + k];
@@ -610,7 +701,8 @@ __global__ void __launch_bounds__(256) mamba_walk_kernel(MambaArgs a, int mode, 
   }
   if (mode != kMambaTree && live) {
 #pragma unroll
-    for (int i = 0; i < NQ; i += 4) *reinterpret_cast<float4*>(st + i) = make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
+    for (int m = 0; m < NQ / 4; ++m)
+      *reinterpret_cast<float4*>(st + 16 * m) = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
   }
 }
 
@@ -729,14 +821,15 @@ torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int6
   dim3 grid(HV, T);
   const int threads = kScanLanes * int(V);
   auto st = at::cuda::getCurrentCUDAStream();
+  constexpr size_t kRowOut = size_t(kMaxPath) * 128 * sizeof(float);  // raw outputs of a chain's rows
   if (K == 128) {
-    gdn_smem_attr(gdn_kernel<128>, sizeof(GdnStage<128>));
-    C10_CUDA_CHECK(launch_pdl(gdn_kernel<128>, grid, threads, sizeof(GdnStage<128>), st.stream(), a,
+    gdn_smem_attr(gdn_kernel<128>, sizeof(GdnStage<128>) + kRowOut);
+    C10_CUDA_CHECK(launch_pdl(gdn_kernel<128>, grid, threads, sizeof(GdnStage<128>) + kRowOut, st.stream(), a,
                               sl.data_ptr<int>(), pa.data_ptr<int>(), norm_w.numel() ? CBF(norm_w) : nullptr,
                               float(eps), BFP(out)));
   } else {
-    gdn_smem_attr(gdn_kernel<64>, sizeof(GdnStage<64>));
-    C10_CUDA_CHECK(launch_pdl(gdn_kernel<64>, grid, threads, sizeof(GdnStage<64>), st.stream(), a,
+    gdn_smem_attr(gdn_kernel<64>, sizeof(GdnStage<64>) + kRowOut);
+    C10_CUDA_CHECK(launch_pdl(gdn_kernel<64>, grid, threads, sizeof(GdnStage<64>) + kRowOut, st.stream(), a,
                               sl.data_ptr<int>(), pa.data_ptr<int>(), norm_w.numel() ? CBF(norm_w) : nullptr,
                               float(eps), BFP(out)));
   }
@@ -767,14 +860,14 @@ void gdn_commit_all(const std::vector<torch::Tensor>& qkv, const std::vector<tor
   GdnArgs a{nullptr, int(qkv[0].stride(0)), nullptr, int(proj[0].stride(0)), 0, int(b_off), int(a_off), nullptr,
             nullptr, nullptr, int(HK), int(HV), int(K), int(V)};
   auto st = at::cuda::getCurrentCUDAStream();
-  dim3 grid(HV, B, nl);
+  dim3 grid(HV * ((V + kCommitV - 1) / kCommitV), B, nl);
   if (K == 128) {
     gdn_smem_attr(gdn_commit_kernel<128>, sizeof(GdnStage<128>));
-    C10_CUDA_CHECK(launch_pdl(gdn_commit_kernel<128>, grid, kScanLanes * int(V), sizeof(GdnStage<128>), st.stream(), a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(),
+    C10_CUDA_CHECK(launch_pdl(gdn_commit_kernel<128>, grid, kScanLanes * kCommitV, sizeof(GdnStage<128>), st.stream(), a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(),
                                                                      rw.size(1), nr.data_ptr<int>()));
   } else {
     gdn_smem_attr(gdn_commit_kernel<64>, sizeof(GdnStage<64>));
-    C10_CUDA_CHECK(launch_pdl(gdn_commit_kernel<64>, grid, kScanLanes * int(V), sizeof(GdnStage<64>), st.stream(), a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(),
+    C10_CUDA_CHECK(launch_pdl(gdn_commit_kernel<64>, grid, kScanLanes * kCommitV, sizeof(GdnStage<64>), st.stream(), a, tab, sl.data_ptr<int>(), rw.data_ptr<int>(),
                                                                    rw.size(1), nr.data_ptr<int>()));
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -790,9 +883,11 @@ static MambaArgs mamba_args(const torch::Tensor& xbc, const torch::Tensor& dt, c
                             int64_t P, int64_t N, int64_t G) {
   TORCH_CHECK(xbc.stride(1) == 1 && dt.stride(1) == 1 && state.is_contiguous());
   TORCH_CHECK(P <= 64 && (N == 128 || N == 64 || N == 16), "mamba: head dim <= 64 and state 16/64/128");
+  const bool vec = (reinterpret_cast<uintptr_t>(xbc.data_ptr()) % 16 == 0) && xbc.stride(0) % 8 == 0 && P % 8 == 0 &&
+                   (H * P) % 8 == 0 && (G * N) % 8 == 0;
   return MambaArgs{CBF(xbc), int(xbc.stride(0)), CBF(dt), int(dt.stride(0)), a_log.data_ptr<float>(),
                    dt_bias.data_ptr<float>(), dskip.data_ptr<float>(), state.data_ptr<float>(), int(H), int(P),
-                   int(N), int(G)};
+                   int(N), int(G), int(vec)};
 }
 
 #define E4_MAMBA_DISPATCH(N_, ...)                                                                      \

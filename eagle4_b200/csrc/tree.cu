@@ -411,6 +411,27 @@ __device__ __forceinline__ void store_work_deltas(int b, int bs, int K, int work
   if (t == 0) *counter = 0u;
 }
 
+// Copy ``rows`` rows of H bf16 values in 16-byte pieces: dst row k <- src row src_row[k] (shared memory). A thread
+// issues up to eight loads before its stores, so the copy costs a few memory round trips instead of one per piece.
+__device__ __forceinline__ void gather_rows16(__nv_bfloat16* __restrict__ dst, const __nv_bfloat16* __restrict__ src,
+                                              const int* src_row, int rows, int H) {
+  constexpr int U = 8;
+  const int vec = H / 8, total = rows * vec;
+  for (int i0 = threadIdx.x; i0 < total; i0 += blockDim.x * U) {
+    uint4 tmp[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i < total) tmp[u] = reinterpret_cast<const uint4*>(src + size_t(src_row[i / vec]) * H)[i % vec];
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i < total) reinterpret_cast<uint4*>(dst + size_t(i / vec) * H)[i % vec] = tmp[u];
+    }
+  }
+}
+
 // The tree's first level for request b (DraftTree.begin semantics): the root's K children (sorted by probability,
 // ties to the lower child, unless the draw order is kept), the frontier (tokens, scores, nodes, the root's hidden
 // row for every lane), the best set {root, children} and, when asked, the depth-0 work deltas.
@@ -451,11 +472,10 @@ __global__ void tree_begin_kernel(const float* __restrict__ root_probs, const in
     best_prev[size_t(b) * work_cap + i] = old_best[i];
     best[size_t(b) * work_cap + i] = i == 0 ? root_score : (i <= K ? ranked[i - 1] : 0.f);
   }
-  const int vec = H / 8;
-  for (int i = t; i < K * vec; i += blockDim.x) {
-    reinterpret_cast<uint4*>(front_hidden + size_t(b * K + i / vec) * H)[i % vec] =
-        reinterpret_cast<const uint4*>(root_hidden + size_t(b) * H)[i % vec];
-  }
+  __shared__ int src_row[8];
+  if (t < K) src_row[t] = b;
+  __syncthreads();
+  gather_rows16(front_hidden + size_t(b) * K * H, root_hidden, src_row, K, H);
   if (deltas_out != nullptr)
     store_work_deltas(b, gridDim.x, K, work_cap, max_verify, old_best, ranked, delta_rows, deltas_out, counter);
 }
@@ -508,13 +528,11 @@ __global__ void tree_step_kernel(const float* __restrict__ probs, const int64_t*
     front_nodes[b * K + t] = pick[t] + layer_start;
     layer_top[b * K + t] = top[t];
   }
-  // frontier hidden rows (16-byte chunks)
-  const int vec = H / 8;
-  for (int i = t; i < K * vec; i += blockDim.x) {
-    const int k = i / vec, c = i % vec;
-    reinterpret_cast<uint4*>(front_hidden + size_t(b * K + k) * H)[c] =
-        reinterpret_cast<const uint4*>(hidden + size_t(b * K + pick[k] / K) * H)[c];
-  }
+  // frontier hidden rows: the picked lanes' draft hidden states
+  __shared__ int src_row[8];
+  if (t < K) src_row[t] = b * K + pick[t] / K;
+  __syncthreads();
+  gather_rows16(front_hidden + size_t(b) * K * H, hidden, src_row, K, H);
   // best set: the work_cap largest values of (best list ++ layer), descending; every value finds its rank in
   // parallel (ties by position), values ranked below work_cap are written at their rank
   const int m = work_cap + KK;
@@ -554,9 +572,9 @@ __global__ void select_rows_kernel(const float* __restrict__ scores, const float
   }
   __syncthreads();
   // compaction in node order: thread t owns the nodes [t*per, (t+1)*per); an exclusive scan of the per-thread
-  // counts (warp shuffles, then the four warp totals) gives each selected node its row
+  // counts (warp shuffles, then the warp totals) gives each selected node its row
   {
-    __shared__ int warp_sum[4];
+    __shared__ int warp_sum[32];
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int per = (n + blockDim.x - 1) / blockDim.x;
     const int i0 = t * per, i1 = min(n, i0 + per);
@@ -720,7 +738,7 @@ void tree_step(const torch::Tensor& probs, const torch::Tensor& toks, const torc
   auto h = hidden.contiguous();
   const int H = h.size(1);
   TORCH_CHECK(H % 8 == 0);
-  C10_CUDA_CHECK(launch_pdl(tree_step_kernel, bs, 128, 0, at::cuda::getCurrentCUDAStream().stream(), 
+  C10_CUDA_CHECK(launch_pdl(tree_step_kernel, bs, 512, 0, at::cuda::getCurrentCUDAStream().stream(), 
       p.data_ptr<float>(), tk.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()), H, K, step,
       layer_start, parent_col, best.size(1), scores.size(1), parents.size(1), ancestors.size(2),
       scores.data_ptr<float>(), tokens.data_ptr<int64_t>(), parents.data_ptr<int64_t>(),
@@ -744,7 +762,7 @@ void tree_begin(const torch::Tensor& root_probs, const torch::Tensor& root_token
               root_tokens.scalar_type() == torch::kInt64);
   const int H = root_hidden.size(1);
   TORCH_CHECK(H % 8 == 0);
-  C10_CUDA_CHECK(launch_pdl(tree_begin_kernel, bs, 128, 0, at::cuda::getCurrentCUDAStream().stream(),
+  C10_CUDA_CHECK(launch_pdl(tree_begin_kernel, bs, 512, 0, at::cuda::getCurrentCUDAStream().stream(),
       root_probs.data_ptr<float>(), root_tokens.data_ptr<int64_t>(),
       reinterpret_cast<const __nv_bfloat16*>(root_hidden.data_ptr()), H, int(K), int(keep_order), float(root_score),
       int(best.size(1)), int(scores.size(1)), scores.data_ptr<float>(), tokens.data_ptr<int64_t>(),
@@ -765,7 +783,7 @@ std::vector<torch::Tensor> select_rows(const torch::Tensor& scores, const torch:
   auto ot = torch::empty({bs, count}, tokens.options());
   auto op = torch::empty({bs, count + 1}, tokens.options().dtype(torch::kInt32));
   auto on = torch::empty({bs, count + 1}, tokens.options());
-  C10_CUDA_CHECK(launch_pdl(select_rows_kernel, bs, 128, 0, at::cuda::getCurrentCUDAStream().stream(),
+  C10_CUDA_CHECK(launch_pdl(select_rows_kernel, bs, 256, 0, at::cuda::getCurrentCUDAStream().stream(),
       scores.data_ptr<float>(), decay.data_ptr<float>(), tokens.data_ptr<int64_t>(), parents.data_ptr<int64_t>(), n,
       scores.size(1), parents.size(1), K, count, ot.data_ptr<int64_t>(), op.data_ptr<int>(), on.data_ptr<int64_t>()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
