@@ -29,6 +29,7 @@ from eagle4_b200 import ops
 from eagle4_b200.core.config import HarnessConfig, Mode
 from eagle4_b200.core.cost_model import WidthStep
 from eagle4_b200.core.draft_tree import DraftTree, TreeShape
+from eagle4_b200.core.limits import COST_BATCH_SIZES
 from eagle4_b200.runtime.pages import PagePool
 from eagle4_b200.runtime.policy import RoundPolicy, ServedChainPolicy, ServedTreeChoice, fit_width
 from eagle4_b200.models.draft import DraftCache, DraftModel
@@ -136,7 +137,10 @@ class Engine:
         self.max_len = max_len + span
         self.span = span
         kv_pages = (kv_tokens if kv_tokens is not None else max_reqs * self.max_len) // page + 2  # + trash page
-        self.tcache = TargetCache.allocate(target.cfg, max_reqs=max_reqs, max_len=self.max_len, page=page,
+        # one cache row beyond the requests' rows: batch rows that pad a round up to its graph bucket use it (its
+        # block-table row maps only the trash page, its recurrent state belongs to no request)
+        self.pad_slot = max_reqs
+        self.tcache = TargetCache.allocate(target.cfg, max_reqs=max_reqs + 1, max_len=self.max_len, page=page,
                                            device=self.device, dtype=self.dtype, kv_pages=kv_pages)
         self.pages = PagePool(self.tcache.block_table, kv_pages, page)
         self.dcache = None
@@ -206,6 +210,9 @@ class Engine:
         self.host_tok = torch.zeros(max_reqs, n, dtype=i64, pin_memory=pin)
         self.host_cnt = torch.zeros(max_reqs, dtype=i32, pin_memory=pin)
         self.use_graphs = use_graphs and dev.type == "cuda"
+        # rounds run at graph buckets (the calibration batch grid up to max_reqs): a batch of bs requests replays the
+        # graph of the smallest bucket >= bs, its extra rows padding on the spare cache row
+        self.buckets = sorted({b for b in COST_BATCH_SIZES if b < max_reqs} | {max_reqs})
         self.graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
         self.pool = torch.cuda.graph_pool_handle() if self.use_graphs else None
         self.graph_launches: Dict[tuple, int] = {}
@@ -570,6 +577,107 @@ class Engine:
         self._graph(("plain", bs), self._plain_round, bs)
 
     # ------------------------------------------------------------------ driver
+    def bucket(self, bs: int) -> int:
+        """The graph batch size a round of ``bs`` requests runs at."""
+        for b in self.buckets:
+            if b >= bs:
+                return b
+        raise ValueError(f"batch {bs} exceeds max_reqs {self.max_reqs}")
+
+    def _pad(self, bs: int, rows: int) -> None:
+        """Batch rows [bs, rows) as inert padding: the spare cache row, one committed position, token 0."""
+        if rows > bs:
+            self.slot[bs:rows] = self.pad_slot
+            self.L[bs:rows] = 1
+            self.root[bs:rows] = 0
+            self.ext_tok[bs:rows] = 0
+            self.ext_cnt[bs:rows] = 1
+
+    def serve_round(self, bs: int, context: int, *, speculative: bool = True,
+                    room: Optional[Sequence[int]] = None):
+        """One serving round over batch rows [0, bs) (padded to the round's graph bucket): a speculative tree or
+        chain round, or a native decode round when the served choice or the verify batch limit says so; then the
+        rows' emitted tokens are read back (one device-to-host copy). ``context``: the batch's mean context length
+        (cost-model input). ``room[b]``: at most this many tokens are taken for row b. Returns (tokens taken per
+        row, tokens emitted per row)."""
+        rows = self.bucket(bs)
+        self._pad(bs, rows)
+        spec = speculative and self.draft is not None
+        over_limit = spec and self.verify_batch_limit is not None and bs > self.verify_batch_limit
+        self._pending_timing = None
+        self._captured = False
+        self._rounds_served += 1
+        if self.heartbeat is not None and self._rounds_served % self.heartbeat_every == 0:
+            # every rank reaches this round; a peer that crashed or hung is named here, before any collective
+            step = self._rounds_served // self.heartbeat_every
+            self.heartbeat.beat(step)
+            self.heartbeat.check(step, self.heartbeat_timeout)
+        chain_t0 = None
+        tree_t0 = None
+        choice = ServedTreeChoice.SPECULATE
+        if spec and self.tree_choice is not None and not over_limit:
+            choice = self.tree_choice.choice(rows)
+            tree_t0 = _Stamp(self.device)
+            tree_t0.record()
+        if over_limit:  # above the verify batch limit: native decode (the draft keeps its pending rows)
+            choice = ServedTreeChoice.NATIVE
+            self._plain(rows)
+        elif spec and choice == ServedTreeChoice.NATIVE:
+            self._plain(rows)
+        elif spec and self.chain_policy is not None:
+            chain_w = self.chain_policy.width(rows)
+            chain_t0 = _Stamp(self.device)
+            chain_t0.record()
+            self._chain_round(rows, chain_w)
+            chain_t1 = _Stamp(self.device)
+            chain_t1.record()
+        elif spec:
+            self._spec_round(rows, context)
+        else:
+            self._plain(rows)
+        if tree_t0 is not None:
+            tree_t1 = _Stamp(self.device)
+            tree_t1.record()
+        self.host_tok[:bs].copy_(self.out_tok[:bs], non_blocking=True)
+        self.host_cnt[:bs].copy_(self.out_cnt[:bs], non_blocking=True)
+        if self.device.type == "cuda":
+            torch.cuda.current_stream().synchronize()
+        if spec and self.policy.cost is not None:
+            self.lagged_scores = self.host_scores.tolist()
+        if self._pending_timing is not None:
+            b_, w_, c_, ev, nsteps = self._pending_timing
+            verify_us, draft_us = ev[1].elapsed_us(ev[2]), ev[0].elapsed_us(ev[1])
+            if self.target.tp is not None:  # every rank must record the same costs to decide alike
+                verify_us, draft_us = self.target.tp.max_over_ranks([verify_us, draft_us])
+            self.policy.record(b_, w_, c_, verify_us, nsteps, draft_us, settled=not self._captured)
+        taken, counts = [], []
+        for b in range(bs):
+            c = int(self.host_cnt[b])
+            take = c if room is None else min(c, room[b])
+            taken.append(self.host_tok[b, :take].tolist())
+            counts.append(c)
+        got = [len(t) for t in taken]
+        if spec:
+            self.stats.record(got)
+        if self.recorder is not None:
+            kind = "plain" if not spec else ("native" if choice == ServedTreeChoice.NATIVE else
+                                             ("chain" if chain_t0 is not None else "tree"))
+            t_us = tree_t0.elapsed_us(tree_t1) if tree_t0 is not None else (
+                chain_t0.elapsed_us(chain_t1) if chain_t0 is not None else None)
+            self.recorder.record(bs=bs, kind=kind, depth=self.last_depth if spec else 0,
+                                 width=self.last_width if spec else 1, tokens=got, round_us=t_us)
+        if tree_t0 is not None:
+            us = tree_t0.elapsed_us(tree_t1)
+            if self.target.tp is not None:
+                us = self.target.tp.max_over_ranks([us])[0]
+            self.tree_choice.record(rows, choice, us, sum(got) / len(got), settled=not self._captured)
+        if chain_t0 is not None:
+            us = chain_t0.elapsed_us(chain_t1)
+            if self.target.tp is not None:
+                us = self.target.tp.max_over_ranks([us])[0]
+            self.chain_policy.record(rows, chain_w, us, sum(got) / len(got), settled=not self._captured)
+        return taken, counts
+
     def generate(self, prompts, max_new_tokens: int, *, speculative: bool = True) -> List[List[int]]:
         """Static batch: all prompts prefill, then rounds until every request has ``max_new_tokens`` tokens."""
         prompts = [p if torch.is_tensor(p) else torch.tensor(list(p), dtype=torch.int64) for p in prompts]
@@ -580,6 +688,7 @@ class Engine:
         ctx = [int(p.shape[0]) for p in prompts]
         marks = [_Stamp(self.device) for _ in range(3)]  # start, prefill done, rounds done
         marks[0].record()
+        self.slot[:bs] = torch.arange(bs, dtype=torch.int32, device=self.device)
         for b, p in enumerate(prompts):
             need = int(p.shape[0]) + max_new_tokens + self.span
             if need > self.max_len:
@@ -592,82 +701,12 @@ class Engine:
         self.host_tok[:bs].copy_(self.out_tok[:bs])
         for b in range(bs):
             outs[b].append(int(self.host_tok[b, 0]))
-        spec = speculative and self.draft is not None
-        over_limit = spec and self.verify_batch_limit is not None and bs > self.verify_batch_limit
         while min(len(o) for o in outs) < max_new_tokens:
-            self._pending_timing = None
-            self._captured = False
-            self._rounds_served += 1
-            if self.heartbeat is not None and self._rounds_served % self.heartbeat_every == 0:
-                # every rank reaches this round; a peer that crashed or hung is named here, before any collective
-                step = self._rounds_served // self.heartbeat_every
-                self.heartbeat.beat(step)
-                self.heartbeat.check(step, self.heartbeat_timeout)
-            chain_t0 = None
-            tree_t0 = None
-            choice = ServedTreeChoice.SPECULATE
-            if spec and self.tree_choice is not None and not over_limit:
-                choice = self.tree_choice.choice(bs)
-                tree_t0 = _Stamp(self.device)
-                tree_t0.record()
-            if over_limit:  # above the verify batch limit: native decode (the draft keeps its pending rows)
-                choice = ServedTreeChoice.NATIVE
-                self._plain(bs)
-            elif spec and choice == ServedTreeChoice.NATIVE:
-                self._plain(bs)
-            elif spec and self.chain_policy is not None:
-                chain_w = self.chain_policy.width(bs)
-                chain_t0 = _Stamp(self.device)
-                chain_t0.record()
-                self._chain_round(bs, chain_w)
-                chain_t1 = _Stamp(self.device)
-                chain_t1.record()
-            elif spec:
-                self._spec_round(bs, sum(ctx) // bs)
-            else:
-                self._plain(bs)
-            if tree_t0 is not None:
-                tree_t1 = _Stamp(self.device)
-                tree_t1.record()
-            self.host_tok[:bs].copy_(self.out_tok[:bs], non_blocking=True)
-            self.host_cnt[:bs].copy_(self.out_cnt[:bs], non_blocking=True)
-            if self.device.type == "cuda":
-                torch.cuda.current_stream().synchronize()
-            if spec and self.policy.cost is not None:
-                self.lagged_scores = self.host_scores.tolist()
-            if self._pending_timing is not None:
-                b_, w_, c_, ev, nsteps = self._pending_timing
-                verify_us, draft_us = ev[1].elapsed_us(ev[2]), ev[0].elapsed_us(ev[1])
-                if self.target.tp is not None:  # every rank must record the same costs to decide alike
-                    verify_us, draft_us = self.target.tp.max_over_ranks([verify_us, draft_us])
-                self.policy.record(b_, w_, c_, verify_us, nsteps, draft_us, settled=not self._captured)
-            got = []
+            taken, counts = self.serve_round(bs, sum(ctx) // bs, speculative=speculative,
+                                             room=[max_new_tokens - len(o) for o in outs])
             for b in range(bs):
-                c = int(self.host_cnt[b])
-                room = max_new_tokens - len(outs[b])
-                take = min(c, room)
-                outs[b].extend(self.host_tok[b, :take].tolist())
-                ctx[b] += c
-                got.append(take)
-            if spec:
-                self.stats.record(got)
-            if self.recorder is not None:
-                kind = "plain" if not spec else ("native" if choice == ServedTreeChoice.NATIVE else
-                                                 ("chain" if chain_t0 is not None else "tree"))
-                t_us = tree_t0.elapsed_us(tree_t1) if tree_t0 is not None else (
-                    chain_t0.elapsed_us(chain_t1) if chain_t0 is not None else None)
-                self.recorder.record(bs=bs, kind=kind, depth=self.last_depth if spec else 0,
-                                     width=self.last_width if spec else 1, tokens=got, round_us=t_us)
-            if tree_t0 is not None:
-                us = tree_t0.elapsed_us(tree_t1)
-                if self.target.tp is not None:
-                    us = self.target.tp.max_over_ranks([us])[0]
-                self.tree_choice.record(bs, choice, us, sum(got) / len(got), settled=not self._captured)
-            if chain_t0 is not None:
-                us = chain_t0.elapsed_us(chain_t1)
-                if self.target.tp is not None:
-                    us = self.target.tp.max_over_ranks([us])[0]
-                self.chain_policy.record(bs, chain_w, us, sum(got) / len(got), settled=not self._captured)
+                outs[b].extend(taken[b])
+                ctx[b] += counts[b]
         marks[2].record()
         if self.device.type == "cuda":
             torch.cuda.current_stream().synchronize()

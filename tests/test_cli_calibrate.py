@@ -68,17 +68,25 @@ def test_serve_app_round_trip():
     from eagle4_b200.serve import Batcher, make_app
 
     llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_batch=2, max_len=256)
-    b = Batcher(llm.engine, 2)
+    prompt = list(range(1, 20))
+    b = Batcher(llm.engine)
     try:
         client = TestClient(make_app(b))
-        r = client.post("/v1/generate", json={"prompt_ids": list(range(1, 20)), "max_new_tokens": 6})
-        assert r.status_code == 200 and len(r.json()["output_ids"]) == 6
-        plain = client.post("/v1/generate", json={"prompt_ids": list(range(1, 20)), "max_new_tokens": 6,
-                                                  "speculative": False})
-        assert plain.json()["output_ids"] == r.json()["output_ids"]
+        r = client.post("/v1/generate", json={"prompt_ids": prompt, "max_new_tokens": 6})
+        assert r.status_code == 200 and r.json()["finish_reason"] == "length"
+        out = r.json()["output_ids"]
+        assert len(out) == 6
+        stop = out[2]
+        s = client.post("/v1/generate", json={"prompt_ids": prompt, "max_new_tokens": 6, "stop_token_ids": [stop]})
+        assert s.json()["finish_reason"] == "stop"
+        assert s.json()["output_ids"] == out[:out.index(stop) + 1]
+        assert client.post("/v1/generate", json={"prompt_ids": [], "max_new_tokens": 6}).status_code in (400, 422)
         assert client.get("/health").json()["rounds"] >= 1
     finally:
         b.stop.set()
+        b.thread.join()
+    plain = llm.generate([torch.tensor(prompt)], 6, speculative=False)[0].tolist()
+    assert plain == out
 
 
 def test_chain_calibration_on_cpu(tmp_path):

@@ -1,0 +1,110 @@
+"""Continuous batching (runtime/scheduler.py): admission between rounds, retirement on per-request stop conditions,
+page-budget waits, padded graph buckets. Greedy outputs must not depend on the batch a request shares rounds with,
+so every request's tokens equal its tokens generated alone."""
+
+import pytest
+import torch
+
+from eagle4_b200.api import LLM, TreeSpec
+from eagle4_b200.runtime.pages import OutOfPages
+from eagle4_b200.runtime.scheduler import RequestParams, Scheduler
+
+
+def _llm(max_batch=2, **kw):
+    return LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_batch=max_batch,
+                         max_len=256, **kw)
+
+
+def _prompts(n, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randint(1, 4096, (int(torch.randint(5, 40, (1,), generator=g)),), generator=g) for _ in range(n)]
+
+
+def _alone(llm, prompt, n, speculative):
+    return llm.generate([prompt], n, speculative=speculative)[0].tolist()
+
+
+@pytest.mark.parametrize("speculative", [True, False])
+def test_continuous_batching_matches_each_request_alone(speculative):
+    llm = _llm(max_batch=2)
+    prompts = _prompts(5)
+    lens = [7, 3, 11, 5, 9]
+    alone = [_alone(llm, p, n, False) for p, n in zip(prompts, lens)]
+    sched = Scheduler(llm.engine, speculative=speculative)
+    reqs = [sched.submit(p, RequestParams(max_new_tokens=n)) for p, n in zip(prompts, lens)]
+    seen_batches = set()
+    while not sched.idle:
+        sched.step()
+        seen_batches.add(len(sched.running))
+        assert len(sched.running) <= 2
+    for r, want, n in zip(reqs, alone, lens):
+        assert r.finish_reason == "length" and r.output == want, (r.rid, r.output, want)
+    assert sorted(sched.free_slots) == [0, 1] and llm.engine.pages.free_pages == llm.engine.pages.num_pages - 1
+
+
+def test_stop_conditions_per_request():
+    llm = _llm(max_batch=4)
+    prompts = _prompts(4, seed=1)
+    free = [_alone(llm, p, 12, False) for p in prompts]
+    sched = Scheduler(llm.engine)
+    stop_tok = free[0][4]
+    eos = free[1][3]
+    reqs = [
+        sched.submit(prompts[0], RequestParams(max_new_tokens=12, stop_token_ids=(stop_tok,))),
+        sched.submit(prompts[1], RequestParams(max_new_tokens=12, eos_token_id=eos)),
+        sched.submit(prompts[2], RequestParams(max_new_tokens=12, eos_token_id=eos, ignore_eos=True)),
+        sched.submit(prompts[3], RequestParams(max_new_tokens=12)),
+    ]
+    sched.run()
+    assert reqs[0].finish_reason == "stop" and reqs[0].output == free[0][:free[0].index(stop_tok) + 1]
+    assert reqs[1].finish_reason == "eos" and reqs[1].output == free[1][:free[1].index(eos) + 1]
+    # one request's stop set never ends another: ignore_eos runs to its length, the plain one too
+    assert reqs[2].finish_reason == "length" and reqs[2].output == free[2]
+    assert reqs[3].finish_reason == "length" and reqs[3].output == free[3]
+
+
+def test_stop_strings_need_a_detokenizer_and_end_on_the_string():
+    llm = _llm(max_batch=1)
+    p = _prompts(1, seed=2)[0]
+    free = _alone(llm, p, 10, False)
+    with pytest.raises(ValueError):
+        Scheduler(llm.engine).submit(p, RequestParams(max_new_tokens=10, stop=("x",)))
+    detok = lambda ids: " ".join(str(t) for t in ids)  # noqa: E731
+    sched = Scheduler(llm.engine, detokenize=detok)
+    r = sched.submit(p, RequestParams(max_new_tokens=10, stop=(str(free[5]),)))
+    sched.run()
+    assert r.finish_reason == "stop" and str(free[5]) in detok(r.output) and len(r.output) <= 6
+
+
+def test_admission_waits_for_pages_and_refuses_what_never_fits():
+    # room for one request at a time: the second waits for the first to release its pages
+    prompts = _prompts(2, seed=3)
+    span = 9  # one round's tree rows: max(verify tokens, steps * top-k) + 1
+    pages = [-(-(int(p.numel()) + 8 + span) // 16) for p in prompts]
+    llm = _llm(max_batch=2, kv_tokens=16 * max(pages))
+    assert llm.engine.span == span and llm.engine.pages.free_pages < sum(pages)
+    alone = [_alone(llm, p, 8, False) for p in prompts]
+    sched = Scheduler(llm.engine)
+    reqs = [sched.submit(p, RequestParams(max_new_tokens=8)) for p in prompts]
+    sched.step()
+    assert len(sched.running) == 1 and len(sched.waiting) == 1
+    sched.run()
+    assert [r.output for r in reqs] == alone
+    small = _llm(max_batch=1, kv_tokens=16)  # two pages besides the trash page
+    s2 = Scheduler(small.engine)
+    s2.submit(prompts[0], RequestParams(max_new_tokens=64))
+    with pytest.raises(OutOfPages):
+        s2.step()
+
+
+def test_padded_bucket_rounds_match():
+    # 9 running requests replay the graph bucket of 10 (the calibration grid has no 9): the padding row must not
+    # disturb the real rows
+    llm = _llm(max_batch=10)
+    assert llm.engine.bucket(9) == 10 and llm.engine.bucket(8) == 8
+    prompts = _prompts(9, seed=4)
+    alone = [_alone(llm, p, 4, False) for p in prompts]
+    sched = Scheduler(llm.engine)
+    reqs = [sched.submit(p, RequestParams(max_new_tokens=4)) for p in prompts]
+    sched.run()
+    assert [r.output for r in reqs] == alone
