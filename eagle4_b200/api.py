@@ -24,6 +24,10 @@ from eagle4_b200.runtime.engine import Engine
 NAMED = {
     "tiny": (configs.tiny_hybrid, configs.tiny_draft),
     "tiny-mamba": (configs.tiny_nemotron, lambda t: dataclasses.replace(configs.tiny_draft(t), aux_layer_ids=(1, 3, 5))),
+    # attn_norm input fusion + latent ReLU^2 MoE draft (the Nemotron-class draft structures)
+    "tiny-moe": (configs.tiny_nemotron, lambda t: dataclasses.replace(configs.tiny_moe_draft(t),
+                                                                      aux_layer_ids=(1, 3, 5))),
+    "nemotron-h-8b-moe": (configs.nemotron_h_8b, configs.nemotron_moe_draft),
     "qwen3.8-27b": (configs.qwen38_27b, configs.qwen38_draft),
     "nemotron-h-8b": (configs.nemotron_h_8b, lambda t: configs.generic_draft(t, heads=32, kv=8, head_dim=128)),
     "llama-3.1-8b": (configs.llama31_8b, configs.eagle3_llama_draft),

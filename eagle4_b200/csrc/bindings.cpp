@@ -3,6 +3,8 @@
 
 namespace e4 {
 torch::Tensor gemm_error_word(torch::Device dev);
+torch::Tensor moe_experts(const torch::Tensor& latent, const torch::Tensor& chosen, const torch::Tensor& weights,
+                          const torch::Tensor& up, const torch::Tensor& down);
 void gemm_launch(const torch::Tensor& x, const torch::Tensor& w, int epi, torch::Tensor y, torch::Tensor yf,
                  const torch::Tensor& res, torch::Tensor amax_val, torch::Tensor amax_idx, double fold_eps);
 torch::Tensor rmsnorm(const torch::Tensor& x, const torch::Tensor& w, double eps, bool offset);
@@ -138,4 +140,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tree_step", &e4::tree_step);
   m.def("tree_begin", &e4::tree_begin);
   m.def("select_rows", &e4::select_rows);
+  m.def("moe_experts", &e4::moe_experts);
 }

@@ -180,6 +180,12 @@ class DraftConfig:
     use_rope: bool = True
     low_rank: Optional[dict] = None  # {"type": "low_rank", "rank": r, "num_candidates": c}
     init_std: float = 0.02
+    # MTP-style input fusion: eh_proj maps concat(normed embed, normed hidden) to H; that projection is the
+    # attention residual and its RMSNorm (pre_attention_layernorm) feeds q/k/v
+    attn_norm: bool = False
+    # latent ReLU^2 MoE MLP (Nemotron-H block): {"experts", "top_k", "inter", "latent", "shared_inter",
+    # "n_group", "topk_group", "norm_topk_prob", "scale"}; None is the dense SwiGLU MLP
+    moe: Optional[dict] = None
 
     @property
     def num_aux(self) -> int:
@@ -214,6 +220,17 @@ class DraftConfig:
             d.update(use_sliding_window=False, layer_types=["full_attention"])
         if self.low_rank:
             d["efficient_lm_head_config"] = dict(self.low_rank)
+        if self.attn_norm:
+            d["attn_norm"] = True
+        if self.moe:
+            m = self.moe
+            d.update(enable_moe=True, moe_architecture="nemotron_latent_relu2", hidden_act="relu2",
+                     n_routed_experts=m["experts"], num_experts_per_tok=m["top_k"], moe_intermediate_size=m["inter"],
+                     moe_latent_size=m["latent"], n_shared_experts=1 if m.get("shared_inter") else 0,
+                     moe_shared_expert_intermediate_size=m.get("shared_inter") or None, n_group=m.get("n_group", 1),
+                     topk_group=m.get("topk_group", 1), norm_topk_prob=bool(m.get("norm_topk_prob", True)),
+                     routed_scaling_factor=float(m.get("scale", 1.0)), scoring_func="sigmoid",
+                     topk_method="noaux_tc")
         return d
 
 
@@ -266,6 +283,30 @@ def tiny_draft(target: TargetConfig, draft_vocab: int = 1024) -> DraftConfig:
         intermediate_size=512, aux_layer_ids=(1, 2, 3), sliding_window=None, rope_theta=1e7,
         low_rank={"type": "low_rank", "rank": 32, "num_candidates": 32},
     )
+
+
+def latent_moe(experts: int, top_k: int, inter: int, latent: int, shared_inter: int, *, n_group: int = 1,
+               topk_group: int = 1, norm_topk_prob: bool = True, scale: float = 1.0) -> dict:
+    return {"experts": experts, "top_k": top_k, "inter": inter, "latent": latent, "shared_inter": shared_inter,
+            "n_group": n_group, "topk_group": topk_group, "norm_topk_prob": norm_topk_prob, "scale": scale}
+
+
+def tiny_moe_draft(target: TargetConfig) -> DraftConfig:
+    """CPU-sized EAGLE-4 draft with both Nemotron draft structures: attn_norm input fusion and a latent ReLU^2 MoE
+    (16 experts, 4 per token in 2 groups, latent 64, shared expert)."""
+    import dataclasses
+
+    return dataclasses.replace(tiny_draft(target), attn_norm=True,
+                               moe=latent_moe(16, 4, 96, 64, 128, n_group=2, topk_group=2, scale=2.5))
+
+
+def nemotron_moe_draft(target: TargetConfig) -> DraftConfig:
+    """A Nemotron-class EAGLE-4 draft shape: attn_norm fusion and a latent ReLU^2 MoE MLP (512 experts, 22 per token,
+    latent 1024, expert FFN 2688, shared expert 5376, routed scale 5)."""
+    import dataclasses
+
+    return dataclasses.replace(generic_draft(target), attn_norm=True,
+                               moe=latent_moe(512, 22, 2688, 1024, 5376, scale=5.0))
 
 
 def tiny_nemotron() -> TargetConfig:

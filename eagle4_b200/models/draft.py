@@ -84,18 +84,29 @@ class DraftModel:
         eps = cfg.rms_norm_eps
         e = ops.embedding(ids, w["embed"])
         x = ops.concat_norms(e, hidden, w["input_layernorm"], w["hidden_norm"], eps)
+        res = hidden
+        if cfg.attn_norm:  # eh_proj input fusion: the projection is the attention residual, its norm feeds q/k/v
+            res = ops.linear(x, w["eh_proj"])
+            x = ops.rmsnorm(res, w["pre_attention_layernorm"], eps, False)
         qkv = ops.linear(x, w["qkv"])
         q, _ = ops.qkv_prepare(qkv, self.attn_shape, pos, write_slot, cache.k, cache.v, None, None)
         o = ops.attention(q, cache.k, cache.v, cache.block_table, cache.page, req, ctx_start, ctx_len, extra,
                           n_extra, cfg.head_dim ** -0.5, max_keys)
         if self.tp is not None:
-            residual, x = self.tp.row_linear(o, w["o_proj"], hidden, w["post_attention_layernorm"], eps)
-            summed, normed = self.tp.row_linear(ops.linear_swiglu(x, w["gate_up"]), w["down"], residual, w["norm"],
-                                                eps)
+            residual, x = self.tp.row_linear(o, w["o_proj"], res, w["post_attention_layernorm"], eps)
+            if cfg.moe:  # the MoE is replicated on every rank: no collective after it
+                summed = ops.latent_moe(x, w, cfg.moe, residual)
+                normed = ops.rmsnorm(summed, w["norm"], eps, False)
+            else:
+                summed, normed = self.tp.row_linear(ops.linear_swiglu(x, w["gate_up"]), w["down"], residual,
+                                                    w["norm"], eps)
         else:
-            residual = ops.linear_residual(o, w["o_proj"], hidden)
+            residual = ops.linear_residual(o, w["o_proj"], res)
             x = ops.rmsnorm(residual, w["post_attention_layernorm"], eps, False)
-            summed = ops.linear_residual(ops.linear_swiglu(x, w["gate_up"]), w["down"], residual)
+            if cfg.moe:
+                summed = ops.latent_moe(x, w, cfg.moe, residual)
+            else:
+                summed = ops.linear_residual(ops.linear_swiglu(x, w["gate_up"]), w["down"], residual)
             normed = ops.rmsnorm(summed, w["norm"], eps, False)
         return normed, (normed if cfg.norm_output else summed)
 

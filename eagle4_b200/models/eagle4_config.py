@@ -167,20 +167,39 @@ def validate_eagle4_draft_config(config) -> None:
                          f"num_hidden_layers={cfg.get('num_hidden_layers')}.")
 
 
-# Structures the validator accepts that this package's draft model does not build.
-UNBUILT = {"enable_moe": True, "attn_norm": True, "enable_post_mlp_norm": True}
+# Structures the validator accepts that this package's draft model does not build (none of the reference's engine
+# adapters builds them either: eagle_harness/models/eagle4_config.py:259-266, sglang/models/llama_eagle4.py:91-100).
+UNBUILT = {"enable_post_mlp_norm": True}
 
 
 def check_supported(config) -> None:
-    """Validate, then refuse structures the draft model does not build (MoE drafts, eh_proj fusion, post-MLP norm,
-    more than one layer)."""
+    """Validate, then refuse structures the draft model does not build: the post-MLP norm, the sparse SwiGLU MoE,
+    more than one layer. attn_norm (eh_proj input fusion), NoPE and the latent ReLU^2 MoE are built."""
     cfg = _as_dict(config)
     validate_eagle4_draft_config(cfg)
     used = [f"{k}={v!r}" for k, v in UNBUILT.items() if cfg.get(k) == v]
     if used:
-        raise NotImplementedError(f"EAGLE-4 drafts with {used} are not built by eagle4_b200 (dense drafts only).")
+        raise NotImplementedError(f"EAGLE-4 drafts with {used} are not built by eagle4_b200.")
+    moe = draft_moe_architecture(cfg)
+    if moe not in (None, LATENT_MOE):
+        raise NotImplementedError(f"EAGLE-4 drafts with the {moe!r} MoE are not built by eagle4_b200 (the latent "
+                                  "ReLU^2 MoE is).")
     if cfg.get("num_hidden_layers") != 1:
         raise NotImplementedError(f"EAGLE-4 drafts with {cfg.get('num_hidden_layers')} layers are not built (1 only).")
+
+
+def _moe_of(cfg: dict) -> Optional[dict]:
+    if draft_moe_architecture(cfg) != LATENT_MOE:
+        return None
+    from eagle4_b200.models.configs import latent_moe
+
+    groups = int(cfg.get("n_group") or 1)
+    return latent_moe(int(cfg["n_routed_experts"]), int(cfg["num_experts_per_tok"]), int(cfg["moe_intermediate_size"]),
+                      int(cfg["moe_latent_size"]),
+                      int(cfg.get("moe_shared_expert_intermediate_size") or 0) if cfg.get("n_shared_experts") else 0,
+                      n_group=groups, topk_group=int(cfg.get("topk_group") or groups),
+                      norm_topk_prob=bool(cfg.get("norm_topk_prob", True)),
+                      scale=float(cfg.get("routed_scaling_factor") or 1.0))
 
 
 def draft_config_from_hf(config, *, target_vocab_size: Optional[int] = None) -> DraftConfig:
@@ -206,4 +225,5 @@ def draft_config_from_hf(config, *, target_vocab_size: Optional[int] = None) -> 
         sliding_window=resolve_draft_sliding_window(cfg) if eagle4 else None,
         fc_norm=bool(cfg.get("fc_norm") or cfg.get("enable_fc_norm")), norm_output=bool(cfg.get("norm_output")),
         use_rope=draft_uses_rope(cfg), low_rank=dict(head) if head else None,
+        attn_norm=bool(cfg.get("attn_norm")) if eagle4 else False, moe=_moe_of(cfg) if eagle4 else None,
     )

@@ -105,11 +105,27 @@ def init_draft(cfg: DraftConfig, *, device="cpu", dtype=torch.float32, seed: int
     w["input_layernorm"] = ones(H)
     w["hidden_norm"] = ones(H)
     qkv_rows = (cfg.num_heads + 2 * cfg.num_kv_heads) * cfg.head_dim
-    w["qkv"] = lin(qkv_rows, 2 * H)
+    if cfg.attn_norm:
+        w["eh_proj"] = lin(H, 2 * H)
+        w["pre_attention_layernorm"] = ones(H)
+    w["qkv"] = lin(qkv_rows, H if cfg.attn_norm else 2 * H)
     w["o_proj"] = lin(H, cfg.num_heads * cfg.head_dim)
     w["post_attention_layernorm"] = ones(H)
-    w["gate_up"] = lin(2 * cfg.intermediate_size, H)
-    w["down"] = lin(H, cfg.intermediate_size)
+    if cfg.moe:
+        m = cfg.moe
+        E, L, F = m["experts"], m["latent"], m["inter"]
+        w["moe_gate"] = _normal((E, H), std, gen, dev, torch.float32)
+        w["moe_bias"] = _normal((E,), std, gen, dev, torch.float32)
+        w["fc1_latent"] = lin(L, H)
+        w["fc2_latent"] = lin(H, L)
+        w["experts_up"] = _normal((E, F, L), std, gen, dev, dtype)
+        w["experts_down"] = _normal((E, L, F), std, gen, dev, dtype)
+        if m.get("shared_inter"):
+            w["shared_up"] = lin(m["shared_inter"], H)
+            w["shared_down"] = lin(H, m["shared_inter"])
+    else:
+        w["gate_up"] = lin(2 * cfg.intermediate_size, H)
+        w["down"] = lin(H, cfg.intermediate_size)
     w["norm"] = ones(H)
     if lm_head is not None and cfg.draft_vocab_size == lm_head.shape[0]:
         w["lm_head"] = lm_head
@@ -163,8 +179,6 @@ def draft_state_dict(cfg: DraftConfig, w: Dict[str, torch.Tensor]) -> Dict[str, 
     """Runtime draft weights in the released safetensors names."""
     H = cfg.hidden_size
     qd, kd = cfg.num_heads * cfg.head_dim, cfg.num_kv_heads * cfg.head_dim
-    F = cfg.intermediate_size
-    gu = w["gate_up"].view(F // 64, 2, 64, H)
     sd = {
         "fc.weight": w["fc"],
         "layers.0.input_layernorm.weight": w["input_layernorm"],
@@ -174,12 +188,28 @@ def draft_state_dict(cfg: DraftConfig, w: Dict[str, torch.Tensor]) -> Dict[str, 
         "layers.0.self_attn.v_proj.weight": w["qkv"][qd + kd:],
         "layers.0.self_attn.o_proj.weight": w["o_proj"],
         "layers.0.post_attention_layernorm.weight": w["post_attention_layernorm"],
-        "layers.0.mlp.gate_proj.weight": gu[:, 0].reshape(F, H),
-        "layers.0.mlp.up_proj.weight": gu[:, 1].reshape(F, H),
-        "layers.0.mlp.down_proj.weight": w["down"],
         "norm.weight": w["norm"],
         "lm_head.weight": w["lm_head"],
     }
+    if cfg.attn_norm:
+        sd["layers.0.eh_proj.weight"] = w["eh_proj"]
+        sd["layers.0.pre_attention_layernorm.weight"] = w["pre_attention_layernorm"]
+    if cfg.moe:
+        p = "layers.0.mlp."
+        sd.update({p + "gate.weight": w["moe_gate"], p + "gate.e_score_correction_bias": w["moe_bias"],
+                   p + "fc1_latent_proj.weight": w["fc1_latent"], p + "fc2_latent_proj.weight": w["fc2_latent"]})
+        for e in range(cfg.moe["experts"]):
+            sd[f"{p}experts.{e}.up_proj.weight"] = w["experts_up"][e]
+            sd[f"{p}experts.{e}.down_proj.weight"] = w["experts_down"][e]
+        if "shared_up" in w:
+            sd[p + "shared_experts.up_proj.weight"] = w["shared_up"]
+            sd[p + "shared_experts.down_proj.weight"] = w["shared_down"]
+    else:
+        F = cfg.intermediate_size
+        gu = w["gate_up"].view(F // 64, 2, 64, H)
+        sd["layers.0.mlp.gate_proj.weight"] = gu[:, 0].reshape(F, H)
+        sd["layers.0.mlp.up_proj.weight"] = gu[:, 1].reshape(F, H)
+        sd["layers.0.mlp.down_proj.weight"] = w["down"]
     for j in range(cfg.num_aux):
         if f"fc_norm.{j}" in w:
             sd[f"fc_norm.{j}.weight"] = w[f"fc_norm.{j}"]
@@ -204,11 +234,27 @@ def draft_from_state_dict(cfg: DraftConfig, sd: Dict[str, torch.Tensor], *, embe
                           g("layers.0.self_attn.v_proj.weight")]),
         "o_proj": g("layers.0.self_attn.o_proj.weight"),
         "post_attention_layernorm": g("layers.0.post_attention_layernorm.weight"),
-        "gate_up": interleave_gate_up(g("layers.0.mlp.gate_proj.weight"), g("layers.0.mlp.up_proj.weight")),
-        "down": g("layers.0.mlp.down_proj.weight"),
         "norm": g("norm.weight"),
         "lm_head": g("lm_head.weight"),
     }
+    if cfg.attn_norm:
+        w["eh_proj"] = g("layers.0.eh_proj.weight")
+        w["pre_attention_layernorm"] = g("layers.0.pre_attention_layernorm.weight")
+    if cfg.moe:
+        p = "layers.0.mlp."
+        E = cfg.moe["experts"]
+        w["moe_gate"] = g(p + "gate.weight").float()
+        w["moe_bias"] = g(p + "gate.e_score_correction_bias").float()
+        w["fc1_latent"] = g(p + "fc1_latent_proj.weight")
+        w["fc2_latent"] = g(p + "fc2_latent_proj.weight")
+        w["experts_up"] = torch.stack([g(f"{p}experts.{e}.up_proj.weight") for e in range(E)])
+        w["experts_down"] = torch.stack([g(f"{p}experts.{e}.down_proj.weight") for e in range(E)])
+        if p + "shared_experts.up_proj.weight" in sd:
+            w["shared_up"] = g(p + "shared_experts.up_proj.weight")
+            w["shared_down"] = g(p + "shared_experts.down_proj.weight")
+    else:
+        w["gate_up"] = interleave_gate_up(g("layers.0.mlp.gate_proj.weight"), g("layers.0.mlp.up_proj.weight"))
+        w["down"] = g("layers.0.mlp.down_proj.weight")
     for j in range(cfg.num_aux):
         if f"fc_norm.{j}.weight" in sd:
             w[f"fc_norm.{j}"] = sd[f"fc_norm.{j}.weight"]

@@ -213,3 +213,21 @@ def advance_round(round_ctr):
         _nat().advance_round(round_ctr)
     else:
         round_ctr += 1
+
+
+# latent MoE MLP ---------------------------------------------------------------------------------------------------
+def latent_moe(x: torch.Tensor, w: dict, moe: dict, residual: torch.Tensor) -> torch.Tensor:
+    """``residual + fc2_latent(routed) + shared(x)`` of a latent ReLU^2 MoE (the Nemotron-H block a Nemotron-class
+    EAGLE-4 draft uses): fp32 sigmoid router with bias-corrected choice, the routed experts in the latent space
+    between ``fc1_latent`` and ``fc2_latent`` weighted by ``scale`` times the routing weights, plus the ReLU^2 shared
+    expert (``eagle_harness/sglang/models/llama_eagle4.py:125-145``)."""
+    chosen, wts = ref.moe_route(x, w["moe_gate"], w["moe_bias"], moe["top_k"], moe.get("n_group", 1),
+                                moe.get("topk_group", 1), moe.get("norm_topk_prob", True))
+    wts = wts * float(moe.get("scale", 1.0))
+    latent = linear(x, w["fc1_latent"])
+    experts = _nat().moe_experts if _cuda(x) else ref.moe_experts
+    routed = experts(latent, chosen, wts, w["experts_up"], w["experts_down"])
+    out = linear_residual(routed, w["fc2_latent"], residual)
+    if "shared_up" in w:
+        out = linear_residual(linear_relu2(x, w["shared_up"]), w["shared_down"], out)
+    return out

@@ -19,7 +19,8 @@ CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 NAME = "_e4"
 
-SOURCES = ["bindings.cpp", "gemm.cu", "kernels.cu", "attention.cu", "recurrent.cu", "tree.cu", "comm.cu", "sampled.cu"]
+SOURCES = ["bindings.cpp", "gemm.cu", "kernels.cu", "attention.cu", "recurrent.cu", "tree.cu", "comm.cu", "sampled.cu",
+           "moe.cu"]
 
 CUDA_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -103,6 +103,12 @@ def linear_relu2(x: torch.Tensor, w: torch.Tensor, fold_eps: Optional[float] = N
     return y
 
 
+def moe_experts(latent: torch.Tensor, chosen: torch.Tensor, weights: torch.Tensor, up: torch.Tensor,
+                down: torch.Tensor) -> torch.Tensor:
+    """Routed latent-MoE experts: route by expert, grouped up / down GEMVs, weighted mix (``csrc/moe.cu``)."""
+    return _C.moe_experts(latent.contiguous(), chosen, weights, up, down)
+
+
 def logits(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     x = _c2(x)
     y = torch.empty(x.shape[0], w.shape[0], dtype=torch.float32, device=x.device)

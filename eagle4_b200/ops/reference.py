@@ -494,3 +494,40 @@ def gdn_commit_all(convs, projs, states, conv_states, a_logs, dt_biases, slots, 
     for conv, proj, st, cs, al, dtb in zip(convs, projs, states, conv_states, a_logs, dt_biases):
         g, beta = gdn_gates(proj[:, a_off: a_off + hv], proj[:, b_off: b_off + hv], al, dtb)
         gdn_commit(conv, g, beta, proj[:, : cfg.gdn_conv_dim], st, cs, slots, rows, n_rows, cfg)
+
+
+# latent MoE (EAGLE-4 Nemotron-class drafts) --------------------------------------------------------------------
+def moe_route(x: torch.Tensor, gate: torch.Tensor, bias: torch.Tensor, top_k: int, n_group: int = 1,
+              topk_group: int = 1, norm_topk_prob: bool = True) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Sigmoid router over bias-corrected scores, in fp32: experts are chosen by ``sigmoid(x gate^T) + bias`` (with
+    ``n_group`` > 1 only inside the ``topk_group`` groups whose two best biased scores sum highest), weighted by their
+    unbiased scores, renormalised over the chosen when ``norm_topk_prob``. Returns (chosen [T, k] int64, best first;
+    weights [T, k] fp32)."""
+    scores = torch.sigmoid(x.float() @ gate.float().t())
+    biased = scores + bias.float()
+    if n_group > 1:
+        T, E = biased.shape
+        per = E // n_group
+        group_score = biased.view(T, n_group, per).topk(min(2, per), dim=-1).values.sum(-1)
+        keep = torch.zeros(T, n_group, dtype=torch.bool, device=x.device)
+        keep.scatter_(1, group_score.topk(topk_group, dim=-1).indices, True)
+        biased = biased.masked_fill(~keep.repeat_interleave(per, dim=1), float("-inf"))
+    chosen = biased.topk(top_k, dim=-1).indices
+    w = scores.gather(1, chosen)
+    if norm_topk_prob:
+        w = w / w.sum(-1, keepdim=True)
+    return chosen, w
+
+
+def moe_experts(latent: torch.Tensor, chosen: torch.Tensor, weights: torch.Tensor, up: torch.Tensor,
+                down: torch.Tensor) -> torch.Tensor:
+    """``sum_j weights[t, j] down_e (relu(up_e latent_t)^2)`` over each token's chosen experts e (j in routing order);
+    the ReLU^2 activations are rounded to the latent's dtype, as the kernel stores them."""
+    lat = latent.float()
+    out = torch.zeros(latent.shape[0], latent.shape[1], dtype=torch.float32, device=latent.device)
+    for j in range(chosen.shape[1]):
+        e = chosen[:, j].long()
+        h = torch.relu(torch.einsum("tfl,tl->tf", up[e].float(), lat)) ** 2
+        h = h.to(latent.dtype).float()
+        out = out + weights[:, j:j + 1].float() * torch.einsum("tlf,tf->tl", down[e].float(), h)
+    return out.to(latent.dtype)

@@ -154,6 +154,8 @@ def local_draft_config(cfg: DraftConfig, world: int, rank: int) -> DraftConfig:
     if world == 1:
         return cfg
     kv, _ = kv_layout(cfg.num_heads, cfg.num_kv_heads, world, rank)
+    if cfg.moe:  # a latent-MoE MLP is replicated (its output needs no collective)
+        return dataclasses.replace(cfg, num_heads=cfg.num_heads // world, num_kv_heads=kv)
     _check(cfg.intermediate_size % (world * MLP_BLOCK) == 0,
            f"draft intermediate size {cfg.intermediate_size} does not split over {world} ranks")
     return dataclasses.replace(cfg, num_heads=cfg.num_heads // world, num_kv_heads=kv,
@@ -162,7 +164,8 @@ def local_draft_config(cfg: DraftConfig, world: int, rank: int) -> DraftConfig:
 
 def shard_draft(cfg: DraftConfig, w: Dict[str, torch.Tensor], world: int, rank: int
                 ) -> Tuple[DraftConfig, Dict[str, torch.Tensor]]:
-    """The draft layer is sharded like a target attention + MLP layer; ``fc``, norms and the head are replicated."""
+    """The draft layer is sharded like a target attention + MLP layer; ``fc``, ``eh_proj``, norms, the head and a
+    latent-MoE MLP are replicated."""
     if world == 1:
         return cfg, w
     loc = local_draft_config(cfg, world, rank)
@@ -175,6 +178,8 @@ def shard_draft(cfg: DraftConfig, w: Dict[str, torch.Tensor], world: int, rank: 
     out["qkv"] = _rows(w["qkv"], [(q0, q0 + hl * d), (off + kv0 * d, off + (kv0 + nkv) * d),
                                   (off + hk * d + kv0 * d, off + hk * d + (kv0 + nkv) * d)])
     out["o_proj"] = _cols(w["o_proj"], q0, q0 + hl * d)
+    if cfg.moe:
+        return loc, out
     il = cfg.intermediate_size // world
     out["gate_up"] = w["gate_up"][2 * rank * il:2 * (rank + 1) * il].contiguous()
     out["down"] = _cols(w["down"], rank * il, (rank + 1) * il)
