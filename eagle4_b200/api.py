@@ -55,6 +55,7 @@ class LLM:
         None is the static tree of ``tree``. ``temperature > 0`` samples (sampled trees with tree rejection)."""
         if isinstance(config, str):
             config = parse_harness_config(config)
+        config = _with_packaged_profile(config, target, draft)
         self.target, self.draft, self.tree = target, draft, tree
         self.engine = Engine(target, draft, max_reqs=max_batch, max_len=max_len, page=page, steps=tree.steps,
                              top_k=tree.top_k, verify_tokens=tree.draft_tokens, config=config,
@@ -95,6 +96,24 @@ class LLM:
         dev_ids = prompt_ids.to(self.target.device, non_blocking=True)
         out = self.engine.generate(dev_ids, max_new_tokens, speculative=speculative)
         return torch.tensor(out, dtype=torch.int64)
+
+
+def _with_packaged_profile(config: Optional[HarnessConfig], target: TargetModel,
+                           draft: Optional[DraftModel]) -> Optional[HarnessConfig]:
+    """A serve-mode config without calibration data takes the packaged cost profile measured on this setup (same
+    GPU, TP size and model shapes), when one ships with the package; anything else is returned unchanged."""
+    if config is None or config.data_path or draft is None or not config.mode.uses_cost_model:
+        return config
+    if target.device.type != "cuda":
+        return config
+    from eagle4_b200.core.cost_profiles import packaged_cost_profile
+
+    if target.tp is not None and target.tp.world > 1:
+        return config  # the packaged profiles are measured on one GPU
+    path = packaged_cost_profile(device_name=torch.cuda.get_device_name(target.device), tp_size=1,
+                                 dtype="bfloat16", quantization=None, target_config=target.cfg.to_hf(),
+                                 draft_config=draft.cfg.to_hf())
+    return dataclasses.replace(config, data_path=path) if path else config
 
 
 def _load_safetensors_dir(path: str, device) -> dict:

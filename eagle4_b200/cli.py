@@ -87,6 +87,12 @@ def _calibrate(args) -> int:
         problems = calibrate(llm.engine, str(args.output), batch_sizes=args.batch_sizes,
                              context_step=args.context_step, context_stop=args.context_stop, repeats=args.repeats,
                              key=key)
+    if args.package:
+        from eagle4_b200.core.cost_profiles import write_profile
+
+        # the directory doubles as a packaged profile: matched by device, TP size and the models' shapes
+        write_profile(str(args.output), devices=[torch.cuda.get_device_name()], tp_size=1,
+                      target_config=llm.target.cfg.to_hf(), draft_config=llm.draft.cfg.to_hf())
     bad = {b: p for b, p in problems.items() if p}
     for b, p in bad.items():
         print(f"batch size {b}: the cost model refuses these costs ({p}); rounds there keep the fixed shape")
@@ -113,6 +119,8 @@ def main(argv: Optional[List[str]] = None) -> int:
     cal.add_argument("--kind", choices=("tree", "chain"), default="tree",
                      help="tree: cost tables from timed forwards; chain: served chain rounds and acceptance")
     cal.add_argument("--dry-run", action="store_true", help="print settings and the serving command only")
+    cal.add_argument("--package", action="store_true",
+                     help="also write profile.json so the directory can ship as a packaged cost profile")
     cal.set_defaults(func=_calibrate)
     chk = sub.add_parser("check", help="report the serving hosts and the native library")
     chk.add_argument("--kernels", action="store_true", help="also load the native CUDA library")
