@@ -136,7 +136,8 @@ class Engine:
         span = max(verify_tokens, steps * top_k) + 1
         self.max_len = max_len + span
         self.span = span
-        kv_pages = (kv_tokens if kv_tokens is not None else max_reqs * self.max_len) // page + 2  # + trash page
+        row_pages = -(-self.max_len // page)  # a row reaching max_len holds whole pages
+        kv_pages = (kv_tokens // page if kv_tokens is not None else max_reqs * row_pages) + 2  # + trash page
         # one cache row beyond the requests' rows: batch rows that pad a round up to its graph bucket use it (its
         # block-table row maps only the trash page, its recurrent state belongs to no request)
         self.pad_slot = max_reqs

@@ -10,6 +10,7 @@ test.
 """
 
 import ctypes
+import gc
 
 import pytest
 import torch
@@ -61,16 +62,25 @@ def test_noalloc_gemm_matches_regular_entry_point():
     x, w, y, _ = operands[0]
     assert _call(fn, x, w, y) == OK
     torch.cuda.synchronize()
-    for x, w, y, want in operands:
-        y.fill_(float("nan"))
-        torch.cuda.synchronize()
-        torch_before = torch.cuda.memory_allocated()
-        free_before, _ = torch.cuda.mem_get_info()
-        assert _call(fn, x, w, y) == OK
-        torch.cuda.synchronize()
-        assert torch.cuda.memory_allocated() == torch_before
-        assert torch.cuda.mem_get_info()[0] == free_before
-        assert _kernel_error(status) == 0
+    want_err = []
+    # garbage of earlier tests must not be collected (and freed) between the two readings
+    gc.collect()
+    gc.disable()
+    try:
+        for x, w, y, want in operands:
+            y.fill_(float("nan"))
+            torch.cuda.synchronize()
+            torch_before = torch.cuda.memory_allocated()
+            free_before, _ = torch.cuda.mem_get_info()
+            assert _call(fn, x, w, y) == OK
+            torch.cuda.synchronize()
+            assert torch.cuda.memory_allocated() == torch_before
+            assert torch.cuda.mem_get_info()[0] == free_before
+            want_err.append((x, w, y, want, _kernel_error(status)))
+    finally:
+        gc.enable()
+    for x, w, y, want, err_word in want_err:
+        assert err_word == 0
         assert torch.equal(y, want), "the allocation-free path must give the regular path's bits"
         ref = x.float() @ w.float().t()
         err = (y.float() - ref).abs().max().item()
