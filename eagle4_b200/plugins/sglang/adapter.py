@@ -249,6 +249,46 @@ class HarnessWorker(_Worker):
 
 
 class HarnessDraftWorker(_DraftWorker):
+    """The draft side of SGLang's rounds: this package's draft round (``plugins.host_round.HostDrafter``: draft KV,
+    pending rows, draft tree, round policy) over SGLang's requests. SGLang's target worker prefills and verifies;
+    ``forward_draft_extend`` takes each prefilled request, ``draft_round`` returns the round's verify rows, and
+    ``finish_round`` takes the accepted path (``eagle_harness/sglang/worker.py:532``, ``drafter.py:482``)."""
+
+    drafter = None
+
+    @classmethod
+    def for_drafter(cls, drafter) -> "HarnessDraftWorker":
+        """A worker around an existing drafter (no SGLang process state)."""
+        w = cls.__new__(cls)
+        w.drafter = drafter
+        return w
+
+    def forward_draft_extend(self, batch, aux_hidden_states, next_token_ids) -> None:
+        """After SGLang's prefill of ``batch``: each request's prompt rows (``aux_hidden_states``, the captured target
+        layers, rows in batch order) and first token enter the drafter."""
+        off = 0
+        for req, first in zip(batch.reqs, next_token_ids.tolist()):
+            n = len(req.origin_input_ids)
+            self.drafter.admit(req.rid, torch.as_tensor(req.origin_input_ids, dtype=torch.int64),
+                               aux_hidden_states[off:off + n], first)
+            off += n
+
+    def draft_round(self, batch) -> dict:
+        """The round's verify input: per request the committed root and the drafted rows chosen by the round policy
+        (tokens and parent rows, ``[bs, w]``)."""
+        rids = [req.rid for req in batch.reqs]
+        tokens, parents = self.drafter.propose(rids)
+        return {"width": int(tokens.shape[1]), "bs": len(rids), "rids": rids, "draft_tokens": tokens,
+                "parent_rows": parents}
+
+    def finish_round(self, spec: dict, accepted, counts, bonus, aux_hidden_states) -> List[List[int]]:
+        """The verify's outcome for ``spec``: the drafter takes the accepted path; returns each request's emitted
+        tokens."""
+        return self.drafter.accept(spec["rids"], spec["draft_tokens"], accepted, counts, bonus, aux_hidden_states)
+
+    def release(self, rid) -> None:
+        self.drafter.release(rid)
+
     def init_attention_backend(self) -> None:
         self.attention = "eagle4_b200.tree_attention"
 

@@ -44,6 +44,27 @@ class HarnessDrafter(_Eagle):
         depth = self.tree.shape.max_depth
         return self.tree.verify_rows(bs, depth, int(next_tokens) - 1)
 
+    # whole rounds: TokenSpeed may hand the draft round to this package (``plugins.host_round.HostDrafter``)
+    drafter = None
+
+    def attach(self, drafter) -> None:
+        self.drafter = drafter
+
+    def prefill_request(self, rid, prompt_ids, aux_hidden_states, first_token) -> None:
+        self.drafter.admit(rid, prompt_ids, aux_hidden_states, first_token)
+
+    def draft_round(self, rids):
+        """Extend, steps under the round policy and the verify selection: (tokens [bs, w], parent rows [bs, w])."""
+        return self.drafter.propose(rids)
+
+    def accept_round(self, rids, tokens, target_ids, parent_rows, aux_hidden_states):
+        """Greedy accept of the verified rows (target ids per row), then the accepted path to the drafter; returns
+        (accepted rows, counts, bonus, emitted tokens per request)."""
+        from eagle4_b200.plugins.common import accept_greedy_rows
+
+        acc, cnt, bonus = accept_greedy_rows(target_ids, tokens, parent_rows)
+        return acc, cnt, bonus, self.drafter.accept(rids, tokens, acc, cnt, bonus, aux_hidden_states)
+
     # the release engine's names for the same policy
     _seed_tree_lanes = seed_tree
     _expand_tree_lanes = expand_tree

@@ -1,5 +1,6 @@
 """The ``eagle_harness`` speculative method inside vLLM (Model Runner V2 builds carrying the speculative-method
-registry): method spec, speculator, tree accept and accepted-path KV compaction on this package's kernels.
+registry): method spec, speculator (draft rounds through ``plugins.host_round.HostDrafter``), tree accept (greedy and
+sampled) and accepted-path KV compaction on this package's kernels.
 
 Reference counterparts: ``eagle_harness/vllm/{plugin,speculator,tree_accept,round_commit,verify_layout}.py``. vLLM
 keeps scheduling, KV allocation and the target forward; the speculator drafts the tree (round policy + draft tree),
@@ -44,18 +45,69 @@ class HarnessMethodSpec(_MethodSpec):
 
 
 class TreeAccept:
-    """The rejection sampler vLLM calls on the verify logits: fused greedy accept (temperature 0) or the sampled
-    tree walk (temperature > 0; q store and node slots from the speculator's sampled draft)."""
+    """The rejection sampler vLLM calls on the verify rows: the fused greedy accept (temperature 0, on target ids or
+    logits), or with a sampling drafter the recursive tree rejection over the drafter's draw-order children and q
+    store (the target's logits at the engine's temperature; ``eagle_harness/vllm/tree_accept.py``)."""
 
-    def __init__(self, sampled_state=None):
-        self.sampled_state = sampled_state
+    def __init__(self, drafter=None):
+        self.drafter = drafter  # a HostDrafter (its engine keeps the round's q store and round counter)
 
-    def __call__(self, target_ids: torch.Tensor, draft_tokens: torch.Tensor, parent_rows: torch.Tensor):
-        return accept_greedy_rows(target_ids, draft_tokens, parent_rows)
+    def __call__(self, target: torch.Tensor, draft_tokens: torch.Tensor, parent_rows: torch.Tensor):
+        """``target``: ``[bs * w]`` target ids or ``[bs * w, V]`` logits. Returns (accepted rows [bs, w] (-1 pad),
+        counts [bs], bonus tokens [bs])."""
+        bs = draft_tokens.shape[0]
+        eng = self.drafter.engine if self.drafter is not None else None
+        if eng is not None and eng.sampled:
+            if target.dim() != 2:
+                raise ValueError("a sampled tree accept needs the target's logits")
+            from eagle4_b200.runtime.engine import SAMPLED_STREAM
+
+            acc, cnt, bonus = ops.sampled_accept(target.float(), eng.temperature, parent_rows, draft_tokens,
+                                                 self.drafter.tree_nodes(bs), eng.q_store, eng.q_ids, eng.node_slot,
+                                                 eng.top_k, eng.seed, eng.round_ctr, SAMPLED_STREAM)
+            ops.advance_round(eng.round_ctr)
+            return acc, cnt, bonus
+        if target.dim() == 2:
+            target = target.argmax(-1)
+        return accept_greedy_rows(target, draft_tokens, parent_rows)
 
 
 class HarnessSpeculator(_Speculator):
-    """Tree speculator: verify layout, accept and KV compaction (the draft forward is the host's draft model)."""
+    """Tree speculator: the draft rounds (``HostDrafter``: extend, steps under the round policy, verify selection),
+    the verify layout, the accept and the KV compaction; vLLM keeps scheduling, KV allocation and the target forward.
+
+    The draft side is reached through ``load_model`` (vLLM hands the speculator its models; here the draft model and
+    the tree budget), ``prefill_request`` after a request's target prefill, ``propose_tree`` before each verify and
+    ``accept_round`` after it (``eagle_harness/vllm/speculator.py:96,247``)."""
+
+    drafter = None
+
+    def load_model(self, draft_model, *, max_reqs: int, max_len: int, tree=(12, 4, 16), config=None,
+                   temperature: float = 0.0, seed: int = 0) -> None:
+        from eagle4_b200.plugins.host_round import HostDrafter
+
+        steps, top_k, width = tree
+        self.drafter = HostDrafter(draft_model, max_reqs=max_reqs, max_len=max_len, steps=steps, top_k=top_k,
+                                   verify_tokens=width, config=config, temperature=temperature, seed=seed)
+
+    def prefill_request(self, req_id, prompt_ids: torch.Tensor, aux_hidden_states: torch.Tensor, first_token) -> None:
+        self.drafter.admit(req_id, prompt_ids, aux_hidden_states, first_token)
+
+    def propose_tree(self, req_ids):
+        """The round's verify rows per request: (tokens [bs, w], parent rows [bs, w], positions offsets and ancestor
+        words from ``verify_layout`` once the host adds its base positions)."""
+        return self.drafter.propose(req_ids)
+
+    def accept_round(self, req_ids, draft_tokens: torch.Tensor, parent_rows: torch.Tensor, target: torch.Tensor,
+                     aux_hidden_states: Optional[torch.Tensor]):
+        """Accept the verified rows (``target``: ids or logits of the rows) and hand the accepted path to the drafter.
+        Returns (accepted rows, counts, bonus, emitted tokens per request)."""
+        acc, cnt, bonus = self.make_rejection_sampler()(target, draft_tokens, parent_rows)
+        emitted = self.drafter.accept(req_ids, draft_tokens, acc, cnt, bonus, aux_hidden_states)
+        return acc, cnt, bonus, emitted
+
+    def finish_request(self, req_id) -> None:
+        self.drafter.release(req_id)
 
     @staticmethod
     def verify_layout(parent_rows: torch.Tensor, base_positions: torch.Tensor):
@@ -67,7 +119,7 @@ class HarnessSpeculator(_Speculator):
         return self.verify_layout(parent_rows, base_positions)
 
     def make_rejection_sampler(self, *args, **kwargs):
-        return TreeAccept()
+        return TreeAccept(self.drafter)
 
     def post_accept(self, k_caches, v_caches, src_slots: torch.Tensor, dst_slots: torch.Tensor) -> None:
         """Move the accepted rows' K/V from their verify slots to the committed positions (all layers, one launch)."""

@@ -251,10 +251,11 @@ class Engine:
         return torch.full((n,), v, dtype=torch.int32, device=self.device)
 
     # ------------------------------------------------------------------ prefill (eager)
-    def prefill(self, b: int, prompt: torch.Tensor, reserve_tokens: Optional[int] = None) -> None:
+    def prefill(self, b: int, prompt: torch.Tensor, reserve_tokens: Optional[int] = None):
         """Prompt of batch row ``b`` through the target (recurrent layers in scan mode); the first token becomes the
         root; the draft consumes all but the last ``N`` prompt rows now and the rest at the first round. The row's
-        KV pages are mapped first, for ``reserve_tokens`` positions (default: the engine's ``max_len``)."""
+        KV pages are mapped first, for ``reserve_tokens`` positions (default: the engine's ``max_len``). Returns
+        (first token [1], the prompt rows' aux hidden states or None)."""
         n = prompt.shape[0]
         slot = int(self.slot[b])
         self.pages.release(slot)
@@ -282,9 +283,17 @@ class Engine:
         self.root[b] = first[0]
         self.out_tok[b, 0] = first[0]
         self.out_cnt[b] = 1
-        if self.draft is None:
-            return
-        nxt = torch.cat([prompt.to(self.device)[1:], first])  # token following each prompt position
+        if self.draft is not None:
+            self._draft_prefill(b, prompt, aux, first)
+        return first, aux
+
+    def _draft_prefill(self, b: int, prompt: torch.Tensor, aux: torch.Tensor, first: torch.Tensor) -> None:
+        """The draft's share of a prefill: the prompt's leading rows through the draft now (their draft KV), the last
+        ``N`` rows (tokens shifted by one, with their aux hidden states) left pending for the first round's extend."""
+        n = prompt.shape[0]
+        slot = int(self.slot[b])
+        pos = torch.arange(n, device=self.device)
+        nxt = torch.cat([prompt.to(self.device)[1:], first.to(self.device).view(1)])  # token after each position
         keep = min(n, self.verify_tokens)
         lead = n - keep
         if lead:
@@ -416,14 +425,27 @@ class Engine:
         tree = self.tree
         if n > 1:
             toks, prow = tree.verify_rows(bs, self.steps, n - 1)
-            tokens = torch.cat([self.root[:bs, None], toks], dim=1) if dev.type != "cuda" else None  # [bs, n]
         else:
             toks = None
-            tokens = self.root[:bs, None].clone() if dev.type != "cuda" else None
             prow = torch.full((bs, 1), -1, dtype=torch.int32, device=dev)
-        L, sl = self.L[:bs], self.slot[:bs]
-        rowidx = torch.arange(n, device=dev)
-        base = (torch.arange(bs, device=dev) * n)[:, None]
+        nodes = tree.last_nodes if n > 1 else torch.full((bs, 1), -1, dtype=torch.int64, device=dev)
+        tokens, acc, cnt, bonus, aux = self._verify_forward(bs, n, toks, prow, nodes)
+        self._record_accept(bs, n, tokens, acc, cnt, bonus, aux)
+        if self.policy.cost is not None:
+            # cumulative decayed scores of this round's best nodes (root first), batch mean: the next round's
+            # lagged verify-width input
+            count = self.verify_tokens - 1
+            _, cum = tree.rank_reference(bs, self.steps, count)
+            self.host_scores[: cum.shape[1]].copy_(cum.mean(dim=0), non_blocking=True)
+
+    def _verify_forward(self, bs: int, n: int, toks: Optional[torch.Tensor], prow: torch.Tensor,
+                        nodes: Optional[torch.Tensor] = None, accept=None):
+        """The target half of a round: rows [root, toks...] per request (``prow``: parent rows, -1 for the root) through
+        the target, accepted (greedy, or the sampled tree walk over ``nodes``; ``accept(hidden, tokens)`` replaces
+        this engine's accept, as a host's rejection sampler does), the accepted rows' recurrent states and KV
+        committed. Returns (tokens [bs, n], accepted rows [bs, n] (-1 pad), counts [bs] int32, bonus [bs],
+        aux hidden [bs * n, A] or None)."""
+        dev = self.device
         if dev.type == "cuda":  # the rows' structure in one launch
             from eagle4_b200.ops import native
 
@@ -434,6 +456,10 @@ class Engine:
                           ctx_start=torch.zeros(bs * n, dtype=torch.int32, device=dev), ctx_len=ctx, extra=extra,
                           n_extra=n_extra, parent=parent, state_slot=req, max_keys=self.max_len)
         else:
+            tokens = torch.cat([self.root[:bs, None], toks], dim=1) if n > 1 else self.root[:bs, None].clone()
+            L, sl = self.L[:bs], self.slot[:bs]
+            rowidx = torch.arange(n, device=dev)
+            base = (torch.arange(bs, device=dev) * n)[:, None]
             depth, anc = tree_rows_meta(prow)
             slots = self._slots(sl[:, None], L[:, None] + rowidx[None, :])  # [bs, n] physical slot of row r at L + r
             key = (~anc).long() * n + rowidx[None, None, :]
@@ -447,8 +473,9 @@ class Engine:
                           state_slot=sl.repeat_interleave(n), max_keys=self.max_len)
         rec = Records()
         out, aux = self.target.forward(rb, self.tcache, rec)
-        if self.sampled:
-            nodes = tree.last_nodes if n > 1 else torch.full((bs, 1), -1, dtype=torch.int64, device=dev)
+        if accept is not None:
+            acc, cnt, bonus = accept(out, tokens)
+        elif self.sampled:
             acc, cnt, bonus = ops.sampled_accept(self.target.logits(out), self.temperature, prow, tokens, nodes,
                                                  self.q_store, self.q_ids, self.node_slot, self.top_k, self.seed,
                                                  self.round_ctr, SAMPLED_STREAM)
@@ -459,12 +486,25 @@ class Engine:
                                                 torch.full((bs,), n, dtype=torch.int32, device=dev))
         cnt = cnt.to(torch.int32)
         accc = acc.long().clamp(min=0)
+        rowidx = torch.arange(n, device=dev)
+        base = (torch.arange(bs, device=dev) * n)[:, None]
         valid = rowidx[None, :] < cnt[:, None]
         rows = torch.where(valid, accc + base, torch.zeros_like(accc)).int()
         src = torch.gather(slots, 1, accc)
         dst = torch.where(valid, slots, src)  # invalid entries copy a slot onto itself (skipped)
-        self.target.commit(self.tcache, rec, rows, cnt, sl, src.reshape(-1), dst.reshape(-1))
-        # emitted tokens: the accepted drafted tokens then the bonus; they are also the next extend's inputs
+        self.target.commit(self.tcache, rec, rows, cnt, self.slot[:bs], src.reshape(-1), dst.reshape(-1))
+        return tokens, acc, cnt, bonus, aux
+
+    def _record_accept(self, bs: int, n: int, tokens: torch.Tensor, acc: torch.Tensor, cnt: torch.Tensor,
+                       bonus: torch.Tensor, aux: Optional[torch.Tensor]) -> None:
+        """The draft side of an accepted round: the emitted tokens (accepted drafted tokens, then the bonus) become
+        the round's output and the next extend's pending rows (with the accepted rows' aux hidden states); committed
+        lengths advance and the bonus becomes the next root."""
+        dev = self.device
+        rowidx = torch.arange(n, device=dev)
+        base = (torch.arange(bs, device=dev) * n)[:, None]
+        accc = acc.long().clamp(min=0)
+        cnt = cnt.to(torch.int32)
         path_tok = torch.gather(tokens, 1, accc)
         shifted = torch.cat([path_tok[:, 1:], torch.zeros_like(path_tok[:, :1])], dim=1)
         c1 = (cnt - 1)[:, None]
@@ -474,15 +514,10 @@ class Engine:
         self.out_cnt[:bs] = cnt
         self.ext_tok[:bs, :n] = emitted
         self.ext_cnt[:bs] = cnt
-        self.ext_aux[:bs, :n] = aux.index_select(0, (accc + base).reshape(-1)).view(bs, n, -1)
+        if aux is not None:
+            self.ext_aux[:bs, :n] = aux.index_select(0, (accc + base).reshape(-1)).view(bs, n, -1)
         self.L[:bs] += cnt.long()
         self.root[:bs] = bonus
-        if self.policy.cost is not None:
-            # cumulative decayed scores of this round's best nodes (root first), batch mean: the next round's
-            # lagged verify-width input
-            count = self.verify_tokens - 1
-            _, cum = tree.rank_reference(bs, self.steps, count)
-            self.host_scores[: cum.shape[1]].copy_(cum.mean(dim=0), non_blocking=True)
 
     def _graph(self, key: tuple, fn, *args) -> None:
         """Run ``fn(*args)``; on a GPU the first call of a key runs eagerly (sizing lazily allocated workspaces)
@@ -511,13 +546,24 @@ class Engine:
 
     def _spec_round(self, bs: int, context: int) -> int:
         """One speculative round driven by the round policy (the reference drafter's decision loop,
-        ``eagle_harness/sglang/drafter.py:482-691``): steps run until a DECIDE depth's work deltas say stop, then
-        the verify width comes from the previous round's scores. Returns the verify width."""
+        ``eagle_harness/sglang/drafter.py:482-691``): the draft half, then the verify. Returns the verify width."""
         policy = self.policy.begin_round(bs)
         timed = self.policy.live is not None
         if timed:
             ev = [_Stamp(self.device) for _ in range(3)]
             ev[0].record()
+        width, depth = self._draft_round(bs, context, policy)
+        if timed:
+            ev[1].record()
+        self._graph(("verify", bs, width), self._phase_verify, bs, width)
+        if timed:
+            ev[2].record()
+            self._pending_timing = (bs, width, context, ev, depth)
+        return width
+
+    def _draft_round(self, bs: int, context: int, policy) -> tuple:
+        """The draft half of a round: extend and depth 1, then steps until a DECIDE depth's work deltas say stop;
+        the verify width comes from the previous round's scores. Returns (verify width, last step depth)."""
         self._graph(("begin", bs), self._phase_begin, bs)
         row = policy.draft_cost_row(bs, context)
         past = policy.history_verify_num(bs)
@@ -555,14 +601,8 @@ class Engine:
             width = fit_width(req, widths, nodes + 1)
         else:
             width = fit_width(verify_count, widths, nodes + 1)
-        if timed:
-            ev[1].record()
-        self._graph(("verify", bs, width), self._phase_verify, bs, width)
-        if timed:
-            ev[2].record()
-            self._pending_timing = (bs, width, context, ev, depth)
         self.last_depth, self.last_width = levels, width
-        return width
+        return width, depth
 
     def _chain_round(self, bs: int, width: int) -> int:
         """One chain round of verify width ``width`` (``width - 1`` drafted tokens, one per depth; width 1 verifies
