@@ -350,7 +350,7 @@ def sweep(args, tree, tp, dev, rank: int, world: int, dist) -> None:
                            "tree": {"steps": tree.steps, "top_k": tree.top_k, "draft_tokens": tree.draft_tokens,
                                     "mode": args.mode}}}
         try:
-            kv = sum(int(p.shape[0]) + args.new_tokens + span for p in plans[b])
+            kv = sum(-(-(int(p.shape[0]) + args.new_tokens + span) // 16) * 16 for p in plans[b])  # whole pages
             llm = LLM.synthetic(args.model, device=dev, seed=0, tree=tree, max_batch=b,
                                 max_len=hi + args.new_tokens + 64, config=json.dumps({"mode": args.mode}), tp=tp,
                                 kv_tokens=kv)

@@ -3,6 +3,7 @@ the outlier filter, sweep plans and chain-width schedules are checked against th
 ``test_core_oracle.py``.)"""
 
 import json
+import os
 import random
 
 import pytest
@@ -89,3 +90,19 @@ def test_packaged_profile_selection(tmp_path, monkeypatch):
     assert cp.packaged_cost_profile(**setup) == str(tmp_path / "b200")
     assert cp.packaged_cost_profile(**dict(setup, tp_size=2)) is None
     assert cp.packaged_cost_profile(**dict(setup, target_config=dict(target, hidden_size=4096))) is None
+
+
+def test_shipped_b200_profile_matches_the_named_shapes_and_passes_the_cost_model():
+    from eagle4_b200.core import cost_profiles as cp
+    from eagle4_b200.core.cost_table import cost_model_problem, load_cost_tables
+    from eagle4_b200.models import configs
+
+    target = configs.qwen38_27b()
+    setup = dict(device_name="NVIDIA B200", tp_size=1, dtype="bfloat16", quantization=None,
+                 target_config=target.to_hf(), draft_config=configs.qwen38_draft(target).to_hf())
+    path = cp.packaged_cost_profile(**setup)
+    assert path is not None and path.endswith("qwen3.8-27b-b200-tp1")
+    assert cp.packaged_cost_profile(**dict(setup, device_name="NVIDIA H100 80GB HBM3")) is None
+    tables = load_cost_tables(os.path.join(path, "cost"))
+    assert sorted(tables) == [1, 2, 4, 8]
+    assert all(cost_model_problem(t, target_is_moe=False) is None for t in tables.values())
