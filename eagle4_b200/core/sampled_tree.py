@@ -191,3 +191,105 @@ def sampled_walk_reference(logits: torch.Tensor, temperature: float, row_parent:
             bonus[b] = tok
             break
     return acc, cnt, bonus
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# Vocabulary-parallel definitions (tensor parallelism): the walk from the target probabilities at the candidates, then
+# the final draw by the rank whose shard holds the target mass (``eagle4_b200/csrc/sampled.cu`` sparse mode,
+# ``shard_mass_kernel``, ``shard_draw_kernel``).
+
+def sampled_walk_sparse_reference(p_cand: torch.Tensor, row_parent: torch.Tensor, row_node: torch.Tensor,
+                                  q_store: torch.Tensor, q_ids: torch.Tensor, node_slot: torch.Tensor, top_k: int,
+                                  seed: int, round_: int, stream: int):
+    """The tree walk from ``p_cand [bs * n, C]`` (target probabilities at each verify row's candidate ids): (accepted
+    rows [bs, n], counts [bs], final row [bs], residual at the final row's candidates [bs, C]). The residual mass is
+    the mass outside the candidates (1 - their sum, at least 0) plus the candidates' residual."""
+    bs, n = row_parent.shape
+    C = q_store.shape[2]
+    acc = torch.zeros(bs, n, dtype=torch.int64)
+    cnt = torch.zeros(bs, dtype=torch.int32)
+    final = torch.zeros(bs, dtype=torch.int32)
+    r_final = torch.zeros(bs, C, dtype=torch.float64)
+    for b in range(bs):
+        row, path = 0, [0]
+        while True:
+            r = p_cand[b * n + row].double().clone()
+            outside = max(1.0 - float(r.sum()), 0.0)
+            nd = int(row_node[b, row])
+            q = q_store[b, 0 if nd < 0 else 1 + nd].double().clone()
+            moved, expect = False, 0
+            for j in range(row + 1, n):
+                if int(row_parent[b, j]) != row:
+                    continue
+                cn = int(row_node[b, j])
+                draw = cn if cn < top_k else (cn - top_k) % top_k
+                if draw != expect:
+                    break
+                expect += 1
+                s = int(node_slot[b, cn])
+                qsum = float(q.sum())
+                m = outside + float(r.sum())
+                qy = float(q[s]) / qsum if qsum > 0 else 0.0
+                u = float(stream_uniforms(seed, round_, stream, [b * n + j])[0])
+                if q[s] > 0 and u * m * qy < float(r[s]):
+                    path.append(j)
+                    row, moved = j, True
+                    break
+                scale = m / qsum if qsum > 0 else 0.0
+                r = (r - scale * q).clamp_min(0)
+                q[s] = 0
+            if moved:
+                continue
+            acc[b, :len(path)] = torch.tensor(path)
+            cnt[b], final[b], r_final[b] = len(path), row, r
+            break
+    return acc, cnt, final, r_final
+
+
+def shard_residual(logits: torch.Tensor, lo: int, temperature: float, mx: torch.Tensor, z: torch.Tensor,
+                   final_row: torch.Tensor, row_node: torch.Tensor, q_ids: torch.Tensor, r_final: torch.Tensor,
+                   n: int) -> torch.Tensor:
+    """The final rows' residual over this rank's shard ``[lo, lo + Vl)`` ([bs, Vl], float64): target probabilities,
+    replaced at candidate ids (first occurrence) by the walk's residual."""
+    bs = final_row.shape[0]
+    vl = logits.shape[1]
+    S = q_ids.shape[1]
+    out = torch.zeros(bs, vl, dtype=torch.float64)
+    for b in range(bs):
+        g = b * n + int(final_row[b])
+        out[b] = torch.exp(logits[g].double() / temperature - float(mx[g])) / float(z[g])
+        nd = int(row_node[b, int(final_row[b])])
+        ids = q_ids.view(-1, q_ids.shape[-1])[b * S + (0 if nd < 0 else 1 + nd)].tolist()
+        seen = set()
+        for c, i in enumerate(ids):
+            if i in seen:
+                continue
+            seen.add(i)
+            if lo <= i < lo + vl:
+                out[b, i - lo] = float(r_final[b, c])
+    return out
+
+
+def shard_draw_reference(resid: torch.Tensor, lo: int, masses: torch.Tensor, rank: int, seed: int, round_: int,
+                         stream: int) -> torch.Tensor:
+    """Final tokens: target = u * (sum of the ranks' masses), the owning rank searches its shard in vocabulary
+    order; -1 on the other ranks. ``masses`` [world, bs]."""
+    bs = resid.shape[0]
+    tok = torch.full((bs,), -1, dtype=torch.int64)
+    for b in range(bs):
+        col = masses[:, b].double()
+        target = float(stream_uniforms(seed, round_, stream + 1, [b])[0]) * float(col.sum())
+        run, owner = 0.0, -1
+        for r in range(col.shape[0]):
+            if col[r] > 0:
+                owner = r
+            if run + float(col[r]) > target and col[r] > 0:
+                owner = r
+                break
+            run += float(col[r])
+        if owner != rank:
+            continue
+        cdf = resid[b].cumsum(0)
+        i = int(torch.searchsorted(cdf, torch.tensor([target - run], dtype=cdf.dtype), right=True)[0])
+        tok[b] = lo + min(i, resid.shape[1] - 1)
+    return tok

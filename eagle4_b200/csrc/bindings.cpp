@@ -3,6 +3,20 @@
 
 namespace e4 {
 torch::Tensor gemm_error_word(torch::Device dev);
+std::vector<torch::Tensor> sampled_walk_sparse(const torch::Tensor& p_cand, const torch::Tensor& row_parent,
+                                               const torch::Tensor& row_tok, const torch::Tensor& row_node,
+                                               const torch::Tensor& q_store, const torch::Tensor& q_ids,
+                                               const torch::Tensor& node_slot, int64_t K, int64_t seed,
+                                               const torch::Tensor& round_ctr, int64_t stream);
+torch::Tensor shard_residual_mass(const torch::Tensor& logits, int64_t lo, double temperature, const torch::Tensor& mx,
+                                  const torch::Tensor& z, const torch::Tensor& final_row,
+                                  const torch::Tensor& row_node, const torch::Tensor& q_ids,
+                                  const torch::Tensor& r_final, int64_t S, int64_t n);
+torch::Tensor shard_draw(const torch::Tensor& logits, int64_t lo, double temperature, const torch::Tensor& mx,
+                         const torch::Tensor& z, const torch::Tensor& final_row, const torch::Tensor& row_node,
+                         const torch::Tensor& q_ids, const torch::Tensor& r_final, int64_t S, int64_t n,
+                         const torch::Tensor& masses, int64_t rank, int64_t seed, const torch::Tensor& round_ctr,
+                         int64_t stream);
 torch::Tensor moe_experts(const torch::Tensor& latent, const torch::Tensor& chosen, const torch::Tensor& weights,
                           const torch::Tensor& up, const torch::Tensor& down);
 void gemm_launch(const torch::Tensor& x, const torch::Tensor& w, int epi, torch::Tensor y, torch::Tensor yf,
@@ -141,4 +155,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tree_begin", &e4::tree_begin);
   m.def("select_rows", &e4::select_rows);
   m.def("moe_experts", &e4::moe_experts);
+  m.def("sampled_walk_sparse", &e4::sampled_walk_sparse);
+  m.def("shard_residual_mass", &e4::shard_residual_mass);
+  m.def("shard_draw", &e4::shard_draw);
 }

@@ -136,6 +136,12 @@ struct WalkArgs {
   int64_t* acc;   // [bs, n] accepted rows (root first)
   int* cnt;       // [bs]
   int64_t* bonus; // [bs] final token
+  // vocabulary-parallel mode (p_cand != nullptr): the target probabilities at each verify row's candidate ids,
+  // normalised over the whole vocabulary, replace the logits; the walk stops before the final draw and leaves the
+  // final row and its residual at the candidates (the draw is done by the ranks that hold the vocabulary shards)
+  const float* p_cand;  // [bs * n, C]
+  int* final_row;       // [bs]
+  float* r_final;       // [bs, C]
 };
 
 E4_DEV float block_sum_walk(float v, float* red) {
@@ -175,21 +181,25 @@ __global__ void __launch_bounds__(kWalkThreads) sampled_accept_kernel(WalkArgs a
   __syncthreads();
   for (int depth = 0; depth < a.n; ++depth) {
     const int row = s_row;
-    const float* lg = a.logits + (size_t(b) * a.n + row) * a.ld;
+    const bool sparse = a.p_cand != nullptr;
+    const float* lg = sparse ? nullptr : a.logits + (size_t(b) * a.n + row) * a.ld;
     // target distribution at this row: p_v = exp(l_v / T - mx) / z
-    float mx = -INFINITY;
-    for (int v = t; v < a.V; v += kWalkThreads) mx = fmaxf(mx, lg[v] * a.inv_t);
-    mx = block_max_walk(mx, red);
-    float z = 0.f;
-    for (int v = t; v < a.V; v += kWalkThreads) z += __expf(lg[v] * a.inv_t - mx);
-    z = block_sum_walk(z, red);
-    const float iz = 1.f / z;
+    float mx = 0.f, iz = 0.f;
+    if (!sparse) {
+      mx = -INFINITY;
+      for (int v = t; v < a.V; v += kWalkThreads) mx = fmaxf(mx, lg[v] * a.inv_t);
+      mx = block_max_walk(mx, red);
+      float z = 0.f;
+      for (int v = t; v < a.V; v += kWalkThreads) z += __expf(lg[v] * a.inv_t - mx);
+      z = block_sum_walk(z, red);
+      iz = 1.f / z;
+    }
     const int64_t nd = node[row];
     const size_t qrow = size_t(b) * a.S + (nd < 0 ? 0 : 1 + size_t(nd));
     for (int c = t; c < a.C; c += kWalkThreads) {
       id_c[c] = a.q_ids[qrow * a.C + c];
       q_c[c] = a.q_store[qrow * a.C + c];
-      r_c[c] = __expf(lg[id_c[c]] * a.inv_t - mx) * iz;
+      r_c[c] = sparse ? a.p_cand[(size_t(b) * a.n + row) * a.C + c] : __expf(lg[id_c[c]] * a.inv_t - mx) * iz;
     }
     __syncthreads();
     float cand_p = 0.f;
@@ -233,6 +243,15 @@ __global__ void __launch_bounds__(kWalkThreads) sampled_accept_kernel(WalkArgs a
       }
       __syncthreads();
       continue;
+    }
+    if (sparse) {  // the shards' owners draw: leave the final row and its candidates' residual
+      for (int c = t; c < a.C; c += kWalkThreads) a.r_final[size_t(b) * a.C + c] = r_c[c];
+      if (t == 0) {
+        a.cnt[b] = s_len;
+        a.final_row[b] = row;
+        a.bonus[b] = -1;
+      }
+      return;
     }
     // final draw from the residual, in vocabulary order: candidates carry r_c, other ids p_v
     // candidate order by id (C <= 256: rank sort in shared memory)
@@ -301,6 +320,167 @@ __global__ void __launch_bounds__(kWalkThreads) sampled_accept_kernel(WalkArgs a
     }
     return;
   }
+}
+
+// Vocabulary-parallel final draw. The residual of request b's final row over this rank's vocabulary shard
+// [lo, lo + Vl): p_v = exp(l_v / T - mx) / z (global row statistics), replaced at candidate ids by the walk's residual
+// r_c (a repeated id counts once, with its lowest slot, as in the single-GPU draw).
+struct ShardDrawArgs {
+  const float* logits;  // [bs * n, ld] this rank's shard of the verify rows' logits
+  int ld, Vl, lo;
+  float inv_t;
+  const float* mx;      // [bs * n] global row max of l / T
+  const float* z;       // [bs * n] global row sum of exp(l / T - mx)
+  const int* final_row; // [bs]
+  const int64_t* row_node;
+  const int* q_ids;     // [bs, S, C]
+  const float* r_final; // [bs, C]
+  int S, C, n, world, rank;
+  float* mass;          // [bs] this rank's residual mass (mass kernel) / [world, bs] every rank's (draw kernel)
+  uint64_t seed;
+  const unsigned* round_ctr;
+  unsigned stream;
+  int64_t* token;       // [bs] the drawn token on the owning rank, -1 elsewhere
+};
+
+// Candidates of the final row that fall in this shard, first occurrence per id (the lowest slot), sorted by id into
+// id_s / r_s; returns their count.
+E4_DEV int shard_candidates(const ShardDrawArgs& a, int b, int* id_s, float* r_s) {
+  __shared__ int n_own;
+  __shared__ int all_id[kMaxCand], keep[kMaxCand];
+  const int row = a.final_row[b];
+  const int64_t nd = a.row_node[size_t(b) * a.n + row];
+  const size_t qrow = size_t(b) * a.S + (nd < 0 ? 0 : 1 + size_t(nd));
+  if (threadIdx.x == 0) n_own = 0;
+  for (int c = threadIdx.x; c < a.C; c += blockDim.x) all_id[c] = a.q_ids[qrow * a.C + c];
+  __syncthreads();
+  for (int c = threadIdx.x; c < a.C; c += blockDim.x) {
+    const int id = all_id[c];
+    bool k = id >= a.lo && id < a.lo + a.Vl;
+    for (int d = 0; d < c && k; ++d) k = all_id[d] != id;
+    keep[c] = k;
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < a.C; c += blockDim.x) {
+    if (!keep[c]) continue;
+    int rank = 0;
+    for (int d = 0; d < a.C; ++d) rank += keep[d] && all_id[d] < all_id[c];
+    id_s[rank] = all_id[c];
+    r_s[rank] = a.r_final[size_t(b) * a.C + c];
+    atomicAdd(&n_own, 1);
+  }
+  __syncthreads();
+  return n_own;
+}
+
+E4_DEV float shard_p(const ShardDrawArgs& a, const float* lg, size_t grow, int v) {
+  return __expf(lg[v] * a.inv_t - a.mx[grow]) / a.z[grow];
+}
+
+// One CTA per request: this shard's residual mass of the final row (chunk sums in vocabulary order, then in chunk
+// order) into mass[b].
+__global__ void __launch_bounds__(kWalkThreads) shard_mass_kernel(ShardDrawArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x, t = threadIdx.x;
+  __shared__ int id_s[kMaxCand];
+  __shared__ float r_s[kMaxCand], chunk_sum[kWalkThreads];
+  const int m = shard_candidates(a, b, id_s, r_s);
+  const size_t grow = size_t(b) * a.n + a.final_row[b];
+  const float* lg = a.logits + grow * a.ld;
+  const int chunk = (a.Vl + kWalkThreads - 1) / kWalkThreads;
+  const int v0 = t * chunk, v1 = min(a.Vl, v0 + chunk);
+  int ci = 0;
+  while (ci < m && id_s[ci] - a.lo < v0) ++ci;
+  float mine = 0.f;
+  for (int v = v0; v < v1; ++v) {
+    if (ci < m && id_s[ci] - a.lo == v) mine += r_s[ci++];
+    else mine += shard_p(a, lg, grow, v);
+  }
+  chunk_sum[t] = mine;
+  __syncthreads();
+  if (t == 0) {
+    float total = 0.f;
+    for (int i = 0; i < kWalkThreads; ++i) total += chunk_sum[i];
+    a.mass[b] = total;
+  }
+}
+
+// One CTA per request: target = u * (sum of every rank's mass, rank order); the rank whose cumulative mass passes the
+// target scans its shard in vocabulary order for the token; the others write -1.
+__global__ void __launch_bounds__(kWalkThreads) shard_draw_kernel(ShardDrawArgs a, int bs) {
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x, t = threadIdx.x;
+  __shared__ int id_s[kMaxCand];
+  __shared__ float r_s[kMaxCand], chunk_sum[kWalkThreads];
+  __shared__ int s_owner, s_tok;
+  __shared__ float s_rem;
+  const unsigned rnd = *a.round_ctr;
+  if (t == 0) {
+    float total = 0.f;
+    for (int r = 0; r < a.world; ++r) total += a.mass[size_t(r) * bs + b];
+    const float target = uniform(a.seed, rnd, a.stream + 1, unsigned(b)) * total;
+    float run = 0.f;
+    int owner = -1;
+    for (int r = 0; r < a.world; ++r) {
+      const float mr = a.mass[size_t(r) * bs + b];
+      if (mr > 0.f) owner = r;  // the last rank with mass takes a target at the very end
+      if (run + mr > target && mr > 0.f) { owner = r; break; }
+      run += mr;
+    }
+    s_owner = owner;
+    s_rem = target - run;
+    s_tok = -1;
+  }
+  __syncthreads();
+  if (s_owner != a.rank) {
+    if (t == 0) a.token[b] = -1;
+    return;
+  }
+  const int m = shard_candidates(a, b, id_s, r_s);
+  const size_t grow = size_t(b) * a.n + a.final_row[b];
+  const float* lg = a.logits + grow * a.ld;
+  const int chunk = (a.Vl + kWalkThreads - 1) / kWalkThreads;
+  const int v0 = t * chunk, v1 = min(a.Vl, v0 + chunk);
+  int ci0 = 0;
+  while (ci0 < m && id_s[ci0] - a.lo < v0) ++ci0;
+  int ci = ci0;
+  float mine = 0.f;
+  for (int v = v0; v < v1; ++v) {
+    if (ci < m && id_s[ci] - a.lo == v) mine += r_s[ci++];
+    else mine += shard_p(a, lg, grow, v);
+  }
+  chunk_sum[t] = mine;
+  __syncthreads();
+  if (t == 0) {
+    float run = 0.f;
+    int own = kWalkThreads - 1;
+    for (int i = 0; i < kWalkThreads; ++i) {
+      if (run + chunk_sum[i] > s_rem && chunk_sum[i] > 0.f) { own = i; break; }
+      run += chunk_sum[i];
+    }
+    chunk_sum[0] = s_rem - run;
+    s_owner = own;
+  }
+  __syncthreads();
+  if (t == s_owner) {
+    const float rem = chunk_sum[0];
+    float run = 0.f;
+    int tok = -1, last = -1;
+    ci = ci0;
+    for (int v = v0; v < v1; ++v) {
+      float pv;
+      if (ci < m && id_s[ci] - a.lo == v) pv = r_s[ci++];
+      else pv = shard_p(a, lg, grow, v);
+      if (pv > 0.f) last = v;
+      run += pv;
+      if (run > rem && pv > 0.f) { tok = v; break; }
+    }
+    s_tok = a.lo + (tok >= 0 ? tok : (last >= 0 ? last : v0));
+  }
+  __syncthreads();
+  if (t == 0) a.token[b] = s_tok;
 }
 
 __global__ void advance_round_kernel(unsigned* ctr) {
@@ -379,6 +559,117 @@ std::vector<torch::Tensor> sampled_accept(const torch::Tensor& logits, double te
     C10_CUDA_CHECK(launch_pdl(sampled_accept_kernel, bs, kWalkThreads, 0, at::cuda::getCurrentCUDAStream().stream(),
                               a));
   return {acc, cnt, bonus};
+}
+
+// Vocabulary-parallel walk: the tree rejection over the verify rows from the target probabilities at each row's
+// candidate ids (``p_cand`` [bs * n, C], normalised over the whole vocabulary). Returns (accepted rows [bs, n],
+// counts [bs], final row [bs], residual at the final row's candidates [bs, C]).
+std::vector<torch::Tensor> sampled_walk_sparse(const torch::Tensor& p_cand, const torch::Tensor& row_parent,
+                                               const torch::Tensor& row_tok, const torch::Tensor& row_node,
+                                               const torch::Tensor& q_store, const torch::Tensor& q_ids,
+                                               const torch::Tensor& node_slot, int64_t K, int64_t seed,
+                                               const torch::Tensor& round_ctr, int64_t stream) {
+  const at::cuda::CUDAGuard g(p_cand.device());
+  const int bs = row_parent.size(0), n = row_parent.size(1);
+  TORCH_CHECK(p_cand.scalar_type() == at::kFloat && p_cand.is_contiguous() && p_cand.size(0) == int64_t(bs) * n &&
+              p_cand.size(1) == q_store.size(2), "sampled_walk_sparse: p_cand [bs * n, C] fp32");
+  TORCH_CHECK(row_parent.scalar_type() == at::kInt && row_parent.is_contiguous());
+  TORCH_CHECK(row_node.scalar_type() == at::kLong && row_node.is_contiguous() && row_tok.is_contiguous());
+  TORCH_CHECK(q_store.size(2) <= kMaxCand, "sampled_walk_sparse: at most 256 candidates");
+  auto acc = torch::zeros({bs, n}, row_tok.options());
+  auto cnt = torch::zeros({bs}, row_parent.options());
+  auto bonus = torch::zeros({bs}, row_tok.options());
+  auto final_row = torch::zeros({bs}, row_parent.options());
+  auto r_final = torch::zeros({bs, q_store.size(2)}, p_cand.options());
+  WalkArgs a{};
+  a.row_parent = row_parent.data_ptr<int>();
+  a.row_tok = row_tok.data_ptr<int64_t>();
+  a.row_node = row_node.data_ptr<int64_t>();
+  a.q_store = q_store.data_ptr<float>();
+  a.q_ids = q_ids.data_ptr<int>();
+  a.node_slot = node_slot.data_ptr<int>();
+  a.S = int(q_store.size(1));
+  a.C = int(q_store.size(2));
+  a.cap = int(node_slot.size(1));
+  a.K = int(K);
+  a.n = n;
+  a.seed = uint64_t(seed);
+  a.round_ctr = reinterpret_cast<const unsigned*>(round_ctr.data_ptr<int>());
+  a.stream = unsigned(stream);
+  a.acc = acc.data_ptr<int64_t>();
+  a.cnt = cnt.data_ptr<int>();
+  a.bonus = bonus.data_ptr<int64_t>();
+  a.p_cand = p_cand.data_ptr<float>();
+  a.final_row = final_row.data_ptr<int>();
+  a.r_final = r_final.data_ptr<float>();
+  if (bs)
+    C10_CUDA_CHECK(launch_pdl(sampled_accept_kernel, bs, kWalkThreads, 0, at::cuda::getCurrentCUDAStream().stream(),
+                              a));
+  return {acc, cnt, final_row, r_final};
+}
+
+static ShardDrawArgs shard_args(const torch::Tensor& logits, int64_t lo, double temperature, const torch::Tensor& mx,
+                                const torch::Tensor& z, const torch::Tensor& final_row, const torch::Tensor& row_node,
+                                const torch::Tensor& q_ids, const torch::Tensor& r_final, int64_t S, int64_t n) {
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1, "shard draw: fp32 logits");
+  TORCH_CHECK(mx.is_contiguous() && z.is_contiguous() && final_row.scalar_type() == at::kInt &&
+              q_ids.scalar_type() == at::kInt && r_final.is_contiguous());
+  ShardDrawArgs a{};
+  a.logits = logits.data_ptr<float>();
+  a.ld = int(logits.stride(0));
+  a.Vl = int(logits.size(1));
+  a.lo = int(lo);
+  a.inv_t = float(1.0 / temperature);
+  a.mx = mx.data_ptr<float>();
+  a.z = z.data_ptr<float>();
+  a.final_row = final_row.data_ptr<int>();
+  a.row_node = row_node.data_ptr<int64_t>();
+  a.q_ids = q_ids.data_ptr<int>();
+  a.r_final = r_final.data_ptr<float>();
+  a.S = int(S);
+  a.C = int(r_final.size(1));
+  a.n = int(n);
+  return a;
+}
+
+// This rank's residual mass of each request's final row over its vocabulary shard [lo, lo + Vl): [bs].
+torch::Tensor shard_residual_mass(const torch::Tensor& logits, int64_t lo, double temperature, const torch::Tensor& mx,
+                                  const torch::Tensor& z, const torch::Tensor& final_row,
+                                  const torch::Tensor& row_node, const torch::Tensor& q_ids,
+                                  const torch::Tensor& r_final, int64_t S, int64_t n) {
+  const at::cuda::CUDAGuard g(logits.device());
+  const int bs = final_row.size(0);
+  auto mass = torch::zeros({bs}, logits.options());
+  ShardDrawArgs a = shard_args(logits, lo, temperature, mx, z, final_row, row_node, q_ids, r_final, S, n);
+  a.mass = mass.data_ptr<float>();
+  if (bs)
+    C10_CUDA_CHECK(launch_pdl(shard_mass_kernel, bs, kWalkThreads, 0, at::cuda::getCurrentCUDAStream().stream(), a));
+  return mass;
+}
+
+// The final tokens: every rank's masses [world, bs] -> the owning rank's draw from its shard, -1 on the others.
+torch::Tensor shard_draw(const torch::Tensor& logits, int64_t lo, double temperature, const torch::Tensor& mx,
+                         const torch::Tensor& z, const torch::Tensor& final_row, const torch::Tensor& row_node,
+                         const torch::Tensor& q_ids, const torch::Tensor& r_final, int64_t S, int64_t n,
+                         const torch::Tensor& masses, int64_t rank, int64_t seed, const torch::Tensor& round_ctr,
+                         int64_t stream) {
+  const at::cuda::CUDAGuard g(logits.device());
+  const int bs = final_row.size(0);
+  TORCH_CHECK(masses.dim() == 2 && masses.size(1) == bs && masses.is_contiguous() &&
+              masses.scalar_type() == at::kFloat, "shard_draw: masses [world, bs] fp32");
+  auto token = torch::empty({bs}, row_node.options());
+  ShardDrawArgs a = shard_args(logits, lo, temperature, mx, z, final_row, row_node, q_ids, r_final, S, n);
+  a.mass = const_cast<float*>(masses.data_ptr<float>());
+  a.world = int(masses.size(0));
+  a.rank = int(rank);
+  a.seed = uint64_t(seed);
+  a.round_ctr = reinterpret_cast<const unsigned*>(round_ctr.data_ptr<int>());
+  a.stream = unsigned(stream);
+  a.token = token.data_ptr<int64_t>();
+  if (bs)
+    C10_CUDA_CHECK(launch_pdl(shard_draw_kernel, bs, kWalkThreads, 0, at::cuda::getCurrentCUDAStream().stream(), a,
+                              bs));
+  return token;
 }
 
 void advance_round(torch::Tensor round_ctr) {

@@ -258,6 +258,17 @@ class TargetModel:
             return self.tp.lm_head_argmax(hidden, self.w["lm_head"], self.lm_lo)
         return ops.lm_head_argmax(hidden, self.w["lm_head"])
 
+    def sampled_accept(self, hidden: torch.Tensor, temperature: float, row_parent, row_tok, row_node, q_store, q_ids,
+                       node_slot, k: int, seed: int, round_ctr, stream: int):
+        """Recursive tree rejection of the rows of ``hidden`` (``ops.sampled_accept``); under tensor parallelism the
+        vocabulary-parallel form, which exchanges row statistics and candidate probabilities instead of logits."""
+        if self.tp is not None and self.tp.world > 1:
+            local = ops.logits(hidden, self.w["lm_head"])
+            return self.tp.sampled_accept(local, self.lm_lo, temperature, row_parent, row_tok, row_node, q_store,
+                                          q_ids, node_slot, k, seed, round_ctr, stream)
+        return ops.sampled_accept(self.logits(hidden), temperature, row_parent, row_tok, row_node, q_store, q_ids,
+                                  node_slot, k, seed, round_ctr, stream)
+
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         local = ops.logits(hidden, self.w["lm_head"])
         if self.tp is not None and self.tp.world > 1:

@@ -175,6 +175,68 @@ class TensorParallel:
         dist.all_gather(parts, local.contiguous(), group=self.group)
         return torch.cat(parts, dim=1)
 
+    def sampled_accept(self, local: torch.Tensor, lo: int, temperature: float, row_parent, row_tok, row_node, q_store,
+                       q_ids, node_slot, k: int, seed: int, round_ctr, stream: int):
+        """Recursive tree rejection over vocabulary-parallel logits (``local``: this rank's fp32 shard of the verify
+        rows' logits, vocabulary ids ``[lo, lo + Vl)``), exchanging a few floats per row instead of the logits:
+
+        1. row statistics: each rank's max and sum of exp over its shard, all-gathered (2 floats per row and rank),
+           combined in rank order into the global max and normaliser;
+        2. the target probabilities at each row's draft candidates, computed by the rank owning each id and
+           sum-reduced ([rows, C] floats);
+        3. the walk, identical on every rank, from those probabilities; it leaves each request's final row and the
+           residual at its candidates;
+        4. the final draw: each rank's residual mass of the final rows (one float per request and rank), then the
+           rank whose cumulative mass passes the target searches its shard; the token is max-reduced.
+
+        Returns (accepted rows [bs, n], counts [bs], final token [bs]) on every rank."""
+        from eagle4_b200.core import sampled_tree as st
+
+        bs, n = row_parent.shape
+        S, C = q_store.shape[1], q_store.shape[2]
+        vl = local.shape[1]
+        cuda = local.is_cuda
+        lg = local.float() * (1.0 / temperature)
+        mx_l = lg.amax(dim=-1)
+        z_l = torch.exp(lg - mx_l[:, None]).sum(dim=-1)
+        stats = torch.stack([mx_l, z_l], dim=1).contiguous()
+        parts = [torch.empty_like(stats) for _ in range(self.world)]
+        dist.all_gather(parts, stats, group=self.group)
+        allst = torch.stack(parts)  # [W, T, 2]
+        mx = allst[..., 0].amax(dim=0)
+        z = (allst[..., 1] * torch.exp(allst[..., 0] - mx[None])).sum(dim=0)
+        node = row_node.reshape(-1)
+        req = torch.arange(bs, device=local.device).repeat_interleave(n)
+        qrow = req * S + torch.where(node < 0, torch.zeros_like(node), node + 1)
+        ids = q_ids.reshape(bs * S, C).index_select(0, qrow).long()
+        own = (ids >= lo) & (ids < lo + vl)
+        vals = lg.gather(1, (ids - lo).clamp(0, vl - 1))
+        p = torch.where(own, torch.exp(vals - mx[:, None]) / z[:, None], torch.zeros_like(vals)).contiguous()
+        dist.all_reduce(p, op=dist.ReduceOp.SUM, group=self.group)
+        if cuda:
+            C_ = _native()
+            acc, cnt, final, r_final = C_.sampled_walk_sparse(p, row_parent, row_tok, row_node, q_store, q_ids,
+                                                              node_slot, k, seed, round_ctr, stream)
+            mass = C_.shard_residual_mass(local.float().contiguous(), lo, temperature, mx.contiguous(),
+                                          z.contiguous(), final, row_node, q_ids, r_final.contiguous(), S, n)
+        else:
+            rnd = int(round_ctr[0])
+            acc, cnt, final, r_final = st.sampled_walk_sparse_reference(p, row_parent, row_node, q_store, q_ids,
+                                                                        node_slot, k, seed, rnd, stream)
+            resid = st.shard_residual(local.float(), lo, temperature, mx, z, final, row_node, q_ids, r_final, n)
+            mass = resid.sum(dim=1).float()
+        masses = [torch.empty_like(mass) for _ in range(self.world)]
+        dist.all_gather(masses, mass.contiguous(), group=self.group)
+        masses = torch.stack(masses).contiguous()
+        if cuda:
+            tok = _native().shard_draw(local.float().contiguous(), lo, temperature, mx.contiguous(), z.contiguous(),
+                                       final, row_node, q_ids, r_final.contiguous(), S, n, masses, self.rank, seed,
+                                       round_ctr, stream)
+        else:
+            tok = st.shard_draw_reference(resid, lo, masses, self.rank, seed, int(round_ctr[0]), stream)
+        dist.all_reduce(tok, op=dist.ReduceOp.MAX, group=self.group)
+        return acc, cnt, tok
+
     def max_over_ranks(self, values: List[float]) -> List[float]:
         """Host floats reduced by MAX over the ranks (measured timings, so every rank decides alike)."""
         if self.world == 1:

@@ -270,7 +270,7 @@ class Engine:
         out, aux = self.target.forward(rb, self.tcache)
         if self.sampled:
             dev = self.device
-            _, _, first = ops.sampled_accept(self.target.logits(out[-1:]), self.temperature,
+            _, _, first = self.target.sampled_accept(out[-1:], self.temperature,
                                              torch.full((1, 1), -1, dtype=torch.int32, device=dev),
                                              torch.zeros(1, 1, dtype=torch.int64, device=dev),
                                              torch.full((1, 1), -1, dtype=torch.int64, device=dev), self.plain_q[:1],
@@ -326,7 +326,7 @@ class Engine:
         out, aux = self.target.forward(rb, self.tcache, rec)
         if self.sampled:  # plain sampling: the walk with no children draws from p
             dev = self.device
-            _, _, ids = ops.sampled_accept(self.target.logits(out), self.temperature,
+            _, _, ids = self.target.sampled_accept(out, self.temperature,
                                            torch.full((bs, 1), -1, dtype=torch.int32, device=dev), self.root[:bs, None],
                                            torch.full((bs, 1), -1, dtype=torch.int64, device=dev), self.plain_q,
                                            self.plain_ids, self.plain_slot, 1, self.seed, self.round_ctr,
@@ -476,7 +476,7 @@ class Engine:
         if accept is not None:
             acc, cnt, bonus = accept(out, tokens)
         elif self.sampled:
-            acc, cnt, bonus = ops.sampled_accept(self.target.logits(out), self.temperature, prow, tokens, nodes,
+            acc, cnt, bonus = self.target.sampled_accept(out, self.temperature, prow, tokens, nodes,
                                                  self.q_store, self.q_ids, self.node_slot, self.top_k, self.seed,
                                                  self.round_ctr, SAMPLED_STREAM)
             ops.advance_round(self.round_ctr)

@@ -113,3 +113,44 @@ def test_sampled_engine_on_gpu():
     assert a.shape == (1, 16) and b.shape == (1, 16)
     assert int(a.max()) < 4096 and int(b.min()) >= 0
     native.check_errors()
+
+
+def test_vocab_parallel_kernels_match_the_full_walk():
+    """The sparse walk and the shard mass / draw kernels, with the vocabulary split in two shards on one GPU, against
+    the full-vocabulary accept kernel."""
+    nat = _native()
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(5)
+    bs, k, c, v = 6, 3, 16, 512
+    n, parent, nodes, q_store, q_ids, node_slot, cap = _random_tree(bs, k, 2, c, v, dev, g)
+    parent, nodes, q_store, q_ids, node_slot = (t.to(dev) for t in (parent, nodes, q_store, q_ids, node_slot))
+    S = q_store.shape[1]
+    agree = total = 0
+    for rnd in range(30):
+        logits = (torch.randn(bs * n, v, generator=g) * 2).to(dev)
+        ctr = torch.full((1,), rnd, dtype=torch.int32, device=dev)
+        tok0 = torch.zeros(bs, n, dtype=torch.int64, device=dev)
+        acc, cnt, bonus = nat.sampled_accept(logits, 0.8, parent, tok0, nodes, q_store, q_ids, node_slot, k, 9, ctr,
+                                             0x10000)
+        lg = logits * (1.0 / 0.8)
+        mx = lg.amax(-1)
+        z = torch.exp(lg - mx[:, None]).sum(-1)
+        node = nodes.reshape(-1)
+        qrow = torch.arange(bs, device=dev).repeat_interleave(n) * S + torch.where(node < 0, 0, node + 1)
+        ids = q_ids.reshape(bs * S, c).index_select(0, qrow).long()
+        p = (torch.exp(lg.gather(1, ids) - mx[:, None]) / z[:, None]).contiguous()
+        sacc, scnt, final, r_final = nat._C.sampled_walk_sparse(p, parent, tok0, nodes, q_store, q_ids, node_slot, k, 9,
+                                                             ctr, 0x10000)
+        shards = [(0, 256), (256, 512)]
+        masses = torch.stack([nat._C.shard_residual_mass(logits[:, lo:hi].contiguous(), lo, 0.8, mx, z, final, nodes,
+                                                      q_ids, r_final, S, n) for lo, hi in shards]).contiguous()
+        toks = torch.stack([nat._C.shard_draw(logits[:, lo:hi].contiguous(), lo, 0.8, mx, z, final, nodes, q_ids,
+                                           r_final, S, n, masses, r, 9, ctr, 0x10000)
+                            for r, (lo, hi) in enumerate(shards)])
+        assert ((toks >= 0).sum(0) == 1).all(), "exactly one rank draws each token"
+        tok = toks.amax(0)
+        for b in range(bs):
+            total += 1
+            agree += int(scnt[b]) == int(cnt[b]) and int(tok[b]) == int(bonus[b]) and torch.equal(
+                sacc[b, :int(scnt[b])], acc[b, :int(cnt[b])])
+    assert agree / total >= 0.95, agree / total

@@ -55,3 +55,59 @@ def test_matches_reference_oracle():
     cu, fu = torch.rand(rows, draws), torch.rand(rows)
     ra, rb = reject_children(p, a, cu, fu), rst.reject_children(p, b, cu, fu)
     assert torch.equal(ra.tokens, rb.tokens) and torch.equal(ra.accepted_position, rb.accepted_position)
+
+
+def _shard_protocol(logits, temperature, parent, nodes, q_store, q_ids, node_slot, k, seed, rnd, stream, bounds):
+    """The vocabulary-parallel accept simulated in one process over vocabulary shards ``bounds``: global row
+    statistics, candidate probabilities, the sparse walk, per-shard residual masses, the owner's draw."""
+    from eagle4_b200.core import sampled_tree as st
+
+    bs, n = parent.shape
+    S, C = q_store.shape[1], q_store.shape[2]
+    lg = logits.double() / temperature
+    mx = lg.amax(-1)
+    z = torch.exp(lg - mx[:, None]).sum(-1)
+    node = nodes.reshape(-1)
+    qrow = torch.arange(bs).repeat_interleave(n) * S + torch.where(node < 0, torch.zeros_like(node), node + 1)
+    ids = q_ids.reshape(bs * S, C)[qrow].long()
+    p = torch.exp(lg.gather(1, ids) - mx[:, None]) / z[:, None]
+    acc, cnt, final, r_final = st.sampled_walk_sparse_reference(p, parent, nodes, q_store, q_ids, node_slot, k, seed,
+                                                                rnd, stream)
+    resid = [st.shard_residual(logits[:, lo:hi], lo, temperature, mx, z, final, nodes, q_ids, r_final, n)
+             for lo, hi in bounds]
+    masses = torch.stack([r.sum(1) for r in resid])
+    toks = torch.stack([st.shard_draw_reference(r, lo, masses, i, seed, rnd, stream)
+                        for i, (r, (lo, _)) in enumerate(zip(resid, bounds))])
+    return acc, cnt, toks.amax(0)
+
+
+def test_vocab_parallel_walk_and_draw_equal_the_full_walk():
+    """The sharded protocol's accepted paths and final tokens equal the full-vocabulary walk's (float64, 3 shards)."""
+    from eagle4_b200.core import sampled_tree as st
+    from eagle4_b200.core.draft_tree import TreeShape
+
+    g = torch.Generator().manual_seed(7)
+    bs, k, c, v = 5, 3, 12, 300
+    shape = TreeShape(k, 3)
+    n = 1 + k + 2
+    parent = torch.zeros(bs, n, dtype=torch.int32)
+    parent[:, 0] = -1
+    parent[:, 1 + k:] = 1
+    nodes = torch.full((bs, n), -1, dtype=torch.int64)
+    nodes[:, 1:1 + k] = torch.arange(k)
+    nodes[:, 1 + k:] = shape.layer_start(2) + torch.arange(2)
+    cap = shape.capacity
+    q_store = torch.softmax(torch.randn(bs, 1 + cap, c, generator=g) * 1.5, -1).float()
+    q_ids = torch.stack([torch.stack([torch.randperm(v, generator=g)[:c] for _ in range(1 + cap)])
+                         for _ in range(bs)]).int()
+    node_slot = torch.stack([torch.randperm(c, generator=g)[:cap] for _ in range(bs)]).int()
+    bounds = [(0, 128), (128, 256), (256, 300)]
+    for rnd in range(25):
+        logits = torch.randn(bs * n, v, generator=g) * 2
+        acc, cnt, bonus = _shard_protocol(logits, 0.8, parent, nodes, q_store, q_ids, node_slot, k, 9, rnd, 0x10000,
+                                          bounds)
+        racc, rcnt, rbonus = st.sampled_walk_reference(logits, 0.8, parent, nodes, q_store, q_ids, node_slot, k, 9,
+                                                       rnd, 0x10000)
+        assert torch.equal(cnt, rcnt) and torch.equal(bonus, rbonus)
+        for b in range(bs):
+            assert torch.equal(acc[b, :int(cnt[b])], racc[b, :int(rcnt[b])])

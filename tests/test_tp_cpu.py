@@ -72,6 +72,44 @@ def test_tp_matches_single_process(world):
         assert res[r]["same_tokens"] and res[r]["spec_eq_plain"] and res[r]["ranks_agree"], res[r]
 
 
+def _sampled_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.set_num_threads(1)
+    try:
+        from eagle4_b200.api import LLM, TreeSpec
+        from eagle4_b200.parallel.tp import TensorParallel
+
+        tp = TensorParallel(backend="torch")
+        kw = dict(device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_len=256, temperature=0.9,
+                  sample_seed=11, max_batch=2)
+        llm = LLM.synthetic("tiny", tp=tp, **kw)
+        ref = LLM.synthetic("tiny", **kw)
+        g = torch.Generator().manual_seed(3)
+        prompts = [torch.randint(0, 4096, (20,), generator=g), torch.randint(0, 4096, (33,), generator=g)]
+        got = llm.generate(prompts, 10).tolist()
+        want = ref.generate(prompts, 10).tolist()
+        gathered = [None] * world
+        dist.all_gather_object(gathered, got)
+        out[rank] = {"equal": got == want, "ranks_agree": all(x == gathered[0] for x in gathered), "got": got,
+                     "want": want}
+    finally:
+        dist.destroy_process_group()
+
+
+def test_vocab_parallel_sampling_equals_one_process():
+    """Sampled speculative decoding at TP2 (the accept exchanges row statistics, candidate probabilities and residual
+    masses instead of the full logits) gives the single-process sampled tokens for the same seed."""
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        out = mgr.dict()
+        mp.start_processes(_sampled_worker, args=(2, _port(), out), nprocs=2, start_method="spawn", join=True)
+        res = dict(out)
+    for r in range(2):
+        assert res[r]["ranks_agree"], res[r]
+        assert res[r]["equal"], (res[r]["got"], res[r]["want"])
+
+
 def test_shard_layouts_cover_the_weights():
     from eagle4_b200.models import weights
 

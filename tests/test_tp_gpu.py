@@ -106,6 +106,15 @@ def _worker(rank, world, port, out):
         gathered = [None] * world
         dist.all_gather_object(gathered, spec.tolist())
         res["ranks_agree"] = all(x == gathered[0] for x in gathered)
+        # sampled decoding: the vocabulary-parallel accept (row statistics, candidate probabilities and residual
+        # masses cross the ranks, not the logits); every rank must hold the same tokens
+        sm = LLM.synthetic("tiny", device=dev, tree=tree, max_len=512, tp=fused, temperature=0.8, sample_seed=3)
+        sampled = sm.generate(prompt[None], 16)
+        gathered = [None] * world
+        dist.all_gather_object(gathered, sampled.tolist())
+        res["sampled_ranks_agree"] = all(x == gathered[0] for x in gathered)
+        res["sampled_in_vocab"] = bool(((sampled >= 0) & (sampled < 4096)).all())
+        sm.engine.graphs.clear()
         native.check_errors(dev)
         res["ok"] = True
         for m in models.values():
@@ -143,3 +152,4 @@ def test_fused_tp_matches_reference_nccl_and_one_gpu(world):
         assert res[r]["fused_vs_nccl"] <= 0.02, summary
         assert res[r]["fused_vs_one"] <= 0.03, summary
         assert res[r]["tok_agree"] >= 0.95 and res[r]["spec_eq_plain"] and res[r]["ranks_agree"], summary
+        assert res[r]["sampled_ranks_agree"] and res[r]["sampled_in_vocab"], res[r]
