@@ -43,11 +43,13 @@ torch::Tensor conv_tree(const torch::Tensor& x, const torch::Tensor& cs, const t
                         const torch::Tensor& parent, const torch::Tensor& w);
 void conv_commit(const torch::Tensor& x, torch::Tensor cs, const torch::Tensor& slots, const torch::Tensor& rows,
                  const torch::Tensor& nrows, int64_t W);
-void conv_commit_scan(torch::Tensor cs, const torch::Tensor& x, const torch::Tensor& slot, int64_t W);
+void conv_commit_scan(torch::Tensor cs, const torch::Tensor& x, const torch::Tensor& slot, int64_t W,
+                      const torch::Tensor& seg);
 torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int64_t z_off, int64_t b_off,
                        int64_t a_off, const torch::Tensor& a_log, const torch::Tensor& dt_bias, torch::Tensor state,
                        const torch::Tensor& slot, const torch::Tensor& parent, const torch::Tensor& norm_w,
-                       double eps, int64_t HK, int64_t HV, int64_t K, int64_t V, bool scan);
+                       double eps, int64_t HK, int64_t HV, int64_t K, int64_t V, bool scan,
+                       const torch::Tensor& seg);
 void gdn_commit_all(const std::vector<torch::Tensor>& qkv, const std::vector<torch::Tensor>& proj,
                     const std::vector<torch::Tensor>& state, const std::vector<torch::Tensor>& conv_state,
                     const std::vector<torch::Tensor>& a_log, const std::vector<torch::Tensor>& dt_bias, int64_t b_off,
@@ -56,7 +58,7 @@ void gdn_commit_all(const std::vector<torch::Tensor>& qkv, const std::vector<tor
 torch::Tensor mamba_tree(const torch::Tensor& xbc, const torch::Tensor& dt, const torch::Tensor& a_log,
                          const torch::Tensor& dt_bias, const torch::Tensor& dskip, torch::Tensor state,
                          const torch::Tensor& slot, const torch::Tensor& parent, int64_t H, int64_t P, int64_t N,
-                         int64_t G, bool scan);
+                         int64_t G, bool scan, const torch::Tensor& seg);
 void mamba_commit(const torch::Tensor& xbc, const torch::Tensor& dt, const torch::Tensor& a_log,
                   const torch::Tensor& dt_bias, const torch::Tensor& dskip, torch::Tensor state,
                   const torch::Tensor& slots, const torch::Tensor& rows, const torch::Tensor& nrows, int64_t H,

@@ -748,26 +748,21 @@ void conv_commit(const torch::Tensor& x, torch::Tensor cs, const torch::Tensor& 
       CBF(x), x.stride(0), BFP(cs), sl.data_ptr<int>(), rw.data_ptr<int>(), rw.size(1), nr.data_ptr<int>(), C, W));
 }
 
-void conv_commit_scan(torch::Tensor cs, const torch::Tensor& x, const torch::Tensor& slot, int64_t W) {
-  // rows of each request are contiguous: commit the last W-1 rows of every run
-  auto seg = segments_of(slot).cpu();
-  const int* s = seg.data_ptr<int>();
-  const int nseg = seg.numel() - 1;
-  std::vector<int> slots_v, nrows_v;
-  std::vector<int> rows_v;
-  const int keep = int(W) - 1;
-  auto slot_c = slot.to(torch::kCPU).to(torch::kInt32);
-  for (int i = 0; i < nseg; ++i) {
-    const int r0 = s[i], r1 = s[i + 1];
-    const int first = std::max(r0, r1 - keep);
-    slots_v.push_back(slot_c.data_ptr<int>()[r0]);
-    nrows_v.push_back(r1 - first);
-    for (int k = 0; k < keep; ++k) rows_v.push_back(first + k < r1 ? first + k : r1 - 1);
-  }
-  auto dev = x.device();
-  auto opt = torch::TensorOptions().dtype(torch::kInt32);
-  auto rows = torch::tensor(rows_v, opt).view({nseg, keep}).to(dev);
-  conv_commit(x, cs, torch::tensor(slots_v, opt).to(dev), rows, torch::tensor(nrows_v, opt).to(dev), W);
+void conv_commit_scan(torch::Tensor cs, const torch::Tensor& x, const torch::Tensor& slot, int64_t W,
+                      const torch::Tensor& seg_in) {
+  // rows of each request are contiguous: commit the last W-1 rows of every run (segments from the caller's device
+  // table when given; otherwise found from the slots on the host)
+  const at::cuda::CUDAGuard g(x.device());
+  const torch::Tensor seg = seg_in.numel() ? seg_in.to(torch::kInt32) : segments_of(slot);
+  const int64_t nseg = seg.numel() - 1;
+  if (nseg <= 0) return;
+  const int64_t keep = W - 1;
+  auto starts = seg.slice(0, 0, nseg), ends = seg.slice(0, 1, nseg + 1);
+  auto nrows = at::clamp_max(ends - starts, keep);
+  auto k = at::arange(keep, seg.options());
+  auto rows = at::minimum((ends - nrows).unsqueeze(1) + k.unsqueeze(0), (ends - 1).unsqueeze(1));
+  auto slots = slot.to(torch::kInt32).index_select(0, starts.to(torch::kLong));
+  conv_commit(x, cs, slots, rows.contiguous(), nrows.contiguous(), W);
 }
 
 template <typename F>
@@ -791,7 +786,8 @@ torch::Tensor gated_rmsnorm(const torch::Tensor& o, const torch::Tensor& z, cons
 torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int64_t z_off, int64_t b_off,
                        int64_t a_off, const torch::Tensor& a_log, const torch::Tensor& dt_bias, torch::Tensor state,
                        const torch::Tensor& slot, const torch::Tensor& parent, const torch::Tensor& norm_w,
-                       double eps, int64_t HK, int64_t HV, int64_t K, int64_t V, bool scan) {
+                       double eps, int64_t HK, int64_t HV, int64_t K, int64_t V, bool scan,
+                       const torch::Tensor& seg_in) {
   const at::cuda::CUDAGuard gd(qkv.device());
   const int T = qkv.size(0);
   auto out = torch::empty({T, HV * V}, qkv.options());
@@ -800,7 +796,7 @@ torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int6
   auto sl = slot.to(torch::kInt32).contiguous(), pa = parent.to(torch::kInt32).contiguous();
   if (scan) {
     // prefill: value-sliced scan into the raw output, then the gated RMSNorm (skipped for raw callers)
-    torch::Tensor seg = segments_of(sl);
+    torch::Tensor seg = seg_in.numel() ? seg_in.to(torch::kInt32).contiguous() : segments_of(sl);
     dim3 grid(HV, seg.numel() - 1, (V + kScanV - 1) / kScanV);
     auto st = at::cuda::getCurrentCUDAStream();
     auto raw = norm_w.numel() ? torch::empty({T, HV * V}, qkv.options()) : out;
@@ -900,14 +896,15 @@ static MambaArgs mamba_args(const torch::Tensor& xbc, const torch::Tensor& dt, c
 torch::Tensor mamba_tree(const torch::Tensor& xbc, const torch::Tensor& dt, const torch::Tensor& a_log,
                          const torch::Tensor& dt_bias, const torch::Tensor& dskip, torch::Tensor state,
                          const torch::Tensor& slot, const torch::Tensor& parent, int64_t H, int64_t P, int64_t N,
-                         int64_t G, bool scan) {
+                         int64_t G, bool scan, const torch::Tensor& seg_in) {
   const at::cuda::CUDAGuard gd(xbc.device());
   const int T = xbc.size(0);
   auto out = torch::empty({T, H, P}, xbc.options());
   if (!T) return out;
   MambaArgs a = mamba_args(xbc, dt, a_log, dt_bias, dskip, state, H, P, N, G);
   auto sl = slot.to(torch::kInt32).contiguous(), pa = parent.to(torch::kInt32).contiguous();
-  torch::Tensor seg = scan ? segments_of(sl) : torch::Tensor();  // tree mode reads no segment table
+  // tree mode reads no segment table; scan mode takes the caller's device table when given
+  torch::Tensor seg = !scan ? torch::Tensor() : (seg_in.numel() ? seg_in.to(torch::kInt32).contiguous() : segments_of(sl));
   dim3 grid(H, scan ? seg.numel() - 1 : T);
   auto st = at::cuda::getCurrentCUDAStream();
   const int* segp = scan ? seg.data_ptr<int>() : nullptr;

@@ -39,6 +39,7 @@ class RowBatch:
     state_slot: torch.Tensor  # [T] int32 recurrent-state slot of the row's request
     scan: bool = False  # recurrent layers update their state in place row by row (prefill chains)
     max_keys: Optional[int] = None  # bound on any row's visible keys (lets attention skip a host read)
+    segments: Optional[torch.Tensor] = None  # scan mode: request boundaries [0, ..., T] int32 on the device
 
     @property
     def num_rows(self) -> int:
@@ -187,9 +188,9 @@ class TargetModel:
         x_pre = proj[:, :cd]
         conv = ops.causal_conv_tree(x_pre, cache.conv[ri], rb.state_slot, rb.parent, w[f"l{i}.conv"])
         y = ops.gdn_mixer(conv, proj, cfg, w[f"l{i}.A_log"], w[f"l{i}.dt_bias"], w[f"l{i}.gnorm"], cache.ssm[ri],
-                          rb.state_slot, rb.parent, rb.scan)
+                          rb.state_slot, rb.parent, rb.scan, rb.segments)
         if rb.scan:
-            ops.conv_commit_scan(cache.conv[ri], x_pre, rb.state_slot, cfg.conv_kernel)
+            ops.conv_commit_scan(cache.conv[ri], x_pre, rb.state_slot, cfg.conv_kernel, rb.segments)
         elif rec is not None:
             rec.layer.append(i)
             rec.x_pre.append(proj)
@@ -208,9 +209,9 @@ class TargetModel:
         dt = proj[:, inner + cd: inner + cd + nh]
         conv = ops.causal_conv_tree(x_pre, cache.conv[ri], rb.state_slot, rb.parent, w[f"l{i}.conv"])
         y = ops.mamba_tree(conv, dt, w[f"l{i}.A_log"], w[f"l{i}.dt_bias"], w[f"l{i}.D"], cache.ssm[ri],
-                           rb.state_slot, rb.parent, cfg, rb.scan)
+                           rb.state_slot, rb.parent, cfg, rb.scan, rb.segments)
         if rb.scan:
-            ops.conv_commit_scan(cache.conv[ri], x_pre, rb.state_slot, cfg.conv_kernel)
+            ops.conv_commit_scan(cache.conv[ri], x_pre, rb.state_slot, cfg.conv_kernel, rb.segments)
         elif rec is not None:
             rec.layer.append(i)
             rec.x_pre.append(x_pre)

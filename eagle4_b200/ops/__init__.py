@@ -93,10 +93,12 @@ def causal_conv_tree(x, conv_state, state_slot, parent, weight):
     return fn(x, conv_state, state_slot, parent, weight)
 
 
-def gdn_mixer(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent, scan: bool):
-    """Fused GDN token mixer after the conv: gates, tree recurrence and gated RMSNorm -> ``[T, HV*V]``."""
-    fn = _nat().gdn_mixer if _cuda(conv) else ref.gdn_mixer
-    return fn(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent, scan)
+def gdn_mixer(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent, scan: bool, segments=None):
+    """Fused GDN token mixer after the conv: gates, tree recurrence and gated RMSNorm -> ``[T, HV*V]``.
+    ``segments``: scan mode's request boundaries on the device (spares a device-to-host read)."""
+    if _cuda(conv):
+        return _nat().gdn_mixer(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent, scan, segments)
+    return ref.gdn_mixer(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent, scan)
 
 
 def gdn_commit_all(convs, projs, states, conv_states, a_logs, dt_biases, slots, rows, n_rows, cfg):
@@ -125,18 +127,20 @@ def gdn_commit(qkv, g, beta, x_pre, state, conv_state, slots, rows, n_rows, cfg)
     return ref.gdn_commit(qkv, g, beta, x_pre, state, conv_state, slots, rows, n_rows, cfg)
 
 
-def conv_commit_scan(conv_state, x_pre, state_slot, kw):
-    fn = _nat().conv_commit_scan if _cuda(x_pre) else ref.conv_commit_scan
-    return fn(conv_state, x_pre, state_slot, kw)
+def conv_commit_scan(conv_state, x_pre, state_slot, kw, segments=None):
+    if _cuda(x_pre):
+        return _nat().conv_commit_scan(conv_state, x_pre, state_slot, kw, segments)
+    return ref.conv_commit_scan(conv_state, x_pre, state_slot, kw)
 
 
 def gated_rmsnorm(o, z, w, eps):
     return _nat().gated_rmsnorm(o, z, w, eps) if _cuda(o) else ref.gated_rmsnorm(o, z, w, eps)
 
 
-def mamba_tree(xbc, dt_raw, a_log, dt_bias, d_skip, state, state_slot, parent, cfg, scan: bool):
-    fn = _nat().mamba_tree if _cuda(xbc) else ref.mamba_tree
-    return fn(xbc, dt_raw, a_log, dt_bias, d_skip, state, state_slot, parent, cfg, scan)
+def mamba_tree(xbc, dt_raw, a_log, dt_bias, d_skip, state, state_slot, parent, cfg, scan: bool, segments=None):
+    if _cuda(xbc):
+        return _nat().mamba_tree(xbc, dt_raw, a_log, dt_bias, d_skip, state, state_slot, parent, cfg, scan, segments)
+    return ref.mamba_tree(xbc, dt_raw, a_log, dt_bias, d_skip, state, state_slot, parent, cfg, scan)
 
 
 def mamba_commit(xbc, dt_raw, a_log, dt_bias, d_skip, x_pre, state, conv_state, slots, rows, n_rows, cfg):

@@ -203,11 +203,13 @@ def _gdn_offsets(cfg):
     return cd, cd + vd, cd + vd + hv
 
 
-def gdn_mixer(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent, scan: bool):
+def gdn_mixer(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent, scan: bool, segments=None):
+    """``segments``: scan mode's request boundaries as a device table ([0, ..., T] int32); without it the boundaries
+    are found from the slots on the host (a device-to-host read)."""
     z_off, b_off, a_off = _gdn_offsets(cfg)
     return _C.gdn_tree(conv, proj, z_off, b_off, a_off, a_log, dt_bias, state, state_slot, parent, norm_w,
                        float(cfg.rms_norm_eps), cfg.gdn_k_heads, cfg.gdn_v_heads, cfg.gdn_k_dim, cfg.gdn_v_dim,
-                       bool(scan))
+                       bool(scan), _NONE if segments is None else segments)
 
 
 def gdn_recurrence(qkv, a, b, a_log, dt_bias, state, state_slot, parent, cfg):
@@ -215,7 +217,7 @@ def gdn_recurrence(qkv, a, b, a_log, dt_bias, state, state_slot, parent, cfg):
     hv = cfg.gdn_v_heads
     raw = torch.cat([b, a], dim=1).contiguous()
     return _C.gdn_tree(qkv, raw, 0, 0, hv, a_log, dt_bias, state, state_slot, parent, _NONE,
-                       float(cfg.rms_norm_eps), cfg.gdn_k_heads, hv, cfg.gdn_k_dim, cfg.gdn_v_dim, False)
+                       float(cfg.rms_norm_eps), cfg.gdn_k_heads, hv, cfg.gdn_k_dim, cfg.gdn_v_dim, False, _NONE)
 
 
 def gdn_commit_all(convs, projs, states, conv_states, a_logs, dt_biases, slots, rows, n_rows, cfg):
@@ -225,13 +227,14 @@ def gdn_commit_all(convs, projs, states, conv_states, a_logs, dt_biases, slots, 
                       cfg.gdn_v_dim, cfg.gdn_conv_dim, cfg.conv_kernel)
 
 
-def conv_commit_scan(conv_state, x_pre, state_slot, kw):
-    _C.conv_commit_scan(conv_state, x_pre, state_slot, int(kw))
+def conv_commit_scan(conv_state, x_pre, state_slot, kw, segments=None):
+    _C.conv_commit_scan(conv_state, x_pre, state_slot, int(kw), _NONE if segments is None else segments)
 
 
-def mamba_tree(xbc, dt_raw, a_log, dt_bias, d_skip, state, state_slot, parent, cfg, scan: bool):
+def mamba_tree(xbc, dt_raw, a_log, dt_bias, d_skip, state, state_slot, parent, cfg, scan: bool, segments=None):
     return _C.mamba_tree(xbc, dt_raw, a_log, dt_bias, d_skip, state, state_slot, parent, cfg.mamba_heads,
-                         cfg.mamba_head_dim, cfg.mamba_state, cfg.mamba_groups, bool(scan))
+                         cfg.mamba_head_dim, cfg.mamba_state, cfg.mamba_groups, bool(scan),
+                         _NONE if segments is None else segments)
 
 
 def mamba_commit(xbc, dt_raw, a_log, dt_bias, d_skip, x_pre, state, conv_state, slots, rows, n_rows, cfg):

@@ -247,6 +247,12 @@ class Engine:
         pos = pos.long()
         return self.tcache.block_table[slot.long(), pos // self.page].long() * self.page + pos % self.page
 
+    def _segments(self, n: int) -> torch.Tensor:
+        """The scan segment table of one request's ``n`` rows, built on the device (no host round trip)."""
+        seg = torch.full((2,), n, dtype=torch.int32, device=self.device)
+        seg[0] = 0
+        return seg
+
     def _i32(self, n: int, v: int) -> torch.Tensor:
         return torch.full((n,), v, dtype=torch.int32, device=self.device)
 
@@ -266,7 +272,8 @@ class Engine:
         rb = RowBatch(ids=prompt.to(self.device), pos=pos, req=self._i32(n, slot), write_slot=slots,
                       ctx_start=self._i32(n, 0), ctx_len=(pos + 1).int(),
                       extra=torch.zeros(n, 1, dtype=torch.int32, device=self.device), n_extra=self._i32(n, 0),
-                      parent=(pos - 1).int(), state_slot=self._i32(n, slot), scan=True, max_keys=n)
+                      parent=(pos - 1).int(), state_slot=self._i32(n, slot), scan=True, max_keys=n,
+                      segments=self._segments(n))
         out, aux = self.target.forward(rb, self.tcache)
         if self.sampled:
             dev = self.device
