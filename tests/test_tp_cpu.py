@@ -40,6 +40,7 @@ def _worker(rank, world, port, out):
         for name, m in (("tp", llm), ("ref", ref)):
             eng = m.engine
             n = prompt.shape[0]
+            eng.pages.reserve(0, n + 1)  # map real KV pages (an unmapped row writes every position to the trash page)
             pos = torch.arange(n)
             slots = eng._slots(torch.tensor(0), pos)
             rb = RowBatch(ids=prompt, pos=pos, req=torch.zeros(n, dtype=torch.int32), write_slot=slots,

@@ -85,6 +85,7 @@ def _worker(rank, world, port, out):
         for name, m in models.items():
             eng = m.engine
             n = prompt.shape[0]
+            eng.pages.reserve(0, n + 1)  # map real KV pages (an unmapped row writes every position to the trash page)
             pos = torch.arange(n, device=dev)
             slots = eng._slots(torch.tensor(0, device=dev), pos)
             z = torch.zeros(n, dtype=torch.int32, device=dev)
