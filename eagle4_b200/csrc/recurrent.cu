@@ -287,56 +287,62 @@ __device__ __forceinline__ void chain_walk(const int* __restrict__ parent, int T
   __syncthreads();
 }
 
-// Tree mode: a cluster of two CTAs per (value head, chain). CTA r of the pair owns value columns
-// [r V/2, (r + 1) V/2), four lanes per column (lane q holding K/4 state elements in groups of four at 16m + 4q + e: a
-// column's lanes load one contiguous 64-byte run per group, and a staged k / q row is read as conflict-free 16-byte
-// pieces). Both CTAs walk the same chain (the chain head's ancestors from the committed state without output, then
-// the chain rows) and keep the rows' raw outputs in shared memory; the gated RMSNorm of a row needs all V columns, so
-// each CTA's sum of squares per row goes to its peer through distributed shared memory, and both add the two partial
-// sums in cluster-rank order. Two 256-thread CTAs per SM replace one 512-thread CTA, so a tree's CTAs spread over the
-// SMs in fewer waves. The commit kernel runs the same step, so a row decoded alone, verified in a tree, or committed
-// gives the same state.
-constexpr int kPairMaxCols = 64;  // value columns per CTA of a pair (V <= 128)
+// Gated RMSNorm of the chain rows' raw outputs (orow[c][v], fp32): warp w finishes rows w, w + 16, ..., lane l the
+// value columns 4l .. 4l+3. o is rounded to bf16, RMS-normalised over the head's V values (a fixed-order warp sum),
+// times w, times silu(z); with no norm weight, the rounded o itself.
+__device__ __forceinline__ void gdn_norm_rows(const GdnArgs& a, const int* rows, int n, int h, const float* orow,
+                                              const __nv_bfloat16* nw, float eps, __nv_bfloat16* out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  for (int c = warp; c < n; c += nwarps) {
+    const int row = rows[c];
+    float ob[4];
+    float x2 = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int v = 4 * lane + e;
+      ob[e] = v < a.V ? __bfloat162float(__float2bfloat16(orow[c * 128 + v])) : 0.f;
+      x2 = fmaf(ob[e], ob[e], x2);
+    }
+    const float rs = rsqrtf(warp_sum(x2) / a.V + eps);
+    __nv_bfloat16* o = out + (size_t(row) * a.HV + h) * a.V;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int v = 4 * lane + e;
+      if (v >= a.V) continue;
+      if (nw == nullptr) {
+        o[v] = __float2bfloat16(ob[e]);
+      } else {
+        const float z = bf(a.proj[size_t(row) * a.ldp + a.z_off + h * a.V + v]);
+        o[v] = __float2bfloat16(ob[e] * rs * bf(nw[v]) * silu(z));
+      }
+    }
+  }
+}
 
-E4_DEV uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-E4_DEV void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// Store ``v`` at the same shared-memory address in CTA ``peer`` of the cluster.
-E4_DEV void st_peer_f32(float* local, uint32_t peer, float v) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(peer));
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
-}
-
+// Tree mode: one CTA of 4 V threads per (value head, chain); the chain's ancestors and rows are replayed from the
+// committed state without writing it (value column v has kScanLanes lanes, lane r holding K/4 state elements in groups
+// of four at 16m + 4r + e: a column's lanes load one contiguous 64-byte run per group, and a staged k / q row is read
+// as conflict-free 16-byte pieces), the chain rows' raw outputs are kept in shared memory and normalised at the end.
+// The commit kernel runs the same step, so a row decoded alone, verified in a tree, or committed gives the same state.
 template <int K>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kScanLanes * kPairMaxCols)
-    gdn_kernel(GdnArgs a, const int* __restrict__ slot, const int* __restrict__ parent,
-               const __nv_bfloat16* __restrict__ nw, float eps, __nv_bfloat16* __restrict__ out) {
+__global__ void __launch_bounds__(512) gdn_kernel(GdnArgs a, const int* __restrict__ slot,
+                                                  const int* __restrict__ parent, const __nv_bfloat16* __restrict__ nw,
+                                                  float eps, __nv_bfloat16* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ __align__(16) uint8_t gdn_smem[];
   GdnStage<K>& st = *reinterpret_cast<GdnStage<K>*>(gdn_smem);
-  float* orow = reinterpret_cast<float*>(gdn_smem + sizeof(GdnStage<K>));  // [kMaxPath][kPairMaxCols]
+  float* orow = reinterpret_cast<float*>(gdn_smem + sizeof(GdnStage<K>));  // [kMaxPath][128]
   __shared__ int win[2 * kMaxPath], fc[2 * kMaxPath], path[kMaxPath], meta[2];
-  __shared__ float ss[2][kMaxPath];  // [cluster rank][chain row] partial sums of squares
-  const uint32_t me = cluster_rank(), peer = me ^ 1u;
-  const int h = blockIdx.x >> 1;
-  const int cols = a.V / 2;
-  const int lc = threadIdx.x / kScanLanes, r = threadIdx.x % kScanLanes;
-  const int v = int(me) * cols + lc;
+  const int h = blockIdx.x;
+  const int v = threadIdx.x / kScanLanes, r = threadIdx.x % kScanLanes;
   const int kh = h / (a.HV / a.HK);
   const int vc = min(v, a.V - 1);
   // later rows have the longer ancestor runs in a tree's node order: start them first
   const int row = gridDim.y - 1 - blockIdx.y;
-  cluster_sync();  // the peer's shared memory exists before anything is stored into it
   chain_walk(parent, gridDim.y, row, win, fc, path, meta);
   const int len = meta[0], pre = meta[1];
-  if (len == 0) return;  // both CTAs of the pair see the same chain
+  if (len == 0) return;
   float S[K / 4];
   load_state4<K>(S, a.state + ((size_t(slot[row]) * a.HV + h) * a.V + vc) * K, r);
   for (int p0 = 0; p0 < len; p0 += kGdnTile) {
@@ -345,41 +351,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kScanLanes * kPairMa
     gdn_stage<K>(a, path + p0, n, h, kh, st);
     for (int j = 0; j < n; ++j) {
       const float o = gdn_step4<K>(S, st, j, vc, r);
-      if (p0 + j >= pre && r == 0 && lc < cols) orow[(p0 + j - pre) * kPairMaxCols + lc] = o;
+      if (p0 + j >= pre && r == 0 && v < a.V) orow[(p0 + j - pre) * 128 + v] = o;
     }
   }
   __syncthreads();
-  // gated RMSNorm of the chain rows: warp w takes rows w, w + nwarps, ...; lane l the columns l, l + 32 of this CTA
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  const int rows = len - pre;
-  for (int c = warp; c < rows; c += nwarps) {
-    float x2 = 0.f;
-    for (int j = lane; j < cols; j += 32) {
-      const float ob = __bfloat162float(__float2bfloat16(orow[c * kPairMaxCols + j]));
-      x2 = fmaf(ob, ob, x2);
-    }
-    x2 = warp_sum(x2);
-    if (lane == 0) {
-      ss[me][c] = x2;
-      st_peer_f32(&ss[me][c], peer, x2);
-    }
-  }
-  cluster_sync();  // both partial sums of every row are in both CTAs
-  for (int c = warp; c < rows; c += nwarps) {
-    const int orow_id = path[pre + c];
-    const float rs = rsqrtf((ss[0][c] + ss[1][c]) / a.V + eps);
-    __nv_bfloat16* o = out + (size_t(orow_id) * a.HV + h) * a.V + int(me) * cols;
-    for (int j = lane; j < cols; j += 32) {
-      const float ob = __bfloat162float(__float2bfloat16(orow[c * kPairMaxCols + j]));
-      if (nw == nullptr) {
-        o[j] = __float2bfloat16(ob);
-      } else {
-        const int vv = int(me) * cols + j;
-        const float z = bf(a.proj[size_t(orow_id) * a.ldp + a.z_off + h * a.V + vv]);
-        o[j] = __float2bfloat16(ob * rs * bf(nw[vv]) * silu(z));
-      }
-    }
-  }
+  gdn_norm_rows(a, path + pre, len - pre, h, orow, nw, eps, out);
 }
 
 template <int K>
@@ -837,11 +813,11 @@ torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int6
     if (!norm_w.numel()) return out;
     return gated_rmsnorm(raw.view({T, HV, V}), proj.narrow(1, z_off, HV * V), norm_w, eps);
   }
-  TORCH_CHECK(V <= 2 * kPairMaxCols && V % 16 == 0, "gdn tree: V a multiple of 16, at most 128");
-  dim3 grid(2 * HV, T);  // clusters of two CTAs along x: (value head, half of its value columns)
-  const int threads = kScanLanes * int(V / 2);
+  TORCH_CHECK(V <= 128, "gdn tree: at most 128 value columns per head");
+  dim3 grid(HV, T);
+  const int threads = kScanLanes * int(V);
   auto st = at::cuda::getCurrentCUDAStream();
-  constexpr size_t kRowOut = size_t(kMaxPath) * kPairMaxCols * sizeof(float);  // raw outputs of a chain's rows
+  constexpr size_t kRowOut = size_t(kMaxPath) * 128 * sizeof(float);  // raw outputs of a chain's rows
   if (K == 128) {
     gdn_smem_attr(gdn_kernel<128>, sizeof(GdnStage<128>) + kRowOut);
     C10_CUDA_CHECK(launch_pdl(gdn_kernel<128>, grid, threads, sizeof(GdnStage<128>) + kRowOut, st.stream(), a,
