@@ -3,6 +3,7 @@
 
 namespace e4 {
 torch::Tensor gemm_error_word(torch::Device dev);
+void gemm_prefill_mode(bool on);
 std::vector<torch::Tensor> sampled_walk_sparse(const torch::Tensor& p_cand, const torch::Tensor& row_parent,
                                                const torch::Tensor& row_tok, const torch::Tensor& row_node,
                                                const torch::Tensor& q_store, const torch::Tensor& q_ids,
@@ -120,6 +121,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "eagle4_b200 sm_100a kernels";
   m.def("error_word", [](int64_t dev) { return e4::gemm_error_word(torch::Device(torch::kCUDA, dev)); });
   m.def("gemm", &e4::gemm_launch, "tcgen05 skinny GEMM with fused epilogue");
+  m.def("gemm_prefill_mode", &e4::gemm_prefill_mode);
   m.def("gemm_allreduce", &e4::gemm_allreduce, "row-parallel GEMM fused with its all-reduce and the residual add");
   m.def("sample_children", &e4::sample_children, "Gumbel-top-k children from candidate logits");
   m.def("sampled_accept", &e4::sampled_accept, "recursive tree rejection over the verify rows");

@@ -61,7 +61,13 @@ struct Params {
   int nt;           // token tile (MMA N): multiple of 16, <= 256
   int n_tiles;      // ceil(N / 128)
   int kb_total;     // ceil(K / 64) k-blocks per tile
-  long total;       // n_tiles * kb_total: the linear k-block space split evenly over the CTAs (stream-K)
+  // Work units: (weight tile, token chunk of nt rows), unit = tile * chunks + chunk. Decode and verify launches have
+  // one chunk (unit = tile). Prefill launches cover every token in ``chunks`` chunks with CTA ranges aligned to whole
+  // units (``aligned``): each unit is one CTA's full-K tile, so no tile is split and nothing is merged.
+  int chunks;
+  int units;        // n_tiles * chunks
+  int aligned;
+  long total;       // units * kb_total: the linear k-block space split evenly over the CTAs (stream-K)
   int stages;
   int epi;
   __nv_bfloat16* y;  // [T, ldy] bf16 output (plain / residual / swiglu / relu2)
@@ -94,6 +100,7 @@ struct Params {
   int ldx;
   float fold_eps;
   int fold;
+  const float* rstd;  // prefill launches: the folded norm's per-token scales for all T rows, computed beforehand
   // 1: every output (and residual) row is 16-byte aligned and whole 8-feature pieces fit in N, so the epilogue
   // stages each 16-token chunk in shared memory and moves it with 16-byte loads and stores (set_vector_epilogue)
   int vec;
@@ -106,7 +113,9 @@ struct Params {
 
 // Stream-K partition: CTA c owns linear k-blocks [start(c), start(c+1)) of the (tile, k-block) space; a tile is
 // split into "pieces" where CTA ranges cut it. The cut points depend only on (N, K, grid), never on T.
-__device__ __forceinline__ long sk_start(const Params& p, int c) { return (long(c) * p.total) / gridDim.x; }
+__device__ __forceinline__ long sk_start(const Params& p, int c) {
+  return p.aligned ? (long(c) * p.units / gridDim.x) * p.kb_total : (long(c) * p.total) / gridDim.x;
+}
 __device__ __forceinline__ int sk_owner(const Params& p, long g) {  // CTA whose range contains k-block g
   return int(((g + 1) * long(gridDim.x) - 1) / p.total);
 }
@@ -278,7 +287,7 @@ __device__ __forceinline__ void tp_gather_tiles(const Params& p, int ep_tid, uns
 // 16-byte loads and stores. The per-element arithmetic is the scalar path's (fp32 add, one rounding), so both give
 // the same bits.
 __device__ __forceinline__ void store_chunk_vec(const Params& p, int tile, int m, int j0, const float* v,
-                                                float* xchg, int ep_tid) {
+                                                float* xchg, int ep_tid, int row0, int Tu) {
   float* st = xchg;  // [16 tokens][128 rows]
   // this thread's two 8-feature residual pieces are requested before the transpose, so their latency overlaps it
   uint4 rres[2];
@@ -286,7 +295,7 @@ __device__ __forceinline__ void store_chunk_vec(const Params& p, int tile, int m
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int q = ep_tid + h * 128, j = j0 + (q >> 4), n = tile * kTileM + (q & 15) * 8;
-      rres[h] = (j < p.T && n < p.N) ? *reinterpret_cast<const uint4*>(p.res + size_t(j) * p.ldr + n)
+      rres[h] = (j < Tu && n < p.N) ? *reinterpret_cast<const uint4*>(p.res + size_t(row0 + j) * p.ldr + n)
                                      : make_uint4(0u, 0u, 0u, 0u);
     }
   }
@@ -297,14 +306,14 @@ __device__ __forceinline__ void store_chunk_vec(const Params& p, int tile, int m
     // rows [0,64) gate, [64,128) up: 16 tokens x 8 pieces of 8 output features, one piece per thread
     const int i = ep_tid >> 3, piece = ep_tid & 7;
     const int j = j0 + i, f = tile * 64 + piece * 8;
-    if (j < p.T && f < p.N / 2) {
+    if (j < Tu && f < p.N / 2) {
       const float* g = st + i * kTileM + piece * 8;
       uint4 out;
       __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&out);
 #pragma unroll
       for (int e = 0; e < 4; ++e)
         o2[e] = __floats2bfloat162_rn(silu(g[2 * e]) * g[64 + 2 * e], silu(g[2 * e + 1]) * g[64 + 2 * e + 1]);
-      *reinterpret_cast<uint4*>(p.y + size_t(j) * p.ldy + f) = out;
+      *reinterpret_cast<uint4*>(p.y + size_t(row0 + j) * p.ldy + f) = out;
     }
   } else {
 #pragma unroll
@@ -312,12 +321,12 @@ __device__ __forceinline__ void store_chunk_vec(const Params& p, int tile, int m
       const int q = ep_tid + h * 128;
       const int i = q >> 4, piece = q & 15;
       const int j = j0 + i, n = tile * kTileM + piece * 8;
-      if (j >= p.T || n >= p.N) continue;
+      if (j >= Tu || n >= p.N) continue;
       const float4 lo = *reinterpret_cast<const float4*>(st + i * kTileM + piece * 8);
       const float4 hi = *reinterpret_cast<const float4*>(st + i * kTileM + piece * 8 + 4);
       float a[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
       if (p.epi == kF32) {
-        float4* dst = reinterpret_cast<float4*>(p.yf + size_t(j) * p.ldy + n);
+        float4* dst = reinterpret_cast<float4*>(p.yf + size_t(row0 + j) * p.ldy + n);
         dst[0] = lo;
         dst[1] = hi;
         continue;
@@ -339,7 +348,7 @@ __device__ __forceinline__ void store_chunk_vec(const Params& p, int tile, int m
       __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&out);
 #pragma unroll
       for (int e = 0; e < 4; ++e) o2[e] = __floats2bfloat162_rn(a[2 * e], a[2 * e + 1]);
-      *reinterpret_cast<uint4*>(p.y + size_t(j) * p.ldy + n) = out;
+      *reinterpret_cast<uint4*>(p.y + size_t(row0 + j) * p.ldy + n) = out;
     }
   }
   named_bar(1, 128);
@@ -378,14 +387,14 @@ __device__ __forceinline__ void add_pieces(float* v, int count, const float4 (&b
 
 // Final epilogue of 16 token columns [j0, j0+16) held by this thread for weight row ``m`` of ``tile``.
 __device__ __forceinline__ void store_chunk(const Params& p, int tile, int m, int j0, const float* v, float* xchg,
-                                            int ep_tid, unsigned half) {
+                                            int ep_tid, unsigned half, int row0, int Tu) {
   const int n = tile * kTileM + m;
   if (p.epi == kAllReduce) {
     tp_send_chunk(p, tile, m, j0, v, xchg, ep_tid, half);
     return;
   }
   if (p.vec && p.epi != kArgmax) {
-    store_chunk_vec(p, tile, m, j0, v, xchg, ep_tid);
+    store_chunk_vec(p, tile, m, j0, v, xchg, ep_tid, row0, Tu);
     return;
   }
   if (p.epi == kSwiGLU) {
@@ -401,7 +410,7 @@ __device__ __forceinline__ void store_chunk(const Params& p, int tile, int m, in
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int j = j0 + i;
-          if (j < p.T) p.y[size_t(j) * p.ldy + f] = __float2bfloat16(silu(v[i]) * xchg[i * 64 + m]);
+          if (j < Tu) p.y[size_t(row0 + j) * p.ldy + f] = __float2bfloat16(silu(v[i]) * xchg[i * 64 + m]);
         }
       }
     }
@@ -447,15 +456,16 @@ __device__ __forceinline__ void store_chunk(const Params& p, int tile, int m, in
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const int j = j0 + i;
-    if (j >= p.T) break;
+    if (j >= Tu) break;
+    const size_t row = size_t(row0 + j);
     float a = v[i];
     if (p.epi == kF32) {
-      p.yf[size_t(j) * p.ldy + n] = a;
+      p.yf[row * p.ldy + n] = a;
       continue;
     }
-    if (p.epi == kResidual) a += __bfloat162float(p.res[size_t(j) * p.ldr + n]);
+    if (p.epi == kResidual) a += __bfloat162float(p.res[row * p.ldr + n]);
     if (p.epi == kReLU2) { a = fmaxf(a, 0.f); a = a * a; }
-    p.y[size_t(j) * p.ldy + n] = __float2bfloat16(a);
+    p.y[row * p.ldy + n] = __float2bfloat16(a);
   }
 }
 
@@ -514,28 +524,29 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
       uint32_t phase = 0;
       // prologue: weight tiles of the first stages, before the dependency wait
       const int pre = int(g_end - g_begin < long(p.stages) ? g_end - g_begin : long(p.stages));
+      // unit u = tile * chunks + chunk: the W tile's rows at (u / chunks) * 128, the X chunk's at (u % chunks) * nt
       for (int i = 0; i < pre; ++i) {
         const long gg = g_begin + i;
-        const int tile = int(gg / p.kb_total), kb = int(gg - long(tile) * p.kb_total);
+        const int unit = int(gg / p.kb_total), kb = int(gg - long(unit) * p.kb_total);
         mbar_expect_tx(&full_bar[i], stage_bytes);
-        tma_load_2d(tiles + i * stage_bytes, &tmap_w, &full_bar[i], kb * kTileK, tile * kTileM, pol_w);
+        tma_load_2d(tiles + i * stage_bytes, &tmap_w, &full_bar[i], kb * kTileK, (unit / p.chunks) * kTileM, pol_w);
       }
       pdl_wait();
       for (int i = 0; i < pre; ++i) {
         const long gg = g_begin + i;
-        const int tile = int(gg / p.kb_total), kb = int(gg - long(tile) * p.kb_total);
-        (void)tile;
-        tma_load_2d(tiles + i * stage_bytes + kWTileBytes, &tmap_x, &full_bar[i], kb * kTileK, 0, pol_x);
+        const int unit = int(gg / p.kb_total), kb = int(gg - long(unit) * p.kb_total);
+        tma_load_2d(tiles + i * stage_bytes + kWTileBytes, &tmap_x, &full_bar[i], kb * kTileK,
+                    (unit % p.chunks) * p.nt, pol_x);
       }
       stage = pre == p.stages ? 0 : pre;
       phase = pre == p.stages ? 1 : 0;
       for (long gg = g_begin + pre; gg < g_end && ok; ++gg) {
-        const int tile = int(gg / p.kb_total), kb = int(gg - long(tile) * p.kb_total);
+        const int unit = int(gg / p.kb_total), kb = int(gg - long(unit) * p.kb_total);
         if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { record_error(p.err, kErrTimeoutProducer); ok = false; break; }
         uint8_t* st = tiles + stage * stage_bytes;
         mbar_expect_tx(&full_bar[stage], stage_bytes);
-        tma_load_2d(st, &tmap_w, &full_bar[stage], kb * kTileK, tile * kTileM, pol_w);
-        tma_load_2d(st + kWTileBytes, &tmap_x, &full_bar[stage], kb * kTileK, 0, pol_x);
+        tma_load_2d(st, &tmap_w, &full_bar[stage], kb * kTileK, (unit / p.chunks) * kTileM, pol_w);
+        tma_load_2d(st + kWTileBytes, &tmap_x, &full_bar[stage], kb * kTileK, (unit % p.chunks) * p.nt, pol_x);
         if (++stage == p.stages) { stage = 0; phase ^= 1; }
       }
     }
@@ -585,7 +596,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
     const int quarter = warp & 3;
     const int m = quarter * 32 + lane;
     float* rsv = xchg + 16 * kTileM;  // [nt] folded-norm scales
-    if (p.fold) {
+    if (p.fold && p.rstd == nullptr) {
       // token t's sum of squares: lane partials over 16-byte pieces in index order, then a butterfly (fixed order)
       for (int t = warp - 2; t < p.nt; t += 4) {
         float ss = 0.f;
@@ -612,7 +623,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
     for (long g = g_begin; g < g_end; ++local) {
       const Piece pc = next_piece(p, g, g_end);
       g += pc.kb1 - pc.kb0;
-      const int tile = pc.tile;
+      const int tile = pc.tile / p.chunks;               // pc.tile is the work unit
+      const int row0 = (pc.tile % p.chunks) * p.nt;     // the unit's first token row
+      const int Tu = min(p.nt, p.T - row0);
+      const float* rs = p.rstd != nullptr ? p.rstd + row0 : rsv;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&acc_full[acc], acc_phase)) { record_error(p.err, kErrTimeoutEpilogue); break; }
@@ -626,9 +640,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
           if (j0 + 16 >= p.nt) { tc_fence_before(); mbar_arrive(&acc_empty[acc]); }
           if (p.fold) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] *= rsv[j0 + i];
+            for (int i = 0; i < 16; ++i) v[i] *= rs[j0 + i];
           }
-          store_chunk(p, tile, m, j0, v, xchg, ep_tid, half);
+          store_chunk(p, tile, m, j0, v, xchg, ep_tid, half, row0, Tu);
         }
         if (p.epi == kAllReduce) tp_finish_tile(p, tile, ep_tid, half, tag, missing);
       } else {
@@ -672,9 +686,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
           auto finish = [&](int j0, float* v) {
             if (p.fold) {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) v[i] *= rsv[j0 + i];
+              for (int i = 0; i < 16; ++i) v[i] *= rs[j0 + i];
             }
-            store_chunk(p, tile, m, j0, v, xchg, ep_tid, half);
+            store_chunk(p, tile, m, j0, v, xchg, ep_tid, half, row0, Tu);
           };
           if (pieces - 1 <= 4) {
             // up to four other pieces: a chunk's pieces are summed as soon as they arrive and the next chunk's loads
@@ -864,6 +878,36 @@ Scratch& scratch(torch::Device dev) {
 torch::Tensor gemm_error_word(torch::Device dev) { return gemm::scratch(dev).err; }
 
 namespace gemm {
+// Prefill GEMMs (set around scan-mode forwards): launches whose epilogue allows it cover every token in one launch of
+// whole (weight tile, 256-token chunk) units, CTA ranges aligned to units. Decode and verify launches keep the
+// token-count-independent stream-K partition that makes a row's result independent of its launch.
+static bool g_prefill = false;
+
+// The folded norm's per-token scale rsqrt(mean(x^2) + eps) of every row of X, one warp per token: lane partials over
+// 16-byte pieces in index order, then a butterfly (the GEMM epilogue's own fold arithmetic).
+__global__ void fold_rstd_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int K, int T, float eps,
+                                 float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + size_t(t) * ldx);
+  float ss = 0.f;
+#pragma unroll 4
+  for (int i = lane; i < K / 8; i += 32) {
+    const uint4 u = xr[i];
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h2[e]);
+      ss = fmaf(f.x, f.x, ss);
+      ss = fmaf(f.y, f.y, ss);
+    }
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) out[t] = rsqrtf(ss / float(K) + eps);
+}
+
 // Checks the operands and launches the GEMM in chunks of at most 256 tokens; ``chunk(p, t0)`` points the chunk's
 // outputs. Returns the number of CTAs launched over all chunks.
 template <class F>
@@ -892,6 +936,45 @@ int launch_chunks(const torch::Tensor& x, const torch::Tensor& w, int epi, F chu
     cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     attr_set = true;
   }
+  const bool unit_epi = epi == kPlain || epi == kResidual || epi == kSwiGLU || epi == kReLU2 || epi == kF32;
+  if (g_prefill && unit_epi && long(n_tiles) * ((T + 255) / 256) >= sms) {
+    // prefill: one launch of whole (tile, chunk) units
+    Params p{};
+    p.T = T;
+    p.N = N;
+    p.K = K;
+    p.chunks = (T + 255) / 256;
+    p.nt = p.chunks > 1 ? 256 : std::max(16, (T + 15) / 16 * 16);
+    p.n_tiles = n_tiles;
+    p.kb_total = kb_total;
+    p.units = n_tiles * p.chunks;
+    p.aligned = 1;
+    p.total = long(p.units) * kb_total;
+    p.epi = epi;
+    p.stages = stage_count(p.nt);
+    const int per = (p.units + sms - 1) / sms;
+    const int ugrid = (p.units + per - 1) / per;
+    p.ws = sc.ws.data_ptr<float>();  // unused: no tile is split
+    p.counters = sc.counters.data_ptr<int>();
+    p.err = sc.err.data_ptr<int>();
+    chunk(p, 0);
+    set_vector_epilogue(p);
+    p.xr = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+    p.ldx = int(x.stride(0));
+    TORCH_CHECK(!p.fold || K % 8 == 0, "gemm: a folded norm needs K % 8 == 0");
+    torch::Tensor rstd;
+    if (p.fold) {
+      rstd = torch::empty({T}, x.options().dtype(torch::kFloat32));
+      C10_CUDA_CHECK(launch_pdl(fold_rstd_kernel, (T + 7) / 8, 256, 0, stream.stream(), p.xr, p.ldx, K, T,
+                                p.fold_eps, rstd.data_ptr<float>()));
+      p.rstd = rstd.data_ptr<float>();
+    }
+    CUtensorMap xmap = make_map(x.data_ptr(), T, K, x.stride(0), p.nt);
+    C10_CUDA_CHECK(launch_pdl(gemm_kernel, ugrid, kThreads, smem_bytes(p.stages, p.nt), stream.stream(), wmap, xmap,
+                              p));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return ugrid;
+  }
   int launched = 0;
   for (int t0 = 0; t0 < T; t0 += 256) {
     const int tc = std::min(256, T - t0);
@@ -902,6 +985,8 @@ int launch_chunks(const torch::Tensor& x, const torch::Tensor& w, int epi, F chu
     p.nt = std::max(16, (tc + 15) / 16 * 16);
     p.n_tiles = n_tiles;
     p.kb_total = kb_total;
+    p.chunks = 1;
+    p.units = n_tiles;
     p.total = total;
     p.epi = epi;
     p.stages = stage_count(p.nt);
@@ -924,6 +1009,9 @@ int launch_chunks(const torch::Tensor& x, const torch::Tensor& w, int epi, F chu
   return launched;
 }
 }  // namespace gemm
+
+// Scan-mode (prefill) forwards switch their GEMMs to whole-unit launches and back.
+void gemm_prefill_mode(bool on) { gemm::g_prefill = on; }
 
 // Launch one GEMM over all T tokens (chunks of 256 tokens per launch).
 // ``fold_eps`` >= 0 folds an RMSNorm into the GEMM (X raw, norm weight pre-multiplied into W's columns).
@@ -1092,6 +1180,8 @@ extern "C" int e4_gemm_bf16_noalloc(const void* x, int ldx, const void* w, int l
   p.nt = std::max(16, (T + 15) / 16 * 16);
   p.n_tiles = n_tiles;
   p.kb_total = kb_total;
+  p.chunks = 1;
+  p.units = n_tiles;
   p.total = total;
   p.epi = kPlain;
   p.stages = stage_count(p.nt);

@@ -231,7 +231,16 @@ class TargetModel:
 
     # ------------------------------------------------------------------ forward
     def forward(self, rb: RowBatch, cache: TargetCache, rec: Optional[Records] = None):
-        """Returns ``(final normed hidden [T, H], aux hidden [T, n_aux * H] or None)``."""
+        """Returns ``(final normed hidden [T, H], aux hidden [T, n_aux * H] or None)``. Scan-mode (prefill) forwards
+        on a GPU run their GEMMs as prefill launches (``native.prefill_gemms``)."""
+        if rb.scan and rb.ids.is_cuda:
+            from eagle4_b200.ops import native
+
+            with native.prefill_gemms():
+                return self._forward(rb, cache, rec)
+        return self._forward(rb, cache, rec)
+
+    def _forward(self, rb: RowBatch, cache: TargetCache, rec: Optional[Records] = None):
         cfg, w = self.cfg, self.w
         eps, off = cfg.rms_norm_eps, cfg.norm_offset
         h = ops.embedding(rb.ids, w["embed"])

@@ -6,6 +6,7 @@ Importing this module on a machine with a GPU loads the extension; if it cannot 
 
 from __future__ import annotations
 
+import contextlib
 import math
 from typing import Dict, Optional, Tuple
 
@@ -68,6 +69,18 @@ def _c2(x: torch.Tensor) -> torch.Tensor:
 
 
 # dense ------------------------------------------------------------------------------------------------------------
+@contextlib.contextmanager
+def prefill_gemms():
+    """GEMMs inside run as prefill launches: every token in one launch of whole (weight tile, 256-token chunk) units
+    (no split tiles, no merges). Only for forwards whose outputs both the speculative and the plain path share
+    (prompt prefill): decode and verify launches keep the partition that is independent of the token count."""
+    _C.gemm_prefill_mode(True)
+    try:
+        yield
+    finally:
+        _C.gemm_prefill_mode(False)
+
+
 def _fold(fold_eps: Optional[float]) -> float:
     return -1.0 if fold_eps is None else float(fold_eps)
 

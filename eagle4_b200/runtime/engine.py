@@ -304,7 +304,13 @@ class Engine:
         keep = min(n, self.verify_tokens)
         lead = n - keep
         if lead:
-            self._draft_rows(nxt[:lead], self.draft.project(aux[:lead]), pos[:lead], slot)
+            if self.device.type == "cuda":  # the prompt's leading rows: prefill GEMM launches
+                from eagle4_b200.ops import native
+
+                with native.prefill_gemms():
+                    self._draft_rows(nxt[:lead], self.draft.project(aux[:lead]), pos[:lead], slot)
+            else:
+                self._draft_rows(nxt[:lead], self.draft.project(aux[:lead]), pos[:lead], slot)
         self.ext_tok[b, :keep] = nxt[lead:]
         self.ext_aux[b, :keep] = aux[lead:]
         self.ext_cnt[b] = keep
