@@ -524,29 +524,44 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
       uint32_t phase = 0;
       // prologue: weight tiles of the first stages, before the dependency wait
       const int pre = int(g_end - g_begin < long(p.stages) ? g_end - g_begin : long(p.stages));
-      // unit u = tile * chunks + chunk: the W tile's rows at (u / chunks) * 128, the X chunk's at (u % chunks) * nt
-      for (int i = 0; i < pre; ++i) {
-        const long gg = g_begin + i;
-        const int unit = int(gg / p.kb_total), kb = int(gg - long(unit) * p.kb_total);
+      // unit u = tile * chunks + chunk: the W tile's rows at (u / chunks) * 128, the X chunk's at (u % chunks) * nt.
+      // The (unit, k-block) position advances incrementally: this one thread issues every load, so its loop stays
+      // free of divisions (the tile and chunk rows are recomputed only when the unit changes).
+      struct Pos {
+        int kb, unit, wrow, xrow;
+      };
+      const int unit0 = int(g_begin / p.kb_total);
+      const Pos start{int(g_begin - long(unit0) * p.kb_total), unit0, (unit0 / p.chunks) * kTileM,
+                      (unit0 % p.chunks) * p.nt};
+      auto advance = [&](Pos& q) {
+        if (++q.kb == p.kb_total) {
+          q.kb = 0;
+          ++q.unit;
+          if (p.chunks == 1) {
+            q.wrow += kTileM;
+          } else {
+            q.wrow = (q.unit / p.chunks) * kTileM;
+            q.xrow = (q.unit % p.chunks) * p.nt;
+          }
+        }
+      };
+      Pos q = start;
+      for (int i = 0; i < pre; ++i, advance(q)) {
         mbar_expect_tx(&full_bar[i], stage_bytes);
-        tma_load_2d(tiles + i * stage_bytes, &tmap_w, &full_bar[i], kb * kTileK, (unit / p.chunks) * kTileM, pol_w);
+        tma_load_2d(tiles + i * stage_bytes, &tmap_w, &full_bar[i], q.kb * kTileK, q.wrow, pol_w);
       }
       pdl_wait();
-      for (int i = 0; i < pre; ++i) {
-        const long gg = g_begin + i;
-        const int unit = int(gg / p.kb_total), kb = int(gg - long(unit) * p.kb_total);
-        tma_load_2d(tiles + i * stage_bytes + kWTileBytes, &tmap_x, &full_bar[i], kb * kTileK,
-                    (unit % p.chunks) * p.nt, pol_x);
-      }
+      q = start;
+      for (int i = 0; i < pre; ++i, advance(q))
+        tma_load_2d(tiles + i * stage_bytes + kWTileBytes, &tmap_x, &full_bar[i], q.kb * kTileK, q.xrow, pol_x);
       stage = pre == p.stages ? 0 : pre;
       phase = pre == p.stages ? 1 : 0;
-      for (long gg = g_begin + pre; gg < g_end && ok; ++gg) {
-        const int unit = int(gg / p.kb_total), kb = int(gg - long(unit) * p.kb_total);
+      for (long gg = g_begin + pre; gg < g_end && ok; ++gg, advance(q)) {
         if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { record_error(p.err, kErrTimeoutProducer); ok = false; break; }
         uint8_t* st = tiles + stage * stage_bytes;
         mbar_expect_tx(&full_bar[stage], stage_bytes);
-        tma_load_2d(st, &tmap_w, &full_bar[stage], kb * kTileK, (unit / p.chunks) * kTileM, pol_w);
-        tma_load_2d(st + kWTileBytes, &tmap_x, &full_bar[stage], kb * kTileK, (unit % p.chunks) * p.nt, pol_x);
+        tma_load_2d(st, &tmap_w, &full_bar[stage], q.kb * kTileK, q.wrow, pol_w);
+        tma_load_2d(st + kWTileBytes, &tmap_x, &full_bar[stage], q.kb * kTileK, q.xrow, pol_x);
         if (++stage == p.stages) { stage = 0; phase ^= 1; }
       }
     }
