@@ -280,7 +280,9 @@ def main() -> None:
         "warmup": args.warmup,
         "ms_per_step": round(spec_ms / args.steps, 3),
         "higher_is_better": True,
-        "scaling": "strong" if tp_mode else "weak",
+        # tensor parallelism splits the same batch over the GPUs (N = 1 included: total work fixed); data-parallel
+        # replicas each serve their own batch
+        "scaling": "weak" if args.parallelism == "dp" and world > 1 else "strong",
         "vs_baseline": round(value / BASELINE_TPS, 4),
         "dtype": "bf16",
         "data": "synthetic: uniform-random prompt ids, random-init N(0,0.02) weights of the named shapes",
