@@ -146,3 +146,32 @@ class HostDrafter:
         cnt = eng.out_cnt[:bs].tolist()
         out = eng.out_tok[:bs].tolist()
         return [row[:c] for row, c in zip(out, cnt)]
+
+
+class ServedTreeRounds:
+    """Served rounds' periods per (batch size, verify width), written to ``<data_path>/rounds/tree.json`` (the served
+    tree schedule's input, ``core.chain_width.served_tree_schedule``): mean round period, mean tokens emitted per
+    request and round, and the round count of every cell. ``flush`` merges the cells into the file (other cells kept);
+    it runs every ``flush_every`` rounds and when the host closes the method."""
+
+    def __init__(self, data_path: str, flush_every: int = 256):
+        self.data_path, self.flush_every = data_path, flush_every
+        self.cells: Dict[Tuple[int, int], List[float]] = {}  # (bs, width) -> [sum us, sum tokens, rounds]
+        self._since = 0
+
+    def record(self, batch_size: int, width: int, round_us: float, tokens_per_request: float) -> None:
+        c = self.cells.setdefault((int(batch_size), int(width)), [0.0, 0.0, 0])
+        c[0] += float(round_us)
+        c[1] += float(tokens_per_request)
+        c[2] += 1
+        self._since += 1
+        if self._since >= self.flush_every:
+            self.flush()
+
+    def flush(self) -> Optional[str]:
+        from eagle4_b200.core.chain_width import merge_tree_rounds
+
+        self._since = 0
+        rows = [{"batch_size": b, "width": w, "round_us": s / n, "accept": max(1.0, a / n), "count": n}
+                for (b, w), (s, a, n) in sorted(self.cells.items()) if n and s > 0]
+        return merge_tree_rounds(self.data_path, rows) if rows else None

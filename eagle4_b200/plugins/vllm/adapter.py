@@ -15,10 +15,11 @@ from typing import Optional
 import torch
 
 from eagle4_b200 import ops
-from eagle4_b200.core.config import HarnessConfig, parse_harness_config
+from eagle4_b200.core.config import HarnessConfig, Mode
 from eagle4_b200.core.draft_tree import rows_meta
 from eagle4_b200.core.limits import req_to_token_span
 from eagle4_b200.plugins.common import accept_greedy_rows, host_base
+from eagle4_b200.plugins.vllm.config import MethodConfig, parse_method_config
 
 METHOD = "eagle_harness"
 
@@ -27,18 +28,17 @@ _Speculator = host_base("vllm.v1.worker.gpu.spec_decode.speculator:DraftModelSpe
 
 
 class HarnessMethodSpec(_MethodSpec):
-    """How vLLM sizes the method: the tree budget from the opaque method config, KV headroom per request."""
+    """How vLLM sizes the method: the tree budget from the opaque method config (``plugins.vllm.config``), KV headroom
+    per request."""
 
     config: Optional[HarnessConfig] = None
-
-    TREE_KEYS = {"node_top_k": 4, "tree_depth": 12, "max_verify_width": 16}  # the vLLM tree's own keys
+    method: Optional[MethodConfig] = None
 
     def configure(self, speculative_config):
-        raw = dict(getattr(speculative_config, "method_config", None) or {})
-        tree = {k: int(raw.pop(k, v)) for k, v in self.TREE_KEYS.items()}
-        self.config = parse_harness_config(raw)
-        self.top_k, self.depth, self.width = tree["node_top_k"], tree["tree_depth"], tree["max_verify_width"]
-        return {"num_speculative_tokens": self.width - 1, "max_verify_width": self.width}
+        self.method = parse_method_config(getattr(speculative_config, "method_config", None))
+        self.config = self.method.harness
+        self.top_k, self.depth, self.width = self.method.node_top_k, self.method.tree_depth, self.method.max_verify_width
+        return {"num_speculative_tokens": self.method.num_speculative_tokens, "max_verify_width": self.width}
 
     def num_lookahead_tokens(self, page_size: int = 1) -> int:
         return req_to_token_span(self.top_k, self.depth, self.width, page_size)
@@ -81,14 +81,42 @@ class HarnessSpeculator(_Speculator):
     ``accept_round`` after it (``eagle_harness/vllm/speculator.py:96,247``)."""
 
     drafter = None
+    batch_policy = None
+    served_rounds = None
 
     def load_model(self, draft_model, *, max_reqs: int, max_len: int, tree=(12, 4, 16), config=None,
-                   temperature: float = 0.0, seed: int = 0) -> None:
-        from eagle4_b200.plugins.host_round import HostDrafter
+                   temperature: float = 0.0, seed: int = 0, method: Optional[MethodConfig] = None) -> None:
+        """``method`` (a parsed ``method_config``) sets the tree, the harness config, the batch policy and the
+        served-round recording; without it ``tree`` = (depth, top-k, verify width) and ``config`` do."""
+        import dataclasses
 
+        from eagle4_b200.core.chain_width import chain_widths
+        from eagle4_b200.plugins.host_round import HostDrafter, ServedTreeRounds
+        from eagle4_b200.plugins.vllm.batch_policy import BatchPolicy
+
+        if method is not None:
+            tree = (method.tree_depth, method.node_top_k, method.max_verify_width)
+            config = method.harness
+            if method.depth_stop_gain is None:  # no depth stop: full-depth trees (the static policy)
+                config = dataclasses.replace(config, mode=Mode.STATIC)
         steps, top_k, width = tree
         self.drafter = HostDrafter(draft_model, max_reqs=max_reqs, max_len=max_len, steps=steps, top_k=top_k,
                                    verify_tokens=width, config=config, temperature=temperature, seed=seed)
+        schedule = None
+        if config is not None and config.data_path:
+            schedule = chain_widths(config.data_path, width, max_reqs, allow_no_spec=True)
+        self.batch_policy = BatchPolicy(verify_batch_limit=self.drafter.engine.verify_batch_limit, schedule=schedule,
+                                        max_num_reqs=max_reqs)
+        if method is not None and method.record_rounds:
+            self.served_rounds = ServedTreeRounds(config.data_path)
+
+    def suspend_drafting(self, num_reqs, req_ids):
+        """vLLM's per-batch hook: True decodes this batch natively."""
+        return self.batch_policy.suspend_drafting(num_reqs, req_ids)
+
+    def verify_budget(self, req_ids, num_draft_tokens):
+        """vLLM's per-batch hook: each request's drafts to verify (a prefix of its tree rows)."""
+        return self.batch_policy.verify_budget(req_ids, num_draft_tokens)
 
     def prefill_request(self, req_id, prompt_ids: torch.Tensor, aux_hidden_states: torch.Tensor, first_token) -> None:
         self.drafter.admit(req_id, prompt_ids, aux_hidden_states, first_token)
@@ -99,12 +127,21 @@ class HarnessSpeculator(_Speculator):
         return self.drafter.propose(req_ids)
 
     def accept_round(self, req_ids, draft_tokens: torch.Tensor, parent_rows: torch.Tensor, target: torch.Tensor,
-                     aux_hidden_states: Optional[torch.Tensor]):
+                     aux_hidden_states: Optional[torch.Tensor], round_us: Optional[float] = None):
         """Accept the verified rows (``target``: ids or logits of the rows) and hand the accepted path to the drafter.
-        Returns (accepted rows, counts, bonus, emitted tokens per request)."""
+        ``round_us``: the host's measured period of this round (recorded when ``record_rounds`` is on). Returns
+        (accepted rows, counts, bonus, emitted tokens per request)."""
         acc, cnt, bonus = self.make_rejection_sampler()(target, draft_tokens, parent_rows)
         emitted = self.drafter.accept(req_ids, draft_tokens, acc, cnt, bonus, aux_hidden_states)
+        if self.served_rounds is not None and round_us:
+            self.served_rounds.record(len(req_ids), draft_tokens.shape[1], round_us,
+                                      sum(len(e) for e in emitted) / max(1, len(emitted)))
         return acc, cnt, bonus, emitted
+
+    def close(self) -> None:
+        """The method ends: recorded served rounds are written."""
+        if self.served_rounds is not None:
+            self.served_rounds.flush()
 
     def finish_request(self, req_id) -> None:
         self.drafter.release(req_id)

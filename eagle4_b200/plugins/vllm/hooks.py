@@ -59,3 +59,30 @@ def missing_hooks() -> List[str]:
 
 
 hook_problems = missing_hooks
+
+
+# Optional speculator hooks: vLLM builds that have them call them per scheduled batch; builds without them skip them
+# (the method still registers). ``plugins.vllm.batch_policy`` answers both.
+OPTIONAL_HOOKS = (
+    HookUse("native decode per batch size", f"{_SPEC}:BaseSpeculator.suspend_drafting", "cpu"),
+    HookUse("drafts verified per batch size", f"{_SPEC}:BaseSpeculator.verify_budget", "cpu"),
+)
+
+
+def host_speculator_hooks() -> List[str]:
+    """The optional hooks this vLLM calls, checked by parameter names against ``batch_policy.SPECULATOR_HOOKS``."""
+    import inspect
+
+    from eagle4_b200.plugins.contract import resolve
+    from eagle4_b200.plugins.vllm.batch_policy import SPECULATOR_HOOKS
+
+    found = []
+    for use in OPTIONAL_HOOKS:
+        name = use.hook.rsplit(".", 1)[1]
+        try:
+            fn = resolve(use.hook)
+        except (ImportError, AttributeError):
+            continue
+        if callable(fn) and tuple(inspect.signature(fn).parameters)[1:] == SPECULATOR_HOOKS[name]:
+            found.append(name)
+    return found
