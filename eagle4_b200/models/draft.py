@@ -18,7 +18,7 @@ Candidate head (EAGLE-4): low-rank scores ``(h @ down^T) @ scores^T`` select the
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Dict, Optional, Tuple
+from typing import Callable, Dict, Optional, Tuple
 
 import torch
 
@@ -80,6 +80,32 @@ class DraftModel:
                 n_extra: torch.Tensor, cache: DraftCache, max_keys: Optional[int] = None
                 ) -> Tuple[torch.Tensor, torch.Tensor]:
         """Returns ``(normed [T, H], next hidden [T, H])``."""
+        x, res = self.layer_input(ids, hidden)
+        qkv = ops.linear(x, self.w["qkv"])
+        q, _ = ops.qkv_prepare(qkv, self.attn_shape, pos, write_slot, cache.k, cache.v, None, None)
+        o = ops.attention(q, cache.k, cache.v, cache.block_table, cache.page, req, ctx_start, ctx_len, extra,
+                          n_extra, self.cfg.head_dim ** -0.5, max_keys)
+        return self.layer_output(o, res)
+
+    def forward_rows(self, ids: torch.Tensor, pos: torch.Tensor, hidden: torch.Tensor,
+                     attend: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
+                     ) -> Tuple[torch.Tensor, torch.Tensor]:
+        """``forward`` with the host's attention: ``attend(q, k, v)`` gets the rows' rotated ``q [T, Hq, D]``, rotated
+        ``k`` and ``v [T, Hkv, D]`` (the host writes them into its own KV cache and attends) and returns
+        ``[T, Hq, D]``. Returns ``(normed, next hidden)`` like ``forward``."""
+        cfg = self.cfg
+        x, res = self.layer_input(ids, hidden)
+        qkv = ops.linear(x, self.w["qkv"])
+        t = qkv.shape[0]
+        # RoPE goes through the same kernel as the engine's rows: it writes the rotated k and the v of row i to slot i
+        k = torch.empty(t, cfg.num_kv_heads, cfg.head_dim, dtype=qkv.dtype, device=qkv.device)
+        v = torch.empty_like(k)
+        slots = torch.arange(t, device=qkv.device)
+        q, _ = ops.qkv_prepare(qkv, self.attn_shape, pos, slots, k, v, None, None)
+        return self.layer_output(attend(q, k, v).reshape(t, -1), res)
+
+    def layer_input(self, ids: torch.Tensor, hidden: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """``(q/k/v projection input, attention residual)`` of the draft layer for token ids and hidden rows."""
         cfg, w = self.cfg, self.w
         eps = cfg.rms_norm_eps
         e = ops.embedding(ids, w["embed"])
@@ -88,10 +114,13 @@ class DraftModel:
         if cfg.attn_norm:  # eh_proj input fusion: the projection is the attention residual, its norm feeds q/k/v
             res = ops.linear(x, w["eh_proj"])
             x = ops.rmsnorm(res, w["pre_attention_layernorm"], eps, False)
-        qkv = ops.linear(x, w["qkv"])
-        q, _ = ops.qkv_prepare(qkv, self.attn_shape, pos, write_slot, cache.k, cache.v, None, None)
-        o = ops.attention(q, cache.k, cache.v, cache.block_table, cache.page, req, ctx_start, ctx_len, extra,
-                          n_extra, cfg.head_dim ** -0.5, max_keys)
+        return x, res
+
+    def layer_output(self, o: torch.Tensor, res: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Attention output ``[T, Hq, D]`` and residual -> ``(normed, next hidden)``: o_proj, MLP (dense or latent
+        MoE), final norm."""
+        cfg, w = self.cfg, self.w
+        eps = cfg.rms_norm_eps
         if self.tp is not None:
             residual, x = self.tp.row_linear(o, w["o_proj"], res, w["post_attention_layernorm"], eps)
             if cfg.moe:  # the MoE is replicated on every rank: no collective after it

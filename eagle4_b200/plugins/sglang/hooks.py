@@ -18,6 +18,7 @@ _VERIFY_INPUT = "sglang.srt.speculative.eagle_info:EagleVerifyInput"
 _EXT = "sglang.srt.layers.attention.linear.verify_extension:LinearAttnVerifyExtension"
 _GRAPH_INFO = "sglang.srt.model_executor.runner.decode_graph_variants:DecodeGraphRunnerInfo"
 _COMMON = "sglang.srt.speculative.eagle_worker_common"
+_LOGITS = "sglang.srt.layers.logits_processor:LogitsProcessor"
 
 MY_ALGO = "eagle4_b200.plugins.sglang.adapter:HarnessSpecAlgo"
 MY_WORKER = "eagle4_b200.plugins.sglang.adapter:HarnessWorker"
@@ -65,6 +66,10 @@ HOOKS = (
     Hook(f"{_EXT}.conv_update", CONV_ARGS, OVERRIDE, MY_MAMBA),
     Hook(f"{_SPEC_INPUT}.greedy_tokens_only", (), FIELD),
     Hook("sglang.srt.layers.logits_processor:LogitsProcessorOutput.next_token_ids", (), FIELD),
+    # the candidate-logits processor of the draft's prefill path (plugins.candidate_logits)
+    Hook(f"{_LOGITS}._get_logits", ("hidden_states", "lm_head", "logits_metadata", "embedding_bias",
+                                    "use_logits_buffer"), OVERRIDE, optional=True),
+    Hook(f"{_LOGITS}._copy_logits_to_buffer", ("logits", "logits_metadata", "use_buffer"), optional=True),
     Hook(f"{_VERIFY_INPUT}.prepared_out_cache_loc", (), FIELD),
     Hook(f"{_SPEC_INPUT}.flashinfer_verify_variant", ("bs", "num_tokens", "q_dtype", "kv_dtype", "head_dim"),
          OVERRIDE, MY_VERIFY_INPUT),

@@ -11,7 +11,7 @@ from __future__ import annotations
 import importlib
 from typing import List, NamedTuple, Optional
 
-from eagle4_b200.plugins.contract import CALL, EXISTS, Hook, problems
+from eagle4_b200.plugins.contract import CALL, EXISTS, OVERRIDE, Hook, override_mismatches, problems
 
 RELEASE_MIN_API_VERSION = 4
 CAPABILITY_API_VERSIONS = frozenset({3})
@@ -62,7 +62,9 @@ HOOKS = (
     Hook(f"{_BASE}.release_round_graphs", (), EXISTS),
     Hook("tokenspeed.runtime.layers.attention.backends.base:AttentionBackend.begin_tree_lanes", ("bs", "live_bs")),
     Hook("tokenspeed.runtime.layers.attention.backends.paged.tree_verify:TreeDraftInputs.set_frontier", (), EXISTS),
-    Hook("tokenspeed.runtime.models.llama_eagle3:LlamaForCausalLMEagle3.exit_logits", (), EXISTS),
+    Hook("tokenspeed.runtime.models.llama_eagle3:LlamaForCausalLMEagle3.exit_logits",
+         ("input_ids", "hidden_states", "aux_hidden_states", "ctx"), OVERRIDE,
+         "eagle4_b200.plugins.tokenspeed.models:LlamaForCausalLMEagle4"),
     Hook("tokenspeed.runtime.execution.context:ForwardContext.gather_ids", (), EXISTS),
     Hook("tokenspeed.runtime.distributed.comm_ops:all_gather", ("tensor", "group", "dim")),
 )
@@ -114,3 +116,8 @@ def hook_problems() -> List[str]:
 
 def sampled_hook_problems() -> List[str]:
     return problems(SAMPLED_HOOKS)
+
+
+def adapter_problems() -> List[str]:
+    """This package's overrides whose signatures differ from the table (checked without TokenSpeed)."""
+    return override_mismatches(HOOKS)

@@ -18,7 +18,7 @@ def register() -> bool:
         return False
     from tokenspeed.runtime.plugins.registry import register_drafter, register_model
 
-    from eagle4_b200.plugins.sglang.models.llama_eagle4 import LlamaForCausalLMEagle4
+    from eagle4_b200.plugins.tokenspeed.models import LlamaForCausalLMEagle4
     from eagle4_b200.plugins.tokenspeed.adapter import ALGORITHM, HarnessDrafter
 
     register_model(cls=LlamaForCausalLMEagle4, architectures=[DRAFT_ARCHITECTURE])

@@ -86,7 +86,8 @@ class HarnessSpeculator(_Speculator):
 
     def load_model(self, draft_model, *, max_reqs: int, max_len: int, tree=(12, 4, 16), config=None,
                    temperature: float = 0.0, seed: int = 0, method: Optional[MethodConfig] = None) -> None:
-        """``method`` (a parsed ``method_config``) sets the tree, the harness config, the batch policy and the
+        """``draft_model``: a ``DraftModel`` or the vLLM draft model class holding one. ``method`` (a parsed
+        ``method_config``) sets the tree, the harness config, the batch policy and the
         served-round recording; without it ``tree`` = (depth, top-k, verify width) and ``config`` do."""
         import dataclasses
 
@@ -94,6 +95,12 @@ class HarnessSpeculator(_Speculator):
         from eagle4_b200.plugins.host_round import HostDrafter, ServedTreeRounds
         from eagle4_b200.plugins.vllm.batch_policy import BatchPolicy
 
+        from eagle4_b200.models.draft import DraftModel
+
+        if not isinstance(draft_model, DraftModel):  # vLLM's model class (plugins.vllm.models) after load_weights
+            draft_model = draft_model.draft
+            if draft_model is None:
+                raise RuntimeError("the draft model's weights are not loaded")
         if method is not None:
             tree = (method.tree_depth, method.node_top_k, method.max_verify_width)
             config = method.harness

@@ -26,8 +26,10 @@ def _install(tmp_path, monkeypatch, hooks, extra, top):
 
 def test_adapter_overrides_match_hook_tables():
     from eagle4_b200.plugins.sglang.hooks import adapter_problems
+    from eagle4_b200.plugins.tokenspeed.hooks import adapter_problems as tokenspeed_problems
 
     assert adapter_problems() == []
+    assert tokenspeed_problems() == []
 
 
 def test_sglang_registers_on_matching_host(tmp_path, monkeypatch):
