@@ -131,14 +131,18 @@ def _load_safetensors_dir(path: str, device) -> dict:
 
 
 def from_pretrained(model_path: str, draft_path: Optional[str] = None, *, device="cuda", dtype=torch.bfloat16,
-                    tree: TreeSpec = TreeSpec(), max_batch: int = 1, max_len: int = 4096, config=None) -> LLM:
+                    tree: TreeSpec = TreeSpec(), max_batch: int = 1, max_len: int = 4096, config=None,
+                    tp=None) -> LLM:
     """An :class:`LLM` from a Hugging Face target directory and an EAGLE-4 / EAGLE-3 draft directory (both with
-    ``config.json`` and safetensors). Draft configs are validated; structures this package does not build raise."""
+    ``config.json`` and safetensors). Draft configs are validated; structures this package does not build raise.
+    With ``tp`` (a :class:`~eagle4_b200.parallel.tp.TensorParallel`) every rank reads the full checkpoints into host
+    memory, keeps its shard and moves only that to its GPU."""
     import json
     import os
 
     from eagle4_b200.models.configs import TargetConfig
     from eagle4_b200.models.eagle4_config import draft_config_from_hf
+    from eagle4_b200.parallel.sharding import shard_draft, shard_target
 
     with open(os.path.join(model_path, "config.json"), encoding="utf-8") as f:
         tcfg = TargetConfig.from_hf(json.load(f))
@@ -148,10 +152,16 @@ def from_pretrained(model_path: str, draft_path: Optional[str] = None, *, device
         with open(os.path.join(draft_path, "config.json"), encoding="utf-8") as f:
             dcfg = draft_config_from_hf(json.load(f), target_vocab_size=tcfg.vocab_size)
         aux = dcfg.aux_layer_ids
+    world, rank = (tp.world, tp.rank) if tp is not None else (1, 0)
     sd = {k: v.to(dtype) if v.is_floating_point() else v for k, v in _load_safetensors_dir(model_path, "cpu").items()}
-    tw = {k: v.to(device) for k, v in weights.target_from_hf(tcfg, sd).items()}
+    full = weights.target_from_hf(tcfg, sd)
     del sd
-    target = TargetModel(tcfg, tw, aux_layer_ids=aux)
+    ltcfg, tw = shard_target(tcfg, full, world, rank)
+    tw = {k: v.to(device) for k, v in tw.items()}
+    target = TargetModel(ltcfg, tw, aux_layer_ids=aux, tp=tp)
     if draft_path is not None:
-        dm = DraftModel(dcfg, weights.load_draft(draft_path, dcfg, device=device, dtype=dtype, embed=tw["embed"]))
+        ldcfg, dw = shard_draft(dcfg, weights.load_draft(draft_path, dcfg, device="cpu", dtype=dtype,
+                                                         embed=full["embed"]), world, rank)
+        dm = DraftModel(ldcfg, {k: v.to(device) for k, v in dw.items()}, tp=tp)
+    del full
     return LLM(target, dm, tree=tree, max_batch=max_batch, max_len=max_len, config=config)

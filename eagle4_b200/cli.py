@@ -38,15 +38,20 @@ def _model_args(args) -> dict:
     return {"model": args.model, "draft": args.draft}
 
 
-def build_llm(model: str, draft: Optional[str], *, max_batch: int, max_len: int, tree, device: str = "cuda",
-              config=None):
-    """A named synthetic shape (random weights) or a checkpoint directory pair."""
+def build_llm(model: str, draft: Optional[str], *, max_batch: int, max_len: int, tree, device="cuda",
+              config=None, tp=None, dtype=None):
+    """A named synthetic shape (random weights) or a checkpoint directory pair; ``tp``: this rank's
+    :class:`~eagle4_b200.parallel.tp.TensorParallel` (the weights are sharded over its group)."""
+    import torch
+
     from eagle4_b200.api import LLM, NAMED, from_pretrained
 
+    dtype = dtype or torch.bfloat16
     if model in NAMED:
-        return LLM.synthetic(model, device=device, tree=tree, max_batch=max_batch, max_len=max_len, config=config)
+        return LLM.synthetic(model, device=device, tree=tree, max_batch=max_batch, max_len=max_len, config=config,
+                             tp=tp, dtype=dtype)
     return from_pretrained(model, draft, device=device, tree=tree, max_batch=max_batch, max_len=max_len,
-                           config=config)
+                           config=config, tp=tp, dtype=dtype)
 
 
 def serve_config(output: Path) -> dict:

@@ -2,6 +2,8 @@
 
     python -m eagle4_b200.serve --model qwen3.8-27b [--draft DIR] [--config JSON] [--max-batch 8] [--port 8000]
     python -m eagle4_b200.serve --model qwen3.8-27b --no-spec ...        # plain decode (parity reference)
+    python -m torch.distributed.run --nproc-per-node 8 --master-addr 127.0.0.1 -m eagle4_b200.serve --model ...
+                                                                          # tensor-parallel over 8 GPUs
 
 ``POST /v1/generate`` with ``{"prompt_ids": [...], "max_new_tokens": n, "stop_token_ids": [...], "eos_token_id": e,
 "ignore_eos": false}`` returns ``{"output_ids": [...], "finish_reason": "length" | "stop" | "eos", "meta": {...}}``.
@@ -35,46 +37,87 @@ except ImportError:  # the HTTP layer is optional; Batcher works without it
 
 class Batcher:
     """The serving loop: submitted requests enter the scheduler between rounds; each caller's future resolves
-    when its request finishes."""
+    when its request finishes. With ``lockstep`` (tensor-parallel serving, rank 0) every step's submissions are
+    first broadcast to the other ranks, which mirror them (:func:`eagle4_b200.runtime.lockstep.follow`)."""
 
-    def __init__(self, engine, max_batch: Optional[int] = None, *, speculative: bool = True):
+    def __init__(self, engine, max_batch: Optional[int] = None, *, speculative: bool = True, lockstep=None):
         self.engine = engine
         self.sched = Scheduler(engine, speculative=speculative)
+        self.lockstep = lockstep
         self.q: "queue.Queue" = queue.Queue()
         self.stop = threading.Event()
         self.futures = {}
+        self.failed: Optional[BaseException] = None
         self.thread = threading.Thread(target=self._loop, daemon=True)
         self.thread.start()
 
     def submit(self, prompt: List[int], params: RequestParams = RequestParams()) -> Future:
         fut: Future = Future()
+        if self.failed is not None:
+            fut.set_exception(RuntimeError(f"serving stopped after an engine error: {self.failed}"))
+            return fut
         self.q.put((prompt, params, fut))
         return fut
 
-    def _drain(self, block: bool) -> None:
+    def close(self, timeout: Optional[float] = None) -> None:
+        """Stop serving (followers are told to stop too); requests still queued are not run."""
+        self.stop.set()
+        self.thread.join(timeout)
+
+    def _drain(self, block: bool) -> list:
+        got = []
         while True:
             try:
-                prompt, params, fut = self.q.get(timeout=0.05) if block else self.q.get_nowait()
+                got.append(self.q.get(timeout=0.05) if block and not got else self.q.get_nowait())
             except queue.Empty:
-                return
-            block = False
-            try:
-                req = self.sched.submit(prompt, params)
-                self.futures[req.rid] = fut
-            except Exception as e:  # noqa: BLE001 - a request the scheduler refuses fails alone
-                fut.set_exception(e)
+                return got
+
+    def _admit(self, subs: list) -> None:
+        from eagle4_b200.runtime.lockstep import Command, apply
+
+        for (_, _, fut), got in zip(subs, apply(self.sched, Command([(p, params) for p, params, _ in subs]))):
+            if isinstance(got, Exception):
+                fut.set_exception(got)
+            else:
+                self.futures[got.rid] = fut
+
+    def _fail(self, e: BaseException) -> None:
+        for fut in self.futures.values():
+            fut.set_exception(e)
+        self.futures.clear()
 
     def _loop(self) -> None:
-        while not self.stop.is_set():
-            self._drain(block=self.sched.idle)
+        import time
+
+        from eagle4_b200.runtime.lockstep import Command
+
+        last = time.monotonic()
+        while True:
+            stopping = self.stop.is_set()
+            subs = [] if stopping else self._drain(block=self.sched.idle)
+            if self.lockstep is not None:
+                now = time.monotonic()
+                if stopping or subs or not self.sched.idle or now - last >= self.lockstep.beat_s:
+                    self.lockstep.exchange(Command([(list(map(int, p)), params) for p, params, _ in subs],
+                                                   stop=stopping))
+                    last = now
+            if stopping:
+                return
+            if subs:
+                self._admit(subs)
             if self.sched.idle:
                 continue
             try:
                 finished = self.sched.step()
             except Exception as e:  # noqa: BLE001 - the engine failed: every request in flight gets the error
-                for fut in self.futures.values():
-                    fut.set_exception(e)
-                self.futures.clear()
+                self._fail(e)
+                if self.lockstep is not None:  # ranks may be out of step: stop serving (a restart recovers)
+                    self.failed = e
+                    try:  # best effort: followers still waiting for a command end cleanly
+                        self.lockstep.exchange(Command(stop=True))
+                    except Exception:  # noqa: BLE001 - the group may be gone already
+                        pass
+                    return
                 self.sched = Scheduler(self.engine, speculative=self.sched.speculative)
                 continue
             for req in finished:
@@ -104,13 +147,19 @@ def make_app(batcher: Batcher):
     @app.get("/health")
     def health():
         st = batcher.engine.stats
+        tp = batcher.engine.target.tp
         return {"queued": batcher.q.qsize() + len(batcher.sched.waiting), "running": len(batcher.sched.running),
-                "rounds": st.rounds, "mean_accept": st.mean_accept}
+                "rounds": st.rounds, "mean_accept": st.mean_accept, "tensor_parallel": tp.world if tp else 1,
+                "failed": None if batcher.failed is None else str(batcher.failed)}
 
     return app
 
 
 def main(argv: Optional[List[str]] = None) -> int:
+    """One process per GPU: launched by ``torch.distributed.run`` with ``--nproc-per-node N`` the model is
+    tensor-parallel over the N ranks; rank 0 serves HTTP and leads, the other ranks follow its scheduler."""
+    import os
+
     ap = argparse.ArgumentParser(prog="eagle4_b200.serve")
     ap.add_argument("--model", required=True)
     ap.add_argument("--draft")
@@ -120,16 +169,50 @@ def main(argv: Optional[List[str]] = None) -> int:
     ap.add_argument("--no-spec", action="store_true", help="plain decode (the parity reference server)")
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--tp-backend", default="fused", choices=["fused", "torch"],
+                    help="tensor-parallel collectives: fused peer-memory kernels, or NCCL through torch")
     args = ap.parse_args(argv)
-    import uvicorn
 
     from eagle4_b200.api import TreeSpec
     from eagle4_b200.cli import build_llm
 
+    tp = lockstep = None
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        from eagle4_b200.parallel.tp import TensorParallel
+        from eagle4_b200.runtime.lockstep import Lockstep
+
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        tp = TensorParallel(backend=args.tp_backend, max_rows=max(256, args.max_batch * 32), max_cols=8192)
+        lockstep = Lockstep()
     llm = build_llm(args.model, args.draft, max_batch=args.max_batch, max_len=args.max_len, tree=TreeSpec(),
-                    config=args.config)
-    uvicorn.run(make_app(Batcher(llm.engine, speculative=not args.no_spec)), host=args.host, port=args.port)
-    return 0
+                    config=args.config, tp=tp)
+    speculative = not args.no_spec
+    try:
+        if lockstep is not None and not lockstep.leader:
+            from eagle4_b200.runtime.lockstep import follow
+
+            follow(llm.engine, lockstep, speculative=speculative)
+            return 0
+        import uvicorn
+
+        batcher = Batcher(llm.engine, speculative=speculative, lockstep=lockstep)
+        try:
+            uvicorn.run(make_app(batcher), host=args.host, port=args.port)
+        finally:
+            batcher.close()
+        return 0 if batcher.failed is None else 1
+    finally:
+        if tp is not None:
+            tp.close()
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
 
 
 if __name__ == "__main__":
