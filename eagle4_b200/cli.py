@@ -4,6 +4,8 @@
 sweep, one CUDA graph per timed shape), fits the cost tables into a fresh directory and prints the serving config
 that uses them (reference ``eagle_harness/cli.py:268-345``, which drives an SGLang or vLLM server instead; the
 settings and output layout are the same: ``settings.json``, the calibration ``data_path`` and ``serve.sh``).
+With ``--tp N`` the command supervises N workers (one per GPU, ``torch.distributed.run``) in a process group of its
+own and ends the group on a failure, an interrupt or ``--timeout``; ``serve.sh`` is written only when they succeed.
 ``check`` reports the serving hosts this package plugs into and, with ``--kernels``, loads the native library.
 """
 
@@ -58,30 +60,44 @@ def serve_config(output: Path) -> dict:
     return {"mode": "serve", "data_path": str(output)}
 
 
-def _calibrate(args) -> int:
+def _serve_command(args) -> str:
+    serve = ["--model", args.model] + (["--draft", args.draft] if args.draft else []) + \
+        ["--config", json.dumps(serve_config(args.output))]
+    if args.tp > 1:
+        launch = ["python", "-m", "torch.distributed.run", "--nnodes", "1", "--nproc-per-node", str(args.tp),
+                  "--master-addr", "127.0.0.1", "-m", "eagle4_b200.serve"]
+    else:
+        launch = ["python", "-m", "eagle4_b200.serve"]
+    return " ".join(shlex.quote(x) for x in launch + serve)
+
+
+def _worker_args(args) -> List[str]:
+    """The calibrate arguments of one tensor-parallel worker (the same measurement, run as one rank)."""
+    out = ["calibrate", "--model", args.model, "--output", str(args.output), "--tp", str(args.tp), "--worker",
+           "--batch-sizes", ",".join(map(str, args.batch_sizes)), "--context-step", str(args.context_step),
+           "--context-stop", str(args.context_stop), "--repeats", str(args.repeats), "--steps", str(args.steps),
+           "--top-k", str(args.top_k), "--draft-tokens", str(args.draft_tokens), "--kind", args.kind]
+    if args.draft:
+        out += ["--draft", args.draft]
+    if args.package:
+        out.append("--package")
+    return out
+
+
+def _measure(args, tp=None) -> dict:
+    """Build the engine (this rank's shard under ``tp``), measure, fit and optionally package; returns the cost
+    model's problems per batch size."""
     import torch
 
     from eagle4_b200.api import TreeSpec
     from eagle4_b200.core.live_costs import CostKey
     from eagle4_b200.runtime.calibrate import calibrate
 
-    if not torch.cuda.is_available() and not args.dry_run:
-        raise RuntimeError("calibration times the GPU; no CUDA device is visible")
-    args.output = (args.output or Path("eagle4-calibration")).resolve()
-    settings = {k: str(v) if isinstance(v, Path) else v for k, v in vars(args).items() if k != "func"}
-    command = f"python -m eagle4_b200.serve --model {shlex.quote(args.model)}" + (
-        f" --draft {shlex.quote(args.draft)}" if args.draft else "") + \
-        f" --config {shlex.quote(json.dumps(serve_config(args.output)))}"
-    if args.dry_run:
-        print(json.dumps(settings, indent=2))
-        print(command)
-        return 0
-    args.output.mkdir(parents=True, exist_ok=False)
-    (args.output / "settings.json").write_text(json.dumps(settings, indent=2) + "\n")
+    world, rank = (tp.world, tp.rank) if tp is not None else (1, 0)
     tree = TreeSpec(args.steps, 1 if args.kind == "chain" else args.top_k, args.draft_tokens)
     llm = build_llm(args.model, args.draft, max_batch=max(args.batch_sizes), max_len=args.context_stop + 256,
-                    tree=tree)
-    key = CostKey(gpu=torch.cuda.get_device_name(), gpu_count=1, model=args.model, draft=str(args.draft or ""),
+                    tree=tree, tp=tp)
+    key = CostKey(gpu=torch.cuda.get_device_name(), gpu_count=world, model=args.model, draft=str(args.draft or ""),
                   engine="eagle4_b200", dtype="bfloat16")
     if args.kind == "chain":
         from eagle4_b200.runtime.calibrate import calibrate_chain
@@ -92,18 +108,123 @@ def _calibrate(args) -> int:
         problems = calibrate(llm.engine, str(args.output), batch_sizes=args.batch_sizes,
                              context_step=args.context_step, context_stop=args.context_stop, repeats=args.repeats,
                              key=key)
-    if args.package:
+    if args.package and rank == 0:
         from eagle4_b200.core.cost_profiles import write_profile
 
         # the directory doubles as a packaged profile: matched by device, TP size and the models' shapes
-        write_profile(str(args.output), devices=[torch.cuda.get_device_name()], tp_size=1,
-                      target_config=llm.target.cfg.to_hf(), draft_config=llm.draft.cfg.to_hf())
-    bad = {b: p for b, p in problems.items() if p}
-    for b, p in bad.items():
-        print(f"batch size {b}: the cost model refuses these costs ({p}); rounds there keep the fixed shape")
+        tcfg, dcfg = _full_configs(args) if world > 1 else (llm.target.cfg, llm.draft.cfg)
+        write_profile(str(args.output), devices=[torch.cuda.get_device_name()], tp_size=world,
+                      target_config=tcfg.to_hf(), draft_config=dcfg.to_hf())
+    return problems
+
+
+def _full_configs(args):
+    """The whole (unsharded) target and draft configs of ``--model`` / ``--draft``."""
+    from eagle4_b200.api import NAMED
+    from eagle4_b200.models.configs import TargetConfig
+    from eagle4_b200.models.eagle4_config import draft_config_from_hf
+
+    if args.model in NAMED:
+        tcfg = NAMED[args.model][0]()
+        return tcfg, NAMED[args.model][1](tcfg)
+    tcfg = TargetConfig.from_hf(json.loads((Path(args.model) / "config.json").read_text()))
+    dcfg = draft_config_from_hf(json.loads((Path(args.draft) / "config.json").read_text()),
+                                target_vocab_size=tcfg.vocab_size)
+    return tcfg, dcfg
+
+
+def _report(problems: dict) -> None:
+    for b, p in problems.items():
+        if p:
+            print(f"batch size {b}: the cost model refuses these costs ({p}); rounds there keep the fixed shape")
+
+
+def _calibrate_worker(args) -> int:
+    """One rank of a tensor-parallel calibration (launched by the supervising ``calibrate --tp N``)."""
+    import datetime
+    import os
+
+    import torch
+    import torch.distributed as dist
+
+    from eagle4_b200.parallel.tp import TensorParallel
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    if dist.get_world_size() != args.tp:
+        raise RuntimeError(f"launched with {dist.get_world_size()} ranks for --tp {args.tp}")
+    tp = TensorParallel(max_rows=max(256, max(args.batch_sizes) * args.draft_tokens), max_cols=8192)
+    try:
+        problems = _measure(args, tp)
+        if tp.rank == 0:
+            _report(problems)
+    finally:
+        tp.close()
+        dist.destroy_process_group()
+    return 0
+
+
+def _calibrate_tp(args) -> int:
+    """Supervise ``--tp N`` workers (one per GPU) in a process group of their own: the group is ended on a failure,
+    a time-out or an interrupt; measurements written so far stay; ``serve.sh`` is written only on success."""
+    import torch
+
+    from eagle4_b200.runtime.supervise import supervise, torchrun
+
+    cmd = torchrun(args.tp, "eagle4_b200.cli", _worker_args(args))
+    if args.dry_run:
+        print(json.dumps(_settings(args), indent=2))
+        print(" ".join(shlex.quote(x) for x in cmd))
+        print(_serve_command(args))
+        return 0
+    if torch.cuda.device_count() < args.tp:
+        raise RuntimeError(f"--tp {args.tp} needs {args.tp} GPUs; {torch.cuda.device_count()} are visible")
+    args.output.mkdir(parents=True, exist_ok=False)
+    (args.output / "settings.json").write_text(json.dumps(_settings(args), indent=2) + "\n")
+    out = supervise(cmd, timeout=args.timeout)
+    if out.timed_out:
+        print(f"eagle4-b200: calibration passed --timeout {args.timeout:g} s and was stopped; partial measurements "
+              f"remain in {args.output}", file=sys.stderr)
+        return out.code
+    if out.interrupted:
+        print(f"eagle4-b200: interrupted; partial measurements remain in {args.output}.", file=sys.stderr)
+        return out.code
+    if not out.ok:
+        print(f"eagle4-b200: calibration workers failed (exit code {out.code}); partial measurements remain in "
+              f"{args.output}", file=sys.stderr)
+        return out.code
+    return _finish(args)
+
+
+def _settings(args) -> dict:
+    return {k: str(v) if isinstance(v, Path) else v for k, v in vars(args).items() if k not in ("func", "worker")}
+
+
+def _finish(args) -> int:
+    command = _serve_command(args)
     (args.output / "serve.sh").write_text("#!/bin/sh\nset -eu\nexec " + command + "\n")
     print(f"Calibration saved in {args.output}. Serve with:\nsh {shlex.quote(str(args.output / 'serve.sh'))}")
     return 0
+
+
+def _calibrate(args) -> int:
+    import torch
+
+    args.output = (args.output or Path("eagle4-calibration")).resolve()
+    if args.worker:
+        return _calibrate_worker(args)
+    if args.tp > 1:
+        return _calibrate_tp(args)
+    if not torch.cuda.is_available() and not args.dry_run:
+        raise RuntimeError("calibration times the GPU; no CUDA device is visible")
+    if args.dry_run:
+        print(json.dumps(_settings(args), indent=2))
+        print(_serve_command(args))
+        return 0
+    args.output.mkdir(parents=True, exist_ok=False)
+    (args.output / "settings.json").write_text(json.dumps(_settings(args), indent=2) + "\n")
+    _report(_measure(args))
+    return _finish(args)
 
 
 def main(argv: Optional[List[str]] = None) -> int:
@@ -126,6 +247,10 @@ def main(argv: Optional[List[str]] = None) -> int:
     cal.add_argument("--dry-run", action="store_true", help="print settings and the serving command only")
     cal.add_argument("--package", action="store_true",
                      help="also write profile.json so the directory can ship as a packaged cost profile")
+    cal.add_argument("--tp", type=_positive, default=1,
+                     help="tensor-parallel GPUs: one worker per GPU under torch.distributed.run, supervised")
+    cal.add_argument("--timeout", type=float, help="seconds before a --tp calibration is stopped (default: none)")
+    cal.add_argument("--worker", action="store_true", help=argparse.SUPPRESS)
     cal.set_defaults(func=_calibrate)
     chk = sub.add_parser("check", help="report the serving hosts and the native library")
     chk.add_argument("--kernels", action="store_true", help="also load the native CUDA library")

@@ -53,6 +53,11 @@ class _Shape:
             self.build()
 
 
+def _gen(dev, bs: int, q: int) -> torch.Generator:
+    """The timed rows' random inputs: the same on every tensor-parallel rank."""
+    return torch.Generator(device=dev).manual_seed(1009 * bs + q)
+
+
 class ForwardTimer:
     """Times target and draft forwards of an :class:`~eagle4_b200.runtime.engine.Engine` at any (bs, q, ctx)."""
 
@@ -71,7 +76,7 @@ class ForwardTimer:
         req = eng.slot[:bs].repeat_interleave(q)
         ctx = torch.zeros(bs, dtype=torch.int64, device=dev)
         r = torch.arange(q, device=dev)
-        ids = torch.randint(0, eng.target.cfg.vocab_size, (n,), device=dev)
+        ids = torch.randint(0, eng.target.cfg.vocab_size, (n,), device=dev, generator=_gen(dev, bs, q))
         tri = (r[None, :] <= r[:, None])  # [q, q] row i sees rows 0..i
         parent = (torch.arange(n, device=dev) - 1).int()
         parent[::q] = -1
@@ -97,8 +102,9 @@ class ForwardTimer:
         req = eng.slot[:bs].repeat_interleave(q)
         ctx = torch.zeros(bs, dtype=torch.int64, device=dev)
         lane = torch.arange(q, device=dev).repeat(bs)
-        ids = torch.randint(0, eng.target.cfg.vocab_size, (n,), device=dev)
-        hidden = (torch.randn(n, draft.cfg.hidden_size, device=dev) * 0.5).to(eng.dtype)
+        g = _gen(dev, bs, q)
+        ids = torch.randint(0, eng.target.cfg.vocab_size, (n,), device=dev, generator=g)
+        hidden = (torch.randn(n, draft.cfg.hidden_size, device=dev, generator=g) * 0.5).to(eng.dtype)
         w = draft.cfg.sliding_window
         k = max(q, eng.top_k)
 
@@ -136,7 +142,10 @@ class ForwardTimer:
                 t0 = time.perf_counter()
                 shape.run()
                 samples.append((time.perf_counter() - t0) * 1e6)
-        return statistics.median(samples)
+        med = statistics.median(samples)
+        tp = self.eng.target.tp
+        # tensor parallel: a step takes as long as its slowest rank, and every rank must fit the same tables
+        return tp.max_over_ranks([med])[0] if tp is not None and tp.world > 1 else med
 
 
 def engine_attention_shapes(engine) -> Tuple[AttentionShape, AttentionShape]:
@@ -151,7 +160,8 @@ def calibrate(engine, data_path: str, *, batch_sizes: Sequence[int], context_ste
               context_stop: int = 4096, intensity: ComputeIntensity = ComputeIntensity.HIGH, repeats: int = 10,
               key: Optional[CostKey] = None, progress: Callable[[str], None] = print) -> Dict[int, Optional[str]]:
     """Measure and fit every batch size into ``data_path``; returns ``{batch size: problem or None}`` from the cost
-    model's table checks."""
+    model's table checks. Under tensor parallelism every rank runs the same timed forwards (each time is the maximum
+    over the ranks), rank 0 alone writes the files (fitted with the TP size) and every rank returns its checks."""
     if engine.draft is None:
         raise ValueError("calibration needs a draft model")
     if max(batch_sizes) > engine.max_reqs:
@@ -159,6 +169,9 @@ def calibrate(engine, data_path: str, *, batch_sizes: Sequence[int], context_ste
     if context_stop + 2 * engine.verify_tokens > engine.max_len:
         raise ValueError(f"context_stop {context_stop} does not fit the engine's max_len {engine.max_len}")
     paths = CalibrationPaths(data_path)
+    world, writer = _tp_role(engine)
+    if not writer:
+        progress = _quiet
     timer = ForwardTimer(engine, repeats)
     draft_shape, target_shape = engine_attention_shapes(engine)
     contexts = list(range(context_step, context_stop + 1, context_step))
@@ -173,9 +186,12 @@ def calibrate(engine, data_path: str, *, batch_sizes: Sequence[int], context_ste
             progress(f"bs {bs} {model}: " + ", ".join(
                 f"q{q}={statistics.median(t.time_us for t in timings[model] if t.query_length == q):.0f}us"
                 for q in qs))
-        fit_step_timings(paths, params, intensity, (draft_shape, timings["slm"]), (target_shape, timings["llm"]))
-    if key is not None:
+        if writer:
+            fit_step_timings(paths, params, intensity, (draft_shape, timings["slm"]), (target_shape, timings["llm"]),
+                             tp_size=world)
+    if key is not None and writer:
         write_key(data_path, key)
+    _files_written(engine)
     tables = load_cost_tables(paths.cost)
     return {bs: cost_model_problem(t, target_is_moe=engine.target.cfg.is_moe) for bs, t in tables.items()}
 
@@ -190,6 +206,9 @@ def calibrate_chain(engine, data_path: str, *, batch_sizes: Sequence[int], promp
     ``engine`` must be a chain engine (top-k 1); width 1 is root-only verification."""
     from eagle4_b200.core.chain_width import save_accept_profile, save_round_times
 
+    _, writer = _tp_role(engine)
+    if not writer:
+        progress = _quiet
     if engine.draft is None or engine.top_k != 1:
         raise ValueError("chain calibration needs a draft and a top-k 1 (chain) engine")
     widths = sorted(widths or range(1, engine.verify_tokens + 1))
@@ -214,12 +233,33 @@ def calibrate_chain(engine, data_path: str, *, batch_sizes: Sequence[int], promp
                 progress(f"bs {bs} width {w}: {rows[-1]['round_us']:.0f} us per round")
     finally:
         engine.chain_policy = saved_policy
-    save_round_times(data_path, rows)
-    if drafts:
-        save_accept_profile(data_path, drafts, accepted)
-    if key is not None:
-        write_key(data_path, key)
+    if writer:  # round periods are already the maximum over the ranks (the engine reduces them before recording)
+        save_round_times(data_path, rows)
+        if drafts:
+            save_accept_profile(data_path, drafts, accepted)
+        if key is not None:
+            write_key(data_path, key)
+    _files_written(engine)
     return data_path
+
+
+def _tp_role(engine) -> Tuple[int, bool]:
+    """(tensor-parallel world size, whether this rank writes the calibration files)."""
+    tp = engine.target.tp
+    return (tp.world, tp.rank == 0) if tp is not None else (1, True)
+
+
+def _files_written(engine) -> None:
+    """Every rank waits until rank 0's files are on disk."""
+    tp = engine.target.tp
+    if tp is not None and tp.world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(group=tp.group)
+
+
+def _quiet(msg: str) -> None:
+    pass
 
 
 class _FixedChain:

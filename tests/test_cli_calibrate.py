@@ -101,3 +101,99 @@ def test_chain_calibration_on_cpu(tmp_path):
     assert set(rounds[1]) == {1, 2, 3, 4}
     assert load_accept_profile(str(tmp_path)) is not None
     assert chain_widths(str(tmp_path), 4, 8)[0][0] == 1
+
+
+def test_tp_dry_run_prints_the_worker_launch_and_a_tensor_parallel_serve_command(capsys, tmp_path):
+    out_dir = tmp_path / "cal"
+    assert cli.main(["calibrate", "--model", "tiny", "--output", str(out_dir), "--tp", "2", "--dry-run"]) == 0
+    lines = capsys.readouterr().out.strip().splitlines()
+    launch, serve = lines[-2], lines[-1]
+    assert "torch.distributed.run" in launch and "--nproc-per-node 2" in launch and "--worker" in launch
+    assert "--master-addr 127.0.0.1" in launch and str(out_dir) in launch
+    assert "torch.distributed.run" in serve and "eagle4_b200.serve" in serve
+    assert not out_dir.exists()
+
+
+def _group_alive(pid: int) -> bool:
+    try:
+        with open(f"/proc/{pid}/status") as f:
+            return not any(line.startswith("State:") and "Z" in line.split()[1] for line in f)
+    except FileNotFoundError:
+        return False
+
+
+@pytest.mark.parametrize("case", ["timeout", "failure"])
+def test_supervisor_ends_the_whole_process_group(tmp_path, case):
+    import sys
+    import time
+
+    from eagle4_b200.runtime.supervise import supervise
+
+    pid_file = tmp_path / "grandchild"
+    code = ("import subprocess, sys, time\n"
+            "p = subprocess.Popen([sys.executable, '-c', 'import time; time.sleep(120)'])\n"
+            f"open({str(pid_file)!r}, 'w').write(str(p.pid))\n"
+            + ("time.sleep(120)\n" if case == "timeout" else "time.sleep(0.5)\nraise SystemExit(3)\n"))
+    t0 = time.monotonic()
+    out = supervise([sys.executable, "-c", code], timeout=5.0, grace=2.0)
+    assert time.monotonic() - t0 < 30
+    if case == "timeout":
+        assert out.timed_out and out.code == 124 and not out.ok
+    else:
+        assert out.code == 3 and not out.timed_out and not out.ok
+    grandchild = int(pid_file.read_text())
+    for _ in range(50):
+        if not _group_alive(grandchild):
+            break
+        time.sleep(0.1)
+    assert not _group_alive(grandchild)
+
+
+def test_supervisor_success():
+    import sys
+
+    from eagle4_b200.runtime.supervise import supervise
+
+    assert supervise([sys.executable, "-c", "pass"], timeout=60).ok
+
+
+def _tp_calibrate_worker(rank, world, port, path, out):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.set_num_threads(1)
+    try:
+        from eagle4_b200.api import LLM, TreeSpec
+        from eagle4_b200.parallel.tp import TensorParallel
+        from eagle4_b200.runtime.calibrate import calibrate
+
+        tp = TensorParallel(backend="torch")
+        llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_len=512, tp=tp)
+        seen = []
+        problems = calibrate(llm.engine, path, batch_sizes=[1], context_step=64, context_stop=128, repeats=2,
+                             progress=seen.append)
+        out[rank] = {"problems": problems, "messages": len(seen), "files": os.path.isdir(os.path.join(path, "cost"))}
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tensor_parallel_calibration_rank0_writes_every_rank_checks(tmp_path):
+    import socket
+
+    import torch.multiprocessing as mp
+
+    from eagle4_b200.core.cost_table import load_cost_tables
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        out = mgr.dict()
+        mp.start_processes(_tp_calibrate_worker, args=(2, port, str(tmp_path), out), nprocs=2, start_method="spawn",
+                           join=True)
+        res = dict(out)
+    assert res[0]["problems"] == res[1]["problems"] and set(res[0]["problems"]) == {1}
+    assert res[0]["messages"] > 0 and res[1]["messages"] == 0 and res[1]["files"]
+    assert 1 in load_cost_tables(os.path.join(tmp_path, "cost"))
