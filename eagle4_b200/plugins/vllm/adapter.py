@@ -43,6 +43,12 @@ class HarnessMethodSpec(_MethodSpec):
     def num_lookahead_tokens(self, page_size: int = 1) -> int:
         return req_to_token_span(self.top_k, self.depth, self.width, page_size)
 
+    def linear_attn_verify_extension(self, vllm_config):
+        """GDN / Mamba2 layers under tree verify (``plugins.vllm.tree_verify``); None for chains (vLLM's kernels)."""
+        from eagle4_b200.plugins.vllm.tree_verify import create_extension
+
+        return create_extension(vllm_config)
+
 
 class TreeAccept:
     """The rejection sampler vLLM calls on the verify rows: the fused greedy accept (temperature 0, on target ids or
@@ -138,7 +144,10 @@ class HarnessSpeculator(_Speculator):
         """Accept the verified rows (``target``: ids or logits of the rows) and hand the accepted path to the drafter.
         ``round_us``: the host's measured period of this round (recorded when ``record_rounds`` is on). Returns
         (accepted rows, counts, bonus, emitted tokens per request)."""
+        from eagle4_b200.plugins.vllm.tree_verify import commit_accepted
+
         acc, cnt, bonus = self.make_rejection_sampler()(target, draft_tokens, parent_rows)
+        commit_accepted(acc, cnt)  # the target's GDN / Mamba2 states resume after the accepted path
         emitted = self.drafter.accept(req_ids, draft_tokens, acc, cnt, bonus, aux_hidden_states)
         if self.served_rounds is not None and round_us:
             self.served_rounds.record(len(req_ids), draft_tokens.shape[1], round_us,
@@ -160,6 +169,10 @@ class HarnessSpeculator(_Speculator):
         return base_positions[:, None] + depth.long(), mask
 
     def prepare_verify_inputs(self, parent_rows: torch.Tensor, base_positions: torch.Tensor):
+        """The verify layout; also stages the tree for the target's GDN / Mamba2 layers."""
+        from eagle4_b200.plugins.vllm.tree_verify import stage_tree
+
+        stage_tree(parent_rows)
         return self.verify_layout(parent_rows, base_positions)
 
     def make_rejection_sampler(self, *args, **kwargs):
