@@ -26,7 +26,8 @@ torch::Tensor rmsnorm(const torch::Tensor& x, const torch::Tensor& w, double eps
 torch::Tensor concat_norms(const torch::Tensor& e, const torch::Tensor& h, const torch::Tensor& we,
                            const torch::Tensor& wh, double eps);
 torch::Tensor embedding(const torch::Tensor& ids, const torch::Tensor& table);
-torch::Tensor gated_rmsnorm(const torch::Tensor& o, const torch::Tensor& z, const torch::Tensor& w, double eps);
+torch::Tensor gated_rmsnorm(const torch::Tensor& o, const torch::Tensor& z, const torch::Tensor& w, double eps,
+                            bool gate_first);
 torch::Tensor qkv_prepare(const torch::Tensor& qkv, const torch::Tensor& pos, const torch::Tensor& slot,
                           torch::Tensor kc, torch::Tensor vc, const c10::optional<torch::Tensor>& qn,
                           const c10::optional<torch::Tensor>& kn, bool norm_offset, const torch::Tensor& cos_t,
@@ -41,7 +42,7 @@ torch::Tensor attention(const torch::Tensor& q, const torch::Tensor& kc, const t
                         const torch::Tensor& ctx_len, const torch::Tensor& extra, const torch::Tensor& n_extra,
                         double scale, int64_t max_keys, const c10::optional<torch::Tensor>& gate);
 torch::Tensor conv_tree(const torch::Tensor& x, const torch::Tensor& cs, const torch::Tensor& slot,
-                        const torch::Tensor& parent, const torch::Tensor& w);
+                        const torch::Tensor& parent, const torch::Tensor& w, const torch::Tensor& bias);
 void conv_commit(const torch::Tensor& x, torch::Tensor cs, const torch::Tensor& slots, const torch::Tensor& rows,
                  const torch::Tensor& nrows, int64_t W);
 void conv_commit_scan(torch::Tensor cs, const torch::Tensor& x, const torch::Tensor& slot, int64_t W,

@@ -121,9 +121,11 @@ __global__ void embedding_kernel(const int64_t* __restrict__ ids, const __nv_bfl
 }
 
 // per (row, group): rmsnorm over D then * silu(z)
+// ``wg``: the weight's stride between groups (0: one [D] weight shared by every group; D: a [G, D] weight).
+// ``gate_first`` 0: y = rmsnorm(o) * w * silu(z) (Qwen3.5 GDN); 1: y = rmsnorm(o * silu(z)) * w (Mamba2 / Nemotron-H).
 __global__ void gated_rmsnorm_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ z, int ldz,
-                                     const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y, int T, int G,
-                                     int D, float eps) {
+                                     const __nv_bfloat16* __restrict__ w, int wg, int gate_first,
+                                     __nv_bfloat16* __restrict__ y, int T, int G, int D, float eps) {
   pdl_wait();
   pdl_trigger();
   // one warp per (row, group)
@@ -132,15 +134,18 @@ __global__ void gated_rmsnorm_kernel(const __nv_bfloat16* __restrict__ o, const 
   const int r = warp / G, g = warp % G;
   if (r >= T) return;
   const __nv_bfloat16* orow = o + (size_t(r) * G + g) * D;
+  const __nv_bfloat16* zrow = z + size_t(r) * ldz + size_t(g) * D;
   float ss = 0.f;
   for (int i = lane; i < D; i += 32) {
-    const float v = bf(orow[i]);
+    const float v = gate_first ? bf(orow[i]) * silu(bf(zrow[i])) : bf(orow[i]);
     ss += v * v;
   }
   const float rs = rsqrtf(warp_sum(ss) / D + eps);
   for (int i = lane; i < D; i += 32) {
-    const float n = bf(orow[i]) * rs * bf(w[i]);
-    y[(size_t(r) * G + g) * D + i] = __float2bfloat16(n * silu(bf(z[size_t(r) * ldz + g * D + i])));
+    const float gz = silu(bf(zrow[i]));
+    const float wv = bf(w[size_t(g) * wg + i]);
+    const float n = gate_first ? bf(orow[i]) * gz * rs * wv : bf(orow[i]) * rs * wv * gz;
+    y[(size_t(r) * G + g) * D + i] = __float2bfloat16(n);
   }
 }
 
@@ -314,17 +319,21 @@ torch::Tensor embedding(const torch::Tensor& ids, const torch::Tensor& table) {
   return y;
 }
 
-torch::Tensor gated_rmsnorm(const torch::Tensor& o, const torch::Tensor& z, const torch::Tensor& w, double eps) {
+torch::Tensor gated_rmsnorm(const torch::Tensor& o, const torch::Tensor& z, const torch::Tensor& w, double eps,
+                            bool gate_first) {
   const at::cuda::CUDAGuard g(o.device());
   auto oc = o.contiguous();
   const int T = oc.size(0), G = oc.size(1), D = oc.size(2);
   TORCH_CHECK(z.stride(-1) == 1);
+  TORCH_CHECK(w.is_contiguous() && (w.numel() == D || w.numel() == int64_t(G) * D),
+              "gated_rmsnorm: the weight is one [D] row shared by the groups or one row per group");
+  const int wg = w.numel() == D ? 0 : D;
   auto y = torch::empty({T, G * D}, o.options());
   const int warps = T * G;
   if (T) {
     C10_CUDA_CHECK(launch_pdl(gated_rmsnorm_kernel, (warps * 32 + 255) / 256, 256, 0,
                               at::cuda::getCurrentCUDAStream().stream(), CBF16(oc), CBF16(z), z.stride(0), CBF16(w),
-                              BF16(y), T, G, D, float(eps)));
+                              wg, gate_first ? 1 : 0, BF16(y), T, G, D, float(eps)));
   }
   return y;
 }

@@ -25,12 +25,12 @@ constexpr int kMaxPath = 64;
 __device__ __forceinline__ float bf(__nv_bfloat16 x) { return __bfloat162float(x); }
 
 // ----------------------------------------------------------------------------------------------- causal conv
-// out[r, c] = silu(sum_j w[c, j] * window_j) over the row's last W inputs along its parent chain (oldest first),
-// taking missing ancestors from the committed window.
+// out[r, c] = silu(bias[c] + sum_j w[c, j] * window_j) over the row's last W inputs along its parent chain (oldest
+// first), taking missing ancestors from the committed window; ``bias`` may be null (no bias).
 __global__ void conv_tree_kernel(const __nv_bfloat16* __restrict__ x, int ldx, const __nv_bfloat16* __restrict__ cs,
                                  const int* __restrict__ slot, const int* __restrict__ parent,
-                                 const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int T, int C,
-                                 int W) {
+                                 const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ bias,
+                                 __nv_bfloat16* __restrict__ out, int T, int C, int W) {
   pdl_wait();
   pdl_trigger();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -43,7 +43,7 @@ __global__ void conv_tree_kernel(const __nv_bfloat16* __restrict__ x, int ldx, c
     cur = parent[cur];
   }
   const int s = slot[r];
-  float acc = 0.f;
+  float acc = bias ? bf(bias[c]) : 0.f;
   for (int j = 0; j < W; ++j) {
     // window position j (0 oldest); the newest n entries come from the chain (chain[0] is the row itself)
     const int from_end = W - 1 - j;
@@ -723,15 +723,20 @@ torch::Tensor segments_of(const torch::Tensor& slot) {
 #define BFP(t) reinterpret_cast<__nv_bfloat16*>((t).data_ptr())
 
 torch::Tensor conv_tree(const torch::Tensor& x, const torch::Tensor& cs, const torch::Tensor& slot,
-                        const torch::Tensor& parent, const torch::Tensor& w) {
+                        const torch::Tensor& parent, const torch::Tensor& w, const torch::Tensor& bias) {
   const at::cuda::CUDAGuard g(x.device());
   const int T = x.size(0), C = x.size(1), W = w.size(1);
   TORCH_CHECK(W <= 8 && x.stride(1) == 1);
+  TORCH_CHECK(bias.numel() == 0 || (bias.numel() == C && bias.scalar_type() == torch::kBFloat16),
+              "conv_tree: the bias has one bf16 value per channel");
   auto out = torch::empty({T, C}, x.options());
   if (T) {
     auto sl = slot.to(torch::kInt32).contiguous(), pa = parent.to(torch::kInt32).contiguous();
+    auto wc = w.contiguous();
+    auto bc = bias.contiguous();
+    const __nv_bfloat16* bp = bias.numel() ? CBF(bc) : nullptr;
     C10_CUDA_CHECK(launch_pdl(conv_tree_kernel, dim3((C + 255) / 256, T), 256, 0, at::cuda::getCurrentCUDAStream().stream(), 
-        CBF(x), x.stride(0), CBF(cs), sl.data_ptr<int>(), pa.data_ptr<int>(), CBF(w.contiguous()), BFP(out), T, C, W));
+        CBF(x), x.stride(0), CBF(cs), sl.data_ptr<int>(), pa.data_ptr<int>(), CBF(wc), bp, BFP(out), T, C, W));
   }
   return out;
 }
@@ -780,7 +785,8 @@ static GdnArgs gdn_args(const torch::Tensor& qkv, const torch::Tensor& proj, int
                  int(K), int(V)};
 }
 
-torch::Tensor gated_rmsnorm(const torch::Tensor& o, const torch::Tensor& z, const torch::Tensor& w, double eps);
+torch::Tensor gated_rmsnorm(const torch::Tensor& o, const torch::Tensor& z, const torch::Tensor& w, double eps,
+                            bool gate_first);
 
 // Gated delta rule + gated RMSNorm over a forest of rows; returns [T, HV*V].
 torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int64_t z_off, int64_t b_off,
@@ -811,7 +817,7 @@ torch::Tensor gdn_tree(const torch::Tensor& qkv, const torch::Tensor& proj, int6
     }
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     if (!norm_w.numel()) return out;
-    return gated_rmsnorm(raw.view({T, HV, V}), proj.narrow(1, z_off, HV * V), norm_w, eps);
+    return gated_rmsnorm(raw.view({T, HV, V}), proj.narrow(1, z_off, HV * V), norm_w, eps, false);
   }
   TORCH_CHECK(V <= 128, "gdn tree: at most 128 value columns per head");
   dim3 grid(HV, T);

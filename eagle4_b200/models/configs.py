@@ -45,6 +45,9 @@ class TargetConfig:
     mamba_head_dim: int = 0
     mamba_state: int = 0
     mamba_groups: int = 1
+    # Mamba2 gated norm: rmsnorm(y * silu(z)) * w as Hugging Face's Nemotron-H computes it (True), or
+    # rmsnorm(y) * w * silu(z) (False: the synthetic Nemotron-H-style shapes)
+    mamba_gate_first: bool = False
     tie_embeddings: bool = False
     init_std: float = 0.02
 
@@ -109,11 +112,18 @@ class TargetConfig:
                 conv_kernel=text.get("linear_conv_kernel_dim", 4), tie_embeddings=bool(hf.get("tie_word_embeddings")),
             )
         if mt == "nemotron_h":
-            pat = text["hybrid_override_pattern"]
-            kind = {"M": ("mamba", None), "*": ("attn", None), "-": (None, "relu2")}
+            kind = {"M": ("mamba", None), "*": ("attn", None), "-": (None, "relu2"),
+                    "mamba": ("mamba", None), "attention": ("attn", None), "mlp": (None, "relu2")}
+            blocks = text.get("hybrid_override_pattern") or text.get("layers_block_type") or []
+            unbuilt = sorted({str(b) for b in blocks if b not in kind})
+            if unbuilt:
+                raise NotImplementedError(f"Nemotron-H blocks {unbuilt} are not built (Mamba2, attention and ReLU^2 "
+                                          "MLP blocks are)")
             return cls(
                 family="nemotron_h", hidden_size=text["hidden_size"], vocab_size=text["vocab_size"],
-                layers=[kind[c] for c in pat], intermediate_size=text["intermediate_size"],
+                layers=[kind[c] for c in blocks], intermediate_size=text["intermediate_size"],
+                mamba_gate_first=bool(text.get("mamba_gate_first", True)),
+                tie_embeddings=bool(text.get("tie_word_embeddings")),
                 rms_norm_eps=text.get("layer_norm_epsilon", 1e-5), num_heads=text["num_attention_heads"],
                 num_kv_heads=text["num_key_value_heads"], head_dim=text.get("head_dim") or
                 text["hidden_size"] // text["num_attention_heads"], rotary_dim=0,
@@ -153,7 +163,8 @@ class TargetConfig:
                         layer_norm_epsilon=self.rms_norm_eps,
                         hybrid_override_pattern="".join(sym[tuple(x)] for x in self.layers),
                         mamba_num_heads=self.mamba_heads, mamba_head_dim=self.mamba_head_dim,
-                        ssm_state_size=self.mamba_state, n_groups=self.mamba_groups, conv_kernel=self.conv_kernel)
+                        ssm_state_size=self.mamba_state, n_groups=self.mamba_groups, conv_kernel=self.conv_kernel,
+                        mamba_gate_first=self.mamba_gate_first)
         return dict(common, model_type="llama", architectures=["LlamaForCausalLM"], rms_norm_eps=self.rms_norm_eps,
                     rope_theta=self.rope_theta)
 

@@ -207,7 +207,8 @@ class TargetModel:
         z = proj[:, :inner]
         x_pre = proj[:, inner: inner + cd]
         dt = proj[:, inner + cd: inner + cd + nh]
-        conv = ops.causal_conv_tree(x_pre, cache.conv[ri], rb.state_slot, rb.parent, w[f"l{i}.conv"])
+        conv = ops.causal_conv_tree(x_pre, cache.conv[ri], rb.state_slot, rb.parent, w[f"l{i}.conv"],
+                                    w.get(f"l{i}.conv_bias"))
         y = ops.mamba_tree(conv, dt, w[f"l{i}.A_log"], w[f"l{i}.dt_bias"], w[f"l{i}.D"], cache.ssm[ri],
                            rb.state_slot, rb.parent, cfg, rb.scan, rb.segments)
         if rb.scan:
@@ -218,7 +219,8 @@ class TargetModel:
             rec.conv_out.append(conv)
             rec.gate_a.append(dt)
         group = cfg.mamba_inner // cfg.mamba_groups
-        y = ops.gated_rmsnorm(y.reshape(y.shape[0], cfg.mamba_groups, group), z, w[f"l{i}.gnorm"], cfg.rms_norm_eps)
+        y = ops.gated_rmsnorm(y.reshape(y.shape[0], cfg.mamba_groups, group), z, w[f"l{i}.gnorm"], cfg.rms_norm_eps,
+                              cfg.mamba_gate_first)
         return self._row(y, w[f"l{i}.out_proj"], h, f"l{i}.norm1")
 
     def _mlp(self, i: int, x: torch.Tensor, h: torch.Tensor, kind: str) -> torch.Tensor:

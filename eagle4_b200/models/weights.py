@@ -300,7 +300,9 @@ def load_draft(path: str, cfg: DraftConfig, *, device="cpu", dtype=None, embed=N
 
 
 def target_from_hf(cfg: TargetConfig, sd: Dict[str, torch.Tensor]) -> Dict[str, torch.Tensor]:
-    """Map a Hugging Face Qwen3.5 / Llama state dict into the fused runtime layout."""
+    """Map a Hugging Face Qwen3.5 / Llama / Nemotron-H state dict into the fused runtime layout."""
+    if cfg.family == "nemotron_h":
+        return _nemotron_from_hf(cfg, sd)
     sd = {k.replace("model.language_model.", "model."): v for k, v in sd.items()}
     g = lambda n: sd[n]  # noqa: E731
     w: Dict[str, torch.Tensor] = {"embed": g("model.embed_tokens.weight"), "norm": g("model.norm.weight")}
@@ -332,4 +334,41 @@ def target_from_hf(cfg: TargetConfig, sd: Dict[str, torch.Tensor]) -> Dict[str, 
             w[f"l{i}.norm2"] = g(p + "post_attention_layernorm.weight")
             w[f"l{i}.gate_up"] = interleave_gate_up(g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight"))
             w[f"l{i}.down"] = g(p + "mlp.down_proj.weight")
+    return w
+
+
+def _nemotron_from_hf(cfg: TargetConfig, sd: Dict[str, torch.Tensor]) -> Dict[str, torch.Tensor]:
+    """Nemotron-H: one mixer per block (Mamba2 ``M``, attention ``*``, ReLU^2 MLP ``-``) behind the block's RMSNorm.
+    The Mamba2 in_proj rows are already ``[z | x B C | dt]``; the conv bias and the gated norm's per-channel weight
+    (one row per group) are kept. Checkpoints name the trunk ``backbone.`` (``model.`` after conversion)."""
+    sd = {k.replace("backbone.", "model.").replace("model.embedding.", "model.embeddings."): v for k, v in sd.items()}
+    g = lambda n: sd[n]  # noqa: E731
+    w: Dict[str, torch.Tensor] = {"embed": g("model.embeddings.weight"), "norm": g("model.norm_f.weight")}
+    w["lm_head"] = sd.get("lm_head.weight", w["embed"])
+    for i, (mixer, mlp) in enumerate(cfg.layers):
+        p = f"model.layers.{i}."
+        m = p + "mixer."
+        if mixer is not None:
+            w[f"l{i}.norm1"] = g(p + "norm.weight")
+        if mixer == "mamba":
+            w[f"l{i}.in_proj"] = g(m + "in_proj.weight")
+            w[f"l{i}.conv"] = g(m + "conv1d.weight").squeeze(1)
+            if m + "conv1d.bias" in sd:
+                w[f"l{i}.conv_bias"] = g(m + "conv1d.bias")
+            w[f"l{i}.A_log"] = g(m + "A_log").float()
+            w[f"l{i}.D"] = g(m + "D").float()
+            w[f"l{i}.dt_bias"] = g(m + "dt_bias").float()
+            w[f"l{i}.gnorm"] = g(m + "norm.weight")
+            w[f"l{i}.out_proj"] = g(m + "out_proj.weight")
+        elif mixer == "attn":
+            w[f"l{i}.qkv"] = torch.cat([g(m + "q_proj.weight"), g(m + "k_proj.weight"), g(m + "v_proj.weight")])
+            w[f"l{i}.o_proj"] = g(m + "o_proj.weight")
+        elif mixer is not None:
+            raise ValueError(f"Nemotron-H layer {i}: mixer {mixer!r} is not built")
+        if mlp == "relu2":
+            w[f"l{i}.norm2"] = g(p + "norm.weight")
+            w[f"l{i}.up"] = g(m + "up_proj.weight")
+            w[f"l{i}.down"] = g(m + "down_proj.weight")
+        elif mlp is not None:
+            raise ValueError(f"Nemotron-H layer {i}: MLP {mlp!r} is not built")
     return w

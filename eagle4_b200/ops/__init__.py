@@ -88,9 +88,10 @@ def attention(q, k_cache, v_cache, block_table, page, req, ctx_start, ctx_len, e
 
 
 # recurrent -------------------------------------------------------------------------------------------------------
-def causal_conv_tree(x, conv_state, state_slot, parent, weight):
+def causal_conv_tree(x, conv_state, state_slot, parent, weight, bias=None):
+    """Tree causal conv + SiLU; ``bias`` ``[C]`` (optional) is added before the SiLU."""
     fn = _nat().causal_conv_tree if _cuda(x) else ref.causal_conv_tree
-    return fn(x, conv_state, state_slot, parent, weight)
+    return fn(x, conv_state, state_slot, parent, weight, bias)
 
 
 def gdn_mixer(conv, proj, cfg, a_log, dt_bias, norm_w, state, state_slot, parent, scan: bool, segments=None):
@@ -133,8 +134,11 @@ def conv_commit_scan(conv_state, x_pre, state_slot, kw, segments=None):
     return ref.conv_commit_scan(conv_state, x_pre, state_slot, kw)
 
 
-def gated_rmsnorm(o, z, w, eps):
-    return _nat().gated_rmsnorm(o, z, w, eps) if _cuda(o) else ref.gated_rmsnorm(o, z, w, eps)
+def gated_rmsnorm(o, z, w, eps, gate_first: bool = False):
+    """``rmsnorm(o) * w * silu(z)`` per group of ``o [T, G, D]``, or with ``gate_first`` ``rmsnorm(o * silu(z)) * w``
+    (Mamba2's form); ``w`` is one ``[D]`` row shared by the groups or ``G * D`` values."""
+    fn = _nat().gated_rmsnorm if _cuda(o) else ref.gated_rmsnorm
+    return fn(o, z, w, eps, gate_first)
 
 
 def mamba_tree(xbc, dt_raw, a_log, dt_bias, d_skip, state, state_slot, parent, cfg, scan: bool, segments=None):

@@ -166,8 +166,8 @@ def concat_norms(e, h, we, wh, eps):
     return _C.concat_norms(e, h, we, wh, float(eps))
 
 
-def gated_rmsnorm(o, z, w, eps):
-    return _C.gated_rmsnorm(o, z, w, float(eps))
+def gated_rmsnorm(o, z, w, eps, gate_first: bool = False):
+    return _C.gated_rmsnorm(o, z, w, float(eps), bool(gate_first))
 
 
 # attention --------------------------------------------------------------------------------------------------------
@@ -207,8 +207,8 @@ def attention(q, k_cache, v_cache, block_table, page, req, ctx_start, ctx_len, e
 
 
 # recurrent --------------------------------------------------------------------------------------------------------
-def causal_conv_tree(x, conv_state, state_slot, parent, weight):
-    return _C.conv_tree(x, conv_state, state_slot, parent, weight)
+def causal_conv_tree(x, conv_state, state_slot, parent, weight, bias=None):
+    return _C.conv_tree(x, conv_state, state_slot, parent, weight, _NONE if bias is None else bias)
 
 
 def _gdn_offsets(cfg):

@@ -186,8 +186,8 @@ def _walk(parent: torch.Tensor, r: int, limit: int):
 
 
 def causal_conv_tree(x: torch.Tensor, conv_state: torch.Tensor, state_slot: torch.Tensor, parent: torch.Tensor,
-                     weight: torch.Tensor) -> torch.Tensor:
-    """Width-``K`` causal depthwise conv + SiLU over a forest of rows.
+                     weight: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Width-``K`` causal depthwise conv (plus ``bias [C]`` when given) + SiLU over a forest of rows.
 
     ``x [T, C]`` pre-conv inputs; ``conv_state [slots, C, K-1]`` the committed last inputs (oldest first);
     ``parent [T]`` the parent row of each row (``-1``: the committed state); ``weight [C, K]``.
@@ -203,7 +203,7 @@ def causal_conv_tree(x: torch.Tensor, conv_state: torch.Tensor, state_slot: torc
         if need > 0:
             st = conv_state[int(state_slot[r])].double()  # [C, K-1]
             win = [st[:, kw - 1 - need + i] for i in range(need)] + win
-        acc = torch.zeros(c, dtype=torch.float64)
+        acc = torch.zeros(c, dtype=torch.float64) if bias is None else bias.double().clone()
         for j in range(kw):
             acc = acc + wd[:, j] * win[j]
         out[r] = F.silu(acc).to(x.dtype)
@@ -304,13 +304,17 @@ def conv_commit_scan(conv_state: torch.Tensor, x_pre: torch.Tensor, state_slot: 
         _shift_conv(conv_state, slot, x_pre, rows, kw)
 
 
-def gated_rmsnorm(o: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    """Per-head RMSNorm of ``o [T, H, D]`` times ``silu(z)``; returns ``[T, H*D]``."""
+def gated_rmsnorm(o: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float, gate_first: bool = False
+                  ) -> torch.Tensor:
+    """Per-head RMSNorm of ``o [T, H, D]`` times ``silu(z)`` (``gate_first``: the RMSNorm of ``o * silu(z)``); returns
+    ``[T, H*D]``. ``w``: one ``[D]`` weight shared by the heads, or ``H * D`` values (one row per head)."""
     od = o.double()
+    gz = F.silu(z.double().reshape(od.shape))
+    if gate_first:
+        od = od * gz
     r = torch.rsqrt(od.square().mean(-1, keepdim=True) + eps)
-    n = od * r * w.double()
-    zz = z.double().view_as(od)
-    return (n * F.silu(zz)).reshape(o.shape[0], -1).to(o.dtype)
+    n = od * r * w.double().reshape(-1, o.shape[-1])
+    return (n if gate_first else n * gz).reshape(o.shape[0], -1).to(o.dtype)
 
 
 # ----------------------------------------------------------------------------------------------- Mamba2

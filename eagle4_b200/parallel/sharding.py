@@ -137,6 +137,10 @@ def shard_target(cfg: TargetConfig, w: Dict[str, torch.Tensor], world: int, rank
             out[p + "in_proj"] = _rows(w[p + "in_proj"], [(x0, x0 + hl * hp)] + [
                 (inner + a, inner + b) for a, b in conv_pieces] + [(inner + cd + rank * hl, inner + cd + (rank + 1) * hl)])
             out[p + "conv"] = _rows(w[p + "conv"], conv_pieces)
+            if p + "conv_bias" in w:
+                out[p + "conv_bias"] = torch.cat([w[p + "conv_bias"][a:b] for a, b in conv_pieces]).contiguous()
+            if w[p + "gnorm"].numel() == inner:  # one weight row per group: this rank's groups
+                out[p + "gnorm"] = w[p + "gnorm"][x0:x0 + hl * hp].contiguous()
             for k in ("A_log", "dt_bias", "D"):
                 out[p + k] = w[p + k][rank * hl:(rank + 1) * hl].contiguous()
             out[p + "out_proj"] = _cols(w[p + "out_proj"], x0, x0 + hl * hp)

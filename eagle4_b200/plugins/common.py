@@ -95,9 +95,12 @@ class TreeVerifyRows:
 
 
 def gdn_conv(rows: TreeVerifyRows, mixed_qkv: torch.Tensor, conv_states: torch.Tensor,
-             weight: torch.Tensor) -> torch.Tensor:
-    """Tree causal conv1d: each row's window is its ancestors' inputs, the committed window below the root."""
-    return ops.causal_conv_tree(mixed_qkv, conv_states, rows.slots, rows.parent, weight)
+             weight: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Tree causal conv1d (plus the layer's conv bias, if any): each row's window is its ancestors' inputs, the
+    committed window below the root."""
+    if bias is not None:
+        bias = bias.to(mixed_qkv.dtype).contiguous()
+    return ops.causal_conv_tree(mixed_qkv, conv_states, rows.slots, rows.parent, weight, bias)
 
 
 def gdn_recurrence(rows: TreeVerifyRows, qkv: torch.Tensor, a: torch.Tensor, b: torch.Tensor, a_log: torch.Tensor,

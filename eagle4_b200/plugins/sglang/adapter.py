@@ -130,7 +130,8 @@ class GdnTreeVerify(_Extension):
 
     def conv_update(self, layer, mixed_qkv, conv_states, cache_indices, intermediate_conv_window,
                     intermediate_state_indices):
-        out = gdn_conv(self.rows, mixed_qkv, conv_states, layer.conv1d.weight.squeeze(1))
+        out = gdn_conv(self.rows, mixed_qkv, conv_states, layer.conv1d.weight.squeeze(1),
+                       getattr(layer.conv1d, "bias", None))
         self.records.setdefault(id(layer), {})["x_pre"] = mixed_qkv
         self.records[id(layer)]["conv_states"] = conv_states
         return out
@@ -185,7 +186,8 @@ class Mamba2TreeVerify(_Extension):
 
     def conv_update(self, layer, mixed_qkv, conv_states, cache_indices, intermediate_conv_window,
                     intermediate_state_indices):
-        return gdn_conv(self.rows, mixed_qkv, conv_states, layer.conv1d.weight.squeeze(1))
+        return gdn_conv(self.rows, mixed_qkv, conv_states, layer.conv1d.weight.squeeze(1),
+                        getattr(layer.conv1d, "bias", None))
 
 
 class TreeAttentionVariant:

@@ -135,6 +135,12 @@ def _scatter_window(conv_state, slots, start, window, channels) -> None:
         conv_state[s, cols, :] = vals
 
 
+def _bias(rows, x: torch.Tensor) -> Optional[torch.Tensor]:
+    """The layer's conv bias (Nemotron-H's Mamba2 has one) in the inputs' dtype, or None."""
+    b = getattr(rows, "conv_bias", None)
+    return None if b is None else b.to(x.dtype).contiguous()
+
+
 class TreeVerify(_Extension):
     """The method's ``LinearAttnVerifyExtension``: tree conv + tree recurrence for GDN and Mamba2 spec rows."""
 
@@ -156,11 +162,9 @@ class TreeVerify(_Extension):
         shape = GdnShape(rows.num_k_heads, rows.num_v_heads, rows.head_k_dim, rows.head_v_dim,
                          int(rows.conv_weight.shape[-1]))
         weight = rows.conv_weight.reshape(channels, -1)
-        if getattr(rows, "conv_bias", None) is not None:
-            raise NotImplementedError("the tree conv has no bias: GDN layers with a conv bias are not served")
         state, window = self._committed(rows, channels, shape.conv_kernel)
         req, parent = _rows(rows.query_start_loc, tokens, x.device)
-        conv = ops.causal_conv_tree(x, window, req, parent, weight)
+        conv = ops.causal_conv_tree(x, window, req, parent, weight, _bias(rows, x))
         out = ops.gdn_recurrence(conv, rows.a, rows.b, rows.A_log, rows.dt_bias, state, req, parent, shape)
         rows.out.view(tokens, -1).copy_(out.view(tokens, -1))
         _STAGE.records.append(_Record("gdn", shape, x.clone(), conv, rows.a.clone(), rows.b.clone(), rows.A_log,
@@ -174,12 +178,10 @@ class TreeVerify(_Extension):
         tokens, channels = x.shape
         shape = MambaShape(rows.num_heads, rows.head_dim, rows.ssm_state_size, rows.n_groups,
                            int(rows.conv_weight.shape[-1]))
-        if getattr(rows, "conv_bias", None) is not None:
-            raise NotImplementedError("the tree conv has no bias: Mamba2 layers with a conv bias are not served")
         weight = rows.conv_weight.reshape(channels, -1)
         state, window = self._committed(rows, channels, shape.conv_kernel)
         req, parent = _rows(rows.query_start_loc, tokens, x.device)
-        conv = ops.causal_conv_tree(x, window, req, parent, weight)
+        conv = ops.causal_conv_tree(x, window, req, parent, weight, _bias(rows, x))
         a_log = torch.log(-rows.A.float())  # vLLM passes A = -exp(A_log)
         dt = rows.dt.reshape(tokens, -1)
         y = ops.mamba_tree(conv, dt, a_log, rows.dt_bias.float(), rows.D.float(), state, req, parent, shape, False)

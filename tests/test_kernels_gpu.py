@@ -253,6 +253,28 @@ def test_conv_tree(nat):
     _close(out, want, 2e-2)
 
 
+def test_conv_tree_with_bias(nat):
+    """Nemotron-H's conv has a bias, added before the SiLU."""
+    T, C, S, W = 6, 96, 2, 4
+    x, w, b = _bf(T, C, seed=43), _bf(C, W, seed=44), _bf(C, seed=45)
+    cs = _bf(S, C, W - 1, seed=46)
+    slot = torch.tensor([0, 0, 0, 1, 1, 1], dtype=torch.int32, device="cuda")
+    parent = torch.tensor([-1, 0, 1, -1, 3, 3], dtype=torch.int32, device="cuda")
+    out = nat.causal_conv_tree(x, cs, slot, parent, w, b)
+    want = ref.causal_conv_tree(x.cpu().float(), cs.cpu().float(), slot.cpu(), parent.cpu(), w.cpu().float(),
+                                b.cpu().float())
+    _close(out, want, 2e-2)
+
+
+def test_gated_rmsnorm_gate_first_and_group_weights(nat):
+    """Nemotron-H's gated norm: rmsnorm(o * silu(z)) with one weight row per group (and the shared-row form)."""
+    o, z = _bf(9, 8, 64, seed=47), _bf(9, 512, seed=48)
+    for w in (_bf(512, seed=49), _bf(64, seed=50)):
+        for first in (False, True):
+            _close(nat.gated_rmsnorm(o, z, w, 1e-5, first),
+                   ref.gated_rmsnorm(o.cpu().float(), z.cpu().float(), w.cpu().float(), 1e-5, first), 2e-2)
+
+
 def test_candidate_tail_and_accept(nat):
     h, w = _bf(5, 512, seed=50), _bf(3000, 512, scale=0.1, seed=51)
     idx = torch.randint(0, 3000, (5, 64), device="cuda")

@@ -42,7 +42,7 @@ def _chain_outputs(kind, shape, params, state0, window0, x, gate, steps):
     xs = x[steps]
     parent = torch.arange(len(steps)) - 1
     slot = torch.zeros(len(steps), dtype=torch.int32)
-    conv = ref.causal_conv_tree(xs, window0[None], slot, parent, params["weight"])
+    conv = ref.causal_conv_tree(xs, window0[None], slot, parent, params["weight"], params.get("bias"))
     if kind == "gdn":
         a, b = gate[0][steps], gate[1][steps]
         g, beta = ref.gdn_gates(a, b, params["A_log"], params["dt_bias"])
@@ -55,7 +55,7 @@ def _chain_outputs(kind, shape, params, state0, window0, x, gate, steps):
 
 def _rows(kind, shape, params, pools, x, gate, num_accepted, qsl, state_indices, tokens):
     out = torch.zeros(tokens, shape.gdn_value_dim if kind == "gdn" else shape.mamba_inner)
-    common = dict(conv_state=pools["conv"], conv_weight=params["weight"][:, None, :], conv_bias=None,
+    common = dict(conv_state=pools["conv"], conv_weight=params["weight"][:, None, :], conv_bias=params.get("bias"),
                   activation="silu", state_indices=state_indices, num_accepted_tokens=num_accepted,
                   query_start_loc=qsl, ssm_state=pools["ssm"], out=out, layer_name="l0")
     if kind == "gdn":
@@ -81,7 +81,8 @@ def _setup(kind, dim_first, seed=0):
         shape = tv.MambaShape(4, 8, 16, 2, KW)
         channels = shape.mamba_inner + 2 * 2 * 16
         params = {"A_log": torch.randn(4, generator=g) * 0.5, "dt_bias": torch.randn(4, generator=g) * 0.5,
-                  "D": torch.randn(4, generator=g), "weight": torch.randn(channels, KW, generator=g) * 0.5}
+                  "D": torch.randn(4, generator=g), "weight": torch.randn(channels, KW, generator=g) * 0.5,
+                  "bias": torch.randn(channels, generator=g) * 0.5}  # Nemotron-H's Mamba2 conv has a bias
         pools = {"ssm": _pool(12, 4, 8, 16, gen=g), "conv": _conv_pool(12, channels, dim_first, g)}
         gate_of = lambda n: torch.randn(n, 4, generator=g)  # noqa: E731
     return shape, channels, params, pools, gate_of, g
