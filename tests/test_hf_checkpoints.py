@@ -1,0 +1,81 @@
+"""Hugging Face Qwen3.5 and Llama checkpoints through ``api.from_pretrained`` (CPU, reference ops): the logits of a
+prompt must match Hugging Face's own model on the same weights (GDN layers with their gated norm, gated attention with
+q/k norms and partial rotary, the zero-centred RMSNorm offset, SwiGLU; Llama's full rotary attention)."""
+
+import json
+import os
+
+import pytest
+import torch
+
+pytest.importorskip("transformers")
+
+
+def _perturb(model, scale=0.02):
+    with torch.no_grad():  # move every weight off its identity / constant init so each mapping matters
+        for name, p in model.named_parameters():
+            p.add_(torch.randn_like(p) * (0.05 if "norm" in name or "bias" in name else scale))
+
+
+def _save(path, cfg, model):
+    from safetensors.torch import save_file
+
+    save_file({k: v.contiguous() for k, v in model.state_dict().items()}, os.path.join(path, "model.safetensors"))
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(cfg.to_dict(), f, default=float)
+
+
+def _prefill_logits(llm, ids):
+    from eagle4_b200.models.target import RowBatch
+
+    eng = llm.engine
+    n = ids.shape[0]
+    eng.pages.reserve(0, n + 1)
+    pos = torch.arange(n)
+    rb = RowBatch(ids=ids, pos=pos, req=torch.zeros(n, dtype=torch.int32), write_slot=eng._slots(torch.tensor(0), pos),
+                  ctx_start=torch.zeros(n, dtype=torch.int32), ctx_len=(pos + 1).int(),
+                  extra=torch.zeros(n, 1, dtype=torch.int32), n_extra=torch.zeros(n, dtype=torch.int32),
+                  parent=(pos - 1).int(), state_slot=torch.zeros(n, dtype=torch.int32), scan=True)
+    h, _ = llm.target.forward(rb, eng.tcache)
+    return llm.target.logits(h).double()
+
+
+def _check(tmp_path, cfg, model):
+    from eagle4_b200.api import from_pretrained
+
+    _save(str(tmp_path), cfg, model)
+    llm = from_pretrained(str(tmp_path), device="cpu", dtype=torch.float32, max_len=64)
+    ids = torch.randint(0, cfg.vocab_size, (13,), generator=torch.Generator().manual_seed(1))
+    with torch.no_grad():
+        want = model(ids[None]).logits[0].double()
+    got = _prefill_logits(llm, ids)
+    assert torch.allclose(got, want, atol=1e-4 * want.abs().max().item(), rtol=1e-4), (got - want).abs().max()
+    assert torch.equal(got.argmax(-1), want.argmax(-1))
+    return llm
+
+
+def test_qwen3_5_checkpoint_logits_match_hugging_face(tmp_path):
+    from transformers import Qwen3_5ForCausalLM, Qwen3_5TextConfig
+
+    torch.manual_seed(0)
+    cfg = Qwen3_5TextConfig(vocab_size=512, hidden_size=128, num_hidden_layers=4,
+                            layer_types=["linear_attention"] * 3 + ["full_attention"], num_attention_heads=4,
+                            num_key_value_heads=2, head_dim=32, intermediate_size=256, linear_num_key_heads=2,
+                            linear_num_value_heads=4, linear_key_head_dim=16, linear_value_head_dim=16,
+                            linear_conv_kernel_dim=4)
+    model = Qwen3_5ForCausalLM(cfg).eval()
+    _perturb(model)
+    llm = _check(tmp_path, cfg, model)
+    assert [m for m, _ in llm.target.cfg.layers] == ["gdn", "gdn", "gdn", "attn"]
+    assert llm.target.cfg.rotary_dim == 8  # partial rotary 0.25 of head_dim 32
+
+
+def test_llama_checkpoint_logits_match_hugging_face(tmp_path):
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    torch.manual_seed(1)
+    cfg = LlamaConfig(vocab_size=512, hidden_size=128, num_hidden_layers=3, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=32, intermediate_size=256, rope_theta=500000.0)
+    model = LlamaForCausalLM(cfg).eval()
+    _perturb(model)
+    _check(tmp_path, cfg, model)
