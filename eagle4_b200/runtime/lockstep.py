@@ -68,11 +68,12 @@ def apply(sched: Scheduler, cmd: Command) -> List[Union[Request, ValueError]]:
     return out
 
 
-def follow(engine, lockstep: Lockstep, *, speculative: bool = True) -> int:
-    """A non-leader rank's serving loop: apply each command, step while requests run, return on stop."""
+def follow(engine, lockstep: Lockstep, *, speculative: bool = True, detokenize=None) -> int:
+    """A non-leader rank's serving loop: apply each command, step while requests run, return on stop.
+    ``detokenize`` must be the leader's (stop strings end requests on every rank alike)."""
     if lockstep.leader:
         raise ValueError("rank 0 leads; follow() runs on the other ranks")
-    sched = Scheduler(engine, speculative=speculative)
+    sched = Scheduler(engine, speculative=speculative, detokenize=detokenize)
     rounds = 0
     while True:
         cmd = lockstep.exchange()

@@ -1,15 +1,22 @@
-"""HTTP server over the continuous-batching scheduler: token ids in, generated token ids out.
+"""HTTP server over the continuous-batching scheduler.
 
     python -m eagle4_b200.serve --model qwen3.8-27b [--draft DIR] [--config JSON] [--max-batch 8] [--port 8000]
+    python -m eagle4_b200.serve --model TARGET_DIR --draft DRAFT_DIR [--tokenizer DIR]   # text in, text out
     python -m eagle4_b200.serve --model qwen3.8-27b --no-spec ...        # plain decode (parity reference)
     python -m torch.distributed.run --nproc-per-node 8 --master-addr 127.0.0.1 -m eagle4_b200.serve --model ...
                                                                           # tensor-parallel over 8 GPUs
 
-``POST /v1/generate`` with ``{"prompt_ids": [...], "max_new_tokens": n, "stop_token_ids": [...], "eos_token_id": e,
-"ignore_eos": false}`` returns ``{"output_ids": [...], "finish_reason": "length" | "stop" | "eos", "meta": {...}}``.
+* ``POST /v1/generate`` with ``{"prompt_ids": [...], "max_new_tokens": n, "stop_token_ids": [...], "eos_token_id": e,
+  "ignore_eos": false}`` returns ``{"output_ids": [...], "finish_reason": "length" | "stop" | "eos", "meta": {...}}``.
+* ``POST /v1/completions`` (the OpenAI completions shape): ``{"prompt": text or token ids, "max_tokens": n,
+  "stop": text(s), "stop_token_ids": [...], "ignore_eos": false}``; text needs a tokenizer (``--tokenizer``, or the
+  target directory's own). Stop strings end a request where they appear and are cut from the returned text; the
+  tokenizer's end-of-sequence token ends it unless ``ignore_eos``.
+* ``GET /health``: queue, running batch, acceptance; ``GET /metrics``: the same and the counters, in Prometheus's
+  text format.
+
 Requests join the running batch between rounds and leave it on their own stop condition
-(:class:`~eagle4_b200.runtime.scheduler.Scheduler`); one worker thread owns the engine. ``GET /health`` reports the
-queue, the running batch and the engine's acceptance statistics.
+(:class:`~eagle4_b200.runtime.scheduler.Scheduler`); one worker thread owns the engine.
 """
 
 from __future__ import annotations
@@ -17,8 +24,9 @@ from __future__ import annotations
 import argparse
 import queue
 import threading
+import time
 from concurrent.futures import Future
-from typing import List, Optional
+from typing import Callable, List, Optional, Union
 
 from eagle4_b200.runtime.scheduler import RequestParams, Scheduler
 
@@ -31,8 +39,17 @@ try:
         stop_token_ids: List[int] = []
         eos_token_id: Optional[int] = None
         ignore_eos: bool = False
+
+    class CompletionRequest(BaseModel):
+        prompt: Union[str, List[int]]
+        max_tokens: int = 16
+        stop: Union[str, List[str], None] = None
+        stop_token_ids: List[int] = []
+        ignore_eos: bool = False
+        temperature: Optional[float] = None
+        model: Optional[str] = None
 except ImportError:  # the HTTP layer is optional; Batcher works without it
-    GenerateRequest = None
+    GenerateRequest = CompletionRequest = None
 
 
 class Batcher:
@@ -40,10 +57,14 @@ class Batcher:
     when its request finishes. With ``lockstep`` (tensor-parallel serving, rank 0) every step's submissions are
     first broadcast to the other ranks, which mirror them (:func:`eagle4_b200.runtime.lockstep.follow`)."""
 
-    def __init__(self, engine, max_batch: Optional[int] = None, *, speculative: bool = True, lockstep=None):
+    def __init__(self, engine, max_batch: Optional[int] = None, *, speculative: bool = True, lockstep=None,
+                 detokenize: Optional[Callable[[List[int]], str]] = None):
+        """``detokenize``: token ids -> text, for requests with stop strings (every rank needs the same one)."""
         self.engine = engine
-        self.sched = Scheduler(engine, speculative=speculative)
+        self.detokenize = detokenize
+        self.sched = Scheduler(engine, speculative=speculative, detokenize=detokenize)
         self.lockstep = lockstep
+        self.counts = {"requests": 0, "finished": 0, "refused": 0, "prompt_tokens": 0, "generated_tokens": 0}
         self.q: "queue.Queue" = queue.Queue()
         self.stop = threading.Event()
         self.futures = {}
@@ -77,8 +98,11 @@ class Batcher:
 
         for (_, _, fut), got in zip(subs, apply(self.sched, Command([(p, params) for p, params, _ in subs]))):
             if isinstance(got, Exception):
+                self.counts["refused"] += 1
                 fut.set_exception(got)
             else:
+                self.counts["requests"] += 1
+                self.counts["prompt_tokens"] += int(got.prompt.numel())
                 self.futures[got.rid] = fut
 
     def _fail(self, e: BaseException) -> None:
@@ -118,18 +142,69 @@ class Batcher:
                     except Exception:  # noqa: BLE001 - the group may be gone already
                         pass
                     return
-                self.sched = Scheduler(self.engine, speculative=self.sched.speculative)
+                self.sched = Scheduler(self.engine, speculative=self.sched.speculative, detokenize=self.detokenize)
                 continue
             for req in finished:
+                self.counts["finished"] += 1
+                self.counts["generated_tokens"] += len(req.output)
                 fut = self.futures.pop(req.rid, None)
                 if fut is not None:
                     fut.set_result(req)
 
 
-def make_app(batcher: Batcher):
+def _cut_at_stop(text: str, stops: List[str]) -> str:
+    """The text before the first stop string (OpenAI's convention: the stop string is not returned)."""
+    cut = min((i for i in (text.find(s) for s in stops) if i >= 0), default=-1)
+    return text if cut < 0 else text[:cut]
+
+
+def metrics_text(batcher: Batcher) -> str:
+    """The server's counters and gauges in Prometheus's text format (read at scrape time)."""
+    from prometheus_client import CollectorRegistry, generate_latest
+    from prometheus_client.core import CounterMetricFamily, GaugeMetricFamily
+
+    st, c = batcher.engine.stats, batcher.counts
+
+    class _Collector:
+        def collect(self):
+            for name, doc, value in (("requests", "requests admitted", c["requests"]),
+                                     ("requests_finished", "requests finished", c["finished"]),
+                                     ("requests_refused", "requests refused at submission", c["refused"]),
+                                     ("prompt_tokens", "prompt tokens admitted", c["prompt_tokens"]),
+                                     ("generated_tokens", "tokens generated by finished requests",
+                                      c["generated_tokens"]),
+                                     ("rounds", "engine rounds (speculative or native)", st.rounds),
+                                     ("emitted_tokens", "tokens emitted by speculative rounds", st.emitted)):
+                yield CounterMetricFamily(f"eagle4_{name}", doc, value=value)
+            acc = CounterMetricFamily("eagle4_accepted_per_request_round", "request-rounds by tokens emitted",
+                                      labels=["tokens"])
+            for k in sorted(st.accepted_hist):
+                acc.add_metric([str(k)], st.accepted_hist[k])
+            yield acc
+            for name, doc, value in (("queued", "requests waiting", batcher.q.qsize() + len(batcher.sched.waiting)),
+                                     ("running", "requests in the running batch", len(batcher.sched.running)),
+                                     ("mean_accept", "mean tokens per request-round", st.mean_accept),
+                                     ("failed", "1 after an engine error stopped serving",
+                                      0 if batcher.failed is None else 1)):
+                yield GaugeMetricFamily(f"eagle4_{name}", doc, value=value)
+
+    reg = CollectorRegistry()
+    reg.register(_Collector())
+    return generate_latest(reg).decode()
+
+
+def make_app(batcher: Batcher, tokenizer=None, model_name: str = "eagle4_b200"):
+    """``tokenizer``: a Hugging Face tokenizer for text prompts and text output (optional)."""
     from fastapi import FastAPI, HTTPException
+    from fastapi.responses import PlainTextResponse
 
     app = FastAPI(title="eagle4_b200")
+
+    def run(prompt_ids, params):
+        try:
+            return batcher.submit(prompt_ids, params).result()
+        except ValueError as e:
+            raise HTTPException(400, str(e)) from e
 
     @app.post("/v1/generate")
     def generate(req: GenerateRequest):
@@ -137,12 +212,41 @@ def make_app(batcher: Batcher):
             raise HTTPException(400, "prompt_ids must be non-empty and max_new_tokens positive")
         params = RequestParams(max_new_tokens=req.max_new_tokens, stop_token_ids=tuple(req.stop_token_ids),
                                eos_token_id=req.eos_token_id, ignore_eos=req.ignore_eos)
-        try:
-            r = batcher.submit(req.prompt_ids, params).result()
-        except ValueError as e:
-            raise HTTPException(400, str(e)) from e
+        r = run(req.prompt_ids, params)
         return {"output_ids": r.output, "finish_reason": r.finish_reason,
                 "meta": {"rounds": r.rounds, "speculative": batcher.sched.speculative}}
+
+    @app.post("/v1/completions")
+    def completions(req: CompletionRequest):
+        if isinstance(req.prompt, str):
+            if tokenizer is None:
+                raise HTTPException(400, "text prompts need a tokenizer (start the server with --tokenizer)")
+            ids = list(tokenizer(req.prompt)["input_ids"])
+        else:
+            ids = list(req.prompt)
+        if not ids or req.max_tokens < 1:
+            raise HTTPException(400, "the prompt must be non-empty and max_tokens positive")
+        temp = float(batcher.engine.temperature)
+        if req.temperature is not None and abs(req.temperature - temp) > 1e-6:
+            raise HTTPException(400, f"this server samples every request at temperature {temp:g}")
+        stops = [req.stop] if isinstance(req.stop, str) else list(req.stop or [])
+        if stops and tokenizer is None:
+            raise HTTPException(400, "stop strings need a tokenizer (start the server with --tokenizer)")
+        eos = getattr(tokenizer, "eos_token_id", None) if tokenizer is not None else None
+        params = RequestParams(max_new_tokens=req.max_tokens, stop_token_ids=tuple(req.stop_token_ids),
+                               eos_token_id=eos, ignore_eos=req.ignore_eos, stop=tuple(stops))
+        r = run(ids, params)
+        text = None
+        if tokenizer is not None:
+            text = tokenizer.decode(r.output)
+            if stops and r.finish_reason == "stop":
+                text = _cut_at_stop(text, stops)
+        return {"id": f"cmpl-{r.rid}", "object": "text_completion", "created": int(time.time()),
+                "model": req.model or model_name,
+                "choices": [{"index": 0, "text": text, "token_ids": r.output,
+                             "finish_reason": "length" if r.finish_reason == "length" else "stop"}],
+                "usage": {"prompt_tokens": len(ids), "completion_tokens": len(r.output),
+                          "total_tokens": len(ids) + len(r.output)}}
 
     @app.get("/health")
     def health():
@@ -152,7 +256,20 @@ def make_app(batcher: Batcher):
                 "rounds": st.rounds, "mean_accept": st.mean_accept, "tensor_parallel": tp.world if tp else 1,
                 "failed": None if batcher.failed is None else str(batcher.failed)}
 
+    @app.get("/metrics", response_class=PlainTextResponse)
+    def metrics():
+        return metrics_text(batcher)
+
     return app
+
+
+def load_tokenizer(path: Optional[str]):
+    """A Hugging Face tokenizer from a local directory (no network), or None."""
+    if not path:
+        return None
+    from transformers import AutoTokenizer
+
+    return AutoTokenizer.from_pretrained(path, local_files_only=True)
 
 
 def main(argv: Optional[List[str]] = None) -> int:
@@ -171,6 +288,8 @@ def main(argv: Optional[List[str]] = None) -> int:
     ap.add_argument("--port", type=int, default=8000)
     ap.add_argument("--tp-backend", default="fused", choices=["fused", "torch"],
                     help="tensor-parallel collectives: fused peer-memory kernels, or NCCL through torch")
+    ap.add_argument("--tokenizer", help="tokenizer directory for text prompts (default: the target directory, "
+                                        "when it has one)")
     args = ap.parse_args(argv)
 
     from eagle4_b200.api import TreeSpec
@@ -193,17 +312,23 @@ def main(argv: Optional[List[str]] = None) -> int:
     llm = build_llm(args.model, args.draft, max_batch=args.max_batch, max_len=args.max_len, tree=TreeSpec(),
                     config=args.config, tp=tp)
     speculative = not args.no_spec
+    tok_dir = args.tokenizer
+    if tok_dir is None and os.path.isfile(os.path.join(args.model, "tokenizer_config.json")):
+        tok_dir = args.model
+    tokenizer = load_tokenizer(tok_dir)
+    detokenize = (lambda ids: tokenizer.decode(ids)) if tokenizer is not None else None
     try:
         if lockstep is not None and not lockstep.leader:
             from eagle4_b200.runtime.lockstep import follow
 
-            follow(llm.engine, lockstep, speculative=speculative)
+            follow(llm.engine, lockstep, speculative=speculative, detokenize=detokenize)
             return 0
         import uvicorn
 
-        batcher = Batcher(llm.engine, speculative=speculative, lockstep=lockstep)
+        batcher = Batcher(llm.engine, speculative=speculative, lockstep=lockstep, detokenize=detokenize)
         try:
-            uvicorn.run(make_app(batcher), host=args.host, port=args.port)
+            uvicorn.run(make_app(batcher, tokenizer, os.path.basename(os.path.normpath(args.model))),
+                        host=args.host, port=args.port)
         finally:
             batcher.close()
         return 0 if batcher.failed is None else 1

@@ -197,3 +197,66 @@ def test_tensor_parallel_calibration_rank0_writes_every_rank_checks(tmp_path):
     assert res[0]["problems"] == res[1]["problems"] and set(res[0]["problems"]) == {1}
     assert res[0]["messages"] > 0 and res[1]["messages"] == 0 and res[1]["files"]
     assert 1 in load_cost_tables(os.path.join(tmp_path, "cost"))
+
+
+def _word_tokenizer(vocab: int):
+    """A tokenizer whose every id is one whitespace-separated word ``<i>`` (no word is part of another)."""
+    from tokenizers import Tokenizer, decoders, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+
+    tok = Tokenizer(models.WordLevel({f"<{i}>": i for i in range(vocab)}, unk_token="<0>"))
+    tok.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
+    tok.decoder = decoders.WordPiece(prefix="##", cleanup=False)
+    return PreTrainedTokenizerFast(tokenizer_object=tok, unk_token="<0>", eos_token="<1>")
+
+
+def test_completions_text_stop_strings_and_metrics():
+    from fastapi.testclient import TestClient
+
+    from eagle4_b200.api import LLM, TreeSpec
+    from eagle4_b200.serve import Batcher, make_app
+
+    llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_batch=2, max_len=256)
+    tok = _word_tokenizer(4096)
+    prompt_ids = list(range(5, 25))
+    plain = llm.generate([torch.tensor(prompt_ids)], 8, speculative=False)[0].tolist()
+    b = Batcher(llm.engine, detokenize=lambda ids: tok.decode(ids))
+    try:
+        client = TestClient(make_app(b, tok, "tiny"))
+        text = " ".join(f"<{i}>" for i in prompt_ids)
+        r = client.post("/v1/completions", json={"prompt": text, "max_tokens": 8, "ignore_eos": True}).json()
+        assert r["choices"][0]["token_ids"] == plain and r["choices"][0]["finish_reason"] == "length"
+        assert r["choices"][0]["text"] == tok.decode(plain) and r["usage"]["prompt_tokens"] == 20
+        stop = f"<{plain[3]}>"
+        first = plain.index(plain[3])
+        s = client.post("/v1/completions", json={"prompt": prompt_ids, "max_tokens": 8, "stop": stop,
+                                                  "ignore_eos": True}).json()
+        assert s["choices"][0]["finish_reason"] == "stop"
+        assert s["choices"][0]["token_ids"] == plain[:first + 1]
+        full = tok.decode(plain[:first + 1])
+        assert s["choices"][0]["text"] == full[:full.index(stop)]  # the stop string is cut from the text
+        bad = client.post("/v1/completions", json={"prompt": prompt_ids, "max_tokens": 4, "temperature": 0.7})
+        assert bad.status_code == 400
+        m = client.get("/metrics").text
+        assert "eagle4_requests_total 2.0" in m and "eagle4_generated_tokens_total" in m
+        assert 'eagle4_accepted_per_request_round_total{tokens="' in m
+    finally:
+        b.close(timeout=60)
+
+
+def test_completions_need_a_tokenizer_for_text():
+    from fastapi.testclient import TestClient
+
+    from eagle4_b200.api import LLM, TreeSpec
+    from eagle4_b200.serve import Batcher, make_app
+
+    llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_batch=1, max_len=256)
+    b = Batcher(llm.engine)
+    try:
+        client = TestClient(make_app(b))
+        assert client.post("/v1/completions", json={"prompt": "hello", "max_tokens": 2}).status_code == 400
+        assert client.post("/v1/completions", json={"prompt": [3, 4], "max_tokens": 2, "stop": "x"}).status_code == 400
+        ok = client.post("/v1/completions", json={"prompt": [3, 4, 5], "max_tokens": 2}).json()
+        assert ok["choices"][0]["text"] is None and len(ok["choices"][0]["token_ids"]) == 2
+    finally:
+        b.close(timeout=60)
