@@ -123,3 +123,36 @@ def test_stop_check_main_in_process(tmp_path):
                           "--vocab", "4096", "--concurrency", "4", "--max-new-tokens", "12", "--out", str(out)])
     rep = json.loads(out.read_text())
     assert rc == 0 and rep["violations"] == 0 and rep["requests"] == 8
+
+
+def test_sampling_check_passes_speculation_and_rejects_a_wrong_sampler(capsys):
+    """Speculative and plain sampling draw from one distribution (tiny model, temperature 0.05, draws of one call
+    sharing speculative rounds); a sampler at another temperature is rejected."""
+    from eagle4_b200.tools import sampling_check as sc
+
+    prompts = sc.synthetic_prompts(1, 12, 4096, seed=0)
+    kw = dict(samples=256, tokens=3, batch=64)
+    meta = {"tokens": 3}
+    plain = {"meta": meta, "prompts": [{"prompt_ids": prompts[0], "samples": s} for s in
+                                       sc.sample_in_process("tiny", prompts, temperature=0.05, speculative=False,
+                                                            seed=1, **kw)]}
+    spec = {"meta": meta, "prompts": [{"prompt_ids": prompts[0], "samples": s} for s in
+                                      sc.sample_in_process("tiny", prompts, temperature=0.05, speculative=True,
+                                                           seed=2, **kw)]}
+    colder = {"meta": meta, "prompts": [{"prompt_ids": prompts[0], "samples": s} for s in
+                                        sc.sample_in_process("tiny", prompts, temperature=0.02, speculative=False,
+                                                             seed=3, **kw)]}
+    assert sc.compare(plain, spec, log=lambda s: None)
+    assert not sc.compare(plain, colder, log=lambda s: None)
+
+
+def test_homogeneity_pools_rare_cells():
+    from collections import Counter
+
+    from eagle4_b200.tools.sampling_check import homogeneity
+
+    a = Counter({1: 50, 2: 50, 3: 2, 4: 1})
+    b = Counter({1: 48, 2: 52, 5: 3})
+    stat, dof, p, tvd = homogeneity(a, b)
+    assert dof == 2 and p > 0.5 and 0 < tvd < 0.1  # cells 1, 2 and the pooled rest
+    assert homogeneity(Counter({1: 5}), Counter({1: 5})) is None
