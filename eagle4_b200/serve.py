@@ -311,6 +311,10 @@ def main(argv: Optional[List[str]] = None) -> int:
         lockstep = Lockstep()
     llm = build_llm(args.model, args.draft, max_batch=args.max_batch, max_len=args.max_len, tree=TreeSpec(),
                     config=args.config, tp=tp)
+    if tp is not None:  # a dead or stalled rank is named by the heartbeat before the next round's collectives
+        from eagle4_b200.parallel.health import process_group_heartbeat
+
+        llm.engine.heartbeat = process_group_heartbeat()
     speculative = not args.no_spec
     tok_dir = args.tokenizer
     if tok_dir is None and os.path.isfile(os.path.join(args.model, "tokenizer_config.json")):
