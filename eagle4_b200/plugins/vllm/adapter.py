@@ -35,10 +35,15 @@ class HarnessMethodSpec(_MethodSpec):
     method: Optional[MethodConfig] = None
 
     def configure(self, speculative_config):
-        self.method = parse_method_config(getattr(speculative_config, "method_config", None))
+        """Fill vLLM's speculative config (draft-token schedule per batch size, ``num_speculative_tokens``, the
+        draft's aux layers: ``plugins.vllm.schedule``) and keep the parsed method."""
+        from eagle4_b200.plugins.vllm.schedule import configure_speculative_config
+
+        self.method = configure_speculative_config(speculative_config)
         self.config = self.method.harness
         self.top_k, self.depth, self.width = self.method.node_top_k, self.method.tree_depth, self.method.max_verify_width
-        return {"num_speculative_tokens": self.method.num_speculative_tokens, "max_verify_width": self.width}
+        return {"num_speculative_tokens": getattr(speculative_config, "num_speculative_tokens", None)
+                or self.method.num_speculative_tokens, "max_verify_width": self.width}
 
     def num_lookahead_tokens(self, page_size: int = 1) -> int:
         return req_to_token_span(self.top_k, self.depth, self.width, page_size)

@@ -29,6 +29,7 @@ class MethodConfig:
     tree_depth: int
     depth_stop_gain: Union[float, str, None] = DERIVED
     record_rounds: bool = False  # served rounds' periods go to <data_path>/rounds/tree.json
+    explicit_width: bool = False  # max_verify_width was set (an unpriced chain may then run at that fixed width)
 
     @property
     def num_speculative_tokens(self) -> int:
@@ -71,4 +72,4 @@ def parse_method_config(method_config: Optional[Mapping[str, Any]]) -> MethodCon
         raise ValueError(f"method_config.record_rounds must be true or false, got {record!r}.")
     if record and not harness.data_path:
         raise ValueError("method_config.record_rounds writes rounds/tree.json under data_path: set data_path.")
-    return MethodConfig(harness, width, top_k, depth, gain, record)
+    return MethodConfig(harness, width, top_k, depth, gain, record, "max_verify_width" in tree)

@@ -1,7 +1,8 @@
 """``LlamaForCausalLMEagle4`` for vLLM: the EAGLE-4 draft head as the ``eagle_harness`` method's draft model.
 
 vLLM hands a draft model its config with two keys of its own (``eagle_aux_hidden_state_layer_ids``, the target layers
-whose outputs feed ``fc``, and ``target_layer_count``); ``check_supported`` drops those and applies this package's
+whose inputs vLLM captures for ``fc``: the checkpoint's output-layer ids plus one, set by the method's configure step,
+and ``target_layer_count``); ``check_supported`` drops those and applies this package's
 draft validation (unknown structural keys, window rules, the single-layer structures; latent ReLU^2 MoE and
 ``attn_norm`` are built, the sparse SwiGLU MoE is not). The model's layer runs on this package's kernels:
 
