@@ -12,6 +12,11 @@
   "stop": text(s), "stop_token_ids": [...], "ignore_eos": false}``; text needs a tokenizer (``--tokenizer``, or the
   target directory's own). Stop strings end a request where they appear and are cut from the returned text; the
   tokenizer's end-of-sequence token ends it unless ``ignore_eos``.
+* ``POST /v1/chat/completions``: ``{"messages": [...], ...}`` through the tokenizer's chat template; the answer is
+  ``choices[0].message``.
+* ``"stream": true`` on either returns server-sent events: one chunk per round with the new tokens and the text they
+  add (text that could still become a stop string, or ends in an incomplete character, is held back to the next
+  chunk), a last chunk with the finish reason and usage, then ``[DONE]``.
 * ``GET /health``: queue, running batch, acceptance; ``GET /metrics``: the same and the counters, in Prometheus's
   text format.
 
@@ -48,8 +53,19 @@ try:
         ignore_eos: bool = False
         temperature: Optional[float] = None
         model: Optional[str] = None
+        stream: bool = False
+
+    class ChatRequest(BaseModel):
+        messages: List[dict]
+        max_tokens: int = 256
+        stop: Union[str, List[str], None] = None
+        stop_token_ids: List[int] = []
+        ignore_eos: bool = False
+        temperature: Optional[float] = None
+        model: Optional[str] = None
+        stream: bool = False
 except ImportError:  # the HTTP layer is optional; Batcher works without it
-    GenerateRequest = CompletionRequest = None
+    GenerateRequest = CompletionRequest = ChatRequest = None
 
 
 class Batcher:
@@ -68,16 +84,22 @@ class Batcher:
         self.q: "queue.Queue" = queue.Queue()
         self.stop = threading.Event()
         self.futures = {}
+        self.streams = {}  # rid -> [request, queue, tokens already sent]
         self.failed: Optional[BaseException] = None
         self.thread = threading.Thread(target=self._loop, daemon=True)
         self.thread.start()
 
-    def submit(self, prompt: List[int], params: RequestParams = RequestParams()) -> Future:
+    def submit(self, prompt: List[int], params: RequestParams = RequestParams(),
+               stream: Optional["queue.Queue"] = None) -> Future:
+        """Queue a request; the future resolves with the finished request. ``stream``: a queue that receives each
+        round's new tokens (a list) as they are emitted, then ``None`` when the request ends."""
         fut: Future = Future()
         if self.failed is not None:
             fut.set_exception(RuntimeError(f"serving stopped after an engine error: {self.failed}"))
+            if stream is not None:
+                stream.put(None)
             return fut
-        self.q.put((prompt, params, fut))
+        self.q.put((prompt, params, fut, stream))
         return fut
 
     def close(self, timeout: Optional[float] = None) -> None:
@@ -96,19 +118,38 @@ class Batcher:
     def _admit(self, subs: list) -> None:
         from eagle4_b200.runtime.lockstep import Command, apply
 
-        for (_, _, fut), got in zip(subs, apply(self.sched, Command([(p, params) for p, params, _ in subs]))):
+        cmd = Command([(p, params) for p, params, _, _ in subs])
+        for (_, _, fut, stream), got in zip(subs, apply(self.sched, cmd)):
             if isinstance(got, Exception):
                 self.counts["refused"] += 1
                 fut.set_exception(got)
+                if stream is not None:
+                    stream.put(None)
             else:
                 self.counts["requests"] += 1
                 self.counts["prompt_tokens"] += int(got.prompt.numel())
                 self.futures[got.rid] = fut
+                if stream is not None:
+                    self.streams[got.rid] = [got, stream, 0]
+
+    def _publish(self) -> None:
+        """Each streamed request's new tokens; ``None`` after its last."""
+        for rid, entry in list(self.streams.items()):
+            req, stream, sent = entry
+            if len(req.output) > sent:
+                stream.put(list(req.output[sent:]))
+                entry[2] = len(req.output)
+            if req.finished:
+                stream.put(None)
+                del self.streams[rid]
 
     def _fail(self, e: BaseException) -> None:
         for fut in self.futures.values():
             fut.set_exception(e)
         self.futures.clear()
+        for _, stream, _ in self.streams.values():
+            stream.put(None)
+        self.streams.clear()
 
     def _loop(self) -> None:
         import time
@@ -122,7 +163,7 @@ class Batcher:
             if self.lockstep is not None:
                 now = time.monotonic()
                 if stopping or subs or not self.sched.idle or now - last >= self.lockstep.beat_s:
-                    self.lockstep.exchange(Command([(list(map(int, p)), params) for p, params, _ in subs],
+                    self.lockstep.exchange(Command([(list(map(int, p)), params) for p, params, _, _ in subs],
                                                    stop=stopping))
                     last = now
             if stopping:
@@ -144,6 +185,7 @@ class Batcher:
                     return
                 self.sched = Scheduler(self.engine, speculative=self.sched.speculative, detokenize=self.detokenize)
                 continue
+            self._publish()
             for req in finished:
                 self.counts["finished"] += 1
                 self.counts["generated_tokens"] += len(req.output)
@@ -196,7 +238,7 @@ def metrics_text(batcher: Batcher) -> str:
 def make_app(batcher: Batcher, tokenizer=None, model_name: str = "eagle4_b200"):
     """``tokenizer``: a Hugging Face tokenizer for text prompts and text output (optional)."""
     from fastapi import FastAPI, HTTPException
-    from fastapi.responses import PlainTextResponse
+    from fastapi.responses import PlainTextResponse, StreamingResponse
 
     app = FastAPI(title="eagle4_b200")
 
@@ -216,14 +258,7 @@ def make_app(batcher: Batcher, tokenizer=None, model_name: str = "eagle4_b200"):
         return {"output_ids": r.output, "finish_reason": r.finish_reason,
                 "meta": {"rounds": r.rounds, "speculative": batcher.sched.speculative}}
 
-    @app.post("/v1/completions")
-    def completions(req: CompletionRequest):
-        if isinstance(req.prompt, str):
-            if tokenizer is None:
-                raise HTTPException(400, "text prompts need a tokenizer (start the server with --tokenizer)")
-            ids = list(tokenizer(req.prompt)["input_ids"])
-        else:
-            ids = list(req.prompt)
+    def params_of(req, ids) -> RequestParams:
         if not ids or req.max_tokens < 1:
             raise HTTPException(400, "the prompt must be non-empty and max_tokens positive")
         temp = float(batcher.engine.temperature)
@@ -233,20 +268,98 @@ def make_app(batcher: Batcher, tokenizer=None, model_name: str = "eagle4_b200"):
         if stops and tokenizer is None:
             raise HTTPException(400, "stop strings need a tokenizer (start the server with --tokenizer)")
         eos = getattr(tokenizer, "eos_token_id", None) if tokenizer is not None else None
-        params = RequestParams(max_new_tokens=req.max_tokens, stop_token_ids=tuple(req.stop_token_ids),
-                               eos_token_id=eos, ignore_eos=req.ignore_eos, stop=tuple(stops))
+        return RequestParams(max_new_tokens=req.max_tokens, stop_token_ids=tuple(req.stop_token_ids),
+                             eos_token_id=eos, ignore_eos=req.ignore_eos, stop=tuple(stops))
+
+    def text_of(tokens, params, final: bool) -> Optional[str]:
+        """The text to show for ``tokens``: cut at a stop string; while streaming, the tail that could still turn
+        into a stop string, or that ends in an incomplete character, is held back."""
+        if tokenizer is None:
+            return None
+        text = tokenizer.decode(tokens)
+        stops = list(params.stop)
+        if stops:
+            cut = _cut_at_stop(text, stops)
+            if len(cut) < len(text):
+                return cut
+            if not final:
+                text = text[:max(0, len(text) - (max(map(len, stops)) - 1))]
+        return text if final else text.rstrip("\ufffd")
+
+    def finish_of(r) -> str:
+        return "length" if r.finish_reason == "length" else "stop"
+
+    def usage(n_prompt: int, n_out: int) -> dict:
+        return {"prompt_tokens": n_prompt, "completion_tokens": n_out, "total_tokens": n_prompt + n_out}
+
+    def sse(ids, params, chunk):
+        """Server-sent events of a streamed request: ``chunk(text delta, new tokens, finish reason)`` per round."""
+        import json
+        import queue as q_
+
+        stream: "q_.Queue" = q_.Queue()
+        fut = batcher.submit(ids, params, stream=stream)
+
+        def events():
+            tokens, shown = [], ""
+            while True:
+                new = stream.get()
+                if new is None:
+                    break
+                tokens += new
+                text = text_of(tokens, params, final=False)
+                delta = None
+                if text is not None:
+                    delta, shown = (text[len(shown):], text) if text.startswith(shown) else ("", shown)
+                yield f"data: {json.dumps(chunk(delta, new, None))}\n\n"
+            try:
+                r = fut.result()
+            except Exception as e:  # noqa: BLE001 - the request failed: report it in the stream
+                yield f"data: {json.dumps({'error': str(e)})}\n\n"
+                return
+            text = text_of(r.output, params, final=True)
+            delta = None if text is None else text[len(shown):] if text.startswith(shown) else ""
+            last = chunk(delta, [], finish_of(r))
+            last["usage"] = usage(len(ids), len(r.output))
+            yield f"data: {json.dumps(last)}\n\n"
+            yield "data: [DONE]\n\n"
+
+        return StreamingResponse(events(), media_type="text/event-stream")
+
+    @app.post("/v1/completions")
+    def completions(req: CompletionRequest):
+        if isinstance(req.prompt, str):
+            if tokenizer is None:
+                raise HTTPException(400, "text prompts need a tokenizer (start the server with --tokenizer)")
+            ids = list(tokenizer(req.prompt)["input_ids"])
+        else:
+            ids = list(req.prompt)
+        params = params_of(req, ids)
+        head = {"object": "text_completion", "created": int(time.time()), "model": req.model or model_name}
+        if req.stream:
+            return sse(ids, params, lambda delta, new, fin: dict(head, id="cmpl-stream", choices=[
+                {"index": 0, "text": delta, "token_ids": new, "finish_reason": fin}]))
         r = run(ids, params)
-        text = None
-        if tokenizer is not None:
-            text = tokenizer.decode(r.output)
-            if stops and r.finish_reason == "stop":
-                text = _cut_at_stop(text, stops)
-        return {"id": f"cmpl-{r.rid}", "object": "text_completion", "created": int(time.time()),
-                "model": req.model or model_name,
-                "choices": [{"index": 0, "text": text, "token_ids": r.output,
-                             "finish_reason": "length" if r.finish_reason == "length" else "stop"}],
-                "usage": {"prompt_tokens": len(ids), "completion_tokens": len(r.output),
-                          "total_tokens": len(ids) + len(r.output)}}
+        return dict(head, id=f"cmpl-{r.rid}", choices=[{"index": 0, "text": text_of(r.output, params, True),
+                                                         "token_ids": r.output, "finish_reason": finish_of(r)}],
+                    usage=usage(len(ids), len(r.output)))
+
+    @app.post("/v1/chat/completions")
+    def chat(req: ChatRequest):
+        if tokenizer is None or not getattr(tokenizer, "chat_template", None):
+            raise HTTPException(400, "chat needs a tokenizer with a chat template (start the server with --tokenizer)")
+        enc = tokenizer.apply_chat_template(req.messages, add_generation_prompt=True, tokenize=True)
+        ids = list(enc["input_ids"] if hasattr(enc, "keys") else enc)  # a list, or an encoding (newer tokenizers)
+        params = params_of(req, ids)
+        head = {"created": int(time.time()), "model": req.model or model_name}
+        if req.stream:
+            return sse(ids, params, lambda delta, new, fin: dict(head, id="chatcmpl-stream",
+                                                                 object="chat.completion.chunk", choices=[
+                {"index": 0, "delta": {"content": delta} if delta else {}, "finish_reason": fin}]))
+        r = run(ids, params)
+        return dict(head, id=f"chatcmpl-{r.rid}", object="chat.completion", choices=[
+            {"index": 0, "message": {"role": "assistant", "content": text_of(r.output, params, True)},
+             "finish_reason": finish_of(r)}], usage=usage(len(ids), len(r.output)))
 
     @app.get("/health")
     def health():

@@ -260,3 +260,60 @@ def test_completions_need_a_tokenizer_for_text():
         assert ok["choices"][0]["text"] is None and len(ok["choices"][0]["token_ids"]) == 2
     finally:
         b.close(timeout=60)
+
+
+def _events(resp):
+    import json as json_
+
+    out = []
+    for line in resp.iter_lines():
+        line = line if isinstance(line, str) else line.decode()
+        if line.startswith("data: "):
+            out.append(line[6:] if line[6:] == "[DONE]" else json_.loads(line[6:]))
+    return out
+
+
+def test_streamed_completions_and_chat():
+    from fastapi.testclient import TestClient
+
+    from eagle4_b200.api import LLM, TreeSpec
+    from eagle4_b200.serve import Batcher, make_app
+
+    llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_batch=2, max_len=256)
+    tok = _word_tokenizer(4096)
+    tok.chat_template = ("{% for m in messages %}<{{ loop.index + 10 }}> {{ m['content'] }} {% endfor %}"
+                         "{% if add_generation_prompt %}<9>{% endif %}")
+    prompt_ids = list(range(30, 45))
+    plain = llm.generate([torch.tensor(prompt_ids)], 10, speculative=False)[0].tolist()
+    b = Batcher(llm.engine, detokenize=lambda ids: tok.decode(ids))
+    try:
+        client = TestClient(make_app(b, tok, "tiny"))
+        with client.stream("POST", "/v1/completions", json={"prompt": prompt_ids, "max_tokens": 10,
+                                                             "ignore_eos": True, "stream": True}) as r:
+            ev = _events(r)
+        assert ev[-1] == "[DONE]" and ev[-2]["choices"][0]["finish_reason"] == "length"
+        chunks = ev[:-1]
+        assert sum((c["choices"][0]["token_ids"] for c in chunks), []) == plain
+        assert "".join(c["choices"][0]["text"] or "" for c in chunks) == tok.decode(plain)
+        assert ev[-2]["usage"]["completion_tokens"] == 10
+        # a stop string inside the stream: the streamed text never shows it
+        stop = f"<{plain[4]}>"
+        with client.stream("POST", "/v1/completions", json={"prompt": prompt_ids, "max_tokens": 10, "stop": stop,
+                                                             "ignore_eos": True, "stream": True}) as r:
+            ev = _events(r)
+        text = "".join(c["choices"][0]["text"] or "" for c in ev[:-1])
+        full = tok.decode(plain[:plain.index(plain[4]) + 1])
+        assert text == full[:full.index(stop)] and ev[-2]["choices"][0]["finish_reason"] == "stop"
+        # chat: the template's prompt, the same tokens as the equivalent completion
+        msgs = [{"role": "user", "content": "<30> <31> <32>"}]
+        want_ids = list(tok.apply_chat_template(msgs, add_generation_prompt=True, tokenize=True)["input_ids"])
+        c = client.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 5, "ignore_eos": True}).json()
+        cmp = client.post("/v1/completions", json={"prompt": want_ids, "max_tokens": 5, "ignore_eos": True}).json()
+        assert c["object"] == "chat.completion" and c["choices"][0]["message"]["content"] == cmp["choices"][0]["text"]
+        assert c["usage"]["prompt_tokens"] == len(want_ids)
+        with client.stream("POST", "/v1/chat/completions", json={"messages": msgs, "max_tokens": 5,
+                                                                  "ignore_eos": True, "stream": True}) as r:
+            ev = _events(r)
+        assert "".join(e["choices"][0]["delta"].get("content", "") for e in ev[:-1]) == cmp["choices"][0]["text"]
+    finally:
+        b.close(timeout=60)
