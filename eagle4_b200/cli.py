@@ -41,7 +41,7 @@ def _model_args(args) -> dict:
 
 
 def build_llm(model: str, draft: Optional[str], *, max_batch: int, max_len: int, tree, device="cuda",
-              config=None, tp=None, dtype=None):
+              config=None, tp=None, dtype=None, temperature: float = 0.0, seed: int = 0):
     """A named synthetic shape (random weights) or a checkpoint directory pair; ``tp``: this rank's
     :class:`~eagle4_b200.parallel.tp.TensorParallel` (the weights are sharded over its group)."""
     import torch
@@ -51,9 +51,9 @@ def build_llm(model: str, draft: Optional[str], *, max_batch: int, max_len: int,
     dtype = dtype or torch.bfloat16
     if model in NAMED:
         return LLM.synthetic(model, device=device, tree=tree, max_batch=max_batch, max_len=max_len, config=config,
-                             tp=tp, dtype=dtype)
+                             tp=tp, dtype=dtype, temperature=temperature, sample_seed=seed)
     return from_pretrained(model, draft, device=device, tree=tree, max_batch=max_batch, max_len=max_len,
-                           config=config, tp=tp, dtype=dtype)
+                           config=config, tp=tp, dtype=dtype, temperature=temperature, sample_seed=seed)
 
 
 def serve_config(output: Path) -> dict:

@@ -403,6 +403,10 @@ def main(argv: Optional[List[str]] = None) -> int:
                     help="tensor-parallel collectives: fused peer-memory kernels, or NCCL through torch")
     ap.add_argument("--tokenizer", help="tokenizer directory for text prompts (default: the target directory, "
                                         "when it has one)")
+    ap.add_argument("--temperature", type=float, default=0.0,
+                    help="0: greedy (equal to plain greedy decoding); > 0: every request sampled at it (tree rejection)")
+    ap.add_argument("--seed", type=int, default=0, help="sampling seed")
+    ap.add_argument("--tree", default="12,4,16", help="steps,top_k,draft_tokens: the largest tree a round may draft")
     args = ap.parse_args(argv)
 
     from eagle4_b200.api import TreeSpec
@@ -422,8 +426,9 @@ def main(argv: Optional[List[str]] = None) -> int:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
         tp = TensorParallel(backend=args.tp_backend, max_rows=max(256, args.max_batch * 32), max_cols=8192)
         lockstep = Lockstep()
-    llm = build_llm(args.model, args.draft, max_batch=args.max_batch, max_len=args.max_len, tree=TreeSpec(),
-                    config=args.config, tp=tp)
+    llm = build_llm(args.model, args.draft, max_batch=args.max_batch, max_len=args.max_len,
+                    tree=TreeSpec(*(int(v) for v in args.tree.split(","))), config=args.config, tp=tp,
+                    temperature=args.temperature, seed=args.seed)
     if tp is not None:  # a dead or stalled rank is named by the heartbeat before the next round's collectives
         from eagle4_b200.parallel.health import process_group_heartbeat
 
