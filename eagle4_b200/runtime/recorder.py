@@ -2,21 +2,22 @@
 
 Each record: round index, batch size, round kind (``tree`` / ``chain`` / ``native`` / ``plain``), drafted depth and
 verify width, tokens emitted per request, and the round's device time when it was timed. ``summary()`` gives tokens
-per round, acceptance histogram and time shares. Enable with ``Engine.recorder = RoundRecorder(path)``.
+per round, acceptance histogram and time shares over the most recent ``keep`` rounds (a long-running server keeps a
+bounded window in memory; the file has every round). Enable with ``Engine.recorder = RoundRecorder(path)``.
 """
 
 from __future__ import annotations
 
 import json
 import os
-from collections import Counter
+from collections import Counter, deque
 from typing import List, Optional
 
 
 class RoundRecorder:
-    def __init__(self, path: Optional[str] = None, flush_every: int = 256):
+    def __init__(self, path: Optional[str] = None, flush_every: int = 256, keep: int = 65536):
         self.path, self.flush_every = path, flush_every
-        self.records: List[dict] = []
+        self.records: "deque[dict]" = deque(maxlen=keep)
         self._pending: List[dict] = []
         self.rounds = 0
 

@@ -407,6 +407,7 @@ def main(argv: Optional[List[str]] = None) -> int:
                     help="0: greedy (equal to plain greedy decoding); > 0: every request sampled at it (tree rejection)")
     ap.add_argument("--seed", type=int, default=0, help="sampling seed")
     ap.add_argument("--tree", default="12,4,16", help="steps,top_k,draft_tokens: the largest tree a round may draft")
+    ap.add_argument("--round-log", help="append one JSON line per served round to this file (rank 0)")
     args = ap.parse_args(argv)
 
     from eagle4_b200.api import TreeSpec
@@ -447,12 +448,18 @@ def main(argv: Optional[List[str]] = None) -> int:
             return 0
         import uvicorn
 
+        if args.round_log:
+            from eagle4_b200.runtime.recorder import RoundRecorder
+
+            llm.engine.recorder = RoundRecorder(args.round_log)
         batcher = Batcher(llm.engine, speculative=speculative, lockstep=lockstep, detokenize=detokenize)
         try:
             uvicorn.run(make_app(batcher, tokenizer, os.path.basename(os.path.normpath(args.model))),
                         host=args.host, port=args.port)
         finally:
             batcher.close()
+            if llm.engine.recorder is not None:
+                llm.engine.recorder.flush()
         return 0 if batcher.failed is None else 1
     finally:
         if tp is not None:
