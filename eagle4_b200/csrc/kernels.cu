@@ -325,14 +325,15 @@ torch::Tensor gated_rmsnorm(const torch::Tensor& o, const torch::Tensor& z, cons
   auto oc = o.contiguous();
   const int T = oc.size(0), G = oc.size(1), D = oc.size(2);
   TORCH_CHECK(z.stride(-1) == 1);
-  TORCH_CHECK(w.is_contiguous() && (w.numel() == D || w.numel() == int64_t(G) * D),
+  TORCH_CHECK(w.numel() == D || w.numel() == int64_t(G) * D,
               "gated_rmsnorm: the weight is one [D] row shared by the groups or one row per group");
   const int wg = w.numel() == D ? 0 : D;
+  auto wc = w.contiguous();
   auto y = torch::empty({T, G * D}, o.options());
   const int warps = T * G;
   if (T) {
     C10_CUDA_CHECK(launch_pdl(gated_rmsnorm_kernel, (warps * 32 + 255) / 256, 256, 0,
-                              at::cuda::getCurrentCUDAStream().stream(), CBF16(oc), CBF16(z), z.stride(0), CBF16(w),
+                              at::cuda::getCurrentCUDAStream().stream(), CBF16(oc), CBF16(z), z.stride(0), CBF16(wc),
                               wg, gate_first ? 1 : 0, BF16(y), T, G, D, float(eps)));
   }
   return y;
