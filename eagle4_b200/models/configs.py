@@ -13,7 +13,7 @@ mixer (``swiglu``, ``relu2`` or none), each behind a pre-norm with a residual ad
 from __future__ import annotations
 
 import json
-from dataclasses import asdict, dataclass, field
+from dataclasses import asdict, dataclass
 from typing import List, Optional, Tuple
 
 

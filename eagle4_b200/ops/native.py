@@ -7,7 +7,6 @@ Importing this module on a machine with a GPU loads the extension; if it cannot 
 from __future__ import annotations
 
 import contextlib
-import math
 from typing import Dict, Optional, Tuple
 
 import torch

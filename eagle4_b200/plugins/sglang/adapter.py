@@ -15,7 +15,7 @@ from __future__ import annotations
 
 import logging
 from functools import cached_property
-from typing import Any, List, Optional
+from typing import List, Optional
 
 import torch
 

@@ -11,7 +11,7 @@ from __future__ import annotations
 import importlib
 from typing import List, NamedTuple, Optional
 
-from eagle4_b200.plugins.contract import CALL, EXISTS, OVERRIDE, Hook, override_mismatches, problems
+from eagle4_b200.plugins.contract import EXISTS, OVERRIDE, Hook, override_mismatches, problems
 
 RELEASE_MIN_API_VERSION = 4
 CAPABILITY_API_VERSIONS = frozenset({3})

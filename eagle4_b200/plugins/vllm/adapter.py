@@ -19,7 +19,7 @@ from eagle4_b200.core.config import HarnessConfig, Mode
 from eagle4_b200.core.draft_tree import rows_meta
 from eagle4_b200.core.limits import req_to_token_span
 from eagle4_b200.plugins.common import accept_greedy_rows, host_base
-from eagle4_b200.plugins.vllm.config import MethodConfig, parse_method_config
+from eagle4_b200.plugins.vllm.config import MethodConfig
 
 METHOD = "eagle_harness"
 

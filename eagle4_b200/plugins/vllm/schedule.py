@@ -25,7 +25,7 @@ and the ``(first, last, value)`` range triples are vLLM's; the reference method 
 
 from __future__ import annotations
 
-from typing import Any, List, Optional, Sequence, Tuple
+from typing import Any, List, Sequence, Tuple
 
 from eagle4_b200.core.chain_width import chain_widths, load_tree_rounds, merge_ranges, served_tree_schedule, width_at
 from eagle4_b200.core.limits import ComputeIntensity, cost_batch_sizes, max_batch_size, verify_buckets

@@ -13,7 +13,7 @@ import logging
 import math
 import os
 from collections import Counter
-from typing import Callable, List, Optional, Sequence
+from typing import List, Optional, Sequence
 
 from eagle4_b200.core.config import HarnessConfig, Mode, build_cost_model
 from eagle4_b200.core.cost_model import CostModel, FixedShapePolicy, depth_loss_ratio

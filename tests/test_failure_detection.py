@@ -129,7 +129,6 @@ def test_batches_above_the_verify_limit_decode_natively():
     import torch
 
     from eagle4_b200.api import LLM, TreeSpec
-    from eagle4_b200.runtime.recorder import RoundRecorder
 
     llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_len=256, max_batch=2,
                         config='{"mode": "static", "max_verify_batch_size": 1}')

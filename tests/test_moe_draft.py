@@ -6,8 +6,6 @@ fc2_latent_proj, ReLU^2 shared expert after: the formula of the reference's
 tests/test_eagle4_model.py:370-392), grouped routing against its definition, the config and checkpoint layouts by
 round trips, and the engine by speculative == plain greedy decoding."""
 
-import dataclasses
-
 import pytest
 import torch
 

@@ -9,7 +9,6 @@ installable offline.
 import importlib
 import sys
 
-import pytest
 import torch
 
 from tests import fake_hosts

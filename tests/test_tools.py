@@ -3,7 +3,6 @@ of speculative against plain decoding, and the mixed-stop batch check (including
 
 import json
 
-import pytest
 import torch
 
 from eagle4_b200.tools import parity, stop_check
