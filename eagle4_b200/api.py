@@ -150,7 +150,8 @@ def from_pretrained(model_path: str, draft_path: Optional[str] = None, *, device
     aux = (2, tcfg.num_layers // 2, tcfg.num_layers - 3)
     if draft_path is not None:
         with open(os.path.join(draft_path, "config.json"), encoding="utf-8") as f:
-            dcfg = draft_config_from_hf(json.load(f), target_vocab_size=tcfg.vocab_size)
+            dcfg = draft_config_from_hf(json.load(f), target_vocab_size=tcfg.vocab_size,
+                                        target_num_layers=tcfg.num_layers)
         aux = dcfg.aux_layer_ids
     world, rank = (tp.world, tp.rank) if tp is not None else (1, 0)
     sd = {k: v.to(dtype) if v.is_floating_point() else v for k, v in _load_safetensors_dir(model_path, "cpu").items()}

@@ -129,7 +129,7 @@ def _full_configs(args):
         return tcfg, NAMED[args.model][1](tcfg)
     tcfg = TargetConfig.from_hf(json.loads((Path(args.model) / "config.json").read_text()))
     dcfg = draft_config_from_hf(json.loads((Path(args.draft) / "config.json").read_text()),
-                                target_vocab_size=tcfg.vocab_size)
+                                target_vocab_size=tcfg.vocab_size, target_num_layers=tcfg.num_layers)
     return tcfg, dcfg
 
 

@@ -15,7 +15,7 @@ Configs are plain dicts here (or any object with ``to_dict()``); no engine is ne
 from __future__ import annotations
 
 from numbers import Integral
-from typing import Any, Dict, Mapping, Optional
+from typing import Any, Dict, Mapping, Optional, Tuple
 
 from eagle4_b200.models.configs import DraftConfig
 from eagle4_b200.models.eagle4_structure import LATENT_MOE_ARCHITECTURE, draft_moe_architecture, draft_uses_rope
@@ -202,8 +202,19 @@ def _moe_of(cfg: dict) -> Optional[dict]:
                       scale=float(cfg.get("routed_scaling_factor") or 1.0))
 
 
-def draft_config_from_hf(config, *, target_vocab_size: Optional[int] = None) -> DraftConfig:
-    """A ``DraftConfig`` from a released EAGLE-4 (or EAGLE-3) draft ``config.json``."""
+def _default_aux(target_num_layers: Optional[int]) -> Tuple[int, ...]:
+    if not target_num_layers:
+        raise ValueError("the draft config names no aux layers (eagle_config.eagle_aux_hidden_state_layer_ids): "
+                         "give the target's layer count")
+    n = int(target_num_layers)
+    return (2, n // 2, n - 3)
+
+
+def draft_config_from_hf(config, *, target_vocab_size: Optional[int] = None,
+                         target_num_layers: Optional[int] = None) -> DraftConfig:
+    """A ``DraftConfig`` from a released EAGLE-4 (or EAGLE-3) draft ``config.json``. A config that names no aux layers
+    (``eagle_config.eagle_aux_hidden_state_layer_ids``; common for EAGLE-3 drafts) takes the usual EAGLE-3 choice for
+    a target of ``target_num_layers`` layers: layers 2, L // 2 and L - 3."""
     cfg = _as_dict(config)
     eagle4 = EAGLE4_ARCH in (cfg.get("architectures") or ())
     if eagle4:
@@ -220,7 +231,8 @@ def draft_config_from_hf(config, *, target_vocab_size: Optional[int] = None) -> 
         vocab_size=vocab, draft_vocab_size=cfg.get("draft_vocab_size") or cfg["vocab_size"],
         num_heads=cfg["num_attention_heads"], num_kv_heads=cfg.get("num_key_value_heads", cfg["num_attention_heads"]),
         head_dim=hd, intermediate_size=cfg["intermediate_size"],
-        aux_layer_ids=tuple(ids) if ids else (2, 0, 0), rms_norm_eps=cfg.get("rms_norm_eps", 1e-6),
+        aux_layer_ids=tuple(ids) if ids else _default_aux(target_num_layers),
+        rms_norm_eps=cfg.get("rms_norm_eps", 1e-6),
         rope_theta=rope.get("rope_theta", cfg.get("rope_theta", 10000.0)),
         sliding_window=resolve_draft_sliding_window(cfg) if eagle4 else None,
         fc_norm=bool(cfg.get("fc_norm") or cfg.get("enable_fc_norm")), norm_output=bool(cfg.get("norm_output")),

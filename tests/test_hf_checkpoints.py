@@ -79,3 +79,42 @@ def test_llama_checkpoint_logits_match_hugging_face(tmp_path):
     model = LlamaForCausalLM(cfg).eval()
     _perturb(model)
     _check(tmp_path, cfg, model)
+
+
+def test_eagle3_draft_without_aux_ids_takes_the_target_default_and_decodes_greedily(tmp_path):
+    """An EAGLE-3 draft whose config names no aux layers (with a reduced draft vocabulary and ``d2t``) over a Llama
+    checkpoint: the aux layers are 2, L // 2, L - 3 of the target, and speculative output equals plain greedy."""
+    import dataclasses
+
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from eagle4_b200.api import TreeSpec, from_pretrained
+    from eagle4_b200.models import configs, weights
+
+    torch.manual_seed(2)
+    cfg = LlamaConfig(vocab_size=512, hidden_size=128, num_hidden_layers=8, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=32, intermediate_size=256)
+    model = LlamaForCausalLM(cfg).eval()
+    _perturb(model)
+    target_dir, draft_dir = tmp_path / "t", tmp_path / "d"
+    target_dir.mkdir()
+    _save(str(target_dir), cfg, model)
+    tcfg = configs.TargetConfig.from_hf(cfg.to_dict())
+    dcfg = dataclasses.replace(configs.eagle3_llama_draft(tcfg), draft_vocab_size=128)
+    dw = weights.init_draft(dcfg, seed=5)
+    weights.save_draft(str(draft_dir), dcfg, dw)
+    hf = json.loads((draft_dir / "config.json").read_text())
+    hf.pop("eagle_config", None)
+    (draft_dir / "config.json").write_text(json.dumps(hf))
+    llm = from_pretrained(str(target_dir), str(draft_dir), device="cpu", dtype=torch.float32, max_len=128,
+                          tree=TreeSpec(4, 2, 8))
+    assert llm.draft.cfg.aux_layer_ids == (2, 4, 5) and llm.draft.cfg.family == "eagle3"
+    prompt = torch.randint(0, 512, (1, 12), generator=torch.Generator().manual_seed(3))
+    spec = llm.generate(prompt, 10)
+    plain = llm.generate(prompt, 10, speculative=False)
+    assert torch.equal(spec, plain)
+    with torch.no_grad():
+        ids = prompt[0].tolist()
+        for _ in range(10):
+            ids.append(int(model(torch.tensor([ids])).logits[0, -1].argmax()))
+    assert plain[0].tolist() == ids[12:]
