@@ -118,3 +118,53 @@ def test_eagle3_draft_without_aux_ids_takes_the_target_default_and_decodes_greed
         for _ in range(10):
             ids.append(int(model(torch.tensor([ids])).logits[0, -1].argmax()))
     assert plain[0].tolist() == ids[12:]
+
+
+def _hf_target(kind):
+    if kind == "qwen3_5":
+        from transformers import Qwen3_5ForCausalLM, Qwen3_5TextConfig
+
+        cfg = Qwen3_5TextConfig(vocab_size=512, hidden_size=128, num_hidden_layers=4,
+                                layer_types=["linear_attention"] * 3 + ["full_attention"], num_attention_heads=4,
+                                num_key_value_heads=2, head_dim=32, intermediate_size=256, linear_num_key_heads=2,
+                                linear_num_value_heads=4, linear_key_head_dim=16, linear_value_head_dim=16,
+                                linear_conv_kernel_dim=4)
+        return cfg, Qwen3_5ForCausalLM(cfg).eval()
+    from transformers import NemotronHConfig, NemotronHForCausalLM
+
+    cfg = NemotronHConfig(vocab_size=512, hidden_size=128, hybrid_override_pattern="M*MM", num_attention_heads=4,
+                          num_key_value_heads=2, head_dim=32, intermediate_size=256, mamba_num_heads=8,
+                          mamba_head_dim=16, ssm_state_size=16, n_groups=2, conv_kernel=4, use_conv_bias=True,
+                          layer_norm_epsilon=1e-5, chunk_size=16, time_step_min=1e-6)
+    return cfg, NemotronHForCausalLM(cfg).eval()
+
+
+@pytest.mark.parametrize("kind", ["qwen3_5", "nemotron_h"])
+def test_eagle4_draft_over_a_checkpoint_target_decodes_plain_greedy(tmp_path, kind):
+    """An EAGLE-4 draft checkpoint (low-rank candidate head) over a Hugging Face target: speculative output equals
+    plain greedy decoding, which equals Hugging Face's own greedy decoding."""
+    import dataclasses
+
+    from eagle4_b200.api import TreeSpec, from_pretrained
+    from eagle4_b200.models import configs, weights
+
+    torch.manual_seed(4)
+    cfg, model = _hf_target(kind)
+    _perturb(model)
+    target_dir, draft_dir = tmp_path / "t", tmp_path / "d"
+    target_dir.mkdir()
+    _save(str(target_dir), cfg, model)
+    tcfg = configs.TargetConfig.from_hf(json.loads((target_dir / "config.json").read_text()))
+    dcfg = dataclasses.replace(configs.tiny_draft(tcfg, draft_vocab=512), aux_layer_ids=(0, 1, 2))
+    weights.save_draft(str(draft_dir), dcfg, weights.init_draft(dcfg, seed=6))
+    llm = from_pretrained(str(target_dir), str(draft_dir), device="cpu", dtype=torch.float32, max_len=128,
+                          tree=TreeSpec(4, 2, 8))
+    prompt = torch.randint(0, 512, (1, 9), generator=torch.Generator().manual_seed(5))
+    spec = llm.generate(prompt, 8)
+    plain = llm.generate(prompt, 8, speculative=False)
+    assert torch.equal(spec, plain)
+    with torch.no_grad():
+        ids = prompt[0].tolist()
+        for _ in range(8):
+            ids.append(int(model(torch.tensor([ids])).logits[0, -1].argmax()))
+    assert plain[0].tolist() == ids[9:]
