@@ -19,7 +19,7 @@ from typing import List, Optional, Tuple
 
 @dataclass
 class TargetConfig:
-    family: str  # "qwen3_5" | "nemotron_h" | "llama"
+    family: str  # "qwen3_5" | "qwen3" | "nemotron_h" | "llama"
     hidden_size: int
     vocab_size: int
     layers: List[Tuple[Optional[str], Optional[str]]]  # (mixer, mlp) per layer
@@ -93,9 +93,24 @@ class TargetConfig:
 
     @classmethod
     def from_hf(cls, hf: dict) -> "TargetConfig":
-        """Map a Hugging Face ``config.json`` (qwen3_5 / qwen3_next text config, nemotron_h, llama)."""
+        """Map a Hugging Face ``config.json`` (Qwen3.5 text config, dense Qwen3, Nemotron-H, Llama). Mixture-of-experts
+        targets are refused (not built)."""
         text = hf.get("text_config", hf)
         mt = text.get("model_type", "")
+        if "moe" in mt or text.get("num_experts") or text.get("n_routed_experts"):
+            raise NotImplementedError(f"mixture-of-experts targets ({mt}) are not built by eagle4_b200's own engine; "
+                                      "serve them through a host plugin")
+        if mt == "qwen3":  # dense Qwen3: attention with q/k norms, full rotary, plain RMSNorm weights
+            hd = text.get("head_dim") or text["hidden_size"] // text["num_attention_heads"]
+            rope = text.get("rope_parameters", {}) or {}
+            return cls(
+                family="qwen3", hidden_size=text["hidden_size"], vocab_size=text["vocab_size"],
+                layers=[("attn", "swiglu")] * text["num_hidden_layers"], intermediate_size=text["intermediate_size"],
+                rms_norm_eps=text.get("rms_norm_eps", 1e-6), num_heads=text["num_attention_heads"],
+                num_kv_heads=text["num_key_value_heads"], head_dim=hd, qk_norm=True, rotary_dim=hd,
+                rope_theta=rope.get("rope_theta", text.get("rope_theta", 1e6)),
+                tie_embeddings=bool(text.get("tie_word_embeddings")),
+            )
         if mt.startswith("qwen3"):
             types = text["layer_types"]
             layers = [("gdn" if t == "linear_attention" else "attn", "swiglu") for t in types]
@@ -157,6 +172,9 @@ class TargetConfig:
                         linear_conv_kernel_dim=self.conv_kernel,
                         rope_parameters={"rope_theta": self.rope_theta,
                                          "partial_rotary_factor": self.rotary_dim / self.head_dim})
+        if self.family == "qwen3":
+            return dict(common, model_type="qwen3", architectures=["Qwen3ForCausalLM"], rms_norm_eps=self.rms_norm_eps,
+                        rope_theta=self.rope_theta)
         if self.family == "nemotron_h":
             sym = {("mamba", None): "M", ("attn", None): "*", (None, "relu2"): "-"}
             return dict(common, model_type="nemotron_h", architectures=["NemotronHForCausalLM"],

@@ -168,3 +168,24 @@ def test_eagle4_draft_over_a_checkpoint_target_decodes_plain_greedy(tmp_path, ki
         for _ in range(8):
             ids.append(int(model(torch.tensor([ids])).logits[0, -1].argmax()))
     assert plain[0].tolist() == ids[9:]
+
+
+def test_dense_qwen3_checkpoint_logits_match_hugging_face(tmp_path):
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    torch.manual_seed(6)
+    cfg = Qwen3Config(vocab_size=512, hidden_size=128, num_hidden_layers=3, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=32, intermediate_size=256)
+    model = Qwen3ForCausalLM(cfg).eval()
+    _perturb(model)
+    llm = _check(tmp_path, cfg, model)
+    assert llm.target.cfg.family == "qwen3" and llm.target.cfg.qk_norm and not llm.target.cfg.norm_offset
+
+
+def test_moe_targets_are_refused():
+    from eagle4_b200.models.configs import TargetConfig
+
+    with pytest.raises(NotImplementedError, match="mixture-of-experts"):
+        TargetConfig.from_hf({"model_type": "qwen3_moe", "num_experts": 64})
+    with pytest.raises(NotImplementedError, match="mixture-of-experts"):
+        TargetConfig.from_hf({"model_type": "qwen3_next", "num_experts": 512})
