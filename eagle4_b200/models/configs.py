@@ -97,7 +97,8 @@ class TargetConfig:
         targets are refused (not built)."""
         text = hf.get("text_config", hf)
         mt = text.get("model_type", "")
-        if "moe" in mt or text.get("num_experts") or text.get("n_routed_experts"):
+        experts = text.get("num_experts") or text.get("n_routed_experts")
+        if "moe" in mt or (experts and mt != "nemotron_h"):  # Nemotron-H names its MoE blocks in the layer pattern
             raise NotImplementedError(f"mixture-of-experts targets ({mt}) are not built by eagle4_b200's own engine; "
                                       "serve them through a host plugin")
         if mt == "qwen3":  # dense Qwen3: attention with q/k norms, full rotary, plain RMSNorm weights
