@@ -22,6 +22,14 @@ class HarnessDrafter(_Eagle):
     """Tree policy over a fixed-shape draft tree (graph-capturable buffers, one per batch bucket)."""
 
     tree: Optional[DraftTree] = None
+    options = None  # TokenSpeedOptions of the launch
+
+    def configure_algorithm(self, algorithm_config):
+        """TokenSpeed hands over the launch's ``--speculative-algorithm-config`` (``plugins.tokenspeed.config``)."""
+        from eagle4_b200.plugins.tokenspeed.config import parse_algorithm_config
+
+        self.options = parse_algorithm_config(algorithm_config)
+        return self.options
 
     def bind_tree_shape(self, top_k: int, depth: int, max_bs: int, hidden: int, device, verify: int) -> None:
         self.tree = DraftTree(TreeShape(top_k, depth), max_bs, hidden, torch.bfloat16, device, max_verify=verify)

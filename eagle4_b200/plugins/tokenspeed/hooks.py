@@ -49,7 +49,8 @@ HOOKS = (
          ("algorithm", "drafter_cls", "model_cls", "captures_aux_hidden_states", "uses_tree_layout")),
     Hook("tokenspeed.runtime.plugins.registry:register_model", ("cls", "architectures")),
     Hook("tokenspeed.runtime.configs.model_profile:ModelProfile", (), EXISTS),
-    Hook(f"{_BASE}.configure_algorithm", ("algorithm_config",)),
+    Hook(f"{_BASE}.configure_algorithm", ("algorithm_config",), OVERRIDE,
+         "eagle4_b200.plugins.tokenspeed.adapter:HarnessDrafter"),
     Hook("tokenspeed.runtime.execution.drafter:drafter_captures_aux_hidden_states", ("algorithm",)),
     Hook(f"{_EAGLE}.bind_tree", ("tree_spec",)),
     Hook(f"{_EAGLE}.bind_tree_lanes", ("tree_spec",)),

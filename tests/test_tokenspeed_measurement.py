@@ -43,3 +43,36 @@ def test_host_timings_fit_into_cost_tables(tmp_path):
         CostMeasurement(str(tmp_path / "x"), batch_size=1, intensity=ComputeIntensity.HIGH, node_top_k=4,
                         verify_num=16, context_step=512, context_stop=1024, draft=AttentionShape(1),
                         target=AttentionShape(16)).write()
+
+
+def test_tokenspeed_algorithm_config():
+    import pytest
+
+    from eagle4_b200.core.config import Mode
+    from eagle4_b200.plugins.tokenspeed.adapter import HarnessDrafter
+    from eagle4_b200.plugins.tokenspeed.config import parse_algorithm_config
+
+    static = parse_algorithm_config({"mode": "static"})
+    assert static.harness.mode is Mode.STATIC and not static.sampled_proposals
+    chain = parse_algorithm_config({"intensity": "chain_intensity", "chain_width_table": [[1, 6], [16, 4], [64, 2]]})
+    assert chain.fully_scheduled and chain.chain_width(1) == 6 and chain.chain_width(20) == 4
+    assert chain.chain_width(512) == 2
+    part = parse_algorithm_config({"intensity": "chain_intensity", "data_path": "/cal",
+                                   "chain_width_table": [[8, 4]]})
+    assert not part.fully_scheduled and part.chain_width(4) is None
+    assert parse_algorithm_config({"data_path": "/cal", "sampled_proposals": True}).sampled_proposals
+    bad = [
+        {},                                                          # serve mode without data or a full table
+        {"mode": "static", "sampled_proposals": True},               # sampling is a serve-mode option
+        {"mode": "calibrate"},                                       # calibrate writes under data_path
+        {"data_path": "/cal", "chain_width_table": [[1, 4]]},        # a table needs chain intensity
+        {"intensity": "chain_intensity", "chain_width_table": [[4, 4], [2, 3]]},  # not increasing
+        {"intensity": "chain_intensity", "chain_width_table": [[1, 1]]},           # width below 2
+        {"mode": "static", "sampled_proposals": "yes"},
+        {"mode": "static", "unknown_key": 1},
+    ]
+    for cfg in bad:
+        with pytest.raises(ValueError):
+            parse_algorithm_config(cfg)
+    drafter = HarnessDrafter()
+    assert drafter.configure_algorithm({"mode": "static"}).harness.mode is Mode.STATIC
