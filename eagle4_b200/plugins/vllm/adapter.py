@@ -96,10 +96,13 @@ class HarnessSpeculator(_Speculator):
     served_rounds = None
 
     def load_model(self, draft_model, *, max_reqs: int, max_len: int, tree=(12, 4, 16), config=None,
-                   temperature: float = 0.0, seed: int = 0, method: Optional[MethodConfig] = None) -> None:
+                   temperature: float = 0.0, seed: int = 0, method: Optional[MethodConfig] = None,
+                   linear_layers=None, key=None) -> None:
         """``draft_model``: a ``DraftModel`` or the vLLM draft model class holding one. ``method`` (a parsed
         ``method_config``) sets the tree, the harness config, the batch policy and the
-        served-round recording; without it ``tree`` = (depth, top-k, verify width) and ``config`` do."""
+        served-round recording; without it ``tree`` = (depth, top-k, verify width) and ``config`` do.
+        ``linear_layers``: the target's GDN / Mamba2 layers, checked to hand their rows to the tree verify (a tree
+        only); ``key``: this worker's setup, checked against the calibration data's before serving."""
         import dataclasses
 
         from eagle4_b200.core.chain_width import chain_widths
@@ -113,11 +116,19 @@ class HarnessSpeculator(_Speculator):
             if draft_model is None:
                 raise RuntimeError("the draft model's weights are not loaded")
         if method is not None:
+            if key is not None:
+                from eagle4_b200.plugins.vllm.schedule import verify_widths
+
+                verify_widths(method, key=key)  # refuses data measured on another setup
             tree = (method.tree_depth, method.node_top_k, method.max_verify_width)
             config = method.harness
             if method.depth_stop_gain is None:  # no depth stop: full-depth trees (the static policy)
                 config = dataclasses.replace(config, mode=Mode.STATIC)
         steps, top_k, width = tree
+        if linear_layers is not None and top_k > 1:
+            from eagle4_b200.plugins.vllm.tree_verify import check_tree_verifiable
+
+            check_tree_verifiable(linear_layers)
         self.drafter = HostDrafter(draft_model, max_reqs=max_reqs, max_len=max_len, steps=steps, top_k=top_k,
                                    verify_tokens=width, config=config, temperature=temperature, seed=seed)
         schedule = None

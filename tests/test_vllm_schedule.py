@@ -102,3 +102,36 @@ def test_method_spec_configure_fills_the_config():
     spec = _spec({"max_verify_width": 32})
     out = HarnessMethodSpec().configure(spec)
     assert spec.num_speculative_tokens_per_batch_size and out["num_speculative_tokens"] == spec.num_speculative_tokens
+
+
+def test_speculator_load_checks_layers_and_the_data_key(tmp_path):
+    import dataclasses
+
+    from eagle4_b200.models import configs, weights
+    from eagle4_b200.models.draft import DraftModel
+    from eagle4_b200.plugins.vllm.adapter import HarnessSpeculator
+
+    tc = configs.tiny_hybrid()
+    dc = configs.tiny_draft(tc, draft_vocab=4096)
+    draft = DraftModel(dc, weights.init_draft(dc, seed=2))
+
+    class QwenGatedDeltaNetAttention:
+        pass
+
+    class ShortConv:
+        pass
+
+    method = parse_method_config({"mode": "static", "node_top_k": 2, "tree_depth": 4, "max_verify_width": 8})
+    HarnessSpeculator().load_model(draft, max_reqs=2, max_len=128, method=method,
+                                   linear_layers=[QwenGatedDeltaNetAttention()])
+    with pytest.raises(RuntimeError, match="ShortConv"):
+        HarnessSpeculator().load_model(draft, max_reqs=2, max_len=128, method=method, linear_layers=[ShortConv()])
+    rows = [{"batch_size": 1, "width": 8, "round_us": 9000.0, "accept": 2.0, "count": 10},
+            {"batch_size": 1, "width": 4, "round_us": 8000.0, "accept": 1.5, "count": 10}]
+    merge_tree_rounds(str(tmp_path), rows)
+    write_key(str(tmp_path), KEY)
+    keyed = dataclasses.replace(method, harness=dataclasses.replace(method.harness, data_path=str(tmp_path)))
+    HarnessSpeculator().load_model(draft, max_reqs=2, max_len=128, method=keyed, key=KEY)
+    with pytest.raises(ValueError, match="another setup"):
+        HarnessSpeculator().load_model(draft, max_reqs=2, max_len=128, method=keyed,
+                                       key=CostKey(**{**KEY.to_dict(), "gpu": "other"}))
