@@ -132,7 +132,7 @@ def _load_safetensors_dir(path: str, device) -> dict:
 
 def from_pretrained(model_path: str, draft_path: Optional[str] = None, *, device="cuda", dtype=torch.bfloat16,
                     tree: TreeSpec = TreeSpec(), max_batch: int = 1, max_len: int = 4096, config=None,
-                    tp=None, temperature: float = 0.0, sample_seed: int = 0) -> LLM:
+                    tp=None, temperature: float = 0.0, sample_seed: int = 0, kv_tokens: Optional[int] = None) -> LLM:
     """An :class:`LLM` from a Hugging Face target directory and an EAGLE-4 / EAGLE-3 draft directory (both with
     ``config.json`` and safetensors). Draft configs are validated; structures this package does not build raise.
     With ``tp`` (a :class:`~eagle4_b200.parallel.tp.TensorParallel`) every rank reads the full checkpoints into host
@@ -166,4 +166,4 @@ def from_pretrained(model_path: str, draft_path: Optional[str] = None, *, device
         dm = DraftModel(ldcfg, {k: v.to(device) for k, v in dw.items()}, tp=tp)
     del full
     return LLM(target, dm, tree=tree, max_batch=max_batch, max_len=max_len, config=config, temperature=temperature,
-               seed=sample_seed)
+               seed=sample_seed, kv_tokens=kv_tokens)

@@ -41,7 +41,8 @@ def _model_args(args) -> dict:
 
 
 def build_llm(model: str, draft: Optional[str], *, max_batch: int, max_len: int, tree, device="cuda",
-              config=None, tp=None, dtype=None, temperature: float = 0.0, seed: int = 0):
+              config=None, tp=None, dtype=None, temperature: float = 0.0, seed: int = 0,
+              kv_tokens: Optional[int] = None):
     """A named synthetic shape (random weights) or a checkpoint directory pair; ``tp``: this rank's
     :class:`~eagle4_b200.parallel.tp.TensorParallel` (the weights are sharded over its group)."""
     import torch
@@ -51,9 +52,10 @@ def build_llm(model: str, draft: Optional[str], *, max_batch: int, max_len: int,
     dtype = dtype or torch.bfloat16
     if model in NAMED:
         return LLM.synthetic(model, device=device, tree=tree, max_batch=max_batch, max_len=max_len, config=config,
-                             tp=tp, dtype=dtype, temperature=temperature, sample_seed=seed)
+                             tp=tp, dtype=dtype, temperature=temperature, sample_seed=seed, kv_tokens=kv_tokens)
     return from_pretrained(model, draft, device=device, tree=tree, max_batch=max_batch, max_len=max_len,
-                           config=config, tp=tp, dtype=dtype, temperature=temperature, sample_seed=seed)
+                           config=config, tp=tp, dtype=dtype, temperature=temperature, sample_seed=seed,
+                           kv_tokens=kv_tokens)
 
 
 def serve_config(output: Path) -> dict:
@@ -128,6 +130,8 @@ def _full_configs(args):
         tcfg = NAMED[args.model][0]()
         return tcfg, NAMED[args.model][1](tcfg)
     tcfg = TargetConfig.from_hf(json.loads((Path(args.model) / "config.json").read_text()))
+    if not args.draft:
+        return tcfg, None
     dcfg = draft_config_from_hf(json.loads((Path(args.draft) / "config.json").read_text()),
                                 target_vocab_size=tcfg.vocab_size, target_num_layers=tcfg.num_layers)
     return tcfg, dcfg
@@ -227,6 +231,17 @@ def _calibrate(args) -> int:
     return _finish(args)
 
 
+def _plan(args) -> int:
+    from eagle4_b200.runtime.memory import B200_GB, plan
+
+    tcfg, dcfg = _full_configs(args)
+    p = plan(tcfg, dcfg, tp=args.tp, max_batch=args.max_batch, max_len=args.max_len, kv_tokens=args.kv_tokens,
+             tree=tuple(int(v) for v in args.tree.split(",")), reserve_gb=args.reserve_gb)
+    summary = p.summary(args.gpu_gb or round(B200_GB, 1))
+    print(json.dumps(summary, indent=2))
+    return 0 if summary["fits"] else 1
+
+
 def main(argv: Optional[List[str]] = None) -> int:
     ap = argparse.ArgumentParser(prog="eagle4-b200", description="EAGLE-4 speculative decoding on B200.")
     sub = ap.add_subparsers(dest="command", required=True)
@@ -252,6 +267,18 @@ def main(argv: Optional[List[str]] = None) -> int:
     cal.add_argument("--timeout", type=float, help="seconds before a --tp calibration is stopped (default: none)")
     cal.add_argument("--worker", action="store_true", help=argparse.SUPPRESS)
     cal.set_defaults(func=_calibrate)
+    pl = sub.add_parser("plan", formatter_class=argparse.ArgumentDefaultsHelpFormatter,
+                        help="device memory of a serving configuration per GPU, and the KV tokens that fit")
+    pl.add_argument("--model", required=True, help="named synthetic shape or target directory")
+    pl.add_argument("--draft", help="draft checkpoint directory (named shapes bring their own draft)")
+    pl.add_argument("--tp", type=_positive, default=1)
+    pl.add_argument("--max-batch", type=_positive, default=8)
+    pl.add_argument("--max-len", type=_positive, default=8192)
+    pl.add_argument("--kv-tokens", type=_positive, help="KV token budget (default: every row at max-len)")
+    pl.add_argument("--tree", default="12,4,16", help="steps,top_k,draft_tokens")
+    pl.add_argument("--gpu-gb", type=float, help="memory budget per GPU in GB (default: a B200's)")
+    pl.add_argument("--reserve-gb", type=float, default=4.0, help="activations, graph pools, buffers, context")
+    pl.set_defaults(func=_plan)
     chk = sub.add_parser("check", help="report the serving hosts and the native library")
     chk.add_argument("--kernels", action="store_true", help="also load the native CUDA library")
     chk.set_defaults(func=lambda a: __import__("eagle4_b200.compat", fromlist=["main"]).main(

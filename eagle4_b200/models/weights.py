@@ -23,13 +23,19 @@ from eagle4_b200.ops.reference import interleave_gate_up
 
 
 def _normal(shape, std, gen, device, dtype):
+    if gen is None:  # the meta device: shapes only (memory planning)
+        return torch.empty(*shape, device=device, dtype=dtype)
     return (torch.randn(*shape, generator=gen, device=device, dtype=torch.float32) * std).to(dtype)
+
+
+def _generator(dev: torch.device, seed: int) -> Optional[torch.Generator]:
+    return None if dev.type == "meta" else torch.Generator(device=dev).manual_seed(seed)
 
 
 def init_target(cfg: TargetConfig, *, device="cpu", dtype=torch.float32, seed: int = 0) -> Dict[str, torch.Tensor]:
     """N(0, std) weights in the fused runtime layout; norms at identity, GDN/Mamba2 gates at HF's defaults."""
     dev = torch.device(device)
-    gen = torch.Generator(device=dev).manual_seed(seed)
+    gen = _generator(dev, seed)
     std = cfg.init_std
     H = cfg.hidden_size
     one = 0.0 if cfg.norm_offset else 1.0
@@ -88,7 +94,7 @@ def init_draft(cfg: DraftConfig, *, device="cpu", dtype=torch.float32, seed: int
     """Random draft head in the runtime layout. ``lm_head`` / ``embed`` may be shared from the target (the draft's
     ``embed_tokens`` is optional in released checkpoints and taken from the target)."""
     dev = torch.device(device)
-    gen = torch.Generator(device=dev).manual_seed(seed)
+    gen = _generator(dev, seed)
     std = cfg.init_std
     H, Ht = cfg.hidden_size, cfg.target_hidden_size
     w: Dict[str, torch.Tensor] = {}
@@ -135,7 +141,10 @@ def init_draft(cfg: DraftConfig, *, device="cpu", dtype=torch.float32, seed: int
         # d2t: draft id -> target id (the first draft_vocab_size target ids, strided over the vocabulary)
         stride = cfg.vocab_size // cfg.draft_vocab_size
         w["d2t"] = (torch.arange(cfg.draft_vocab_size, device=dev) * stride).long()
-    if cfg.low_rank:
+    if cfg.low_rank and dev.type == "meta":
+        w["lr_down"] = torch.empty(cfg.rank, H, device=dev, dtype=dtype)
+        w["lr_scores"] = torch.empty(cfg.draft_vocab_size, cfg.rank, device=dev, dtype=dtype)
+    elif cfg.low_rank:
         down, scores = low_rank_factors(w["lm_head"], cfg.rank, seed=seed)
         w["lr_down"] = down.to(dtype)
         w["lr_scores"] = scores.to(dtype)

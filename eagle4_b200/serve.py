@@ -408,6 +408,8 @@ def main(argv: Optional[List[str]] = None) -> int:
     ap.add_argument("--seed", type=int, default=0, help="sampling seed")
     ap.add_argument("--tree", default="12,4,16", help="steps,top_k,draft_tokens: the largest tree a round may draft")
     ap.add_argument("--round-log", help="append one JSON line per served round to this file (rank 0)")
+    ap.add_argument("--kv-tokens", type=int, help="KV cache positions shared by the running requests (default: "
+                                                 "every row at --max-len; `eagle4-b200 plan` gives what fits)")
     args = ap.parse_args(argv)
 
     from eagle4_b200.api import TreeSpec
@@ -429,7 +431,7 @@ def main(argv: Optional[List[str]] = None) -> int:
         lockstep = Lockstep()
     llm = build_llm(args.model, args.draft, max_batch=args.max_batch, max_len=args.max_len,
                     tree=TreeSpec(*(int(v) for v in args.tree.split(","))), config=args.config, tp=tp,
-                    temperature=args.temperature, seed=args.seed)
+                    temperature=args.temperature, seed=args.seed, kv_tokens=args.kv_tokens)
     if tp is not None:  # a dead or stalled rank is named by the heartbeat before the next round's collectives
         from eagle4_b200.parallel.health import process_group_heartbeat
 

@@ -317,3 +317,36 @@ def test_streamed_completions_and_chat():
         assert "".join(e["choices"][0]["delta"].get("content", "") for e in ev[:-1]) == cmp["choices"][0]["text"]
     finally:
         b.close(timeout=60)
+
+
+def test_memory_plan_matches_the_engine_allocations(capsys):
+    from eagle4_b200.api import NAMED, LLM, TreeSpec
+    from eagle4_b200.runtime.memory import plan
+
+    tcfg = NAMED["tiny"][0]()
+    dcfg = NAMED["tiny"][1](tcfg)
+    llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_batch=3, max_len=200,
+                        kv_tokens=1024)
+    eng = llm.engine
+
+    def nbytes(ts):
+        seen, n = set(), 0
+        for t in ts:
+            if torch.is_tensor(t) and id(t) not in seen:
+                seen.add(id(t))
+                n += t.numel() * t.element_size()
+        return n
+
+    p = plan(tcfg, dcfg, max_batch=3, max_len=200, kv_tokens=1024, tree=(4, 2, 8), dtype=torch.float32,
+             reserve_gb=0)
+    assert p.state_bytes == nbytes(eng.tcache.conv + eng.tcache.ssm)
+    slots = eng.tcache.k[0].shape[0]
+    kv = nbytes(eng.tcache.k + eng.tcache.v) + nbytes([eng.dcache.k, eng.dcache.v])
+    assert p.kv_bytes_per_token * slots == kv
+    model_w = nbytes(list(llm.target.w.values()) + list(llm.draft.w.values()))
+    assert abs(p.weights - model_w) <= 0.02 * model_w  # the engine may fold norms into projection copies
+    assert p.kv_tokens_within(p.weights + p.state_bytes + 10 * p.kv_bytes_per_token * 1024) == 10 * 1024
+    assert cli.main(["plan", "--model", "qwen3.8-27b", "--max-batch", "64", "--max-len", "8192"]) == 0
+    out = json.loads(capsys.readouterr().out)
+    assert out["fits"] and 50 < out["weights"] < 60 and out["max_kv_tokens"] > out["kv_tokens"]
+    assert cli.main(["plan", "--model", "qwen3.8-27b", "--max-batch", "512", "--max-len", "32768"]) == 1
