@@ -97,6 +97,37 @@ class LLM:
         out = self.engine.generate(dev_ids, max_new_tokens, speculative=speculative)
         return torch.tensor(out, dtype=torch.int64)
 
+    def complete(self, prompts, tokenizer=None, *, max_new_tokens: int = 128, stop=(), stop_token_ids=(),
+                 ignore_eos: bool = False, speculative: bool = True) -> list:
+        """Continuous-batching generation of many requests, each ending on its own stop condition.
+
+        ``prompts``: texts (with ``tokenizer``, a Hugging Face tokenizer) or token-id lists; more prompts than
+        ``max_batch`` queue and join the batch as rows free up. Returns one dict per prompt, in order:
+        ``token_ids``, ``finish_reason`` (``length`` / ``stop`` / ``eos``) and, with a tokenizer, ``text`` (cut
+        before the first stop string that ended it)."""
+        from eagle4_b200.runtime.scheduler import RequestParams, Scheduler
+
+        stop = (stop,) if isinstance(stop, str) else tuple(stop)
+        if (stop or any(isinstance(p, str) for p in prompts)) and tokenizer is None:
+            raise ValueError("text prompts and stop strings need a tokenizer")
+        detok = (lambda ids: tokenizer.decode(ids)) if tokenizer is not None else None
+        eos = getattr(tokenizer, "eos_token_id", None) if tokenizer is not None else None
+        params = RequestParams(max_new_tokens=max_new_tokens, stop_token_ids=tuple(stop_token_ids), eos_token_id=eos,
+                               ignore_eos=ignore_eos, stop=stop)
+        sched = Scheduler(self.engine, speculative=speculative, detokenize=detok)
+        reqs = [sched.submit(list(tokenizer(p)["input_ids"]) if isinstance(p, str) else list(p), params)
+                for p in prompts]
+        sched.run()
+        out = []
+        for r in reqs:
+            row = {"token_ids": list(r.output), "finish_reason": r.finish_reason}
+            if tokenizer is not None:
+                text = tokenizer.decode(r.output)
+                cuts = [i for i in (text.find(x) for x in stop) if i >= 0] if r.finish_reason == "stop" else []
+                row["text"] = text[:min(cuts)] if cuts else text
+            out.append(row)
+        return out
+
 
 def _with_packaged_profile(config: Optional[HarnessConfig], target: TargetModel,
                            draft: Optional[DraftModel]) -> Optional[HarnessConfig]:

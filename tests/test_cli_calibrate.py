@@ -8,6 +8,7 @@ import torch
 
 from eagle4_b200 import cli, compat
 from eagle4_b200.plugins import contract
+from tests.helpers import word_tokenizer
 
 
 def test_cli_dry_run(capsys, tmp_path):
@@ -199,17 +200,6 @@ def test_tensor_parallel_calibration_rank0_writes_every_rank_checks(tmp_path):
     assert 1 in load_cost_tables(os.path.join(tmp_path, "cost"))
 
 
-def _word_tokenizer(vocab: int):
-    """A tokenizer whose every id is one whitespace-separated word ``<i>`` (no word is part of another)."""
-    from tokenizers import Tokenizer, decoders, models, pre_tokenizers
-    from transformers import PreTrainedTokenizerFast
-
-    tok = Tokenizer(models.WordLevel({f"<{i}>": i for i in range(vocab)}, unk_token="<0>"))
-    tok.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
-    tok.decoder = decoders.WordPiece(prefix="##", cleanup=False)
-    return PreTrainedTokenizerFast(tokenizer_object=tok, unk_token="<0>", eos_token="<1>")
-
-
 def test_completions_text_stop_strings_and_metrics():
     from fastapi.testclient import TestClient
 
@@ -217,7 +207,7 @@ def test_completions_text_stop_strings_and_metrics():
     from eagle4_b200.serve import Batcher, make_app
 
     llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_batch=2, max_len=256)
-    tok = _word_tokenizer(4096)
+    tok = word_tokenizer(4096)
     prompt_ids = list(range(5, 25))
     plain = llm.generate([torch.tensor(prompt_ids)], 8, speculative=False)[0].tolist()
     b = Batcher(llm.engine, detokenize=lambda ids: tok.decode(ids))
@@ -280,7 +270,7 @@ def test_streamed_completions_and_chat():
     from eagle4_b200.serve import Batcher, make_app
 
     llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_batch=2, max_len=256)
-    tok = _word_tokenizer(4096)
+    tok = word_tokenizer(4096)
     tok.chat_template = ("{% for m in messages %}<{{ loop.index + 10 }}> {{ m['content'] }} {% endfor %}"
                          "{% if add_generation_prompt %}<9>{% endif %}")
     prompt_ids = list(range(30, 45))

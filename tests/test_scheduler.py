@@ -108,3 +108,23 @@ def test_padded_bucket_rounds_match():
     reqs = [sched.submit(p, RequestParams(max_new_tokens=4)) for p in prompts]
     sched.run()
     assert [r.output for r in reqs] == alone
+
+
+def test_llm_complete_texts_with_stops():
+    from tests.helpers import word_tokenizer
+
+    llm = _llm(max_batch=2)
+    tok = word_tokenizer(4096)
+    prompts = _prompts(3)
+    alone = [_alone(llm, p, 6, False) for p in prompts]
+    texts = [" ".join(f"<{i}>" for i in p.tolist()) for p in prompts]
+    out = llm.complete(texts, tok, max_new_tokens=6, ignore_eos=True)
+    assert [o["token_ids"] for o in out] == alone and all(o["finish_reason"] == "length" for o in out)
+    stop = f"<{alone[1][2]}>"
+    out = llm.complete([texts[1]], tok, max_new_tokens=6, stop=stop, ignore_eos=True)[0]
+    assert out["finish_reason"] == "stop" and stop not in out["text"]
+    assert out["token_ids"] == alone[1][:alone[1].index(alone[1][2]) + 1]
+    ids = llm.complete([p.tolist() for p in prompts], max_new_tokens=4)
+    assert [o["token_ids"] for o in ids] == [a[:4] for a in alone] and "text" not in ids[0]
+    with pytest.raises(ValueError):
+        llm.complete(["text"], max_new_tokens=2)
