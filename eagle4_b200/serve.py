@@ -68,14 +68,20 @@ except ImportError:  # the HTTP layer is optional; Batcher works without it
     GenerateRequest = CompletionRequest = ChatRequest = None
 
 
+class QueueFull(RuntimeError):
+    """The server's queue is at its limit (HTTP 503)."""
+
+
 class Batcher:
     """The serving loop: submitted requests enter the scheduler between rounds; each caller's future resolves
     when its request finishes. With ``lockstep`` (tensor-parallel serving, rank 0) every step's submissions are
     first broadcast to the other ranks, which mirror them (:func:`eagle4_b200.runtime.lockstep.follow`)."""
 
     def __init__(self, engine, max_batch: Optional[int] = None, *, speculative: bool = True, lockstep=None,
-                 detokenize: Optional[Callable[[List[int]], str]] = None):
-        """``detokenize``: token ids -> text, for requests with stop strings (every rank needs the same one)."""
+                 detokenize: Optional[Callable[[List[int]], str]] = None, max_queue: Optional[int] = None):
+        """``detokenize``: token ids -> text, for requests with stop strings (every rank needs the same one).
+        ``max_queue``: requests waiting beyond the running batch above which new ones are refused (``QueueFull``)."""
+        self.max_queue = max_queue
         self.engine = engine
         self.detokenize = detokenize
         self.sched = Scheduler(engine, speculative=speculative, detokenize=detokenize)
@@ -94,13 +100,24 @@ class Batcher:
         """Queue a request; the future resolves with the finished request. ``stream``: a queue that receives each
         round's new tokens (a list) as they are emitted, then ``None`` when the request ends."""
         fut: Future = Future()
+        refusal = None
         if self.failed is not None:
-            fut.set_exception(RuntimeError(f"serving stopped after an engine error: {self.failed}"))
+            refusal = RuntimeError(f"serving stopped after an engine error: {self.failed}")
+        elif self.max_queue is not None and self.queued >= self.max_queue:
+            refusal = QueueFull(f"{self.queued} requests are waiting (the limit is {self.max_queue}); retry later")
+        if refusal is not None:
+            self.counts["refused"] += 1
+            fut.set_exception(refusal)
             if stream is not None:
                 stream.put(None)
             return fut
         self.q.put((prompt, params, fut, stream))
         return fut
+
+    @property
+    def queued(self) -> int:
+        """Requests submitted and not yet running."""
+        return self.q.qsize() + len(self.sched.waiting)
 
     def close(self, timeout: Optional[float] = None) -> None:
         """Stop serving (followers are told to stop too); requests still queued are not run."""
@@ -247,6 +264,12 @@ def make_app(batcher: Batcher, tokenizer=None, model_name: str = "eagle4_b200"):
             return batcher.submit(prompt_ids, params).result()
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
+        except QueueFull as e:
+            raise HTTPException(503, str(e)) from e
+
+    @app.get("/v1/models")
+    def models():
+        return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "eagle4_b200"}]}
 
     @app.post("/v1/generate")
     def generate(req: GenerateRequest):
@@ -299,6 +322,9 @@ def make_app(batcher: Batcher, tokenizer=None, model_name: str = "eagle4_b200"):
 
         stream: "q_.Queue" = q_.Queue()
         fut = batcher.submit(ids, params, stream=stream)
+        if fut.done() and fut.exception() is not None:  # refused at submission: an HTTP error, not a stream
+            e = fut.exception()
+            raise HTTPException(503 if isinstance(e, QueueFull) else 400, str(e))
 
         def events():
             tokens, shown = [], ""
@@ -365,7 +391,7 @@ def make_app(batcher: Batcher, tokenizer=None, model_name: str = "eagle4_b200"):
     def health():
         st = batcher.engine.stats
         tp = batcher.engine.target.tp
-        return {"queued": batcher.q.qsize() + len(batcher.sched.waiting), "running": len(batcher.sched.running),
+        return {"queued": batcher.queued, "running": len(batcher.sched.running),
                 "rounds": st.rounds, "mean_accept": st.mean_accept, "tensor_parallel": tp.world if tp else 1,
                 "failed": None if batcher.failed is None else str(batcher.failed)}
 
@@ -408,6 +434,7 @@ def main(argv: Optional[List[str]] = None) -> int:
     ap.add_argument("--seed", type=int, default=0, help="sampling seed")
     ap.add_argument("--tree", default="12,4,16", help="steps,top_k,draft_tokens: the largest tree a round may draft")
     ap.add_argument("--round-log", help="append one JSON line per served round to this file (rank 0)")
+    ap.add_argument("--max-queue", type=int, help="waiting requests above which new ones get HTTP 503")
     ap.add_argument("--kv-tokens", type=int, help="KV cache positions shared by the running requests (default: "
                                                  "every row at --max-len; `eagle4-b200 plan` gives what fits)")
     args = ap.parse_args(argv)
@@ -454,7 +481,8 @@ def main(argv: Optional[List[str]] = None) -> int:
             from eagle4_b200.runtime.recorder import RoundRecorder
 
             llm.engine.recorder = RoundRecorder(args.round_log)
-        batcher = Batcher(llm.engine, speculative=speculative, lockstep=lockstep, detokenize=detokenize)
+        batcher = Batcher(llm.engine, speculative=speculative, lockstep=lockstep, detokenize=detokenize,
+                          max_queue=args.max_queue)
         try:
             uvicorn.run(make_app(batcher, tokenizer, os.path.basename(os.path.normpath(args.model))),
                         host=args.host, port=args.port)

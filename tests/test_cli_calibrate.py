@@ -340,3 +340,37 @@ def test_memory_plan_matches_the_engine_allocations(capsys):
     out = json.loads(capsys.readouterr().out)
     assert out["fits"] and 50 < out["weights"] < 60 and out["max_kv_tokens"] > out["kv_tokens"]
     assert cli.main(["plan", "--model", "qwen3.8-27b", "--max-batch", "512", "--max-len", "32768"]) == 1
+
+
+def test_queue_limit_and_models_endpoint():
+    from fastapi.testclient import TestClient
+
+    from eagle4_b200.api import LLM, TreeSpec
+    from eagle4_b200.runtime.scheduler import RequestParams
+    from eagle4_b200.serve import Batcher, QueueFull, make_app
+
+    llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_batch=1, max_len=256)
+    b = Batcher(llm.engine, max_queue=0)
+    try:
+        client = TestClient(make_app(b, None, "tiny"))
+        assert client.get("/v1/models").json()["data"][0]["id"] == "tiny"
+        r = client.post("/v1/completions", json={"prompt": [3, 4, 5], "max_tokens": 2})
+        assert r.status_code == 503
+        with client.stream("POST", "/v1/completions", json={"prompt": [3, 4], "max_tokens": 2, "stream": True}) as s:
+            assert s.status_code == 503
+        assert b.counts["refused"] == 2
+    finally:
+        b.close(timeout=60)
+    # a burst larger than the queue: some run, the rest are refused, none is lost
+    b = Batcher(llm.engine, max_queue=1)
+    try:
+        futs = [b.submit([5, 6, 7], RequestParams(max_new_tokens=3)) for _ in range(6)]
+        results = []
+        for f in futs:
+            try:
+                results.append(len(f.result(timeout=120).output))
+            except QueueFull:
+                results.append("full")
+        assert results.count(3) >= 1 and all(r in (3, "full") for r in results)
+    finally:
+        b.close(timeout=60)
