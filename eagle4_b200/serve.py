@@ -54,6 +54,7 @@ try:
         temperature: Optional[float] = None
         model: Optional[str] = None
         stream: bool = False
+        n: int = 1
 
     class ChatRequest(BaseModel):
         messages: List[dict]
@@ -64,6 +65,7 @@ try:
         temperature: Optional[float] = None
         model: Optional[str] = None
         stream: bool = False
+        n: int = 1
 except ImportError:  # the HTTP layer is optional; Batcher works without it
     GenerateRequest = CompletionRequest = ChatRequest = None
 
@@ -259,9 +261,13 @@ def make_app(batcher: Batcher, tokenizer=None, model_name: str = "eagle4_b200"):
 
     app = FastAPI(title="eagle4_b200")
 
-    def run(prompt_ids, params):
+    def run(prompt_ids, params, n: int = 1):
+        """``n`` independent requests of one prompt (they share rounds); their finished requests in order."""
+        if not 1 <= n <= 64:
+            raise HTTPException(400, "n must be in 1..64")
+        futs = [batcher.submit(prompt_ids, params) for _ in range(n)]
         try:
-            return batcher.submit(prompt_ids, params).result()
+            return [f.result() for f in futs]
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
         except QueueFull as e:
@@ -277,7 +283,7 @@ def make_app(batcher: Batcher, tokenizer=None, model_name: str = "eagle4_b200"):
             raise HTTPException(400, "prompt_ids must be non-empty and max_new_tokens positive")
         params = RequestParams(max_new_tokens=req.max_new_tokens, stop_token_ids=tuple(req.stop_token_ids),
                                eos_token_id=req.eos_token_id, ignore_eos=req.ignore_eos)
-        r = run(req.prompt_ids, params)
+        r = run(req.prompt_ids, params)[0]
         return {"output_ids": r.output, "finish_reason": r.finish_reason,
                 "meta": {"rounds": r.rounds, "speculative": batcher.sched.speculative}}
 
@@ -363,12 +369,14 @@ def make_app(batcher: Batcher, tokenizer=None, model_name: str = "eagle4_b200"):
         params = params_of(req, ids)
         head = {"object": "text_completion", "created": int(time.time()), "model": req.model or model_name}
         if req.stream:
+            if req.n != 1:
+                raise HTTPException(400, "streamed completions take n = 1")
             return sse(ids, params, lambda delta, new, fin: dict(head, id="cmpl-stream", choices=[
                 {"index": 0, "text": delta, "token_ids": new, "finish_reason": fin}]))
-        r = run(ids, params)
-        return dict(head, id=f"cmpl-{r.rid}", choices=[{"index": 0, "text": text_of(r.output, params, True),
-                                                         "token_ids": r.output, "finish_reason": finish_of(r)}],
-                    usage=usage(len(ids), len(r.output)))
+        rs = run(ids, params, req.n)
+        return dict(head, id=f"cmpl-{rs[0].rid}", choices=[
+            {"index": i, "text": text_of(r.output, params, True), "token_ids": r.output, "finish_reason": finish_of(r)}
+            for i, r in enumerate(rs)], usage=usage(len(ids), sum(len(r.output) for r in rs)))
 
     @app.post("/v1/chat/completions")
     def chat(req: ChatRequest):
@@ -379,13 +387,16 @@ def make_app(batcher: Batcher, tokenizer=None, model_name: str = "eagle4_b200"):
         params = params_of(req, ids)
         head = {"created": int(time.time()), "model": req.model or model_name}
         if req.stream:
+            if req.n != 1:
+                raise HTTPException(400, "streamed completions take n = 1")
             return sse(ids, params, lambda delta, new, fin: dict(head, id="chatcmpl-stream",
                                                                  object="chat.completion.chunk", choices=[
                 {"index": 0, "delta": {"content": delta} if delta else {}, "finish_reason": fin}]))
-        r = run(ids, params)
-        return dict(head, id=f"chatcmpl-{r.rid}", object="chat.completion", choices=[
-            {"index": 0, "message": {"role": "assistant", "content": text_of(r.output, params, True)},
-             "finish_reason": finish_of(r)}], usage=usage(len(ids), len(r.output)))
+        rs = run(ids, params, req.n)
+        return dict(head, id=f"chatcmpl-{rs[0].rid}", object="chat.completion", choices=[
+            {"index": i, "message": {"role": "assistant", "content": text_of(r.output, params, True)},
+             "finish_reason": finish_of(r)} for i, r in enumerate(rs)],
+            usage=usage(len(ids), sum(len(r.output) for r in rs)))
 
     @app.get("/health")
     def health():

@@ -374,3 +374,25 @@ def test_queue_limit_and_models_endpoint():
         assert results.count(3) >= 1 and all(r in (3, "full") for r in results)
     finally:
         b.close(timeout=60)
+
+
+def test_n_choices_sample_independently():
+    from fastapi.testclient import TestClient
+
+    from eagle4_b200.api import LLM, TreeSpec
+    from eagle4_b200.serve import Batcher, make_app
+
+    llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_batch=4, max_len=256,
+                        temperature=0.05, sample_seed=3)
+    b = Batcher(llm.engine)
+    try:
+        client = TestClient(make_app(b, None, "tiny"))
+        r = client.post("/v1/completions", json={"prompt": list(range(5, 17)), "max_tokens": 6, "n": 4}).json()
+        assert [c["index"] for c in r["choices"]] == [0, 1, 2, 3]
+        outs = [tuple(c["token_ids"]) for c in r["choices"]]
+        assert all(len(o) == 6 for o in outs) and len(set(outs)) > 1  # independent draws
+        assert r["usage"]["completion_tokens"] == 24
+        bad = client.post("/v1/completions", json={"prompt": [5, 6], "max_tokens": 2, "n": 2, "stream": True})
+        assert bad.status_code == 400
+    finally:
+        b.close(timeout=60)
