@@ -52,8 +52,10 @@ def test_aux_and_head_checks():
 
 
 def test_reference_profile_config_parses():
-    path = "/root/reference/eagle_harness/core/profiles/mi355x-qwen3.8-27b-tp1/draft_config.json"
+    """The draft config shipped with the reference's profiles (the package installed under ``baseline/_ref``)."""
+    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    path = os.path.join(root, "eagle_harness", "core", "profiles", "mi355x-qwen3.8-27b-tp1", "draft_config.json")
     if not os.path.exists(path):
-        pytest.skip("reference profile not present")
+        pytest.skip("the reference package is not installed under baseline/_ref")
     dc = draft_config_from_hf(json.load(open(path)))
     assert dc.hidden_size == 5120 and dc.sliding_window == 4096
