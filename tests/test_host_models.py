@@ -274,3 +274,24 @@ def test_tokenspeed_candidate_head_over_two_vocab_shards():
     assert res[0]["ids_ok"] and res[1]["ids_ok"]
     assert res[0]["ids"] == res[1]["ids"] and res[0]["probs"] == res[1]["probs"]
     assert res[0]["rows"] == (0, V // 2) and res[1]["rows"] == (V // 2, V // 2)
+
+
+def test_sglang_model_shares_the_embedding_and_answers_the_worker():
+    from eagle4_b200.plugins.sglang.models.llama_eagle4 import LlamaForCausalLMEagle4
+
+    dc, w = _draft()
+    model = LlamaForCausalLMEagle4(dc.to_hf())
+    embed = w["embed"].clone()
+    model.set_embed_and_head(embed, torch.zeros(1))  # the head argument is not taken
+    model.load_weights(weights.draft_state_dict(dc, w).items())
+    assert model.draft.w["embed"] is embed and model.draft.w["lm_head"].shape[0] == V
+    assert model.get_hot_token_id() is None
+    assert model.get_attention_sliding_window_size() == (dc.sliding_window - 1 if dc.sliding_window else None)
+    normed = torch.randn(4, dc.hidden_size, generator=torch.Generator().manual_seed(9))
+    probs, ids = model.candidate_topk(normed, 3)
+    p2, i2 = DraftModel(dc, w).candidates(normed, 3)
+    assert torch.equal(ids, i2) and torch.allclose(probs, p2)
+    cand = model.proposal_candidates(normed)
+    assert cand.logits.shape == (4, dc.num_candidates) and cand.token_ids.dtype == torch.int64
+    full = cl.scatter_to_vocab(cand, V)
+    assert torch.equal(torch.topk(full, 3).indices, i2)
