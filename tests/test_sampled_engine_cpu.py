@@ -62,3 +62,21 @@ def test_sampled_engine_runs_on_cpu():
     plain = llm.generate(prompt, 10, speculative=False)
     assert spec.shape == (1, 10) and plain.shape == (1, 10)
     assert int(llm.engine.round_ctr[0]) > 0
+
+
+def test_second_run_same_bits():
+    """Two fresh engines with the same weights and seed emit the same tokens, greedy and sampled, speculative and
+    plain; another sampling seed draws other tokens."""
+    from eagle4_b200.api import LLM, TreeSpec
+
+    prompt = torch.randint(0, 4096, (2, 20), generator=torch.Generator().manual_seed(1))
+
+    def run(temperature, seed, speculative):
+        llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_batch=2,
+                            max_len=256, temperature=temperature, sample_seed=seed)
+        return llm.generate(prompt, 12, speculative=speculative)
+
+    for temperature in (0.0, 0.05):
+        for speculative in (True, False):
+            assert torch.equal(run(temperature, 3, speculative), run(temperature, 3, speculative))
+    assert not torch.equal(run(0.05, 3, True), run(0.05, 4, True))
