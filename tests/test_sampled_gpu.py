@@ -154,3 +154,22 @@ def test_vocab_parallel_kernels_match_the_full_walk():
             agree += int(scnt[b]) == int(cnt[b]) and int(tok[b]) == int(bonus[b]) and torch.equal(
                 sacc[b, :int(scnt[b])], acc[b, :int(cnt[b])])
     assert agree / total >= 0.95, agree / total
+
+
+def test_second_run_same_bits_on_gpu():
+    """Fresh engines with the same weights and sampling seed emit the same tokens on the GPU (greedy and sampled)."""
+    from eagle4_b200.api import LLM, TreeSpec
+    from eagle4_b200.ops import native
+
+    prompt = torch.randint(0, 4096, (2, 24), generator=torch.Generator().manual_seed(2))
+
+    def run(temperature):
+        llm = LLM.synthetic("tiny", device="cuda", tree=TreeSpec(4, 2, 8), max_batch=2, max_len=256,
+                            temperature=temperature, sample_seed=5)
+        out = llm.generate(prompt, 12)
+        del llm
+        return out
+
+    for temperature in (0.0, 1.0):
+        assert torch.equal(run(temperature), run(temperature))
+    native.check_errors()
