@@ -242,6 +242,47 @@ def _plan(args) -> int:
     return 0 if summary["fits"] else 1
 
 
+def calibration_report(data: Path, max_verify_width: int = 16, target_is_moe: bool = False) -> dict:
+    """What a calibration directory holds and what serve mode would take from it."""
+    from eagle4_b200.core.chain_width import chain_widths, load_accept_profile, load_round_times, load_tree_rounds
+    from eagle4_b200.core.chain_width import served_tree_schedule
+    from eagle4_b200.core.cost_table import cost_model_problem, load_cost_tables
+    from eagle4_b200.core.limits import ComputeIntensity, max_batch_size
+    from eagle4_b200.core.live_costs import read_key
+
+    data = Path(data)
+    if not data.is_dir():
+        raise OSError(f"{data} is not a directory")
+    key = read_key(str(data))
+    out: dict = {"data_path": str(data), "key": key.to_dict() if key else None}
+    tables = load_cost_tables(str(data / "cost")) if (data / "cost").is_dir() else {}
+    out["cost_tables"] = {
+        str(b): {"contexts": [t.cache_length_start, t.cache_length_start + t.cache_length_step * t.max_interval_id],
+                 "intervals": len(t.intervals), "problem": cost_model_problem(t, target_is_moe=target_is_moe)}
+        for b, t in sorted(tables.items())}
+    limit = max_batch_size(ComputeIntensity.CHAIN)
+    profile = load_accept_profile(str(data))
+    out["accept_profile"] = None if profile is None else {
+        "max_width": profile.max_width, "expected_tokens": {w: round(profile.expected_tokens(w), 3)
+                                                            for w in range(1, profile.max_width + 1)}}
+    out["chain_round_times"] = sorted(load_round_times(str(data)) or {})
+    out["chain_schedule"] = chain_widths(str(data), max_verify_width, limit, allow_no_spec=True) \
+        if profile is not None else None
+    rounds = load_tree_rounds(str(data))
+    out["tree_rounds"] = sorted(rounds) if rounds else []
+    out["tree_schedule"] = served_tree_schedule(rounds, max_verify_width, max_batch_size(ComputeIntensity.HIGH)) \
+        if rounds else None
+    out["profile"] = (data / "profile.json").is_file()
+    return out
+
+
+def _report_dir(args) -> int:
+    rep = calibration_report(args.data, args.max_verify_width, args.moe_target)
+    print(json.dumps(rep, indent=2))
+    bad = [b for b, t in rep["cost_tables"].items() if t["problem"]]
+    return 1 if bad else 0
+
+
 def main(argv: Optional[List[str]] = None) -> int:
     ap = argparse.ArgumentParser(prog="eagle4-b200", description="EAGLE-4 speculative decoding on B200.")
     sub = ap.add_subparsers(dest="command", required=True)
@@ -279,6 +320,12 @@ def main(argv: Optional[List[str]] = None) -> int:
     pl.add_argument("--gpu-gb", type=float, help="memory budget per GPU in GB (default: a B200's)")
     pl.add_argument("--reserve-gb", type=float, default=4.0, help="activations, graph pools, buffers, context")
     pl.set_defaults(func=_plan)
+    rep = sub.add_parser("report", formatter_class=argparse.ArgumentDefaultsHelpFormatter,
+                         help="summarise a calibration directory: setup, tables, schedules, cost-model checks")
+    rep.add_argument("data", type=Path, help="calibration directory (data_path)")
+    rep.add_argument("--max-verify-width", type=_positive, default=16)
+    rep.add_argument("--moe-target", action="store_true", help="check the tables as for a mixture-of-experts target")
+    rep.set_defaults(func=_report_dir)
     chk = sub.add_parser("check", help="report the serving hosts and the native library")
     chk.add_argument("--kernels", action="store_true", help="also load the native CUDA library")
     chk.set_defaults(func=lambda a: __import__("eagle4_b200.compat", fromlist=["main"]).main(

@@ -396,3 +396,25 @@ def test_n_choices_sample_independently():
         assert bad.status_code == 400
     finally:
         b.close(timeout=60)
+
+
+def test_calibration_report(tmp_path, capsys):
+    from eagle4_b200.api import LLM, TreeSpec
+    from eagle4_b200.core.chain_width import merge_tree_rounds
+    from eagle4_b200.core.live_costs import CostKey
+    from eagle4_b200.runtime.calibrate import calibrate
+
+    llm = LLM.synthetic("tiny", device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_len=512)
+    key = CostKey(gpu="cpu", gpu_count=1, model="tiny", draft="", engine="eagle4_b200", dtype="float32")
+    calibrate(llm.engine, str(tmp_path), batch_sizes=[1], context_step=64, context_stop=128, repeats=2, key=key,
+              progress=lambda s: None)
+    merge_tree_rounds(str(tmp_path), [{"batch_size": 1, "width": 8, "round_us": 9000.0, "accept": 2.0, "count": 9},
+                                      {"batch_size": 1, "width": 4, "round_us": 5000.0, "accept": 1.9, "count": 9}])
+    rep = cli.calibration_report(tmp_path, max_verify_width=8)
+    assert rep["key"]["model"] == "tiny" and set(rep["cost_tables"]) == {"1"}
+    assert rep["cost_tables"]["1"]["intervals"] >= 1 and rep["tree_rounds"] == [1]
+    assert rep["accept_profile"] is None and rep["chain_schedule"] is None
+    code = cli.main(["report", str(tmp_path), "--max-verify-width", "8"])
+    out = json.loads(capsys.readouterr().out)
+    assert out["data_path"] == str(tmp_path) and code in (0, 1)
+    assert cli.main(["report", str(tmp_path / "missing")]) == 1
