@@ -294,6 +294,60 @@ class Engine:
             self._draft_prefill(b, prompt, aux, first)
         return first, aux
 
+    def prefill_many(self, rows: List[int], prompts: List[torch.Tensor],
+                     reserve_tokens: Optional[List[int]] = None) -> List[torch.Tensor]:
+        """Several requests' prompts through the target in one scan-mode forward (each request its own segment of
+        contiguous rows; per-row attention, per-segment recurrences and row-independent GEMMs make every request's
+        result the one ``prefill`` gives it alone), then each request's first token and draft share as in
+        ``prefill``. ``rows``: the batch rows (their ``slot`` set). Returns the first tokens, in order."""
+        if len(rows) == 1:
+            return [self.prefill(rows[0], prompts[0], reserve_tokens[0] if reserve_tokens else None)[0]]
+        dev = self.device
+        lens = [int(p.shape[0]) for p in prompts]
+        slots_of = [int(self.slot[b]) for b in rows]
+        for i, slot in enumerate(slots_of):
+            self.pages.release(slot)
+            self.pages.reserve(slot, reserve_tokens[i] if reserve_tokens is not None else self.max_len)
+            self.tcache.reset_slot(slot)
+        pos = torch.cat([torch.arange(n, device=dev) for n in lens])
+        slot_rows = torch.cat([self._i32(n, s) for n, s in zip(lens, slots_of)])
+        starts = [0]
+        for n in lens:
+            starts.append(starts[-1] + n)
+        parent = torch.arange(starts[-1], device=dev, dtype=torch.int32) - 1
+        parent[torch.tensor(starts[:-1], device=dev)] = -1
+        t = starts[-1]
+        rb = RowBatch(ids=torch.cat([p.to(dev) for p in prompts]), pos=pos, req=slot_rows,
+                      write_slot=self._slots(slot_rows.long(), pos), ctx_start=self._i32(t, 0),
+                      ctx_len=(pos + 1).int(), extra=torch.zeros(t, 1, dtype=torch.int32, device=dev),
+                      n_extra=self._i32(t, 0), parent=parent, state_slot=slot_rows, scan=True, max_keys=max(lens),
+                      segments=torch.tensor(starts, dtype=torch.int32, device=dev))
+        out, aux = self.target.forward(rb, self.tcache)
+        last = torch.tensor([s - 1 for s in starts[1:]], device=dev)
+        firsts: List[torch.Tensor] = []
+        if self.sampled:  # one draw per request, in order, as ``prefill`` draws them
+            for i in range(len(rows)):
+                _, _, first = self.target.sampled_accept(
+                    out[last[i]:last[i] + 1], self.temperature,
+                    torch.full((1, 1), -1, dtype=torch.int32, device=dev), torch.zeros(1, 1, dtype=torch.int64,
+                                                                                      device=dev),
+                    torch.full((1, 1), -1, dtype=torch.int64, device=dev), self.plain_q[:1], self.plain_ids[:1],
+                    self.plain_slot[:1], 1, self.seed, self.round_ctr, SAMPLED_STREAM + 2)
+                ops.advance_round(self.round_ctr)
+                firsts.append(first.view(1))
+        else:
+            ids, _ = self.target.greedy(out.index_select(0, last))
+            firsts = [ids[i:i + 1] for i in range(len(rows))]
+        for i, b in enumerate(rows):
+            first = firsts[i]
+            self.L[b] = lens[i]
+            self.root[b] = first[0]
+            self.out_tok[b, 0] = first[0]
+            self.out_cnt[b] = 1
+            if self.draft is not None:
+                self._draft_prefill(b, prompts[i], aux[starts[i]:starts[i + 1]], first)
+        return firsts
+
     def _draft_prefill(self, b: int, prompt: torch.Tensor, aux: torch.Tensor, first: torch.Tensor) -> None:
         """The draft's share of a prefill: the prompt's leading rows through the draft now (their draft KV), the last
         ``N`` rows (tokens shifted by one, with their aux hidden states) left pending for the first round's extend."""

@@ -3,7 +3,8 @@
 Under tensor parallelism every rank runs the same engine rounds over its weight shard, so every rank must admit the
 same requests in the same order and step the same rounds. Rank 0 owns the request queue (the HTTP front end); before
 each step it broadcasts one :class:`Command` (the requests submitted since the last step, or stop) over a separate
-gloo group, and every other rank applies it to its own :class:`~eagle4_b200.runtime.scheduler.Scheduler` (:func:`follow`).
+gloo group, and every other rank applies it to its own
+:class:`~eagle4_b200.runtime.scheduler.Scheduler` (:func:`follow`).
 The schedulers then stay identical without further messages: admission and retirement depend only on the submitted
 requests and the emitted tokens, which every rank computes alike (the greedy head's argmax is exchanged between
 ranks), and the engine's timing-based round choices take the maximum over ranks before deciding.
@@ -68,12 +69,14 @@ def apply(sched: Scheduler, cmd: Command) -> List[Union[Request, ValueError]]:
     return out
 
 
-def follow(engine, lockstep: Lockstep, *, speculative: bool = True, detokenize=None) -> int:
+def follow(engine, lockstep: Lockstep, *, speculative: bool = True, detokenize=None,
+           batch_prefill: bool = False) -> int:
     """A non-leader rank's serving loop: apply each command, step while requests run, return on stop.
-    ``detokenize`` must be the leader's (stop strings end requests on every rank alike)."""
+    ``detokenize`` and ``batch_prefill`` must be the leader's (stop strings end requests, and prefills group, on
+    every rank alike)."""
     if lockstep.leader:
         raise ValueError("rank 0 leads; follow() runs on the other ranks")
-    sched = Scheduler(engine, speculative=speculative, detokenize=detokenize)
+    sched = Scheduler(engine, speculative=speculative, detokenize=detokenize, batch_prefill=batch_prefill)
     rounds = 0
     while True:
         cmd = lockstep.exchange()

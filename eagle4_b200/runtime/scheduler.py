@@ -65,9 +65,13 @@ class Request:
 
 
 class Scheduler:
-    def __init__(self, engine, *, speculative: bool = True, detokenize: Optional[Callable[[List[int]], str]] = None):
-        """``detokenize``: token ids -> text, needed only for requests with stop strings."""
+    def __init__(self, engine, *, speculative: bool = True, detokenize: Optional[Callable[[List[int]], str]] = None,
+                 batch_prefill: bool = False, prefill_tokens: int = 8192):
+        """``detokenize``: token ids -> text, needed only for requests with stop strings. ``batch_prefill``: the
+        requests admitted in one step prefill together, in groups of up to ``prefill_tokens`` prompt tokens (one
+        target forward per group instead of one per request; the results are each request's alone)."""
         self.engine = engine
+        self.batch_prefill, self.prefill_tokens = batch_prefill, prefill_tokens
         self.speculative = speculative
         self.detokenize = detokenize
         self.waiting: Deque[Request] = deque()
@@ -93,6 +97,19 @@ class Scheduler:
         self.waiting.append(req)
         return req
 
+    def _started(self, req: Request, b: int, done: List[Request]) -> None:
+        """A prefilled request joins the running batch at row ``b`` with its first token."""
+        self.running.append(req)
+        self.ctx.append(int(req.prompt.numel()))
+        if self._take(req, [int(self.engine.out_tok[b, 0])]):
+            done.append(req)
+
+    def _prefill_group(self, group: List[tuple], done: List[Request]) -> None:
+        self.engine.prefill_many([b for b, _, _ in group], [r.prompt for _, r, _ in group],
+                                 [need for _, _, need in group])
+        for b, req, _ in group:
+            self._started(req, b, done)
+
     def _need(self, prompt: torch.Tensor, params: RequestParams) -> int:
         return int(prompt.numel()) + params.max_new_tokens + self.engine.span
 
@@ -101,24 +118,34 @@ class Scheduler:
         eng = self.engine
         done = []
         fresh = not self.running
+        group: List[tuple] = []  # (row, request, need) admitted and waiting for a batched prefill
+        planned = 0  # pages the group will take
         while self.waiting and self.free_slots:
             req = self.waiting[0]
             need = self._need(req.prompt, req.params)
-            if eng.pages.pages_for(need) > eng.pages.free_pages:
-                if not self.running:
+            if eng.pages.pages_for(need) > eng.pages.free_pages - planned:
+                if not self.running and not group:
                     raise OutOfPages(f"request {req.rid} needs {eng.pages.pages_for(need)} pages; the pool has "
                                      f"{eng.pages.free_pages} with nothing running")
                 break
             self.waiting.popleft()
-            b = len(self.running)
+            b = len(self.running) + len(group)
             req.slot = self.free_slots.pop()
             eng.slot[b] = req.slot
-            eng.prefill(b, req.prompt, reserve_tokens=need)
-            first = int(eng.out_tok[b, 0])
-            self.running.append(req)
-            self.ctx.append(int(req.prompt.numel()))
-            if self._take(req, [first]):
-                done.append(req)
+            if not self.batch_prefill:
+                eng.prefill(b, req.prompt, reserve_tokens=need)
+                self._started(req, b, done)
+                continue
+            if group and sum(int(r.prompt.numel()) for _, r, _ in group) + int(req.prompt.numel()) > \
+                    self.prefill_tokens:
+                self._prefill_group(group, done)
+                group, planned = [], 0
+                b = len(self.running)
+                eng.slot[b] = req.slot
+            group.append((b, req, need))
+            planned += eng.pages.pages_for(need)
+        if group:
+            self._prefill_group(group, done)
         if done:
             self._retire(done)
         if fresh and eng.tree is not None:

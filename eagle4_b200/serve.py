@@ -80,13 +80,15 @@ class Batcher:
     first broadcast to the other ranks, which mirror them (:func:`eagle4_b200.runtime.lockstep.follow`)."""
 
     def __init__(self, engine, max_batch: Optional[int] = None, *, speculative: bool = True, lockstep=None,
-                 detokenize: Optional[Callable[[List[int]], str]] = None, max_queue: Optional[int] = None):
+                 detokenize: Optional[Callable[[List[int]], str]] = None, max_queue: Optional[int] = None,
+                 batch_prefill: bool = False):
         """``detokenize``: token ids -> text, for requests with stop strings (every rank needs the same one).
         ``max_queue``: requests waiting beyond the running batch above which new ones are refused (``QueueFull``)."""
         self.max_queue = max_queue
         self.engine = engine
         self.detokenize = detokenize
-        self.sched = Scheduler(engine, speculative=speculative, detokenize=detokenize)
+        self.batch_prefill = batch_prefill
+        self.sched = Scheduler(engine, speculative=speculative, detokenize=detokenize, batch_prefill=batch_prefill)
         self.lockstep = lockstep
         self.counts = {"requests": 0, "finished": 0, "refused": 0, "prompt_tokens": 0, "generated_tokens": 0}
         self.q: "queue.Queue" = queue.Queue()
@@ -202,7 +204,8 @@ class Batcher:
                     except Exception:  # noqa: BLE001 - the group may be gone already
                         pass
                     return
-                self.sched = Scheduler(self.engine, speculative=self.sched.speculative, detokenize=self.detokenize)
+                self.sched = Scheduler(self.engine, speculative=self.sched.speculative, detokenize=self.detokenize,
+                                       batch_prefill=self.batch_prefill)
                 continue
             self._publish()
             for req in finished:
@@ -441,11 +444,14 @@ def main(argv: Optional[List[str]] = None) -> int:
     ap.add_argument("--tokenizer", help="tokenizer directory for text prompts (default: the target directory, "
                                         "when it has one)")
     ap.add_argument("--temperature", type=float, default=0.0,
-                    help="0: greedy (equal to plain greedy decoding); > 0: every request sampled at it (tree rejection)")
+                    help="0: greedy (equal to plain greedy decoding); > 0: every request sampled at it "
+                         "(tree rejection)")
     ap.add_argument("--seed", type=int, default=0, help="sampling seed")
     ap.add_argument("--tree", default="12,4,16", help="steps,top_k,draft_tokens: the largest tree a round may draft")
     ap.add_argument("--round-log", help="append one JSON line per served round to this file (rank 0)")
     ap.add_argument("--max-queue", type=int, help="waiting requests above which new ones get HTTP 503")
+    ap.add_argument("--batch-prefill", action="store_true",
+                    help="requests admitted in one step prefill in one target forward (groups of up to 8192 tokens)")
     ap.add_argument("--kv-tokens", type=int, help="KV cache positions shared by the running requests (default: "
                                                  "every row at --max-len; `eagle4-b200 plan` gives what fits)")
     args = ap.parse_args(argv)
@@ -484,7 +490,8 @@ def main(argv: Optional[List[str]] = None) -> int:
         if lockstep is not None and not lockstep.leader:
             from eagle4_b200.runtime.lockstep import follow
 
-            follow(llm.engine, lockstep, speculative=speculative, detokenize=detokenize)
+            follow(llm.engine, lockstep, speculative=speculative, detokenize=detokenize,
+                   batch_prefill=args.batch_prefill)
             return 0
         import uvicorn
 
@@ -493,7 +500,7 @@ def main(argv: Optional[List[str]] = None) -> int:
 
             llm.engine.recorder = RoundRecorder(args.round_log)
         batcher = Batcher(llm.engine, speculative=speculative, lockstep=lockstep, detokenize=detokenize,
-                          max_queue=args.max_queue)
+                          max_queue=args.max_queue, batch_prefill=args.batch_prefill)
         try:
             uvicorn.run(make_app(batcher, tokenizer, os.path.basename(os.path.normpath(args.model))),
                         host=args.host, port=args.port)

@@ -128,3 +128,37 @@ def test_llm_complete_texts_with_stops():
     assert [o["token_ids"] for o in ids] == [a[:4] for a in alone] and "text" not in ids[0]
     with pytest.raises(ValueError):
         llm.complete(["text"], max_new_tokens=2)
+
+
+@pytest.mark.parametrize("temperature", [0.0, 0.05])
+def test_batched_prefill_gives_each_request_its_own_result(temperature):
+    """Admitted requests prefilled together (in groups bounded by a token budget) emit exactly what one-by-one
+    prefills emit: greedy, and sampled with the same seed."""
+    prompts = _prompts(5, seed=4)
+    lens = [6, 4, 7, 3, 5]
+
+    def serve(batch_prefill, budget=8192):
+        llm = _llm(max_batch=3, temperature=temperature, sample_seed=2)
+        sched = Scheduler(llm.engine, batch_prefill=batch_prefill, prefill_tokens=budget)
+        reqs = [sched.submit(p, RequestParams(max_new_tokens=n)) for p, n in zip(prompts, lens)]
+        sched.run()
+        return [r.output for r in reqs]
+
+    want = serve(False)
+    assert serve(True) == want
+    assert serve(True, budget=40) == want  # several groups per admission step
+
+
+def test_batched_prefill_engine_matches_single_prefills():
+    llm = _llm(max_batch=3)
+    eng = llm.engine
+    prompts = _prompts(3, seed=6)
+    one = []
+    for b, p in enumerate(prompts):
+        eng.slot[b] = b
+        one.append(int(eng.prefill(b, p)[0][0]))
+    state = [t.clone() for t in eng.tcache.ssm]
+    firsts = eng.prefill_many([0, 1, 2], prompts)
+    assert [int(f[0]) for f in firsts] == one
+    for a, b in zip(state, eng.tcache.ssm):
+        assert torch.allclose(a[:3], b[:3], atol=1e-6)

@@ -28,3 +28,33 @@ def test_continuous_batching_on_gpu_matches_alone(speculative):
     assert [r.output for r in reqs] == alone
     assert 9 in batches or any(b not in llm.engine.buckets for b in batches)  # a padded bucket was replayed
     native.check_errors(torch.device("cuda"))
+
+
+def test_batched_prefill_on_gpu_matches_single_prefills():
+    """Several prompts in one prefill forward: each request's recurrent state and attention cache end as its own
+    prefill leaves them (within bf16 rounding: a longer forward may take another GEMM partition)."""
+    from eagle4_b200.api import LLM, TreeSpec
+    from eagle4_b200.ops import native
+
+    llm = LLM.synthetic("tiny", device="cuda", tree=TreeSpec(4, 2, 8), max_batch=4, max_len=512)
+    eng = llm.engine
+    g = torch.Generator().manual_seed(11)
+    prompts = [torch.randint(1, 4096, (n,), generator=g) for n in (37, 120, 9, 64)]
+    for b in range(4):
+        eng.slot[b] = b
+    def keys():  # every request's K rows in position order (the pages may move between the two prefills)
+        return [[t[eng._slots(torch.tensor(b, device="cuda"), torch.arange(p.numel(), device="cuda"))].float()
+                 for b, p in enumerate(prompts)] for t in eng.tcache.k]
+
+    single = [int(eng.prefill(b, p)[0][0]) for b, p in enumerate(prompts)]
+    ssm = [t[:4].float().clone() for t in eng.tcache.ssm]
+    k = keys()
+    firsts = [int(f[0]) for f in eng.prefill_many([0, 1, 2, 3], prompts)]
+    torch.cuda.synchronize()
+    native.check_errors(torch.device("cuda"))
+    assert sum(a == b for a, b in zip(firsts, single)) >= 3  # a near tie may flip one first token
+    for a, b in zip(ssm, eng.tcache.ssm):
+        assert (a - b[:4].float()).abs().max() <= 2e-2 * (a.abs().max() + 1e-6)
+    for layer_a, layer_b in zip(k, keys()):
+        for a, b in zip(layer_a, layer_b):
+            assert (a - b).abs().max() <= 2e-2 * (a.abs().max() + 1e-6)

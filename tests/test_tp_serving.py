@@ -19,7 +19,7 @@ def _port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, speculative, out):
+def _worker(rank, world, port, speculative, out, batch_prefill=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     torch.set_num_threads(1)
@@ -40,7 +40,7 @@ def _worker(rank, world, port, speculative, out):
         alone = [llm.generate([p], n, speculative=False)[0].tolist() for p, n in zip(prompts, lens)]
         ls = Lockstep(timeout_s=30.0, beat_s=0.2)
         if rank == 0:
-            b = Batcher(llm.engine, speculative=speculative, lockstep=ls)
+            b = Batcher(llm.engine, speculative=speculative, lockstep=ls, batch_prefill=batch_prefill)
             futs = [b.submit(p.tolist(), RequestParams(max_new_tokens=n)) for p, n in zip(prompts, lens)]
             bad = b.submit([1] * 300, RequestParams(max_new_tokens=4))
             got = [f.result(timeout=600).output for f in futs]
@@ -56,7 +56,7 @@ def _worker(rank, world, port, speculative, out):
             out[rank] = {"got": got, "alone": alone, "refused": refused, "beats": beats,
                          "failed": b.failed is not None}
         else:
-            rounds = follow(llm.engine, ls, speculative=speculative)
+            rounds = follow(llm.engine, ls, speculative=speculative, batch_prefill=batch_prefill)
             out[rank] = {"rounds": rounds, "alone": alone}
     finally:
         dist.destroy_process_group()
@@ -74,3 +74,12 @@ def test_tensor_parallel_serving_in_lockstep(speculative):
     assert lead["refused"] and not lead["failed"]
     assert 2 <= lead["beats"] <= 10
     assert follower["rounds"] > 0
+
+
+def test_tensor_parallel_serving_with_batched_prefill():
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        out = mgr.dict()
+        mp.start_processes(_worker, args=(2, _port(), True, out, True), nprocs=2, start_method="spawn", join=True)
+        res = dict(out)
+    assert res[0]["got"] == res[0]["alone"] and res[0]["refused"]
