@@ -132,3 +132,35 @@ def test_shard_layouts_cover_the_weights():
     assert (loc.num_heads, loc.num_kv_heads, loc.gdn_k_heads, loc.gdn_v_heads) == (3, 1, 2, 6)
     with pytest.raises(ValueError):
         sharding.local_target_config(q, 3, 0)
+
+
+def _mamba_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.set_num_threads(1)
+    try:
+        from eagle4_b200.api import LLM, TreeSpec
+        from eagle4_b200.parallel.tp import TensorParallel
+
+        kw = dict(device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_len=256, max_batch=2)
+        llm = LLM.synthetic("tiny-mamba", tp=TensorParallel(backend="torch"), **kw)
+        ref = LLM.synthetic("tiny-mamba", **kw)
+        g = torch.Generator().manual_seed(5)
+        prompts = [torch.randint(0, 4096, (18,), generator=g), torch.randint(0, 4096, (27,), generator=g)]
+        spec = llm.generate(prompts, 10).tolist()
+        plain = llm.generate(prompts, 10, speculative=False).tolist()
+        out[rank] = {"spec": spec, "plain": plain, "one": ref.generate(prompts, 10, speculative=False).tolist()}
+    finally:
+        dist.destroy_process_group()
+
+
+def test_mamba_hybrid_under_tensor_parallelism():
+    """A Nemotron-H-style Mamba2 hybrid at TP2 (heads, groups and their norm weights sharded): speculative == plain,
+    and both equal the single-process greedy tokens."""
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        out = mgr.dict()
+        mp.start_processes(_mamba_worker, args=(2, _port(), out), nprocs=2, start_method="spawn", join=True)
+        res = dict(out)
+    for r in range(2):
+        assert res[r]["spec"] == res[r]["plain"] == res[r]["one"]
