@@ -141,6 +141,8 @@ class Engine:
         # one cache row beyond the requests' rows: batch rows that pad a round up to its graph bucket use it (its
         # block-table row maps only the trash page, its recurrent state belongs to no request)
         self.pad_slot = max_reqs
+        # prompts longer than this prefill in chunks (the recurrent states and the KV carry over between chunks)
+        self.prefill_chunk = 8192
         self.tcache = TargetCache.allocate(target.cfg, max_reqs=max_reqs + 1, max_len=self.max_len, page=page,
                                            device=self.device, dtype=self.dtype, kv_pages=kv_pages)
         self.pages = PagePool(self.tcache.block_table, kv_pages, page)
@@ -267,14 +269,20 @@ class Engine:
         self.pages.release(slot)
         self.pages.reserve(slot, reserve_tokens if reserve_tokens is not None else self.max_len)
         self.tcache.reset_slot(slot)
-        pos = torch.arange(n, device=self.device)
-        slots = self._slots(torch.tensor(slot, device=self.device), pos)
-        rb = RowBatch(ids=prompt.to(self.device), pos=pos, req=self._i32(n, slot), write_slot=slots,
-                      ctx_start=self._i32(n, 0), ctx_len=(pos + 1).int(),
-                      extra=torch.zeros(n, 1, dtype=torch.int32, device=self.device), n_extra=self._i32(n, 0),
-                      parent=(pos - 1).int(), state_slot=self._i32(n, slot), scan=True, max_keys=n,
-                      segments=self._segments(n))
-        out, aux = self.target.forward(rb, self.tcache)
+        auxes = []
+        for s in range(0, n, self.prefill_chunk):  # long prompts in chunks: bounded activations, same results
+            e = min(n, s + self.prefill_chunk)
+            t = e - s
+            pos = torch.arange(s, e, device=self.device)
+            slots = self._slots(torch.tensor(slot, device=self.device), pos)
+            rb = RowBatch(ids=prompt[s:e].to(self.device), pos=pos, req=self._i32(t, slot), write_slot=slots,
+                          ctx_start=self._i32(t, 0), ctx_len=(pos + 1).int(),
+                          extra=torch.zeros(t, 1, dtype=torch.int32, device=self.device), n_extra=self._i32(t, 0),
+                          parent=torch.arange(-1, t - 1, device=self.device, dtype=torch.int32),
+                          state_slot=self._i32(t, slot), scan=True, max_keys=e, segments=self._segments(t))
+            out, aux = self.target.forward(rb, self.tcache)
+            auxes.append(aux)
+        aux = auxes[0] if len(auxes) == 1 else (None if auxes[0] is None else torch.cat(auxes))
         if self.sampled:
             dev = self.device
             _, _, first = self.target.sampled_accept(out[-1:], self.temperature,

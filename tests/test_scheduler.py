@@ -162,3 +162,27 @@ def test_batched_prefill_engine_matches_single_prefills():
     assert [int(f[0]) for f in firsts] == one
     for a, b in zip(state, eng.tcache.ssm):
         assert torch.allclose(a[:3], b[:3], atol=1e-6)
+
+
+@pytest.mark.parametrize("model", ["tiny", "tiny-mamba"])
+def test_chunked_prefill_matches_one_forward(model):
+    """A prompt longer than the prefill chunk goes through the target in pieces (the recurrent and conv states and the
+    KV carry over between pieces): the first token, the aux rows, the states and the speculative output equal one
+    forward's."""
+    def run(chunk):
+        llm = LLM.synthetic(model, device="cpu", dtype=torch.float32, tree=TreeSpec(4, 2, 8), max_batch=1,
+                            max_len=256)
+        eng = llm.engine
+        eng.prefill_chunk = chunk
+        prompt = _prompts(1, seed=9)[0].repeat(3)[:70]
+        eng.slot[0] = 0
+        first, aux = eng.prefill(0, prompt)
+        state = [t[:1].clone() for t in eng.tcache.ssm] + [t[:1].clone() for t in eng.tcache.conv]
+        return int(first[0]), aux, state, llm.generate([prompt], 12, speculative=True)[0].tolist()
+
+    f1, a1, s1, g1 = run(8192)
+    f2, a2, s2, g2 = run(16)
+    assert f1 == f2 and g1 == g2
+    assert torch.allclose(a1, a2, atol=1e-5)
+    for a, b in zip(s1, s2):
+        assert torch.allclose(a, b, atol=1e-5)
