@@ -87,6 +87,17 @@ class DraftModel:
                           n_extra, self.cfg.head_dim ** -0.5, max_keys)
         return self.layer_output(o, res)
 
+    def write_kv(self, ids: torch.Tensor, hidden: torch.Tensor, pos: torch.Tensor, write_slot: torch.Tensor,
+                 cache: DraftCache) -> None:
+        """Only the rows' draft KV: the layer input, the q/k/v projection and the rotated k and v written to
+        ``write_slot``, without the attention, the MLP or the head. A single-layer draft's KV at a position depends
+        on that position's input alone, so the KV equals what ``forward`` writes; rows whose outputs are never read
+        (a prompt's leading rows) need nothing else. Reference counterpart: ``kv_only_prefill``
+        (``eagle_harness/sglang/draft_kv.py:39``)."""
+        x, _ = self.layer_input(ids, hidden)
+        qkv = ops.linear(x, self.w["qkv"])
+        ops.qkv_prepare(qkv, self.attn_shape, pos, write_slot, cache.k, cache.v, None, None)
+
     def forward_rows(self, ids: torch.Tensor, pos: torch.Tensor, hidden: torch.Tensor,
                      attend: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
                      ) -> Tuple[torch.Tensor, torch.Tensor]:

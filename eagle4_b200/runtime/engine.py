@@ -41,6 +41,9 @@ class RoundStats:
     rounds: int = 0
     emitted: int = 0
     accepted_hist: Dict[int, int] = field(default_factory=dict)
+    # natively decoded positions left without draft KV (the draft's attention reads stale KV there until its window
+    # moves past them); the reference counts the same slots (``StaleDraftKV``, ``eagle_harness/sglang/draft_kv.py:90``)
+    draft_kv_holes: int = 0
 
     def record(self, accepted: Sequence[int]) -> None:
         self.rounds += 1
@@ -205,6 +208,9 @@ class Engine:
         self.slot = torch.arange(max_reqs, dtype=i32, device=dev)
         self.ext_tok = torch.zeros(max_reqs, n, dtype=i64, device=dev)
         self.ext_cnt = torch.zeros(max_reqs, dtype=i32, device=dev)
+        # host mirror of ext_cnt (prefills and the rounds' read-back counts set it): a native round on a request
+        # whose ring is full drops its oldest pending row, a position that never gets draft KV
+        self.pending_host = [0] * max_reqs
         aux_w = (draft.cfg.num_aux * draft.cfg.target_hidden_size) if draft is not None else 1
         self.ext_aux = torch.zeros(max_reqs, n, aux_w, dtype=self.dtype, device=dev)
         self.out_tok = torch.zeros(max_reqs, n, dtype=i64, device=dev)
@@ -365,27 +371,31 @@ class Engine:
         nxt = torch.cat([prompt.to(self.device)[1:], first.to(self.device).view(1)])  # token after each position
         keep = min(n, self.verify_tokens)
         lead = n - keep
-        if lead:
-            if self.device.type == "cuda":  # the prompt's leading rows: prefill GEMM launches
+        if lead:  # the leading rows' outputs are never read: only their draft KV is written
+            if self.device.type == "cuda":  # prefill GEMM launches
                 from eagle4_b200.ops import native
 
                 with native.prefill_gemms():
-                    self._draft_rows(nxt[:lead], self.draft.project(aux[:lead]), pos[:lead], slot)
+                    self._draft_kv(nxt[:lead], self.draft.project(aux[:lead]), pos[:lead], slot)
             else:
-                self._draft_rows(nxt[:lead], self.draft.project(aux[:lead]), pos[:lead], slot)
+                self._draft_kv(nxt[:lead], self.draft.project(aux[:lead]), pos[:lead], slot)
         self.ext_tok[b, :keep] = nxt[lead:]
         self.ext_aux[b, :keep] = aux[lead:]
         self.ext_cnt[b] = keep
+        self.pending_host[b] = keep
 
-    def _draft_rows(self, ids, hidden, pos, slot: int):
-        w = self.draft.cfg.sliding_window
-        t = ids.shape[0]
-        start = (pos - w + 1).clamp(min=0) if w else torch.zeros_like(pos)
-        # rows are the positions 0..t-1 (the prompt's leading rows): at most min(w, t) visible keys
-        return self.draft.forward(ids, hidden, pos, self._i32(t, slot),
-                                  self._slots(torch.tensor(slot, device=self.device), pos), start.int(),
-                                  (pos + 1).int(), torch.zeros(t, 1, dtype=torch.int32, device=self.device),
-                                  self._i32(t, 0), self.dcache, max_keys=min(w, t) if w else t)
+    def _track_pending(self, bs: int, counts: List[int], native: bool) -> None:
+        n = self.verify_tokens
+        for b in range(bs):
+            if not native:
+                self.pending_host[b] = min(counts[b], n)
+            elif self.pending_host[b] >= n:
+                self.stats.draft_kv_holes += 1
+            else:
+                self.pending_host[b] += 1
+
+    def _draft_kv(self, ids, hidden, pos, slot: int) -> None:
+        self.draft.write_kv(ids, hidden, pos, self._slots(torch.tensor(slot, device=self.device), pos), self.dcache)
 
     # ------------------------------------------------------------------ device-state rounds
     def _plain_round(self, bs: int) -> None:
@@ -775,6 +785,8 @@ class Engine:
         got = [len(t) for t in taken]
         if spec:
             self.stats.record(got)
+        if self.draft is not None:
+            self._track_pending(bs, counts, native=not spec or choice == ServedTreeChoice.NATIVE or over_limit)
         if self.recorder is not None:
             kind = "plain" if not spec else ("native" if choice == ServedTreeChoice.NATIVE else
                                              ("chain" if chain_t0 is not None else "tree"))

@@ -193,6 +193,7 @@ class Scheduler:
         eng = self.engine
         for t in (eng.L, eng.root, eng.slot, eng.ext_tok, eng.ext_cnt, eng.ext_aux):
             t[dst] = t[src]
+        eng.pending_host[dst] = eng.pending_host[src]
 
     # ------------------------------------------------------------------ rounds
     def step(self) -> List[Request]:

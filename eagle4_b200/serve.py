@@ -238,7 +238,9 @@ def metrics_text(batcher: Batcher) -> str:
                                      ("generated_tokens", "tokens generated by finished requests",
                                       c["generated_tokens"]),
                                      ("rounds", "engine rounds (speculative or native)", st.rounds),
-                                     ("emitted_tokens", "tokens emitted by speculative rounds", st.emitted)):
+                                     ("emitted_tokens", "tokens emitted by speculative rounds", st.emitted),
+                                     ("draft_kv_holes", "natively decoded positions left without draft KV",
+                                      st.draft_kv_holes)):
                 yield CounterMetricFamily(f"eagle4_{name}", doc, value=value)
             acc = CounterMetricFamily("eagle4_accepted_per_request_round", "request-rounds by tokens emitted",
                                       labels=["tokens"])

@@ -230,6 +230,7 @@ def test_completions_text_stop_strings_and_metrics():
         m = client.get("/metrics").text
         assert "eagle4_requests_total 2.0" in m and "eagle4_generated_tokens_total" in m
         assert 'eagle4_accepted_per_request_round_total{tokens="' in m
+        assert "eagle4_draft_kv_holes_total" in m
     finally:
         b.close(timeout=60)
 

@@ -186,3 +186,42 @@ def test_chunked_prefill_matches_one_forward(model):
     assert torch.allclose(a1, a2, atol=1e-5)
     for a, b in zip(s1, s2):
         assert torch.allclose(a, b, atol=1e-5)
+
+
+def test_prompt_leading_rows_get_only_draft_kv():
+    """The draft's share of a prefill writes the leading rows' KV without their attention or MLP: the KV equals a
+    full draft forward's over the same rows."""
+    llm = _llm(max_batch=1)
+    eng = llm.engine
+    prompt = _prompts(1, seed=3)[0].repeat(4)[:60]
+    eng.slot[0] = 0
+    first, aux = eng.prefill(0, prompt)
+    lead = prompt.shape[0] - min(prompt.shape[0], eng.verify_tokens)
+    slots = eng._slots(torch.tensor(0), torch.arange(lead))
+    k_kv, v_kv = eng.dcache.k.view(-1, *eng.dcache.k.shape[-2:])[slots], eng.dcache.v.view(-1, *eng.dcache.v.shape[-2:])[slots]
+    eng.dcache.k.zero_()
+    eng.dcache.v.zero_()
+    pos = torch.arange(lead)
+    nxt = prompt[1:lead + 1]
+    eng.draft.forward(nxt, eng.draft.project(aux[:lead]), pos, torch.zeros(lead, dtype=torch.int32), slots,
+                      torch.zeros(lead, dtype=torch.int32), (pos + 1).int(), torch.zeros(lead, 1, dtype=torch.int32),
+                      torch.zeros(lead, dtype=torch.int32), eng.dcache, max_keys=lead)
+    assert torch.equal(eng.dcache.k.view(-1, *eng.dcache.k.shape[-2:])[slots], k_kv)
+    assert torch.equal(eng.dcache.v.view(-1, *eng.dcache.v.shape[-2:])[slots], v_kv)
+
+
+def test_native_rounds_count_positions_left_without_draft_kv():
+    """Above the verify batch limit every round is native; a request's pending ring holds N rows, so each native
+    token after the ring is full leaves one position without draft KV, and the count follows rows that move."""
+    llm = _llm(max_batch=2)
+    eng = llm.engine
+    n = eng.verify_tokens
+    eng.verify_batch_limit = 1
+    prompts = [p[:8] if p.shape[0] >= 8 else p.repeat(8)[:8] for p in _prompts(2, seed=5)]
+    sched = Scheduler(eng)
+    reqs = [sched.submit(p, RequestParams(max_new_tokens=n + 6)) for p in prompts]
+    sched.run()
+    assert all(len(r.output) == n + 6 for r in reqs)
+    # ring full after the prefill (N of the 8 prompt rows pending); the first emitted token is the prefill's, so
+    # n + 5 native rounds per request, each one a hole
+    assert eng.stats.draft_kv_holes == 2 * (n + 5)
