@@ -27,11 +27,12 @@ import torch
 
 from eagle4_b200 import ops
 from eagle4_b200.core.config import HarnessConfig, Mode
-from eagle4_b200.core.cost_model import WidthStep
+from eagle4_b200.core.cost_model import CostModel
 from eagle4_b200.core.draft_tree import DraftTree, TreeShape
 from eagle4_b200.core.limits import COST_BATCH_SIZES
 from eagle4_b200.runtime.pages import PagePool
 from eagle4_b200.runtime.policy import RoundPolicy, ServedChainPolicy, ServedTreeChoice, fit_width
+from eagle4_b200.runtime.round_plan import DECIDE, KIND as PLAN_KIND, LAST, LAUNCH, RoundCheck, round_plan
 from eagle4_b200.models.draft import DraftCache, DraftModel
 from eagle4_b200.models.target import Records, RowBatch, TargetCache, TargetModel
 
@@ -228,6 +229,8 @@ class Engine:
         self._captured = False  # a graph was captured during the current round
         self.last_timing: Dict[str, float] = {}
         self.stats = RoundStats()
+        # set to a RoundCheck to compare every planned DECIDE stop with the cost model's own decision
+        self.round_check: Optional[RoundCheck] = None
         self.recorder = None  # a runtime.recorder.RoundRecorder to keep per-round records
         if self.tree is not None:
             self.host_deltas = torch.zeros(tuple(self.tree.deltas.shape), dtype=torch.float32, pin_memory=pin)
@@ -650,25 +653,39 @@ class Engine:
         """The draft half of a round: extend and depth 1, then steps until a DECIDE depth's work deltas say stop;
         the verify width comes from the previous round's scores. Returns (verify width, last step depth)."""
         self._graph(("begin", bs), self._phase_begin, bs)
-        row = policy.draft_cost_row(bs, context)
         past = policy.history_verify_num(bs)
+        # a cost-model tree round fixes its stop rule up front (RoundPlan); chains and the fixed shape ask per depth
+        # (the cost row is read before the plan: a DECIDE changes the size tier the row depends on)
+        is_cost = isinstance(policy, CostModel)
+        row = policy.draft_cost_row(bs, context) if not is_cost or self.round_check is not None else None
+        if is_cost and self.round_check is not None:
+            self.round_check.begin(policy)
+        plan = round_plan(policy, bs, context, self.steps - 1) if is_cost else None
+        if is_cost and plan is None:  # chain rounds: the cost model decides per depth
+            row = policy.draft_cost_row(bs, context)
         deltas_ready = torch.cuda.Event() if self.device.type == "cuda" else None
         slot = 0
         depth = 0
         while depth < self.steps - 1:
-            kind = policy.width_step(depth)
-            if kind is WidthStep.LAST:
+            kind = plan.kind[depth] if plan is not None else PLAN_KIND[policy.width_step(depth)]
+            if kind == LAST:
                 break
-            if kind is WidthStep.LAUNCH:
+            if kind == LAUNCH:
                 if deltas_ready is not None:
                     deltas_ready.record()
                 slot = depth
-            elif kind is WidthStep.DECIDE:
+            elif kind == DECIDE:
                 if deltas_ready is not None:
                     deltas_ready.synchronize()
-                budget = policy.deltas_budget(past)
-                deltas = self.host_deltas[slot, budget - 1].tolist()
-                if policy.tree_width(depth, bs, past, row, deltas).stop:
+                if plan is not None:
+                    deltas = self.host_deltas[slot, plan.budget].tolist()
+                    stop = plan.stop(depth, deltas)
+                    if self.round_check is not None:
+                        self.round_check.compare(policy, plan, depth, bs, past, row, deltas)
+                else:
+                    deltas = self.host_deltas[slot, policy.deltas_budget(past) - 1].tolist()
+                    stop = policy.tree_width(depth, bs, past, row, deltas).stop
+                if stop:
                     break
             depth += 1
             self._graph(("step", bs, depth), self._phase_step, bs, depth)
