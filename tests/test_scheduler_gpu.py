@@ -58,3 +58,26 @@ def test_batched_prefill_on_gpu_matches_single_prefills():
     for layer_a, layer_b in zip(k, keys()):
         for a, b in zip(layer_a, layer_b):
             assert (a - b).abs().max() <= 2e-2 * (a.abs().max() + 1e-6)
+
+
+def test_chunked_prefill_on_gpu_matches_one_forward():
+    """A prompt longer than the prefill chunk goes through in pieces: the recurrent states and the attention keys
+    end as one forward leaves them (within bf16 rounding: pieces may take another GEMM partition)."""
+    from eagle4_b200.api import LLM, TreeSpec
+    from eagle4_b200.ops import native
+
+    llm = LLM.synthetic("tiny", device="cuda", tree=TreeSpec(4, 2, 8), max_batch=1, max_len=512)
+    eng = llm.engine
+    prompt = torch.randint(1, 4096, (200,), generator=torch.Generator().manual_seed(13))
+    eng.slot[0] = 0
+    rows = eng._slots(torch.tensor(0, device="cuda"), torch.arange(200, device="cuda"))
+    results = []
+    for chunk in (8192, 48):
+        eng.prefill_chunk = chunk
+        eng.prefill(0, prompt)
+        torch.cuda.synchronize()
+        native.check_errors(torch.device("cuda"))
+        results.append(([t[:1].float().clone() for t in eng.tcache.ssm],
+                        [t[rows].float().clone() for t in eng.tcache.k]))
+    for a, b in zip(results[0][0] + results[0][1], results[1][0] + results[1][1]):
+        assert (a - b).abs().max() <= 2e-2 * (a.abs().max() + 1e-6)
