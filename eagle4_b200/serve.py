@@ -456,7 +456,11 @@ def main(argv: Optional[List[str]] = None) -> int:
                     help="requests admitted in one step prefill in one target forward (groups of up to 8192 tokens)")
     ap.add_argument("--kv-tokens", type=int, help="KV cache positions shared by the running requests (default: "
                                                  "every row at --max-len; `eagle4-b200 plan` gives what fits)")
+    ap.add_argument("--prefill-chunk", type=int, default=8192,
+                    help="a longer prompt prefills in pieces of this many tokens (bounds the activations)")
     args = ap.parse_args(argv)
+    if args.prefill_chunk < 1:
+        ap.error("--prefill-chunk must be >= 1")
 
     from eagle4_b200.api import TreeSpec
     from eagle4_b200.cli import build_llm
@@ -478,6 +482,7 @@ def main(argv: Optional[List[str]] = None) -> int:
     llm = build_llm(args.model, args.draft, max_batch=args.max_batch, max_len=args.max_len,
                     tree=TreeSpec(*(int(v) for v in args.tree.split(","))), config=args.config, tp=tp,
                     temperature=args.temperature, seed=args.seed, kv_tokens=args.kv_tokens)
+    llm.engine.prefill_chunk = args.prefill_chunk
     if tp is not None:  # a dead or stalled rank is named by the heartbeat before the next round's collectives
         from eagle4_b200.parallel.health import process_group_heartbeat
 
