@@ -4,9 +4,11 @@ The plan builds the same tensors the engine builds, on PyTorch's ``meta`` device
 draft weights as this rank keeps them under tensor parallelism (shared tensors counted once), the target's paged KV
 cache and recurrent states, the draft's KV cache. Everything scales with the KV token budget except the weights and
 the per-request states, so the plan also answers the largest ``kv_tokens`` that fits a memory budget (the server's
-``--kv-tokens``). ``reserve_gb`` stands for what the plan does not count: activations, CUDA graph pools, the
-tensor-parallel buffers, the CUDA context (a few GB at the flagship shapes; measure with ``torch.cuda.mem_get_info``
-on the target GPU for a tighter figure).
+``--kv-tokens``). ``prefill`` estimates the largest transient of a prefill: one piece of ``prefill_chunk`` rows
+through the widest projection plus a few hidden-size buffers, and the aux hidden states of a whole ``max_len``
+prompt kept for the draft. ``reserve_gb`` stands for what the plan does not count: decode activations, CUDA graph
+pools, the tensor-parallel buffers, the CUDA context (a few GB at the flagship shapes; measure with
+``torch.cuda.mem_get_info`` on the target GPU for a tighter figure).
 """
 
 from __future__ import annotations
@@ -27,6 +29,7 @@ class MemoryPlan:
     state_bytes: int         # recurrent states (conv windows, SSM states) of every cache row
     kv_tokens: int
     reserve: int
+    prefill: int = 0         # bytes of the largest prefill transient (one piece's activations, the prompt's aux rows)
 
     @property
     def kv(self) -> int:
@@ -34,11 +37,11 @@ class MemoryPlan:
 
     @property
     def total(self) -> int:
-        return self.weights + self.kv + self.state_bytes + self.reserve
+        return self.weights + self.kv + self.state_bytes + self.reserve + self.prefill
 
     def kv_tokens_within(self, budget_bytes: float) -> int:
         """The largest KV token budget (a multiple of 1024) whose plan fits ``budget_bytes``."""
-        free = budget_bytes - self.weights - self.state_bytes - self.reserve
+        free = budget_bytes - self.weights - self.state_bytes - self.reserve - self.prefill
         return max(0, int(free // self.kv_bytes_per_token) // 1024 * 1024)
 
     def summary(self, budget_gb: Optional[float] = None) -> Dict[str, float]:
@@ -61,8 +64,8 @@ def _bytes(tensors) -> int:
 
 
 def plan(target_cfg, draft_cfg=None, *, tp: int = 1, max_batch: int = 1, max_len: int = 4096, page: int = 16,
-         tree=(12, 4, 16), kv_tokens: Optional[int] = None, dtype=torch.bfloat16, reserve_gb: float = 4.0
-         ) -> MemoryPlan:
+         tree=(12, 4, 16), kv_tokens: Optional[int] = None, dtype=torch.bfloat16, reserve_gb: float = 4.0,
+         prefill_chunk: int = 8192) -> MemoryPlan:
     """The memory of rank 0 of a ``tp``-way engine (ranks differ at most by a vocabulary shard's rounding)."""
     from eagle4_b200.models import weights
     from eagle4_b200.models.draft import DraftCache
@@ -86,5 +89,11 @@ def plan(target_cfg, draft_cfg=None, *, tp: int = 1, max_batch: int = 1, max_len
     state = _bytes(one.conv + one.ssm)
     if ldc is not None:
         kv_page += _bytes([DraftCache.allocate(ldc, one.block_table, page, meta, dtype, pages=1).k]) * 2
+    esize = torch.empty(0, dtype=dtype).element_size()
+    widest = max((t.shape[0] for name, t in ltw.items() if t.dim() == 2 and name not in ("embed", "lm_head")),
+                 default=0)
+    hidden = target_cfg.hidden_size
+    aux = len(draft_cfg.aux_layer_ids) * hidden if draft_cfg is not None else 0
+    prefill = (min(prefill_chunk, max_len) * (widest + 4 * hidden) + max_len * aux) * esize
     return MemoryPlan(weights=w_bytes, kv_bytes_per_token=kv_page // page, state_bytes=state,
-                      kv_tokens=int(tokens), reserve=int(reserve_gb * GB))
+                      kv_tokens=int(tokens), reserve=int(reserve_gb * GB), prefill=int(prefill))

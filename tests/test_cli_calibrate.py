@@ -336,7 +336,10 @@ def test_memory_plan_matches_the_engine_allocations(capsys):
     assert p.kv_bytes_per_token * slots == kv
     model_w = nbytes(list(llm.target.w.values()) + list(llm.draft.w.values()))
     assert abs(p.weights - model_w) <= 0.02 * model_w  # the engine may fold norms into projection copies
-    assert p.kv_tokens_within(p.weights + p.state_bytes + 10 * p.kv_bytes_per_token * 1024) == 10 * 1024
+    assert p.kv_tokens_within(p.weights + p.state_bytes + p.prefill + 10 * p.kv_bytes_per_token * 1024) == 10 * 1024
+    # the prefill transient: one piece through the widest projection and the aux rows of a max_len prompt
+    widest = max(t.shape[0] for n, t in llm.target.w.items() if t.dim() == 2 and n not in ("embed", "lm_head"))
+    assert p.prefill == (200 * (widest + 4 * tcfg.hidden_size) + 200 * dcfg.num_aux * tcfg.hidden_size) * 4
     assert cli.main(["plan", "--model", "qwen3.8-27b", "--max-batch", "64", "--max-len", "8192"]) == 0
     out = json.loads(capsys.readouterr().out)
     assert out["fits"] and 50 < out["weights"] < 60 and out["max_kv_tokens"] > out["kv_tokens"]
