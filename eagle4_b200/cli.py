@@ -236,7 +236,8 @@ def _plan(args) -> int:
 
     tcfg, dcfg = _full_configs(args)
     p = plan(tcfg, dcfg, tp=args.tp, max_batch=args.max_batch, max_len=args.max_len, kv_tokens=args.kv_tokens,
-             tree=tuple(int(v) for v in args.tree.split(",")), reserve_gb=args.reserve_gb)
+             tree=tuple(int(v) for v in args.tree.split(",")), reserve_gb=args.reserve_gb,
+             prefill_chunk=args.prefill_chunk)
     summary = p.summary(args.gpu_gb or round(B200_GB, 1))
     print(json.dumps(summary, indent=2))
     return 0 if summary["fits"] else 1
@@ -318,7 +319,8 @@ def main(argv: Optional[List[str]] = None) -> int:
     pl.add_argument("--kv-tokens", type=_positive, help="KV token budget (default: every row at max-len)")
     pl.add_argument("--tree", default="12,4,16", help="steps,top_k,draft_tokens")
     pl.add_argument("--gpu-gb", type=float, help="memory budget per GPU in GB (default: a B200's)")
-    pl.add_argument("--reserve-gb", type=float, default=4.0, help="activations, graph pools, buffers, context")
+    pl.add_argument("--reserve-gb", type=float, default=4.0, help="decode activations, graph pools, buffers, context")
+    pl.add_argument("--prefill-chunk", type=_positive, default=8192, help="the server's --prefill-chunk")
     pl.set_defaults(func=_plan)
     rep = sub.add_parser("report", formatter_class=argparse.ArgumentDefaultsHelpFormatter,
                          help="summarise a calibration directory: setup, tables, schedules, cost-model checks")
